@@ -1,0 +1,70 @@
+// cm_common.cuh -- shared internals of libcormorant_cuda.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "cormorant_cuda.h"
+
+namespace cm {
+
+// ---------------------------------------------------------------------------
+// Host side: context, errors, scratch
+// ---------------------------------------------------------------------------
+struct Context {
+    int device = -1;
+    int sm_count = 0;
+    int* status = nullptr;          // device status word (0 = ok, else a CM_E* code)
+    uint64_t timeout_ns = 2000000000ull;  // bounded device-side waits
+};
+
+Context* ctx();                      // nullptr before cm_init
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+int enter(const Context** out);      // checks init, selects the device
+void count_launch(unsigned n = 1);
+int finish_sync(cm_stream_t stream); // synchronize + read/clear the status word
+
+// Stream-ordered scratch from the device's default memory pool.
+int scratch_alloc(void** p, size_t bytes, cudaStream_t s);
+void scratch_free(void* p, cudaStream_t s);
+
+// Grid size for a grid-stride kernel: a multiple of the SM count.
+inline unsigned grid_for(const Context* c, uint64_t work_items, unsigned block, unsigned per_sm) {
+    const uint64_t need = (work_items + block - 1) / block;
+    const uint64_t cap = (uint64_t)c->sm_count * per_sm;
+    return (unsigned)(need < cap ? (need ? need : 1) : cap);
+}
+
+// ---------------------------------------------------------------------------
+// Device side: Q8.8 narrowing
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int16_t sat16(int32_t v) {
+    return (int16_t)max(-32768, min(32767, v));
+}
+
+// saturate_cast<ap_fixed<16,8>>(ap_fixed<32,16> acc): floor by 8 bits, clamp.
+// `acc` is the raw Q16.16 accumulator, already reduced mod 2^32.
+__device__ __forceinline__ int16_t narrow_acc(uint32_t acc) {
+    return sat16(((int32_t)acc) >> 8);   // arithmetic shift == floor
+}
+
+// Unsigned 32-bit division by a run-time invariant divisor with a
+// multiply-high and a shift (Granlund & Montgomery, "Division by invariant
+// integers using multiplication", PLDI 1994, Fig. 4.1).
+struct FastDiv {
+    uint32_t d, mul, shift;
+    FastDiv() : d(1), mul(0), shift(0) {}
+    explicit FastDiv(uint32_t div) : d(div ? div : 1) {
+        uint32_t l = 0;
+        while (l < 32 && (1ull << l) < d) ++l;
+        shift = l;
+        mul = (uint32_t)((((1ull << 32) * ((1ull << l) - d)) / d) + 1);
+    }
+    __device__ __forceinline__ uint32_t div(uint32_t n) const {
+        const uint64_t t = __umulhi(n, mul);
+        return (uint32_t)((t + n) >> shift);
+    }
+};
+
+}  // namespace cm

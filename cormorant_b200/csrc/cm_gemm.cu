@@ -1,0 +1,639 @@
+// cm_gemm.cu -- MatmulKernel on B200 (reference: kernels/matmul/kernel/MatmulKernel.cpp)
+// and the tcgen05 Q8.8 GEMM core it shares with ConvKernel.
+//
+// Exactness.  The reference accumulates exact Q8.8 x Q8.8 products in an
+// ap_fixed<32,16> (int32, wraps mod 2^32) and narrows once (MatmulKernel.cpp:204,
+// :217-218).  Write every int16 word as x = 256*h + l' + 128 with
+// h = x >> 8 in [-128, 127] and l' = (x & 255) - 128 in [-128, 127], both int8.
+// With x' = x - 128 = 256*h + l':
+//   sum_k a*b = sum a'b' + 128*sum_k a' + 128*sum_k b' + 16384*K
+//   sum a'b'  = 2^16*sum(ah*bh) + 2^8*(sum(ah*bl') + sum(al'*bh)) + sum(al'*bl')
+// The three int8 dot products run on the tensor cores (tcgen05.mma kind::i8,
+// s8 x s8 -> s32, four MMAs per K step into three TMEM accumulators); the two
+// rank-1 terms come from the split pre-pass.  All of it is reduced mod 2^32,
+// which is exactly the reference's wrap, so the result is bit-identical.
+// Each accumulator's magnitude stays below K * 2^15, so K <= 65535 never
+// overflows an int32 on the way.
+//
+// Kernel (one 128x128 output tile per CTA, 192 threads, 1 CTA per SM):
+//   warp 0   TMA producer: per K block of 128 bytes, one 4-D box {128 k, 128 rows,
+//            2 planes, 1 batch} for A and one for B (32 KB each, 128-byte swizzle),
+//            3-stage ring guarded by full/empty mbarriers.  No multicast.
+//   warp 1   allocates 512 TMEM columns; lane 0 issues the MMAs and commits.
+//   warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns of each accumulator,
+//            recombine, narrow, store int16 rows.
+// Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
+// CM_ETIMEOUT in the status word and winds down instead of hanging.
+#include <cuda.h>
+
+#include "cm_gemm.cuh"
+
+namespace cm {
+namespace {
+
+constexpr int BM = 128, BN = 128, BK = 128, STAGES = 3;
+constexpr int PLANE_TILE = BM * BK;                 // 16 KB
+constexpr int OPERAND_TILE = 2 * PLANE_TILE;        // hi + lo = 32 KB
+constexpr int STAGE_BYTES = 2 * OPERAND_TILE;       // A + B = 64 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t COL_HH = 0, COL_X = 128, COL_LL = 256;
+
+// Instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = 128.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+struct WaitCtl {
+    volatile int* abort;   // shared flag: some role gave up
+    int* status;           // device status word
+    uint64_t timeout_ns;
+};
+
+// Bounded wait: returns false (and raises the abort flag) on timeout or abort.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& w) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = gtimer();
+    for (uint32_t it = 1;; ++it) {
+        if (mbar_try(bar, parity)) return true;
+        if ((it & 63u) == 0) {
+            if (*w.abort) return false;
+            if (gtimer() - t0 > w.timeout_ns) {
+                atomicCAS(w.status, 0, CM_ETIMEOUT);
+                *w.abort = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
+// 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+#define CM_R32(i) "=r"(r[i])
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : CM_R32(0), CM_R32(1), CM_R32(2), CM_R32(3), CM_R32(4), CM_R32(5), CM_R32(6), CM_R32(7), CM_R32(8),
+          CM_R32(9), CM_R32(10), CM_R32(11), CM_R32(12), CM_R32(13), CM_R32(14), CM_R32(15), CM_R32(16),
+          CM_R32(17), CM_R32(18), CM_R32(19), CM_R32(20), CM_R32(21), CM_R32(22), CM_R32(23), CM_R32(24),
+          CM_R32(25), CM_R32(26), CM_R32(27), CM_R32(28), CM_R32(29), CM_R32(30), CM_R32(31)
+        : "r"(taddr));
+}
+#undef CM_R32
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+struct GemmArgs {
+    uint32_t rows, cols, num_kb, a_batches, b_batches;
+    const int32_t* rowterm;
+    const int32_t* colterm;
+    int16_t* out;
+    uint64_t ldo, out_bs;
+    uint32_t z_base;
+    int* status;
+    uint64_t timeout_ns;
+};
+
+__global__ void __launch_bounds__(192, 1)
+    gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+    // bars[0..S) full, bars[S..2S) empty, bars[2S] acc_full
+    volatile uint32_t* tmem_slot = (volatile uint32_t*)(bars + 2 * STAGES + 1);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t n0 = blockIdx.x * BN;   // output column tile (B rows)
+    const uint32_t m0 = blockIdx.y * BM;   // output row tile (A rows)
+    const uint32_t z = blockIdx.z + g.z_base;
+    const uint32_t ba = g.a_batches == 1 ? 0u : z;
+    const uint32_t bb = g.b_batches == 1 ? 0u : z;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(smem_u32(&bars[s]), 1);
+            mbar_init(smem_u32(&bars[STAGES + s]), 1);
+        }
+        mbar_init(smem_u32(&bars[2 * STAGES]), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        tc_fence_before();
+    }
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const WaitCtl wc{abort_flag, g.status, g.timeout_ns};
+
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t issued = 0;
+            for (uint32_t kb = 0; kb < g.num_kb; ++kb) {
+                const uint32_t s = kb % STAGES, round = kb / STAGES;
+                if (!mbar_wait(smem_u32(&bars[STAGES + s]), (round & 1u) ^ 1u, wc)) break;
+                const uint32_t full = smem_u32(&bars[s]);
+                mbar_expect_tx(full, STAGE_BYTES);
+                uint8_t* st = smem + s * STAGE_BYTES;
+                tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)m0, 0, (int)ba);
+                tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)(kb * BK), (int)n0, 0, (int)bb);
+                ++issued;
+            }
+            if (*abort_flag) {
+                // let copies already in flight land before the CTA exits
+                const uint32_t first = issued > (uint32_t)STAGES ? issued - STAGES : 0u;
+                WaitCtl drain{abort_flag, g.status, g.timeout_ns};
+                for (uint32_t kb = first; kb < issued; ++kb) {
+                    volatile int never = 0;
+                    drain.abort = &never;
+                    mbar_wait(smem_u32(&bars[kb % STAGES]), (kb / STAGES) & 1u, drain);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (uint32_t kb = 0; kb < g.num_kb; ++kb) {
+                const uint32_t s = kb % STAGES, round = kb / STAGES;
+                if (!mbar_wait(smem_u32(&bars[s]), round & 1u, wc)) break;
+                tc_fence_after();
+                const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
+                const uint32_t b0 = a0 + OPERAND_TILE;
+#pragma unroll
+                for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                    const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
+                    const uint64_t bh = sdesc(b0 + kk * 32), bl = sdesc(b0 + PLANE_TILE + kk * 32);
+                    const uint32_t acc = (kb | kk) != 0u;
+                    umma_i8(tmem + COL_HH, ah, bh, acc);
+                    umma_i8(tmem + COL_X, ah, bl, acc);
+                    umma_i8(tmem + COL_X, al, bh, 1u);
+                    umma_i8(tmem + COL_LL, al, bl, acc);
+                }
+                umma_commit(smem_u32(&bars[STAGES + s]));   // frees the stage once these MMAs have read it
+            }
+            umma_commit(smem_u32(&bars[2 * STAGES]));      // accumulators complete (or nothing in flight)
+        }
+    } else {
+        // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32).
+        const uint32_t quarter = warp & 3u;
+        const uint32_t row = m0 + quarter * 32 + lane;
+        // One lane waits; the verdict is broadcast so that the .sync.aligned
+        // TMEM loads below are executed by the whole warp or not at all.
+        uint32_t ok = 0;
+        if (lane == 0) ok = (mbar_wait(smem_u32(&bars[2 * STAGES]), 0, wc) && !*abort_flag) ? 1u : 0u;
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+        __syncwarp();
+        tc_fence_after();
+        if (ok) {
+            const uint32_t rt = row < g.rows ? (uint32_t)g.rowterm[(uint64_t)ba * g.rows + row] : 0u;
+            const int32_t* ct = g.colterm + (uint64_t)bb * g.cols;
+            int16_t* orow = g.out + (uint64_t)z * g.out_bs + (uint64_t)row * g.ldo;
+            const uint32_t tl = tmem + ((quarter * 32u) << 16);
+#pragma unroll 1
+            for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
+                if (n0 + c0 >= g.cols) break;
+                uint32_t hh[32], xx[32], ll[32];
+                tmem_ld32(tl + COL_HH + c0, hh);
+                tmem_ld32(tl + COL_X + c0, xx);
+                tmem_ld32(tl + COL_LL + c0, ll);
+                tmem_ld_wait();
+                if (row < g.rows) {
+                    const uint32_t col0 = n0 + c0;
+                    int16_t v[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const uint32_t col = col0 + j;
+                        const uint32_t cterm = col < g.cols ? (uint32_t)__ldg(ct + col) : 0u;
+                        const uint32_t acc = (hh[j] << 16) + (xx[j] << 8) + ll[j] + rt + cterm;
+                        v[j] = narrow_acc(acc);
+                    }
+                    int16_t* dst = orow + col0;
+                    if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
+                        uint4* d4 = (uint4*)dst;
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint4 w;
+                            w.x = (uint32_t)(uint16_t)v[8 * q + 0] | ((uint32_t)(uint16_t)v[8 * q + 1] << 16);
+                            w.y = (uint32_t)(uint16_t)v[8 * q + 2] | ((uint32_t)(uint16_t)v[8 * q + 3] << 16);
+                            w.z = (uint32_t)(uint16_t)v[8 * q + 4] | ((uint32_t)(uint16_t)v[8 * q + 5] << 16);
+                            w.w = (uint32_t)(uint16_t)v[8 * q + 6] | ((uint32_t)(uint16_t)v[8 * q + 7] << 16);
+                            d4[q] = w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < g.cols) dst[j] = v[j];
+                    }
+                }
+            }
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// split pre-passes
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ int32_t word_sum_minus128(uint32_t u) {
+    return (int32_t)(int16_t)(u & 0xFFFFu) + (int32_t)(int16_t)(u >> 16) - 256;
+}
+
+// One warp per (bt, row).
+__global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restrict__ src, uint64_t src_bs, uint64_t ld,
+                                                         uint32_t rows, uint32_t K, uint32_t K_pad, uint64_t nrows_total,
+                                                         int8_t* __restrict__ planes, int32_t* __restrict__ rowterm,
+                                                         const int16_t* __restrict__ bias) {
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+    for (uint64_t t = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < nrows_total; t += warps) {
+        const uint64_t bt = t / rows, r = t - bt * rows;
+        const int16_t* s = src + bt * src_bs + r * ld;
+        int8_t* dh = planes + ((bt * 2 + 0) * rows + r) * (uint64_t)K_pad;
+        int8_t* dl = planes + ((bt * 2 + 1) * rows + r) * (uint64_t)K_pad;
+        int32_t sum = 0;
+        uint32_t k_done = 0;
+        if (((uintptr_t)s & 15u) == 0) {
+            const uint32_t nv = K / 8;
+            const uint4* s4 = (const uint4*)s;
+            for (uint32_t i = lane; i < nv; i += 32) {
+                const uint4 v = __ldcs(s4 + i);
+                uint2 h, l;
+                h.x = __byte_perm(v.x, v.y, 0x7531);
+                h.y = __byte_perm(v.z, v.w, 0x7531);
+                l.x = __byte_perm(v.x, v.y, 0x6420) ^ 0x80808080u;
+                l.y = __byte_perm(v.z, v.w, 0x6420) ^ 0x80808080u;
+                *(uint2*)(dh + 8 * (uint64_t)i) = h;
+                *(uint2*)(dl + 8 * (uint64_t)i) = l;
+                sum += word_sum_minus128(v.x) + word_sum_minus128(v.y) + word_sum_minus128(v.z) + word_sum_minus128(v.w);
+            }
+            k_done = nv * 8;
+        }
+        for (uint32_t k = k_done + lane; k < K; k += 32) {
+            const int16_t x = s[k];
+            dh[k] = (int8_t)(x >> 8);
+            dl[k] = (int8_t)((x & 255) - 128);
+            sum += (int32_t)x - 128;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+        if (lane == 0) {
+            uint32_t term = (uint32_t)sum * 128u + (uint32_t)K * 16384u;
+            if (bias) term += (uint32_t)((int32_t)bias[r] * 256);
+            rowterm[t] = (int32_t)term;
+        }
+    }
+}
+
+struct MatSrc {
+    const int16_t* src; uint64_t src_bs, ld;
+    __device__ __forceinline__ int16_t operator()(uint32_t bt, uint32_t k, uint32_t c) const {
+        return src[(uint64_t)bt * src_bs + (uint64_t)k * ld + c];
+    }
+};
+
+struct Im2colSrc {
+    const int16_t* x;
+    ConvGeom g;
+    FastDiv fd_khw, fd_kw, fd_ow;
+    uint32_t khw;
+    __device__ __forceinline__ int16_t operator()(uint32_t n, uint32_t k, uint32_t p) const {
+        const uint32_t c = fd_khw.div(k);
+        const uint32_t rs = k - c * khw;
+        const uint32_t r = fd_kw.div(rs);
+        const uint32_t s = rs - r * g.kw;
+        const uint32_t oh = fd_ow.div(p);
+        const uint32_t ow = p - oh * g.out_w;
+        const int64_t ih = (int64_t)oh * g.sh + (int64_t)r * g.dh - (int64_t)g.pt;
+        const int64_t iw = (int64_t)ow * g.sw + (int64_t)s * g.dw - (int64_t)g.pl;
+        if (ih < 0 || ih >= (int64_t)g.H || iw < 0 || iw >= (int64_t)g.W) return 0;
+        return __ldg(x + (((uint64_t)n * g.C + c) * g.H + (uint64_t)ih) * g.W + (uint64_t)iw);
+    }
+};
+
+// 64 (k) x 64 (column) tile through shared memory: coalesced reads along the
+// column index, 16-byte plane writes along k; column terms via atomics.
+template <class Src>
+__global__ void __launch_bounds__(256) split_cols_kernel(Src src, uint32_t cols, uint32_t K, uint32_t K_pad,
+                                                         int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    __shared__ int16_t tile[64][66];
+    const uint32_t k0 = blockIdx.x * 64, c0 = blockIdx.y * 64, bt = blockIdx.z;
+    const uint32_t tid = threadIdx.x;
+#pragma unroll 4
+    for (uint32_t i = 0; i < 16; ++i) {
+        const uint32_t e = tid + i * 256;
+        const uint32_t kk = e >> 6, cc = e & 63;
+        const uint32_t k = k0 + kk, c = c0 + cc;
+        tile[kk][cc] = (k < K && c < cols) ? src(bt, k, c) : (int16_t)0;
+    }
+    __syncthreads();
+    const uint32_t cc = tid >> 2, j = tid & 3;
+    const uint32_t c = c0 + cc, kk0 = j * 16;
+    int32_t sum = 0;
+    if (c < cols) {
+        uint32_t hw[4], lw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            uint32_t h = 0, l = 0;
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const uint32_t kk = kk0 + 4 * q + b;
+                const int16_t x = tile[kk][cc];
+                h |= (uint32_t)(uint8_t)(x >> 8) << (8 * b);
+                l |= (uint32_t)(uint8_t)((x & 255) ^ 0x80) << (8 * b);
+                if (k0 + kk < K) sum += (int32_t)x - 128;
+            }
+            hw[q] = h;
+            lw[q] = l;
+        }
+        if (k0 + kk0 < K_pad) {
+            int8_t* dh = planes + (((uint64_t)bt * 2 + 0) * cols + c) * K_pad + k0 + kk0;
+            int8_t* dl = planes + (((uint64_t)bt * 2 + 1) * cols + c) * K_pad + k0 + kk0;
+            *(uint4*)dh = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)dl = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+    }
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+    if (j == 0 && c < cols) atomicAdd((unsigned int*)(colterm + (uint64_t)bt * cols + c), (uint32_t)sum * 128u);
+}
+
+__global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
+    const uint64_t rc = (uint64_t)rows * cols;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t z = t / rc, rem = t - z * rc;
+        const uint64_t r = rem / cols, c = rem - r * cols;
+        out[z * out_bs + r * ldo + c] = 0;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// host: tensor maps
+// ---------------------------------------------------------------------------
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// planes [batches][2][rows][K_pad] int8; box {128 k, 128 rows, 2 planes, 1 batch}.
+int make_plane_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t K_pad, uint32_t rows, uint32_t batches) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)base & 15u) != 0 || (K_pad & 15u) != 0) return set_error(CM_EINVAL, "plane buffer misaligned");
+    const cuuint64_t dims[4] = {K, rows, 2, batches};
+    const cuuint64_t strides[3] = {(cuuint64_t)K_pad, (cuuint64_t)rows * K_pad, (cuuint64_t)2 * rows * K_pad};
+    const cuuint32_t box[4] = {(cuuint32_t)BK, (cuuint32_t)BM, 2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CM_OK;
+}
+
+}  // namespace
+
+int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
+    if (p.K == 0) return fill_zero(cx, p.out, p.batch, p.rows, p.cols, p.ldo, p.out_bs, s);
+    if (p.K > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "reduction length %u exceeds %u", p.K, kMaxGemmK);
+    CUtensorMap ta, tb;
+    int rc = make_plane_map(&ta, p.a_planes, p.K, p.K_pad, p.rows, p.a_batches);
+    if (rc) return rc;
+    rc = make_plane_map(&tb, p.b_planes, p.K, p.K_pad, p.cols, p.b_batches);
+    if (rc) return rc;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+        attr_set = true;
+    }
+    GemmArgs g;
+    g.rows = p.rows; g.cols = p.cols; g.num_kb = (p.K + BK - 1) / BK;
+    g.a_batches = p.a_batches; g.b_batches = p.b_batches;
+    g.rowterm = p.rowterm; g.colterm = p.colterm;
+    g.out = p.out; g.ldo = p.ldo; g.out_bs = p.out_bs;
+    g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    const dim3 block(192);
+    for (uint32_t z0 = 0; z0 < p.batch; z0 += 65535u) {
+        const uint32_t nz = min(65535u, p.batch - z0);
+        g.z_base = z0;
+        const dim3 grid((p.cols + BN - 1) / BN, (p.rows + BM - 1) / BM, nz);
+        gemm_q88_kernel<<<grid, block, SMEM_BYTES, s>>>(ta, tb, g);
+        count_launch();
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
+}
+
+int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
+               uint32_t nbt, int8_t* planes, int32_t* rowterm, const int16_t* bias, cudaStream_t s) {
+    const uint64_t total = (uint64_t)rows * nbt;
+    if (total == 0) return CM_OK;
+    const unsigned grid = grid_for(cx, total * 32, 256, 16);
+    split_rows_kernel<<<grid, 256, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
+    count_launch();
+    return CM_OK;
+}
+
+int split_cols(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
+               uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s) {
+    if ((uint64_t)cols * nbt == 0) return CM_OK;
+    cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)cols * nbt * sizeof(int32_t), s);
+    if (e != cudaSuccess) return cuda_error(e, "memset colterm");
+    if (K == 0) return CM_OK;
+    for (uint32_t b0 = 0; b0 < nbt; b0 += 65535u) {
+        const uint32_t nb = min(65535u, nbt - b0);
+        const dim3 grid((K + 63) / 64, (cols + 63) / 64, nb);
+        MatSrc m{src + (uint64_t)b0 * src_bs, src_bs, ld};
+        split_cols_kernel<MatSrc><<<grid, 256, 0, s>>>(m, cols, K, pad_k(K),
+                                                      planes + (uint64_t)b0 * 2 * cols * pad_k(K),
+                                                      colterm + (uint64_t)b0 * cols);
+        count_launch();
+    }
+    return CM_OK;
+}
+
+int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_t nimg, int8_t* planes,
+                 int32_t* colterm, cudaStream_t s) {
+    const uint32_t P = g.out_h * g.out_w;
+    const uint32_t K = g.C * g.kh * g.kw;
+    if ((uint64_t)P * nimg == 0) return CM_OK;
+    cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)P * nimg * sizeof(int32_t), s);
+    if (e != cudaSuccess) return cuda_error(e, "memset colterm");
+    if (K == 0) return CM_OK;
+    Im2colSrc src;
+    src.g = g;
+    src.khw = g.kh * g.kw;
+    src.fd_khw = FastDiv(src.khw);
+    src.fd_kw = FastDiv(g.kw);
+    src.fd_ow = FastDiv(g.out_w);
+    for (uint32_t n0 = 0; n0 < nimg; n0 += 65535u) {
+        const uint32_t nb = min(65535u, nimg - n0);
+        src.x = x + (uint64_t)n0 * g.C * g.H * g.W;
+        const dim3 grid((K + 63) / 64, (P + 63) / 64, nb);
+        split_cols_kernel<Im2colSrc><<<grid, 256, 0, s>>>(src, P, K, pad_k(K), planes + (uint64_t)n0 * 2 * P * pad_k(K),
+                                                          colterm + (uint64_t)n0 * P);
+        count_launch();
+    }
+    return CM_OK;
+}
+
+int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, uint32_t cols, uint64_t ldo,
+              uint64_t out_bs, cudaStream_t s) {
+    const uint64_t total = (uint64_t)batch * rows * cols;
+    if (total == 0) return CM_OK;
+    fill_zero_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(out, rows, cols, ldo, out_bs, total);
+    count_launch();
+    return CM_OK;
+}
+
+}  // namespace cm
+
+using namespace cm;
+
+// ---------------------------------------------------------------------------
+// MatmulKernel entry (MatmulKernel.h:68-79)
+// ---------------------------------------------------------------------------
+extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                               unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                               unsigned c_batch_stride, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (n == 0 || m == 0 || batch == 0) return CM_OK;
+    if (!c || (k > 0 && (!a || !b))) return set_error(CM_EINVAL, "cm_matmul: null buffer");
+    cudaStream_t s = (cudaStream_t)stream;
+    if (batch > 1 && (uint64_t)c_batch_stride < (uint64_t)n * m) {
+        // Output slices of different batch steps overlap; the reference's batch
+        // loop runs in order (MatmulKernel.cpp:108-112), so later steps win.
+        if (c_batch_stride == 0) {
+            const uint64_t last = batch - 1;
+            return cm_matmul_async(a ? a + last * a_batch_stride : a, b ? b + last * b_batch_stride : b, c, n, k,
+                                   m, 1, a_batch_stride, b_batch_stride, 0, stream);
+        }
+        for (uint64_t bi = 0; bi < batch; ++bi) {
+            rc = cm_matmul_async(a ? a + bi * a_batch_stride : a, b ? b + bi * b_batch_stride : b,
+                                 c + bi * c_batch_stride, n, k, m, 1, a_batch_stride, b_batch_stride, 0, stream);
+            if (rc) return rc;
+        }
+        return CM_OK;
+    }
+    if (k == 0) return fill_zero(cx, c, batch, n, m, m, c_batch_stride, s);
+    if (k > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_matmul: k = %u exceeds %u", k, kMaxGemmK);
+    const uint32_t a_batches = a_batch_stride == 0 ? 1u : batch;
+    const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;
+    const uint64_t K_pad = pad_k(k);
+    const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * m * K_pad + 255) & ~255ull;
+    const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)b_batches * m * 4 + 255) & ~255ull;
+    void* scratch = nullptr;
+    rc = scratch_alloc(&scratch, a_bytes + b_bytes + rt_bytes + ct_bytes, s);
+    if (rc) return rc;
+    int8_t* ap = (int8_t*)scratch;
+    int8_t* bp = ap + a_bytes;
+    int32_t* rt = (int32_t*)(bp + b_bytes);
+    int32_t* ct = (int32_t*)((uint8_t*)rt + rt_bytes);
+    rc = split_rows(cx, a, a_batch_stride, k, n, k, a_batches, ap, rt, nullptr, s);
+    if (!rc) rc = split_cols(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s);
+    if (!rc) {
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, rt, ct, c, m, c_batch_stride, batch};
+        rc = gemm_launch(cx, p, s);
+    }
+    scratch_free(scratch, s);
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul");
+}
+
+extern "C" int cm_matmul(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                         unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride) {
+    int rc = cm_matmul_async(a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
+extern "C" int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, unsigned b_off, int16_t* c,
+                            unsigned c_off, unsigned n, unsigned k, unsigned m, unsigned batch,
+                            unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride) {
+    return cm_matmul(a ? a + a_off : a, b ? b + b_off : b, c ? c + c_off : c, n, k, m, batch, a_batch_stride,
+                     b_batch_stride, c_batch_stride);
+}

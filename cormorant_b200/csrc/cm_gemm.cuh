@@ -1,0 +1,57 @@
+// cm_gemm.cuh -- the Q8.8 tensor-core GEMM shared by MatMul and Conv.
+//
+// Data layout in HBM (all produced by the split pre-passes in cm_gemm.cu):
+//   A planes  [a_batches][2][rows][K_pad] int8   row-major over K (K-major)
+//   B planes  [b_batches][2][cols][K_pad] int8   (B^T: one row per output column)
+//   plane 0 = hi = x >> 8 (signed), plane 1 = lo' = (x & 255) - 128 (signed)
+//   rowterm   [a_batches][rows] int32, colterm [b_batches][cols] int32
+//   out[z*out_bs + row*ldo + col] = sat16(floor(acc / 256)), with
+//   acc = 2^16*HH + 2^8*(HL + LH) + LL + rowterm[row] + colterm[col]  (mod 2^32)
+// which equals the exact sum of int16 products (see cm_gemm.cu).
+#pragma once
+
+#include "cm_common.cuh"
+
+namespace cm {
+
+struct GemmPlan {
+    const int8_t* a_planes; uint32_t rows; uint32_t a_batches;
+    const int8_t* b_planes; uint32_t cols; uint32_t b_batches;
+    uint32_t K, K_pad;
+    const int32_t* rowterm;
+    const int32_t* colterm;
+    int16_t* out; uint64_t ldo, out_bs;
+    uint32_t batch;
+};
+
+constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude
+
+inline uint32_t pad_k(uint32_t K) { return (K + 15u) & ~15u; }
+
+// Launch the tcgen05 GEMM (all arguments device-resident, stream-ordered).
+int gemm_launch(const Context* cx, const GemmPlan& g, cudaStream_t s);
+
+// Split int16 rows into hi/lo planes + row terms:
+//   element (bt, r, k) = src[bt*src_bs + r*ld + k], r < rows, k < K, bt < nbt;
+//   rowterm[bt*rows + r] = 128*sum_k(x - 128) + 16384*K + (bias ? bias[r] << 8 : 0).
+int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
+               uint32_t nbt, int8_t* planes, int32_t* rowterm, const int16_t* bias, cudaStream_t s);
+
+// Split + transpose int16 matrix columns into hi/lo planes + column terms:
+//   element (bt, k, c) = src[bt*src_bs + k*ld + c], c < cols, k < K;
+//   colterm[bt*cols + c] = 128*sum_k(x - 128).
+int split_cols(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
+               uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s);
+
+// im2col + split for ConvKernel: column p = oh*out_w + ow of image n, row k = (c, r, s).
+struct ConvGeom {
+    uint32_t C, H, W, out_h, out_w, kh, kw, sh, sw, dh, dw, pt, pl;
+};
+int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_t nimg, int8_t* planes,
+                 int32_t* colterm, cudaStream_t s);
+
+// Zero-fill out[z*out_bs + r*ldo + c] (the K == 0 case: an empty sum narrows to 0).
+int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, uint32_t cols, uint64_t ldo,
+              uint64_t out_bs, cudaStream_t s);
+
+}  // namespace cm

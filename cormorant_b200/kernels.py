@@ -1,0 +1,98 @@
+"""Host-side mirror of the reference kernel interface.
+
+The four functions keep the names, argument order and meaning of the
+reference kernels (kernels/*/include/*.h) with buffers given as device int16
+tensors (or raw device addresses as ints).  Without ``stream`` a call blocks
+until the kernel is done, like the reference's Start + ``while (!IsDone)``
+helpers (inference-scheduler/src/codegen/_source.py:208-217); with ``stream``
+(a ``torch.cuda.Stream`` or a raw ``cudaStream_t`` int) it is enqueued and
+returns at once.  Failures raise ``CormorantError``; there is no CPU path.
+"""
+from __future__ import annotations
+
+from typing import Any
+
+from ._lib import CormorantError, check, lib  # noqa: F401
+
+OP_ADD, OP_SUB, OP_MUL, OP_DIV, OP_RELU, OP_RELU6 = range(6)   # VectorOP.h:50-57
+POOL_MAX, POOL_AVG, POOL_LP = 0, 1, 2                          # pool Config.h.in:47-49
+
+
+def _addr(t: Any) -> int | None:
+    """Device address of a torch tensor (int16, CUDA) or a raw int; None stays None."""
+    if t is None:
+        return None
+    if isinstance(t, int):
+        return t
+    if getattr(t, "is_cuda", False):
+        if str(t.dtype) not in ("torch.int16", "torch.uint16"):
+            raise TypeError(f"expected an int16 tensor, got {t.dtype}")
+        return int(t.data_ptr())
+    raise TypeError("buffers must be CUDA tensors or device addresses")
+
+
+def _stream(s: Any) -> int | None:
+    if s is None:
+        return None
+    if isinstance(s, int):
+        return s
+    return int(s.cuda_stream)
+
+
+def init(instance: str | int = "0") -> None:
+    """Select the device (X<Kernel>_Initialize analogue, _source.py:602-608)."""
+    check(lib().cm_init(str(instance).encode()))
+
+
+def release() -> None:
+    check(lib().cm_release())
+
+
+def synchronize(stream: Any = None) -> None:
+    check(lib().cm_synchronize(_stream(stream)))
+
+
+def launch_count() -> int:
+    return int(lib().cm_launch_count())
+
+
+def VectorOPKernel(a, b, c, size, op, outer=1, a_inc=0, b_inc=0, stream=None) -> None:
+    """c[o*(a_inc+b_inc)+i] = op(a[o*a_inc+i], b[o*b_inc+i]) -- VectorOP.h:86-95."""
+    L = lib()
+    args = (_addr(a), _addr(b), _addr(c), size, op, outer, a_inc, b_inc)
+    check(L.cm_vectorop(*args) if stream is None else L.cm_vectorop_async(*args, _stream(stream)))
+
+
+def MatmulKernel(a, b, c, n, k, m, batch=1, a_batch_stride=None, b_batch_stride=None, c_batch_stride=None,
+                 stream=None) -> None:
+    """Batched Q8.8 GEMM C[n][m] = A[n][k] x B[k][m] -- MatmulKernel.h:68-79.
+
+    Omitted strides default to the dense packing (n*k, k*m, n*m)."""
+    a_bs = n * k if a_batch_stride is None else a_batch_stride
+    b_bs = k * m if b_batch_stride is None else b_batch_stride
+    c_bs = n * m if c_batch_stride is None else c_batch_stride
+    L = lib()
+    args = (_addr(a), _addr(b), _addr(c), n, k, m, batch, a_bs, b_bs, c_bs)
+    check(L.cm_matmul(*args) if stream is None else L.cm_matmul_async(*args, _stream(stream)))
+
+
+def ConvKernel(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1,
+               stride_w=1, dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=None, is_depthwise=0,
+               stream=None) -> None:
+    """NCHW 2-D convolution -- ConvKernel.h:79-101."""
+    if has_bias is None:
+        has_bias = int(bias is not None)
+    L = lib()
+    args = (_addr(x), _addr(weight), _addr(bias), _addr(y), batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+            stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, int(has_bias), int(is_depthwise))
+    check(L.cm_conv(*args) if stream is None else L.cm_conv_async(*args, _stream(stream)))
+
+
+def PoolingKernel(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
+                  pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, lp_order=2, count_include_pad=0,
+                  stream=None) -> None:
+    """Max / Average / Lp pooling and their Global variants -- PoolingKernel.h:63-83."""
+    L = lib()
+    args = (_addr(x), _addr(y), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+            pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
+    check(L.cm_pool(*args) if stream is None else L.cm_pool_async(*args, _stream(stream)))

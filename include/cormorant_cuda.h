@@ -1,0 +1,164 @@
+/*
+ * cormorant_cuda.h -- C ABI of libcormorant_cuda.so, the B200 (sm_100a)
+ * implementation of Cormorant's four Q8.8 kernels.
+ *
+ * Every kernel entry keeps the reference kernel's argument list, order and
+ * meaning; only the buffer arguments change from "physical DDR address
+ * programmed into an AXI-Lite register" to "CUDA device pointer".  Data are
+ * raw ap_fixed<16,8> words (int16, value = raw / 256); outputs are bit-exact
+ * with the reference C-simulation.
+ *
+ * Reference interfaces replaced (paths relative to the reference project):
+ *   cm_vectorop  <- VectorOPKernel   kernels/vectorop/include/VectorOP.h:86-95,
+ *                   programmed by run_op()       inference-scheduler/src/codegen/_source.py:175-217
+ *   cm_matmul    <- MatmulKernel     kernels/matmul/include/MatmulKernel.h:68-79,
+ *                   programmed by run_matmul()   _source.py:220-258
+ *   cm_matmul_at <- run_matmul_at()  _source.py:261-299 (element offsets added to a/b/c)
+ *   cm_conv      <- ConvKernel       kernels/conv/include/ConvKernel.h:79-101,
+ *                   programmed by run_conv()     _source.py:302-362
+ *   cm_pool      <- PoolingKernel    kernels/pool/include/PoolingKernel.h:63-83,
+ *                   programmed by run_pool()     _source.py:365-420
+ *   cm_init / cm_release  <- X<Kernel>_Initialize(&inst, name) / X<Kernel>_Release
+ *                   (_source.py:602-634: int rc, 0 = OK)
+ *   cm_buf_*     <- inference_buf_*  inference-scheduler/src/codegen/_buf_impl.py:25-236
+ *                   ("phys" becomes the device address)
+ *
+ * Conventions
+ *   - Every call returns CM_OK (0) or a negative CM_E* code; nothing aborts or
+ *     throws across the ABI.  cm_last_error() describes the last failure of
+ *     the calling thread.
+ *   - The plain entry points are synchronous, like the reference's
+ *     Start + while(!IsDone) helpers: they return after the work is complete
+ *     and report device-side errors.  The *_async twins enqueue on `stream`
+ *     (a cudaStream_t; NULL = legacy default stream) and return at once;
+ *     cm_synchronize(stream) waits and reports device-side errors.
+ *   - `b` (unary ops) and `bias` (has_bias == 0) may be NULL, as in the reference.
+ *   - The caller owns every input/output buffer.  Scratch for the tensor-core
+ *     kernels comes from the device's stream-ordered memory pool on the call's
+ *     stream, so concurrent calls on different streams do not share scratch.
+ */
+#ifndef CORMORANT_CUDA_H
+#define CORMORANT_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+#define CM_OK            0
+#define CM_EINVAL       (-1)  /* bad argument (null pointer, size overflow, ...) */
+#define CM_EUNSUPPORTED (-2)  /* valid for the reference but not implemented here */
+#define CM_ECUDA        (-3)  /* a CUDA runtime/driver call failed */
+#define CM_ETIMEOUT     (-4)  /* a device-side bounded wait expired; the kernel returned early */
+#define CM_ENOMEM       (-5)  /* device or pinned-host allocation failed */
+#define CM_ENOINIT      (-6)  /* cm_init has not succeeded in this process */
+
+/* ---- operation codes (VectorOP.h:50-57, PoolingKernel Config.h.in:35-51) -- */
+#define CM_OP_ADD   0u
+#define CM_OP_SUB   1u
+#define CM_OP_MUL   2u
+#define CM_OP_DIV   3u
+#define CM_OP_RELU  4u
+#define CM_OP_RELU6 5u
+#define CM_POOL_MAX 0u
+#define CM_POOL_AVG 1u
+#define CM_POOL_LP  2u
+
+typedef void* cm_stream_t; /* cudaStream_t */
+
+/* ---- lifecycle ------------------------------------------------------------ */
+/* instance: device ordinal as text ("0", "cuda:1"); NULL or "" = device 0.
+ * Mirrors X<Kernel>_Initialize(&inst, "<uio name>") (_source.py:602-608). */
+int cm_init(const char* instance);
+int cm_release(void);
+int cm_device(void);                          /* ordinal chosen by cm_init, or CM_ENOINIT */
+const char* cm_strerror(int status);
+const char* cm_last_error(void);
+int cm_synchronize(cm_stream_t stream);       /* wait, then read + clear the device status word */
+uint64_t cm_launch_count(void);               /* kernels launched by this library so far */
+const char* cm_version(void);
+
+/* ---- VectorOPKernel ----------------------------------------------------------
+ * c[o*(a_inc+b_inc) + i] = op(a[o*a_inc + i], b[o*b_inc + i]),  o < outer, i < size.
+ * op: CM_OP_*; any other value copies a (VectorOP.cpp:108). */
+int cm_vectorop(const int16_t* a, const int16_t* b, int16_t* c, unsigned size, unsigned op,
+                unsigned outer, unsigned a_inc, unsigned b_inc);
+int cm_vectorop_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned size, unsigned op,
+                      unsigned outer, unsigned a_inc, unsigned b_inc, cm_stream_t stream);
+
+/* ---- MatmulKernel --------------------------------------------------------------
+ * c[bi*c_bs + r*m + j] = sat(floor((sum_t a[bi*a_bs + r*k + t] * b[bi*b_bs + t*m + j]) / 256)),
+ * accumulated in int32 modulo 2^32; a stride of 0 broadcasts that operand. */
+int cm_matmul(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+              unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+              unsigned c_batch_stride);
+int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k,
+                    unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                    unsigned c_batch_stride, cm_stream_t stream);
+/* run_matmul_at(): the same call with element offsets applied to each buffer. */
+int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, unsigned b_off, int16_t* c,
+                 unsigned c_off, unsigned n, unsigned k, unsigned m, unsigned batch,
+                 unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride);
+
+/* ---- ConvKernel ----------------------------------------------------------------
+ * NCHW conv; weights [out_ch][in_ch][kh][kw] (depthwise: [out_ch][1][kh][kw],
+ * input channel = output channel); out-of-range input taps read 0; bias[m]
+ * initialises the accumulator as bias << 8. */
+int cm_conv(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+            unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+            unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+            unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+            unsigned pad_left, unsigned has_bias, unsigned is_depthwise);
+int cm_conv_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+                  unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                  unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                  unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                  unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
+                  cm_stream_t stream);
+
+/* ---- PoolingKernel -------------------------------------------------------------
+ * pool_type CM_POOL_MAX / AVG / LP (any value >= 2 is LP); lp_order 1 = sum|x|,
+ * any other value = sqrt(sum x^2); count_include_pad selects the AVG divisor. */
+int cm_pool(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+            unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+            unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+            unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+            unsigned count_include_pad);
+int cm_pool_async(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+                  unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                  unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                  unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                  unsigned count_include_pad, cm_stream_t stream);
+
+/* ---- buffers: mirror of inference_buf_* (_buf_impl.py:25-236) ------------------
+ * An owner buffer is a device allocation plus a pinned host mirror of the same
+ * size; views alias a slice of an owner.  `virt` is the host mirror, `dev` the
+ * device address handed to the kernels (the reference's "phys"). */
+typedef struct cm_buf {
+    void*    virt;
+    uint64_t dev;
+    unsigned count;      /* elements (int16 words) */
+    unsigned refcount;
+    unsigned is_owner;
+    int      device;
+} cm_buf_t;
+
+cm_buf_t* cm_buf_alloc(unsigned n_elem);
+void      cm_buf_free(cm_buf_t* buf);
+void      cm_buf_retain(cm_buf_t* buf);
+void      cm_buf_release(cm_buf_t* buf);
+int16_t*  cm_buf_ptr(cm_buf_t* buf);
+uint64_t  cm_buf_dev(const cm_buf_t* buf);
+unsigned  cm_buf_count(const cm_buf_t* buf);
+void      cm_buf_init_view(cm_buf_t* view, cm_buf_t* base, unsigned offset_elems,
+                           unsigned count_elems);
+int       cm_buf_sync_to_device(cm_buf_t* buf);
+int       cm_buf_sync_from_device(cm_buf_t* buf);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CORMORANT_CUDA_H */

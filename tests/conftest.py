@@ -1,0 +1,35 @@
+"""Shared pytest configuration: the `gpu` marker and common fixtures.
+
+`-m "not gpu"` runs the CPU suite (oracle vs reference vs golden vectors,
+host logic, C-ABI exports); `-m gpu` runs the parity tests on a B200 through
+the C ABI of libcormorant_cuda.so.
+"""
+import os
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 GPU (sm_100a)")
+
+
+@pytest.fixture(scope="session")
+def port():
+    import oracle
+    p = oracle.port()
+    p.set_threads(min(os.cpu_count() or 1, 64))
+    return p
+
+
+@pytest.fixture(scope="session")
+def cm():
+    """The product library, initialised on cuda:0 (GPU tests only)."""
+    import cormorant_b200 as cmb
+    cmb.init("0")
+    return cmb

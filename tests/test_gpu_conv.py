@@ -1,0 +1,111 @@
+"""ConvKernel parity on the GPU: cm_conv (im2col split + tcgen05 GEMM; depthwise on
+CUDA cores) vs the C restatement, bit-exact on raw int16 words.
+
+The case list mirrors the reference's TestConvSim.cpp:284-628 geometries
+(1x1, 3x3 with/without padding, stride 2, bias, batch, partial channel tiles,
+dilation, 5x5, multi-tile, non-square, asymmetric padding, depthwise variants,
+saturation), then adds the LeNet and ResNet-18 layer shapes of the BASELINE
+configs and edge cases (empty reduction, wide reductions, full-range data).
+"""
+import numpy as np
+import pytest
+
+from tests._util import assert_same, dev, empty, host, rand16
+
+pytestmark = pytest.mark.gpu
+
+
+def osz(n, k, s, d, p0, p1):
+    return (n + p0 + p1 - (d * (k - 1) + 1)) // s + 1
+
+
+# (N, C, H, W, M, kh, kw, sh, sw, dh, dw, pt, pl, pb, pr, bias, dw_mode)
+REF_CASES = [
+    (1, 1, 5, 5, 1, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0, 0, 0),
+    (1, 1, 5, 5, 1, 3, 3, 1, 1, 1, 1, 0, 0, 0, 0, 0, 0),
+    (1, 1, 5, 5, 1, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),
+    (1, 1, 6, 6, 1, 3, 3, 2, 2, 1, 1, 0, 0, 0, 0, 0, 0),
+    (1, 1, 5, 5, 2, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 1, 5, 5, 1, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),
+    (1, 21, 5, 5, 1, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),
+    (1, 1, 5, 5, 11, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (1, 1, 9, 9, 1, 3, 3, 1, 1, 2, 2, 0, 0, 0, 0, 0, 0),
+    (1, 1, 7, 7, 1, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0, 0, 0),
+    (1, 35, 14, 14, 17, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (1, 1, 6, 8, 2, 3, 5, 1, 1, 1, 1, 0, 0, 0, 0, 0, 0),
+    (1, 1, 7, 7, 1, 3, 3, 2, 2, 1, 1, 1, 1, 0, 0, 0, 0),
+    (1, 4, 8, 8, 4, 3, 3, 1, 1, 1, 1, 0, 0, 0, 0, 0, 1),
+    (1, 4, 8, 8, 4, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),
+    (1, 11, 6, 6, 11, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 1),
+    (1, 4, 9, 9, 4, 3, 3, 1, 1, 2, 2, 0, 0, 0, 0, 0, 1),
+    (1, 8, 8, 8, 8, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 0, 1),
+    # LeNet-5 layers (config 0) and ResNet-18 layer shapes (config 3) at small batch
+    (1, 1, 28, 28, 6, 5, 5, 1, 1, 1, 1, 2, 2, 2, 2, 1, 0),
+    (1, 6, 14, 14, 16, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+    (2, 3, 224, 224, 64, 7, 7, 2, 2, 1, 1, 3, 3, 3, 3, 1, 0),
+    (2, 64, 56, 56, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 64, 56, 56, 128, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 64, 56, 56, 128, 1, 1, 2, 2, 1, 1, 0, 0, 0, 0, 1, 0),
+    (2, 256, 14, 14, 512, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 512, 7, 7, 512, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    # odd shapes: K not a multiple of 16, stride > kernel, dilation with padding
+    (3, 5, 13, 11, 7, 2, 3, 3, 2, 2, 3, 1, 2, 0, 1, 1, 0),
+    (1, 130, 9, 9, 129, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+]
+
+
+def run(cm, port, case, dist, seed):
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    rng = np.random.default_rng(seed)
+    lo, hi = (-256, 256) if dist == "q8" else (-32768, 32768)
+    x = rand16(rng, N * C * H * W, lo, hi)
+    w = rand16(rng, M * (1 if dwm else C) * kh * kw, lo, hi)
+    bias = rand16(rng, M, lo, hi)
+    y = empty(N * M * oh * ow)
+    cm.ConvKernel(dev(x), dev(w), dev(bias) if hb else None, y, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt,
+                  pl, hb, dwm)
+    want = port.conv(x, w, bias if hb else None, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)
+    assert_same(host(y), want, f"case {case} {dist}")
+
+
+@pytest.mark.parametrize("case", REF_CASES)
+@pytest.mark.parametrize("dist", ["q8", "full"])
+def test_cases(cm, port, case, dist):
+    run(cm, port, case, dist, seed=sum(case) * 13 + (dist == "full"))
+
+
+@pytest.mark.parametrize("w_val,b_val,sat", [(256, 32767, 32767), (-256, -32768, -32768)])
+def test_saturation(cm, port, w_val, b_val, sat):
+    """TestConvSim.cpp:594-628: x = AP_MAX, w = +-1.0, bias = AP_MAX / AP_MIN saturates."""
+    x = np.full(9, 32767, np.int16)
+    w = np.array([w_val], np.int16)
+    b = np.array([b_val], np.int16)
+    y = empty(9)
+    cm.ConvKernel(dev(x), dev(w), dev(b), y, 1, 1, 3, 3, 1, 3, 3, 1, 1)
+    got = host(y)
+    assert (got == sat).all()
+    assert_same(got, port.conv(x, w, b, 1, 1, 3, 3, 1, 3, 3, 1, 1), "saturation")
+
+
+def test_empty_reduction_writes_bias(cm, port):
+    b = np.array([5, -7, 300], np.int16)
+    y = empty(2 * 3 * 4)
+    cm.ConvKernel(dev(np.zeros(1, np.int16)), dev(np.zeros(1, np.int16)), dev(b), y, 2, 0, 2, 2, 3, 2, 2, 1, 1)
+    assert_same(host(y), np.tile(np.repeat(b, 4), 2), "in_ch = 0")
+
+
+def test_resnet_conv1_batch8_sampled(cm, port):
+    """ResNet-18 stem at batch 8 (chunked im2col), checked plane by plane for a sample of (n, m)."""
+    N, C, H, W, M = 8, 3, 224, 224, 64
+    rng = np.random.default_rng(77)
+    x = rand16(rng, N * C * H * W, 0, 256)
+    w = rand16(rng, M * C * 49, -128, 128)
+    bias = rand16(rng, M, -64, 64)
+    y = empty(N * M * 112 * 112)
+    cm.ConvKernel(dev(x), dev(w), dev(bias), y, N, C, H, W, M, 112, 112, 7, 7, 2, 2, 1, 1, 3, 3, 1, 0)
+    nidx = rng.integers(0, N, 24)
+    midx = rng.integers(0, M, 24)
+    want = port.conv_planes(x, w, bias, C, H, W, M, 112, 112, 7, 7, 2, 2, 1, 1, 3, 3, 1, 0, nidx, midx)
+    got = host(y).reshape(N, M, -1)[nidx, midx]
+    assert_same(got, want, "stem sampled planes")

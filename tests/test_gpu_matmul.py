@@ -1,0 +1,129 @@
+"""MatmulKernel parity on the GPU: cm_matmul (tcgen05 int8 byte-split) vs the oracle.
+
+Bit-exact on raw int16 words.  Shapes follow the reference's own test matrix
+(TestMatmulSim.cpp:276-349: unit dims, partial tiles in every dimension,
+multi-tile, batch with A or B broadcast), its saturation KATs
+(TestMatmulSim.cpp:364-367), accumulator wrap with full-range operands, the
+K == 0 and overlapping-output edge cases, and every BASELINE sweep shape
+(full compare at 256^3, sampled rows at the larger shapes).
+"""
+import numpy as np
+import pytest
+
+from tests._util import assert_same, dev, empty, host, rand16
+
+pytestmark = pytest.mark.gpu
+
+# (n, k, m, batch) -- TILE_N=4, TILE_K=256, TILE_M=16 in the reference; 128-tiles here
+SHAPES = [(1, 1, 1, 1), (4, 256, 16, 1), (8, 256, 16, 1), (4, 512, 16, 1), (4, 256, 32, 1), (6, 256, 16, 1),
+          (4, 261, 16, 1), (4, 256, 19, 1), (6, 261, 19, 1), (7, 13, 5, 1), (5, 1, 17, 1), (1, 256, 16, 1),
+          (4, 256, 1, 1), (12, 519, 33, 1), (128, 128, 128, 1), (129, 130, 131, 2), (255, 257, 383, 3),
+          (1, 400, 120, 1), (1, 120, 84, 1), (1, 84, 10, 1), (256, 512, 1000, 1), (300, 17, 200, 4),
+          (64, 32, 64, 5), (33, 4096, 65, 1)]
+
+
+@pytest.mark.parametrize("n,k,m,batch", SHAPES)
+@pytest.mark.parametrize("dist", ["q8", "full"])
+def test_shapes(cm, port, n, k, m, batch, dist):
+    rng = np.random.default_rng(n * 7919 + k * 31 + m + batch)
+    lo, hi = (-1024, 1024) if dist == "q8" else (-32768, 32768)
+    a = rand16(rng, batch * n * k, lo, hi)
+    b = rand16(rng, batch * k * m, lo, hi)
+    c = empty(batch * n * m)
+    cm.MatmulKernel(dev(a), dev(b), c, n, k, m, batch)
+    assert_same(host(c), port.matmul(a, b, n, k, m, batch), f"{n}x{k}x{m} b{batch} {dist}")
+
+
+@pytest.mark.parametrize("a_bs,b_bs", [(0, None), (None, 0), (0, 0)])
+def test_broadcast(cm, port, a_bs, b_bs):
+    n, k, m, batch = 5, 64, 19, 4
+    rng = np.random.default_rng(11)
+    a_bs = n * k if a_bs is None else a_bs
+    b_bs = k * m if b_bs is None else b_bs
+    a = rand16(rng, max((batch - 1) * a_bs + n * k, 1))
+    b = rand16(rng, max((batch - 1) * b_bs + k * m, 1))
+    c = empty(batch * n * m)
+    cm.MatmulKernel(dev(a), dev(b), c, n, k, m, batch, a_bs, b_bs, n * m)
+    assert_same(host(c), port.matmul(a, b, n, k, m, batch, a_bs, b_bs, n * m), f"strides {a_bs},{b_bs}")
+
+
+@pytest.mark.parametrize("a_val,b_val,sat", [(25600, 25600, 32767), (25600, -25600, -32768)])
+def test_saturation_kat(cm, port, a_val, b_val, sat):
+    """a = 100.0, b = +-100.0, K = 3: 30000.0 saturates to AP_MAX / AP_MIN."""
+    n, k, m = 4, 3, 16
+    a = np.full(n * k, a_val, np.int16)
+    b = np.full(k * m, b_val, np.int16)
+    c = empty(n * m)
+    cm.MatmulKernel(dev(a), dev(b), c, n, k, m)
+    got = host(c)
+    assert (got == sat).all()
+    assert_same(got, port.matmul(a, b, n, k, m), "saturation")
+
+
+def test_accumulator_wrap(cm, port):
+    """Sums past +-2^31 at Q16.16 wrap (AP_WRAP) before the single saturating narrow."""
+    n, k, m = 16, 4096, 48
+    a = np.full(n * k, 32767, np.int16)
+    b = np.full(k * m, 32767, np.int16)
+    a[::2] = -32768
+    c = empty(n * m)
+    cm.MatmulKernel(dev(a), dev(b), c, n, k, m)
+    assert_same(host(c), port.matmul(a, b, n, k, m), "wrap")
+
+
+def test_k_zero_writes_zeros(cm, port):
+    c = empty(3 * 5 * 2)
+    cm.MatmulKernel(dev(np.zeros(1, np.int16)), dev(np.zeros(1, np.int16)), c, 3, 0, 5, 2, 0, 0, 15)
+    assert (host(c) == 0).all()
+
+
+def test_overlapping_output_batches(cm, port):
+    """c_batch_stride < n*m: later batch steps overwrite earlier ones, as in the reference loop."""
+    n, k, m, batch = 4, 40, 8, 3
+    rng = np.random.default_rng(5)
+    a = rand16(rng, batch * n * k)
+    b = rand16(rng, batch * k * m)
+    for c_bs in (0, 8, 20):
+        c_len = (batch - 1) * c_bs + n * m
+        init = np.full(c_len, -23131, np.int16)
+        c = dev(init)
+        cm.MatmulKernel(dev(a), dev(b), c, n, k, m, batch, n * k, k * m, c_bs)
+        assert_same(host(c), port.matmul(a, b, n, k, m, batch, n * k, k * m, c_bs, c=init.copy()), f"c_bs={c_bs}")
+
+
+def test_strided_offsets(cm, port):
+    """run_matmul_at-style element offsets that break 16-byte alignment of every operand."""
+    n, k, m, batch = 9, 37, 23, 2
+    rng = np.random.default_rng(9)
+    A = rand16(rng, batch * n * k + 3)
+    B = rand16(rng, batch * k * m + 5)
+    c = empty(batch * n * m + 7)
+    ta, tb = dev(A), dev(B)
+    cm.MatmulKernel(ta[3:], tb[5:], c[7:], n, k, m, batch)
+    assert_same(host(c)[7:], port.matmul(A[3:], B[5:], n, k, m, batch), "offsets")
+
+
+SWEEP = [(256, 256, 256, 64), (1024, 1024, 1024, 64), (4096, 4096, 4096, 64), (8192, 4096, 11008, 8)]
+
+
+@pytest.mark.parametrize("n,k,m,batch", SWEEP)
+def test_sweep_shapes(cm, port, n, k, m, batch):
+    """BASELINE MatMul sweep: raw int16 uniform [-1024, 1024), seeded; sampled rows when large."""
+    import torch
+    rng = np.random.default_rng(42 + 2 + n)
+    gen = torch.Generator(device="cpu").manual_seed(n * 31 + k)
+    a = torch.randint(-1024, 1024, (batch * n * k,), dtype=torch.int16, generator=gen)
+    b = torch.randint(-1024, 1024, (batch * k * m,), dtype=torch.int16, generator=gen)
+    c = empty(batch * n * m)
+    cm.MatmulKernel(a.cuda(), b.cuda(), c, n, k, m, batch)
+    an, bn = a.numpy(), b.numpy()
+    if n * k * m * batch <= (1 << 30):
+        assert_same(host(c), port.matmul(an, bn, n, k, m, batch), "sweep full")
+        return
+    rows = 96
+    bidx = rng.integers(0, batch, rows)
+    ridx = rng.integers(0, n, rows)
+    bidx[0], ridx[0] = batch - 1, n - 1
+    want = port.matmul_rows(an, bn, n, k, m, n * k, k * m, bidx, ridx)
+    got = host(c).reshape(batch, n, m)[bidx, ridx]
+    assert_same(got, want, f"sweep {n}x{k}x{m} b{batch} sampled rows")
