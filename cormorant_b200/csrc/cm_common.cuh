@@ -29,6 +29,15 @@ int finish_sync(cm_stream_t stream); // synchronize + read/clear the status word
 int scratch_alloc(void** p, size_t bytes, cudaStream_t s);
 void scratch_free(void* p, cudaStream_t s);
 
+// Opt-in device timing of the library's own launches: CUDA events recorded on
+// the launch stream around each kernel while profiling is on (cm_profile_*).
+enum ProfKind { PK_GEMM = 0, PK_SPLIT, PK_VECTOROP, PK_POOL, PK_CONV_AUX, PK_COUNT };
+struct ProfScope {
+    int kind; cudaStream_t s; cudaEvent_t a = nullptr;
+    ProfScope(int k, cudaStream_t st);
+    ~ProfScope();
+};
+
 // Grid size for a grid-stride kernel: a multiple of the SM count.
 inline unsigned grid_for(const Context* c, uint64_t work_items, unsigned block, unsigned per_sm) {
     const uint64_t need = (work_items + block - 1) / block;

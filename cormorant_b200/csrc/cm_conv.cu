@@ -84,7 +84,10 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         if ((uint64_t)kh * kw > 0 && (!x || !weight)) return set_error(CM_EINVAL, "cm_conv: null buffer");
         DwArgs a{in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
                  has_bias ? 1u : 0u};
-        conv_depthwise_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total);
+        {
+            ProfScope ps_(PK_CONV_AUX, s);
+            conv_depthwise_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total);
+        }
         count_launch();
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv depthwise");
@@ -92,7 +95,10 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
 
     const uint64_t K64 = (uint64_t)in_ch * kh * kw;
     if (K64 == 0) {
-        conv_bias_fill_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(bias, y, out_ch, P, total, has_bias ? 1u : 0u);
+        {
+            ProfScope ps_(PK_CONV_AUX, s);
+            conv_bias_fill_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(bias, y, out_ch, P, total, has_bias ? 1u : 0u);
+        }
         count_launch();
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv bias fill");

@@ -497,7 +497,10 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
         const uint32_t nz = min(65535u, p.batch - z0);
         g.z_base = z0;
         const dim3 grid((p.cols + BN - 1) / BN, (p.rows + BM - 1) / BM, nz);
-        gemm_q88_kernel<<<grid, block, SMEM_BYTES, s>>>(ta, tb, g);
+        {
+            ProfScope ps_(PK_GEMM, s);
+            gemm_q88_kernel<<<grid, block, SMEM_BYTES, s>>>(ta, tb, g);
+        }
         count_launch();
     }
     cudaError_t e = cudaGetLastError();
@@ -509,7 +512,10 @@ int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
     const uint64_t total = (uint64_t)rows * nbt;
     if (total == 0) return CM_OK;
     const unsigned grid = grid_for(cx, total * 32, 256, 16);
-    split_rows_kernel<<<grid, 256, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
+    {
+        ProfScope ps_(PK_SPLIT, s);
+        split_rows_kernel<<<grid, 256, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
+    }
     count_launch();
     return CM_OK;
 }
@@ -524,9 +530,12 @@ int split_cols(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
         const uint32_t nb = min(65535u, nbt - b0);
         const dim3 grid((K + 63) / 64, (cols + 63) / 64, nb);
         MatSrc m{src + (uint64_t)b0 * src_bs, src_bs, ld};
-        split_cols_kernel<MatSrc><<<grid, 256, 0, s>>>(m, cols, K, pad_k(K),
-                                                      planes + (uint64_t)b0 * 2 * cols * pad_k(K),
-                                                      colterm + (uint64_t)b0 * cols);
+        {
+            ProfScope ps_(PK_SPLIT, s);
+            split_cols_kernel<MatSrc><<<grid, 256, 0, s>>>(m, cols, K, pad_k(K),
+                                                          planes + (uint64_t)b0 * 2 * cols * pad_k(K),
+                                                          colterm + (uint64_t)b0 * cols);
+        }
         count_launch();
     }
     return CM_OK;
@@ -550,8 +559,11 @@ int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_
         const uint32_t nb = min(65535u, nimg - n0);
         src.x = x + (uint64_t)n0 * g.C * g.H * g.W;
         const dim3 grid((K + 63) / 64, (P + 63) / 64, nb);
-        split_cols_kernel<Im2colSrc><<<grid, 256, 0, s>>>(src, P, K, pad_k(K), planes + (uint64_t)n0 * 2 * P * pad_k(K),
-                                                          colterm + (uint64_t)n0 * P);
+        {
+            ProfScope ps_(PK_SPLIT, s);
+            split_cols_kernel<Im2colSrc><<<grid, 256, 0, s>>>(src, P, K, pad_k(K), planes + (uint64_t)n0 * 2 * P * pad_k(K),
+                                                              colterm + (uint64_t)n0 * P);
+        }
         count_launch();
     }
     return CM_OK;
@@ -561,7 +573,10 @@ int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, ui
               uint64_t out_bs, cudaStream_t s) {
     const uint64_t total = (uint64_t)batch * rows * cols;
     if (total == 0) return CM_OK;
-    fill_zero_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(out, rows, cols, ldo, out_bs, total);
+    {
+        ProfScope ps_(PK_CONV_AUX, s);
+        fill_zero_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(out, rows, cols, ldo, out_bs, total);
+    }
     count_launch();
     return CM_OK;
 }

@@ -203,7 +203,10 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
            cudaStream_t s) {
     if (global) {
         const unsigned grid = grid_for(cx, planes * 32, 256, 8);
-        pool_global_kernel<TYPE><<<grid, 256, 0, s>>>(x, y, planes, p0.in_h * p0.in_w);
+        {
+            ProfScope ps_(PK_POOL, s);
+            pool_global_kernel<TYPE><<<grid, 256, 0, s>>>(x, y, planes, p0.in_h * p0.in_w);
+        }
         count_launch();
         return CM_OK;
     }
@@ -221,10 +224,16 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         const size_t smem = (size_t)rows_needed * p.in_w * 2 + 16;
         const uint64_t blocks = planes * p.n_bands;
         if (blocks >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "cm_pool: too many planes");
-        pool_window_kernel<TYPE><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+        {
+            ProfScope ps_(PK_POOL, s);
+            pool_window_kernel<TYPE><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+        }
     } else {
         const uint64_t total = planes * p.out_h * p.out_w;
-        pool_direct_kernel<TYPE><<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, y, p, total);
+        {
+            ProfScope ps_(PK_POOL, s);
+            pool_direct_kernel<TYPE><<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, y, p, total);
+        }
     }
     count_launch();
     return CM_OK;

@@ -6,6 +6,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "cm_common.cuh"
 
@@ -57,6 +58,36 @@ int finish_sync(cm_stream_t stream) {
         return set_error(st, "device-side status %d (%s)", st, cm_strerror(st));
     }
     return CM_OK;
+}
+
+// ---- profiling --------------------------------------------------------------
+static const char* kProfNames[PK_COUNT] = {"gemm_q88", "split", "vectorop", "pool", "conv_aux"};
+struct ProfPair { int kind; cudaEvent_t a, b; };
+static std::mutex g_prof_mu;
+static bool g_prof_on = false;
+static std::vector<ProfPair> g_prof_pairs;
+static std::vector<cudaEvent_t> g_prof_free;
+
+static cudaEvent_t prof_event() {
+    cudaEvent_t e = nullptr;
+    if (!g_prof_free.empty()) { e = g_prof_free.back(); g_prof_free.pop_back(); }
+    else cudaEventCreate(&e);
+    return e;
+}
+
+ProfScope::ProfScope(int k, cudaStream_t st) : kind(k), s(st) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    if (!g_prof_on) return;
+    a = prof_event();
+    cudaEventRecord(a, s);
+}
+
+ProfScope::~ProfScope() {
+    if (!a) return;
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    cudaEvent_t b = prof_event();
+    cudaEventRecord(b, s);
+    g_prof_pairs.push_back({kind, a, b});
 }
 
 int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
@@ -153,6 +184,43 @@ int cm_release(void) {
 int cm_device(void) { return g_ready ? g_ctx.device : CM_ENOINIT; }
 
 uint64_t cm_launch_count(void) { return g_launches.load(); }
+
+int cm_profile_begin(void) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    for (auto& pp : g_prof_pairs) { g_prof_free.push_back(pp.a); g_prof_free.push_back(pp.b); }
+    g_prof_pairs.clear();
+    g_prof_on = true;
+    return CM_OK;
+}
+
+int cm_profile_end(void) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    g_prof_on = false;
+    return CM_OK;
+}
+
+int cm_profile_read(const char* kernel, double* total_ms, uint64_t* launches) {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    int kind = -1;
+    for (int i = 0; i < PK_COUNT; ++i)
+        if (kernel && !strcmp(kernel, kProfNames[i])) kind = i;
+    if (kind < 0) return set_error(CM_EINVAL, "unknown kernel '%s'", kernel ? kernel : "(null)");
+    double ms = 0.0;
+    uint64_t n = 0;
+    for (auto& pp : g_prof_pairs) {
+        if (pp.kind != kind) continue;
+        cudaError_t e = cudaEventSynchronize(pp.b);
+        if (e != cudaSuccess) return cuda_error(e, "cudaEventSynchronize");
+        float t = 0.f;
+        e = cudaEventElapsedTime(&t, pp.a, pp.b);
+        if (e != cudaSuccess) return cuda_error(e, "cudaEventElapsedTime");
+        ms += t;
+        ++n;
+    }
+    if (total_ms) *total_ms = ms;
+    if (launches) *launches = n;
+    return CM_OK;
+}
 
 int cm_synchronize(cm_stream_t stream) {
     const Context* c;

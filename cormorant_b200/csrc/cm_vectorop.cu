@@ -139,7 +139,10 @@ template <int OP>
 int launch_general(const Context* cx, const VopCall& v, cudaStream_t s) {
     const uint64_t c_len = (uint64_t)(v.outer - 1) * v.c_inc + v.size;
     const unsigned grid = grid_for(cx, c_len, 256, 16);
-    vop_general_kernel<OP><<<grid, 256, 0, s>>>(v.a, v.b, v.c, c_len, v.size, v.outer, v.a_inc, v.b_inc, v.c_inc);
+    {
+        ProfScope ps_(PK_VECTOROP, s);
+        vop_general_kernel<OP><<<grid, 256, 0, s>>>(v.a, v.b, v.c, c_len, v.size, v.outer, v.a_inc, v.b_inc, v.c_inc);
+    }
     count_launch();
     return CM_OK;
 }
@@ -151,10 +154,16 @@ int launch_vec(const Context* cx, const int16_t* a, const int16_t* b, int16_t* c
     if (total == 0) return CM_OK;
     const unsigned grid = grid_for(cx, (total + UNROLL - 1) / UNROLL, 256, 8);
     if (rows == 1) {
-        vop_vec_kernel<OP, false><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total, FastDiv(1), 0, 0, 0);
+        {
+            ProfScope ps_(PK_VECTOROP, s);
+            vop_vec_kernel<OP, false><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total, FastDiv(1), 0, 0, 0);
+        }
     } else {
-        vop_vec_kernel<OP, true><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total,
-                                                      FastDiv((uint32_t)nv), a_inc_v, b_inc_v, c_inc_v);
+        {
+            ProfScope ps_(PK_VECTOROP, s);
+            vop_vec_kernel<OP, true><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total,
+                                                          FastDiv((uint32_t)nv), a_inc_v, b_inc_v, c_inc_v);
+        }
     }
     count_launch();
     return CM_OK;

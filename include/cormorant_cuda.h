@@ -81,6 +81,15 @@ int cm_synchronize(cm_stream_t stream);       /* wait, then read + clear the dev
 uint64_t cm_launch_count(void);               /* kernels launched by this library so far */
 const char* cm_version(void);
 
+/* ---- device timing of this library's launches (no reference counterpart) --
+ * Between cm_profile_begin and cm_profile_end every kernel launch is bracketed
+ * by CUDA events on its own stream.  cm_profile_read waits for those events
+ * and returns the summed device time and launch count of one kernel family:
+ * "gemm_q88", "split", "vectorop", "pool" or "conv_aux". */
+int cm_profile_begin(void);
+int cm_profile_end(void);
+int cm_profile_read(const char* kernel, double* total_ms, uint64_t* launches);
+
 /* ---- VectorOPKernel ----------------------------------------------------------
  * c[o*(a_inc+b_inc) + i] = op(a[o*a_inc + i], b[o*b_inc + i]),  o < outer, i < size.
  * op: CM_OP_*; any other value copies a (VectorOP.cpp:108). */
