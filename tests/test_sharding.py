@@ -1,0 +1,57 @@
+"""Host-side multi-GPU logic on CPU: shard ranges and the output gather, as
+world_size-2 (and 3) gloo process groups on 127.0.0.1."""
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from cormorant_b200.sharding import gather_batches, shard_range
+
+
+@pytest.mark.parametrize("total", [0, 1, 7, 8, 64, 256, 1 << 28])
+@pytest.mark.parametrize("world", [1, 2, 3, 4, 8])
+def test_shard_ranges_partition(total, world):
+    start = 0
+    for r in range(world):
+        lo, cnt = shard_range(total, r, world)
+        assert lo == start and cnt >= 0
+        start += cnt
+    assert start == total
+    counts = [shard_range(total, r, world)[1] for r in range(world)]
+    assert max(counts) - min(counts) <= 1
+
+
+def test_bad_rank():
+    with pytest.raises(ValueError):
+        shard_range(8, 2, 2)
+
+
+def _worker(rank, world, port, total, per_item, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        lo, cnt = shard_range(total, rank, world)
+        # each "batch item" b holds words b*1000 + j (what a per-item kernel would write)
+        local = torch.tensor([b * 1000 + j for b in range(lo, lo + cnt) for j in range(per_item)], dtype=torch.int16)
+        full = gather_batches(local, total, per_item)
+        want = torch.tensor([b * 1000 + j for b in range(total) for j in range(per_item)], dtype=torch.int16)
+        q.put((rank, bool(torch.equal(full, want))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,total", [(2, 8), (2, 7), (3, 8)])
+def test_gather_batches_gloo(world, total):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + (os.getpid() % 500) + world * 7 + total
+    procs = [ctx.Process(target=_worker, args=(r, world, port, total, 5, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok in res), res
