@@ -35,6 +35,8 @@ def gather_batches(local, total: int, per_item: int, group=None):
         raise ValueError(f"rank {rank}: expected {counts[rank] * per_item} words, got {local.numel()}")
     padded = torch.zeros(cmax * per_item, dtype=local.dtype, device=local.device)
     padded[: local.numel()] = local.reshape(-1)
-    parts = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(parts, padded, group=group)
-    return torch.cat([p[: c * per_item] for p, c in zip(parts, counts)])
+    # neither NCCL nor gloo has an int16 type; an all-gather only moves bytes
+    wire = padded.view(torch.uint8)
+    parts = [torch.empty_like(wire) for _ in range(world)]
+    dist.all_gather(parts, wire, group=group)
+    return torch.cat([p.view(local.dtype)[: c * per_item] for p, c in zip(parts, counts)])

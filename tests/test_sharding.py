@@ -31,16 +31,20 @@ def test_bad_rank():
 def _worker(rank, world, port, total, per_item, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    os.environ["GLOO_SOCKET_IFNAME"] = "lo"
     try:
+        dist.init_process_group("gloo", rank=rank, world_size=world)
         lo, cnt = shard_range(total, rank, world)
         # each "batch item" b holds words b*1000 + j (what a per-item kernel would write)
         local = torch.tensor([b * 1000 + j for b in range(lo, lo + cnt) for j in range(per_item)], dtype=torch.int16)
         full = gather_batches(local, total, per_item)
         want = torch.tensor([b * 1000 + j for b in range(total) for j in range(per_item)], dtype=torch.int16)
         q.put((rank, bool(torch.equal(full, want))))
+    except Exception as e:  # report instead of leaving the parent waiting
+        q.put((rank, False, repr(e)))
     finally:
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world,total", [(2, 8), (2, 7), (3, 8)])
@@ -54,4 +58,4 @@ def test_gather_batches_gloo(world, total):
     res = [q.get(timeout=120) for _ in procs]
     for p in procs:
         p.join(timeout=60)
-    assert all(ok for _, ok in res), res
+    assert all(r[1] for r in res), res
