@@ -39,6 +39,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_matmul": (C.c_int, [_p, _p, _p] + [_u] * 7),
     "cm_matmul_async": (C.c_int, [_p, _p, _p] + [_u] * 7 + [_p]),
     "cm_matmul_at": (C.c_int, [_p, _u, _p, _u, _p, _u] + [_u] * 7),
+    "cm_matmul_noalloc": (C.c_int, [_p, _p, _p] + [_u] * 7 + [_p]),
     "cm_conv": (C.c_int, [_p, _p, _p, _p] + [_u] * 17),
     "cm_conv_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 17 + [_p]),
     "cm_pool": (C.c_int, [_p, _p] + [_u] * 17),

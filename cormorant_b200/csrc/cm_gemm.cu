@@ -26,6 +26,8 @@
 // CM_ETIMEOUT in the status word and winds down instead of hanging.
 #include <cuda.h>
 
+#include <mutex>
+
 #include "cm_gemm.cuh"
 
 namespace cm {
@@ -644,6 +646,104 @@ extern "C" int cm_matmul(const int16_t* a, const int16_t* b, int16_t* c, unsigne
                          unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride) {
     int rc = cm_matmul_async(a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, nullptr);
     return rc ? rc : finish_sync(nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// cm_matmul_noalloc: the MatMul entry for callers that must not allocate.
+//
+// Some callers cannot call cudaMalloc at all once they are running: code whose
+// device memory is owned by another allocator that has reserved the GPU, and
+// run loops that by contract allocate nothing after initialisation (the
+// reference's generated inference_run() is one: every buffer comes from the
+// single pool that inference_init() sets up).  cm_matmul takes its scratch
+// (the int8 operand planes and the row/column terms) from the stream-ordered
+// pool; this variant uses the fixed array below instead, so it never calls
+// cudaMalloc, cudaMallocAsync, cudaFree or any allocating routine.
+//
+// The array is a file-scope __device__ object, so every GPU that loads this
+// library holds CM_MATMUL_NOALLOC_SCRATCH_BYTES of it until the process exits.
+// Its host-side name is only a stand-in, never a device address: the device
+// address comes from cudaGetSymbolAddress, taken once per device, with that
+// device current, on the first call made on it.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_matmul_noalloc_scratch[CM_MATMUL_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+int noalloc_scratch(int device, void** out) {
+    if (device < 0 || device >= 64) return set_error(CM_EUNSUPPORTED, "device ordinal %d", device);
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_matmul_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(noalloc scratch)");
+        g_noalloc_addr[device] = p;
+    }
+    *out = g_noalloc_addr[device];
+    return CM_OK;
+}
+
+// One batch-step range [bi0, bi0 + nb) of a matmul, all scratch in `base`.
+int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_t* b, int16_t* c, uint32_t n,
+                uint32_t k, uint32_t m, uint32_t nb, uint32_t a_bs, uint32_t b_bs, uint64_t c_bs, cudaStream_t s) {
+    const uint32_t a_batches = a_bs == 0 ? 1u : nb;
+    const uint32_t b_batches = b_bs == 0 ? 1u : nb;
+    const uint64_t K_pad = pad_k(k);
+    const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * m * K_pad + 255) & ~255ull;
+    const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)b_batches * m * 4 + 255) & ~255ull;
+    if (a_bytes + b_bytes + rt_bytes + ct_bytes > CM_MATMUL_NOALLOC_SCRATCH_BYTES)
+        return set_error(CM_EINVAL,
+                         "cm_matmul_noalloc: needs %llu bytes of scratch, the fixed array holds %llu "
+                         "(use cm_matmul for larger calls)",
+                         (unsigned long long)(a_bytes + b_bytes + rt_bytes + ct_bytes),
+                         (unsigned long long)CM_MATMUL_NOALLOC_SCRATCH_BYTES);
+    int8_t* ap = (int8_t*)base;
+    int8_t* bp = ap + a_bytes;
+    int32_t* rt = (int32_t*)(bp + b_bytes);
+    int32_t* ct = (int32_t*)((uint8_t*)rt + rt_bytes);
+    // Every word the GEMM reads is rewritten here: plane rows k < K and all row
+    // terms by the splits; the column terms are cleared before they are summed.
+    int rc = split_rows(cx, a, a_bs, k, n, k, a_batches, ap, rt, nullptr, s);
+    if (!rc) rc = split_cols(cx, b, b_bs, m, m, k, b_batches, bp, ct, s);
+    if (!rc) {
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, rt, ct, c, m, c_bs, nb};
+        rc = gemm_launch(cx, p, s);
+    }
+    return rc;
+}
+}  // namespace
+
+extern "C" int cm_matmul_noalloc(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                                 unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                                 unsigned c_batch_stride, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (n == 0 || m == 0 || batch == 0) return CM_OK;
+    if (!c || (k > 0 && (!a || !b))) return set_error(CM_EINVAL, "cm_matmul_noalloc: null buffer");
+    if (k > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_matmul_noalloc: k = %u exceeds %u", k, kMaxGemmK);
+    cudaStream_t s = (cudaStream_t)stream;
+    if (k == 0) return fill_zero(cx, c, batch, n, m, m, c_batch_stride, s);
+    void* base = nullptr;
+    rc = noalloc_scratch(cx->device, &base);
+    if (rc) return rc;
+    if (batch > 1 && (uint64_t)c_batch_stride < (uint64_t)n * m) {
+        // Overlapping output slices: batch steps in order, later ones win; the
+        // steps follow each other on `stream`, so they may reuse the scratch.
+        const uint64_t first = c_batch_stride == 0 ? batch - 1 : 0;
+        for (uint64_t bi = first; bi < batch && !rc; ++bi)
+            rc = noalloc_run(cx, (uint8_t*)base, a + bi * a_batch_stride, b + bi * b_batch_stride,
+                             c + bi * c_batch_stride, n, k, m, 1, a_batch_stride, b_batch_stride, 0, s);
+    } else {
+        rc = noalloc_run(cx, (uint8_t*)base, a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, s);
+    }
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul_noalloc");
 }
 
 extern "C" int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, unsigned b_off, int16_t* c,

@@ -107,6 +107,26 @@ int cm_matmul(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsign
 int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k,
                     unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
                     unsigned c_batch_stride, cm_stream_t stream);
+/* Allocation-free MatMul (no counterpart in the reference).  Same arguments and
+ * result as cm_matmul, enqueued on `stream` (wait with cm_synchronize).  For
+ * callers that cannot call cudaMalloc once running -- e.g. a run loop that,
+ * like the reference's generated inference_run(), must not allocate after
+ * initialisation, or code whose device memory is owned by another allocator.
+ * It never allocates: its scratch is a fixed device array inside this library
+ * of CM_MATMUL_NOALLOC_SCRATCH_BYTES, held on every GPU that loads the library
+ * until the process exits.  Calls whose scratch need exceeds it return
+ * CM_EINVAL; the need is, in bytes (each term rounded up to 256):
+ *   A_b*2*n*K16 + B_b*2*m*K16 + A_b*n*4 + B_b*m*4,
+ *   K16 = k rounded up to 16, A_b = (a_batch_stride ? batch : 1), B_b likewise.
+ * The first call on a device looks up the array's device address (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  All calls share the one array: calls that can overlap on the GPU
+ * (different streams without ordering between them) race and must not be issued. */
+#define CM_MATMUL_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+int cm_matmul_noalloc(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k,
+                      unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                      unsigned c_batch_stride, cm_stream_t stream);
+
 /* run_matmul_at(): the same call with element offsets applied to each buffer. */
 int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, unsigned b_off, int16_t* c,
                  unsigned c_off, unsigned n, unsigned k, unsigned m, unsigned batch,
