@@ -107,7 +107,7 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
     if (K64 > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_conv: in_ch*kh*kw = %llu exceeds %u", (unsigned long long)K64, kMaxGemmK);
     const uint32_t K = (uint32_t)K64, K_pad = pad_k(K);
 
-    const uint64_t per_img = 2 * P * K_pad;
+    const uint64_t per_img = 2 * (uint64_t)K * pad_c((uint32_t)P);
     uint64_t chunk = kIm2colBudget / per_img;
     if (chunk == 0) chunk = 1;
     if (chunk > batch) chunk = batch;
@@ -129,8 +129,8 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
         rc = split_im2col(cx, x + n0 * (uint64_t)in_ch * in_h * in_w, geo, nb, bp, ct, s);
         if (rc) break;
-        GemmPlan p{wp, out_ch, 1, bp, (uint32_t)P, nb, K, K_pad, rt, ct, y + n0 * (uint64_t)out_ch * P, P,
-                   (uint64_t)out_ch * P, nb};
+        GemmPlan p{wp, out_ch, 1, bp, (uint32_t)P, nb, K, K_pad, pad_c((uint32_t)P), rt, ct,
+                   y + n0 * (uint64_t)out_ch * P, P, (uint64_t)out_ch * P, nb};
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);

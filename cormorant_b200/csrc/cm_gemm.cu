@@ -8,24 +8,31 @@
 // With x' = x - 128 = 256*h + l':
 //   sum_k a*b = sum a'b' + 128*sum_k a' + 128*sum_k b' + 16384*K
 //   sum a'b'  = 2^16*sum(ah*bh) + 2^8*(sum(ah*bl') + sum(al'*bh)) + sum(al'*bl')
-// The three int8 dot products run on the tensor cores (tcgen05.mma kind::i8,
-// s8 x s8 -> s32, four MMAs per K step into three TMEM accumulators); the two
-// rank-1 terms come from the split pre-pass.  All of it is reduced mod 2^32,
+// The four int8 dot products run on the tensor cores (tcgen05.mma kind::i8,
+// s8 x s8 -> s32); the two rank-1 terms come from the split pre-pass.  All of it is reduced mod 2^32,
 // which is exactly the reference's wrap, so the result is bit-identical.
 // Each accumulator's magnitude stays below K * 2^15, so K <= 65535 never
 // overflows an int32 on the way.
 //
 // Kernel (one 128x128 output tile per CTA, 192 threads, 1 CTA per SM):
-//   warp 0   TMA producer: per K block of 128 bytes, one 4-D box {128 k, 128 rows,
-//            2 planes, 1 batch} for A and one for B (32 KB each, 128-byte swizzle),
+//   warp 0   TMA producer: per K block of 128, one 4-D box {128 k, 128 rows, 2 planes,
+//            1 batch} of the K-major A planes and one box {128 n, 128 k, 2 planes,
+//            1 batch} of the N-major B planes (32 KB each, 128-byte swizzle),
 //            3-stage ring guarded by full/empty mbarriers.  No multicast.
-//   warp 1   allocates 512 TMEM columns; lane 0 issues the MMAs and commits.
+//   warp 1   allocates all 512 TMEM columns; lane 0 issues the MMAs and commits.
+//            The B box lands as two N-major 128-column atoms [Bh | Bl] = one
+//            256-column operand, so each 32-deep K step is two M=128, N=256 MMAs:
+//            Ah x [Bh|Bl] -> (HH | HL) and Al x [Bh|Bl] -> (LH | LL), four
+//            128-column int32 accumulators.
+//            N=256 halves the shared-memory operand reads per MAC against N=128,
+//            which is what bounds this kernel (TMA writes share the bandwidth).
 //   warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns of each accumulator,
 //            recombine, narrow, store int16 rows.
 // Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
 // CM_ETIMEOUT in the status word and winds down instead of hanging.
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "cm_gemm.cuh"
@@ -37,12 +44,18 @@ constexpr int BM = 128, BN = 128, BK = 128, STAGES = 3;
 constexpr int PLANE_TILE = BM * BK;                 // 16 KB
 constexpr int OPERAND_TILE = 2 * PLANE_TILE;        // hi + lo = 32 KB
 constexpr int STAGE_BYTES = 2 * OPERAND_TILE;       // A + B = 64 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_USED = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+// The whole per-CTA maximum is requested (1 CTA per SM either way), so every
+// operand descriptor stays inside this CTA's own allocation with margin.
+constexpr int SMEM_BYTES = 232448;
+static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_HH = 0, COL_X = 128, COL_LL = 256;
+constexpr uint32_t COL_HH = 0, COL_HL = 128, COL_LH = 256, COL_LL = 384;
+constexpr uint32_t MMA_N = 2 * BN;   // [Bh; Bl]
 
-// Instruction descriptor: D s32, A s8, B s8, both K-major, M = 128, N = 128.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128, N = 256.
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(MMA_N >> 3) << 17) |
+                           ((uint32_t)(BM >> 4) << 24);
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -106,10 +119,18 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups
-// 1024 bytes apart (SBO), version 1 (sm_100).
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: rows of 128 bytes
+// of K, 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
 __device__ __forceinline__ uint64_t sdesc(uint32_t addr) {
     return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// N-major, 128-byte swizzle: each K row holds 128 bytes of N; 8-row K groups are
+// 1024 bytes apart (SBO); the two 128-column N atoms (hi plane, lo plane) are
+// one plane tile apart (LBO = 16 KB).
+__device__ __forceinline__ uint64_t sdesc_n(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)(16384 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
@@ -201,7 +222,7 @@ __global__ void __launch_bounds__(192, 1)
                 mbar_expect_tx(full, STAGE_BYTES);
                 uint8_t* st = smem + s * STAGE_BYTES;
                 tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)m0, 0, (int)ba);
-                tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)(kb * BK), (int)n0, 0, (int)bb);
+                tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)n0, (int)(kb * BK), 0, (int)bb);
                 ++issued;
             }
             if (*abort_flag) {
@@ -226,12 +247,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
                 for (uint32_t kk = 0; kk < BK / 32; ++kk) {
                     const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
-                    const uint64_t bh = sdesc(b0 + kk * 32), bl = sdesc(b0 + PLANE_TILE + kk * 32);
+                    const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x (Bh | Bl)
                     const uint32_t acc = (kb | kk) != 0u;
-                    umma_i8(tmem + COL_HH, ah, bh, acc);
-                    umma_i8(tmem + COL_X, ah, bl, acc);
-                    umma_i8(tmem + COL_X, al, bh, 1u);
-                    umma_i8(tmem + COL_LL, al, bl, acc);
+                    umma_i8(tmem + COL_HH, ah, bhl, acc);         // -> HH | HL
+                    umma_i8(tmem + COL_LH, al, bhl, acc);         // -> LH | LL
                 }
                 umma_commit(smem_u32(&bars[STAGES + s]));   // frees the stage once these MMAs have read it
             }
@@ -256,10 +275,18 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
             for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
                 if (n0 + c0 >= g.cols) break;
-                uint32_t hh[32], xx[32], ll[32];
-                tmem_ld32(tl + COL_HH + c0, hh);
-                tmem_ld32(tl + COL_X + c0, xx);
-                tmem_ld32(tl + COL_LL + c0, ll);
+                // acc = 2^16*HH + 2^8*(HL + LH) + LL = ((((HH << 8) + HL + LH) << 8) + LL
+                uint32_t p[32], q[32];
+                tmem_ld32(tl + COL_HH + c0, p);
+                tmem_ld32(tl + COL_HL + c0, q);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) p[j] = (p[j] << 8) + q[j];
+                tmem_ld32(tl + COL_LH + c0, q);
+                tmem_ld_wait();
+#pragma unroll
+                for (int j = 0; j < 32; ++j) p[j] = (p[j] + q[j]) << 8;
+                tmem_ld32(tl + COL_LL + c0, q);
                 tmem_ld_wait();
                 if (row < g.rows) {
                     const uint32_t col0 = n0 + c0;
@@ -268,7 +295,7 @@ __global__ void __launch_bounds__(192, 1)
                     for (int j = 0; j < 32; ++j) {
                         const uint32_t col = col0 + j;
                         const uint32_t cterm = col < g.cols ? (uint32_t)__ldg(ct + col) : 0u;
-                        const uint32_t acc = (hh[j] << 16) + (xx[j] << 8) + ll[j] + rt + cterm;
+                        const uint32_t acc = p[j] + q[j] + rt + cterm;
                         v[j] = narrow_acc(acc);
                     }
                     int16_t* dst = orow + col0;
@@ -354,77 +381,105 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restri
     }
 }
 
-struct MatSrc {
-    const int16_t* src; uint64_t src_bs, ld;
-    __device__ __forceinline__ int16_t operator()(uint32_t bt, uint32_t k, uint32_t c) const {
-        return src[(uint64_t)bt * src_bs + (uint64_t)k * ld + c];
-    }
-};
-
-struct Im2colSrc {
-    const int16_t* x;
-    ConvGeom g;
-    FastDiv fd_khw, fd_kw, fd_ow;
-    uint32_t khw;
-    __device__ __forceinline__ int16_t operator()(uint32_t n, uint32_t k, uint32_t p) const {
-        const uint32_t c = fd_khw.div(k);
-        const uint32_t rs = k - c * khw;
-        const uint32_t r = fd_kw.div(rs);
-        const uint32_t s = rs - r * g.kw;
-        const uint32_t oh = fd_ow.div(p);
-        const uint32_t ow = p - oh * g.out_w;
-        const int64_t ih = (int64_t)oh * g.sh + (int64_t)r * g.dh - (int64_t)g.pt;
-        const int64_t iw = (int64_t)ow * g.sw + (int64_t)s * g.dw - (int64_t)g.pl;
-        if (ih < 0 || ih >= (int64_t)g.H || iw < 0 || iw >= (int64_t)g.W) return 0;
-        return __ldg(x + (((uint64_t)n * g.C + c) * g.H + (uint64_t)ih) * g.W + (uint64_t)iw);
-    }
-};
-
-// 64 (k) x 64 (column) tile through shared memory: coalesced reads along the
-// column index, 16-byte plane writes along k; column terms via atomics.
-template <class Src>
-__global__ void __launch_bounds__(256) split_cols_kernel(Src src, uint32_t cols, uint32_t K, uint32_t K_pad,
-                                                         int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
-    __shared__ int16_t tile[64][66];
-    const uint32_t k0 = blockIdx.x * 64, c0 = blockIdx.y * 64, bt = blockIdx.z;
-    const uint32_t tid = threadIdx.x;
-#pragma unroll 4
-    for (uint32_t i = 0; i < 16; ++i) {
-        const uint32_t e = tid + i * 256;
-        const uint32_t kk = e >> 6, cc = e & 63;
-        const uint32_t k = k0 + kk, c = c0 + cc;
-        tile[kk][cc] = (k < K && c < cols) ? src(bt, k, c) : (int16_t)0;
-    }
-    __syncthreads();
-    const uint32_t cc = tid >> 2, j = tid & 3;
-    const uint32_t c = c0 + cc, kk0 = j * 16;
-    int32_t sum = 0;
-    if (c < cols) {
-        uint32_t hw[4], lw[4];
+// B rows -> N-major planes.  Thread = 8 consecutive columns over a chunk of K:
+// 16-byte loads and 8-byte plane stores, both coalesced along N; the column
+// terms are summed in registers and added once per chunk.
+__global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict__ src, uint64_t src_bs, uint64_t ld,
+                                                       uint32_t cols, uint32_t K, uint32_t C_pad, uint32_t k_chunk,
+                                                       int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    const uint32_t bt = blockIdx.z;
+    const uint32_t c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (c8 >= cols) return;
+    const uint32_t k0 = blockIdx.y * k_chunk, k1 = min(K, k0 + k_chunk);
+    const int16_t* sp = src + (uint64_t)bt * src_bs + c8;
+    int8_t* dh = planes + (uint64_t)bt * 2 * K * C_pad + c8;
+    int8_t* dl = dh + (uint64_t)K * C_pad;
+    int32_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    const bool vec = c8 + 8 <= cols && ((uintptr_t)sp & 15u) == 0 && (ld & 7u) == 0;
+    if (vec) {
+        uint32_t k = k0;
+        for (; k + 4 <= k1; k += 4) {
+            uint4 v[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            uint32_t h = 0, l = 0;
+            for (int u = 0; u < 4; ++u) v[u] = __ldcs((const uint4*)(sp + (uint64_t)(k + u) * ld));
 #pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                const uint32_t kk = kk0 + 4 * q + b;
-                const int16_t x = tile[kk][cc];
-                h |= (uint32_t)(uint8_t)(x >> 8) << (8 * b);
-                l |= (uint32_t)(uint8_t)((x & 255) ^ 0x80) << (8 * b);
-                if (k0 + kk < K) sum += (int32_t)x - 128;
+            for (int u = 0; u < 4; ++u) {
+                const uint64_t o = (uint64_t)(k + u) * C_pad;
+                *(uint2*)(dh + o) = make_uint2(__byte_perm(v[u].x, v[u].y, 0x7531), __byte_perm(v[u].z, v[u].w, 0x7531));
+                *(uint2*)(dl + o) = make_uint2(__byte_perm(v[u].x, v[u].y, 0x6420) ^ 0x80808080u,
+                                               __byte_perm(v[u].z, v[u].w, 0x6420) ^ 0x80808080u);
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    sum[2 * j] += (int32_t)(int16_t)(w[j] & 0xFFFFu) - 128;
+                    sum[2 * j + 1] += (int32_t)(int16_t)(w[j] >> 16) - 128;
+                }
             }
-            hw[q] = h;
-            lw[q] = l;
         }
-        if (k0 + kk0 < K_pad) {
-            int8_t* dh = planes + (((uint64_t)bt * 2 + 0) * cols + c) * K_pad + k0 + kk0;
-            int8_t* dl = planes + (((uint64_t)bt * 2 + 1) * cols + c) * K_pad + k0 + kk0;
-            *(uint4*)dh = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *(uint4*)dl = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        for (; k < k1; ++k) {
+            const uint4 v = __ldcs((const uint4*)(sp + (uint64_t)k * ld));
+            const uint64_t o = (uint64_t)k * C_pad;
+            *(uint2*)(dh + o) = make_uint2(__byte_perm(v.x, v.y, 0x7531), __byte_perm(v.z, v.w, 0x7531));
+            *(uint2*)(dl + o) = make_uint2(__byte_perm(v.x, v.y, 0x6420) ^ 0x80808080u,
+                                           __byte_perm(v.z, v.w, 0x6420) ^ 0x80808080u);
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                sum[2 * j] += (int32_t)(int16_t)(w[j] & 0xFFFFu) - 128;
+                sum[2 * j + 1] += (int32_t)(int16_t)(w[j] >> 16) - 128;
+            }
+        }
+    } else {
+        const uint32_t nc = min(8u, cols - c8);
+        for (uint32_t k = k0; k < k1; ++k) {
+            const uint64_t o = (uint64_t)k * C_pad;
+            for (uint32_t j = 0; j < nc; ++j) {
+                const int16_t x = sp[(uint64_t)k * ld + j];
+                dh[o + j] = (int8_t)(x >> 8);
+                dl[o + j] = (int8_t)((x & 255) - 128);
+                sum[j] += (int32_t)x - 128;
+            }
         }
     }
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
-    sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
-    if (j == 0 && c < cols) atomicAdd((unsigned int*)(colterm + (uint64_t)bt * cols + c), (uint32_t)sum * 128u);
+    const uint32_t nc = min(8u, cols - c8);
+    for (uint32_t j = 0; j < nc; ++j)
+        atomicAdd((unsigned int*)(colterm + (uint64_t)bt * cols + c8 + j), (uint32_t)sum[j] * 128u);
+}
+
+// im2col -> N-major planes.  Thread = one output pixel p of image n over a
+// chunk of taps k = (c, r, s); consecutive threads hold consecutive pixels, so
+// input reads follow the row and plane writes are contiguous bytes.
+__global__ void __launch_bounds__(256) im2col_kn_kernel(const int16_t* __restrict__ x, ConvGeom g, uint32_t P,
+                                                        uint32_t K, uint32_t P_pad, uint32_t k_chunk, FastDiv fd_ow,
+                                                        int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    const uint32_t n = blockIdx.z;
+    const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
+    if (p >= P) return;
+    const uint32_t k0 = blockIdx.y * k_chunk, k1 = min(K, k0 + k_chunk);
+    const uint32_t oh = fd_ow.div(p), ow = p - oh * g.out_w;
+    const int32_t ihb = (int32_t)(oh * g.sh) - (int32_t)g.pt;
+    const int32_t iwb = (int32_t)(ow * g.sw) - (int32_t)g.pl;
+    const uint32_t khw = g.kh * g.kw;
+    uint32_t c = k0 / khw, rs = k0 - c * khw;
+    uint32_t r = rs / g.kw, s = rs - r * g.kw;
+    const int16_t* xn = x + (uint64_t)n * g.C * g.H * g.W;
+    int8_t* dh = planes + (uint64_t)n * 2 * K * P_pad + p;
+    int8_t* dl = dh + (uint64_t)K * P_pad;
+    int32_t sum = 0;
+    for (uint32_t k = k0; k < k1; ++k) {
+        const int32_t ih = ihb + (int32_t)(r * g.dh), iw = iwb + (int32_t)(s * g.dw);
+        int16_t v = 0;
+        if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
+            v = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
+        dh[(uint64_t)k * P_pad] = (int8_t)(v >> 8);
+        dl[(uint64_t)k * P_pad] = (int8_t)((v & 255) - 128);
+        sum += (int32_t)v - 128;
+        if (++s == g.kw) {
+            s = 0;
+            if (++r == g.kh) { r = 0; ++c; }
+        }
+    }
+    atomicAdd((unsigned int*)(colterm + (uint64_t)n * P + p), (uint32_t)sum * 128u);
 }
 
 __global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
@@ -472,6 +527,22 @@ int make_plane_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t K_pa
     return CM_OK;
 }
 
+// planes [batches][2][K][C_pad] int8 (N-major); box {128 n, 128 k, 2 planes, 1 batch}.
+int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t C_pad, uint32_t K, uint32_t batches) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)base & 15u) != 0 || (C_pad & 15u) != 0) return set_error(CM_EINVAL, "plane buffer misaligned");
+    const cuuint64_t dims[4] = {cols, K, 2, batches};
+    const cuuint64_t strides[3] = {(cuuint64_t)C_pad, (cuuint64_t)K * C_pad, (cuuint64_t)2 * K * C_pad};
+    const cuuint32_t box[4] = {(cuuint32_t)BN, (cuuint32_t)BK, 2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return CM_OK;
+}
+
 }  // namespace
 
 int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
@@ -480,7 +551,7 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     CUtensorMap ta, tb;
     int rc = make_plane_map(&ta, p.a_planes, p.K, p.K_pad, p.rows, p.a_batches);
     if (rc) return rc;
-    rc = make_plane_map(&tb, p.b_planes, p.K, p.K_pad, p.cols, p.b_batches);
+    rc = make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, p.b_batches);
     if (rc) return rc;
     static bool attr_set = false;
     if (!attr_set) {
@@ -522,21 +593,33 @@ int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
     return CM_OK;
 }
 
-int split_cols(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
-               uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s) {
+// K chunk so that the grid has a few waves of CTAs (each chunk adds one atomic per column).
+static uint32_t pick_k_chunk(uint32_t K, uint64_t other_ctas, uint32_t sm_count) {
+    const uint64_t target = 4ull * sm_count;
+    uint64_t splits = other_ctas >= target ? 1 : (target + other_ctas - 1) / other_ctas;
+    uint64_t chunk = (K + splits - 1) / splits;
+    chunk = std::max<uint64_t>(chunk, 64);
+    return (uint32_t)std::min<uint64_t>(chunk, K ? K : 1);
+}
+
+int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
+             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s) {
     if ((uint64_t)cols * nbt == 0) return CM_OK;
     cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)cols * nbt * sizeof(int32_t), s);
     if (e != cudaSuccess) return cuda_error(e, "memset colterm");
     if (K == 0) return CM_OK;
+    const uint32_t vec_threads = (cols + 7) / 8;
+    const uint32_t block = std::min<uint32_t>(256, (vec_threads + 31) / 32 * 32);
+    const uint32_t gx = (vec_threads + block - 1) / block;
+    const uint32_t k_chunk = pick_k_chunk(K, (uint64_t)gx * nbt, cx->sm_count);
+    const uint32_t C_pad = pad_c(cols);
     for (uint32_t b0 = 0; b0 < nbt; b0 += 65535u) {
-        const uint32_t nb = min(65535u, nbt - b0);
-        const dim3 grid((K + 63) / 64, (cols + 63) / 64, nb);
-        MatSrc m{src + (uint64_t)b0 * src_bs, src_bs, ld};
+        const uint32_t nb = std::min(65535u, nbt - b0);
+        const dim3 grid(gx, (K + k_chunk - 1) / k_chunk, nb);
         {
             ProfScope ps_(PK_SPLIT, s);
-            split_cols_kernel<MatSrc><<<grid, 256, 0, s>>>(m, cols, K, pad_k(K),
-                                                          planes + (uint64_t)b0 * 2 * cols * pad_k(K),
-                                                          colterm + (uint64_t)b0 * cols);
+            split_kn_kernel<<<grid, block, 0, s>>>(src + (uint64_t)b0 * src_bs, src_bs, ld, cols, K, C_pad, k_chunk,
+                                                  planes + (uint64_t)b0 * 2 * K * C_pad, colterm + (uint64_t)b0 * cols);
         }
         count_launch();
     }
@@ -551,20 +634,18 @@ int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_
     cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)P * nimg * sizeof(int32_t), s);
     if (e != cudaSuccess) return cuda_error(e, "memset colterm");
     if (K == 0) return CM_OK;
-    Im2colSrc src;
-    src.g = g;
-    src.khw = g.kh * g.kw;
-    src.fd_khw = FastDiv(src.khw);
-    src.fd_kw = FastDiv(g.kw);
-    src.fd_ow = FastDiv(g.out_w);
+    const uint32_t block = std::min<uint32_t>(256, (P + 31) / 32 * 32);
+    const uint32_t gx = (P + block - 1) / block;
+    const uint32_t k_chunk = pick_k_chunk(K, (uint64_t)gx * nimg, cx->sm_count);
+    const uint32_t P_pad = pad_c(P);
     for (uint32_t n0 = 0; n0 < nimg; n0 += 65535u) {
-        const uint32_t nb = min(65535u, nimg - n0);
-        src.x = x + (uint64_t)n0 * g.C * g.H * g.W;
-        const dim3 grid((K + 63) / 64, (P + 63) / 64, nb);
+        const uint32_t nb = std::min(65535u, nimg - n0);
+        const dim3 grid(gx, (K + k_chunk - 1) / k_chunk, nb);
         {
             ProfScope ps_(PK_SPLIT, s);
-            split_cols_kernel<Im2colSrc><<<grid, 256, 0, s>>>(src, P, K, pad_k(K), planes + (uint64_t)n0 * 2 * P * pad_k(K),
-                                                              colterm + (uint64_t)n0 * P);
+            im2col_kn_kernel<<<grid, block, 0, s>>>(x + (uint64_t)n0 * g.C * g.H * g.W, g, P, K, P_pad, k_chunk,
+                                                   FastDiv(g.out_w), planes + (uint64_t)n0 * 2 * K * P_pad,
+                                                   colterm + (uint64_t)n0 * P);
         }
         count_launch();
     }
@@ -620,7 +701,7 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;
     const uint64_t K_pad = pad_k(k);
     const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
-    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * m * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * k * pad_c(m) + 255) & ~255ull;
     const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
     const uint64_t ct_bytes = ((uint64_t)b_batches * m * 4 + 255) & ~255ull;
     void* scratch = nullptr;
@@ -631,9 +712,9 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     int32_t* rt = (int32_t*)(bp + b_bytes);
     int32_t* ct = (int32_t*)((uint8_t*)rt + rt_bytes);
     rc = split_rows(cx, a, a_batch_stride, k, n, k, a_batches, ap, rt, nullptr, s);
-    if (!rc) rc = split_cols(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s);
+    if (!rc) rc = split_kn(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s);
     if (!rc) {
-        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, rt, ct, c, m, c_batch_stride, batch};
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, c_batch_stride, batch};
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);
@@ -692,7 +773,7 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
     const uint32_t b_batches = b_bs == 0 ? 1u : nb;
     const uint64_t K_pad = pad_k(k);
     const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
-    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * m * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * k * pad_c(m) + 255) & ~255ull;
     const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
     const uint64_t ct_bytes = ((uint64_t)b_batches * m * 4 + 255) & ~255ull;
     if (a_bytes + b_bytes + rt_bytes + ct_bytes > CM_MATMUL_NOALLOC_SCRATCH_BYTES)
@@ -708,9 +789,9 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
     // Every word the GEMM reads is rewritten here: plane rows k < K and all row
     // terms by the splits; the column terms are cleared before they are summed.
     int rc = split_rows(cx, a, a_bs, k, n, k, a_batches, ap, rt, nullptr, s);
-    if (!rc) rc = split_cols(cx, b, b_bs, m, m, k, b_batches, bp, ct, s);
+    if (!rc) rc = split_kn(cx, b, b_bs, m, m, k, b_batches, bp, ct, s);
     if (!rc) {
-        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, rt, ct, c, m, c_bs, nb};
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, c_bs, nb};
         rc = gemm_launch(cx, p, s);
     }
     return rc;

@@ -1,9 +1,10 @@
 // cm_gemm.cuh -- the Q8.8 tensor-core GEMM shared by MatMul and Conv.
 //
 // Data layout in HBM (all produced by the split pre-passes in cm_gemm.cu):
-//   A planes  [a_batches][2][rows][K_pad] int8   row-major over K (K-major)
-//   B planes  [b_batches][2][cols][K_pad] int8   (B^T: one row per output column)
+//   A planes  [a_batches][2][rows][K_pad] int8   K-major (rows of A, K contiguous)
+//   B planes  [b_batches][2][K][C_pad]    int8   N-major (rows of B, N contiguous)
 //   plane 0 = hi = x >> 8 (signed), plane 1 = lo' = (x & 255) - 128 (signed)
+//   K_pad = K rounded up to 16, C_pad = cols rounded up to 16 (16-byte TMA strides)
 //   rowterm   [a_batches][rows] int32, colterm [b_batches][cols] int32
 //   out[z*out_bs + row*ldo + col] = sat16(floor(acc / 256)), with
 //   acc = 2^16*HH + 2^8*(HL + LH) + LL + rowterm[row] + colterm[col]  (mod 2^32)
@@ -17,7 +18,7 @@ namespace cm {
 struct GemmPlan {
     const int8_t* a_planes; uint32_t rows; uint32_t a_batches;
     const int8_t* b_planes; uint32_t cols; uint32_t b_batches;
-    uint32_t K, K_pad;
+    uint32_t K, K_pad, C_pad;
     const int32_t* rowterm;
     const int32_t* colterm;
     int16_t* out; uint64_t ldo, out_bs;
@@ -27,6 +28,7 @@ struct GemmPlan {
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude
 
 inline uint32_t pad_k(uint32_t K) { return (K + 15u) & ~15u; }
+inline uint32_t pad_c(uint32_t C) { return (C + 15u) & ~15u; }
 
 // Launch the tcgen05 GEMM (all arguments device-resident, stream-ordered).
 int gemm_launch(const Context* cx, const GemmPlan& g, cudaStream_t s);
@@ -37,13 +39,14 @@ int gemm_launch(const Context* cx, const GemmPlan& g, cudaStream_t s);
 int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
                uint32_t nbt, int8_t* planes, int32_t* rowterm, const int16_t* bias, cudaStream_t s);
 
-// Split + transpose int16 matrix columns into hi/lo planes + column terms:
+// Split int16 matrix rows of B into N-major hi/lo planes + column terms:
 //   element (bt, k, c) = src[bt*src_bs + k*ld + c], c < cols, k < K;
-//   colterm[bt*cols + c] = 128*sum_k(x - 128).
-int split_cols(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
-               uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s);
+//   planes[((bt*2 + p)*K + k)*C_pad + c]; colterm[bt*cols + c] = 128*sum_k(x - 128).
+int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
+             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s);
 
-// im2col + split for ConvKernel: column p = oh*out_w + ow of image n, row k = (c, r, s).
+// im2col + split for ConvKernel: column p = oh*out_w + ow of image n, row k = (c, r, s),
+// N-major planes [n][2][K][P_pad]; out-of-range taps read 0.
 struct ConvGeom {
     uint32_t C, H, W, out_h, out_w, kh, kw, sh, sw, dh, dw, pt, pl;
 };

@@ -49,8 +49,8 @@ __device__ __forceinline__ int16_t finalize(uint32_t acc, uint32_t denom) {
 
 struct PoolP {
     uint32_t in_h, in_w, out_h, out_w, ph, pw, sh, sw, pt, pl, dh, dw, cip;
-    uint32_t band_rows, n_bands;
-    FastDiv fd_ow;
+    uint32_t band_rows, n_bands, pitch, off0;
+    FastDiv fd_ow, fd_vpr;
 };
 
 template <int TYPE>
@@ -88,46 +88,118 @@ __device__ __forceinline__ int16_t pool_pixel(const PoolP& p, uint32_t oh, uint3
     return finalize<TYPE>(acc, p.cip ? p.ph * p.pw : valid);
 }
 
-template <int TYPE>
-__global__ void __launch_bounds__(256) pool_window_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y, PoolP p) {
-    extern __shared__ __align__(16) int16_t smem[];
+// Window kernel.  The CTA's band of output rows touches input rows
+// [ih_lo, ih_lo + rows) and columns [-pad_left, ...); they are staged in shared
+// memory as a padded tile whose out-of-range cells hold the window identity
+// (-128.0 for MAX, 0 otherwise), so taps need no bounds checks and all offsets
+// are 32-bit.  Column iw lives at tile column off0 + iw, off0 a multiple of 8,
+// so 16-byte-aligned input rows copy as 128-bit words.  PH/PW > 0 fix the
+// window size at compile time (fully unrolled taps); 0 means "from p".
+template <int TYPE, int PH, int PW>
+__global__ void __launch_bounds__(256) pool_tile_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y, PoolP p) {
+    extern __shared__ __align__(16) int16_t tile[];
+    const uint32_t ph = PH ? PH : p.ph, pw = PW ? PW : p.pw;
     const uint64_t blk = blockIdx.x;
     const uint64_t plane = blk / p.n_bands;
     const uint32_t band = (uint32_t)(blk - plane * p.n_bands);
     const uint32_t oh0 = band * p.band_rows;
     const uint32_t oh1 = min(p.out_h, oh0 + p.band_rows);
-    const int64_t ih_lo = (int64_t)oh0 * p.sh - (int64_t)p.pt;
-    const int64_t ih_hi = (int64_t)(oh1 - 1) * p.sh + (int64_t)(p.ph ? p.ph - 1 : 0) * p.dh - (int64_t)p.pt;
-    const int64_t r_lo = ih_lo > 0 ? ih_lo : 0;
-    const int64_t r_hi = ih_hi < (int64_t)p.in_h - 1 ? ih_hi : (int64_t)p.in_h - 1;
-    const uint64_t count = (r_hi >= r_lo && p.ph) ? (uint64_t)(r_hi - r_lo + 1) * p.in_w : 0;
+    const int32_t ih_lo = (int32_t)(oh0 * p.sh) - (int32_t)p.pt;
+    const uint32_t rows = (oh1 - 1 - oh0) * p.sh + (ph - 1) * p.dh + 1;
+    const uint32_t pitch = p.pitch, off0 = p.off0, in_w = p.in_w;
+    const int16_t pad = (TYPE == P_MAX) ? (int16_t)-32768 : (int16_t)0;
+    const int16_t* xp = x + plane * (uint64_t)p.in_h * in_w;
 
-    // Stage the contiguous input range; shared and global addresses share
-    // their offset mod 16 so the middle moves as 128-bit words.
-    const int16_t* src = x + plane * (uint64_t)p.in_h * p.in_w + (uint64_t)r_lo * p.in_w;
-    const uint32_t mis = (uint32_t)(((uintptr_t)src & 15u) >> 1);
-    int16_t* tile = smem + mis;
-    if (((uintptr_t)src & 1u) == 0) {
-        const uint64_t head = mis ? ((uint64_t)(8 - mis) < count ? (uint64_t)(8 - mis) : count) : 0;
-        const uint64_t nvec = (count - head) / 8;
-        for (uint64_t i = threadIdx.x; i < head; i += blockDim.x) tile[i] = src[i];
-        const uint4* s4 = (const uint4*)(src + head);
-        uint4* d4 = (uint4*)(tile + head);
-        for (uint64_t i = threadIdx.x; i < nvec; i += blockDim.x) d4[i] = __ldcs(s4 + i);
-        for (uint64_t i = head + nvec * 8 + threadIdx.x; i < count; i += blockDim.x) tile[i] = src[i];
+    // Rows of the tile that hold input data: [t_lo, t_hi) <-> input rows ih_lo + t.
+    const int32_t t_lo = max(0, -ih_lo);
+    const int32_t t_hi = max(t_lo, min((int32_t)rows, (int32_t)p.in_h - ih_lo));
+    // 1) identity in the padding: whole rows outside the input, and the side margins
+    {
+        const uint32_t lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+        for (uint32_t tr = threadIdx.x >> 5; tr < rows; tr += nwarps) {
+            int16_t* trow = tile + tr * pitch;
+            if ((int32_t)tr < t_lo || (int32_t)tr >= t_hi) {
+                for (uint32_t c = lane; c < pitch; c += 32) trow[c] = pad;
+            } else {
+                for (uint32_t c = lane; c < off0; c += 32) trow[c] = pad;
+                for (uint32_t c = off0 + in_w + lane; c < pitch; c += 32) trow[c] = pad;
+            }
+        }
+    }
+    // 2) input rows: one flat stream of 128-bit loads when every row starts 16-byte aligned
+    const int16_t* src = xp + (uint64_t)(ih_lo + t_lo) * in_w;
+    const uint32_t nrow = (uint32_t)(t_hi - t_lo);
+    if ((in_w & 7u) == 0 && ((uintptr_t)xp & 15u) == 0) {
+        const uint32_t vpr = in_w / 8, total = nrow * vpr;
+        const uint4* s4 = (const uint4*)src;
+        for (uint32_t i0 = threadIdx.x; i0 < total; i0 += 4 * blockDim.x) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t i = i0 + u * blockDim.x;
+                if (i < total) v[u] = __ldcs(s4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t i = i0 + u * blockDim.x;
+                if (i < total) {
+                    const uint32_t r = p.fd_vpr.div(i), c8 = i - r * vpr;
+                    *(uint4*)(tile + (t_lo + r) * pitch + off0 + 8 * c8) = v[u];
+                }
+            }
+        }
     } else {
-        for (uint64_t i = threadIdx.x; i < count; i += blockDim.x) tile[i] = src[i];
+        for (uint32_t i = threadIdx.x; i < nrow * in_w; i += blockDim.x) {
+            const uint32_t r = i / in_w, c = i - r * in_w;
+            tile[(t_lo + r) * pitch + off0 + c] = src[i];
+        }
     }
     __syncthreads();
 
     const uint32_t n_out = (oh1 - oh0) * p.out_w;
     int16_t* yp = y + plane * (uint64_t)p.out_h * p.out_w;
-    const uint32_t in_w = p.in_w;
+    const uint32_t drow = p.dh * pitch, shp = p.sh * pitch;
     for (uint32_t idx = threadIdx.x; idx < n_out; idx += blockDim.x) {
         const uint32_t q = p.fd_ow.div(idx);
         const uint32_t oh = oh0 + q, ow = idx - q * p.out_w;
-        yp[(uint64_t)oh * p.out_w + ow] = pool_pixel<TYPE>(
-            p, oh, ow, [&](int64_t ih, int64_t iw) { return (int32_t)tile[(uint64_t)(ih - r_lo) * in_w + iw]; });
+        const int16_t* base = tile + q * shp + off0 - p.pl + ow * p.sw;
+        int32_t m = -32768;
+        uint32_t sum = 0;
+#pragma unroll
+        for (uint32_t r = 0; r < (PH ? PH : 1u); ++r) {
+            for (uint32_t rr = (PH ? r : 0u); rr < (PH ? r + 1 : ph); ++rr) {
+                const int16_t* row = base + rr * drow;
+#pragma unroll
+                for (uint32_t s = 0; s < (PW ? PW : 1u); ++s) {
+                    for (uint32_t ss = (PW ? s : 0u); ss < (PW ? s + 1 : pw); ++ss) {
+                        const int32_t v = row[ss * p.dw];
+                        if (TYPE == P_MAX) m = max(m, v);
+                        else if (TYPE == P_AVG) sum += (uint32_t)v;
+                        else if (TYPE == P_LP1) sum += (uint32_t)(v < 0 ? -v : v);
+                        else sum += (uint32_t)(v * v);
+                    }
+                }
+            }
+        }
+        uint32_t acc;
+        if (TYPE == P_MAX) acc = (uint32_t)(m * 256);
+        else if (TYPE == P_LP2) acc = sum;
+        else acc = sum * 256u;
+        uint32_t denom = ph * pw;
+        if (TYPE == P_AVG && !p.cip) {
+            // valid taps = valid rows x valid columns of the window
+            uint32_t vr = 0, vc = 0;
+            for (uint32_t r = 0; r < ph; ++r) {
+                const int32_t ih = (int32_t)(oh * p.sh + r * p.dh) - (int32_t)p.pt;
+                vr += (ih >= 0 && ih < (int32_t)p.in_h);
+            }
+            for (uint32_t c = 0; c < pw; ++c) {
+                const int32_t iw = (int32_t)(ow * p.sw + c * p.dw) - (int32_t)p.pl;
+                vc += (iw >= 0 && iw < (int32_t)in_w);
+            }
+            denom = vr * vc;
+        }
+        yp[(uint64_t)oh * p.out_w + ow] = finalize<TYPE>(acc, denom);
     }
 }
 
@@ -167,13 +239,20 @@ __global__ void __launch_bounds__(256) pool_global_kernel(const int16_t* __restr
         if (((uintptr_t)xp & 15u) == 0) {
             const uint32_t nvec = hw / 8;
             const uint4* x4 = (const uint4*)xp;
-            for (uint32_t i = lane; i < nvec; i += 32) {
-                const uint4 v = __ldcs(x4 + i);
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+            for (uint32_t i0 = lane; i0 < nvec; i0 += 4 * 32) {
+                uint4 v[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    reduce_word<TYPE>(acc, (int32_t)(int16_t)(w[j] & 0xFFFF));
-                    reduce_word<TYPE>(acc, (int32_t)(int16_t)(w[j] >> 16));
+                for (int u = 0; u < 4; ++u)
+                    if (i0 + 32 * u < nvec) v[u] = __ldcs(x4 + i0 + 32 * u);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    if (i0 + 32 * u >= nvec) break;
+                    const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        reduce_word<TYPE>(acc, (int32_t)(int16_t)(w[j] & 0xFFFF));
+                        reduce_word<TYPE>(acc, (int32_t)(int16_t)(w[j] >> 16));
+                    }
                 }
             }
             for (uint32_t i = nvec * 8 + lane; i < hw; i += 32) reduce_word<TYPE>(acc, xp[i]);
@@ -211,22 +290,36 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         return CM_OK;
     }
     PoolP p = p0;
+    // Padded-tile kernel when one output row's window rows fit the budget and all
+    // tile offsets fit comfortably in 32 bits.
     const uint64_t win_rows = (uint64_t)(p.ph ? p.ph - 1 : 0) * p.dh + 1;
-    const uint64_t max_rows = (kSmemBudget - 16) / 2 / (p.in_w ? p.in_w : 1);
-    if (win_rows <= max_rows && p.in_w > 0) {
+    const uint64_t off0 = ((uint64_t)p.pl + 7) & ~7ull;
+    const uint64_t span = off0 - p.pl + (uint64_t)(p.out_w - 1) * p.sw + (uint64_t)(p.pw ? p.pw - 1 : 0) * p.dw + 1;
+    const uint64_t pitch = (std::max<uint64_t>(off0 + p.in_w, span) + 7) & ~7ull;
+    const bool small = p.in_h < (1u << 24) && p.in_w < (1u << 24) && p.out_h < (1u << 24) && p.pt < (1u << 24) &&
+                       (uint64_t)p.sh * p.out_h < (1ull << 30) && win_rows < (1ull << 24);
+    if (p.ph > 0 && p.pw > 0 && small && win_rows * pitch * 2 <= kSmemBudget) {
         uint64_t band = p.out_h;
+        const uint64_t max_rows = kSmemBudget / (pitch * 2);
         if (p.sh > 0) band = std::min<uint64_t>(band, (max_rows - win_rows) / p.sh + 1);
         if (band == 0) band = 1;
         p.band_rows = (uint32_t)band;
         p.n_bands = (uint32_t)((p.out_h + band - 1) / band);
+        p.pitch = (uint32_t)pitch;
+        p.off0 = (uint32_t)off0;
         p.fd_ow = FastDiv(p.out_w);
-        const uint64_t rows_needed = std::min<uint64_t>((uint64_t)(band - 1) * p.sh + win_rows, p.in_h ? p.in_h : 1);
-        const size_t smem = (size_t)rows_needed * p.in_w * 2 + 16;
+        p.fd_vpr = FastDiv(std::max<uint32_t>(p.in_w / 8, 1u));
+        const size_t smem = (size_t)((band - 1) * p.sh + win_rows) * pitch * 2;
         const uint64_t blocks = planes * p.n_bands;
         if (blocks >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "cm_pool: too many planes");
         {
             ProfScope ps_(PK_POOL, s);
-            pool_window_kernel<TYPE><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+            if (p.ph == 3 && p.pw == 3)
+                pool_tile_kernel<TYPE, 3, 3><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+            else if (p.ph == 2 && p.pw == 2)
+                pool_tile_kernel<TYPE, 2, 2><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+            else
+                pool_tile_kernel<TYPE, 0, 0><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
         }
     } else {
         const uint64_t total = planes * p.out_h * p.out_w;

@@ -24,20 +24,37 @@ namespace {
 
 enum { K_ADD = 0, K_SUB, K_MUL, K_DIV, K_RELU, K_RELU6, K_COPY };
 
-// trunc((a * 256) / b) for b != 0, exact.  |a*256| < 2^23 and |b| <= 2^15 are
-// exact in float; the quotient estimate un * rcp(ud) carries a relative error
-// below 2^-23, so for a true quotient below 2^23 it is off by less than one and
-// truncates to q-1, q or q+1; one remainder test in each direction fixes it
-// (reciprocal estimate plus integer correction, e.g. Hacker's Delight ch. 10).
+// Exact conversions for 0 <= x <= 2^23 by the classic bias trick: the integer
+// is placed in the mantissa of 2^23 (bit pattern 0x4B000000 + x), and 2^23 is
+// subtracted in float -- two full-rate ops instead of a quarter-rate convert.
+__device__ __forceinline__ float u23_to_f(uint32_t x) {
+    return __fsub_rn(__uint_as_float(0x4B000000u + x), 8388608.0f);
+}
+// Nearest integer (ties to even) of 0 <= f < 2^23, by the same bias.
+__device__ __forceinline__ uint32_t f_to_u23_rn(float f) {
+    return __float_as_uint(__fadd_rn(f, 8388608.0f)) - 0x4B000000u;
+}
+
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+
+// trunc((a * 256) / b) for b != 0, exact, as far as int16 saturation can tell.
+// un = |a*256| <= 2^23 and ud = |b| in [1, 2^15] are exact in float.  rcp.approx
+// has a relative error below 2^-23 and the product adds at most 2^-24, so for a
+// true quotient Q = un/ud < 2^21 the estimate qf is within 0.38 of Q and its
+// nearest integer is floor(Q) or floor(Q)+1; one remainder test removes the
+// excess (reciprocal estimate plus integer correction, Hacker's Delight ch. 10).
+// For Q >= 2^21 every candidate saturates to the same int16 as the exact value.
 __device__ __forceinline__ int32_t div_q88(int32_t a, int32_t b) {
     const int32_t n = a * 256;
     const uint32_t un = (uint32_t)(n < 0 ? -n : n);
     const uint32_t ud = (uint32_t)(b < 0 ? -b : b);
-    const float qf = __fmul_rn(__uint2float_rn(un), __frcp_rn(__uint2float_rn(ud)));
-    uint32_t q = __float2uint_rz(qf);
-    const int32_t r = (int32_t)(un - q * ud);   // true remainder is in (-ud, 2ud): exact mod 2^32
-    if (r < 0) q -= 1;
-    else if (r >= (int32_t)ud) q += 1;
+    const float qf = __fmul_rn(u23_to_f(un), rcp_approx(u23_to_f(ud)));
+    uint32_t q = f_to_u23_rn(qf);
+    if ((int32_t)(un - q * ud) < 0) q -= 1;     // true remainder is in (-ud, ud): exact mod 2^32
     return ((n ^ b) < 0) ? -(int32_t)q : (int32_t)q;
 }
 

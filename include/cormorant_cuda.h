@@ -116,8 +116,8 @@ int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, 
  * of CM_MATMUL_NOALLOC_SCRATCH_BYTES, held on every GPU that loads the library
  * until the process exits.  Calls whose scratch need exceeds it return
  * CM_EINVAL; the need is, in bytes (each term rounded up to 256):
- *   A_b*2*n*K16 + B_b*2*m*K16 + A_b*n*4 + B_b*m*4,
- *   K16 = k rounded up to 16, A_b = (a_batch_stride ? batch : 1), B_b likewise.
+ *   A_b*2*n*K16 + B_b*2*k*M16 + A_b*n*4 + B_b*m*4,
+ *   K16, M16 = k, m rounded up to 16, A_b = (a_batch_stride ? batch : 1), B_b likewise.
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any stream
  * capture.  All calls share the one array: calls that can overlap on the GPU
