@@ -32,6 +32,8 @@ import sys
 import time
 from pathlib import Path
 
+import numpy as np
+
 ROOT = Path(__file__).resolve().parent
 if str(ROOT) not in sys.path:
     sys.path.insert(0, str(ROOT))
@@ -418,7 +420,109 @@ class PoolSweep:
         self.Y.free()
 
 
-WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep}
+class NetworkBench:
+    """LeNet-5 (config 0, batch 1, CUDA-graph replay) or ResNet-18-shaped (config 3, batch 256)."""
+    unit = "images/s"
+    dominant = "gemm_q88"
+
+    def __init__(self, rank, world, which):
+        from cormorant_b200 import networks
+        self.which, self.rank, self.world = which, rank, world
+        if which == "lenet":
+            self.batch_total, self.local = 1 * world, 1          # replicas: one batch-1 stream per GPU
+            self.net = networks.lenet5(batch=1)
+            self.metric = "LeNet-5 images/s (batch 1 per GPU, CUDA-graph replay)"
+        else:
+            _, self.local = shard(256, rank, world)
+            self.batch_total = 256
+            self.net = networks.resnet18(batch=max(self.local, 1))
+            self.metric = "ResNet-18-shaped images/s (batch 256)"
+        self.units_total = float(self.batch_total)
+        self.units_local = float(self.local)
+        self.dom_units_local = 8.0 * self.net.macs_per_image * self.local   # int8 ops (4 MMAs x 2 per MAC)
+
+    def config(self, world):
+        if self.which == "lenet":
+            return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
+                    "parallelism": f"replicas only: one batch-1 stream per GPU ({world})",
+                    "launches": "whole call list captured once as a CUDA graph and replayed"}
+        return {"workload": "resnet18-shaped (BASELINE configs[3])", "batch": 256,
+                "input": "256x3x224x224 uniform [0,1)", "macs_per_image": self.net.macs_per_image,
+                "parallelism": f"batch-sharded over {world} GPU(s)", "l2": "inputs larger than L2 (77 MB input, 1.1 GB activations)"}
+
+    def setup(self):
+        import torch
+        from cormorant_b200 import networks
+        self.x = networks.make_input(self.net)
+        self.bufs = networks.gpu_buffers(self.net, self.x)
+        self.graph = None
+        if self.which == "lenet":
+            import cormorant_b200 as cm
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for _ in range(3):            # warm: module loading and attribute setup happen outside capture
+                    networks.execute(self.net, networks.GpuBackend(s), self.bufs)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            l0 = cm.launch_count()
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream()), self.bufs)
+            self.launches_per_step = cm.launch_count() - l0
+            torch.cuda.synchronize()
+
+    def step(self, cm, stream):
+        from cormorant_b200 import networks
+        if self.graph is not None:
+            self.graph.replay()
+        elif self.local > 0:
+            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+
+    def per_part(self, cm, stream, iters):
+        import ctypes as C
+        import torch
+        from cormorant_b200 import networks
+        L = cm.lib()
+        L.cm_profile_begin()
+        for _ in range(iters):
+            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+        torch.cuda.synchronize()
+        L.cm_profile_end()
+        out = {}
+        for kind in ("gemm_q88", "split", "pool", "vectorop", "conv_aux"):
+            ms, cnt = C.c_double(), C.c_uint64()
+            L.cm_profile_read(kind.encode(), C.byref(ms), C.byref(cnt))
+            out[kind + "_ms"] = round(ms.value / iters, 4)
+        return [out]
+
+    def release(self):
+        self.bufs = None
+        self.graph = None
+
+    def e2e_setup(self):
+        import torch
+        from cormorant_b200 import networks
+        self.bufs = networks.gpu_buffers(self.net)
+        self.hx = torch.from_numpy(self.x.copy()).pin_memory()
+        out_words = self.net.buffers[self.net.resolve(self.net.output)]
+        self.hy = torch.empty(out_words, dtype=torch.int16).pin_memory()
+        self.h2d = self.hx.numel() * 2
+        self.d2h = out_words * 2
+
+    def e2e_step(self):
+        import torch
+        from cormorant_b200 import networks
+        self.bufs[self.net.input].copy_(self.hx, non_blocking=True)
+        networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream()), self.bufs)
+        self.hy.copy_(self.bufs[self.net.resolve(self.net.output)], non_blocking=True)
+
+    def e2e_release(self):
+        self.bufs = None
+
+
+WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
+             "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
 
 
 # --------------------------------------------------------------------------------------
@@ -458,6 +562,43 @@ def _cpu_worker(args):
             chk.vectorop(a, b, n, op)
             units += (3 if op < 4 else 2) * n * 2.0 / 1e9
         dt = time.perf_counter() - t0
+    elif config in ("lenet", "resnet"):
+        from cormorant_b200 import networks     # the call list only (pure Python, no GPU)
+        net = networks.lenet5(batch=1) if config == "lenet" else networks.resnet18(batch=1)
+        x = networks.make_input(net)
+        bufs = {name: np.zeros(max(w, 1), np.int16) for name, w in net.buffers.items()}
+        bufs.update({name: np.asarray(a, np.int16) for name, a in net.consts.items()})
+        bufs[net.input][:] = x
+        R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
+        dt = 0.0
+        for node in net.nodes:
+            nk = node[0]
+            t0 = time.perf_counter()
+            scale = 1.0
+            if nk == "conv":
+                _, xn, wn, bn, yn, a = node
+                a = list(a)
+                m = a[4]
+                if config == "resnet" and m > 8:
+                    # the reference's output-channel tile (TILE_M = 8); time scaled by m / 8
+                    per = a[1] * a[7] * a[8]
+                    w8, b8 = R(wn)[: 8 * per], (R(bn)[:8] if bn else None)
+                    a[4] = 8
+                    chk.conv(R(xn), w8, b8, *a)
+                    scale = m / 8.0
+                else:
+                    R(yn)[:] = chk.conv(R(xn), R(wn), R(bn), *a)[: R(yn).size]
+            elif nk == "vectorop":
+                _, an, bn, cn, a = node
+                R(cn)[:] = chk.vectorop(R(an), R(bn), *a, c=R(cn).copy())[: R(cn).size]
+            elif nk == "pool":
+                _, xn, yn, a = node
+                R(yn)[:] = chk.pool(R(xn), *a)[: R(yn).size]
+            else:
+                _, an, bn, cn, a = node
+                R(cn)[:] = chk.matmul(R(an), R(bn), *a)[: R(cn).size]
+            dt += (time.perf_counter() - t0) * scale
+        units = 1.0
     else:
         N, C, H, W = POOL_SHAPE
         nb, cs = 1, 8
@@ -475,6 +616,9 @@ SAMPLE_TEXT = {
     "matmul": "4 output rows of one batch item per sweep shape per worker process (reference MatmulKernel with n=4)",
     "vectorop": "2^20 elements per op per worker process",
     "pool": "one image x 8 channels of [.,64,112,112] per variant per worker process",
+    "lenet": "one whole LeNet-5 inference (batch 1) per worker process",
+    "resnet": ("one ResNet-18 image per worker process; each conv layer computes 8 of its output channels "
+               "(the reference's TILE_M) and its time is scaled by out_ch / 8; pools and vector ops run in full"),
 }
 
 
@@ -492,13 +636,17 @@ def cpu_sample(config: str, workers: int, pool=None):
         pool.join()
     units = sum(r[0] for r in res)
     kind = res[0][2]
+    if config == "resnet":
+        # scaled per-image estimates: the workers run in parallel, each at 1/dt images per second
+        rate = sum(r[0] / r[1] for r in res)
+        return rate, 1.0, kind
     return units, wall, kind
 
 
 def cpu_units_to_value(config, units, seconds):
     if config == "matmul":
         return units / seconds / 1e9       # GOPS
-    return units / seconds                 # GB/s (units already in GB)
+    return units / seconds                 # GB/s (units already in GB) or images/s
 
 
 def int8_peak() -> int:
@@ -652,11 +800,17 @@ def main():
     value = wl.units_total / (ms_per_step * 1e-3)
     if args.config == "matmul":
         value /= 1e9
+    if getattr(wl, "graph", None) is not None:
+        launches = wl.launches_per_step * K        # graph replays launch the captured kernels
     launches_total = int(sum_over_ranks(float(launches)))
 
     peaks = load_peaks()
     # achieved on the dominant kernel (rank 0): algorithmic units of all its launches / their device time
-    if args.config == "matmul":
+    if args.config == "lenet":
+        roof = {"bound": "launch", "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
+                "kernel": "whole network, CUDA graph",
+                "note": "0.83 MOPs per image: latency-bound; no roofline fraction (too small)"}
+    elif wl.dominant == "gemm_q88":
         achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e12 if dms.value > 0 else 0.0
         # burst figure for a timed region of about a second or less, sustained beyond
         which = "bf16_sustained" if elapsed_ms > 1500.0 else "bf16"
@@ -713,8 +867,8 @@ def main():
     if rank == 0:
         line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": K, "warmup": W,
                 "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "q8.8 int16 (ap_fixed<16,8>); s8 tcgen05 MMA, s32 accumulate" if args.config == "matmul"
-                else "q8.8 int16 (ap_fixed<16,8>), int32 / IEEE f32 epilogue",
+                "dtype": "q8.8 int16 (ap_fixed<16,8>); s8 tcgen05 MMA, s32 accumulate"
+                if wl.dominant == "gemm_q88" else "q8.8 int16 (ap_fixed<16,8>), int32 / IEEE f32 epilogue",
                 "data": "synthetic (seeded)", "config": wl.config(world), "roofline": roof,
                 "cpu_baseline": cpu_line, "e2e": e2e, "gpu_launches": launches_total, "clocks": clocks}
         if per_part is not None:

@@ -163,8 +163,10 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+constexpr uint32_t GROUP_M = 8;
+
 struct GemmArgs {
-    uint32_t rows, cols, num_kb, a_batches, b_batches;
+    uint32_t rows, cols, num_kb, a_batches, b_batches, tiles_m, tiles_n;
     const int32_t* rowterm;
     const int32_t* colterm;
     int16_t* out;
@@ -184,8 +186,15 @@ __global__ void __launch_bounds__(192, 1)
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint32_t n0 = blockIdx.x * BN;   // output column tile (B rows)
-    const uint32_t m0 = blockIdx.y * BM;   // output row tile (A rows)
+    // Grouped tile order: blocks of GROUP_M row tiles sweep the column tiles
+    // together, so the CTAs in flight share a few A and B panels in L2.
+    const uint32_t per_group = GROUP_M * g.tiles_n;
+    const uint32_t group = blockIdx.x / per_group;
+    const uint32_t first_m = group * GROUP_M;
+    const uint32_t gsize = min(GROUP_M, g.tiles_m - first_m);
+    const uint32_t local = blockIdx.x - group * per_group;
+    const uint32_t m0 = (first_m + local % gsize) * BM;   // output row tile (A rows)
+    const uint32_t n0 = (local / gsize) * BN;             // output column tile (B columns)
     const uint32_t z = blockIdx.z + g.z_base;
     const uint32_t ba = g.a_batches == 1 ? 0u : z;
     const uint32_t bb = g.b_batches == 1 ? 0u : z;
@@ -561,6 +570,9 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     }
     GemmArgs g;
     g.rows = p.rows; g.cols = p.cols; g.num_kb = (p.K + BK - 1) / BK;
+    g.tiles_m = (p.rows + BM - 1) / BM;
+    g.tiles_n = (p.cols + BN - 1) / BN;
+    if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
     g.a_batches = p.a_batches; g.b_batches = p.b_batches;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
     g.out = p.out; g.ldo = p.ldo; g.out_bs = p.out_bs;
@@ -569,7 +581,7 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     for (uint32_t z0 = 0; z0 < p.batch; z0 += 65535u) {
         const uint32_t nz = min(65535u, p.batch - z0);
         g.z_base = z0;
-        const dim3 grid((p.cols + BN - 1) / BN, (p.rows + BM - 1) / BM, nz);
+        const dim3 grid(g.tiles_m * g.tiles_n, 1, nz);
         {
             ProfScope ps_(PK_GEMM, s);
             gemm_q88_kernel<<<grid, block, SMEM_BYTES, s>>>(ta, tb, g);

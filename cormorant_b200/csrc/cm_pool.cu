@@ -49,7 +49,7 @@ __device__ __forceinline__ int16_t finalize(uint32_t acc, uint32_t denom) {
 
 struct PoolP {
     uint32_t in_h, in_w, out_h, out_w, ph, pw, sh, sw, pt, pl, dh, dw, cip;
-    uint32_t band_rows, n_bands, pitch, off0;
+    uint32_t band_rows, n_bands, pitch, off0, buf_elems, row_groups;
     FastDiv fd_ow, fd_vpr;
 };
 
@@ -88,118 +88,171 @@ __device__ __forceinline__ int16_t pool_pixel(const PoolP& p, uint32_t oh, uint3
     return finalize<TYPE>(acc, p.cip ? p.ph * p.pw : valid);
 }
 
-// Window kernel.  The CTA's band of output rows touches input rows
-// [ih_lo, ih_lo + rows) and columns [-pad_left, ...); they are staged in shared
-// memory as a padded tile whose out-of-range cells hold the window identity
-// (-128.0 for MAX, 0 otherwise), so taps need no bounds checks and all offsets
-// are 32-bit.  Column iw lives at tile column off0 + iw, off0 a multiple of 8,
-// so 16-byte-aligned input rows copy as 128-bit words.  PH/PW > 0 fix the
-// window size at compile time (fully unrolled taps); 0 means "from p".
-template <int TYPE, int PH, int PW>
-__global__ void __launch_bounds__(256) pool_tile_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y, PoolP p) {
-    extern __shared__ __align__(16) int16_t tile[];
+// Window kernel (persistent, double-buffered).  Work item = (plane, band of
+// output rows).  A band's input rows [ih_lo, ih_lo + rows) and columns
+// [-pad_left, ...) are staged in shared memory as a padded tile whose
+// out-of-range cells hold the window identity (-128.0 for MAX, 0 otherwise), so
+// taps need no bounds checks.  Column iw lives at tile column off0 + iw with
+// off0 a multiple of 8, so 16-byte-aligned input rows are copied with 16-byte
+// cp.async; each CTA fetches its next item into the second buffer while it
+// computes the current one.  PH..DW > 0 fix the window geometry at compile time
+// (fully unrolled taps with immediate offsets); 0 means "from p".
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(smem_dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
+
+template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW>
+__global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
+                                                          PoolP p, uint64_t items, uint32_t aligned) {
+    extern __shared__ __align__(16) int16_t smem[];
+    __shared__ float inv_tab[65];
     const uint32_t ph = PH ? PH : p.ph, pw = PW ? PW : p.pw;
-    const uint64_t blk = blockIdx.x;
-    const uint64_t plane = blk / p.n_bands;
-    const uint32_t band = (uint32_t)(blk - plane * p.n_bands);
-    const uint32_t oh0 = band * p.band_rows;
-    const uint32_t oh1 = min(p.out_h, oh0 + p.band_rows);
-    const int32_t ih_lo = (int32_t)(oh0 * p.sh) - (int32_t)p.pt;
-    const uint32_t rows = (oh1 - 1 - oh0) * p.sh + (ph - 1) * p.dh + 1;
+    const uint32_t sh = SH ? SH : p.sh, sw = SW ? SW : p.sw;
+    const uint32_t dh = DH ? DH : p.dh, dw = DW ? DW : p.dw;
     const uint32_t pitch = p.pitch, off0 = p.off0, in_w = p.in_w;
     const int16_t pad = (TYPE == P_MAX) ? (int16_t)-32768 : (int16_t)0;
-    const int16_t* xp = x + plane * (uint64_t)p.in_h * in_w;
+    if (TYPE == P_AVG && threadIdx.x < 65) inv_tab[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, (float)threadIdx.x) : 0.0f;
 
-    // Rows of the tile that hold input data: [t_lo, t_hi) <-> input rows ih_lo + t.
-    const int32_t t_lo = max(0, -ih_lo);
-    const int32_t t_hi = max(t_lo, min((int32_t)rows, (int32_t)p.in_h - ih_lo));
-    // 1) identity in the padding: whole rows outside the input, and the side margins
-    {
+    // Stage item `it` into `tile`: identity margins with plain stores, input rows
+    // with cp.async (committed as one group) or plain copies when misaligned.
+    auto issue = [&](uint64_t it, uint32_t tb) {   // tb: element offset of the tile buffer in smem
+        const uint64_t plane = it / p.n_bands;
+        const uint32_t band = (uint32_t)(it - plane * p.n_bands);
+        const uint32_t oh0 = band * p.band_rows, oh1 = min(p.out_h, oh0 + p.band_rows);
+        const int32_t ih_lo = (int32_t)(oh0 * sh) - (int32_t)p.pt;
+        const uint32_t rows = (oh1 - 1 - oh0) * sh + (ph - 1) * dh + 1;
+        const int32_t t_lo = max(0, -ih_lo);
+        const int32_t t_hi = max(t_lo, min((int32_t)rows, (int32_t)p.in_h - ih_lo));
         const uint32_t lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
         for (uint32_t tr = threadIdx.x >> 5; tr < rows; tr += nwarps) {
-            int16_t* trow = tile + tr * pitch;
+            const uint32_t trow = tb + tr * pitch;
             if ((int32_t)tr < t_lo || (int32_t)tr >= t_hi) {
-                for (uint32_t c = lane; c < pitch; c += 32) trow[c] = pad;
+                for (uint32_t c = lane; c < pitch; c += 32) smem[trow + c] = pad;
             } else {
-                for (uint32_t c = lane; c < off0; c += 32) trow[c] = pad;
-                for (uint32_t c = off0 + in_w + lane; c < pitch; c += 32) trow[c] = pad;
+                for (uint32_t c = lane; c < off0; c += 32) smem[trow + c] = pad;
+                for (uint32_t c = off0 + in_w + lane; c < pitch; c += 32) smem[trow + c] = pad;
             }
         }
-    }
-    // 2) input rows: one flat stream of 128-bit loads when every row starts 16-byte aligned
-    const int16_t* src = xp + (uint64_t)(ih_lo + t_lo) * in_w;
-    const uint32_t nrow = (uint32_t)(t_hi - t_lo);
-    if ((in_w & 7u) == 0 && ((uintptr_t)xp & 15u) == 0) {
-        const uint32_t vpr = in_w / 8, total = nrow * vpr;
-        const uint4* s4 = (const uint4*)src;
-        for (uint32_t i0 = threadIdx.x; i0 < total; i0 += 4 * blockDim.x) {
-            uint4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t i = i0 + u * blockDim.x;
-                if (i < total) v[u] = __ldcs(s4 + i);
+        const int16_t* src = x + plane * (uint64_t)p.in_h * in_w + (uint64_t)(ih_lo + t_lo) * in_w;
+        const uint32_t nrow = (uint32_t)(t_hi - t_lo);
+        if (aligned) {
+            const uint32_t vpr = in_w / 8, total = nrow * vpr;
+            for (uint32_t i = threadIdx.x; i < total; i += blockDim.x) {
+                const uint32_t r = p.fd_vpr.div(i), c8 = i - r * vpr;
+                cp_async16(&smem[tb + (t_lo + r) * pitch + off0 + 8 * c8], src + 8 * (uint64_t)i);
             }
-#pragma unroll
-            for (int u = 0; u < 4; ++u) {
-                const uint32_t i = i0 + u * blockDim.x;
-                if (i < total) {
-                    const uint32_t r = p.fd_vpr.div(i), c8 = i - r * vpr;
-                    *(uint4*)(tile + (t_lo + r) * pitch + off0 + 8 * c8) = v[u];
-                }
+        } else {
+            for (uint32_t i = threadIdx.x; i < nrow * in_w; i += blockDim.x) {
+                const uint32_t r = i / in_w, c = i - r * in_w;
+                smem[tb + (t_lo + r) * pitch + off0 + c] = src[i];
             }
         }
-    } else {
-        for (uint32_t i = threadIdx.x; i < nrow * in_w; i += blockDim.x) {
-            const uint32_t r = i / in_w, c = i - r * in_w;
-            tile[(t_lo + r) * pitch + off0 + c] = src[i];
-        }
-    }
-    __syncthreads();
+        cp_async_commit();
+    };
 
-    const uint32_t n_out = (oh1 - oh0) * p.out_w;
-    int16_t* yp = y + plane * (uint64_t)p.out_h * p.out_w;
-    const uint32_t drow = p.dh * pitch, shp = p.sh * pitch;
-    for (uint32_t idx = threadIdx.x; idx < n_out; idx += blockDim.x) {
-        const uint32_t q = p.fd_ow.div(idx);
-        const uint32_t oh = oh0 + q, ow = idx - q * p.out_w;
-        const int16_t* base = tile + q * shp + off0 - p.pl + ow * p.sw;
-        int32_t m = -32768;
-        uint32_t sum = 0;
-#pragma unroll
-        for (uint32_t r = 0; r < (PH ? PH : 1u); ++r) {
-            for (uint32_t rr = (PH ? r : 0u); rr < (PH ? r + 1 : ph); ++rr) {
-                const int16_t* row = base + rr * drow;
-#pragma unroll
-                for (uint32_t s = 0; s < (PW ? PW : 1u); ++s) {
-                    for (uint32_t ss = (PW ? s : 0u); ss < (PW ? s + 1 : pw); ++ss) {
-                        const int32_t v = row[ss * p.dw];
-                        if (TYPE == P_MAX) m = max(m, v);
-                        else if (TYPE == P_AVG) sum += (uint32_t)v;
-                        else if (TYPE == P_LP1) sum += (uint32_t)(v < 0 ? -v : v);
-                        else sum += (uint32_t)(v * v);
-                    }
+    // Compute item `it` from tile buffer `tb`.  Thread t owns output column ow of
+    // row group g (t = g*out_w + ow) and walks that group's consecutive output
+    // rows, so per output there are only the taps and two pointer increments.
+    auto compute = [&](uint64_t it, uint32_t tb) {
+        const uint64_t plane = it / p.n_bands;
+        const uint32_t band = (uint32_t)(it - plane * p.n_bands);
+        const uint32_t oh0 = band * p.band_rows, oh1 = min(p.out_h, oh0 + p.band_rows);
+        const uint32_t nr = oh1 - oh0, G = p.row_groups;
+        const uint32_t rpg = (nr + G - 1) / G;
+        const uint32_t rowstep = dh * pitch, advance = sh * pitch;
+        for (uint32_t t = threadIdx.x; t < G * p.out_w; t += blockDim.x) {
+            const uint32_t g = p.fd_ow.div(t), ow = t - g * p.out_w;
+            const uint32_t r0 = g * rpg, r1 = min(nr, r0 + rpg);
+            if (r0 >= r1) continue;
+            uint32_t base = tb + r0 * advance + off0 - p.pl + ow * sw;
+            int16_t* yo = y + plane * (uint64_t)p.out_h * p.out_w + (uint64_t)(oh0 + r0) * p.out_w + ow;
+            uint32_t vc = pw;       // AVG without padding in the divisor: valid columns of this ow
+            if (TYPE == P_AVG && !p.cip) {
+                vc = 0;
+                for (uint32_t c = 0; c < pw; ++c) {
+                    const int32_t iw = (int32_t)(ow * sw + c * dw) - (int32_t)p.pl;
+                    vc += (iw >= 0 && iw < (int32_t)in_w);
                 }
             }
-        }
-        uint32_t acc;
-        if (TYPE == P_MAX) acc = (uint32_t)(m * 256);
-        else if (TYPE == P_LP2) acc = sum;
-        else acc = sum * 256u;
-        uint32_t denom = ph * pw;
-        if (TYPE == P_AVG && !p.cip) {
-            // valid taps = valid rows x valid columns of the window
-            uint32_t vr = 0, vc = 0;
-            for (uint32_t r = 0; r < ph; ++r) {
-                const int32_t ih = (int32_t)(oh * p.sh + r * p.dh) - (int32_t)p.pt;
-                vr += (ih >= 0 && ih < (int32_t)p.in_h);
+            // Window reduction of output row q (tile offset b); compile-time windows
+            // gather all taps first and reduce them as a tree to keep chains short.
+            auto reduce = [&](uint32_t b) -> uint32_t {
+                if (PH && PW) {
+                    int32_t v[(PH * PW > 0) ? PH * PW : 1];
+#pragma unroll
+                    for (uint32_t r = 0; r < (uint32_t)PH; ++r)
+#pragma unroll
+                        for (uint32_t c = 0; c < (uint32_t)PW; ++c) v[r * PW + c] = smem[b + r * rowstep + c * dw];
+#pragma unroll
+                    for (uint32_t i = 0; i < PH * PW; ++i) {
+                        if (TYPE == P_LP1) v[i] = v[i] < 0 ? -v[i] : v[i];
+                        else if (TYPE == P_LP2) v[i] = v[i] * v[i];
+                    }
+#pragma unroll
+                    for (uint32_t w = 1; w < PH * PW; w *= 2)
+#pragma unroll
+                        for (uint32_t i = 0; i + w < PH * PW; i += 2 * w)
+                            v[i] = (TYPE == P_MAX) ? max(v[i], v[i + w]) : (int32_t)((uint32_t)v[i] + (uint32_t)v[i + w]);
+                    return (TYPE == P_MAX) ? (uint32_t)(v[0] * 256) : (TYPE == P_LP2 ? (uint32_t)v[0] : (uint32_t)v[0] * 256u);
+                } else {
+                    int32_t m = -32768;
+                    uint32_t sum = 0;
+                    for (uint32_t r = 0; r < ph; ++r) {
+                        const uint32_t row = b + r * rowstep;
+                        for (uint32_t c = 0; c < pw; ++c) {
+                            const int32_t x1 = smem[row + c * dw];
+                            if (TYPE == P_MAX) m = max(m, x1);
+                            else if (TYPE == P_AVG) sum += (uint32_t)x1;
+                            else if (TYPE == P_LP1) sum += (uint32_t)(x1 < 0 ? -x1 : x1);
+                            else sum += (uint32_t)(x1 * x1);
+                        }
+                    }
+                    return (TYPE == P_MAX) ? (uint32_t)(m * 256) : (TYPE == P_LP2 ? sum : sum * 256u);
+                }
+            };
+            auto emit = [&](uint32_t acc, uint32_t q) -> int16_t {
+                if (TYPE == P_AVG) {
+                    uint32_t denom = ph * pw;
+                    if (!p.cip) {
+                        uint32_t vr = 0;
+                        const int32_t ihq = (int32_t)((oh0 + q) * sh) - (int32_t)p.pt;
+#pragma unroll
+                        for (uint32_t r = 0; r < (PH ? (uint32_t)PH : ph); ++r) {
+                            const int32_t ih = ihq + (int32_t)(r * dh);
+                            vr += (ih >= 0 && ih < (int32_t)p.in_h);
+                        }
+                        denom = vr * vc;
+                    }
+                    const float inv = denom <= 64u ? inv_tab[denom] : __fdiv_rn(1.0f, __uint2float_rn(denom));
+                    return narrow_acc(acc_from_float(__fmul_rn(acc_to_float(acc), inv)));
+                }
+                return finalize<TYPE>(acc, 0);
+            };
+            uint32_t q = r0;
+            for (; q + 2 <= r1; q += 2, base += 2 * advance, yo += 2 * p.out_w) {
+                const uint32_t a0 = reduce(base), a1 = reduce(base + advance);
+                yo[0] = emit(a0, q);
+                yo[p.out_w] = emit(a1, q + 1);
             }
-            for (uint32_t c = 0; c < pw; ++c) {
-                const int32_t iw = (int32_t)(ow * p.sw + c * p.dw) - (int32_t)p.pl;
-                vc += (iw >= 0 && iw < (int32_t)in_w);
-            }
-            denom = vr * vc;
+            if (q < r1) *yo = emit(reduce(base), q);
         }
-        yp[(uint64_t)oh * p.out_w + ow] = finalize<TYPE>(acc, denom);
+    };
+
+    uint32_t cur = 0, other = p.buf_elems;
+    uint64_t it = blockIdx.x;
+    if (it < items) issue(it, cur);
+    for (; it < items; it += gridDim.x) {
+        const uint64_t nxt = it + gridDim.x;
+        if (nxt < items) issue(nxt, other);
+        else cp_async_commit();            // empty group keeps the wait count uniform
+        cp_async_wait1();                  // item `it` has landed
+        __syncthreads();
+        compute(it, cur);
+        __syncthreads();                   // the buffer may be refilled next
+        const uint32_t t = cur; cur = other; other = t;
     }
 }
 
@@ -275,7 +328,8 @@ __global__ void __launch_bounds__(256) pool_global_kernel(const int16_t* __restr
     }
 }
 
-constexpr size_t kSmemBudget = 48 * 1024;
+// Per tile buffer (two per CTA): small enough for 8 resident CTAs per SM.
+constexpr size_t kSmemBudget = 16 * 1024;
 
 template <int TYPE>
 int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, const PoolP& p0, bool global,
@@ -299,6 +353,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
     const bool small = p.in_h < (1u << 24) && p.in_w < (1u << 24) && p.out_h < (1u << 24) && p.pt < (1u << 24) &&
                        (uint64_t)p.sh * p.out_h < (1ull << 30) && win_rows < (1ull << 24);
     if (p.ph > 0 && p.pw > 0 && small && win_rows * pitch * 2 <= kSmemBudget) {
+        // Two tile buffers per CTA (double buffering); each at most kSmemBudget / 2 ... kSmemBudget.
         uint64_t band = p.out_h;
         const uint64_t max_rows = kSmemBudget / (pitch * 2);
         if (p.sh > 0) band = std::min<uint64_t>(band, (max_rows - win_rows) / p.sh + 1);
@@ -309,17 +364,32 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         p.off0 = (uint32_t)off0;
         p.fd_ow = FastDiv(p.out_w);
         p.fd_vpr = FastDiv(std::max<uint32_t>(p.in_w / 8, 1u));
-        const size_t smem = (size_t)((band - 1) * p.sh + win_rows) * pitch * 2;
-        const uint64_t blocks = planes * p.n_bands;
-        if (blocks >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "cm_pool: too many planes");
+        p.row_groups = std::max<uint32_t>(1u, 256u / p.out_w);
+        const uint64_t buf_rows = (band - 1) * p.sh + win_rows;
+        p.buf_elems = (uint32_t)(buf_rows * pitch);
+        const size_t smem = (size_t)2 * p.buf_elems * 2;
+        const uint64_t items = planes * p.n_bands;
+        const uint32_t aligned = ((p.in_w & 7u) == 0 && ((uintptr_t)x & 15u) == 0) ? 1u : 0u;
+        // resident CTAs per SM from the shared-memory footprint, at most 8 (2048 threads)
+        const uint64_t per_sm = std::max<uint64_t>(1, std::min<uint64_t>(8, (220u * 1024u) / (smem + 1024)));
+        const uint64_t grid = std::min<uint64_t>(items, (uint64_t)cx->sm_count * per_sm);
         {
             ProfScope ps_(PK_POOL, s);
-            if (p.ph == 3 && p.pw == 3)
-                pool_tile_kernel<TYPE, 3, 3><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
-            else if (p.ph == 2 && p.pw == 2)
-                pool_tile_kernel<TYPE, 2, 2><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+#define CM_POOL_LAUNCH(PH_, PW_, SH_, SW_, DH_, DW_)                                                     \
+    do {                                                                                                 \
+        auto k_ = pool_stream_kernel<TYPE, PH_, PW_, SH_, SW_, DH_, DW_>;                               \
+        cudaFuncSetAttribute(k_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);               \
+        k_<<<(unsigned)grid, 256, smem, s>>>(x, y, p, items, aligned);                                  \
+    } while (0)
+            if (p.ph == 3 && p.pw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
+                CM_POOL_LAUNCH(3, 3, 2, 2, 1, 1);
+            else if (p.ph == 3 && p.pw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 2 && p.dw == 2)
+                CM_POOL_LAUNCH(3, 3, 2, 2, 2, 2);
+            else if (p.ph == 2 && p.pw == 2 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
+                CM_POOL_LAUNCH(2, 2, 2, 2, 1, 1);
             else
-                pool_tile_kernel<TYPE, 0, 0><<<(unsigned)blocks, 256, smem, s>>>(x, y, p);
+                CM_POOL_LAUNCH(0, 0, 0, 0, 0, 0);
+#undef CM_POOL_LAUNCH
         }
     } else {
         const uint64_t total = planes * p.out_h * p.out_w;

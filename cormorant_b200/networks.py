@@ -1,0 +1,247 @@
+"""The two whole-network configurations of the benchmark, as kernel-call lists.
+
+The reference compiles an ONNX graph into a sequence of run_op / run_matmul /
+run_conv / run_pool calls over one buffer pool (inference-scheduler/src/nodes.py,
+src/codegen/_source.py).  `onnx` is not needed here: each network below is
+written directly as the call list the scheduler derives for it:
+
+* Conv  -> ConvKernel (bias as a conv input: has_bias = 1)        nodes.py:956-1119
+* Relu  -> VectorOPKernel(op=RELU, outer=1), b not read              nodes.py:414-453
+* Add   -> VectorOPKernel(op=ADD) over the whole tensor (residual)
+* MaxPool / GlobalAveragePool -> PoolingKernel (global = pool over H x W, stride 1, pad 0)
+                                                                      nodes.py:1274-1418
+* Reshape -> alias of the input buffer, no kernel                   nodes.py:1425-1493
+* Gemm(x[N,K], W[K,M], b[M]) -> MatMul(n=N, k=K, m=M, batch=1) then
+  Add(size=M, outer=N, a_inc=M, b_inc=0)  (Gemm -> MatMul + Add, graph.py:83-188)
+
+Each node is a plain tuple; `execute` walks the list on any backend that offers
+the four kernels (the GPU backend here; the tests replay the same list on the
+CPU oracle).  Weights are seeded synthetic data with the configurations' shapes
+and distributions.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+OP_ADD, OP_RELU = 0, 4
+
+
+def conv_out(n: int, k: int, s: int, p: int, d: int = 1) -> int:
+    return (n + 2 * p - d * (k - 1) - 1) // s + 1
+
+
+@dataclass
+class Net:
+    name: str
+    batch: int
+    input: str
+    output: str
+    buffers: dict = field(default_factory=dict)      # name -> number of int16 words
+    consts: dict = field(default_factory=dict)       # name -> int16 array (weights, biases)
+    nodes: list = field(default_factory=list)        # (kind, args...) -- see execute()
+    aliases: dict = field(default_factory=dict)      # Reshape: name -> name
+    macs_per_image: int = 0
+
+    def buf(self, name: str, words: int) -> str:
+        self.buffers[name] = int(words)
+        return name
+
+    def resolve(self, name: str) -> str:
+        while name in self.aliases:
+            name = self.aliases[name]
+        return name
+
+
+def q88_floor(v: np.ndarray) -> np.ndarray:
+    return np.clip(np.floor(v * 256.0), -32768, 32767).astype(np.int16)
+
+
+def q88_round(v: np.ndarray) -> np.ndarray:
+    """dtype.py quantize(): clip, round half to even at 2^-8."""
+    return np.clip(np.round(np.clip(v, -128.0, 127.99609375) * 256.0), -32768, 32767).astype(np.int16)
+
+
+class _Builder:
+    def __init__(self, net: Net, rng: np.random.Generator, weight_fn):
+        self.net, self.rng, self.weight_fn = net, rng, weight_fn
+        self.count = 0
+
+    def _name(self, kind: str) -> str:
+        self.count += 1
+        return f"{kind}{self.count}"
+
+    def conv(self, x, c, h, w, m, k, s, p, bias=True):
+        n = self.net.batch
+        oh, ow = conv_out(h, k, s, p), conv_out(w, k, s, p)
+        wn, bn = self._name("W"), self._name("B")
+        self.net.consts[wn] = self.weight_fn((m, c, k, k), c * k * k)
+        self.net.consts[bn] = self.weight_fn((m,), None) if bias else np.zeros(m, np.int16)
+        y = self.net.buf(self._name("conv"), n * m * oh * ow)
+        self.net.nodes.append(("conv", x, wn, bn if bias else None, y,
+                               (n, c, h, w, m, oh, ow, k, k, s, s, 1, 1, p, p, int(bias), 0)))
+        self.net.macs_per_image += m * oh * ow * c * k * k
+        return y, m, oh, ow
+
+    def relu(self, x, words):
+        y = self.net.buf(self._name("relu"), words)
+        self.net.nodes.append(("vectorop", x, None, y, (words, OP_RELU, 1, 0, 0)))
+        return y
+
+    def add(self, a, b, words):
+        y = self.net.buf(self._name("add"), words)
+        self.net.nodes.append(("vectorop", a, b, y, (words, OP_ADD, 1, 0, 0)))
+        return y
+
+    def pool(self, x, c, h, w, k, s, p, kind, global_=False):
+        n = self.net.batch
+        if global_:
+            oh = ow = 1
+            args = (n, c, h, w, 1, 1, h, w, 1, 1, 0, 0, 1, 1, kind, 2, 0)
+        else:
+            oh, ow = conv_out(h, k, s, p), conv_out(w, k, s, p)
+            args = (n, c, h, w, oh, ow, k, k, s, s, p, p, 1, 1, kind, 2, 0)
+        y = self.net.buf(self._name("pool"), n * c * oh * ow)
+        self.net.nodes.append(("pool", x, y, args))
+        return y, oh, ow
+
+    def reshape(self, x):
+        y = self._name("reshape")
+        self.net.aliases[y] = x
+        return y
+
+    def gemm(self, x, k, m):
+        n = self.net.batch
+        wn, bn = self._name("W"), self._name("B")
+        self.net.consts[wn] = self.weight_fn((k, m), k)
+        self.net.consts[bn] = self.weight_fn((m,), None)
+        t = self.net.buf(self._name("mm"), n * m)
+        self.net.nodes.append(("matmul", x, wn, t, (n, k, m, 1, n * k, k * m, n * m)))
+        y = self.net.buf(self._name("gemm"), n * m)
+        self.net.nodes.append(("vectorop", t, bn, y, (m, OP_ADD, n, m, 0)))
+        self.net.macs_per_image += k * m
+        return y
+
+
+def lenet5(batch: int = 1, seed: int = 42) -> Net:
+    """LeNet-5-style CNN, 1x1x28x28 input uniform [0,1) (RNE to Q8.8);
+    weights and biases uniform [-0.5, 0.5) rounded down to a multiple of 1/256."""
+    rng = np.random.default_rng(seed)
+    net = Net("lenet5", batch, "x", "")
+    net.buf("x", batch * 28 * 28)
+    wfn = lambda shape, fan_in: q88_floor(rng.uniform(-0.5, 0.5, size=shape)).reshape(-1)  # noqa: E731
+    b = _Builder(net, rng, wfn)
+    y, c, h, w = b.conv("x", 1, 28, 28, 6, 5, 1, 2)
+    y = b.relu(y, batch * c * h * w)
+    y, h, w = b.pool(y, c, h, w, 2, 2, 0, 0)
+    y, c, h, w = b.conv(y, 6, h, w, 16, 5, 1, 0)
+    y = b.relu(y, batch * c * h * w)
+    y, h, w = b.pool(y, c, h, w, 2, 2, 0, 0)
+    y = b.reshape(y)                                          # [N, 400]
+    y = b.gemm(y, 400, 120)
+    y = b.relu(y, batch * 120)
+    y = b.gemm(y, 120, 84)
+    y = b.relu(y, batch * 84)
+    net.output = b.gemm(y, 84, 10)
+    return net
+
+
+def resnet18(batch: int = 256, seed: int = 42, num_classes: int = 1000) -> Net:
+    """ResNet-18-shaped plain CNN (no normalisation layers), 3x224x224
+    input uniform [0,1) (RNE to Q8.8); He-scaled normal weights N(0, 2/fan_in) and
+    N(0, 0.01^2) biases, rounded to Q8.8."""
+    rng = np.random.default_rng(seed)
+    net = Net("resnet18", batch, "x", "")
+    net.buf("x", batch * 3 * 224 * 224)
+
+    def wfn(shape, fan_in):
+        sd = np.sqrt(2.0 / fan_in) if fan_in else 0.01
+        return q88_round(rng.normal(0.0, sd, size=shape)).reshape(-1)
+
+    b = _Builder(net, rng, wfn)
+    y, c, h, w = b.conv("x", 3, 224, 224, 64, 7, 2, 3)
+    y = b.relu(y, batch * c * h * w)
+    y, h, w = b.pool(y, c, h, w, 3, 2, 1, 0)                 # 56 x 56
+    for width, stride in ((64, 1), (128, 2), (256, 2), (512, 2)):
+        for blk in range(2):
+            s = stride if blk == 0 else 1
+            t, c2, h2, w2 = b.conv(y, c, h, w, width, 3, s, 1)
+            t = b.relu(t, batch * c2 * h2 * w2)
+            t, c2, h2, w2 = b.conv(t, c2, h2, w2, width, 3, 1, 1)
+            if s != 1 or c != width:
+                sc, _, _, _ = b.conv(y, c, h, w, width, 1, s, 0)
+            else:
+                sc = y
+            y = b.add(t, sc, batch * c2 * h2 * w2)
+            y = b.relu(y, batch * c2 * h2 * w2)
+            c, h, w = c2, h2, w2
+    y, _, _ = b.pool(y, c, h, w, h, 1, 0, 1, global_=True)   # [N, 512, 1, 1]
+    y = b.reshape(y)
+    net.output = b.gemm(y, 512, num_classes)
+    return net
+
+
+def make_input(net: Net, seed: int = 7) -> np.ndarray:
+    """Input uniform [0, 1), rounded to Q8.8 (dtype.py quantize)."""
+    rng = np.random.default_rng(seed)
+    return q88_round(rng.uniform(0.0, 1.0, size=net.buffers[net.input]))
+
+
+def execute(net: Net, backend, bufs: dict) -> None:
+    """Run every node of `net` on `backend` over `bufs` (name -> backend buffer).
+
+    backend offers vectorop(a, b, c, size, op, outer, a_inc, b_inc),
+    matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars)
+    and pool(x, y, *17 scalars)."""
+    R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
+    for node in net.nodes:
+        kind = node[0]
+        if kind == "conv":
+            _, x, wn, bn, y, args = node
+            backend.conv(R(x), R(wn), R(bn), R(y), *args)
+        elif kind == "vectorop":
+            _, a, bb, c, args = node
+            backend.vectorop(R(a), R(bb), R(c), *args)
+        elif kind == "pool":
+            _, x, y, args = node
+            backend.pool(R(x), R(y), *args)
+        elif kind == "matmul":
+            _, a, bb, c, args = node
+            backend.matmul(R(a), R(bb), R(c), *args)
+        else:
+            raise ValueError(kind)
+
+
+class GpuBackend:
+    """The four kernels of libcormorant_cuda.so on one CUDA stream (asynchronous)."""
+
+    def __init__(self, stream=None):
+        from . import kernels
+        self.k = kernels
+        self.stream = stream
+
+    def vectorop(self, a, b, c, size, op, outer, a_inc, b_inc):
+        self.k.VectorOPKernel(a, b, c, size, op, outer, a_inc, b_inc, stream=self.stream)
+
+    def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
+        self.k.MatmulKernel(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, stream=self.stream)
+
+    def conv(self, x, w, bias, y, *args):
+        self.k.ConvKernel(x, w, bias, y, *args, stream=self.stream)
+
+    def pool(self, x, y, *args):
+        self.k.PoolingKernel(x, y, *args, stream=self.stream)
+
+
+def gpu_buffers(net: Net, x=None):
+    """Device buffers for every activation and constant of `net` (torch int16 tensors)."""
+    import torch
+    bufs = {}
+    for name, words in net.buffers.items():
+        bufs[name] = torch.empty(max(words, 1), dtype=torch.int16, device="cuda")
+    for name, arr in net.consts.items():
+        bufs[name] = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+    if x is not None:
+        bufs[net.input].copy_(torch.from_numpy(np.ascontiguousarray(x, np.int16)))
+    return bufs
