@@ -28,7 +28,9 @@ enum { P_MAX = 0, P_AVG = 1, P_LP1 = 2, P_LP2 = 3 };
 // AccData_t(float f) on the raw Q16.16 word.
 __device__ __forceinline__ uint32_t acc_from_float(float f) {
     if (isnan(f)) return 0u;
-    return (uint32_t)(unsigned long long)__float2ll_rd(__fmul_rn(f, 65536.0f));  // exact scale, floor
+    const float t = __fmul_rn(f, 65536.0f);          // exact scale; |t| <= 2^31 here
+    if (t >= 2147483648.0f) return 0x80000000u;       // +2^31 wraps to -2^31 (AP_WRAP)
+    return (uint32_t)__float2int_rd(t);               // floor
 }
 
 // float(AccData_t acc) -- round to nearest even, then the exact 2^-16 scale.
@@ -49,8 +51,8 @@ __device__ __forceinline__ int16_t finalize(uint32_t acc, uint32_t denom) {
 
 struct PoolP {
     uint32_t in_h, in_w, out_h, out_w, ph, pw, sh, sw, pt, pl, dh, dw, cip;
-    uint32_t band_rows, n_bands, pitch, off0, buf_elems, row_groups;
-    FastDiv fd_ow, fd_vpr;
+    uint32_t band_rows, n_bands, pitch, off0, buf_elems, row_groups, strips;
+    FastDiv fd_ow, fd_vpr, fd_strips;
 };
 
 template <int TYPE>
@@ -104,7 +106,7 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src)
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
-template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW>
+template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PL>
 __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                           PoolP p, uint64_t items, uint32_t aligned) {
     extern __shared__ __align__(16) int16_t smem[];
@@ -241,6 +243,103 @@ __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restr
         }
     };
 
+    // Strip compute for compile-time geometry (PL >= 0): thread = V = 8/SW
+    // consecutive outputs of one row group.  Their taps lie in NC aligned 16-byte
+    // chunks per tap row, loaded whole; taps are picked from registers at
+    // compile-time positions, so each output costs ~NC*PH/V shared loads.
+    constexpr bool VEC = PL >= 0 && PH > 0 && PW > 0 && SW > 0 && DW > 0 && (8 % (SW > 0 ? SW : 1)) == 0;
+    constexpr int V = VEC ? 8 / SW : 1;
+    constexpr int E = PL <= 0 ? 0 : ((PL + 7) / 8) * 8 - PL;   // tile column of output 0's first tap, mod 8
+    constexpr int NC = VEC ? (E + (V - 1) * SW + (PW - 1) * DW + 8) / 8 : 1;
+    auto compute_vec = [&](uint64_t it, uint32_t tb) {
+        const uint64_t plane = it / p.n_bands;
+        const uint32_t band = (uint32_t)(it - plane * p.n_bands);
+        const uint32_t oh0 = band * p.band_rows, oh1 = min(p.out_h, oh0 + p.band_rows);
+        const uint32_t nr = oh1 - oh0, G = p.row_groups, nstrips = p.strips;
+        const uint32_t rpg = (nr + G - 1) / G;
+        const uint32_t rowstep = DH * pitch, advance = SH * pitch;
+        for (uint32_t t = threadIdx.x; t < G * nstrips; t += blockDim.x) {
+            const uint32_t g = p.fd_strips.div(t), j = t - g * nstrips;
+            const uint32_t r0 = g * rpg, r1 = min(nr, r0 + rpg);
+            if (r0 >= r1) continue;
+            const uint32_t ow0 = j * V;
+            uint32_t base = tb + r0 * advance + 8 * j;   // chunk holding tile column E + 8j: 16-byte aligned
+            int16_t* yo = y + plane * (uint64_t)p.out_h * p.out_w + (uint64_t)(oh0 + r0) * p.out_w + ow0;
+            const uint32_t nv = min((uint32_t)V, p.out_w - ow0);
+            uint32_t vc[V];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                vc[v] = PW;
+                if (TYPE == P_AVG && !p.cip) {
+                    vc[v] = 0;
+#pragma unroll
+                    for (int c = 0; c < PW; ++c) {
+                        const int32_t iw = (int32_t)((ow0 + v) * SW + c * DW) - PL;
+                        vc[v] += (iw >= 0 && iw < (int32_t)in_w);
+                    }
+                }
+            }
+            for (uint32_t q = r0; q < r1; ++q, base += advance, yo += p.out_w) {
+                int32_t acc[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) acc[v] = (TYPE == P_MAX) ? -32768 : 0;
+#pragma unroll
+                for (int r = 0; r < PH; ++r) {
+                    uint32_t w[NC * 4];
+#pragma unroll
+                    for (int c = 0; c < NC; ++c) {
+                        const uint4 u = *(const uint4*)&smem[base + r * rowstep + 8 * c];
+                        w[4 * c] = u.x; w[4 * c + 1] = u.y; w[4 * c + 2] = u.z; w[4 * c + 3] = u.w;
+                    }
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+#pragma unroll
+                        for (int c = 0; c < PW; ++c) {
+                            const int idx = E + v * SW + c * DW;
+                            const int32_t x1 = (int32_t)(int16_t)((w[idx >> 1] >> (16 * (idx & 1))) & 0xFFFFu);
+                            if (TYPE == P_MAX) acc[v] = max(acc[v], x1);
+                            else if (TYPE == P_AVG) acc[v] += x1;
+                            else if (TYPE == P_LP1) acc[v] += (x1 < 0 ? -x1 : x1);
+                            else acc[v] = (int32_t)((uint32_t)acc[v] + (uint32_t)(x1 * x1));
+                        }
+                }
+                uint32_t vr = PH;
+                if (TYPE == P_AVG && !p.cip) {
+                    vr = 0;
+                    const int32_t ihq = (int32_t)((oh0 + q) * SH) - (int32_t)p.pt;
+#pragma unroll
+                    for (int r = 0; r < PH; ++r) {
+                        const int32_t ih = ihq + r * DH;
+                        vr += (ih >= 0 && ih < (int32_t)p.in_h);
+                    }
+                }
+                int16_t out[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    uint32_t a;
+                    if (TYPE == P_MAX) a = (uint32_t)(acc[v] * 256);
+                    else if (TYPE == P_LP2) a = (uint32_t)acc[v];
+                    else a = (uint32_t)acc[v] * 256u;
+                    if (TYPE == P_AVG) {
+                        const uint32_t denom = p.cip ? PH * PW : vr * vc[v];
+                        const float inv = inv_tab[denom];
+                        out[v] = narrow_acc(acc_from_float(__fmul_rn(acc_to_float(a), inv)));
+                    } else {
+                        out[v] = finalize<TYPE>(a, 0);
+                    }
+                }
+                if (nv == (uint32_t)V && V == 4 && ((uintptr_t)yo & 7u) == 0) {
+                    *(uint2*)yo = make_uint2((uint32_t)(uint16_t)out[0] | ((uint32_t)(uint16_t)out[1 % V] << 16),
+                                             (uint32_t)(uint16_t)out[2 % V] | ((uint32_t)(uint16_t)out[3 % V] << 16));
+                } else {
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+                        if ((uint32_t)v < nv) yo[v] = out[v];
+                }
+            }
+        }
+    };
+
     uint32_t cur = 0, other = p.buf_elems;
     uint64_t it = blockIdx.x;
     if (it < items) issue(it, cur);
@@ -250,9 +349,182 @@ __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restr
         else cp_async_commit();            // empty group keeps the wait count uniform
         cp_async_wait1();                  // item `it` has landed
         __syncthreads();
-        compute(it, cur);
+        if (VEC) compute_vec(it, cur);
+        else compute(it, cur);
         __syncthreads();                   // the buffer may be refilled next
         const uint32_t t = cur; cur = other; other = t;
+    }
+}
+
+// Row-streaming kernel for compile-time geometries (no shared memory).
+// Thread = (plane, strip j of V = 8/SW consecutive outputs).  Each input row the
+// strip needs is read once: one coalesced 16-byte load of input columns
+// [8j, 8j+8), plus PL columns on the left and HR on the right taken from the
+// neighbouring lanes' loads by warp shuffle (a direct 2-byte load at warp
+// edges; the window identity outside the plane).  The row's horizontal window
+// reductions for the V outputs go into a register ring over the progression of
+// tap rows (spaced DH); consecutive output rows advance it by SH/DH rows, so a
+// row shared by two output rows is reduced once.
+template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PT, int PL>
+__global__ void __launch_bounds__(256) pool_rows_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
+                                                        PoolP p, uint64_t total) {
+    constexpr int V = 8 / SW;
+    constexpr int SPAN = (V - 1) * SW + (PW - 1) * DW + 1;   // input columns under the strip
+    constexpr int HR = SPAN - PL - 8 > 0 ? SPAN - PL - 8 : 0;
+    constexpr int ADV = SH / DH;                             // new tap rows per output row
+    static_assert(SH % DH == 0 && PL <= 8 && HR <= 8 && V * SW == 8, "geometry");
+    __shared__ float inv_tab[PH * PW + 1];
+    if (TYPE == P_AVG && threadIdx.x <= PH * PW) inv_tab[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, (float)threadIdx.x) : 0.0f;
+    __syncthreads();
+
+    const int32_t pad = (TYPE == P_MAX) ? -32768 : 0;
+    const uint32_t lane = threadIdx.x & 31;
+    const uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool live = t < total;
+    const uint64_t tt = live ? t : total - 1;                // inactive lanes mirror a real strip
+    const uint32_t nstrips = p.strips;
+    const uint64_t plane = tt / nstrips;
+    const uint32_t j = (uint32_t)(tt - plane * nstrips);
+    const uint32_t in_w = p.in_w, in_h = p.in_h;
+    const int16_t* xp = x + plane * (uint64_t)in_h * in_w + 8 * j;
+    const bool first = j == 0, last = j == nstrips - 1;
+
+    // Input row ih of this strip: one 16-byte load (zeros outside the plane).
+    auto lrow = [&](int32_t ih) -> uint4 {
+        uint4 c = make_uint4(0, 0, 0, 0);
+        if (ih >= 0 && ih < (int32_t)in_h) c = __ldcs((const uint4*)(xp + (uint64_t)ih * in_w));
+        return c;
+    };
+    // Horizontal reductions of input row ih (loaded as c) for this strip's V outputs.
+    auto hrow = [&](int32_t ih, uint4 c, int32_t (&h)[V]) {
+        const bool ok = ih >= 0 && ih < (int32_t)in_h;
+        const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+        int32_t e[SPAN];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (PL + k < SPAN) e[PL + k] = ok ? (int32_t)(int16_t)(w[k >> 1] >> (16 * (k & 1))) : pad;
+        if (PL > 0) {
+            const uint32_t nb = __shfl_up_sync(0xFFFFFFFFu, c.w, 1);           // left neighbour's columns 6, 7
+            const uint32_t nb2 = __shfl_up_sync(0xFFFFFFFFu, c.z, 1);          // columns 4, 5
+#pragma unroll
+            for (int k = 0; k < PL; ++k) {
+                const int col = 8 - PL + k;                                    // column in the left chunk
+                int32_t v = pad;
+                if (ok && !first) {
+                    if (lane > 0) v = (int32_t)(int16_t)((col >= 6 ? nb : nb2) >> (16 * (col & 1)));
+                    else v = xp[(int64_t)ih * in_w - 8 + col];
+                }
+                e[k] = v;
+            }
+        }
+        if (HR > 0) {
+            const uint32_t nb = __shfl_down_sync(0xFFFFFFFFu, c.x, 1);         // right neighbour's columns 0, 1
+            const uint32_t nb2 = __shfl_down_sync(0xFFFFFFFFu, c.y, 1);        // columns 2, 3
+#pragma unroll
+            for (int k = 0; k < HR; ++k) {
+                int32_t v = pad;
+                if (ok && !last) {
+                    if (lane < 31) v = (int32_t)(int16_t)((k >= 2 ? nb2 : nb) >> (16 * (k & 1)));
+                    else v = xp[(int64_t)ih * in_w + 8 + k];
+                }
+                e[PL + 8 + k] = v;
+            }
+        }
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            int32_t a = (TYPE == P_MAX) ? -32768 : 0;
+#pragma unroll
+            for (int c2 = 0; c2 < PW; ++c2) {
+                const int32_t x1 = e[v * SW + c2 * DW];
+                if (TYPE == P_MAX) a = max(a, x1);
+                else if (TYPE == P_AVG) a += x1;
+                else if (TYPE == P_LP1) a += (x1 < 0 ? -x1 : x1);
+                else a = (int32_t)((uint32_t)a + (uint32_t)(x1 * x1));
+            }
+            h[v] = a;
+        }
+    };
+
+    uint32_t vc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        vc[v] = PW;
+        if (TYPE == P_AVG && !p.cip) {
+            vc[v] = 0;
+#pragma unroll
+            for (int c2 = 0; c2 < PW; ++c2) {
+                const int32_t iw = (int32_t)((8 * j / SW + v) * SW + c2 * DW) - PL;
+                vc[v] += (iw >= 0 && iw < (int32_t)in_w);
+            }
+        }
+    }
+    const uint32_t ow0 = j * V;
+    const uint32_t nv = ow0 < p.out_w ? min((uint32_t)V, p.out_w - ow0) : 0u;
+    int16_t* yo = y + plane * (uint64_t)p.out_h * p.out_w + ow0;
+
+    // Rows entering the ring at output row oh: tap rows r = PH-ADV .. PH-1.
+    constexpr int NEW = ADV < PH ? ADV : PH;
+    auto new_row = [&](uint32_t oh, int i) -> int32_t { return (int32_t)(oh * SH) - PT + (PH - NEW + i) * DH; };
+    int32_t ring[PH][V];
+#pragma unroll
+    for (int r = 0; r < PH; ++r) hrow(-PT + r * DH, lrow(-PT + r * DH), ring[r]);
+    uint4 ahead[NEW];                                        // loads for the next output row, in flight
+#pragma unroll
+    for (int i = 0; i < NEW; ++i) ahead[i] = lrow(new_row(1, i));
+    for (uint32_t oh = 0; oh < p.out_h; ++oh) {
+        if (oh > 0) {
+            uint4 cur[NEW];
+#pragma unroll
+            for (int i = 0; i < NEW; ++i) cur[i] = ahead[i];
+#pragma unroll
+            for (int i = 0; i < NEW; ++i) ahead[i] = lrow(oh + 1 < p.out_h ? new_row(oh + 1, i) : -1);
+#pragma unroll
+            for (int r = 0; r + ADV < PH; ++r)
+#pragma unroll
+                for (int v = 0; v < V; ++v) ring[r][v] = ring[r + ADV][v];
+#pragma unroll
+            for (int i = 0; i < NEW; ++i) hrow(new_row(oh, i), cur[i], ring[PH - NEW + i]);
+        }
+        uint32_t vr = PH;
+        if (TYPE == P_AVG && !p.cip) {
+            vr = 0;
+#pragma unroll
+            for (int r = 0; r < PH; ++r) {
+                const int32_t ih = (int32_t)(oh * SH) - PT + r * DH;
+                vr += (ih >= 0 && ih < (int32_t)in_h);
+            }
+        }
+        int16_t out[V];
+#pragma unroll
+        for (int v = 0; v < V; ++v) {
+            int32_t a = ring[0][v];
+#pragma unroll
+            for (int r = 1; r < PH; ++r) {
+                if (TYPE == P_MAX) a = max(a, ring[r][v]);
+                else a = (int32_t)((uint32_t)a + (uint32_t)ring[r][v]);
+            }
+            uint32_t acc;
+            if (TYPE == P_MAX) acc = (uint32_t)(a * 256);
+            else if (TYPE == P_LP2) acc = (uint32_t)a;
+            else acc = (uint32_t)a * 256u;
+            if (TYPE == P_AVG) {
+                const uint32_t denom = p.cip ? PH * PW : vr * vc[v];
+                out[v] = narrow_acc(acc_from_float(__fmul_rn(acc_to_float(acc), inv_tab[denom])));
+            } else {
+                out[v] = finalize<TYPE>(acc, 0);
+            }
+        }
+        if (live) {
+            int16_t* dst = yo + (uint64_t)oh * p.out_w;
+            if (nv == (uint32_t)V && V == 4 && ((uintptr_t)dst & 7u) == 0) {
+                *(uint2*)dst = make_uint2((uint32_t)(uint16_t)out[0] | ((uint32_t)(uint16_t)out[1 % V] << 16),
+                                          (uint32_t)(uint16_t)out[2 % V] | ((uint32_t)(uint16_t)out[3 % V] << 16));
+            } else {
+#pragma unroll
+                for (int v = 0; v < V; ++v)
+                    if ((uint32_t)v < nv) dst[v] = out[v];
+            }
+        }
     }
 }
 
@@ -349,9 +621,44 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
     const uint64_t win_rows = (uint64_t)(p.ph ? p.ph - 1 : 0) * p.dh + 1;
     const uint64_t off0 = ((uint64_t)p.pl + 7) & ~7ull;
     const uint64_t span = off0 - p.pl + (uint64_t)(p.out_w - 1) * p.sw + (uint64_t)(p.pw ? p.pw - 1 : 0) * p.dw + 1;
-    const uint64_t pitch = (std::max<uint64_t>(off0 + p.in_w, span) + 7) & ~7ull;
+    uint64_t pitch = (std::max<uint64_t>(off0 + p.in_w, span) + 7) & ~7ull;
+    // Compile-time geometries with a strip kernel: (ph, pw, sh, sw, dh, dw, pad_left).
+    int spec = -1;
+    const uint32_t specs[3][7] = {{3, 3, 2, 2, 1, 1, 1}, {3, 3, 2, 2, 2, 2, 1}, {2, 2, 2, 2, 1, 1, 0}};
+    for (int i = 0; i < 3; ++i)
+        if (p.ph == specs[i][0] && p.pw == specs[i][1] && p.sh == specs[i][2] && p.sw == specs[i][3] &&
+            p.dh == specs[i][4] && p.dw == specs[i][5] && p.pl == specs[i][6])
+            spec = i;
+    if (spec >= 0) {
+        // strips of V = 8/sw outputs read NC aligned 16-byte chunks per tap row
+        const uint64_t V = 8 / p.sw, E = off0 - p.pl;
+        const uint64_t NC = (E + (V - 1) * p.sw + (p.pw - 1) * p.dw + 8) / 8;
+        const uint64_t nstrips = (p.out_w + V - 1) / V;
+        const uint64_t need = 8 * (nstrips - 1) + 8 * NC;   // strip j reads tile columns [8j, 8j + 8 NC)
+        pitch = std::max<uint64_t>(pitch, (need + 7) & ~7ull);
+        p.strips = (uint32_t)nstrips;
+        p.fd_strips = FastDiv(p.strips);
+    }
     const bool small = p.in_h < (1u << 24) && p.in_w < (1u << 24) && p.out_h < (1u << 24) && p.pt < (1u << 24) &&
-                       (uint64_t)p.sh * p.out_h < (1ull << 30) && win_rows < (1ull << 24);
+                       (uint64_t)p.sh * p.out_h < (1ull << 30) && win_rows < (1ull << 24) && pitch < (1u << 20);
+    // Row-streaming kernel: compile-time geometry, 16-byte-aligned rows, and exactly
+    // one 8-column input chunk per strip of V outputs.
+    if (spec >= 0 && (p.in_w & 7u) == 0 && ((uintptr_t)x & 15u) == 0 && p.in_w == 8 * p.strips &&
+        p.pt == p.pl && p.in_h < (1u << 24) && p.out_h < (1u << 24) && planes * p.strips < (1ull << 40)) {
+        const uint64_t total = planes * p.strips;
+        const uint64_t blocks = (total + 255) / 256;
+        {
+            ProfScope ps_(PK_POOL, s);
+            if (spec == 0)
+                pool_rows_kernel<TYPE, 3, 3, 2, 2, 1, 1, 1, 1><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+            else if (spec == 1)
+                pool_rows_kernel<TYPE, 3, 3, 2, 2, 2, 2, 1, 1><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+            else
+                pool_rows_kernel<TYPE, 2, 2, 2, 2, 1, 1, 0, 0><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+        }
+        count_launch();
+        return CM_OK;
+    }
     if (p.ph > 0 && p.pw > 0 && small && win_rows * pitch * 2 <= kSmemBudget) {
         // Two tile buffers per CTA (double buffering); each at most kSmemBudget / 2 ... kSmemBudget.
         uint64_t band = p.out_h;
@@ -364,7 +671,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         p.off0 = (uint32_t)off0;
         p.fd_ow = FastDiv(p.out_w);
         p.fd_vpr = FastDiv(std::max<uint32_t>(p.in_w / 8, 1u));
-        p.row_groups = std::max<uint32_t>(1u, 256u / p.out_w);
+        p.row_groups = spec >= 0 ? std::max<uint32_t>(1u, 256u / p.strips) : std::max<uint32_t>(1u, 256u / p.out_w);
         const uint64_t buf_rows = (band - 1) * p.sh + win_rows;
         p.buf_elems = (uint32_t)(buf_rows * pitch);
         const size_t smem = (size_t)2 * p.buf_elems * 2;
@@ -375,20 +682,20 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         const uint64_t grid = std::min<uint64_t>(items, (uint64_t)cx->sm_count * per_sm);
         {
             ProfScope ps_(PK_POOL, s);
-#define CM_POOL_LAUNCH(PH_, PW_, SH_, SW_, DH_, DW_)                                                     \
+#define CM_POOL_LAUNCH(PH_, PW_, SH_, SW_, DH_, DW_, PL_)                                                \
     do {                                                                                                 \
-        auto k_ = pool_stream_kernel<TYPE, PH_, PW_, SH_, SW_, DH_, DW_>;                               \
+        auto k_ = pool_stream_kernel<TYPE, PH_, PW_, SH_, SW_, DH_, DW_, PL_>;                          \
         cudaFuncSetAttribute(k_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);               \
         k_<<<(unsigned)grid, 256, smem, s>>>(x, y, p, items, aligned);                                  \
     } while (0)
-            if (p.ph == 3 && p.pw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
-                CM_POOL_LAUNCH(3, 3, 2, 2, 1, 1);
-            else if (p.ph == 3 && p.pw == 3 && p.sh == 2 && p.sw == 2 && p.dh == 2 && p.dw == 2)
-                CM_POOL_LAUNCH(3, 3, 2, 2, 2, 2);
-            else if (p.ph == 2 && p.pw == 2 && p.sh == 2 && p.sw == 2 && p.dh == 1 && p.dw == 1)
-                CM_POOL_LAUNCH(2, 2, 2, 2, 1, 1);
+            if (spec == 0)
+                CM_POOL_LAUNCH(3, 3, 2, 2, 1, 1, 1);
+            else if (spec == 1)
+                CM_POOL_LAUNCH(3, 3, 2, 2, 2, 2, 1);
+            else if (spec == 2)
+                CM_POOL_LAUNCH(2, 2, 2, 2, 1, 1, 0);
             else
-                CM_POOL_LAUNCH(0, 0, 0, 0, 0, 0);
+                CM_POOL_LAUNCH(0, 0, 0, 0, 0, 0, -1);
 #undef CM_POOL_LAUNCH
         }
     } else {

@@ -99,3 +99,25 @@ def test_sweep_full_size(cm, port, sweep_input, case):
     _, ph, pw, sh, sw, pt, pl, dh, dw, t, lp, cip = case
     N, C, H, W = 256, 64, 112, 112
     run_case(cm, port, sweep_input, N, C, H, W, ph, pw, sh, sw, pt, pl, dh, dw, 0, t, lp, cip)
+
+
+# Layouts the row-streaming kernel takes (input width a multiple of 8, one 8-column chunk per
+# strip of outputs): several planes per warp, planes straddling warps, both dilations, 2x2.
+ROWS = [
+    (3, 5, 16, 16, 3, 3, 2, 2, 1, 1, 1, 1, 0),
+    (2, 7, 40, 64, 3, 3, 2, 2, 1, 1, 1, 1, 0),
+    (1, 9, 24, 112, 3, 3, 2, 2, 1, 1, 1, 1, 0),
+    (2, 5, 30, 64, 3, 3, 2, 2, 1, 1, 2, 2, 0),
+    (1, 11, 20, 112, 3, 3, 2, 2, 1, 1, 2, 2, 0),
+    (2, 6, 18, 64, 2, 2, 2, 2, 0, 0, 1, 1, 0),
+    (1, 13, 9, 40, 2, 2, 2, 2, 0, 0, 1, 1, 0),
+]
+
+
+@pytest.mark.parametrize("geom", ROWS)
+@pytest.mark.parametrize("typ", TYPES)
+def test_row_stream_layouts(cm, port, geom, typ):
+    N, C, H, W = geom[:4]
+    rng = np.random.default_rng(zlib.crc32(repr(("rows", geom, typ)).encode()))
+    x = rand16(rng, N * C * H * W)
+    run_case(cm, port, x, *geom, *typ)
