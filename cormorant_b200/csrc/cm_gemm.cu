@@ -116,6 +116,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                            int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -170,10 +178,13 @@ struct GemmArgs {
     const int32_t* rowterm;
     const int32_t* colterm;
     int16_t* out;
-    uint64_t ldo, out_bs;
+    uint64_t ldo, ldc, out_bs;
     uint32_t z_base;
     int* status;
     uint64_t timeout_ns;
+    // implicit conv (conv != 0): tile rows = bn images x bh rows x bw columns
+    uint32_t conv, tiles_w, tiles_h, bw_log, bh_log, bn_log;
+    uint32_t nimg, out_h, out_w, sw, sh, dh, kb_per_r;
 };
 
 __global__ void __launch_bounds__(192, 1)
@@ -193,8 +204,19 @@ __global__ void __launch_bounds__(192, 1)
     const uint32_t first_m = group * GROUP_M;
     const uint32_t gsize = min(GROUP_M, g.tiles_m - first_m);
     const uint32_t local = blockIdx.x - group * per_group;
-    const uint32_t m0 = (first_m + local % gsize) * BM;   // output row tile (A rows)
+    const uint32_t tm = first_m + local % gsize;
+    const uint32_t m0 = tm * BM;                          // output row tile (A rows)
     const uint32_t n0 = (local / gsize) * BN;             // output column tile (B columns)
+    // conv: the row tile is (image block, output-row block, output-column block)
+    uint32_t cw0 = 0, ch0 = 0, cn0 = 0;
+    if (g.conv) {
+        const uint32_t t_hw = g.tiles_w * g.tiles_h;
+        const uint32_t tn = tm / t_hw, rem = tm - tn * t_hw;
+        const uint32_t th = rem / g.tiles_w;
+        cn0 = tn << g.bn_log;
+        ch0 = th << g.bh_log;
+        cw0 = (rem - th * g.tiles_w) << g.bw_log;
+    }
     const uint32_t z = blockIdx.z + g.z_base;
     const uint32_t ba = g.a_batches == 1 ? 0u : z;
     const uint32_t bb = g.b_batches == 1 ? 0u : z;
@@ -230,7 +252,14 @@ __global__ void __launch_bounds__(192, 1)
                 const uint32_t full = smem_u32(&bars[s]);
                 mbar_expect_tx(full, STAGE_BYTES);
                 uint8_t* st = smem + s * STAGE_BYTES;
-                tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)m0, 0, (int)ba);
+                if (g.conv) {
+                    const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
+                    const int c1 = (int)(cw0 * g.sw), c2 = (int)(ch0 * g.sh + r * g.dh);
+                    tma_load_5d(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)cn0, 0);
+                    tma_load_5d(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)cn0, 1);
+                } else {
+                    tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)m0, 0, (int)ba);
+                }
                 tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)n0, (int)(kb * BK), 0, (int)bb);
                 ++issued;
             }
@@ -268,7 +297,23 @@ __global__ void __launch_bounds__(192, 1)
     } else {
         // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32).
         const uint32_t quarter = warp & 3u;
-        const uint32_t row = m0 + quarter * 32 + lane;
+        const uint32_t i = quarter * 32 + lane;           // TMEM lane = A tile row
+        bool valid;
+        uint64_t rt_idx, o_off;
+        if (g.conv) {
+            const uint32_t ow = cw0 + (i & ((1u << g.bw_log) - 1u));
+            const uint32_t oh = ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
+            const uint32_t n = cn0 + (i >> (g.bw_log + g.bh_log));
+            valid = ow < g.out_w && oh < g.out_h && n < g.nimg;
+            const uint64_t pix = (uint64_t)oh * g.out_w + ow;
+            rt_idx = (uint64_t)n * g.out_h * g.out_w + pix;
+            o_off = (uint64_t)n * g.out_bs + pix;
+        } else {
+            const uint32_t row = m0 + i;
+            valid = row < g.rows;
+            rt_idx = (uint64_t)ba * g.rows + row;
+            o_off = (uint64_t)z * g.out_bs + (uint64_t)row * g.ldo;
+        }
         // One lane waits; the verdict is broadcast so that the .sync.aligned
         // TMEM loads below are executed by the whole warp or not at all.
         uint32_t ok = 0;
@@ -277,9 +322,9 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         tc_fence_after();
         if (ok) {
-            const uint32_t rt = row < g.rows ? (uint32_t)g.rowterm[(uint64_t)ba * g.rows + row] : 0u;
+            const uint32_t rt = valid ? (uint32_t)g.rowterm[rt_idx] : 0u;
             const int32_t* ct = g.colterm + (uint64_t)bb * g.cols;
-            int16_t* orow = g.out + (uint64_t)z * g.out_bs + (uint64_t)row * g.ldo;
+            int16_t* orow = g.out + o_off;
             const uint32_t tl = tmem + ((quarter * 32u) << 16);
 #pragma unroll 1
             for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
@@ -297,7 +342,7 @@ __global__ void __launch_bounds__(192, 1)
                 for (int j = 0; j < 32; ++j) p[j] = (p[j] + q[j]) << 8;
                 tmem_ld32(tl + COL_LL + c0, q);
                 tmem_ld_wait();
-                if (row < g.rows) {
+                if (valid) {
                     const uint32_t col0 = n0 + c0;
                     int16_t v[32];
 #pragma unroll
@@ -308,7 +353,13 @@ __global__ void __launch_bounds__(192, 1)
                         v[j] = narrow_acc(acc);
                     }
                     int16_t* dst = orow + col0;
-                    if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
+                    if (g.ldc != 1) {
+                        // column-strided output (conv: y[m][p] with rows = pixels): each
+                        // store is coalesced across the warp's consecutive rows
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (col0 + j < g.cols) orow[(uint64_t)(col0 + j) * g.ldc] = v[j];
+                    } else if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
                         uint4* d4 = (uint4*)dst;
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
@@ -552,9 +603,34 @@ int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t 
     return CM_OK;
 }
 
+// Conv A planes [2][nimg][Hp][Wp][Cp] viewed as {KR k, Wp pixels, Hp rows, nimg, 2}:
+// dim 0 (the taps (s, c) of one kernel row) overlaps dim 1 by design, the
+// pixel stride being Cp bytes.  Box {128, bw*sw, bh*sh, bn, 1} with traversal
+// strides {1, sw, sh, 1, 1} = 128 pixels x 128 bytes of K.  Every in-range
+// (pixel, k) address stays inside the buffer plus (kw-1)*Cp bytes of slack.
+int make_conv_map(CUtensorMap* m, const ConvA& c) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)c.planes & 15u) != 0 || (c.Cp & 15u) != 0) return set_error(CM_EINVAL, "conv plane buffer misaligned");
+    const uint32_t bw = 1u << c.bw_log, bh = 1u << c.bh_log, bn = 1u << c.bn_log;
+    if (bw * bh * bn != (uint32_t)BM || bw * c.sw > 256 || bh * c.sh > 256 || c.sw > 8 || c.sh > 8)
+        return set_error(CM_EINVAL, "conv tile shape");
+    const uint64_t row = (uint64_t)c.Wp * c.Cp, img = row * c.Hp;
+    const cuuint64_t dims[5] = {c.KR, c.Wp, c.Hp, c.nimg, 2};
+    const cuuint64_t strides[4] = {(cuuint64_t)c.Cp, (cuuint64_t)row, (cuuint64_t)img, (cuuint64_t)img * c.nimg};
+    const cuuint32_t box[5] = {(cuuint32_t)BK, bw * c.sw, bh * c.sh, bn, 1};
+    const cuuint32_t estr[5] = {1, c.sw, c.sh, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void*)c.planes, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled (conv) failed (%d)", (int)r);
+    return CM_OK;
+}
+
 }  // namespace
 
 int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
+    if (p.conv) return gemm_launch_conv(cx, p, s);
     if (p.K == 0) return fill_zero(cx, p.out, p.batch, p.rows, p.cols, p.ldo, p.out_bs, s);
     if (p.K > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "reduction length %u exceeds %u", p.K, kMaxGemmK);
     CUtensorMap ta, tb;
@@ -575,8 +651,9 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
     g.a_batches = p.a_batches; g.b_batches = p.b_batches;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
-    g.out = p.out; g.ldo = p.ldo; g.out_bs = p.out_bs;
+    g.out = p.out; g.ldo = p.ldo; g.ldc = p.ldc ? p.ldc : 1; g.out_bs = p.out_bs;
     g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    g.conv = 0;
     const dim3 block(192);
     for (uint32_t z0 = 0; z0 < p.batch; z0 += 65535u) {
         const uint32_t nz = min(65535u, p.batch - z0);
@@ -590,6 +667,46 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     }
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
+}
+
+int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
+    const ConvA& c = *p.conv;
+    if (p.K == 0 || p.K % BK != 0 || c.KR_pad % BK != 0 || p.K != c.kh * c.KR_pad)
+        return set_error(CM_EINVAL, "conv GEMM reduction layout");
+    CUtensorMap ta, tb;
+    int rc = make_conv_map(&ta, c);
+    if (rc) return rc;
+    rc = make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, 1);
+    if (rc) return rc;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+        attr_set = true;
+    }
+    GemmArgs g{};
+    g.conv = 1;
+    g.bw_log = c.bw_log; g.bh_log = c.bh_log; g.bn_log = c.bn_log;
+    g.tiles_w = (c.out_w + (1u << c.bw_log) - 1) >> c.bw_log;
+    g.tiles_h = (c.out_h + (1u << c.bh_log) - 1) >> c.bh_log;
+    const uint64_t tiles_img = (c.nimg + (1u << c.bn_log) - 1) >> c.bn_log;
+    const uint64_t tiles_m = tiles_img * g.tiles_w * g.tiles_h;
+    g.cols = p.cols; g.num_kb = p.K / BK; g.kb_per_r = c.KR_pad / BK;
+    g.tiles_n = (p.cols + BN - 1) / BN;
+    if (tiles_m * g.tiles_n >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    g.tiles_m = (uint32_t)tiles_m;
+    g.rows = 0; g.a_batches = 1; g.b_batches = 1;
+    g.nimg = c.nimg; g.out_h = c.out_h; g.out_w = c.out_w; g.sw = c.sw; g.sh = c.sh; g.dh = c.dh;
+    g.rowterm = p.rowterm; g.colterm = p.colterm;
+    g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs; g.z_base = 0;
+    g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    {
+        ProfScope ps_(PK_GEMM, s);
+        gemm_q88_kernel<<<dim3(g.tiles_m * g.tiles_n), dim3(192), SMEM_BYTES, s>>>(ta, tb, g);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "conv gemm launch");
 }
 
 int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
@@ -726,7 +843,7 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     rc = split_rows(cx, a, a_batch_stride, k, n, k, a_batches, ap, rt, nullptr, s);
     if (!rc) rc = split_kn(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s);
     if (!rc) {
-        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, c_batch_stride, batch};
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, 1, c_batch_stride, batch};
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);
@@ -803,7 +920,7 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
     int rc = split_rows(cx, a, a_bs, k, n, k, a_batches, ap, rt, nullptr, s);
     if (!rc) rc = split_kn(cx, b, b_bs, m, m, k, b_batches, bp, ct, s);
     if (!rc) {
-        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, c_bs, nb};
+        GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, 1, c_bs, nb};
         rc = gemm_launch(cx, p, s);
     }
     return rc;

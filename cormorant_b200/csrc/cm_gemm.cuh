@@ -6,7 +6,7 @@
 //   plane 0 = hi = x >> 8 (signed), plane 1 = lo' = (x & 255) - 128 (signed)
 //   K_pad = K rounded up to 16, C_pad = cols rounded up to 16 (16-byte TMA strides)
 //   rowterm   [a_batches][rows] int32, colterm [b_batches][cols] int32
-//   out[z*out_bs + row*ldo + col] = sat16(floor(acc / 256)), with
+//   out[z*out_bs + row*ldo + col*ldc] = sat16(floor(acc / 256)), with
 //   acc = 2^16*HH + 2^8*(HL + LH) + LL + rowterm[row] + colterm[col]  (mod 2^32)
 // which equals the exact sum of int16 products (see cm_gemm.cu).
 #pragma once
@@ -15,14 +15,34 @@
 
 namespace cm {
 
+// Implicit-GEMM A operand of a convolution (rows = output pixels, K = taps):
+// planes [2][nimg][Hp][Wp][Cp] int8, the input in channels-last order with the
+// spatial zero padding written out (x = 0 is h = 0, l' = -128), Cp = C rounded up
+// to 16.  For fixed kernel row r the taps (s, c) of one output pixel are the
+// kw*Cp consecutive bytes starting at its first input pixel, so K is ordered
+// (r, s, c) with each r's kw*Cp bytes padded to KR_pad (a multiple of 128) and
+// the A tile of K block (r, kb) is one TMA box {128 k, bw pixels (stride sw),
+// bh rows (stride sh), bn images} at (kb*128, ow0*sw, oh0*sh + r*dh, n0).
+// Tile rows are (image, row, column) in that order with bw*bh*bn = 128,
+// all three powers of two.
+struct ConvA {
+    const int8_t* planes;
+    uint32_t nimg, Cp, Hp, Wp, KR, KR_pad, kh, sh, sw, dh;
+    uint32_t out_h, out_w, bw_log, bh_log, bn_log;
+};
+
 struct GemmPlan {
     const int8_t* a_planes; uint32_t rows; uint32_t a_batches;
     const int8_t* b_planes; uint32_t cols; uint32_t b_batches;
     uint32_t K, K_pad, C_pad;
     const int32_t* rowterm;
     const int32_t* colterm;
-    int16_t* out; uint64_t ldo, out_bs;
+    int16_t* out; uint64_t ldo, ldc, out_bs;     // out[z*out_bs + row*ldo + col*ldc]
     uint32_t batch;
+    // Conv implicit GEMM (a_planes, rows, a_batches, K_pad and batch unused):
+    // output pixel (n, oh, ow), channel col -> out[n*out_bs + (oh*out_w + ow) + col*ldc],
+    // rowterm[n*out_h*out_w + oh*out_w + ow]; K = kh*KR_pad.
+    const ConvA* conv = nullptr;
 };
 
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude
@@ -32,6 +52,7 @@ inline uint32_t pad_c(uint32_t C) { return (C + 15u) & ~15u; }
 
 // Launch the tcgen05 GEMM (all arguments device-resident, stream-ordered).
 int gemm_launch(const Context* cx, const GemmPlan& g, cudaStream_t s);
+int gemm_launch_conv(const Context* cx, const GemmPlan& g, cudaStream_t s);
 
 // Split int16 rows into hi/lo planes + row terms:
 //   element (bt, r, k) = src[bt*src_bs + r*ld + k], r < rows, k < K, bt < nbt;

@@ -51,6 +51,14 @@ REF_CASES = [
     # odd shapes: K not a multiple of 16, stride > kernel, dilation with padding
     (3, 5, 13, 11, 7, 2, 3, 3, 2, 2, 3, 1, 2, 0, 1, 1, 0),
     (1, 130, 9, 9, 129, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+    # implicit-GEMM geometry (channels-last planes, TMA box per kernel row): 1x1 stride-2
+    # shortcut, kw*C exactly 128 with row dilation, partial channel tile with images
+    # past the batch in the last tile, output rows wider than one tile, strides 3 and 8
+    (3, 128, 14, 14, 256, 1, 1, 2, 2, 1, 1, 0, 0, 0, 0, 1, 0),
+    (2, 32, 9, 13, 40, 3, 4, 1, 2, 2, 1, 2, 1, 1, 0, 1, 0),
+    (5, 64, 7, 7, 100, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),
+    (1, 96, 20, 150, 24, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 64, 40, 40, 16, 3, 3, 3, 8, 1, 1, 1, 1, 0, 0, 1, 0),
 ]
 
 
