@@ -13,11 +13,12 @@
 // terms carry bias << 8 (ConvKernel.cpp:160-169).  The epilogue writes
 // y[n][m][p] (NCHW) with column stride P.
 //
-// Explicit im2col (everything else): rows = output channels (weights
-// [M][C*kh*kw], already K-major), columns = output pixels of one image, K in
-// the weight layout's (c, r, s) order; the im2col pre-pass gathers each
-// column's taps into N-major planes.  Images are processed in chunks so that
-// either form's scratch stays bounded.
+// Explicit im2col (everything else, e.g. the 3-channel stem): rows = output
+// pixels of a chunk of images, columns = output channels, K in the weight
+// layout's (c, r, s) order; the im2col pre-pass gathers each row's taps into
+// K-major planes.  Images are processed in chunks so that either form's
+// scratch stays bounded.  Outputs of at most 64 channels use the GEMM's
+// 64-column tiles (packed weight planes).
 //
 // Depthwise conv (is_depthwise = 1, ConvKernel.cpp:251-319) is a per-channel
 // kh x kw stencil: CUDA cores, one thread per output pixel, int32 wrap sum.
@@ -78,51 +79,58 @@ struct NhwcGeom {
 
 // x [nimg][C][H][W] -> planes [2][nimg][Hp][Wp][Cp] (hi, lo'), the spatial padding
 // and the channels c >= C written as x = 0; S[n][hp][wp] = sum_{c<C} (x - 128).
-// Block = one padded input row segment of `wchunk` pixels: the segment is read
-// channel by channel (coalesced along w) into shared memory, then written
-// pixel by pixel (coalesced along c).
-__global__ void __launch_bounds__(256) conv_nhwc_split_kernel(const int16_t* __restrict__ x, NhwcGeom g, uint32_t wchunk,
+// Block = 256 consecutive padded pixels of one image, all channels in tiles of
+// 32: each tile is read channel by channel (thread = pixel, so a warp reads 32
+// neighbouring pixels of one channel and the block 512 bytes of each channel
+// row), transposed through shared memory, and written as two 16-byte runs of
+// 16 channels per plane; the thread keeps its pixel's channel sum.
+constexpr uint32_t kNhwcPix = 256, kNhwcCh = 32;
+
+__global__ void __launch_bounds__(256) conv_nhwc_split_kernel(const int16_t* __restrict__ x, NhwcGeom g,
                                                               int8_t* __restrict__ planes, int32_t* __restrict__ S) {
-    extern __shared__ int16_t tile[];                       // [wchunk][Cp + 2]
-    const uint32_t pitch = g.Cp + 2;
-    int32_t* ssum = (int32_t*)(tile + (uint64_t)wchunk * pitch);
-    const uint32_t n = blockIdx.z, hp = blockIdx.y, w0 = blockIdx.x * wchunk;
-    const uint32_t nw = min(wchunk, g.Wp - w0);
-    const int32_t ih = (int32_t)hp - (int32_t)g.pt;
-    const bool row_in = ih >= 0 && ih < (int32_t)g.H;
-    for (uint32_t t = threadIdx.x; t < nw; t += blockDim.x) ssum[t] = 0;
-    const int16_t* xr = x + (uint64_t)n * g.C * g.H * g.W + (row_in ? (uint64_t)ih * g.W : 0);
-    for (uint32_t t = threadIdx.x; t < g.Cp * nw; t += blockDim.x) {
-        const uint32_t c = t / nw, w = t - c * nw;
-        const int32_t iw = (int32_t)(w0 + w) - (int32_t)g.pl;
-        int16_t v = 0;
-        if (c < g.C && row_in && iw >= 0 && iw < (int32_t)g.W) v = __ldg(xr + (uint64_t)c * g.H * g.W + (uint32_t)iw);
-        tile[w * pitch + c] = v;
+    __shared__ int16_t tile[kNhwcCh][kNhwcPix + 2];
+    const uint32_t n = blockIdx.y;
+    const uint32_t HWp = g.Hp * g.Wp;
+    const uint32_t q = threadIdx.x;
+    const uint32_t qp = blockIdx.x * kNhwcPix + q;
+    const uint64_t HW = (uint64_t)g.H * g.W;
+    int64_t src = -1;
+    if (qp < HWp) {
+        const uint32_t hp = qp / g.Wp, wp = qp - hp * g.Wp;
+        const int32_t ih = (int32_t)hp - (int32_t)g.pt, iw = (int32_t)wp - (int32_t)g.pl;
+        if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
+            src = (int64_t)(((uint64_t)n * g.C * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
     }
-    __syncthreads();
-    const uint32_t cq = g.Cp / 4;
-    const uint64_t base = (((uint64_t)n * g.Hp + hp) * g.Wp + w0) * g.Cp;
-    const uint64_t plane = (uint64_t)g.nimg * g.Hp * g.Wp * g.Cp;
-    for (uint32_t t = threadIdx.x; t < cq * nw; t += blockDim.x) {
-        const uint32_t w = t / cq, c4 = (t - w * cq) * 4;
-        const int16_t* tp = tile + w * pitch + c4;
-        uint32_t hi = 0, lo = 0;
-        int32_t sum = 0;
+    const uint64_t plane = (uint64_t)g.nimg * HWp * g.Cp;
+    int8_t* dst = planes + ((uint64_t)n * HWp + qp) * g.Cp;
+    int32_t sum = 0;
+    for (uint32_t c0 = 0; c0 < g.Cp; c0 += kNhwcCh) {
+        __syncthreads();
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int16_t v = tp[j];
-            hi |= (uint32_t)(uint8_t)(v >> 8) << (8 * j);
-            lo |= (uint32_t)(((uint32_t)v & 255u) ^ 0x80u) << (8 * j);
-            if (c4 + j < g.C) sum += (int32_t)v - 128;
+        for (uint32_t c = 0; c < kNhwcCh; ++c) {
+            int16_t v = 0;
+            if (src >= 0 && c0 + c < g.C) v = __ldg(x + (uint64_t)src + (uint64_t)(c0 + c) * HW);
+            tile[c][q] = v;
         }
-        const uint64_t o = base + (uint64_t)w * g.Cp + c4;
-        *(uint32_t*)(planes + o) = hi;
-        *(uint32_t*)(planes + plane + o) = lo;
-        atomicAdd(&ssum[w], sum);
+        __syncthreads();
+        if (qp < HWp) {
+#pragma unroll
+            for (uint32_t h = 0; h < kNhwcCh; h += 16) {
+                if (c0 + h >= g.Cp) break;
+                uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+#pragma unroll
+                for (uint32_t j = 0; j < 16; ++j) {
+                    const int16_t v = tile[h + j][q];
+                    hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << (8 * (j % 4));
+                    lw[j / 4] |= (((uint32_t)v & 255u) ^ 0x80u) << (8 * (j % 4));
+                    if (c0 + h + j < g.C) sum += (int32_t)v - 128;
+                }
+                *(uint4*)(dst + c0 + h) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                *(uint4*)(dst + plane + c0 + h) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            }
+        }
     }
-    __syncthreads();
-    for (uint32_t t = threadIdx.x; t < nw; t += blockDim.x)
-        S[((uint64_t)n * g.Hp + hp) * g.Wp + w0 + t] = ssum[t];
+    if (qp < HWp) S[(uint64_t)n * HWp + qp] = sum;
 }
 
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
@@ -142,45 +150,147 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
     }
 }
 
-// weights [M][C][kh][kw] -> N-major planes [2][Kt][M_pad], row k' = r*KR_pad + s*Cp + c;
-// k' outside the real taps holds h = l' = 0 and so adds nothing to any product.
-__global__ void __launch_bounds__(256) conv_weight_kn_kernel(const int16_t* __restrict__ w, uint32_t M, uint32_t C,
-                                                             uint32_t kh, uint32_t kw, uint32_t Cp, uint32_t KR_pad,
-                                                             uint32_t M_pad, uint32_t Kt, int8_t* __restrict__ planes) {
-    const uint64_t total = (uint64_t)Kt * M;
-    const uint64_t plane = (uint64_t)Kt * M_pad;
-    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
-        const uint32_t kp = (uint32_t)(t / M), m = (uint32_t)(t - (uint64_t)kp * M);
-        const uint32_t r = kp / KR_pad, rem = kp - r * KR_pad;
-        const uint32_t s = rem / Cp, c = rem - s * Cp;
-        int8_t hi = 0, lo = 0;
-        if (s < kw && c < C) {
-            const int16_t v = __ldg(w + (((uint64_t)m * C + c) * kh + r) * kw + s);
-            hi = (int8_t)(v >> 8);
-            lo = (int8_t)((v & 255) - 128);
+// weights [M][C][kh][kw] -> N-major planes: tap k = (c, r, s) of output channel m
+// goes to row k' = r*KR_pad + s*Cp + c, element (p, k', m) at
+// planes[p*plane + k'*pitch + m] -- [2][Kt][M_pad] (pitch M_pad, plane Kt*M_pad)
+// or packed [Kt][64 hi | 64 lo] (pitch 128, plane 64) for M <= 64.  The rows
+// that hold no tap stay as zeroed beforehand (h = l' = 0 adds nothing).
+// colterm[m] += 128 * sum_k (w - 128), plus 16384 * K + (bias << 8) from the
+// first tile (mod 2^32; colterm zeroed beforehand).  Block = 32 channels x 128
+// taps: rows of w read along k, transposed through shared memory, written as
+// 16-byte runs of 16 channels.  With kh = kw = 1, C = Cp = KR_pad = K the rows
+// keep the natural order.
+__global__ void __launch_bounds__(256) conv_weights_kernel(const int16_t* __restrict__ w, const int16_t* __restrict__ bias,
+                                                           uint32_t M, uint32_t C, uint32_t kh, uint32_t kw, uint32_t Cp,
+                                                           uint32_t KR_pad, uint32_t pitch, uint64_t plane,
+                                                           int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    __shared__ int16_t tile[32][130];
+    const uint32_t khw = kh * kw, K = C * khw;
+    const uint32_t k0 = blockIdx.x * 128, m0 = blockIdx.y * 32;
+    const uint32_t t = threadIdx.x;
+    {
+        const uint32_t ml = t / 8, kq = (t % 8) * 16, m = m0 + ml;
+        int32_t sum = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < 16; ++j) {
+            const uint32_t k = k0 + kq + j;
+            int16_t v = 0;
+            if (m < M && k < K) {
+                v = __ldg(w + (uint64_t)m * K + k);
+                sum += (int32_t)v - 128;
+            }
+            tile[ml][kq + j] = v;
         }
-        planes[(uint64_t)kp * M_pad + m] = hi;
-        planes[plane + (uint64_t)kp * M_pad + m] = lo;
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 2);
+        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 4);
+        if ((t % 8) == 0 && m < M) {
+            uint32_t add = (uint32_t)sum * 128u;
+            if (blockIdx.x == 0) {
+                add += K * 16384u;
+                if (bias) add += (uint32_t)((int32_t)bias[m] * 256);
+            }
+            atomicAdd((unsigned int*)(colterm + m), add);
+        }
+    }
+    __syncthreads();
+    const uint32_t kl = t / 2, half = t % 2, k = k0 + kl;
+    // a run of 16 channels that starts below M ends within the row (M_pad, or 64 packed)
+    if (k < K && m0 + 16 * half < M) {
+        const uint32_t c = k / khw, rs = k - c * khw;
+        const uint32_t r = rs / kw, sx = rs - r * kw;
+        const uint64_t o = ((uint64_t)r * KR_pad + (uint64_t)sx * Cp + c) * pitch + m0 + 16 * half;
+        uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (uint32_t j = 0; j < 16; ++j) {
+            const int16_t v = tile[16 * half + j][kl];
+            hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << (8 * (j % 4));
+            lw[j / 4] |= (uint32_t)(uint8_t)((v & 255) - 128) << (8 * (j % 4));
+        }
+        *(uint4*)(planes + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *(uint4*)(planes + plane + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
 }
 
-// colterm[m] = 128 * sum_k (w - 128) + 16384 * K + (bias ? bias[m] << 8 : 0)  (mod 2^32); warp per m.
-__global__ void __launch_bounds__(256) conv_colterm_kernel(const int16_t* __restrict__ w, const int16_t* __restrict__ bias,
-                                                           uint32_t M, uint32_t K, int32_t* __restrict__ colterm) {
-    const uint32_t lane = threadIdx.x & 31u;
-    const uint64_t warps = (uint64_t)gridDim.x * blockDim.x / 32;
-    for (uint64_t m = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32; m < M; m += warps) {
-        const int16_t* wr = w + m * K;
-        int32_t sum = 0;
-        for (uint32_t k = lane; k < K; k += 32) sum += (int32_t)__ldg(wr + k) - 128;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
-        if (lane == 0) {
-            uint32_t term = (uint32_t)sum * 128u + K * 16384u;
-            if (bias) term += (uint32_t)((int32_t)bias[m] * 256);
-            colterm[m] = (int32_t)term;
-        }
+// Weight planes + column terms for a conv GEMM (see conv_weights_kernel).
+int conv_weights(const Context* cx, const int16_t* weight, const int16_t* bias, uint32_t M, uint32_t C, uint32_t kh,
+                 uint32_t kw, uint32_t Cp, uint32_t KR_pad, uint32_t pitch, uint64_t plane, uint64_t plane_bytes,
+                 int8_t* planes, int32_t* colterm, cudaStream_t s) {
+    cudaError_t e = cudaMemsetAsync(planes, 0, plane_bytes, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(colterm, 0, (size_t)M * sizeof(int32_t), s);
+    if (e != cudaSuccess) return cuda_error(e, "memset conv weights");
+    const uint32_t K = C * kh * kw;
+    const dim3 grid((K + 127) / 128, (M + 31) / 32);
+    {
+        ProfScope ps_(PK_SPLIT, s);
+        conv_weights_kernel<<<grid, 256, 0, s>>>(weight, bias, M, C, kh, kw, Cp, KR_pad, pitch, plane, planes, colterm);
     }
+    count_launch();
+    return CM_OK;
+}
+
+// im2col -> K-major planes [2][rows][K_pad], row = n*P + p (output pixel p of image
+// n), column k = (c, r, s) in the weight layout's order; out-of-range taps read
+// 0 (ConvKernel.cpp:184-202).  rowterm[row] = 128 * sum_k (x - 128).
+// Block = 128 rows, thread = one row: for each slice of up to 160 columns the
+// thread gathers its taps (a warp reads one tap of 32 neighbouring pixels),
+// packs them into 16-byte runs in shared memory, and the block then copies the
+// slice out as consecutive 16-byte runs (whole rows when K_pad <= 160).
+constexpr uint32_t kIcRows = 128, kIcSlice = 160, kIcPitch = kIcSlice + 16;
+
+__global__ void __launch_bounds__(kIcRows) im2col_rows_kernel(const int16_t* __restrict__ x, ConvGeom g, uint32_t P,
+                                                              uint64_t rows, uint32_t K, uint32_t K_pad,
+                                                              int8_t* __restrict__ planes, int32_t* __restrict__ rowterm) {
+    __shared__ __align__(16) int8_t stage[2][kIcRows * kIcPitch];
+    const uint64_t plane = rows * K_pad;
+    const uint64_t r0 = (uint64_t)blockIdx.x * kIcRows;
+    const uint64_t t = r0 + threadIdx.x;
+    const bool live = t < rows;
+    const uint32_t n = live ? (uint32_t)(t / P) : 0u;
+    const uint32_t p = live ? (uint32_t)(t - (uint64_t)n * P) : 0u;
+    const uint32_t oh = p / g.out_w, ow = p - oh * g.out_w;
+    const int32_t ihb = (int32_t)(oh * g.sh) - (int32_t)g.pt;
+    const int32_t iwb = (int32_t)(ow * g.sw) - (int32_t)g.pl;
+    const int16_t* xn = x + (uint64_t)n * g.C * g.H * g.W;
+    const uint32_t nrows = rows - r0 < kIcRows ? (uint32_t)(rows - r0) : kIcRows;
+    uint32_t c = 0, r = 0, sx = 0;
+    int32_t sum = 0;
+    for (uint32_t s0 = 0; s0 < K_pad; s0 += kIcSlice) {
+        const uint32_t sw = min(kIcSlice, K_pad - s0);      // multiple of 16
+        for (uint32_t k0 = s0; k0 < s0 + sw; k0 += 16) {
+            uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (uint32_t j = 0; j < 16; ++j) {
+                int16_t v = 0;
+                if (live && k0 + j < K) {
+                    const int32_t ih = ihb + (int32_t)(r * g.dh), iw = iwb + (int32_t)(sx * g.dw);
+                    if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
+                        v = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
+                    sum += (int32_t)v - 128;
+                    if (++sx == g.kw) {
+                        sx = 0;
+                        if (++r == g.kh) { r = 0; ++c; }
+                    }
+                }
+                hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << (8 * (j % 4));
+                lw[j / 4] |= (((uint32_t)v & 255u) ^ 0x80u) << (8 * (j % 4));
+            }
+            const uint32_t o = threadIdx.x * kIcPitch + (k0 - s0);
+            *(uint4*)(stage[0] + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(stage[1] + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        __syncthreads();
+        const uint32_t cpr = sw / 16, nchunks = nrows * cpr;
+        for (uint32_t i = threadIdx.x; i < nchunks; i += kIcRows) {
+            const uint32_t rr = i / cpr, cc = i - rr * cpr;
+            const uint64_t go = (r0 + rr) * K_pad + s0 + 16 * cc;
+            const uint32_t so = rr * kIcPitch + 16 * cc;
+            *(uint4*)(planes + go) = *(const uint4*)(stage[0] + so);
+            *(uint4*)(planes + plane + go) = *(const uint4*)(stage[1] + so);
+        }
+        __syncthreads();
+    }
+    if (live) rowterm[t] = (int32_t)((uint32_t)sum * 128u);
 }
 
 uint32_t pow2_ceil(uint32_t v) {
@@ -201,8 +311,8 @@ struct ImplicitPlan {
 
 // The implicit GEMM applies when each kernel row's taps are one contiguous run
 // of the channels-last input (dilation_w == 1), the traversal strides fit TMA
-// (<= 8), and padding every kernel row's kw*Cp bytes up to 128 costs at most
-// half again the real reduction length.
+// (<= 8), and the channel padding (C up to Cp, kw*Cp up to 32) costs at most
+// half again the real reduction length in MMA steps.
 bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
                    uint32_t dh, uint32_t dw, ImplicitPlan* ip) {
     if (dw != 1 || sh == 0 || sw == 0 || sh > 8 || sw > 8 || kh == 0 || kw == 0 || C == 0) return false;
@@ -210,10 +320,13 @@ bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint
     if (Cp > 8192) return false;
     const uint64_t KR = (uint64_t)kw * Cp, KR_pad = (KR + 127) & ~127ull, Kt = KR_pad * kh;
     const uint64_t Kreal = (uint64_t)C * kh * kw;
-    if (2 * Kt > 3 * Kreal || Kt > (1ull << 30)) return false;
+    // MMA work: every kernel row runs ceil(KR/32) 32-deep steps (the zero tail of
+    // each row's last block is skipped); allow at most half again the real taps
+    const uint64_t steps = (uint64_t)kh * ((KR + 31) / 32) * 32;
+    if (2 * steps > 3 * Kreal || Kt > (1ull << 30)) return false;
     const uint64_t Hp = (uint64_t)(out_h - 1) * sh + (uint64_t)(kh - 1) * dh + 1;
     const uint64_t Wp = (uint64_t)(out_w - 1) * sw + (kw - 1) + 1;
-    if (Hp >= (1ull << 31) || Wp >= (1ull << 31)) return false;
+    if (Hp * Wp >= (1ull << 31)) return false;
     uint32_t bw = std::min<uint32_t>(pow2_ceil(out_w), 128);
     while (bw * sw > 256) bw >>= 1;
     uint32_t bh = std::min<uint32_t>(pow2_ceil(out_h), 128 / bw);
@@ -277,12 +390,15 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
     if (plan_implicit(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &ip)) {
         // rows = output pixels of a chunk of images, columns = output channels
         const uint32_t M_pad = pad_c(out_ch);
+        const bool packed = out_ch <= 64;                 // one 64-column tile
+        const uint32_t w_pitch = packed ? 128u : M_pad;
+        const uint64_t w_plane = packed ? 64u : (uint64_t)ip.Kt * M_pad;
         const uint64_t img_plane = (uint64_t)ip.Hp * ip.Wp * ip.Cp;
         uint64_t chunk = kNhwcBudget / (2 * img_plane);
         if (chunk == 0) chunk = 1;
         if (chunk > batch) chunk = batch;
         if (chunk > (1u << 24)) chunk = 1u << 24;
-        const uint64_t w_bytes = ((uint64_t)2 * ip.Kt * M_pad + 255) & ~255ull;
+        const uint64_t w_bytes = ((uint64_t)ip.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
         const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
         const uint64_t a_bytes = (2 * chunk * img_plane + ip.KR + 256 + 255) & ~255ull;   // + slack past the last pixel
         const uint64_t s_bytes = (chunk * ip.Hp * ip.Wp * 4 + 255) & ~255ull;
@@ -295,31 +411,20 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         int8_t* apl = (int8_t*)ct + ct_bytes;
         int32_t* S = (int32_t*)(apl + a_bytes);
         int32_t* rt = (int32_t*)((int8_t*)S + s_bytes);
-        {
-            ProfScope ps_(PK_SPLIT, s);
-            const uint64_t wtot = (uint64_t)ip.Kt * out_ch;
-            conv_weight_kn_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad,
-                                                                            M_pad, ip.Kt, wpl);
-            conv_colterm_kernel<<<grid_for(cx, (uint64_t)out_ch * 32, 256, 8), 256, 0, s>>>(
-                weight, has_bias ? bias : nullptr, out_ch, K, ct);
-        }
-        count_launch();
-        count_launch();
-        const uint32_t wchunk = std::min<uint32_t>(ip.Wp, std::max<uint32_t>(1u, 46000u / (2 * (ip.Cp + 2) + 4)));
-        const size_t nhwc_smem = (size_t)wchunk * (ip.Cp + 2) * 2 + (size_t)wchunk * 4;
+        rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch, w_plane,
+                          w_bytes, wpl, ct, s);
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
             const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
             const NhwcGeom ng{in_ch, in_h, in_w, ip.Cp, ip.Hp, ip.Wp, pad_top, pad_left, nb};
             const uint64_t tot = (uint64_t)nb * P;
             {
                 ProfScope ps_(PK_SPLIT, s);
+                const uint32_t gx = (uint32_t)(((uint64_t)ip.Hp * ip.Wp + kNhwcPix - 1) / kNhwcPix);
                 for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                     const uint32_t bz = std::min(65535u, nb - b0);
-                    NhwcGeom gb = ng;
-                    const dim3 grid((ip.Wp + wchunk - 1) / wchunk, ip.Hp, bz);
-                    // the plane stride stays that of the whole chunk
-                    conv_nhwc_split_kernel<<<grid, 256, nhwc_smem, s>>>(
-                        x + (n0 + b0) * (uint64_t)in_ch * in_h * in_w, gb, wchunk, apl + (uint64_t)b0 * img_plane,
+                    // the plane stride stays that of the whole chunk (ng.nimg = nb)
+                    conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(
+                        x + (n0 + b0) * (uint64_t)in_ch * in_h * in_w, ng, apl + (uint64_t)b0 * img_plane,
                         S + (uint64_t)b0 * ip.Hp * ip.Wp);
                     count_launch();
                 }
@@ -332,6 +437,7 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, ip.Kt, ip.Kt, M_pad, rt, ct,
                        y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
+            p.b_packed = packed ? 1u : 0u;
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -340,30 +446,45 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv");
     }
 
-    const uint64_t per_img = 2 * (uint64_t)K * pad_c((uint32_t)P);
+    // Explicit im2col: rows = output pixels of a chunk of images (K-major planes),
+    // columns = output channels, K in the weight layout's (c, r, s) order.
+    const uint32_t M_pad = pad_c(out_ch);
+    const bool packed = out_ch <= 64;
+    const uint32_t w_pitch = packed ? 128u : M_pad;
+    const uint64_t w_plane = packed ? 64u : (uint64_t)K * M_pad;
+    const uint64_t per_img = 2 * (uint64_t)K_pad * P;
     uint64_t chunk = kIm2colBudget / per_img;
     if (chunk == 0) chunk = 1;
     if (chunk > batch) chunk = batch;
-    const uint64_t w_bytes = ((uint64_t)2 * out_ch * K_pad + 255) & ~255ull;
-    const uint64_t rt_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
-    const uint64_t b_bytes = (chunk * per_img + 255) & ~255ull;
-    const uint64_t ct_bytes = (chunk * P * 4 + 255) & ~255ull;
+    if (chunk * P >= (1ull << 31)) chunk = ((1ull << 31) - 1) / P;
+    const uint64_t w_bytes = ((uint64_t)K * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+    const uint64_t a_bytes = (chunk * per_img + 255) & ~255ull;
+    const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
     void* scratch = nullptr;
-    rc = scratch_alloc(&scratch, w_bytes + rt_bytes + b_bytes + ct_bytes, s);
+    rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + rt_bytes, s);
     if (rc) return rc;
-    int8_t* wp = (int8_t*)scratch;
-    int32_t* rt = (int32_t*)(wp + w_bytes);
-    int8_t* bp = (int8_t*)rt + rt_bytes;
-    int32_t* ct = (int32_t*)(bp + b_bytes);
+    int8_t* wpl = (int8_t*)scratch;
+    int32_t* ct = (int32_t*)(wpl + w_bytes);
+    int8_t* apl = (int8_t*)ct + ct_bytes;
+    int32_t* rt = (int32_t*)(apl + a_bytes);
 
-    rc = split_rows(cx, weight, 0, K, out_ch, K, 1, wp, rt, has_bias ? bias : nullptr, s);
+    // natural tap order: kh = kw = 1, C = Cp = KR_pad = K
+    rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, K, 1, 1, K, K, w_pitch, w_plane, w_bytes, wpl, ct, s);
     const ConvGeom geo{in_ch, in_h, in_w, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left};
     for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
         const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
-        rc = split_im2col(cx, x + n0 * (uint64_t)in_ch * in_h * in_w, geo, nb, bp, ct, s);
-        if (rc) break;
-        GemmPlan p{wp, out_ch, 1, bp, (uint32_t)P, nb, K, K_pad, pad_c((uint32_t)P), rt, ct,
-                   y + n0 * (uint64_t)out_ch * P, P, 1, (uint64_t)out_ch * P, nb};
+        const uint64_t rows = (uint64_t)nb * P;
+        {
+            ProfScope ps_(PK_SPLIT, s);
+            im2col_rows_kernel<<<(unsigned)((rows + kIcRows - 1) / kIcRows), kIcRows, 0, s>>>(x + n0 * (uint64_t)in_ch * in_h * in_w, geo,
+                                                                         (uint32_t)P, rows, K, K_pad, apl, rt);
+        }
+        count_launch();
+        GemmPlan p{apl, (uint32_t)rows, 1, wpl, out_ch, 1, K, K_pad, M_pad, rt, ct,
+                   y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
+        p.b_packed = packed ? 1u : 0u;
+        p.rows_per_img = (uint32_t)P;
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);

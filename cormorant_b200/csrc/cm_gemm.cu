@@ -40,22 +40,34 @@
 namespace cm {
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 128, STAGES = 3;
-constexpr int PLANE_TILE = BM * BK;                 // 16 KB
-constexpr int OPERAND_TILE = 2 * PLANE_TILE;        // hi + lo = 32 KB
-constexpr int STAGE_BYTES = 2 * OPERAND_TILE;       // A + B = 64 KB
-constexpr int SMEM_USED = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int BM = 128, BK = 128;
+constexpr int PLANE_TILE = BM * BK;                 // 16 KB: one plane of a 128 x 128 operand tile
+constexpr int OPERAND_TILE = 2 * PLANE_TILE;        // A hi + lo = 32 KB
 // The whole per-CTA maximum is requested (1 CTA per SM either way), so every
 // operand descriptor stays inside this CTA's own allocation with margin.
 constexpr int SMEM_BYTES = 232448;
-static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
 constexpr uint32_t TMEM_COLS = 512;
-constexpr uint32_t COL_HH = 0, COL_HL = 128, COL_LH = 256, COL_LL = 384;
-constexpr uint32_t MMA_N = 2 * BN;   // [Bh; Bl]
 
-// Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128, N = 256.
-constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(MMA_N >> 3) << 17) |
-                           ((uint32_t)(BM >> 4) << 24);
+// Column tile TBN = 128: B box = two N-major 128-column atoms [Bh | Bl] (32 KB),
+// four 128-column accumulators fill TMEM (one buffer).  TBN = 64 (outputs with
+// at most 64 columns): B is stored packed, each K row = [64 hi | 64 lo] bytes, so
+// one 128-byte atom is the whole [Bh | Bl] operand (16 KB); the four 64-column
+// accumulators take 256 TMEM columns and are double-buffered.
+template <int TBN>
+struct Cfg {
+    static constexpr int B_TILE = TBN == 128 ? 2 * PLANE_TILE : PLANE_TILE;
+    static constexpr int STAGE = OPERAND_TILE + B_TILE;
+    static constexpr int STAGES = TBN == 128 ? 3 : 4;
+    static constexpr int NBUF = TBN == 128 ? 1 : 2;
+    static constexpr uint32_t ACC_COLS = 4 * TBN;      // HH | HL | LH | LL
+    static constexpr uint32_t MMA_N = 2 * TBN;         // [Bh | Bl]
+    // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128, N = MMA_N.
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((MMA_N >> 3) << 17) |
+                                      ((uint32_t)(BM >> 4) << 24);
+    static constexpr int SMEM_USED = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
+    static_assert(NBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -142,13 +154,17 @@ __device__ __forceinline__ uint64_t sdesc_n(uint32_t addr) {
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t accumulate) {
+__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "setp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "l"(a), "l"(b), "r"(IDESC), "r"(accumulate)
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
         : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
@@ -174,59 +190,96 @@ __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.
 constexpr uint32_t GROUP_M = 8;
 
 struct GemmArgs {
-    uint32_t rows, cols, num_kb, a_batches, b_batches, tiles_m, tiles_n;
+    uint32_t rows, cols, num_kb, a_batches, b_batches, tiles_m, tiles_n, batch;
     const int32_t* rowterm;
     const int32_t* colterm;
     int16_t* out;
     uint64_t ldo, ldc, out_bs;
-    uint32_t z_base;
     int* status;
     uint64_t timeout_ns;
     // implicit conv (conv != 0): tile rows = bn images x bh rows x bw columns
     uint32_t conv, tiles_w, tiles_h, bw_log, bh_log, bn_log;
     uint32_t nimg, out_h, out_w, sw, sh, dh, kb_per_r;
+    // rows_per_img != 0: row = n*rows_per_img + p -> out[n*out_bs + p + col*ldc]
+    uint32_t rows_per_img;
+    uint32_t ksteps;          // 32-deep MMA steps covering K (conv: covering one kernel row's KR bytes)
 };
 
-__global__ void __launch_bounds__(192, 1)
-    gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
-    // bars[0..S) full, bars[S..2S) empty, bars[2S] acc_full
-    volatile uint32_t* tmem_slot = (volatile uint32_t*)(bars + 2 * STAGES + 1);
-    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+struct Tile {
+    uint32_t m0, n0, z, ba, bb;
+    uint32_t cw0, ch0, cn0;   // conv: first output column, row and image of the row tile
+};
 
-    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    // Grouped tile order: blocks of GROUP_M row tiles sweep the column tiles
-    // together, so the CTAs in flight share a few A and B panels in L2.
+// Tile t of the flattened (batch, grouped row/column) order.  Blocks of GROUP_M
+// row tiles sweep the column tiles together, so the ~148 tiles in flight share
+// a few A and B panels in L2.
+template <int TBN>
+__device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t) {
+    Tile c;
+    const uint64_t per_z = (uint64_t)g.tiles_m * g.tiles_n;
+    c.z = (uint32_t)(t / per_z);
+    const uint32_t local_t = (uint32_t)(t - (uint64_t)c.z * per_z);
     const uint32_t per_group = GROUP_M * g.tiles_n;
-    const uint32_t group = blockIdx.x / per_group;
+    const uint32_t group = local_t / per_group;
     const uint32_t first_m = group * GROUP_M;
     const uint32_t gsize = min(GROUP_M, g.tiles_m - first_m);
-    const uint32_t local = blockIdx.x - group * per_group;
+    const uint32_t local = local_t - group * per_group;
     const uint32_t tm = first_m + local % gsize;
-    const uint32_t m0 = tm * BM;                          // output row tile (A rows)
-    const uint32_t n0 = (local / gsize) * BN;             // output column tile (B columns)
-    // conv: the row tile is (image block, output-row block, output-column block)
-    uint32_t cw0 = 0, ch0 = 0, cn0 = 0;
+    c.m0 = tm * BM;
+    c.n0 = (local / gsize) * TBN;
+    c.ba = g.a_batches == 1 ? 0u : c.z;
+    c.bb = g.b_batches == 1 ? 0u : c.z;
+    c.cw0 = c.ch0 = c.cn0 = 0;
     if (g.conv) {
         const uint32_t t_hw = g.tiles_w * g.tiles_h;
         const uint32_t tn = tm / t_hw, rem = tm - tn * t_hw;
         const uint32_t th = rem / g.tiles_w;
-        cn0 = tn << g.bn_log;
-        ch0 = th << g.bh_log;
-        cw0 = (rem - th * g.tiles_w) << g.bw_log;
+        c.cn0 = tn << g.bn_log;
+        c.ch0 = th << g.bh_log;
+        c.cw0 = (rem - th * g.tiles_w) << g.bw_log;
     }
-    const uint32_t z = blockIdx.z + g.z_base;
-    const uint32_t ba = g.a_batches == 1 ? 0u : z;
-    const uint32_t bb = g.b_batches == 1 ? 0u : z;
+    return c;
+}
+
+// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+//   warp 0      TMA producer (continuous stage ring across tiles)
+//   warp 1      TMEM owner; lane 0 issues the MMAs of each tile into an accumulator
+//               buffer once the epilogue has drained it
+//   warps 2-9   epilogue: warp w reads TMEM lanes 32*(w%4).. of column half (w-2)/4,
+//               combines the four accumulators into registers, releases the buffer,
+//               then adds the rank-1 terms, narrows and stores while the next
+//               tile's MMAs run.
+template <int TBN>
+__global__ void __launch_bounds__(320, 1)
+    gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+    using C = Cfg<TBN>;
+    constexpr int STAGES = C::STAGES, NBUF = C::NBUF;
+    constexpr uint32_t HALF = TBN / 2;                  // columns per epilogue warp
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + STAGES * C::STAGE);
+    // bars: [0,S) full, [S,2S) empty, [2S,2S+NBUF) acc_full, [2S+NBUF,2S+2NBUF) acc_empty, then done
+    uint64_t* full_b = bars;
+    uint64_t* empty_b = bars + STAGES;
+    uint64_t* accf_b = bars + 2 * STAGES;
+    uint64_t* acce_b = accf_b + NBUF;
+    uint64_t* done_b = acce_b + NBUF;
+    volatile uint32_t* tmem_slot = (volatile uint32_t*)(done_b + 1);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint64_t total = (uint64_t)g.batch * g.tiles_m * g.tiles_n;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
-            mbar_init(smem_u32(&bars[s]), 1);
-            mbar_init(smem_u32(&bars[STAGES + s]), 1);
+            mbar_init(smem_u32(&full_b[s]), 1);
+            mbar_init(smem_u32(&empty_b[s]), 1);
         }
-        mbar_init(smem_u32(&bars[2 * STAGES]), 1);
+        for (int b = 0; b < NBUF; ++b) {
+            mbar_init(smem_u32(&accf_b[b]), 1);
+            mbar_init(smem_u32(&acce_b[b]), 8);
+        }
+        mbar_init(smem_u32(done_b), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -245,140 +298,170 @@ __global__ void __launch_bounds__(192, 1)
 
     if (warp == 0) {
         if (lane == 0) {
-            uint32_t issued = 0;
-            for (uint32_t kb = 0; kb < g.num_kb; ++kb) {
-                const uint32_t s = kb % STAGES, round = kb / STAGES;
-                if (!mbar_wait(smem_u32(&bars[STAGES + s]), (round & 1u) ^ 1u, wc)) break;
-                const uint32_t full = smem_u32(&bars[s]);
-                mbar_expect_tx(full, STAGE_BYTES);
-                uint8_t* st = smem + s * STAGE_BYTES;
-                if (g.conv) {
-                    const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
-                    const int c1 = (int)(cw0 * g.sw), c2 = (int)(ch0 * g.sh + r * g.dh);
-                    tma_load_5d(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)cn0, 0);
-                    tma_load_5d(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)cn0, 1);
-                } else {
-                    tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)m0, 0, (int)ba);
+            uint32_t it = 0;
+            for (uint64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
+                const Tile tc = decode_tile<TBN>(g, t);
+                for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(smem_u32(&empty_b[s]), (round & 1u) ^ 1u, wc)) break;
+                    const uint32_t full = smem_u32(&full_b[s]);
+                    mbar_expect_tx(full, C::STAGE);
+                    uint8_t* st = smem + s * C::STAGE;
+                    if (g.conv) {
+                        const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
+                        const int c1 = (int)(tc.cw0 * g.sw), c2 = (int)(tc.ch0 * g.sh + r * g.dh);
+                        tma_load_5d(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 0);
+                        tma_load_5d(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 1);
+                    } else {
+                        tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)tc.m0, 0, (int)tc.ba);
+                    }
+                    tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), 0, (int)tc.bb);
                 }
-                tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)n0, (int)(kb * BK), 0, (int)bb);
-                ++issued;
             }
             if (*abort_flag) {
                 // let copies already in flight land before the CTA exits
-                const uint32_t first = issued > (uint32_t)STAGES ? issued - STAGES : 0u;
-                WaitCtl drain{abort_flag, g.status, g.timeout_ns};
-                for (uint32_t kb = first; kb < issued; ++kb) {
-                    volatile int never = 0;
-                    drain.abort = &never;
-                    mbar_wait(smem_u32(&bars[kb % STAGES]), (kb / STAGES) & 1u, drain);
-                }
+                const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
+                volatile int never = 0;
+                WaitCtl drain{&never, g.status, g.timeout_ns};
+                for (uint32_t k = first; k < it; ++k) mbar_wait(smem_u32(&full_b[k % STAGES]), (k / STAGES) & 1u, drain);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            for (uint32_t kb = 0; kb < g.num_kb; ++kb) {
-                const uint32_t s = kb % STAGES, round = kb / STAGES;
-                if (!mbar_wait(smem_u32(&bars[s]), round & 1u, wc)) break;
+            uint32_t it = 0, j = 0;
+            bool ok = true;
+            for (uint64_t t = blockIdx.x; ok && t < total; t += gridDim.x, ++j) {
+                const uint32_t buf = j % NBUF, use = j / NBUF;
+                if (!mbar_wait(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, wc)) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(smem + s * STAGE_BYTES);
-                const uint32_t b0 = a0 + OPERAND_TILE;
+                const uint32_t d = tmem + buf * C::ACC_COLS;
+                for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(smem_u32(&full_b[s]), round & 1u, wc)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(smem + s * C::STAGE);
+                    const uint32_t b0 = a0 + OPERAND_TILE;
+                    // 32-deep steps of this block that hold any tap (the rest are zero in A and B)
+                    const uint32_t steps = g.conv ? g.ksteps - (kb % g.kb_per_r) * (BK / 32) : g.ksteps - kb * (BK / 32);
 #pragma unroll
-                for (uint32_t kk = 0; kk < BK / 32; ++kk) {
-                    const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
-                    const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x (Bh | Bl)
-                    const uint32_t acc = (kb | kk) != 0u;
-                    umma_i8(tmem + COL_HH, ah, bhl, acc);         // -> HH | HL
-                    umma_i8(tmem + COL_LH, al, bhl, acc);         // -> LH | LL
+                    for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                        if (kk >= steps) break;
+                        const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
+                        const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x [Bh | Bl]
+                        const uint32_t acc = (kb | kk) != 0u;
+                        umma_i8(d, ah, bhl, C::IDESC, acc);                 // -> HH | HL
+                        umma_i8(d + 2 * TBN, al, bhl, C::IDESC, acc);       // -> LH | LL
+                    }
+                    umma_commit(smem_u32(&empty_b[s]));   // frees the stage once these MMAs have read it
                 }
-                umma_commit(smem_u32(&bars[STAGES + s]));   // frees the stage once these MMAs have read it
+                if (ok) umma_commit(smem_u32(&accf_b[buf]));
             }
-            umma_commit(smem_u32(&bars[2 * STAGES]));      // accumulators complete (or nothing in flight)
+            // every MMA issued by this thread has completed once `done` fires
+            umma_commit(smem_u32(done_b));
+            volatile int never = 0;
+            WaitCtl drain{&never, g.status, g.timeout_ns};
+            mbar_wait(smem_u32(done_b), 0, drain);
         }
     } else {
-        // Epilogue: warp w reads TMEM lanes [32*(w%4), 32*(w%4)+32).
         const uint32_t quarter = warp & 3u;
+        const uint32_t half = (warp - 2) >> 2;
         const uint32_t i = quarter * 32 + lane;           // TMEM lane = A tile row
-        bool valid;
-        uint64_t rt_idx, o_off;
-        if (g.conv) {
-            const uint32_t ow = cw0 + (i & ((1u << g.bw_log) - 1u));
-            const uint32_t oh = ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
-            const uint32_t n = cn0 + (i >> (g.bw_log + g.bh_log));
-            valid = ow < g.out_w && oh < g.out_h && n < g.nimg;
-            const uint64_t pix = (uint64_t)oh * g.out_w + ow;
-            rt_idx = (uint64_t)n * g.out_h * g.out_w + pix;
-            o_off = (uint64_t)n * g.out_bs + pix;
-        } else {
-            const uint32_t row = m0 + i;
-            valid = row < g.rows;
-            rt_idx = (uint64_t)ba * g.rows + row;
-            o_off = (uint64_t)z * g.out_bs + (uint64_t)row * g.ldo;
-        }
-        // One lane waits; the verdict is broadcast so that the .sync.aligned
-        // TMEM loads below are executed by the whole warp or not at all.
-        uint32_t ok = 0;
-        if (lane == 0) ok = (mbar_wait(smem_u32(&bars[2 * STAGES]), 0, wc) && !*abort_flag) ? 1u : 0u;
-        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-        __syncwarp();
-        tc_fence_after();
-        if (ok) {
-            const uint32_t rt = valid ? (uint32_t)g.rowterm[rt_idx] : 0u;
-            const int32_t* ct = g.colterm + (uint64_t)bb * g.cols;
-            int16_t* orow = g.out + o_off;
-            const uint32_t tl = tmem + ((quarter * 32u) << 16);
-#pragma unroll 1
-            for (uint32_t c0 = 0; c0 < BN; c0 += 32) {
-                if (n0 + c0 >= g.cols) break;
-                // acc = 2^16*HH + 2^8*(HL + LH) + LL = ((((HH << 8) + HL + LH) << 8) + LL
-                uint32_t p[32], q[32];
-                tmem_ld32(tl + COL_HH + c0, p);
-                tmem_ld32(tl + COL_HL + c0, q);
-                tmem_ld_wait();
+        const uint32_t cbase = half * HALF;
+        uint32_t j = 0;
+        for (uint64_t t = blockIdx.x; t < total; t += gridDim.x, ++j) {
+            const uint32_t buf = j % NBUF, use = j / NBUF;
+            // One lane waits; the verdict is broadcast so that the .sync.aligned
+            // TMEM loads below are executed by the whole warp or not at all.
+            uint32_t ok = 0;
+            if (lane == 0) ok = (mbar_wait(smem_u32(&accf_b[buf]), use & 1u, wc) && !*abort_flag) ? 1u : 0u;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            __syncwarp();
+            if (!ok) break;
+            tc_fence_after();
+            const Tile tc = decode_tile<TBN>(g, t);
+            bool valid;
+            uint64_t rt_idx, o_off;
+            if (g.conv) {
+                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
+                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
+                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                valid = ow < g.out_w && oh < g.out_h && n < g.nimg;
+                const uint64_t pix = (uint64_t)oh * g.out_w + ow;
+                rt_idx = (uint64_t)n * g.out_h * g.out_w + pix;
+                o_off = (uint64_t)n * g.out_bs + pix;
+            } else {
+                const uint32_t row = tc.m0 + i;
+                valid = row < g.rows;
+                rt_idx = (uint64_t)tc.ba * g.rows + row;
+                if (g.rows_per_img) {
+                    const uint32_t n = row / g.rows_per_img;
+                    o_off = (uint64_t)n * g.out_bs + (row - n * g.rows_per_img);
+                } else {
+                    o_off = (uint64_t)tc.z * g.out_bs + (uint64_t)row * g.ldo;
+                }
+            }
+            const uint32_t rt = valid ? (uint32_t)__ldg(g.rowterm + rt_idx) : 0u;
+            const int32_t* ct = g.colterm + (uint64_t)tc.bb * g.cols;
+            // Drain: acc = 2^16*HH + 2^8*(HL + LH) + LL + rowterm + colterm, narrowed
+            // and packed two int16 per word (even column in the low half).
+            uint32_t pk[HALF / 2];
+            const uint32_t tl = tmem + buf * C::ACC_COLS + ((quarter * 32u) << 16) + cbase;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) p[j] = (p[j] << 8) + q[j];
-                tmem_ld32(tl + COL_LH + c0, q);
-                tmem_ld_wait();
+            for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+                const uint32_t col0 = tc.n0 + cbase + c0;
+                if (col0 < g.cols) {
+                    uint32_t p[32], q[32];
+                    tmem_ld32(tl + c0, p);
+                    tmem_ld32(tl + TBN + c0, q);
+                    tmem_ld_wait();
 #pragma unroll
-                for (int j = 0; j < 32; ++j) p[j] = (p[j] + q[j]) << 8;
-                tmem_ld32(tl + COL_LL + c0, q);
-                tmem_ld_wait();
-                if (valid) {
-                    const uint32_t col0 = n0 + c0;
-                    int16_t v[32];
+                    for (int k = 0; k < 32; ++k) p[k] = (p[k] << 8) + q[k];
+                    tmem_ld32(tl + 2 * TBN + c0, q);
+                    tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const uint32_t col = col0 + j;
-                        const uint32_t cterm = col < g.cols ? (uint32_t)__ldg(ct + col) : 0u;
-                        const uint32_t acc = p[j] + q[j] + rt + cterm;
-                        v[j] = narrow_acc(acc);
-                    }
-                    int16_t* dst = orow + col0;
-                    if (g.ldc != 1) {
-                        // column-strided output (conv: y[m][p] with rows = pixels): each
-                        // store is coalesced across the warp's consecutive rows
+                    for (int k = 0; k < 32; ++k) p[k] = (p[k] + q[k]) << 8;
+                    tmem_ld32(tl + 3 * TBN + c0, q);
+                    tmem_ld_wait();
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < g.cols) orow[(uint64_t)(col0 + j) * g.ldc] = v[j];
-                    } else if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
-                        uint4* d4 = (uint4*)dst;
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            uint4 w;
-                            w.x = (uint32_t)(uint16_t)v[8 * q + 0] | ((uint32_t)(uint16_t)v[8 * q + 1] << 16);
-                            w.y = (uint32_t)(uint16_t)v[8 * q + 2] | ((uint32_t)(uint16_t)v[8 * q + 3] << 16);
-                            w.z = (uint32_t)(uint16_t)v[8 * q + 4] | ((uint32_t)(uint16_t)v[8 * q + 5] << 16);
-                            w.w = (uint32_t)(uint16_t)v[8 * q + 6] | ((uint32_t)(uint16_t)v[8 * q + 7] << 16);
-                            d4[q] = w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (col0 + j < g.cols) dst[j] = v[j];
+                    for (int k = 0; k < 32; k += 2) {
+                        const uint32_t ca = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
+                        const uint32_t cb = col0 + k + 1 < g.cols ? (uint32_t)__ldg(ct + col0 + k + 1) : 0u;
+                        const uint16_t lo = (uint16_t)narrow_acc(p[k] + q[k] + rt + ca);
+                        const uint16_t hi = (uint16_t)narrow_acc(p[k + 1] + q[k + 1] + rt + cb);
+                        pk[(c0 + k) / 2] = (uint32_t)lo | ((uint32_t)hi << 16);
                     }
                 }
             }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce_b[buf]));   // buffer free for the next tile
+            if (!valid) continue;
+            int16_t* orow = g.out + o_off;
+#pragma unroll
+            for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+                const uint32_t col0 = tc.n0 + cbase + c0;
+                if (col0 >= g.cols) break;
+                int16_t* dst = orow + col0;
+                if (g.ldc != 1) {
+                    // column-strided output (conv: y[m][p] with rows = pixels): each
+                    // store is coalesced across the warp's consecutive rows
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        if (col0 + k < g.cols)
+                            orow[(uint64_t)(col0 + k) * g.ldc] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
+                } else if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
+                    uint4* d4 = (uint4*)dst;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q)
+                        d4[q] = make_uint4(pk[c0 / 2 + 4 * q], pk[c0 / 2 + 4 * q + 1], pk[c0 / 2 + 4 * q + 2],
+                                           pk[c0 / 2 + 4 * q + 3]);
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 32; ++k)
+                        if (col0 + k < g.cols) dst[k] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
+                }
+            }
         }
-        tc_fence_before();
     }
     __syncthreads();
     if (warp == 1) {
@@ -444,16 +527,19 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restri
 // B rows -> N-major planes.  Thread = 8 consecutive columns over a chunk of K:
 // 16-byte loads and 8-byte plane stores, both coalesced along N; the column
 // terms are summed in registers and added once per chunk.
+// Plane layout: element (bt, p, k, c) at planes[bt*batch_pitch + p*plane_off + k*C_pad + c]
+// (C_pad = row pitch): [2][K][C_pad] per batch, or packed [K][64 hi | 64 lo].
 __global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict__ src, uint64_t src_bs, uint64_t ld,
                                                        uint32_t cols, uint32_t K, uint32_t C_pad, uint32_t k_chunk,
+                                                       uint64_t plane_off, uint64_t batch_pitch,
                                                        int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
     const uint32_t bt = blockIdx.z;
     const uint32_t c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (c8 >= cols) return;
     const uint32_t k0 = blockIdx.y * k_chunk, k1 = min(K, k0 + k_chunk);
     const int16_t* sp = src + (uint64_t)bt * src_bs + c8;
-    int8_t* dh = planes + (uint64_t)bt * 2 * K * C_pad + c8;
-    int8_t* dl = dh + (uint64_t)K * C_pad;
+    int8_t* dh = planes + (uint64_t)bt * batch_pitch + c8;
+    int8_t* dl = dh + plane_off;
     int32_t sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     const bool vec = c8 + 8 <= cols && ((uintptr_t)sp & 15u) == 0 && (ld & 7u) == 0;
     if (vec) {
@@ -504,42 +590,6 @@ __global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict
     const uint32_t nc = min(8u, cols - c8);
     for (uint32_t j = 0; j < nc; ++j)
         atomicAdd((unsigned int*)(colterm + (uint64_t)bt * cols + c8 + j), (uint32_t)sum[j] * 128u);
-}
-
-// im2col -> N-major planes.  Thread = one output pixel p of image n over a
-// chunk of taps k = (c, r, s); consecutive threads hold consecutive pixels, so
-// input reads follow the row and plane writes are contiguous bytes.
-__global__ void __launch_bounds__(256) im2col_kn_kernel(const int16_t* __restrict__ x, ConvGeom g, uint32_t P,
-                                                        uint32_t K, uint32_t P_pad, uint32_t k_chunk, FastDiv fd_ow,
-                                                        int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
-    const uint32_t n = blockIdx.z;
-    const uint32_t p = blockIdx.x * blockDim.x + threadIdx.x;
-    if (p >= P) return;
-    const uint32_t k0 = blockIdx.y * k_chunk, k1 = min(K, k0 + k_chunk);
-    const uint32_t oh = fd_ow.div(p), ow = p - oh * g.out_w;
-    const int32_t ihb = (int32_t)(oh * g.sh) - (int32_t)g.pt;
-    const int32_t iwb = (int32_t)(ow * g.sw) - (int32_t)g.pl;
-    const uint32_t khw = g.kh * g.kw;
-    uint32_t c = k0 / khw, rs = k0 - c * khw;
-    uint32_t r = rs / g.kw, s = rs - r * g.kw;
-    const int16_t* xn = x + (uint64_t)n * g.C * g.H * g.W;
-    int8_t* dh = planes + (uint64_t)n * 2 * K * P_pad + p;
-    int8_t* dl = dh + (uint64_t)K * P_pad;
-    int32_t sum = 0;
-    for (uint32_t k = k0; k < k1; ++k) {
-        const int32_t ih = ihb + (int32_t)(r * g.dh), iw = iwb + (int32_t)(s * g.dw);
-        int16_t v = 0;
-        if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
-            v = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
-        dh[(uint64_t)k * P_pad] = (int8_t)(v >> 8);
-        dl[(uint64_t)k * P_pad] = (int8_t)((v & 255) - 128);
-        sum += (int32_t)v - 128;
-        if (++s == g.kw) {
-            s = 0;
-            if (++r == g.kh) { r = 0; ++c; }
-        }
-    }
-    atomicAdd((unsigned int*)(colterm + (uint64_t)n * P + p), (uint32_t)sum * 128u);
 }
 
 __global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
@@ -594,7 +644,7 @@ int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t 
     if (((uintptr_t)base & 15u) != 0 || (C_pad & 15u) != 0) return set_error(CM_EINVAL, "plane buffer misaligned");
     const cuuint64_t dims[4] = {cols, K, 2, batches};
     const cuuint64_t strides[3] = {(cuuint64_t)C_pad, (cuuint64_t)K * C_pad, (cuuint64_t)2 * K * C_pad};
-    const cuuint32_t box[4] = {(cuuint32_t)BN, (cuuint32_t)BK, 2, 1};
+    const cuuint32_t box[4] = {128, (cuuint32_t)BK, 2, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -627,63 +677,82 @@ int make_conv_map(CUtensorMap* m, const ConvA& c) {
     return CM_OK;
 }
 
+// B planes packed for 64-column tiles: [batches][K][128] int8, each K row =
+// [64 hi | 64 lo] bytes of one column tile; box {128, 128 k, 1, 1}.
+int make_packed_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t batches) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)base & 15u) != 0) return set_error(CM_EINVAL, "plane buffer misaligned");
+    const cuuint64_t dims[4] = {128, K, 1, batches};
+    const cuuint64_t strides[3] = {128, (cuuint64_t)K * 128, (cuuint64_t)K * 128};
+    const cuuint32_t box[4] = {128, (cuuint32_t)BK, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled (packed) failed (%d)", (int)r);
+    return CM_OK;
+}
+
+template <int TBN>
+int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+        attr_set = true;
+    }
+    g.tiles_n = (g.cols + TBN - 1) / TBN;
+    const uint64_t total = (uint64_t)g.batch * g.tiles_m * g.tiles_n;
+    if (total == 0) return CM_OK;
+    if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 32)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    const unsigned grid = (unsigned)std::min<uint64_t>(total, (uint64_t)cx->sm_count);
+    g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    {
+        ProfScope ps_(PK_GEMM, s);
+        gemm_q88_kernel<TBN><<<grid, 320, SMEM_BYTES, s>>>(ta, tb, g);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
+}
+
 }  // namespace
 
 int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     if (p.conv) return gemm_launch_conv(cx, p, s);
     if (p.K == 0) return fill_zero(cx, p.out, p.batch, p.rows, p.cols, p.ldo, p.out_bs, s);
     if (p.K > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "reduction length %u exceeds %u", p.K, kMaxGemmK);
+    if (p.b_packed && p.cols > 64) return set_error(CM_EINVAL, "packed B needs at most 64 columns");
     CUtensorMap ta, tb;
     int rc = make_plane_map(&ta, p.a_planes, p.K, p.K_pad, p.rows, p.a_batches);
     if (rc) return rc;
-    rc = make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, p.b_batches);
+    rc = p.b_packed ? make_packed_map(&tb, p.b_planes, p.K, p.b_batches)
+                    : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, p.b_batches);
     if (rc) return rc;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
-        attr_set = true;
-    }
-    GemmArgs g;
+    GemmArgs g{};
     g.rows = p.rows; g.cols = p.cols; g.num_kb = (p.K + BK - 1) / BK;
     g.tiles_m = (p.rows + BM - 1) / BM;
-    g.tiles_n = (p.cols + BN - 1) / BN;
-    if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    g.batch = p.batch;
     g.a_batches = p.a_batches; g.b_batches = p.b_batches;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
     g.out = p.out; g.ldo = p.ldo; g.ldc = p.ldc ? p.ldc : 1; g.out_bs = p.out_bs;
-    g.status = cx->status; g.timeout_ns = cx->timeout_ns;
     g.conv = 0;
-    const dim3 block(192);
-    for (uint32_t z0 = 0; z0 < p.batch; z0 += 65535u) {
-        const uint32_t nz = min(65535u, p.batch - z0);
-        g.z_base = z0;
-        const dim3 grid(g.tiles_m * g.tiles_n, 1, nz);
-        {
-            ProfScope ps_(PK_GEMM, s);
-            gemm_q88_kernel<<<grid, block, SMEM_BYTES, s>>>(ta, tb, g);
-        }
-        count_launch();
-    }
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
+    g.rows_per_img = p.rows_per_img;
+    g.ksteps = (p.K + 31) / 32;
+    return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
 }
 
 int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     const ConvA& c = *p.conv;
     if (p.K == 0 || p.K % BK != 0 || c.KR_pad % BK != 0 || p.K != c.kh * c.KR_pad)
         return set_error(CM_EINVAL, "conv GEMM reduction layout");
+    if (p.b_packed && p.cols > 64) return set_error(CM_EINVAL, "packed B needs at most 64 columns");
     CUtensorMap ta, tb;
     int rc = make_conv_map(&ta, c);
     if (rc) return rc;
-    rc = make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, 1);
+    rc = p.b_packed ? make_packed_map(&tb, p.b_planes, p.K, 1) : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, 1);
     if (rc) return rc;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
-        attr_set = true;
-    }
     GemmArgs g{};
     g.conv = 1;
     g.bw_log = c.bw_log; g.bh_log = c.bh_log; g.bn_log = c.bn_log;
@@ -691,22 +760,15 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.tiles_h = (c.out_h + (1u << c.bh_log) - 1) >> c.bh_log;
     const uint64_t tiles_img = (c.nimg + (1u << c.bn_log) - 1) >> c.bn_log;
     const uint64_t tiles_m = tiles_img * g.tiles_w * g.tiles_h;
-    g.cols = p.cols; g.num_kb = p.K / BK; g.kb_per_r = c.KR_pad / BK;
-    g.tiles_n = (p.cols + BN - 1) / BN;
-    if (tiles_m * g.tiles_n >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    if (tiles_m >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
     g.tiles_m = (uint32_t)tiles_m;
-    g.rows = 0; g.a_batches = 1; g.b_batches = 1;
+    g.cols = p.cols; g.num_kb = p.K / BK; g.kb_per_r = c.KR_pad / BK;
+    g.ksteps = (c.KR + 31) / 32;
+    g.batch = 1; g.rows = 0; g.a_batches = 1; g.b_batches = 1;
     g.nimg = c.nimg; g.out_h = c.out_h; g.out_w = c.out_w; g.sw = c.sw; g.sh = c.sh; g.dh = c.dh;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
-    g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs; g.z_base = 0;
-    g.status = cx->status; g.timeout_ns = cx->timeout_ns;
-    {
-        ProfScope ps_(PK_GEMM, s);
-        gemm_q88_kernel<<<dim3(g.tiles_m * g.tiles_n), dim3(192), SMEM_BYTES, s>>>(ta, tb, g);
-    }
-    count_launch();
-    cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? CM_OK : cuda_error(e, "conv gemm launch");
+    g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
+    return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
 }
 
 int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
@@ -732,7 +794,8 @@ static uint32_t pick_k_chunk(uint32_t K, uint64_t other_ctas, uint32_t sm_count)
 }
 
 int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
-             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s) {
+             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s, bool packed) {
+    if (packed && cols > 64) return set_error(CM_EINVAL, "packed B needs at most 64 columns");
     if ((uint64_t)cols * nbt == 0) return CM_OK;
     cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)cols * nbt * sizeof(int32_t), s);
     if (e != cudaSuccess) return cuda_error(e, "memset colterm");
@@ -741,40 +804,17 @@ int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld
     const uint32_t block = std::min<uint32_t>(256, (vec_threads + 31) / 32 * 32);
     const uint32_t gx = (vec_threads + block - 1) / block;
     const uint32_t k_chunk = pick_k_chunk(K, (uint64_t)gx * nbt, cx->sm_count);
-    const uint32_t C_pad = pad_c(cols);
+    const uint32_t C_pad = packed ? 128u : pad_c(cols);
+    const uint64_t plane_off = packed ? 64u : (uint64_t)K * C_pad;
+    const uint64_t batch_pitch = packed ? (uint64_t)K * 128 : 2ull * K * C_pad;
     for (uint32_t b0 = 0; b0 < nbt; b0 += 65535u) {
         const uint32_t nb = std::min(65535u, nbt - b0);
         const dim3 grid(gx, (K + k_chunk - 1) / k_chunk, nb);
         {
             ProfScope ps_(PK_SPLIT, s);
             split_kn_kernel<<<grid, block, 0, s>>>(src + (uint64_t)b0 * src_bs, src_bs, ld, cols, K, C_pad, k_chunk,
-                                                  planes + (uint64_t)b0 * 2 * K * C_pad, colterm + (uint64_t)b0 * cols);
-        }
-        count_launch();
-    }
-    return CM_OK;
-}
-
-int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_t nimg, int8_t* planes,
-                 int32_t* colterm, cudaStream_t s) {
-    const uint32_t P = g.out_h * g.out_w;
-    const uint32_t K = g.C * g.kh * g.kw;
-    if ((uint64_t)P * nimg == 0) return CM_OK;
-    cudaError_t e = cudaMemsetAsync(colterm, 0, (size_t)P * nimg * sizeof(int32_t), s);
-    if (e != cudaSuccess) return cuda_error(e, "memset colterm");
-    if (K == 0) return CM_OK;
-    const uint32_t block = std::min<uint32_t>(256, (P + 31) / 32 * 32);
-    const uint32_t gx = (P + block - 1) / block;
-    const uint32_t k_chunk = pick_k_chunk(K, (uint64_t)gx * nimg, cx->sm_count);
-    const uint32_t P_pad = pad_c(P);
-    for (uint32_t n0 = 0; n0 < nimg; n0 += 65535u) {
-        const uint32_t nb = std::min(65535u, nimg - n0);
-        const dim3 grid(gx, (K + k_chunk - 1) / k_chunk, nb);
-        {
-            ProfScope ps_(PK_SPLIT, s);
-            im2col_kn_kernel<<<grid, block, 0, s>>>(x + (uint64_t)n0 * g.C * g.H * g.W, g, P, K, P_pad, k_chunk,
-                                                   FastDiv(g.out_w), planes + (uint64_t)n0 * 2 * K * P_pad,
-                                                   colterm + (uint64_t)n0 * P);
+                                                  plane_off, batch_pitch, planes + (uint64_t)b0 * batch_pitch,
+                                                  colterm + (uint64_t)b0 * cols);
         }
         count_launch();
     }
@@ -830,7 +870,9 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;
     const uint64_t K_pad = pad_k(k);
     const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
-    const uint64_t b_bytes = ((uint64_t)b_batches * 2 * k * pad_c(m) + 255) & ~255ull;
+    // outputs of at most 64 columns use 64-column tiles (packed B, double-buffered accumulators)
+    const bool packed = m <= 64;
+    const uint64_t b_bytes = ((uint64_t)b_batches * k * (packed ? 128 : 2 * pad_c(m)) + 255) & ~255ull;
     const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
     const uint64_t ct_bytes = ((uint64_t)b_batches * m * 4 + 255) & ~255ull;
     void* scratch = nullptr;
@@ -841,9 +883,10 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     int32_t* rt = (int32_t*)(bp + b_bytes);
     int32_t* ct = (int32_t*)((uint8_t*)rt + rt_bytes);
     rc = split_rows(cx, a, a_batch_stride, k, n, k, a_batches, ap, rt, nullptr, s);
-    if (!rc) rc = split_kn(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s);
+    if (!rc) rc = split_kn(cx, b, b_batch_stride, m, m, k, b_batches, bp, ct, s, packed);
     if (!rc) {
         GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, 1, c_batch_stride, batch};
+        p.b_packed = packed ? 1u : 0u;
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);

@@ -43,6 +43,12 @@ struct GemmPlan {
     // output pixel (n, oh, ow), channel col -> out[n*out_bs + (oh*out_w + ow) + col*ldc],
     // rowterm[n*out_h*out_w + oh*out_w + ow]; K = kh*KR_pad.
     const ConvA* conv = nullptr;
+    // B planes packed for one 64-column tile: [b_batches][K][128] int8, each K row
+    // = [64 hi | 64 lo] (cols <= 64; C_pad unused).
+    uint32_t b_packed = 0;
+    // rows_per_img != 0 (plain mode): row = n*rows_per_img + p is written to
+    // out[n*out_bs + p + col*ldc] (conv output pixels of several images, NCHW)
+    uint32_t rows_per_img = 0;
 };
 
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude
@@ -63,16 +69,14 @@ int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
 // Split int16 matrix rows of B into N-major hi/lo planes + column terms:
 //   element (bt, k, c) = src[bt*src_bs + k*ld + c], c < cols, k < K;
 //   planes[((bt*2 + p)*K + k)*C_pad + c]; colterm[bt*cols + c] = 128*sum_k(x - 128).
+//   packed = true (cols <= 64): planes[bt*K*128 + k*128 + p*64 + c] instead.
 int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t cols, uint32_t K,
-             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s);
+             uint32_t nbt, int8_t* planes, int32_t* colterm, cudaStream_t s, bool packed = false);
 
-// im2col + split for ConvKernel: column p = oh*out_w + ow of image n, row k = (c, r, s),
-// N-major planes [n][2][K][P_pad]; out-of-range taps read 0.
+// Convolution geometry (input C x H x W, output out_h x out_w, kernel kh x kw).
 struct ConvGeom {
     uint32_t C, H, W, out_h, out_w, kh, kw, sh, sw, dh, dw, pt, pl;
 };
-int split_im2col(const Context* cx, const int16_t* x, const ConvGeom& g, uint32_t nimg, int8_t* planes,
-                 int32_t* colterm, cudaStream_t s);
 
 // Zero-fill out[z*out_bs + r*ldo + c] (the K == 0 case: an empty sum narrows to 0).
 int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, uint32_t cols, uint64_t ldo,

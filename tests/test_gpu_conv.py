@@ -59,6 +59,10 @@ REF_CASES = [
     (5, 64, 7, 7, 100, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),
     (1, 96, 20, 150, 24, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
     (2, 64, 40, 40, 16, 3, 3, 3, 8, 1, 1, 1, 1, 0, 0, 1, 0),
+    # explicit im2col (rows = pixels of several images): column dilation with more than
+    # 64 output channels, and narrow input channels with row tiles spanning images
+    (2, 5, 17, 19, 96, 3, 3, 1, 2, 2, 2, 2, 2, 2, 2, 1, 0),
+    (4, 3, 30, 30, 24, 5, 5, 2, 2, 1, 1, 2, 2, 2, 2, 1, 0),
 ]
 
 
