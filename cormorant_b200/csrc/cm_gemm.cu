@@ -35,6 +35,7 @@
 #include <algorithm>
 #include <mutex>
 
+#include "cm_async.cuh"
 #include "cm_gemm.cuh"
 
 namespace cm {
@@ -68,57 +69,6 @@ struct Cfg {
     static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
     static_assert(NBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ uint64_t gtimer() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-struct WaitCtl {
-    volatile int* abort;   // shared flag: some role gave up
-    int* status;           // device status word
-    uint64_t timeout_ns;
-};
-
-// Bounded wait: returns false (and raises the abort flag) on timeout or abort.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& w) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = gtimer();
-    for (uint32_t it = 1;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 63u) == 0) {
-            if (*w.abort) return false;
-            if (gtimer() - t0 > w.timeout_ns) {
-                atomicCAS(w.status, 0, CM_ETIMEOUT);
-                *w.abort = 1;
-                return false;
-            }
-        }
-    }
-}
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
                                             int c3) {
@@ -163,9 +113,7 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a, uint64_t b,
         : "memory");
 }
 
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
+
 
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");

@@ -18,7 +18,7 @@
 // wraps to 32 bits; NaN (LP2 of a wrapped negative sum) converts to 0.
 #include <algorithm>
 
-#include "cm_common.cuh"
+#include "cm_async.cuh"
 
 namespace cm {
 namespace {
@@ -528,6 +528,202 @@ __global__ void __launch_bounds__(256) pool_rows_kernel(const int16_t* __restric
     }
 }
 
+// Whole-plane kernel for compile-time geometries whose input plane fits in
+// shared memory (at most kPlaneMax bytes, rows of a multiple of 8 columns).
+// Persistent CTAs walk the planes.  Warp 0 is the producer: each plane arrives
+// as ONE bulk copy on the TMA engine (a long sequential DRAM stream) into one
+// of kPlaneBufs buffers, issued as soon as every consumer thread has released
+// that buffer (full / empty mbarriers, no CTA-wide barrier).  A buffer holds
+// the plane between rows of window-identity cells (PT above, the rows the last
+// output row reaches below), written once per CTA, so only the strips at the
+// plane's left and right edges check their halo columns.  The other threads
+// are (band of output rows, strip j of V = 8/SW outputs): per input row one
+// 16-byte shared-memory read of columns [8j, 8j+8) plus PL / HR halo columns and
+// the horizontal window reductions, kept in a ring over the PH tap rows so that
+// a row shared by consecutive output rows of the band is reduced once.
+constexpr uint32_t kPlaneMax = 28 * 1024;
+constexpr uint32_t kPlaneBufs = 2;
+
+template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PT, int PL>
+__global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y, PoolP p,
+                                                         uint64_t planes, uint32_t buf_bytes, uint32_t rows_bot,
+                                                         int* status, uint64_t timeout_ns) {
+    constexpr int V = 8 / SW;
+    constexpr int SPAN = (V - 1) * SW + (PW - 1) * DW + 1;   // input columns under the strip
+    constexpr int HR = SPAN - PL - 8 > 0 ? SPAN - PL - 8 : 0;
+    constexpr int ADV = SH / DH;                             // new tap rows per output row
+    constexpr int NEW = ADV < PH ? ADV : PH;
+    static_assert(PL <= 8 && HR <= 8 && V * SW == 8 && SH % DH == 0, "geometry");
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    __shared__ uint64_t full_b[kPlaneBufs], empty_b[kPlaneBufs];
+    __shared__ float inv_tab[PH * PW + 1];
+    __shared__ int abort_flag;
+    const int32_t pad = (TYPE == P_MAX) ? -32768 : 0;
+    const uint32_t in_w = p.in_w, in_h = p.in_h;
+    const uint32_t plane_elems = in_h * in_w, plane_bytes = plane_elems * 2;
+    const uint64_t out_elems = (uint64_t)p.out_h * p.out_w;
+    const uint32_t consumers = blockDim.x - 32;
+    // window identity in the frame rows of every buffer
+    for (uint32_t b = 0; b < kPlaneBufs; ++b) {
+        int16_t* bp = (int16_t*)(smem_raw + b * buf_bytes);
+        for (uint32_t i = threadIdx.x; i < (PT + rows_bot) * in_w; i += blockDim.x)
+            bp[i < PT * in_w ? i : plane_elems + i] = (int16_t)pad;
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+    if (threadIdx.x == 0) {
+        for (uint32_t b = 0; b < kPlaneBufs; ++b) {
+            mbar_init(smem_u32(&full_b[b]), 1);
+            mbar_init(smem_u32(&empty_b[b]), consumers);
+        }
+        abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (TYPE == P_AVG && threadIdx.x <= PH * PW) inv_tab[threadIdx.x] = threadIdx.x ? __fdiv_rn(1.0f, (float)threadIdx.x) : 0.0f;
+    __syncthreads();
+    const WaitCtl wc{&abort_flag, status, timeout_ns};
+
+    if (threadIdx.x < 32) {
+        const uint32_t lane = threadIdx.x;
+        uint32_t k = 0;
+        if (lane == 0) {
+            for (uint64_t plane = blockIdx.x; plane < planes; plane += gridDim.x, ++k) {
+                const uint32_t b = k % kPlaneBufs;
+                if (k >= kPlaneBufs && !mbar_wait(smem_u32(&empty_b[b]), ((k / kPlaneBufs) - 1) & 1u, wc)) break;
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                const uint32_t bar = smem_u32(&full_b[b]);
+                mbar_expect_tx(bar, plane_bytes);
+                bulk_g2s(smem_u32(smem_raw + b * buf_bytes) + PT * in_w * 2, x + plane * plane_elems, plane_bytes, bar);
+            }
+        }
+        if (lane == 0) {
+            if (abort_flag) {
+                // let the copies still in flight land before the CTA's shared memory is released
+                volatile int never = 0;
+                const WaitCtl drain{&never, status, timeout_ns};
+                for (uint32_t q = k > kPlaneBufs ? k - kPlaneBufs : 0u; q < k; ++q)
+                    mbar_wait(smem_u32(&full_b[q % kPlaneBufs]), (q / kPlaneBufs) & 1u, drain);
+            }
+        }
+        return;
+    }
+
+    // consumer thread = (band bnd of p.band_rows output rows, strip j)
+    const uint32_t ct = threadIdx.x - 32;
+    const uint32_t nstrips = p.strips;
+    const uint32_t j = ct % nstrips, bnd = ct / nstrips;
+    const uint32_t oh0 = bnd * p.band_rows, oh1 = min(p.out_h, oh0 + p.band_rows);
+    const bool first = j == 0, last = j == nstrips - 1;
+    const uint32_t ow0 = j * V;
+    const uint32_t nv = ow0 < p.out_w ? min((uint32_t)V, p.out_w - ow0) : 0u;
+    uint32_t vc[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+        vc[v] = PW;
+        if (TYPE == P_AVG && !p.cip) {
+            vc[v] = 0;
+#pragma unroll
+            for (int c2 = 0; c2 < PW; ++c2) {
+                const int32_t iw = (int32_t)((ow0 + v) * SW + c2 * DW) - PL;
+                vc[v] += (iw >= 0 && iw < (int32_t)in_w);
+            }
+        }
+    }
+
+    uint32_t k = 0;
+    for (uint64_t plane = blockIdx.x; plane < planes; plane += gridDim.x, ++k) {
+        const uint32_t b = k % kPlaneBufs;
+        if (!mbar_wait(smem_u32(&full_b[b]), (k / kPlaneBufs) & 1u, wc)) break;
+        // element (ih, iw) of the plane; rows -PT.. and in_h.. hold the identity
+        const int16_t* sp = (const int16_t*)(smem_raw + b * buf_bytes) + PT * in_w;
+        int16_t* yp = y + plane * out_elems;
+        // Horizontal reductions of input row ih for this strip's V outputs.
+        auto hrow = [&](int32_t ih, int32_t (&h)[V]) {
+            const int16_t* row = sp + ih * (int32_t)in_w + 8 * j;
+            int32_t e[SPAN];
+            const uint4 c = *(const uint4*)row;
+            const uint32_t w[4] = {c.x, c.y, c.z, c.w};
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                if (PL + q < SPAN) e[PL + q] = (int32_t)(int16_t)(w[q >> 1] >> (16 * (q & 1)));
+#pragma unroll
+            for (int q = 0; q < PL; ++q) e[q] = first ? pad : (int32_t)row[q - PL];
+#pragma unroll
+            for (int q = 0; q < HR; ++q) e[PL + 8 + q] = last ? pad : (int32_t)row[8 + q];
+#pragma unroll
+            for (int v = 0; v < V; ++v) {
+                int32_t a = (TYPE == P_MAX) ? -32768 : 0;
+#pragma unroll
+                for (int c2 = 0; c2 < PW; ++c2) {
+                    const int32_t x1 = e[v * SW + c2 * DW];
+                    if (TYPE == P_MAX) a = max(a, x1);
+                    else if (TYPE == P_AVG) a += x1;
+                    else if (TYPE == P_LP1) a += (x1 < 0 ? -x1 : x1);
+                    else a = (int32_t)((uint32_t)a + (uint32_t)(x1 * x1));
+                }
+                h[v] = a;
+            }
+        };
+        if (oh0 < oh1) {
+            int32_t ring[PH][V];
+#pragma unroll
+            for (int r = 0; r < PH; ++r) hrow((int32_t)(oh0 * SH) - PT + r * DH, ring[r]);
+            for (uint32_t oh = oh0; oh < oh1; ++oh) {
+                if (oh > oh0) {
+#pragma unroll
+                    for (int r = 0; r + ADV < PH; ++r)
+#pragma unroll
+                        for (int v = 0; v < V; ++v) ring[r][v] = ring[r + ADV][v];
+#pragma unroll
+                    for (int i = 0; i < NEW; ++i) hrow((int32_t)(oh * SH) - PT + (PH - NEW + i) * DH, ring[PH - NEW + i]);
+                }
+                uint32_t vr = PH;
+                if (TYPE == P_AVG && !p.cip) {
+                    vr = 0;
+#pragma unroll
+                    for (int r = 0; r < PH; ++r) {
+                        const int32_t ih = (int32_t)(oh * SH) - PT + r * DH;
+                        vr += (ih >= 0 && ih < (int32_t)in_h);
+                    }
+                }
+                int16_t out[V];
+#pragma unroll
+                for (int v = 0; v < V; ++v) {
+                    int32_t a = ring[0][v];
+#pragma unroll
+                    for (int r = 1; r < PH; ++r) {
+                        if (TYPE == P_MAX) a = max(a, ring[r][v]);
+                        else a = (int32_t)((uint32_t)a + (uint32_t)ring[r][v]);
+                    }
+                    if (TYPE == P_AVG) {
+                        // float(acc) * 2^-16 * (1/denom), floored at 2^-16: the power-of-two
+                        // scales are exact, so this is floor(rn(float(a * 256) * (1/denom)))
+                        const float f = __fmul_rn(__int2float_rn((int32_t)((uint32_t)a * 256u)),
+                                                  inv_tab[p.cip ? PH * PW : vr * vc[v]]);
+                        out[v] = narrow_acc(f >= 2147483648.0f ? 0x80000000u : (uint32_t)__float2int_rd(f));
+                    } else {
+                        uint32_t acc;
+                        if (TYPE == P_MAX) acc = (uint32_t)(a * 256);
+                        else if (TYPE == P_LP2) acc = (uint32_t)a;
+                        else acc = (uint32_t)a * 256u;
+                        out[v] = finalize<TYPE>(acc, 0);
+                    }
+                }
+                int16_t* dst = yp + (uint64_t)oh * p.out_w + ow0;
+                if (nv == (uint32_t)V && V == 4 && ((uintptr_t)dst & 7u) == 0) {
+                    *(uint2*)dst = make_uint2((uint32_t)(uint16_t)out[0] | ((uint32_t)(uint16_t)out[1 % V] << 16),
+                                              (uint32_t)(uint16_t)out[2 % V] | ((uint32_t)(uint16_t)out[3 % V] << 16));
+                } else {
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+                        if ((uint32_t)v < nv) dst[v] = out[v];
+                }
+            }
+        }
+        mbar_arrive(smem_u32(&empty_b[b]));   // this thread is done with the buffer
+    }
+}
+
 // Fallback when one output row's input rows do not fit in shared memory.
 template <int TYPE>
 __global__ void __launch_bounds__(256) pool_direct_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
@@ -641,6 +837,47 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
     }
     const bool small = p.in_h < (1u << 24) && p.in_w < (1u << 24) && p.out_h < (1u << 24) && p.pt < (1u << 24) &&
                        (uint64_t)p.sh * p.out_h < (1ull << 30) && win_rows < (1ull << 24) && pitch < (1u << 20);
+    // Whole-plane kernel: compile-time geometry, the plane fits a shared-memory
+    // buffer, 16-byte-aligned planes and rows, one 8-column chunk per strip.
+    const uint64_t plane_bytes = (uint64_t)p.in_h * p.in_w * 2;
+    if (spec >= 0 && (p.in_w & 7u) == 0 && ((uintptr_t)x & 15u) == 0 && p.in_w == 8 * p.strips && p.pt == p.pl &&
+        plane_bytes > 0 && plane_bytes <= kPlaneMax && p.out_h < (1u << 16) && p.strips <= 240 &&
+        (uint64_t)(p.out_h - 1) * p.sh < p.in_h + 64) {
+        // consumer threads = strips x bands of `band_rows` output rows (>= 2 rows a band
+        // for the row reuse), at most 480 of them next to the producer warp
+        uint32_t rows = 2;
+        while (p.strips * ((p.out_h + rows - 1) / rows) > 480) ++rows;
+        p.band_rows = rows;
+        const uint32_t threads = 32 + p.strips * ((p.out_h + rows - 1) / rows);
+        // buffer: the plane framed by PT rows above, the rows the last output row reaches
+        // below the plane, and 8 columns each side
+        const int64_t max_ih = (int64_t)(p.out_h - 1) * p.sh - p.pt + (int64_t)(p.ph - 1) * p.dh;
+        const uint32_t rows_bot = (uint32_t)std::max<int64_t>(0, max_ih - ((int64_t)p.in_h - 1));
+        const uint32_t buf_bytes = (uint32_t)(((uint64_t)(p.pt + p.in_h + rows_bot) * p.in_w * 2 + 127) & ~127ull);
+        const size_t smem = kPlaneBufs * (size_t)buf_bytes;
+        {
+            ProfScope ps_(PK_POOL, s);
+#define CM_PLANE_LAUNCH(PH_, PW_, SH_, SW_, DH_, DW_, PT_, PL_)                                          \
+    do {                                                                                                 \
+        auto k_ = pool_plane_kernel<TYPE, PH_, PW_, SH_, SW_, DH_, DW_, PT_, PL_>;                      \
+        cudaFuncSetAttribute(k_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);               \
+        int per_sm = 1;                                                                                  \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_, (int)threads, smem);                 \
+        const uint64_t grid = std::min<uint64_t>(planes, (uint64_t)cx->sm_count * std::max(per_sm, 1)); \
+        k_<<<(unsigned)grid, threads, smem, s>>>(x, y, p, planes, buf_bytes, rows_bot, cx->status, cx->timeout_ns); \
+    } while (0)
+            if (spec == 0)
+                CM_PLANE_LAUNCH(3, 3, 2, 2, 1, 1, 1, 1);
+            else if (spec == 1)
+                CM_PLANE_LAUNCH(3, 3, 2, 2, 2, 2, 1, 1);
+            else
+                CM_PLANE_LAUNCH(2, 2, 2, 2, 1, 1, 0, 0);
+#undef CM_PLANE_LAUNCH
+        }
+        count_launch();
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CM_OK : cuda_error(e, "pool plane kernel");
+    }
     // Row-streaming kernel: compile-time geometry, 16-byte-aligned rows, and exactly
     // one 8-column input chunk per strip of V outputs.
     if (spec >= 0 && (p.in_w & 7u) == 0 && ((uintptr_t)x & 15u) == 0 && p.in_w == 8 * p.strips &&

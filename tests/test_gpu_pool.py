@@ -101,9 +101,14 @@ def test_sweep_full_size(cm, port, sweep_input, case):
     run_case(cm, port, sweep_input, N, C, H, W, ph, pw, sh, sw, pt, pl, dh, dw, 0, t, lp, cip)
 
 
-# Layouts the row-streaming kernel takes (input width a multiple of 8, one 8-column chunk per
-# strip of outputs): several planes per warp, planes straddling warps, both dilations, 2x2.
+# Layouts of the compile-time geometries with input width a multiple of 8 (one 8-column chunk
+# per strip of outputs): planes of at most 32 KB go through the whole-plane kernel (several
+# planes per CTA), larger ones through the row-streaming kernel (planes straddling warps).
 ROWS = [
+    (1, 3, 160, 128, 3, 3, 2, 2, 1, 1, 1, 1, 0),
+    (1, 2, 150, 120, 3, 3, 2, 2, 1, 1, 2, 2, 0),
+    (1, 2, 144, 120, 2, 2, 2, 2, 0, 0, 1, 1, 0),
+    (5, 131, 12, 16, 3, 3, 2, 2, 1, 1, 1, 1, 0),
     (3, 5, 16, 16, 3, 3, 2, 2, 1, 1, 1, 1, 0),
     (2, 7, 40, 64, 3, 3, 2, 2, 1, 1, 1, 1, 0),
     (1, 9, 24, 112, 3, 3, 2, 2, 1, 1, 1, 1, 0),
