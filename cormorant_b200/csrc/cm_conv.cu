@@ -293,6 +293,109 @@ __global__ void __launch_bounds__(kIcRows) im2col_rows_kernel(const int16_t* __r
     if (live) rowterm[t] = (int32_t)((uint32_t)sum * 128u);
 }
 
+// im2col from a shared-memory window: block = up to 128 consecutive output
+// pixels of one output row (thread = pixel).  The block first stages the input
+// window those pixels read -- C channels x kh tap rows x the columns they span,
+// zero outside the image, followed by a run of zeros that the K padding points
+// at -- with loads coalesced along the row; then each thread walks its taps
+// through a per-slice offset table (one broadcast read and one window read per
+// tap, no bounds checks), packs pairs of words into hi/lo bytes with byte
+// permutes, and the K-major rows are written through the same staging as
+// im2col_rows_kernel.
+constexpr uint32_t kWinMax = 96 * 1024;   // window bytes
+
+__global__ void __launch_bounds__(kIcRows) im2col_win_kernel(const int16_t* __restrict__ x, ConvGeom g, uint32_t P,
+                                                             uint64_t rows, uint32_t K, uint32_t K_pad, uint32_t WC,
+                                                             FastDiv fd_wc, FastDiv fd_kh, int8_t* __restrict__ planes,
+                                                             int32_t* __restrict__ rowterm) {
+    extern __shared__ __align__(16) uint8_t smem_dyn[];
+    int8_t* stage0 = (int8_t*)smem_dyn;
+    int8_t* stage1 = stage0 + kIcRows * kIcPitch;
+    uint32_t* tab = (uint32_t*)(stage1 + kIcRows * kIcPitch);         // kIcSlice entries
+    int16_t* win = (int16_t*)(tab + kIcSlice);                         // [C][kh][WC], then zeros
+    const uint32_t ow0 = blockIdx.x * kIcRows, oh = blockIdx.y, n = blockIdx.z;
+    const uint32_t npix = min(kIcRows, g.out_w - ow0);
+    const uint32_t khw = g.kh * g.kw;
+    const uint32_t wrows = g.C * g.kh, wcells = wrows * WC, zeros = (kIcRows - 1) * g.sw + 1;
+    // stage the window: tap row r of channel c is input row oh*sh - pt + r*dh,
+    // window column q is input column ow0*sw - pl + q; 8 loads in flight per thread
+    {
+        const int32_t ih0 = (int32_t)(oh * g.sh) - (int32_t)g.pt, iw0 = (int32_t)(ow0 * g.sw) - (int32_t)g.pl;
+        const int16_t* xn = x + (uint64_t)n * g.C * g.H * g.W;
+        for (uint32_t i0 = 0; i0 < wcells; i0 += 8 * kIcRows) {
+            int16_t v[8];
+#pragma unroll
+            for (uint32_t m = 0; m < 8; ++m) {
+                const uint32_t i = i0 + m * kIcRows + threadIdx.x;
+                v[m] = 0;
+                if (i < wcells) {
+                    const uint32_t wr = fd_wc.div(i), q = i - wr * WC;
+                    const uint32_t c = fd_kh.div(wr), r = wr - c * g.kh;
+                    const int32_t ih = ih0 + (int32_t)(r * g.dh), iw = iw0 + (int32_t)q;
+                    if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
+                        v[m] = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
+                }
+            }
+#pragma unroll
+            for (uint32_t m = 0; m < 8; ++m) {
+                const uint32_t i = i0 + m * kIcRows + threadIdx.x;
+                if (i < wcells) win[i] = v[m];
+            }
+        }
+        for (uint32_t i = threadIdx.x; i < zeros; i += kIcRows) win[wcells + i] = 0;
+    }
+    const uint32_t t = threadIdx.x;
+    const bool live = t < npix;
+    const int16_t* wp = win + (live ? t : 0u) * g.sw;
+    const uint64_t row0 = (uint64_t)n * P + (uint64_t)oh * g.out_w + ow0;   // first K-major row of the block
+    const uint64_t plane = rows * K_pad;
+    uint32_t sum = 0;                                  // sum of the taps' words (padding reads 0)
+    for (uint32_t s0 = 0; s0 < K_pad; s0 += kIcSlice) {
+        const uint32_t sw = min(kIcSlice, K_pad - s0);
+        __syncthreads();   // window staged / previous slice copied out
+        for (uint32_t i = threadIdx.x; i < sw; i += kIcRows) {
+            const uint32_t k = s0 + i;
+            uint32_t off = wcells;                            // K padding: the zero run
+            if (k < K) {
+                const uint32_t c = k / khw, rs = k - c * khw;
+                const uint32_t r = rs / g.kw, sx = rs - r * g.kw;
+                off = (c * g.kh + r) * WC + sx * g.dw;
+            }
+            tab[i] = off;
+        }
+        __syncthreads();
+        for (uint32_t k0 = 0; k0 < sw; k0 += 16) {
+            uint32_t u[8];
+#pragma unroll
+            for (uint32_t jj = 0; jj < 8; ++jj) {
+                const int16_t v0 = wp[tab[k0 + 2 * jj]], v1 = wp[tab[k0 + 2 * jj + 1]];
+                sum += (uint32_t)(int32_t)v0 + (uint32_t)(int32_t)v1;
+                u[jj] = (uint32_t)(uint16_t)v0 | ((uint32_t)(uint16_t)v1 << 16);
+            }
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (uint32_t q = 0; q < 4; ++q) {
+                hw[q] = __byte_perm(u[2 * q], u[2 * q + 1], 0x7531);
+                lw[q] = __byte_perm(u[2 * q], u[2 * q + 1], 0x6420) ^ 0x80808080u;
+            }
+            const uint32_t o = t * kIcPitch + k0;
+            *(uint4*)(stage0 + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(stage1 + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        __syncthreads();
+        const uint32_t cpr = sw / 16, nchunks = npix * cpr;
+        for (uint32_t i = threadIdx.x; i < nchunks; i += kIcRows) {
+            const uint32_t rr = i / cpr, cc = i - rr * cpr;
+            const uint64_t go = (row0 + rr) * K_pad + s0 + 16 * cc;
+            const uint32_t so = rr * kIcPitch + 16 * cc;
+            *(uint4*)(planes + go) = *(const uint4*)(stage0 + so);
+            *(uint4*)(planes + plane + go) = *(const uint4*)(stage1 + so);
+        }
+    }
+    // rowterm = 128 * sum_k (x - 128) over the K real taps
+    if (live) rowterm[row0 + t] = (int32_t)((sum - 128u * K) * 128u);
+}
+
 uint32_t pow2_ceil(uint32_t v) {
     uint32_t p = 1;
     while (p < v && p < (1u << 30)) p <<= 1;
@@ -472,13 +575,33 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
     // natural tap order: kh = kw = 1, C = Cp = KR_pad = K
     rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, K, 1, 1, K, K, w_pitch, w_plane, w_bytes, wpl, ct, s);
     const ConvGeom geo{in_ch, in_h, in_w, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left};
+    // shared-memory window im2col when one block's window (C x kh rows x the columns
+    // 128 pixels span) fits; the direct gather otherwise
+    const uint64_t WC64 = (uint64_t)(std::min<uint32_t>(out_w, kIcRows) - 1) * stride_w + (uint64_t)(kw - 1) * dilation_w + 1;
+    const uint64_t win_bytes = ((uint64_t)in_ch * kh * WC64 + (uint64_t)(kIcRows - 1) * stride_w + 1) * 2;
+    const uint32_t WC = (uint32_t)std::min<uint64_t>(WC64, 1u << 20);
+    size_t win_smem = 0;
+    if (win_bytes <= kWinMax && out_h <= 65535 && batch <= 65535) {
+        win_smem = (size_t)2 * kIcRows * kIcPitch + kIcSlice * 4 + (size_t)win_bytes;
+        if (cudaFuncSetAttribute(im2col_win_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)win_smem) != cudaSuccess) {
+            cudaGetLastError();
+            win_smem = 0;
+        }
+    }
     for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
         const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
         const uint64_t rows = (uint64_t)nb * P;
         {
             ProfScope ps_(PK_SPLIT, s);
-            im2col_rows_kernel<<<(unsigned)((rows + kIcRows - 1) / kIcRows), kIcRows, 0, s>>>(x + n0 * (uint64_t)in_ch * in_h * in_w, geo,
-                                                                         (uint32_t)P, rows, K, K_pad, apl, rt);
+            const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
+            if (win_smem) {
+                const dim3 grid((out_w + kIcRows - 1) / kIcRows, out_h, nb);
+                im2col_win_kernel<<<grid, kIcRows, win_smem, s>>>(xc, geo, (uint32_t)P, rows, K, K_pad, WC, FastDiv(WC),
+                                                                  FastDiv(kh), apl, rt);
+            } else {
+                im2col_rows_kernel<<<(unsigned)((rows + kIcRows - 1) / kIcRows), kIcRows, 0, s>>>(xc, geo, (uint32_t)P, rows,
+                                                                                              K, K_pad, apl, rt);
+            }
         }
         count_launch();
         GemmPlan p{apl, (uint32_t)rows, 1, wpl, out_ch, 1, K, K_pad, M_pad, rt, ct,

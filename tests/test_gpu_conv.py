@@ -63,6 +63,10 @@ REF_CASES = [
     # 64 output channels, and narrow input channels with row tiles spanning images
     (2, 5, 17, 19, 96, 3, 3, 1, 2, 2, 2, 2, 2, 2, 2, 1, 0),
     (4, 3, 30, 30, 24, 5, 5, 2, 2, 1, 1, 2, 2, 2, 2, 1, 0),
+    # explicit im2col whose shared-memory window does not fit (direct gather), and one
+    # whose output rows are wider than a window block
+    (1, 600, 9, 300, 8, 3, 3, 1, 1, 1, 2, 1, 2, 1, 2, 1, 0),
+    (2, 3, 11, 300, 20, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
 ]
 
 
