@@ -133,6 +133,130 @@ __global__ void __launch_bounds__(256) conv_nhwc_split_kernel(const int16_t* __r
     if (qp < HWp) S[(uint64_t)n * HWp + qp] = sum;
 }
 
+// Four-pixel variant (H*W a multiple of 4, 8-byte aligned input): block = 256
+// consecutive input pixels of one image (64 quads), channels in tiles of 32.
+// Load: thread = (quad, channel), one 8-byte read of 4 pixels of a channel row.
+// Convert: thread = (quad, 8 channels), eight 8-byte shared reads, byte
+// permutes into 8-byte hi/lo runs per pixel written at the pixel's padded
+// position.  The padding frame is written by conv_nhwc_border_kernel.
+__global__ void __launch_bounds__(256) conv_nhwc_split4_kernel(const int16_t* __restrict__ x, NhwcGeom g,
+                                                               int8_t* __restrict__ planes, int32_t* __restrict__ S) {
+    __shared__ uint2 tile[kNhwcCh][64 + 1];                 // [channel][quad], 4 words per entry
+    const uint32_t n = blockIdx.y;
+    const uint32_t HW = g.H * g.W, nq = HW / 4;
+    const uint32_t q0 = blockIdx.x * 64;
+    const uint32_t HWp = g.Hp * g.Wp;
+    const uint64_t plane = (uint64_t)g.nimg * HWp * g.Cp;
+    const uint2* xq = (const uint2*)(x + (uint64_t)n * g.C * HW);
+    // load role
+    const uint32_t lq = threadIdx.x & 63u, lc = threadIdx.x >> 6;
+    // convert role: quad cq, channels 8*cg .. 8*cg + 7 of the tile
+    const uint32_t cq = threadIdx.x >> 2, cg = threadIdx.x & 3u;
+    const bool qlive = q0 + cq < nq;
+    // padded position of each pixel; input pixels no tap reads (beyond Hp / Wp) are skipped
+    uint64_t dst[4];
+    bool keep[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint32_t p = 4 * (q0 + cq) + j;
+        const uint32_t h = p / g.W, w = p - h * g.W;
+        keep[j] = qlive && h + g.pt < g.Hp && w + g.pl < g.Wp;
+        dst[j] = (((uint64_t)n * g.Hp + h + g.pt) * g.Wp + w + g.pl) * g.Cp;
+    }
+    int32_t sum[4] = {0, 0, 0, 0};
+    for (uint32_t c0 = 0; c0 < g.Cp; c0 += kNhwcCh) {
+        __syncthreads();
+#pragma unroll
+        for (uint32_t i = 0; i < kNhwcCh / 4; ++i) {
+            const uint32_t c = lc + 4 * i;
+            uint2 v = make_uint2(0, 0);
+            if (q0 + lq < nq && c0 + c < g.C) v = __ldg(xq + (uint64_t)(c0 + c) * nq + q0 + lq);
+            tile[c][lq] = v;
+        }
+        __syncthreads();
+        if (qlive && c0 + 8 * cg < g.Cp) {
+            uint2 v[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) v[c] = tile[8 * cg + c][cq];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                if (c0 + 8 * cg + c < g.C) {
+                    sum[0] += (int32_t)(int16_t)(v[c].x & 0xFFFFu);
+                    sum[1] += (int32_t)(int16_t)(v[c].x >> 16);
+                    sum[2] += (int32_t)(int16_t)(v[c].y & 0xFFFFu);
+                    sum[3] += (int32_t)(int16_t)(v[c].y >> 16);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                // word holding pixel j of channel c: v[c].x (j < 2) or v[c].y; halfword j & 1
+                const uint32_t hs = (j & 1) ? 3u : 1u, ls = (j & 1) ? 2u : 0u;   // byte of the hi / lo half
+                uint32_t hw[2], lw[2];
+#pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2) {
+                    const uint32_t a0 = j < 2 ? v[4 * h2].x : v[4 * h2].y, a1 = j < 2 ? v[4 * h2 + 1].x : v[4 * h2 + 1].y;
+                    const uint32_t a2 = j < 2 ? v[4 * h2 + 2].x : v[4 * h2 + 2].y, a3 = j < 2 ? v[4 * h2 + 3].x : v[4 * h2 + 3].y;
+                    const uint32_t h01 = __byte_perm(a0, a1, hs | ((hs + 4) << 4)), h23 = __byte_perm(a2, a3, hs | ((hs + 4) << 4));
+                    const uint32_t l01 = __byte_perm(a0, a1, ls | ((ls + 4) << 4)), l23 = __byte_perm(a2, a3, ls | ((ls + 4) << 4));
+                    hw[h2] = __byte_perm(h01, h23, 0x5410);
+                    lw[h2] = __byte_perm(l01, l23, 0x5410) ^ 0x80808080u;
+                }
+                if (keep[j]) {
+                    const uint64_t o = dst[j] + c0 + 8 * cg;
+                    *(uint2*)(planes + o) = make_uint2(hw[0], hw[1]);
+                    *(uint2*)(planes + plane + o) = make_uint2(lw[0], lw[1]);
+                }
+            }
+        }
+    }
+    // the four channel groups of a quad meet by shuffle; padded channels (x = 0) add nothing
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 1);
+        sum[j] += __shfl_xor_sync(0xFFFFFFFFu, sum[j], 2);
+    }
+    if (cg == 0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            if (keep[j]) S[dst[j] / g.Cp] = (int32_t)((uint32_t)sum[j] - 128u * g.C);
+    }
+}
+
+// Padding frame of the channels-last planes: every padded pixel outside the
+// input gets x = 0 in all channels (h = 0, l' = -128) and S = -128 * C.  Grid y =
+// image; the frame is enumerated directly: pt rows on top, the rows below the
+// input, then the left / right margins of the input rows.
+__global__ void __launch_bounds__(256) conv_nhwc_border_kernel(NhwcGeom g, int8_t* __restrict__ planes,
+                                                               int32_t* __restrict__ S) {
+    const uint32_t n = blockIdx.y;
+    const uint32_t HWp = g.Hp * g.Wp;
+    const uint64_t plane = (uint64_t)g.nimg * HWp * g.Cp;
+    const uint32_t cq = g.Cp / 16;
+    const uint32_t rows_in = min(g.H, g.Hp > g.pt ? g.Hp - g.pt : 0u);            // input rows inside the window
+    const uint32_t top = min(g.pt, g.Hp) * g.Wp;
+    const uint32_t bot = (g.Hp > g.pt + rows_in ? g.Hp - g.pt - rows_in : 0u) * g.Wp;
+    const uint32_t L = min(g.pl, g.Wp), R = g.Wp > g.pl + g.W ? g.Wp - g.pl - g.W : 0u;
+    const uint64_t nb = (uint64_t)top + bot + (uint64_t)rows_in * (L + R);
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nb * cq; t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t e = (uint32_t)(t / cq), run = (uint32_t)(t - (uint64_t)e * cq);
+        uint32_t hp, wp;
+        if (e < top) {
+            hp = e / g.Wp; wp = e - hp * g.Wp;
+        } else if (e < top + bot) {
+            const uint32_t f = e - top;
+            hp = g.pt + rows_in + f / g.Wp; wp = f % g.Wp;
+        } else {
+            const uint32_t f = e - top - bot, row = f / (L + R), col = f - row * (L + R);
+            hp = g.pt + row; wp = col < L ? col : g.pl + g.W + (col - L);
+        }
+        const uint64_t pix = (uint64_t)n * HWp + (uint64_t)hp * g.Wp + wp;
+        const uint64_t o = pix * g.Cp + 16 * run;
+        *(uint4*)(planes + o) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(planes + plane + o) = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+        if (run == 0) S[pix] = (int32_t)(0u - 128u * g.C);
+    }
+}
+
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
 __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
                                                            uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw,
@@ -522,14 +646,35 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
             const uint64_t tot = (uint64_t)nb * P;
             {
                 ProfScope ps_(PK_SPLIT, s);
-                const uint32_t gx = (uint32_t)(((uint64_t)ip.Hp * ip.Wp + kNhwcPix - 1) / kNhwcPix);
+                const uint64_t HW = (uint64_t)in_h * in_w;
+                const bool quads = HW % 4 == 0 && ((uintptr_t)x & 7u) == 0 && HW < (1ull << 31);
+                const uint32_t gx = quads ? (uint32_t)((HW / 4 + 63) / 64)
+                                          : (uint32_t)(((uint64_t)ip.Hp * ip.Wp + kNhwcPix - 1) / kNhwcPix);
                 for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                     const uint32_t bz = std::min(65535u, nb - b0);
                     // the plane stride stays that of the whole chunk (ng.nimg = nb)
-                    conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(
-                        x + (n0 + b0) * (uint64_t)in_ch * in_h * in_w, ng, apl + (uint64_t)b0 * img_plane,
-                        S + (uint64_t)b0 * ip.Hp * ip.Wp);
-                    count_launch();
+                    const int16_t* xb = x + (n0 + b0) * (uint64_t)in_ch * in_h * in_w;
+                    int8_t* pb = apl + (uint64_t)b0 * img_plane;
+                    int32_t* Sb = S + (uint64_t)b0 * ip.Hp * ip.Wp;
+                    if (quads) {
+                        conv_nhwc_split4_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+                        count_launch();
+                    } else {
+                        conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+                        count_launch();
+                    }
+                }
+                if (quads && (pad_top || pad_left || ip.Hp > pad_top + in_h || ip.Wp > pad_left + in_w)) {
+                    const uint64_t frame = (uint64_t)2 * (ip.Hp + ip.Wp) * (pad_top + pad_left + ip.Hp + ip.Wp) * (ip.Cp / 16);
+                    const uint32_t bx = (uint32_t)std::min<uint64_t>(8, (frame + 255) / 256);
+                    for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
+                        NhwcGeom gb = ng;
+                        const uint32_t bz = std::min(65535u, nb - b0);
+                        // images b0.. of the chunk: shift the planes / S bases, keep the chunk's plane stride
+                        conv_nhwc_border_kernel<<<dim3(bx, bz), 256, 0, s>>>(gb, apl + (uint64_t)b0 * img_plane,
+                                                                            S + (uint64_t)b0 * ip.Hp * ip.Wp);
+                        count_launch();
+                    }
                 }
                 conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h,
                                                                             stride_w, dilation_h, tot, rt);
