@@ -816,12 +816,13 @@ def main():
         which = "bf16_sustained" if elapsed_ms > 1500.0 else "bf16"
         peak = 2.0 * peaks[which]
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": profile_traffic("gemm_q88"),
+                "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"gemm_q88:{args.config}"),
                 "kernel": "gemm_q88_kernel",
                 "note": (f"int8 tensor ops (4 s8 MMAs per Q8.8 MAC, x2 ops per MAC) per second on rank 0; peak = "
                          f"2 x {peaks['source']} bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} "
                          f"{peaks[which]} TF/s (dense int8 rate is twice bf16 on B200); traffic = DRAM bytes of "
-                         f"one 4096^3 x 64 launch (profiles/)")}
+                         + ("one 4096^3 x 64 launch" if args.config == "matmul" else "one layer-1 3x3 conv GEMM launch")
+                         + " (ncu, profiles/)")}
     else:
         achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e9 if dms.value > 0 else 0.0
         peak = peaks["hbm_gbs"]
