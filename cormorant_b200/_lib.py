@@ -30,7 +30,9 @@ SIGNATURES: dict[str, tuple] = {
     "cm_last_error": (C.c_char_p, []),
     "cm_synchronize": (C.c_int, [_p]),
     "cm_launch_count": (C.c_uint64, []),
+    "cm_set_direct_limit": (C.c_uint64, [C.c_uint64]),
     "cm_version": (C.c_char_p, []),
+    "cm_selftest_wait_timeout": (C.c_int, [_u]),
     "cm_profile_begin": (C.c_int, []),
     "cm_profile_end": (C.c_int, []),
     "cm_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),

@@ -16,6 +16,9 @@ struct Context {
     int sm_count = 0;
     int* status = nullptr;          // device status word (0 = ok, else a CM_E* code)
     uint64_t timeout_ns = 2000000000ull;  // bounded device-side waits
+    // MatMul / standard conv with at most this many MACs run as one CUDA-core
+    // kernel (launch-bound sizes: no split pre-passes, no tensor-core pipeline)
+    uint64_t direct_max_macs = 1ull << 22;
 };
 
 Context* ctx();                      // nullptr before cm_init

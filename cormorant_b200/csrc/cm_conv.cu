@@ -59,6 +59,46 @@ __global__ void __launch_bounds__(256) conv_depthwise_kernel(const int16_t* __re
     }
 }
 
+// Launch-bound sizes: standard conv with G consecutive lanes per output word
+// (G a power of two <= 32) taking the kernel rows (c, r) = lane, lane + G, ...;
+// the int32 wrap sums meet by shuffle, bias << 8 is added, one narrowing
+// follows (ConvKernel.cpp:160-230).
+__global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restrict__ x, const int16_t* __restrict__ w,
+                                                          const int16_t* __restrict__ bias, int16_t* __restrict__ y,
+                                                          DwArgs a, uint64_t total, uint32_t G) {
+    const uint64_t ohw = (uint64_t)a.out_h * a.out_w;
+    const uint32_t khw = a.kh * a.kw, rows = a.C * a.kh;
+    const uint32_t g = threadIdx.x & (G - 1);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / G;
+    for (uint64_t t0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / G; t0 < (total + stride - 1) / stride * stride;
+         t0 += stride) {
+        const bool live = t0 < total;
+        const uint64_t t = live ? t0 : 0;
+        const uint64_t plane = t / ohw;            // n * M + m
+        const uint64_t p = t - plane * ohw;
+        const uint64_t n = plane / a.M, m = plane - n * a.M;
+        const uint32_t oh = (uint32_t)(p / a.out_w), ow = (uint32_t)(p - (uint64_t)oh * a.out_w);
+        uint32_t acc = 0;
+        for (uint32_t kr = g; live && kr < rows; kr += G) {
+            const uint32_t c = kr / a.kh, r = kr - c * a.kh;
+            const int64_t ih = (int64_t)oh * a.sh + (int64_t)r * a.dh - (int64_t)a.pt;
+            if (ih < 0 || ih >= (int64_t)a.H) continue;
+            const int16_t* xr = x + ((n * a.C + c) * (uint64_t)a.H + (uint64_t)ih) * a.W;
+            const int16_t* wr = w + (m * a.C + c) * (uint64_t)khw + (uint64_t)r * a.kw;
+            for (uint32_t s = 0; s < a.kw; ++s) {
+                const int64_t iw = (int64_t)ow * a.sw + (int64_t)s * a.dw - (int64_t)a.pl;
+                if (iw < 0 || iw >= (int64_t)a.W) continue;
+                acc += (uint32_t)((int32_t)__ldg(xr + iw) * (int32_t)__ldg(wr + s));
+            }
+        }
+        for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        if (live && g == 0) {
+            if (a.has_bias) acc += (uint32_t)((int32_t)bias[m] * 256);
+            y[t] = narrow_acc(acc);
+        }
+    }
+}
+
 // Empty reduction (in_ch * kh * kw == 0): every output is bias (or 0).
 __global__ void conv_bias_fill_kernel(const int16_t* __restrict__ bias, int16_t* __restrict__ y, uint32_t M,
                                       uint64_t ohw, uint64_t total, uint32_t has_bias) {
@@ -610,6 +650,18 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv bias fill");
     }
     if (!x || !weight) return set_error(CM_EINVAL, "cm_conv: null buffer");
+    if ((unsigned __int128)total * K64 <= cx->direct_max_macs) {
+        DwArgs a{in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
+                 has_bias ? 1u : 0u};
+        {
+            ProfScope ps_(PK_CONV_AUX, s);
+            const uint32_t G = direct_lanes(cx, total, (uint64_t)in_ch * kh);
+            conv_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total, G);
+        }
+        count_launch();
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv direct");
+    }
     if (K64 > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_conv: in_ch*kh*kw = %llu exceeds %u", (unsigned long long)K64, kMaxGemmK);
     const uint32_t K = (uint32_t)K64, K_pad = pad_k(K);
 

@@ -540,6 +540,34 @@ __global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict
         atomicAdd((unsigned int*)(colterm + (uint64_t)bt * cols + c8 + j), (uint32_t)sum[j] * 128u);
 }
 
+// Launch-bound sizes: G consecutive lanes per output word (G a power of two,
+// <= 32) take the k products q = lane, lane + G, ...; their int32 wrap sums
+// meet by shuffle (addition mod 2^32 is order-free, so the result is the exact
+// reference sum) and one narrowing follows (MatmulKernel.cpp:204-218).
+__global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b,
+                                                            int16_t* __restrict__ c, uint32_t n, uint32_t k, uint32_t m,
+                                                            uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, uint64_t total,
+                                                            uint32_t G) {
+    const uint64_t nm = (uint64_t)n * m;
+    const uint32_t g = threadIdx.x & (G - 1);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / G;
+    // whole warps iterate together (the shuffles below need every lane)
+    for (uint64_t t0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / G; t0 < (total + stride - 1) / stride * stride;
+         t0 += stride) {
+        const bool live = t0 < total;
+        const uint64_t t = live ? t0 : 0;
+        const uint64_t z = t / nm, r = t - z * nm;
+        const uint32_t i = (uint32_t)(r / m), j = (uint32_t)(r - (uint64_t)i * m);
+        const int16_t* ar = a + z * a_bs + (uint64_t)i * k;
+        const int16_t* bc = b + z * b_bs + j;
+        uint32_t acc = 0;
+        if (live)
+            for (uint32_t q = g; q < k; q += G) acc += (uint32_t)((int32_t)__ldg(ar + q) * (int32_t)__ldg(bc + (uint64_t)q * m));
+        for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+        if (live && g == 0) c[z * c_bs + (uint64_t)i * m + j] = narrow_acc(acc);
+    }
+}
+
 __global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
     const uint64_t rc = (uint64_t)rows * cols;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
@@ -666,6 +694,15 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
 }
 
 }  // namespace
+
+// Lanes per output for the direct kernels: enough threads to fill the GPU,
+// at most 32 and at most the reduction length.
+uint32_t direct_lanes(const Context* cx, uint64_t outputs, uint64_t red) {
+    uint32_t G = 1;
+    const uint64_t want = (uint64_t)cx->sm_count * 1024;
+    while (G < 32 && outputs * G < want && 2ull * G <= red) G *= 2;
+    return G;
+}
 
 int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     if (p.conv) return gemm_launch_conv(cx, p, s);
@@ -813,6 +850,19 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
         return CM_OK;
     }
     if (k == 0) return fill_zero(cx, c, batch, n, m, m, c_batch_stride, s);
+    const unsigned __int128 macs = (unsigned __int128)batch * n * m * k;
+    const uint64_t total = (uint64_t)batch * n * m;
+    if (macs <= cx->direct_max_macs) {
+        {
+            ProfScope ps_(PK_GEMM, s);
+            const uint32_t G = direct_lanes(cx, total, k);
+            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(a, b, c, n, k, m, a_batch_stride,
+                                                                               b_batch_stride, c_batch_stride, total, G);
+        }
+        count_launch();
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul direct");
+    }
     if (k > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_matmul: k = %u exceeds %u", k, kMaxGemmK);
     const uint32_t a_batches = a_batch_stride == 0 ? 1u : batch;
     const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;

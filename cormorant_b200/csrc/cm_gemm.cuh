@@ -78,6 +78,9 @@ struct ConvGeom {
     uint32_t C, H, W, out_h, out_w, kh, kw, sh, sw, dh, dw, pt, pl;
 };
 
+// Lanes per output word for the launch-bound CUDA-core kernels (power of two <= 32).
+uint32_t direct_lanes(const Context* cx, uint64_t outputs, uint64_t red);
+
 // Zero-fill out[z*out_bs + r*ldo + c] (the K == 0 case: an empty sum narrows to 0).
 int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, uint32_t cols, uint64_t ldo,
               uint64_t out_bs, cudaStream_t s);

@@ -166,6 +166,8 @@ int cm_init(const char* instance) {
     }
     const char* tmo = getenv("CM_TIMEOUT_MS");
     if (tmo && *tmo) c.timeout_ns = (uint64_t)strtoull(tmo, nullptr, 10) * 1000000ull;
+    const char* dm = getenv("CM_DIRECT_MAX_MACS");
+    if (dm && *dm) c.direct_max_macs = (uint64_t)strtoull(dm, nullptr, 10);
     g_ctx = c;
     g_ready = true;
     return CM_OK;
@@ -220,6 +222,13 @@ int cm_profile_read(const char* kernel, double* total_ms, uint64_t* launches) {
     if (total_ms) *total_ms = ms;
     if (launches) *launches = n;
     return CM_OK;
+}
+
+uint64_t cm_set_direct_limit(uint64_t macs) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const uint64_t old = g_ctx.direct_max_macs;
+    g_ctx.direct_max_macs = macs;
+    return old;
 }
 
 int cm_synchronize(cm_stream_t stream) {

@@ -79,7 +79,18 @@ const char* cm_strerror(int status);
 const char* cm_last_error(void);
 int cm_synchronize(cm_stream_t stream);       /* wait, then read + clear the device status word */
 uint64_t cm_launch_count(void);               /* kernels launched by this library so far */
+/* MatMul / standard Conv calls of at most `macs` multiply-accumulates run as one
+ * CUDA-core kernel instead of the split + tensor-core pipeline (default 2^22, or
+ * the CM_DIRECT_MAX_MACS environment variable at cm_init; 0 = never).  Returns the
+ * previous limit.  No reference counterpart; both paths are bit-exact. */
+uint64_t cm_set_direct_limit(uint64_t macs);
 const char* cm_version(void);
+
+/* ---- failure-path self test (no reference counterpart) ------------------------
+ * Launches one kernel whose bounded mbarrier wait can never be satisfied; after
+ * timeout_ms (1..10000) it records CM_ETIMEOUT and returns.  Returns CM_ETIMEOUT
+ * (the status word is read and cleared), and the library stays usable. */
+int cm_selftest_wait_timeout(unsigned timeout_ms);
 
 /* ---- device timing of this library's launches (no reference counterpart) --
  * Between cm_profile_begin and cm_profile_end every kernel launch is bracketed

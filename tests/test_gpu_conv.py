@@ -12,7 +12,7 @@ import pytest
 
 from tests._util import assert_same, dev, empty, host, rand16
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("mac_path")]
 
 
 def osz(n, k, s, d, p0, p1):
@@ -111,6 +111,7 @@ def test_empty_reduction_writes_bias(cm, port):
     assert_same(host(y), np.tile(np.repeat(b, 4), 2), "in_ch = 0")
 
 
+@pytest.mark.big
 def test_resnet_conv1_batch8_sampled(cm, port):
     """ResNet-18 stem at batch 8 (chunked im2col), checked plane by plane for a sample of (n, m)."""
     N, C, H, W, M = 8, 3, 224, 224, 64

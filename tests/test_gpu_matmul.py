@@ -12,7 +12,7 @@ import pytest
 
 from tests._util import assert_same, dev, empty, host, rand16
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("mac_path")]
 
 # (n, k, m, batch) -- TILE_N=4, TILE_K=256, TILE_M=16 in the reference; 128-tiles here
 SHAPES = [(1, 1, 1, 1), (4, 256, 16, 1), (8, 256, 16, 1), (4, 512, 16, 1), (4, 256, 32, 1), (6, 256, 16, 1),
@@ -107,6 +107,7 @@ SWEEP = [(256, 256, 256, 64), (1024, 1024, 1024, 64), (4096, 4096, 4096, 64), (8
 
 
 @pytest.mark.parametrize("n,k,m,batch", SWEEP)
+@pytest.mark.big
 def test_sweep_shapes(cm, port, n, k, m, batch):
     """BASELINE MatMul sweep: raw int16 uniform [-1024, 1024), seeded; sampled rows when large."""
     import torch
