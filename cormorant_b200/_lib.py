@@ -44,6 +44,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_matmul_noalloc": (C.c_int, [_p, _p, _p] + [_u] * 7 + [_p]),
     "cm_conv": (C.c_int, [_p, _p, _p, _p] + [_u] * 17),
     "cm_conv_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 17 + [_p]),
+    "cm_conv_fused": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p]),
+    "cm_conv_fused_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p, _p]),
     "cm_pool": (C.c_int, [_p, _p] + [_u] * 17),
     "cm_pool_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
     "cm_buf_alloc": (_p, [_u]),

@@ -59,13 +59,30 @@ __global__ void __launch_bounds__(256) conv_depthwise_kernel(const int16_t* __re
     }
 }
 
+// Fused elementwise epilogue (cm_conv_fused): bit 1 adds the residual word at the
+// same index with saturation (VectorOP ADD), then bit 0 applies ReLU (VectorOP
+// RELU; VectorOP.cpp:8-35, :106-111).
+__device__ __forceinline__ int16_t epilogue_word(int16_t v, uint32_t epi, const int16_t* resid, uint64_t i) {
+    int32_t r = v;
+    if (epi & 2u) r = sat16(r + (int32_t)resid[i]);
+    if (epi & 1u) r = max(r, 0);
+    return (int16_t)r;
+}
+
+__global__ void __launch_bounds__(256) conv_epilogue_kernel(int16_t* __restrict__ y, const int16_t* __restrict__ resid,
+                                                            uint64_t total, uint32_t epi) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
+        y[t] = epilogue_word(y[t], epi, resid, t);
+}
+
 // Launch-bound sizes: standard conv with G consecutive lanes per output word
 // (G a power of two <= 32) taking the kernel rows (c, r) = lane, lane + G, ...;
 // the int32 wrap sums meet by shuffle, bias << 8 is added, one narrowing
 // follows (ConvKernel.cpp:160-230).
 __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restrict__ x, const int16_t* __restrict__ w,
                                                           const int16_t* __restrict__ bias, int16_t* __restrict__ y,
-                                                          DwArgs a, uint64_t total, uint32_t G) {
+                                                          DwArgs a, uint64_t total, uint32_t G, uint32_t epi,
+                                                          const int16_t* __restrict__ resid) {
     const uint64_t ohw = (uint64_t)a.out_h * a.out_w;
     const uint32_t khw = a.kh * a.kw, rows = a.C * a.kh;
     const uint32_t g = threadIdx.x & (G - 1);
@@ -94,7 +111,7 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
         for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
         if (live && g == 0) {
             if (a.has_bias) acc += (uint32_t)((int32_t)bias[m] * 256);
-            y[t] = narrow_acc(acc);
+            y[t] = epilogue_word(narrow_acc(acc), epi, resid, t);
         }
     }
 }
@@ -609,11 +626,13 @@ bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint
 
 using namespace cm;
 
-extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
-                             unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h,
-                             unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
-                             unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
-                             unsigned has_bias, unsigned is_depthwise, cm_stream_t stream) {
+namespace {
+
+int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch, unsigned in_ch,
+              unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
+              unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+              unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epi, const int16_t* resid,
+              cm_stream_t stream) {
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
@@ -633,8 +652,9 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         {
             ProfScope ps_(PK_CONV_AUX, s);
             conv_depthwise_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total);
+            if (epi) conv_epilogue_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(y, resid, total, epi);
         }
-        count_launch();
+        count_launch(epi ? 2 : 1);
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv depthwise");
     }
@@ -644,8 +664,9 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         {
             ProfScope ps_(PK_CONV_AUX, s);
             conv_bias_fill_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(bias, y, out_ch, P, total, has_bias ? 1u : 0u);
+            if (epi) conv_epilogue_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(y, resid, total, epi);
         }
-        count_launch();
+        count_launch(epi ? 2 : 1);
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv bias fill");
     }
@@ -656,7 +677,7 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
         {
             ProfScope ps_(PK_CONV_AUX, s);
             const uint32_t G = direct_lanes(cx, total, (uint64_t)in_ch * kh);
-            conv_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total, G);
+            conv_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total, G, epi, resid);
         }
         count_launch();
         cudaError_t e = cudaGetLastError();
@@ -738,6 +759,8 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
                        y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
+            p.epi = epi;
+            p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -805,12 +828,48 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
                    y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
         p.b_packed = packed ? 1u : 0u;
         p.rows_per_img = (uint32_t)P;
+        p.epi = epi;
+        p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);
     if (rc) return rc;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv");
+}
+
+}  // namespace
+
+extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
+                             unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h,
+                             unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
+                             unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
+                             unsigned has_bias, unsigned is_depthwise, cm_stream_t stream) {
+    return conv_impl(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                     dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, 0u, nullptr, stream);
+}
+
+extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+                                   unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                                   unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                                   unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                                   unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
+                                   const int16_t* resid, cm_stream_t stream) {
+    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_fused: epilogue must be 0..3");
+    if ((epilogue & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv_fused: residual buffer is null");
+    return conv_impl(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                     dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue, resid, stream);
+}
+
+extern "C" int cm_conv_fused(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
+                             unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h,
+                             unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
+                             unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
+                             unsigned has_bias, unsigned is_depthwise, unsigned epilogue, const int16_t* resid) {
+    int rc = cm_conv_fused_async(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
+                                 stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue,
+                                 resid, nullptr);
+    return rc ? rc : finish_sync(nullptr);
 }
 
 extern "C" int cm_conv(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,

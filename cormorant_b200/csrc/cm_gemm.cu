@@ -151,6 +151,10 @@ struct GemmArgs {
     // rows_per_img != 0: row = n*rows_per_img + p -> out[n*out_bs + p + col*ldc]
     uint32_t rows_per_img;
     uint32_t ksteps;          // 32-deep MMA steps covering K (conv: covering one kernel row's KR bytes)
+    // fused elementwise epilogue on the narrowed word v (bit 1: v = sat16(v + resid at the
+    // output's index), then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
+    uint32_t epi;
+    const int16_t* resid;
 };
 
 struct Tile {
@@ -385,6 +389,27 @@ __global__ void __launch_bounds__(320, 1)
             if (lane == 0) mbar_arrive(smem_u32(&acce_b[buf]));   // buffer free for the next tile
             if (!valid) continue;
             int16_t* orow = g.out + o_off;
+            if (g.epi) {
+                const int16_t* rrow = g.resid + o_off;
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+                    const uint32_t col0 = tc.n0 + cbase + c0;
+                    if (col0 >= g.cols) break;
+#pragma unroll
+                    for (int k = 0; k < 32; k += 2) {
+                        int32_t v0 = (int16_t)(pk[(c0 + k) / 2] & 0xFFFFu), v1 = (int16_t)(pk[(c0 + k) / 2] >> 16);
+                        if (g.epi & 2u) {
+                            if (col0 + k < g.cols) v0 = sat16(v0 + (int32_t)rrow[(uint64_t)(col0 + k) * g.ldc]);
+                            if (col0 + k + 1 < g.cols) v1 = sat16(v1 + (int32_t)rrow[(uint64_t)(col0 + k + 1) * g.ldc]);
+                        }
+                        if (g.epi & 1u) {
+                            v0 = max(v0, 0);
+                            v1 = max(v1, 0);
+                        }
+                        pk[(c0 + k) / 2] = (uint32_t)(uint16_t)v0 | ((uint32_t)(uint16_t)v1 << 16);
+                    }
+                }
+            }
 #pragma unroll
             for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
                 const uint32_t col0 = tc.n0 + cbase + c0;
@@ -725,6 +750,7 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.conv = 0;
     g.rows_per_img = p.rows_per_img;
     g.ksteps = (p.K + 31) / 32;
+    g.epi = p.epi; g.resid = p.resid;
     return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
 }
 
@@ -753,6 +779,7 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.nimg = c.nimg; g.out_h = c.out_h; g.out_w = c.out_w; g.sw = c.sw; g.sh = c.sh; g.dh = c.dh;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
     g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
+    g.epi = p.epi; g.resid = p.resid;
     return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
 }
 

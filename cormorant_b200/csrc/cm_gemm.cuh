@@ -49,6 +49,10 @@ struct GemmPlan {
     // rows_per_img != 0 (plain mode): row = n*rows_per_img + p is written to
     // out[n*out_bs + p + col*ldc] (conv output pixels of several images, NCHW)
     uint32_t rows_per_img = 0;
+    // fused epilogue: bit 1 = add `resid` (same indexing as out, saturating), then
+    // bit 0 = ReLU -- VectorOP ADD / RELU applied to the narrowed words
+    uint32_t epi = 0;
+    const int16_t* resid = nullptr;
 };
 
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude

@@ -88,6 +88,24 @@ def ConvKernel(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_
     check(L.cm_conv(*args) if stream is None else L.cm_conv_async(*args, _stream(stream)))
 
 
+EPI_NONE, EPI_RELU, EPI_ADD, EPI_ADD_RELU = 0, 1, 2, 3
+
+
+def ConvKernelFused(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1,
+                    stride_w=1, dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=None, is_depthwise=0,
+                    epilogue=EPI_RELU, resid=None, stream=None) -> None:
+    """ConvKernel followed by VectorOP ADD (with `resid`) and/or RELU, fused into the conv's
+    epilogue (cm_conv_fused).  Not a reference kernel: the word-for-word result of the
+    reference call sequence Conv -> [Add(resid)] -> [Relu]."""
+    if has_bias is None:
+        has_bias = int(bias is not None)
+    L = lib()
+    args = (_addr(x), _addr(weight), _addr(bias), _addr(y), batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+            stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, int(has_bias), int(is_depthwise),
+            int(epilogue), _addr(resid))
+    check(L.cm_conv_fused(*args) if stream is None else L.cm_conv_fused_async(*args, _stream(stream)))
+
+
 def PoolingKernel(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
                   pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, lp_order=2, count_include_pad=0,
                   stream=None) -> None:

@@ -188,16 +188,86 @@ def make_input(net: Net, seed: int = 7) -> np.ndarray:
     return q88_round(rng.uniform(0.0, 1.0, size=net.buffers[net.input]))
 
 
+def _inputs(node) -> list:
+    kind = node[0]
+    if kind == "conv":
+        names = [node[1], node[2], node[3]] + ([node[7]] if len(node) > 7 else [])
+    elif kind in ("vectorop", "matmul"):
+        names = [node[1], node[2]]
+    else:
+        names = [node[1]]
+    return [n for n in names if n is not None]
+
+
+def fuse(net: Net, residual: bool = False) -> Net:
+    """The call list with Conv -> Relu chains (and, with residual=True, Conv -> Add and
+    Conv -> Add -> Relu chains) folded into one conv call with a fused epilogue
+    (cm_conv_fused): the same words, without writing and re-reading the intermediate
+    tensors.  A chain is folded only when each intermediate result has no other reader
+    (and is not the network output).  The residual form reads the other Add operand in
+    the GEMM epilogue one 64-byte channel segment at a time, which on B200 costs more
+    than the separate Add pass it saves for the ResNet-18 shapes, so it is off by default."""
+    R = net.resolve
+    reads: dict = {}
+    for node in net.nodes:
+        for name in _inputs(node):
+            reads[R(name)] = reads.get(R(name), 0) + 1
+    reads[R(net.output)] = reads.get(R(net.output), 0) + 1
+
+    def whole(node, words):                  # a full-tensor elementwise call (no broadcast)
+        return node[0] == "vectorop" and node[4][0] == words and node[4][2:] == (1, 0, 0)
+
+    def relu_of(node, y):
+        return whole(node, net.buffers[y]) and node[4][1] == OP_RELU and R(node[1]) == y
+
+    def add_with(node, y):
+        return (whole(node, net.buffers[y]) and node[4][1] == OP_ADD and node[2] is not None
+                and y in (R(node[1]), R(node[2])) and R(node[1]) != R(node[2]))
+
+    out, nodes, i = [], net.nodes, 0
+    while i < len(nodes):
+        node = nodes[i]
+        if node[0] == "conv" and len(node) == 6 and i + 1 < len(nodes) and reads.get(R(node[4]), 0) == 1:
+            _, x, wn, bn, y, args = node
+            y, nxt = R(y), nodes[i + 1]
+            if relu_of(nxt, y):
+                out.append(("conv", x, wn, bn, nxt[3], args, 1, None))
+                i += 2
+                continue
+            if residual and add_with(nxt, y):
+                other = nxt[2] if R(nxt[1]) == y else nxt[1]
+                c = R(nxt[3])
+                if i + 2 < len(nodes) and reads.get(c, 0) == 1 and relu_of(nodes[i + 2], c):
+                    out.append(("conv", x, wn, bn, nodes[i + 2][3], args, 3, other))
+                    i += 3
+                else:
+                    out.append(("conv", x, wn, bn, nxt[3], args, 2, other))
+                    i += 2
+                continue
+        out.append(node)
+        i += 1
+    used = {R(n) for node in out for n in _inputs(node)} | {R(node[4] if node[0] == "conv" else node[3] if node[0] in ("vectorop", "matmul") else node[2]) for node in out}
+    used |= {R(net.input), R(net.output)}
+    fused = Net(net.name + "+fused", net.batch, net.input, net.output,
+                buffers={k: v for k, v in net.buffers.items() if k in used}, consts=dict(net.consts), nodes=out,
+                aliases=dict(net.aliases), macs_per_image=net.macs_per_image)
+    return fused
+
+
 def execute(net: Net, backend, bufs: dict) -> None:
     """Run every node of `net` on `backend` over `bufs` (name -> backend buffer).
 
     backend offers vectorop(a, b, c, size, op, outer, a_inc, b_inc),
-    matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars)
-    and pool(x, y, *17 scalars)."""
+    matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars),
+    pool(x, y, *17 scalars) and, for fused call lists, conv_fused(x, w, bias, y, *17
+    scalars, epilogue, resid)."""
     R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
     for node in net.nodes:
         kind = node[0]
-        if kind == "conv":
+        if kind == "conv" and len(node) > 6:
+            _, x, wn, bn, y, args, epi, resid = node
+            backend.conv_fused(R(x), R(wn), R(bn), R(y), *args, epi, R(resid))
+        elif kind == "conv":
             _, x, wn, bn, y, args = node
             backend.conv(R(x), R(wn), R(bn), R(y), *args)
         elif kind == "vectorop":
@@ -229,6 +299,10 @@ class GpuBackend:
 
     def conv(self, x, w, bias, y, *args):
         self.k.ConvKernel(x, w, bias, y, *args, stream=self.stream)
+
+    def conv_fused(self, x, w, bias, y, *args):
+        *geo, epi, resid = args
+        self.k.ConvKernelFused(x, w, bias, y, *geo, epilogue=epi, resid=resid, stream=self.stream)
 
     def pool(self, x, y, *args):
         self.k.PoolingKernel(x, y, *args, stream=self.stream)

@@ -159,6 +159,26 @@ int cm_conv_async(const int16_t* x, const int16_t* weight, const int16_t* bias, 
                   unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
                   cm_stream_t stream);
 
+/* ---- Conv with a fused elementwise epilogue (no reference counterpart) -------
+ * The same convolution as cm_conv, then on every narrowed output word v:
+ *   epilogue bit 1: v = sat16(v + resid[i])   (VectorOP ADD, resid laid out like y)
+ *   epilogue bit 0: v = max(v, 0)             (VectorOP RELU)
+ * 0 = plain cm_conv, 1 = Conv+Relu, 2 = Conv+Add, 3 = Conv+Add+Relu -- the result equals
+ * the reference's ConvKernel followed by those VectorOP calls, word for word, without
+ * writing and re-reading the intermediate tensors. */
+int cm_conv_fused(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+                  unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                  unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                  unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                  unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
+                  const int16_t* resid);
+int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+                        unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                        unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                        unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                        unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
+                        const int16_t* resid, cm_stream_t stream);
+
 /* ---- PoolingKernel -------------------------------------------------------------
  * pool_type CM_POOL_MAX / AVG / LP (any value >= 2 is LP); lp_order 1 = sum|x|,
  * any other value = sqrt(sum x^2); count_include_pad selects the AVG divisor. */

@@ -126,3 +126,36 @@ def test_resnet_conv1_batch8_sampled(cm, port):
     want = port.conv_planes(x, w, bias, C, H, W, M, 112, 112, 7, 7, 2, 2, 1, 1, 3, 3, 1, 0, nidx, midx)
     got = host(y).reshape(N, M, -1)[nidx, midx]
     assert_same(got, want, "stem sampled planes")
+
+
+FUSED = [  # implicit GEMM (several layouts), explicit im2col (stem-like), 1x1 output plane
+    (2, 64, 14, 14, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 64, 15, 15, 128, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 1, 0),
+    (2, 3, 30, 30, 24, 7, 7, 2, 2, 1, 1, 3, 3, 3, 3, 1, 0),
+    (3, 32, 3, 3, 70, 3, 3, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+    (2, 4, 8, 8, 4, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 1),     # depthwise: epilogue pass
+]
+
+
+@pytest.mark.parametrize("case", FUSED)
+@pytest.mark.parametrize("epi", [1, 2, 3])
+def test_conv_fused_epilogue(cm, port, case, epi):
+    """cm_conv_fused == ConvKernel then VectorOP ADD (residual) and/or RELU, word for word."""
+    from cormorant_b200 import kernels
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    rng = np.random.default_rng(sum(case) + epi)
+    x = rand16(rng, N * C * H * W, -2048, 2048)
+    w = rand16(rng, M * (1 if dwm else C) * kh * kw, -512, 512)
+    bias = rand16(rng, M, -2048, 2048)
+    r = rand16(rng, N * M * oh * ow)
+    y = empty(N * M * oh * ow)
+    kernels.ConvKernelFused(dev(x), dev(w), dev(bias), y, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb,
+                            dwm, epilogue=epi, resid=dev(r))
+    size = N * M * oh * ow
+    want = port.conv(x, w, bias, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)[:size]
+    if epi & 2:
+        want = port.vectorop(want, r, size, 0, 1, 0, 0)[:size]
+    if epi & 1:
+        want = port.vectorop(want, None, size, 4, 1, 0, 0)[:size]
+    assert_same(host(y), want, f"fused {case} epi {epi}")

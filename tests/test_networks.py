@@ -25,6 +25,16 @@ class OracleBackend:
     def conv(self, x, w, bias, y, *args):
         y[:] = self.chk.conv(x, w, bias, *args)[: y.size]
 
+    def conv_fused(self, x, w, bias, y, *args):
+        """The reference call sequence Conv -> [Add(resid)] -> [Relu] on the checker."""
+        *geo, epi, resid = args
+        t = self.chk.conv(x, w, bias, *geo)[: y.size]
+        if epi & 2:
+            t = self.chk.vectorop(t, resid, y.size, networks.OP_ADD, 1, 0, 0)[: y.size]
+        if epi & 1:
+            t = self.chk.vectorop(t, None, y.size, networks.OP_RELU, 1, 0, 0)[: y.size]
+        y[:] = t
+
     def pool(self, x, y, *args):
         y[:] = self.chk.pool(x, *args)[: y.size]
 
@@ -91,3 +101,65 @@ def test_resnet18_batch256_sampled_images(cm, port):
     got = np.concatenate([logits[0], logits[255]])
     assert_same(got, want[small.resolve(small.output)], "resnet18 logits of images 0 and 255")
     assert len(np.unique(got)) > 10                       # not a degenerate (saturated) network
+
+
+def test_fusion_pass_shapes():
+    """Conv -> Relu (and with residual=True Conv -> Add -> Relu) chains fold; nothing else changes."""
+    rn = networks.fuse(networks.resnet18(batch=1), residual=True)
+    kinds = [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else None) for n in rn.nodes]
+    assert kinds.count(("conv", 1)) == 9 and kinds.count(("conv", 3)) == 8 and kinds.count(("conv", None)) == 3
+    assert kinds.count(("vectorop", None)) == 1          # the classifier's bias add stays
+    rn = networks.fuse(networks.resnet18(batch=1))
+    kinds = [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else None) for n in rn.nodes]
+    assert kinds.count(("conv", 1)) == 9 and kinds.count(("conv", None)) == 11 and kinds.count(("vectorop", None)) == 17
+    ln = networks.fuse(networks.lenet5())
+    assert [n[0] for n in ln.nodes].count("vectorop") == 5 and all(len(n) == 8 for n in ln.nodes if n[0] == "conv")
+
+
+def test_fused_call_list_equals_reference_sequence_on_cpu(port):
+    """The folded LeNet call list, replayed on the checker with the reference's call
+    sequence for each fused conv, gives the same logits as the original list."""
+    net = networks.lenet5()
+    fn = networks.fuse(net)
+    x = networks.make_input(net)
+    a, b = cpu_buffers(net, x), cpu_buffers(fn, x)
+    networks.execute(net, OracleBackend(port), a)
+    networks.execute(fn, OracleBackend(port), b)
+    assert_same(b[fn.resolve(fn.output)], a[net.resolve(net.output)], "fused lenet logits")
+
+
+@pytest.mark.gpu
+def test_lenet_fused_gpu_every_activation(cm, port):
+    net = networks.fuse(networks.lenet5())
+    x = networks.make_input(net)
+    want = cpu_buffers(net, x)
+    networks.execute(net, OracleBackend(port), want)
+    for limit in (0, 1 << 26):                  # tensor-core and CUDA-core conv paths
+        old = cm.lib().cm_set_direct_limit(limit)
+        try:
+            bufs = networks.gpu_buffers(net, x)
+            networks.execute(net, networks.GpuBackend(), bufs)
+            import torch
+            torch.cuda.synchronize()
+        finally:
+            cm.lib().cm_set_direct_limit(old)
+        for name in net.buffers:
+            assert_same(bufs[name].cpu().numpy(), want[name], f"fused lenet buffer {name} (direct limit {limit})")
+
+
+@pytest.mark.gpu
+def test_resnet18_fused_batch256_sampled_images(cm, port):
+    import torch
+    net = networks.fuse(networks.resnet18(batch=256), residual=True)
+    x = networks.make_input(net)
+    bufs = networks.gpu_buffers(net, x)
+    networks.execute(net, networks.GpuBackend(), bufs)
+    torch.cuda.synchronize()
+    logits = bufs[net.resolve(net.output)].cpu().numpy().reshape(256, -1)
+    small = networks.resnet18(batch=2)                    # the unfused reference call list
+    per = 3 * 224 * 224
+    xs = np.concatenate([x[:per], x[255 * per:256 * per]])
+    want = cpu_buffers(small, xs)
+    networks.execute(small, OracleBackend(port), want)
+    got = np.concatenate([logits[0], logits[255]])
+    assert_same(got, want[small.resolve(small.output)], "fused resnet18 logits of images 0 and 255")
