@@ -19,6 +19,8 @@ struct Context {
     // MatMul / standard conv with at most this many MACs run as one CUDA-core
     // kernel (launch-bound sizes: no split pre-passes, no tensor-core pipeline)
     uint64_t direct_max_macs = 1ull << 22;
+    // 128-column GEMM tiles run on CTA pairs (tcgen05 cta_group::2); CM_GEMM_PAIRS=0 turns it off
+    int gemm_pairs = 1;
 };
 
 Context* ctx();                      // nullptr before cm_init

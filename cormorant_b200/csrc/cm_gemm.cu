@@ -54,17 +54,19 @@ constexpr uint32_t TMEM_COLS = 512;
 // at most 64 columns): B is stored packed, each K row = [64 hi | 64 lo] bytes, so
 // one 128-byte atom is the whole [Bh | Bl] operand (16 KB); the four 64-column
 // accumulators take 256 TMEM columns and are double-buffered.
-template <int TBN>
+template <int TBN, int CG = 1>
 struct Cfg {
-    static constexpr int B_TILE = TBN == 128 ? 2 * PLANE_TILE : PLANE_TILE;
+    static_assert(CG == 1 || TBN == 128, "CTA pairs use 128-column tiles");
+    // a CTA pair holds one B plane per CTA (Bh in the even CTA, Bl in the odd one)
+    static constexpr int B_TILE = CG == 2 ? PLANE_TILE : (TBN == 128 ? 2 * PLANE_TILE : PLANE_TILE);
     static constexpr int STAGE = OPERAND_TILE + B_TILE;
-    static constexpr int STAGES = TBN == 128 ? 3 : 4;
+    static constexpr int STAGES = CG == 2 ? 4 : (TBN == 128 ? 3 : 4);
     static constexpr int NBUF = TBN == 128 ? 1 : 2;
     static constexpr uint32_t ACC_COLS = 4 * TBN;      // HH | HL | LH | LL
     static constexpr uint32_t MMA_N = 2 * TBN;         // [Bh | Bl]
-    // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128, N = MMA_N.
+    // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128 * CG, N = MMA_N.
     static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((MMA_N >> 3) << 17) |
-                                      ((uint32_t)(BM >> 4) << 24);
+                                      ((uint32_t)((BM * CG) >> 4) << 24);
     static constexpr int SMEM_USED = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
     static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
     static_assert(NBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
@@ -119,6 +121,62 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
 
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// shared::cluster address of the same shared variable in CTA `rank` of the cluster
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// TMA loads whose completion is signalled on the pair leader's mbarrier (bar is a
+// shared::cluster address).  No multicast: each CTA loads into its own shared memory.
+__device__ __forceinline__ void tma_load_4d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                                 int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, int c2,
+                                                 int c3, int c4) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
+        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_i8_pair(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on the mbarrier at this shared offset in every CTA of `mask` once the pair's
+// MMAs issued so far have completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar, uint16_t mask) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+                 "h"(mask)
+                 : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 #define CM_R32(i) "=r"(r[i])
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
@@ -139,6 +197,7 @@ constexpr uint32_t GROUP_M = 8;
 
 struct GemmArgs {
     uint32_t rows, cols, num_kb, a_batches, b_batches, tiles_m, tiles_n, batch;
+    uint32_t tiles_mc;        // row tiles per CTA group: ceil(tiles_m / CG)
     const int32_t* rowterm;
     const int32_t* colterm;
     int16_t* out;
@@ -162,21 +221,22 @@ struct Tile {
     uint32_t cw0, ch0, cn0;   // conv: first output column, row and image of the row tile
 };
 
-// Tile t of the flattened (batch, grouped row/column) order.  Blocks of GROUP_M
-// row tiles sweep the column tiles together, so the ~148 tiles in flight share
-// a few A and B panels in L2.
-template <int TBN>
-__device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t) {
+// Tile t of the flattened (batch, grouped row/column) order, for CTA `rank` of a
+// group of CG CTAs that share it (CG = 2: a pair computes 2 x 128 rows; CTA r takes
+// row tile CG*tmc + r).  Blocks of GROUP_M row tiles sweep the column tiles
+// together, so the ~148 tiles in flight share a few A and B panels in L2.
+template <int TBN, int CG>
+__device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint32_t rank) {
     Tile c;
-    const uint64_t per_z = (uint64_t)g.tiles_m * g.tiles_n;
+    const uint64_t per_z = (uint64_t)g.tiles_mc * g.tiles_n;
     c.z = (uint32_t)(t / per_z);
     const uint32_t local_t = (uint32_t)(t - (uint64_t)c.z * per_z);
     const uint32_t per_group = GROUP_M * g.tiles_n;
     const uint32_t group = local_t / per_group;
     const uint32_t first_m = group * GROUP_M;
-    const uint32_t gsize = min(GROUP_M, g.tiles_m - first_m);
+    const uint32_t gsize = min(GROUP_M, g.tiles_mc - first_m);
     const uint32_t local = local_t - group * per_group;
-    const uint32_t tm = first_m + local % gsize;
+    const uint32_t tm = (first_m + local % gsize) * CG + rank;
     c.m0 = tm * BM;
     c.n0 = (local / gsize) * TBN;
     c.ba = g.a_batches == 1 ? 0u : c.z;
@@ -193,18 +253,27 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t) {
     return c;
 }
 
-// Persistent kernel: one CTA per SM walks tiles blockIdx.x, +gridDim.x, ...
+// Persistent kernel: one CTA per SM (CG = 1), or one CTA pair per two SMs
+// (CG = 2, a 2-CTA cluster), walking tiles cluster, +clusters, ...
 //   warp 0      TMA producer (continuous stage ring across tiles)
-//   warp 1      TMEM owner; lane 0 issues the MMAs of each tile into an accumulator
-//               buffer once the epilogue has drained it
+//   warp 1      TMEM owner; lane 0 (of the pair's even CTA) issues the MMAs of each
+//               tile into an accumulator buffer once the epilogue has drained it
 //   warps 2-9   epilogue: warp w reads TMEM lanes 32*(w%4).. of column half (w-2)/4,
 //               combines the four accumulators into registers, releases the buffer,
 //               then adds the rank-1 terms, narrows and stores while the next
 //               tile's MMAs run.
-template <int TBN>
+// CTA pairs (tcgen05 cta_group::2, M = 256): each CTA loads its own 128 rows of A
+// (both planes) and ONE plane of B (even CTA Bh, odd CTA Bl); one MMA per plane of A
+// multiplies the pair's 256 rows by [Bh | Bl], each CTA's TMEM receiving its own rows'
+// accumulators.  Per CTA and 32-deep K step that is 8 KB of A and 8 KB of B read for
+// 256 tensor cycles, against 24 KB for a single CTA -- the shared-memory traffic the
+// single-CTA kernel is bound by.  All TMA completions and epilogue releases go to the
+// even CTA's barriers; its MMA commits arrive on both CTAs' barriers (multicast
+// commit).  No TMA multicast is used.
+template <int TBN, int CG>
 __global__ void __launch_bounds__(320, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    using C = Cfg<TBN>;
+    using C = Cfg<TBN, CG>;
     constexpr int STAGES = C::STAGES, NBUF = C::NBUF;
     constexpr uint32_t HALF = TBN / 2;                  // columns per epilogue warp
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -220,7 +289,11 @@ __global__ void __launch_bounds__(320, 1)
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const uint64_t total = (uint64_t)g.batch * g.tiles_m * g.tiles_n;
+    const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+    const bool leader = rank == 0;
+    const uint64_t cid = blockIdx.x / CG, ncl = gridDim.x / CG;
+    const uint64_t total = (uint64_t)g.batch * g.tiles_mc * g.tiles_n;
+    constexpr uint16_t kPairMask = 0x3;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -229,7 +302,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(smem_u32(&accf_b[b]), 1);
-            mbar_init(smem_u32(&acce_b[b]), 8);
+            mbar_init(smem_u32(&acce_b[b]), 8 * CG);
         }
         mbar_init(smem_u32(done_b), 1);
         *abort_flag = 0;
@@ -237,13 +310,20 @@ __global__ void __launch_bounds__(320, 1)
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == 1) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
-                     "r"(TMEM_COLS)
-                     : "memory");
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        if (CG == 2)
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+        else
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+        if (CG == 2) asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        else asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
         tc_fence_before();
     }
     __syncthreads();
+    if (CG == 2) cluster_sync_all();      // both CTAs' barriers exist before any remote arrival
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const WaitCtl wc{abort_flag, g.status, g.timeout_ns};
@@ -251,27 +331,43 @@ __global__ void __launch_bounds__(320, 1)
     if (warp == 0) {
         if (lane == 0) {
             uint32_t it = 0;
-            for (uint64_t t = blockIdx.x; t < total && !*abort_flag; t += gridDim.x) {
-                const Tile tc = decode_tile<TBN>(g, t);
+            for (uint64_t t = cid; t < total && !*abort_flag; t += ncl) {
+                const Tile tc = decode_tile<TBN, CG>(g, t, rank);
                 for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(smem_u32(&empty_b[s]), (round & 1u) ^ 1u, wc)) break;
-                    const uint32_t full = smem_u32(&full_b[s]);
-                    mbar_expect_tx(full, C::STAGE);
                     uint8_t* st = smem + s * C::STAGE;
-                    if (g.conv) {
-                        const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
-                        const int c1 = (int)(tc.cw0 * g.sw), c2 = (int)(tc.ch0 * g.sh + r * g.dh);
-                        tma_load_5d(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 0);
-                        tma_load_5d(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 1);
+                    if (CG == 2) {
+                        const uint32_t full = map_to_rank(smem_u32(&full_b[s]), 0);   // the pair leader's barrier
+                        if (leader) mbar_expect_tx(smem_u32(&full_b[s]), CG * C::STAGE);
+                        if (g.conv) {
+                            const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
+                            const int c1 = (int)(tc.cw0 * g.sw), c2 = (int)(tc.ch0 * g.sh + r * g.dh);
+                            tma_load_5d_pair(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 0);
+                            tma_load_5d_pair(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 1);
+                        } else {
+                            tma_load_4d_pair(smem_u32(st), &tmA, full, (int)(kb * BK), (int)tc.m0, 0, (int)tc.ba);
+                        }
+                        tma_load_4d_pair(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), (int)rank,
+                                         (int)tc.bb);
                     } else {
-                        tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)tc.m0, 0, (int)tc.ba);
+                        const uint32_t full = smem_u32(&full_b[s]);
+                        mbar_expect_tx(full, C::STAGE);
+                        if (g.conv) {
+                            const uint32_t r = kb / g.kb_per_r, kk = (kb - r * g.kb_per_r) * BK;
+                            const int c1 = (int)(tc.cw0 * g.sw), c2 = (int)(tc.ch0 * g.sh + r * g.dh);
+                            tma_load_5d(smem_u32(st), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 0);
+                            tma_load_5d(smem_u32(st + PLANE_TILE), &tmA, full, (int)kk, c1, c2, (int)tc.cn0, 1);
+                        } else {
+                            tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)tc.m0, 0, (int)tc.ba);
+                        }
+                        tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), 0, (int)tc.bb);
                     }
-                    tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), 0, (int)tc.bb);
                 }
             }
-            if (*abort_flag) {
-                // let copies already in flight land before the CTA exits
+            if (*abort_flag && leader) {
+                // let copies already in flight land before the CTA exits (a pair's copies
+                // all complete on the leader's barriers)
                 const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
                 volatile int never = 0;
                 WaitCtl drain{&never, g.status, g.timeout_ns};
@@ -279,10 +375,10 @@ __global__ void __launch_bounds__(320, 1)
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
+        if (lane == 0 && leader) {
             uint32_t it = 0, j = 0;
             bool ok = true;
-            for (uint64_t t = blockIdx.x; ok && t < total; t += gridDim.x, ++j) {
+            for (uint64_t t = cid; ok && t < total; t += ncl, ++j) {
                 const uint32_t buf = j % NBUF, use = j / NBUF;
                 if (!mbar_wait(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, wc)) break;
                 tc_fence_after();
@@ -301,15 +397,26 @@ __global__ void __launch_bounds__(320, 1)
                         const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
                         const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x [Bh | Bl]
                         const uint32_t acc = (kb | kk) != 0u;
-                        umma_i8(d, ah, bhl, C::IDESC, acc);                 // -> HH | HL
-                        umma_i8(d + 2 * TBN, al, bhl, C::IDESC, acc);       // -> LH | LL
+                        if (CG == 2) {
+                            umma_i8_pair(d, ah, bhl, C::IDESC, acc);            // -> HH | HL (both CTAs)
+                            umma_i8_pair(d + 2 * TBN, al, bhl, C::IDESC, acc);  // -> LH | LL
+                        } else {
+                            umma_i8(d, ah, bhl, C::IDESC, acc);                 // -> HH | HL
+                            umma_i8(d + 2 * TBN, al, bhl, C::IDESC, acc);       // -> LH | LL
+                        }
                     }
-                    umma_commit(smem_u32(&empty_b[s]));   // frees the stage once these MMAs have read it
+                    // frees the stage (in both CTAs of a pair) once these MMAs have read it
+                    if (CG == 2) umma_commit_pair(smem_u32(&empty_b[s]), kPairMask);
+                    else umma_commit(smem_u32(&empty_b[s]));
                 }
-                if (ok) umma_commit(smem_u32(&accf_b[buf]));
+                if (ok) {
+                    if (CG == 2) umma_commit_pair(smem_u32(&accf_b[buf]), kPairMask);
+                    else umma_commit(smem_u32(&accf_b[buf]));
+                }
             }
             // every MMA issued by this thread has completed once `done` fires
-            umma_commit(smem_u32(done_b));
+            if (CG == 2) umma_commit_pair(smem_u32(done_b), 0x1);
+            else umma_commit(smem_u32(done_b));
             volatile int never = 0;
             WaitCtl drain{&never, g.status, g.timeout_ns};
             mbar_wait(smem_u32(done_b), 0, drain);
@@ -320,7 +427,7 @@ __global__ void __launch_bounds__(320, 1)
         const uint32_t i = quarter * 32 + lane;           // TMEM lane = A tile row
         const uint32_t cbase = half * HALF;
         uint32_t j = 0;
-        for (uint64_t t = blockIdx.x; t < total; t += gridDim.x, ++j) {
+        for (uint64_t t = cid; t < total; t += ncl, ++j) {
             const uint32_t buf = j % NBUF, use = j / NBUF;
             // One lane waits; the verdict is broadcast so that the .sync.aligned
             // TMEM loads below are executed by the whole warp or not at all.
@@ -330,7 +437,7 @@ __global__ void __launch_bounds__(320, 1)
             __syncwarp();
             if (!ok) break;
             tc_fence_after();
-            const Tile tc = decode_tile<TBN>(g, t);
+            const Tile tc = decode_tile<TBN, CG>(g, t, rank);
             bool valid;
             uint64_t rt_idx, o_off;
             if (g.conv) {
@@ -386,7 +493,10 @@ __global__ void __launch_bounds__(320, 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&acce_b[buf]));   // buffer free for the next tile
+            if (lane == 0) {                                      // buffer free for the next tile
+                if (CG == 2) mbar_arrive_cluster(map_to_rank(smem_u32(&acce_b[buf]), 0));
+                else mbar_arrive(smem_u32(&acce_b[buf]));
+            }
             if (!valid) continue;
             int16_t* orow = g.out + o_off;
             if (g.epi) {
@@ -437,9 +547,14 @@ __global__ void __launch_bounds__(320, 1)
         }
     }
     __syncthreads();
+    // a pair's CTAs read each other's shared memory and barriers until here
+    if (CG == 2) cluster_sync_all();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        if (CG == 2)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
     }
 }
 
@@ -639,13 +754,15 @@ int make_plane_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t K_pa
 }
 
 // planes [batches][2][K][C_pad] int8 (N-major); box {128 n, 128 k, 2 planes, 1 batch}.
-int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t C_pad, uint32_t K, uint32_t batches) {
+// plane_box = 2: both planes per box (one CTA); 1: one plane per box (CTA pairs).
+int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t C_pad, uint32_t K, uint32_t batches,
+                    uint32_t plane_box = 2) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
     if (((uintptr_t)base & 15u) != 0 || (C_pad & 15u) != 0) return set_error(CM_EINVAL, "plane buffer misaligned");
     const cuuint64_t dims[4] = {cols, K, 2, batches};
     const cuuint64_t strides[3] = {(cuuint64_t)C_pad, (cuuint64_t)K * C_pad, (cuuint64_t)2 * K * C_pad};
-    const cuuint32_t box[4] = {128, (cuuint32_t)BK, 2, 1};
+    const cuuint32_t box[4] = {128, (cuuint32_t)BK, plane_box, 1};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -695,28 +812,62 @@ int make_packed_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t bat
     return CM_OK;
 }
 
-template <int TBN>
+template <int TBN, int CG>
 int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    static int per_sm_clusters = -1;   // co-resident clusters of CG CTAs (one CTA per SM)
+    if (per_sm_clusters < 0) {
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
-        attr_set = true;
+        int n = cx->sm_count / CG;
+        if (CG > 1) {
+            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+            cudaLaunchConfig_t q{};
+            q.gridDim = dim3(CG * n);
+            q.blockDim = dim3(320);
+            q.dynamicSmemBytes = SMEM_BYTES;
+            cudaLaunchAttribute at{};
+            at.id = cudaLaunchAttributeClusterDimension;
+            at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+            q.attrs = &at; q.numAttrs = 1;
+            int m = 0;
+            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG>, &q) == cudaSuccess && m > 0) n = m;
+            cudaGetLastError();
+        }
+        per_sm_clusters = n;
     }
     g.tiles_n = (g.cols + TBN - 1) / TBN;
-    const uint64_t total = (uint64_t)g.batch * g.tiles_m * g.tiles_n;
+    g.tiles_mc = (g.tiles_m + CG - 1) / CG;
+    const uint64_t total = (uint64_t)g.batch * g.tiles_mc * g.tiles_n;
     if (total == 0) return CM_OK;
     if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 32)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
-    const unsigned grid = (unsigned)std::min<uint64_t>(total, (uint64_t)cx->sm_count);
+    const unsigned clusters = (unsigned)std::min<uint64_t>(total, (uint64_t)per_sm_clusters);
     g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    cudaError_t e;
     {
         ProfScope ps_(PK_GEMM, s);
-        gemm_q88_kernel<TBN><<<grid, 320, SMEM_BYTES, s>>>(ta, tb, g);
+        if (CG == 1) {
+            gemm_q88_kernel<TBN, CG><<<clusters, 320, SMEM_BYTES, s>>>(ta, tb, g);
+            e = cudaGetLastError();
+        } else {
+            cudaLaunchConfig_t q{};
+            q.gridDim = dim3(CG * clusters);
+            q.blockDim = dim3(320);
+            q.dynamicSmemBytes = SMEM_BYTES;
+            q.stream = s;
+            cudaLaunchAttribute at{};
+            at.id = cudaLaunchAttributeClusterDimension;
+            at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+            q.attrs = &at; q.numAttrs = 1;
+            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG>, ta, tb, g);
+        }
     }
     count_launch();
-    cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
 }
+
+// CTA pairs for 128-column tiles when there are at least two row tiles (off with
+// CM_GEMM_PAIRS=0 in the environment at cm_init).
+bool use_pairs(const Context* cx, uint32_t tiles_m) { return cx->gemm_pairs && tiles_m >= 2; }
 
 }  // namespace
 
@@ -737,12 +888,14 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     CUtensorMap ta, tb;
     int rc = make_plane_map(&ta, p.a_planes, p.K, p.K_pad, p.rows, p.a_batches);
     if (rc) return rc;
+    const uint32_t tiles_m = (p.rows + BM - 1) / BM;
+    const bool pairs = !p.b_packed && use_pairs(cx, tiles_m);
     rc = p.b_packed ? make_packed_map(&tb, p.b_planes, p.K, p.b_batches)
-                    : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, p.b_batches);
+                    : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, p.b_batches, pairs ? 1u : 2u);
     if (rc) return rc;
     GemmArgs g{};
     g.rows = p.rows; g.cols = p.cols; g.num_kb = (p.K + BK - 1) / BK;
-    g.tiles_m = (p.rows + BM - 1) / BM;
+    g.tiles_m = tiles_m;
     g.batch = p.batch;
     g.a_batches = p.a_batches; g.b_batches = p.b_batches;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
@@ -751,7 +904,8 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.rows_per_img = p.rows_per_img;
     g.ksteps = (p.K + 31) / 32;
     g.epi = p.epi; g.resid = p.resid;
-    return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
+    if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
+    return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);
 }
 
 int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
@@ -762,7 +916,12 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     CUtensorMap ta, tb;
     int rc = make_conv_map(&ta, c);
     if (rc) return rc;
-    rc = p.b_packed ? make_packed_map(&tb, p.b_planes, p.K, 1) : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, 1);
+    const uint64_t tiles_img0 = (c.nimg + (1u << c.bn_log) - 1) >> c.bn_log;
+    const uint64_t tiles_m0 = tiles_img0 * ((c.out_w + (1u << c.bw_log) - 1) >> c.bw_log) *
+                              ((c.out_h + (1u << c.bh_log) - 1) >> c.bh_log);
+    const bool pairs = !p.b_packed && use_pairs(cx, (uint32_t)std::min<uint64_t>(tiles_m0, 1u << 30));
+    rc = p.b_packed ? make_packed_map(&tb, p.b_planes, p.K, 1)
+                    : make_nmajor_map(&tb, p.b_planes, p.cols, p.C_pad, p.K, 1, pairs ? 1u : 2u);
     if (rc) return rc;
     GemmArgs g{};
     g.conv = 1;
@@ -780,7 +939,8 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.rowterm = p.rowterm; g.colterm = p.colterm;
     g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
     g.epi = p.epi; g.resid = p.resid;
-    return p.b_packed ? launch_persistent<64>(cx, ta, tb, g, s) : launch_persistent<128>(cx, ta, tb, g, s);
+    if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
+    return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);
 }
 
 int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,
