@@ -438,15 +438,15 @@ class NetworkBench:
             self.net = networks.resnet18(batch=max(self.local, 1))
             self.metric = "ResNet-18-shaped images/s (batch 256)"
         self.fused = not UNFUSED
-        if self.fused:                                           # Conv->Relu / Conv->Add->Relu folded
-            self.net = networks.fuse(self.net)
+        if self.fused:                                           # Conv->Relu (/ Conv->Add->Relu) folded
+            self.net = networks.fuse(self.net, residual=FUSE_RESIDUAL)
         self.units_total = float(self.batch_total)
         self.units_local = float(self.local)
         self.dom_units_local = 8.0 * self.net.macs_per_image * self.local   # int8 ops (4 MMAs x 2 per MAC)
 
     def config(self, world):
-        calls = ("reference call list, Conv->Relu and Conv->Add->Relu chains folded into cm_conv_fused"
-                 if self.fused else "reference call list, one C-ABI call per node")
+        calls = ("reference call list, Conv->Relu" + (" and Conv->Add->Relu" if FUSE_RESIDUAL else "")
+                 + " chains folded into cm_conv_fused" if self.fused else "reference call list, one C-ABI call per node")
         if self.which == "lenet":
             return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
                     "parallelism": f"replicas only: one batch-1 stream per GPU ({world})", "calls": calls,
@@ -548,6 +548,7 @@ class NetworkBench:
 
 
 UNFUSED = False      # --unfused: networks run node by node
+FUSE_RESIDUAL = False  # --fuse-residual: also fold Conv->Add->Relu
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -714,13 +715,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-workers", type=int, default=0)
     ap.add_argument("--per-part", action="store_true", help="add a per-shape/per-variant device-time breakdown")
+    ap.add_argument("--fuse-residual", action="store_true",
+                    help="lenet/resnet: also fold Conv->Add->Relu chains (residual read in the conv epilogue)")
     ap.add_argument("--unfused", action="store_true",
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
     args = ap.parse_args()
-    global UNFUSED
+    global UNFUSED, FUSE_RESIDUAL
     UNFUSED = args.unfused
+    FUSE_RESIDUAL = args.fuse_residual
     if args.int8_peak:
         return int8_peak()
     if args.shape:
