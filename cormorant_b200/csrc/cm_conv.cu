@@ -377,7 +377,7 @@ __global__ void __launch_bounds__(256) conv_weights_kernel(const int16_t* __rest
     __syncthreads();
     const uint32_t kl = t / 2, half = t % 2, k = k0 + kl;
     // a run of 16 channels that starts below M ends within the row (M_pad, or 64 packed)
-    if (k < K && m0 + 16 * half < M) {
+    if (planes && k < K && m0 + 16 * half < M) {
         const uint32_t c = k / khw, rs = k - c * khw;
         const uint32_t r = rs / kw, sx = rs - r * kw;
         const uint64_t o = ((uint64_t)r * KR_pad + (uint64_t)sx * Cp + c) * pitch + m0 + 16 * half;
@@ -397,7 +397,7 @@ __global__ void __launch_bounds__(256) conv_weights_kernel(const int16_t* __rest
 int conv_weights(const Context* cx, const int16_t* weight, const int16_t* bias, uint32_t M, uint32_t C, uint32_t kh,
                  uint32_t kw, uint32_t Cp, uint32_t KR_pad, uint32_t pitch, uint64_t plane, uint64_t plane_bytes,
                  int8_t* planes, int32_t* colterm, cudaStream_t s) {
-    cudaError_t e = cudaMemsetAsync(planes, 0, plane_bytes, s);
+    cudaError_t e = planes ? cudaMemsetAsync(planes, 0, plane_bytes, s) : cudaSuccess;
     if (e == cudaSuccess) e = cudaMemsetAsync(colterm, 0, (size_t)M * sizeof(int32_t), s);
     if (e != cudaSuccess) return cuda_error(e, "memset conv weights");
     const uint32_t K = C * kh * kw;
@@ -621,6 +621,122 @@ bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint
     return true;
 }
 
+// ---- space-to-depth form of strided convolutions with few input channels -----
+// A conv with stride s in both directions equals a stride-1 conv over the input
+// regrouped into s x s blocks: virtual pixel (h', w') holds channels (th, tw, c) =
+// x[c][s*h' + th - pt][s*w' + tw - pl] (zero outside the image), and the virtual
+// kernel is ceil(kh/s) x ceil(kw/s) with tap (r', u', th, tw, c) = w[c][s*r' + th][s*u' + tw]
+// (zero where that index is past the original kernel).  For the 3-channel 7x7 stride-2
+// stem this is 12 channels and a 4x4 kernel: the implicit GEMM applies (no im2col
+// buffer).  The virtual taps past the original kernel have zero weights, so the row
+// terms are the box sums over the ORIGINAL taps (conv_rowterm_kernel over per-pixel
+// channel sums of the padded original image) and the column terms come from the
+// original weights.
+
+struct S2dPlan {
+    uint32_t s, C2, kh2, kw2, Hpo, Wpo;
+    ImplicitPlan ip;
+};
+
+bool plan_s2d(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
+              uint32_t dh, uint32_t dw, S2dPlan* sp) {
+    if (sh != sw || sh < 2 || sh > 4 || dh != 1 || dw != 1 || C == 0 || kh == 0 || kw == 0) return false;
+    const uint32_t s = sh, C2 = s * s * C;
+    if (C2 > 64) return false;
+    const uint32_t kh2 = (kh + s - 1) / s, kw2 = (kw + s - 1) / s;
+    ImplicitPlan ip;
+    if (!plan_implicit(C2, out_h, out_w, kh2, kw2, 1, 1, 1, 1, &ip)) {
+        // plan_implicit's waste rule counts the virtual taps as real; re-plan without it
+        const uint64_t Cp = (C2 + 15ull) & ~15ull, KR = (uint64_t)kw2 * Cp, KR_pad = (KR + 127) & ~127ull;
+        const uint64_t Hp = (uint64_t)out_h + kh2 - 1, Wp = (uint64_t)out_w + kw2 - 1;
+        if (Hp * Wp >= (1ull << 31)) return false;
+        uint32_t bw = std::min<uint32_t>(pow2_ceil(out_w), 128);
+        uint32_t bh = std::min<uint32_t>(pow2_ceil(out_h), 128 / bw);
+        ip.Cp = (uint32_t)Cp; ip.Hp = (uint32_t)Hp; ip.Wp = (uint32_t)Wp;
+        ip.KR = (uint32_t)KR; ip.KR_pad = (uint32_t)KR_pad; ip.Kt = (uint32_t)(KR_pad * kh2);
+        ip.bw = bw; ip.bh = bh; ip.bn = 128 / (bw * bh);
+    }
+    // MMA steps against the original taps: allow up to 2x (the im2col it replaces costs more)
+    const uint64_t steps = (uint64_t)kh2 * ((ip.KR + 31) / 32) * 32;
+    if (steps > 2ull * C * kh * kw) return false;
+    sp->s = s; sp->C2 = C2; sp->kh2 = kh2; sp->kw2 = kw2;
+    sp->Hpo = ip.Hp * s; sp->Wpo = ip.Wp * s;
+    sp->ip = ip;
+    return true;
+}
+
+struct S2dGeom {
+    uint32_t C, H, W, s, C2, Cp, Hs, Ws, pt, pl, Hpo, Wpo, nimg;
+};
+
+// x [nimg][C][H][W] -> virtual planes [2][nimg][Hs][Ws][Cp]; channels >= C2 hold x = 0.
+// So[n][hp][wp] = sum_c (x - 128) over the ORIGINAL padded image (x = 0 outside).
+// Thread = one virtual pixel: s*s*C reads, Cp/16 16-byte runs per plane.
+__global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __restrict__ x, S2dGeom g, uint64_t total,
+                                                             int8_t* __restrict__ planes, int32_t* __restrict__ So) {
+    const uint64_t plane = (uint64_t)g.nimg * g.Hs * g.Ws * g.Cp;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint64_t n = t / ((uint64_t)g.Hs * g.Ws);
+        const uint32_t rem = (uint32_t)(t - n * g.Hs * g.Ws);
+        const uint32_t hv = rem / g.Ws, wv = rem - hv * g.Ws;
+        const int16_t* xn = x + n * g.C * g.H * g.W;
+        int8_t* dst = planes + t * g.Cp;
+        for (uint32_t c0 = 0; c0 < g.Cp; c0 += 16) {
+            uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
+            for (uint32_t j = 0; j < 16 && c0 + j < g.C2; ++j) {
+                const uint32_t c2 = c0 + j, blk = c2 / g.C, c = c2 - blk * g.C;
+                const uint32_t th = blk / g.s, tw = blk - th * g.s;
+                const int32_t ih = (int32_t)(g.s * hv + th) - (int32_t)g.pt, iw = (int32_t)(g.s * wv + tw) - (int32_t)g.pl;
+                int16_t v = 0;
+                if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
+                    v = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
+                const uint32_t sh = 8 * (j % 4);
+                hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << sh;
+                lw[j / 4] = (lw[j / 4] & ~(0xFFu << sh)) | (((uint32_t)v & 255u) ^ 0x80u) << sh;
+            }
+            *(uint4*)(dst + c0) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(dst + plane + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        // per original pixel channel sums for the row terms
+        for (uint32_t th = 0; th < g.s; ++th)
+            for (uint32_t tw = 0; tw < g.s; ++tw) {
+                const int32_t ih = (int32_t)(g.s * hv + th) - (int32_t)g.pt, iw = (int32_t)(g.s * wv + tw) - (int32_t)g.pl;
+                const bool in = ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W;
+                int32_t sum = 0;
+                for (uint32_t c = 0; c < g.C; ++c)
+                    sum += (in ? (int32_t)__ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw) : 0) - 128;
+                So[(n * g.Hpo + g.s * hv + th) * g.Wpo + g.s * wv + tw] = sum;
+            }
+    }
+}
+
+// Virtual weights -> N-major planes (layout as conv_weights_kernel): row
+// k' = r'*KR_pad + u'*Cp + (th*s + tw)*C + c holds w[m][c][s*r' + th][s*u' + tw], zero past
+// the original kernel.  Thread per (k', m); the weights are small.
+__global__ void __launch_bounds__(256) conv_s2d_weights_kernel(const int16_t* __restrict__ w, uint32_t M, uint32_t C,
+                                                               uint32_t kh, uint32_t kw, uint32_t s, uint32_t kw2,
+                                                               uint32_t Cp, uint32_t KR_pad, uint32_t Kt, uint32_t pitch,
+                                                               uint64_t plane, int8_t* __restrict__ planes) {
+    const uint64_t total = (uint64_t)Kt * M;
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+        const uint32_t kp = (uint32_t)(t / M), m = (uint32_t)(t - (uint64_t)kp * M);
+        const uint32_t r2 = kp / KR_pad, rem = kp - r2 * KR_pad;
+        const uint32_t u2 = rem / Cp, c2 = rem - u2 * Cp;
+        int8_t hi = 0, lo = 0;
+        if (u2 < kw2 && c2 < s * s * C) {
+            const uint32_t blk = c2 / C, c = c2 - blk * C, th = blk / s, tw = blk - th * s;
+            const uint32_t r = s * r2 + th, q = s * u2 + tw;
+            if (r < kh && q < kw) {
+                const int16_t v = __ldg(w + (((uint64_t)m * C + c) * kh + r) * kw + q);
+                hi = (int8_t)(v >> 8);
+                lo = (int8_t)((v & 255) - 128);
+            }
+        }
+        planes[(uint64_t)kp * pitch + m] = hi;
+        planes[plane + (uint64_t)kp * pitch + m] = lo;
+    }
+}
+
 }  // namespace
 }  // namespace cm
 
@@ -756,6 +872,69 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
             const ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
                            out_h, out_w, log2u(ip.bw), log2u(ip.bh), log2u(ip.bn)};
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, ip.Kt, ip.Kt, M_pad, rt, ct,
+                       y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
+            p.conv = &ca;
+            p.b_packed = packed ? 1u : 0u;
+            p.epi = epi;
+            p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
+            rc = gemm_launch(cx, p, s);
+        }
+        scratch_free(scratch, s);
+        if (rc) return rc;
+        cudaError_t e = cudaGetLastError();
+        return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv");
+    }
+
+    S2dPlan sp;
+    if (plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp)) {
+        const ImplicitPlan& vp = sp.ip;
+        const uint32_t M_pad = pad_c(out_ch);
+        const bool packed = out_ch <= 64;
+        const uint32_t w_pitch = packed ? 128u : M_pad;
+        const uint64_t w_plane = packed ? 64u : (uint64_t)vp.Kt * M_pad;
+        const uint64_t img_plane = (uint64_t)vp.Hp * vp.Wp * vp.Cp;
+        const uint64_t img_so = (uint64_t)sp.Hpo * sp.Wpo;
+        uint64_t chunk = kNhwcBudget / (2 * img_plane + 4 * img_so);
+        if (chunk == 0) chunk = 1;
+        if (chunk > batch) chunk = batch;
+        if (chunk > (1u << 24)) chunk = 1u << 24;
+        const uint64_t w_bytes = ((uint64_t)vp.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+        const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+        const uint64_t a_bytes = (2 * chunk * img_plane + vp.KR + 256 + 255) & ~255ull;
+        const uint64_t s_bytes = (chunk * img_so * 4 + 255) & ~255ull;
+        const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
+        void* scratch = nullptr;
+        rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + s_bytes + rt_bytes, s);
+        if (rc) return rc;
+        int8_t* wpl = (int8_t*)scratch;
+        int32_t* ct = (int32_t*)(wpl + w_bytes);
+        int8_t* apl = (int8_t*)ct + ct_bytes;
+        int32_t* So = (int32_t*)(apl + a_bytes);
+        int32_t* rt = (int32_t*)((int8_t*)So + s_bytes);
+        // column terms from the original weights (real taps, bias), planes of the virtual kernel
+        rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, 0, 0, 0, 0, 0, nullptr, ct, s);
+        if (!rc) {
+            ProfScope ps_(PK_SPLIT, s);
+            const uint64_t wtot = (uint64_t)vp.Kt * out_ch;
+            conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
+                                                                              vp.Cp, vp.KR_pad, vp.Kt, w_pitch, w_plane, wpl);
+            count_launch();
+        }
+        for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
+            const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
+            const S2dGeom sg{in_ch, in_h, in_w, sp.s, sp.C2, vp.Cp, vp.Hp, vp.Wp, pad_top, pad_left, sp.Hpo, sp.Wpo, nb};
+            const uint64_t vtot = (uint64_t)nb * vp.Hp * vp.Wp, tot = (uint64_t)nb * P;
+            {
+                ProfScope ps_(PK_SPLIT, s);
+                conv_s2d_split_kernel<<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(x + n0 * (uint64_t)in_ch * in_h * in_w, sg,
+                                                                                vtot, apl, So);
+                conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s,
+                                                                            sp.s, 1, tot, rt);
+                count_launch(2);
+            }
+            const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh2, 1, 1, 1,
+                           out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};
+            GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, vp.Kt, vp.Kt, M_pad, rt, ct,
                        y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;

@@ -67,6 +67,11 @@ REF_CASES = [
     # whose output rows are wider than a window block
     (1, 600, 9, 300, 8, 3, 3, 1, 1, 1, 2, 1, 2, 1, 2, 1, 0),
     (2, 3, 11, 300, 20, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
+    # space-to-depth form (stride s in both directions, s*s*C channels): odd sizes with
+    # asymmetric padding, more than 64 output channels, stride 4
+    (2, 3, 35, 29, 40, 7, 7, 2, 2, 1, 1, 3, 2, 3, 1, 1, 0),
+    (1, 4, 33, 33, 100, 5, 5, 2, 2, 1, 1, 2, 2, 2, 2, 1, 0),
+    (2, 2, 26, 26, 16, 4, 4, 4, 4, 1, 1, 1, 1, 1, 1, 1, 0),
 ]
 
 
