@@ -548,7 +548,7 @@ class NetworkBench:
 
 
 UNFUSED = False      # --unfused: networks run node by node
-FUSE_RESIDUAL = False  # --fuse-residual: also fold Conv->Add->Relu
+FUSE_RESIDUAL = True   # --no-fuse-residual: fold Conv->Relu only
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -715,8 +715,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-workers", type=int, default=0)
     ap.add_argument("--per-part", action="store_true", help="add a per-shape/per-variant device-time breakdown")
-    ap.add_argument("--fuse-residual", action="store_true",
-                    help="lenet/resnet: also fold Conv->Add->Relu chains (residual read in the conv epilogue)")
+    ap.add_argument("--no-fuse-residual", action="store_true",
+                    help="lenet/resnet: fold Conv->Relu only (keep the residual Add / Relu passes)")
     ap.add_argument("--unfused", action="store_true",
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
@@ -724,7 +724,7 @@ def main():
     args = ap.parse_args()
     global UNFUSED, FUSE_RESIDUAL
     UNFUSED = args.unfused
-    FUSE_RESIDUAL = args.fuse_residual
+    FUSE_RESIDUAL = not args.no_fuse_residual
     if args.int8_peak:
         return int8_peak()
     if args.shape:

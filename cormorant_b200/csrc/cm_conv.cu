@@ -671,9 +671,16 @@ struct S2dGeom {
 
 // x [nimg][C][H][W] -> virtual planes [2][nimg][Hs][Ws][Cp]; channels >= C2 hold x = 0.
 // So[n][hp][wp] = sum_c (x - 128) over the ORIGINAL padded image (x = 0 outside).
-// Thread = one virtual pixel: s*s*C reads, Cp/16 16-byte runs per plane.
+// Thread = one virtual pixel: each of its s*s*C words is read once (for the planes and
+// the channel sums), Cp/16 16-byte runs per plane.  s*s*C <= 64.
+// S_, C_ > 0 fix s and C at compile time (the channel index of every word is then a
+// constant and the packing stays in registers); 0 takes them from g.
+template <int S_, int C_>
 __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __restrict__ x, S2dGeom g, uint64_t total,
                                                              int8_t* __restrict__ planes, int32_t* __restrict__ So) {
+    constexpr uint32_t CPC = S_ > 0 ? ((uint32_t)(S_ * S_ * C_) + 15u) / 16u * 16u : 0u;
+    const uint32_t S = S_ > 0 ? (uint32_t)S_ : g.s, CC = C_ > 0 ? (uint32_t)C_ : g.C;
+    const uint32_t Cp = CPC ? CPC : g.Cp;
     const uint64_t plane = (uint64_t)g.nimg * g.Hs * g.Ws * g.Cp;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t n = t / ((uint64_t)g.Hs * g.Ws);
@@ -681,32 +688,34 @@ __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __re
         const uint32_t hv = rem / g.Ws, wv = rem - hv * g.Ws;
         const int16_t* xn = x + n * g.C * g.H * g.W;
         int8_t* dst = planes + t * g.Cp;
-        for (uint32_t c0 = 0; c0 < g.Cp; c0 += 16) {
-            uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u};
-            for (uint32_t j = 0; j < 16 && c0 + j < g.C2; ++j) {
-                const uint32_t c2 = c0 + j, blk = c2 / g.C, c = c2 - blk * g.C;
-                const uint32_t th = blk / g.s, tw = blk - th * g.s;
-                const int32_t ih = (int32_t)(g.s * hv + th) - (int32_t)g.pt, iw = (int32_t)(g.s * wv + tw) - (int32_t)g.pl;
-                int16_t v = 0;
-                if (ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W)
-                    v = __ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw);
-                const uint32_t sh = 8 * (j % 4);
-                hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << sh;
-                lw[j / 4] = (lw[j / 4] & ~(0xFFu << sh)) | (((uint32_t)v & 255u) ^ 0x80u) << sh;
-            }
-            *(uint4*)(dst + c0) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *(uint4*)(dst + plane + c0) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
-        // per original pixel channel sums for the row terms
-        for (uint32_t th = 0; th < g.s; ++th)
-            for (uint32_t tw = 0; tw < g.s; ++tw) {
-                const int32_t ih = (int32_t)(g.s * hv + th) - (int32_t)g.pt, iw = (int32_t)(g.s * wv + tw) - (int32_t)g.pl;
+        uint32_t hw[16], lw[16];                         // up to 64 channels per plane
+#pragma unroll
+        for (int q = 0; q < 16; ++q) { hw[q] = 0; lw[q] = 0x80808080u; }
+        uint32_t c2 = 0;
+#pragma unroll
+        for (uint32_t th = 0; th < S; ++th)
+#pragma unroll
+            for (uint32_t tw = 0; tw < S; ++tw) {
+                const int32_t ih = (int32_t)(S * hv + th) - (int32_t)g.pt, iw = (int32_t)(S * wv + tw) - (int32_t)g.pl;
                 const bool in = ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W;
+                const int16_t* xp = xn + (in ? (uint64_t)ih * g.W + (uint32_t)iw : 0);
                 int32_t sum = 0;
-                for (uint32_t c = 0; c < g.C; ++c)
-                    sum += (in ? (int32_t)__ldg(xn + ((uint64_t)c * g.H + (uint32_t)ih) * g.W + (uint32_t)iw) : 0) - 128;
-                So[(n * g.Hpo + g.s * hv + th) * g.Wpo + g.s * wv + tw] = sum;
+#pragma unroll
+                for (uint32_t c = 0; c < CC; ++c, ++c2) {
+                    const int16_t v = in ? __ldg(xp + (uint64_t)c * g.H * g.W) : (int16_t)0;
+                    sum += (int32_t)v - 128;
+                    const uint32_t q = c2 >> 2, sh = 8 * (c2 & 3);
+                    hw[q] |= (uint32_t)(uint8_t)(v >> 8) << sh;
+                    lw[q] = (lw[q] & ~(0xFFu << sh)) | ((((uint32_t)v & 255u) ^ 0x80u) << sh);
+                }
+                So[(n * g.Hpo + S * hv + th) * g.Wpo + S * wv + tw] = sum;
             }
+#pragma unroll
+        for (uint32_t c0 = 0; c0 < Cp; c0 += 16) {
+            const uint32_t q = c0 / 4;
+            *(uint4*)(dst + c0) = make_uint4(hw[q], hw[q + 1], hw[q + 2], hw[q + 3]);
+            *(uint4*)(dst + plane + c0) = make_uint4(lw[q], lw[q + 1], lw[q + 2], lw[q + 3]);
+        }
     }
 }
 
@@ -926,8 +935,11 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
             const uint64_t vtot = (uint64_t)nb * vp.Hp * vp.Wp, tot = (uint64_t)nb * P;
             {
                 ProfScope ps_(PK_SPLIT, s);
-                conv_s2d_split_kernel<<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(x + n0 * (uint64_t)in_ch * in_h * in_w, sg,
-                                                                                vtot, apl, So);
+                const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
+                if (sp.s == 2 && in_ch == 3)
+                    conv_s2d_split_kernel<2, 3><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
+                else
+                    conv_s2d_split_kernel<0, 0><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
                 conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s,
                                                                             sp.s, 1, tot, rt);
                 count_launch(2);

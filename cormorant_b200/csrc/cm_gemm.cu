@@ -63,6 +63,10 @@ struct Cfg {
     static constexpr int STAGES = CG == 2 ? 4 : (TBN == 128 ? 3 : 4);
     static constexpr int NBUF = TBN == 128 ? 1 : 2;
     static constexpr uint32_t ACC_COLS = 4 * TBN;      // HH | HL | LH | LL
+    // epilogue warps: 4 TMEM lane quarters x 4 column groups (the epilogue must keep up
+    // with short mainloops: conv tiles with few K blocks, fused residual reads)
+    static constexpr int EPI_WARPS = 16;
+    static constexpr int THREADS = 64 + 32 * EPI_WARPS;
     static constexpr uint32_t MMA_N = 2 * TBN;         // [Bh | Bl]
     // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128 * CG, N = MMA_N.
     static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((MMA_N >> 3) << 17) |
@@ -191,6 +195,23 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 }
 #undef CM_R32
 
+#define CM_R16(i) "=r"(r[i])
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+        : CM_R16(0), CM_R16(1), CM_R16(2), CM_R16(3), CM_R16(4), CM_R16(5), CM_R16(6), CM_R16(7), CM_R16(8),
+          CM_R16(9), CM_R16(10), CM_R16(11), CM_R16(12), CM_R16(13), CM_R16(14), CM_R16(15)
+        : "r"(taddr));
+}
+#undef CM_R16
+
+template <int W>
+__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[W]) {
+    if constexpr (W == 32) tmem_ld32(taddr, r);
+    else tmem_ld16(taddr, r);
+}
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 constexpr uint32_t GROUP_M = 8;
@@ -258,8 +279,9 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
 //   warp 0      TMA producer (continuous stage ring across tiles)
 //   warp 1      TMEM owner; lane 0 (of the pair's even CTA) issues the MMAs of each
 //               tile into an accumulator buffer once the epilogue has drained it
-//   warps 2-9   epilogue: warp w reads TMEM lanes 32*(w%4).. of column half (w-2)/4,
-//               combines the four accumulators into registers, releases the buffer,
+//   warps 2-17  epilogue: warp w reads TMEM lanes 32*(w%4).. of column group (w-2)/4,
+//               combines the four accumulators
+//               into registers, releases the buffer,
 //               then adds the rank-1 terms, narrows and stores while the next
 //               tile's MMAs run.
 // CTA pairs (tcgen05 cta_group::2, M = 256): each CTA loads its own 128 rows of A
@@ -271,11 +293,12 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
 // even CTA's barriers; its MMA commits arrive on both CTAs' barriers (multicast
 // commit).  No TMA multicast is used.
 template <int TBN, int CG>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
     using C = Cfg<TBN, CG>;
     constexpr int STAGES = C::STAGES, NBUF = C::NBUF;
-    constexpr uint32_t HALF = TBN / 2;                  // columns per epilogue warp
+    constexpr uint32_t HALF = TBN / (C::EPI_WARPS / 4);  // columns per epilogue warp
+    constexpr uint32_t CW = 16;                           // columns per TMEM load
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint64_t* bars = (uint64_t*)(smem + STAGES * C::STAGE);
@@ -302,7 +325,7 @@ __global__ void __launch_bounds__(320, 1)
         }
         for (int b = 0; b < NBUF; ++b) {
             mbar_init(smem_u32(&accf_b[b]), 1);
-            mbar_init(smem_u32(&acce_b[b]), 8 * CG);
+            mbar_init(smem_u32(&acce_b[b]), C::EPI_WARPS * CG);
         }
         mbar_init(smem_u32(done_b), 1);
         *abort_flag = 0;
@@ -466,23 +489,23 @@ __global__ void __launch_bounds__(320, 1)
             uint32_t pk[HALF / 2];
             const uint32_t tl = tmem + buf * C::ACC_COLS + ((quarter * 32u) << 16) + cbase;
 #pragma unroll
-            for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+            for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
                 const uint32_t col0 = tc.n0 + cbase + c0;
                 if (col0 < g.cols) {
-                    uint32_t p[32], q[32];
-                    tmem_ld32(tl + c0, p);
-                    tmem_ld32(tl + TBN + c0, q);
+                    uint32_t p[CW], q[CW];
+                    tmem_ld<CW>(tl + c0, p);
+                    tmem_ld<CW>(tl + TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) p[k] = (p[k] << 8) + q[k];
-                    tmem_ld32(tl + 2 * TBN + c0, q);
+                    for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
+                    tmem_ld<CW>(tl + 2 * TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) p[k] = (p[k] + q[k]) << 8;
-                    tmem_ld32(tl + 3 * TBN + c0, q);
+                    for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] + q[k]) << 8;
+                    tmem_ld<CW>(tl + 3 * TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int k = 0; k < 32; k += 2) {
+                    for (int k = 0; k < (int)CW; k += 2) {
                         const uint32_t ca = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
                         const uint32_t cb = col0 + k + 1 < g.cols ? (uint32_t)__ldg(ct + col0 + k + 1) : 0u;
                         const uint16_t lo = (uint16_t)narrow_acc(p[k] + q[k] + rt + ca);
@@ -499,14 +522,17 @@ __global__ void __launch_bounds__(320, 1)
             }
             if (!valid) continue;
             int16_t* orow = g.out + o_off;
-            if (g.epi) {
+            if (g.epi == 1u) {
+#pragma unroll
+                for (uint32_t q = 0; q < HALF / 2; ++q) pk[q] = __vmaxs2(pk[q], 0u);   // ReLU on both halfwords
+            } else if (g.epi) {
                 const int16_t* rrow = g.resid + o_off;
 #pragma unroll
-                for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
                     const uint32_t col0 = tc.n0 + cbase + c0;
                     if (col0 >= g.cols) break;
 #pragma unroll
-                    for (int k = 0; k < 32; k += 2) {
+                    for (int k = 0; k < (int)CW; k += 2) {
                         int32_t v0 = (int16_t)(pk[(c0 + k) / 2] & 0xFFFFu), v1 = (int16_t)(pk[(c0 + k) / 2] >> 16);
                         if (g.epi & 2u) {
                             if (col0 + k < g.cols) v0 = sat16(v0 + (int32_t)rrow[(uint64_t)(col0 + k) * g.ldc]);
@@ -521,7 +547,7 @@ __global__ void __launch_bounds__(320, 1)
                 }
             }
 #pragma unroll
-            for (uint32_t c0 = 0; c0 < HALF; c0 += 32) {
+            for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
                 const uint32_t col0 = tc.n0 + cbase + c0;
                 if (col0 >= g.cols) break;
                 int16_t* dst = orow + col0;
@@ -529,18 +555,18 @@ __global__ void __launch_bounds__(320, 1)
                     // column-strided output (conv: y[m][p] with rows = pixels): each
                     // store is coalesced across the warp's consecutive rows
 #pragma unroll
-                    for (int k = 0; k < 32; ++k)
+                    for (int k = 0; k < (int)CW; ++k)
                         if (col0 + k < g.cols)
                             orow[(uint64_t)(col0 + k) * g.ldc] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
-                } else if (col0 + 32 <= g.cols && ((uintptr_t)dst & 15u) == 0) {
+                } else if (col0 + CW <= g.cols && ((uintptr_t)dst & 15u) == 0) {
                     uint4* d4 = (uint4*)dst;
 #pragma unroll
-                    for (int q = 0; q < 4; ++q)
+                    for (int q = 0; q < (int)CW / 8; ++q)
                         d4[q] = make_uint4(pk[c0 / 2 + 4 * q], pk[c0 / 2 + 4 * q + 1], pk[c0 / 2 + 4 * q + 2],
                                            pk[c0 / 2 + 4 * q + 3]);
                 } else {
 #pragma unroll
-                    for (int k = 0; k < 32; ++k)
+                    for (int k = 0; k < (int)CW; ++k)
                         if (col0 + k < g.cols) dst[k] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
                 }
             }
@@ -823,7 +849,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * n);
-            q.blockDim = dim3(320);
+            q.blockDim = dim3(Cfg<TBN, CG>::THREADS);
             q.dynamicSmemBytes = SMEM_BYTES;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
@@ -846,12 +872,12 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            gemm_q88_kernel<TBN, CG><<<clusters, 320, SMEM_BYTES, s>>>(ta, tb, g);
+            gemm_q88_kernel<TBN, CG><<<clusters, Cfg<TBN, CG>::THREADS, SMEM_BYTES, s>>>(ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * clusters);
-            q.blockDim = dim3(320);
+            q.blockDim = dim3(Cfg<TBN, CG>::THREADS);
             q.dynamicSmemBytes = SMEM_BYTES;
             q.stream = s;
             cudaLaunchAttribute at{};

@@ -199,14 +199,12 @@ def _inputs(node) -> list:
     return [n for n in names if n is not None]
 
 
-def fuse(net: Net, residual: bool = False) -> Net:
-    """The call list with Conv -> Relu chains (and, with residual=True, Conv -> Add and
-    Conv -> Add -> Relu chains) folded into one conv call with a fused epilogue
+def fuse(net: Net, residual: bool = True) -> Net:
+    """The call list with Conv -> Relu chains and (residual=True) Conv -> Add and
+    Conv -> Add -> Relu chains folded into one conv call with a fused epilogue
     (cm_conv_fused): the same words, without writing and re-reading the intermediate
     tensors.  A chain is folded only when each intermediate result has no other reader
-    (and is not the network output).  The residual form reads the other Add operand in
-    the GEMM epilogue one 64-byte channel segment at a time, which on B200 costs more
-    than the separate Add pass it saves for the ResNet-18 shapes, so it is off by default."""
+    (and is not the network output)."""
     R = net.resolve
     reads: dict = {}
     for node in net.nodes:
