@@ -1,0 +1,164 @@
+"""The generated C project (cormorant_b200.codegen): the reference scheduler's
+inference.h / inference.c / test_inference.c layout with libcormorant_cuda.so as the
+backend.  CPU tests check the buffer plan, the emitted API and files, and that the
+project compiles with -Werror and links; GPU tests compile and run it and compare the
+network output for the reference's ramp input with the oracle, word for word (the
+reference's own generated GT check, inference-scheduler/src/codegen/_test.py)."""
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from cormorant_b200 import codegen, networks
+from tests.test_networks import OracleBackend, cpu_buffers
+
+ROOT = Path(__file__).resolve().parent.parent
+LIB = ROOT / "cormorant_b200" / "libcormorant_cuda.so"
+INCLUDE = ROOT / "include"
+
+NETS = {
+    "lenet5": lambda: networks.lenet5(),
+    "lenet5_b3": lambda: networks.lenet5(batch=3),
+    "resnet18_b2": lambda: networks.resnet18(batch=2),
+}
+
+
+def _net(name, fused):
+    net = NETS[name]()
+    return networks.fuse(net) if fused else net
+
+
+def _expected(net, port):
+    bufs = cpu_buffers(net, codegen.ramp_input(net))
+    networks.execute(net, OracleBackend(port), bufs)
+    return bufs[net.resolve(net.output)].copy()
+
+
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("name", list(NETS))
+def test_layout_never_overlaps_live_tensors(name, fused):
+    """Two intermediates that are live at the same node never share a word of the pool."""
+    net = _net(name, fused)
+    L = codegen.plan_layout(net)
+    io = {net.resolve(net.input), net.resolve(net.output)}
+    inter = {net.resolve(codegen._output(n)) for n in net.nodes} - io
+    assert set(L.acts) == inter
+    items = list(L.acts.items())
+    for name_a, (oa, wa) in items:
+        assert oa % codegen.ALIGN_WORDS == 0 and oa + wa <= L.act_words
+        fa, la = L.live[name_a]
+        for name_b, (ob, wb) in items:
+            if name_a >= name_b:
+                continue
+            fb, lb = L.live[name_b]
+            if fa <= lb and fb <= la:           # live ranges meet
+                assert oa + wa <= ob or ob + wb <= oa, (name_a, name_b)
+    # weights: back to back, aligned, disjoint
+    spans = sorted(L.weights.values())
+    for (o1, w1), (o2, _) in zip(spans, spans[1:]):
+        assert o1 % codegen.ALIGN_WORDS == 0 and o1 + w1 <= o2
+    assert L.act_words <= sum(codegen._align(net.buffers[n]) for n in L.acts)
+
+
+def test_layout_reuses_memory_on_resnet():
+    net = networks.fuse(networks.resnet18(batch=2))
+    L = codegen.plan_layout(net)
+    total = sum(net.buffers[n] for n in L.acts)
+    assert L.act_words < total / 2
+
+
+def test_emitted_api_and_weight_files(tmp_path):
+    net = networks.fuse(networks.lenet5())
+    out = net.resolve(net.output)
+    exp = np.arange(10, dtype=np.int16)
+    files = codegen.emit_project(net, tmp_path, expected=exp)
+    h = (tmp_path / "include/inference.h").read_text()
+    for sym in ("typedef int16_t Data_t;", "INFERENCE_BYTES_PER_ELEM  2u", "inference_buf_alloc(unsigned n_elem)",
+                "inference_buf_init_view(", "inference_buf_sync_to_device(", "inference_buf_fill_float(",
+                "INFERENCE_BUF_POOL_SIZE_BYTES", "int  inference_init(const char *vectoropkernel_instance,",
+                "const char *matmulkernel_instance", "const char *convkernel_instance",
+                "const char *poolingkernel_instance", "void inference_deinit(void);",
+                f"int inference_run(inference_buf_t *in_x, inference_buf_t *out_{out});",
+                "#define INFERENCE_X_SIZE  784u", f"#define INFERENCE_{out.upper()}_SIZE  10u"):
+        assert sym in h, sym
+    src = (tmp_path / "src/inference.c").read_text()
+    assert src.count("cm_conv_fused_async(") == 2             # Conv+Relu twice
+    assert src.count("cm_matmul_async(") == 3 and src.count("cm_pool_async(") == 2
+    assert src.count("CHECK(cm_synchronize(NULL));") == 1
+    # weights above the threshold go to .dat files (raw little-endian words), the rest inline
+    for name, arr in net.consts.items():
+        dat = tmp_path / "weights" / f"{name}.dat"
+        if arr.size > codegen.LARGE_WEIGHT_THRESHOLD:
+            assert dat.read_bytes() == np.asarray(arr, "<i2").tobytes()
+            assert f'_load_weight(&w_{name}, "{name}")' in src
+        else:
+            assert not dat.exists() and f"static const Data_t {name}_init[{arr.size}]" in src
+    assert "test/test_inference.c" in files and "expected" not in " ".join(files)
+
+
+def test_large_expected_goes_to_dat(tmp_path):
+    net = networks.fuse(networks.resnet18(batch=5))
+    exp = np.arange(5000, dtype=np.int16)
+    codegen.emit_project(net, tmp_path, expected=exp)
+    out = net.resolve(net.output)
+    assert (tmp_path / "expected" / f"{out}.dat").read_bytes() == exp.astype("<i2").tobytes()
+    t = (tmp_path / "test/test_inference.c").read_text()
+    assert f'_load_expected(&exp_heap, "{out}"' in t
+    with pytest.raises(ValueError):
+        codegen.emit_project(net, tmp_path / "bad", expected=exp[:10])
+
+
+def test_ramp_input_matches_reference_fill():
+    net = networks.lenet5(batch=100)                       # 78400 words: wraps past 0xFFFF
+    r = codegen.ramp_input(net)
+    assert r.dtype == np.int16 and r.size == 78400
+    assert r[0] == 0 and r[255] == 255 and r[32768] == -32768 and r[65535] == -1 and r[65536] == 0
+
+
+@pytest.mark.skipif(not LIB.exists(), reason="libcormorant_cuda.so not built")
+@pytest.mark.parametrize("fused", [False, True])
+def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, fused):
+    """gcc -Wall -Wextra -Werror over the generated sources, linked against the library;
+    with no GPU visible inference_init reports the failure and the test binary exits 1."""
+    net = _net("resnet18_b2", fused)
+    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
+    exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is visible: the run itself is covered by the gpu tests")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 1
+    assert "inference_init" in r.stderr and "cm_init" in r.stderr
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("name", list(NETS))
+def test_generated_project_bit_exact_on_gpu(tmp_path, port, name, fused):
+    net = _net(name, fused)
+    exp = _expected(net, port)
+    codegen.emit_project(net, tmp_path, expected=exp)
+    exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
+    r = subprocess.run([str(exe), "20"], capture_output=True, text=True, timeout=600, cwd=tmp_path)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "test_inference PASSED" in r.stdout and "timing: 20 runs" in r.stdout
+
+
+@pytest.mark.gpu
+def test_generated_project_reports_missing_weights_and_mismatch(tmp_path, port):
+    net = networks.fuse(networks.lenet5())
+    exp = _expected(net, port)
+    exp_bad = exp.copy()
+    exp_bad[3] ^= 1
+    codegen.emit_project(net, tmp_path, expected=exp_bad)
+    exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "test_inference FAILED (1 mismatches)" in r.stdout
+    out = net.resolve(net.output)
+    assert f"GT MISMATCH {out}[3]" in r.stderr
+    big = next(n for n, a in net.consts.items() if a.size > codegen.LARGE_WEIGHT_THRESHOLD)
+    os.remove(tmp_path / "weights" / f"{big}.dat")
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and "cannot open weight file" in r.stderr
