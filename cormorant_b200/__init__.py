@@ -9,5 +9,6 @@ batch-sharded multi-GPU driver (``sharding``).
 from ._lib import CormorantError, lib  # noqa: F401
 from .kernels import (  # noqa: F401
     OP_ADD, OP_DIV, OP_MUL, OP_RELU, OP_RELU6, OP_SUB, POOL_AVG, POOL_LP, POOL_MAX,
-    ConvKernel, MatmulKernel, PoolingKernel, VectorOPKernel, init, launch_count, release, synchronize,
+    ConvKernel, ConvKernelFused, MatmulKernel, MatmulKernelFused, PoolingKernel, VectorOPKernel, init,
+    launch_count, release, synchronize,
 )

@@ -40,6 +40,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_vectorop_async": (C.c_int, [_p, _p, _p] + [_u] * 5 + [_p]),
     "cm_matmul": (C.c_int, [_p, _p, _p] + [_u] * 7),
     "cm_matmul_async": (C.c_int, [_p, _p, _p] + [_u] * 7 + [_p]),
+    "cm_matmul_fused": (C.c_int, [_p, _p, _p] + [_u] * 8 + [_p]),
+    "cm_matmul_fused_async": (C.c_int, [_p, _p, _p] + [_u] * 8 + [_p, _p]),
     "cm_matmul_at": (C.c_int, [_p, _u, _p, _u, _p, _u] + [_u] * 7),
     "cm_matmul_noalloc": (C.c_int, [_p, _p, _p] + [_u] * 7 + [_p]),
     "cm_conv": (C.c_int, [_p, _p, _p, _p] + [_u] * 17),

@@ -48,7 +48,7 @@ from pathlib import Path
 
 import numpy as np
 
-from .networks import Net, _inputs
+from .networks import Net, _inputs, output_of as _output
 
 LARGE_WEIGHT_THRESHOLD = 4096          # inference-scheduler/src/tensor.py:35
 LARGE_EXPECTED_THRESHOLD = 4096        # inference-scheduler/src/codegen/_simulate.py:190
@@ -65,10 +65,6 @@ _OP_NAMES = {0: "ADD", 1: "SUB", 2: "MUL", 3: "DIV", 4: "RELU", 5: "RELU6"}
 
 def _align(n: int) -> int:
     return (n + ALIGN_WORDS - 1) // ALIGN_WORDS * ALIGN_WORDS
-
-
-def _output(node) -> str:
-    return node[4] if node[0] == "conv" else node[3] if node[0] in ("vectorop", "matmul") else node[2]
 
 
 @dataclass
@@ -165,7 +161,9 @@ class _Emitter:
         self.net = net
         self.R = net.resolve
         self.layout = plan_layout(net)
-        kinds = {n[0] for n in net.nodes}
+        # one init parameter per kernel of the unfused call list, as the reference's
+        # generated header has, so the signature does not change with fusion
+        kinds = set(net.source_kinds) or {n[0] for n in net.nodes}
         self.kernels = [k for k in KERNELS if k[0] in kinds]
         self.lib_path = lib_path
         self.in_c, self.out_c = self.R(net.input), self.R(net.output)
@@ -294,6 +292,13 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             return (f"    /* {i}: VectorOP {_OP_NAMES.get(int(args[1]), args[1])} -> {self.R(c_)} */\n"
                     f"    CHECK(cm_vectorop_async({self._dev(a_)}, {self._dev(b_)}, {self._dev(c_, False)}, "
                     f"{a}, NULL));")
+        if kind == "matmul" and len(node) > 5:
+            _, a_, b_, c_, args, epi, bias = node
+            a = ", ".join(f"{int(v)}u" for v in args)
+            what = "MatMul" + ("+Add" if epi & 2 else "") + ("+Relu" if epi & 1 else "")
+            return (f"    /* {i}: {what} -> {self.R(c_)} */\n"
+                    f"    CHECK(cm_matmul_fused_async({self._dev(a_)}, {self._dev(b_)}, {self._dev(c_, False)}, "
+                    f"{a}, {int(epi)}u, {self._dev(bias)}, NULL));")
         if kind == "matmul":
             _, a_, b_, c_, args = node
             a = ", ".join(f"{int(v)}u" for v in args)

@@ -190,6 +190,63 @@ __global__ void __launch_bounds__(256) conv_nhwc_split_kernel(const int16_t* __r
     if (qp < HWp) S[(uint64_t)n * HWp + qp] = sum;
 }
 
+// Whole-image variant for small maps whose H*W is not a multiple of 4 (7x7, 9x9 ...):
+// block = one image.  Its C*H*W words are one contiguous run, read into shared memory
+// with 4-byte loads (2-byte when the run is not 4-byte aligned); then item (padded
+// pixel, 16 channels) -- consecutive threads take consecutive 16-channel groups, so
+// the 16-byte hi / lo stores of a pixel are contiguous -- converts its 16 words, and
+// the channel sums meet by shared-memory atomics.  Every padded pixel is written
+// (the frame as x = 0), so no border pass follows.
+constexpr uint32_t kImgSplitThreads = 512;
+constexpr uint32_t kImgSplitSmem = 100u * 1024u;
+
+__global__ void __launch_bounds__(kImgSplitThreads) conv_nhwc_split_img_kernel(const int16_t* __restrict__ x, NhwcGeom g,
+                                                                               int8_t* __restrict__ planes,
+                                                                               int32_t* __restrict__ S) {
+    extern __shared__ __align__(16) uint8_t img_smem[];
+    const uint32_t HW = g.H * g.W, words = g.C * HW;
+    int16_t* img = (int16_t*)img_smem;
+    int32_t* ssum = (int32_t*)(img_smem + (((uint64_t)words * 2 + 15) & ~15ull));
+    const uint32_t n = blockIdx.x;
+    const uint32_t HWp = g.Hp * g.Wp;
+    const int16_t* xi = x + (uint64_t)n * words;
+    if ((((uintptr_t)xi) & 3u) == 0) {
+        const uint32_t* x4 = (const uint32_t*)xi;
+        uint32_t* i4 = (uint32_t*)img;
+        for (uint32_t i = threadIdx.x; i < words / 2; i += blockDim.x) i4[i] = __ldg(x4 + i);
+        if ((words & 1u) && threadIdx.x == 0) img[words - 1] = __ldg(xi + words - 1);
+    } else {
+        for (uint32_t i = threadIdx.x; i < words; i += blockDim.x) img[i] = __ldg(xi + i);
+    }
+    for (uint32_t p = threadIdx.x; p < HWp; p += blockDim.x) ssum[p] = 0;
+    __syncthreads();
+    const uint64_t plane = (uint64_t)g.nimg * HWp * g.Cp;
+    const uint32_t groups = g.Cp / 16, items = HWp * groups;
+    for (uint32_t it = threadIdx.x; it < items; it += blockDim.x) {
+        const uint32_t p = it / groups, grp = it - p * groups;
+        const uint32_t hp = p / g.Wp, wp = p - hp * g.Wp;
+        const int32_t ih = (int32_t)hp - (int32_t)g.pt, iw = (int32_t)wp - (int32_t)g.pl;
+        const bool inside = ih >= 0 && ih < (int32_t)g.H && iw >= 0 && iw < (int32_t)g.W;
+        const uint32_t pix = inside ? (uint32_t)ih * g.W + (uint32_t)iw : 0u;
+        uint32_t hw[4] = {0, 0, 0, 0}, lw[4] = {0, 0, 0, 0};
+        int32_t sum = 0;
+#pragma unroll
+        for (uint32_t j = 0; j < 16; ++j) {
+            const uint32_t c = grp * 16 + j;
+            const int16_t v = (inside && c < g.C) ? img[c * HW + pix] : (int16_t)0;
+            hw[j / 4] |= (uint32_t)(uint8_t)(v >> 8) << (8 * (j % 4));
+            lw[j / 4] |= (((uint32_t)v & 255u) ^ 0x80u) << (8 * (j % 4));
+            if (c < g.C) sum += (int32_t)v - 128;
+        }
+        int8_t* dst = planes + ((uint64_t)n * HWp + p) * g.Cp + grp * 16;
+        *(uint4*)dst = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+        *(uint4*)(dst + plane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        atomicAdd(&ssum[p], sum);
+    }
+    __syncthreads();
+    for (uint32_t p = threadIdx.x; p < HWp; p += blockDim.x) S[(uint64_t)n * HWp + p] = ssum[p];
+}
+
 // Four-pixel variant (H*W a multiple of 4, 8-byte aligned input): block = 256
 // consecutive input pixels of one image (64 quads), channels in tiles of 32.
 // Load: thread = (quad, channel), one 8-byte read of 4 pixels of a channel row.
@@ -719,6 +776,85 @@ __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __re
     }
 }
 
+// Row form of the same conversion for fixed S_, C_: block = virtual row hv of one image
+// (grid (Hs, images)).  The S_ x C_ input rows it covers are staged in shared memory with
+// coalesced loads (rows outside the image as zeros), then thread wv converts virtual pixel
+// (hv, wv): no divisions, shared-memory reads, So written as one S_-word run per
+// original row.  S_*C_*W words fit in kS2dRowSmem.
+constexpr uint32_t kS2dRowThreads = 128;
+constexpr uint32_t kS2dRowSmem = 32u * 1024u;
+
+template <int S_, int C_>
+__global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int16_t* __restrict__ x, S2dGeom g,
+                                                                        int8_t* __restrict__ planes,
+                                                                        int32_t* __restrict__ So) {
+    static_assert(S_ >= 2 && S_ * S_ * C_ <= 64, "space-to-depth channels");
+    constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (C2 + 15u) / 16u * 16u;
+    extern __shared__ __align__(16) int16_t rowbuf[];      // [S_ * C_][W]
+    const uint32_t hv = blockIdx.x, n = blockIdx.y;
+    const uint32_t W = g.W;
+    const int16_t* xn = x + (uint64_t)n * C_ * g.H * W;
+    const bool pairs = (W & 1u) == 0 && (((uintptr_t)x) & 3u) == 0;
+#pragma unroll
+    for (uint32_t r = 0; r < (uint32_t)(S_ * C_); ++r) {
+        const uint32_t th = r / C_, c = r % C_;
+        const int32_t ih = (int32_t)(S_ * hv + th) - (int32_t)g.pt;
+        int16_t* dst = rowbuf + r * W;
+        if (ih >= 0 && ih < (int32_t)g.H) {
+            const int16_t* src = xn + ((uint64_t)c * g.H + (uint32_t)ih) * W;
+            if (pairs) {
+                for (uint32_t i = threadIdx.x; i < W / 2; i += blockDim.x)
+                    ((uint32_t*)dst)[i] = __ldg((const uint32_t*)src + i);
+            } else {
+                for (uint32_t i = threadIdx.x; i < W; i += blockDim.x) dst[i] = __ldg(src + i);
+            }
+        } else {
+            for (uint32_t i = threadIdx.x; i < W; i += blockDim.x) dst[i] = 0;
+        }
+    }
+    __syncthreads();
+    const uint64_t plane = (uint64_t)g.nimg * g.Hs * g.Ws * g.Cp;
+    for (uint32_t wv = threadIdx.x; wv < g.Ws; wv += blockDim.x) {
+        uint32_t hw[CPC / 4], lw[CPC / 4];
+#pragma unroll
+        for (uint32_t q = 0; q < CPC / 4; ++q) { hw[q] = 0; lw[q] = 0x80808080u; }
+#pragma unroll
+        for (uint32_t th = 0; th < (uint32_t)S_; ++th) {
+            int32_t sums[S_];
+#pragma unroll
+            for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) {
+                const int32_t iw = (int32_t)(S_ * wv + tw) - (int32_t)g.pl;
+                const bool in = iw >= 0 && iw < (int32_t)W;
+                int32_t sum = 0;
+#pragma unroll
+                for (uint32_t c = 0; c < (uint32_t)C_; ++c) {
+                    const uint32_t c2 = (th * S_ + tw) * C_ + c;
+                    const int16_t v = in ? rowbuf[(th * C_ + c) * W + (uint32_t)iw] : (int16_t)0;
+                    sum += (int32_t)v - 128;
+                    const uint32_t q = c2 >> 2, sh = 8 * (c2 & 3);
+                    hw[q] |= (uint32_t)(uint8_t)(v >> 8) << sh;
+                    lw[q] = (lw[q] & ~(0xFFu << sh)) | ((((uint32_t)v & 255u) ^ 0x80u) << sh);
+                }
+                sums[tw] = sum;
+            }
+            int32_t* so = So + ((uint64_t)n * g.Hpo + S_ * hv + th) * g.Wpo + S_ * wv;
+            if constexpr (S_ == 2) {
+                *(int2*)so = make_int2(sums[0], sums[1]);
+            } else {
+#pragma unroll
+                for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) so[tw] = sums[tw];
+            }
+        }
+        int8_t* dst = planes + (((uint64_t)n * g.Hs + hv) * g.Ws + wv) * g.Cp;
+#pragma unroll
+        for (uint32_t c0 = 0; c0 < CPC; c0 += 16) {
+            const uint32_t q = c0 / 4;
+            *(uint4*)(dst + c0) = make_uint4(hw[q], hw[q + 1], hw[q + 2], hw[q + 3]);
+            *(uint4*)(dst + plane + c0) = make_uint4(lw[q], lw[q + 1], lw[q + 2], lw[q + 3]);
+        }
+    }
+}
+
 // Virtual weights -> N-major planes (layout as conv_weights_kernel): row
 // k' = r'*KR_pad + u'*Cp + (th*s + tw)*C + c holds w[m][c][s*r' + th][s*u' + tw], zero past
 // the original kernel.  Thread per (k', m); the weights are small.
@@ -846,6 +982,17 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
                 ProfScope ps_(PK_SPLIT, s);
                 const uint64_t HW = (uint64_t)in_h * in_w;
                 const bool quads = HW % 4 == 0 && ((uintptr_t)x & 7u) == 0 && HW < (1ull << 31);
+                const uint64_t img_smem = (((uint64_t)in_ch * HW * 2 + 15) & ~15ull) + (uint64_t)ip.Hp * ip.Wp * 4;
+                const bool whole = !quads && img_smem <= kImgSplitSmem;
+                if (whole) {
+                    static bool attr = false;
+                    if (!attr) {
+                        cudaError_t e = cudaFuncSetAttribute(conv_nhwc_split_img_kernel,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kImgSplitSmem);
+                        if (e != cudaSuccess) { scratch_free(scratch, s); return cuda_error(e, "cudaFuncSetAttribute(split_img)"); }
+                        attr = true;
+                    }
+                }
                 const uint32_t gx = quads ? (uint32_t)((HW / 4 + 63) / 64)
                                           : (uint32_t)(((uint64_t)ip.Hp * ip.Wp + kNhwcPix - 1) / kNhwcPix);
                 for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
@@ -856,6 +1003,9 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
                     int32_t* Sb = S + (uint64_t)b0 * ip.Hp * ip.Wp;
                     if (quads) {
                         conv_nhwc_split4_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+                        count_launch();
+                    } else if (whole) {
+                        conv_nhwc_split_img_kernel<<<bz, kImgSplitThreads, (size_t)img_smem, s>>>(xb, ng, pb, Sb);
                         count_launch();
                     } else {
                         conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
@@ -936,13 +1086,25 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
             {
                 ProfScope ps_(PK_SPLIT, s);
                 const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
-                if (sp.s == 2 && in_ch == 3)
+                const uint64_t row_smem = (uint64_t)sp.s * in_ch * in_w * 2;
+                if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
+                    for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
+                        const uint32_t bz = std::min(65535u, nb - b0);
+                        // images b0..: shift the input, planes and So bases; the plane stride stays the chunk's
+                        conv_s2d_rows_kernel<2, 3><<<dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s>>>(
+                            xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so);
+                        count_launch();
+                    }
+                } else if (sp.s == 2 && in_ch == 3) {
                     conv_s2d_split_kernel<2, 3><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
-                else
+                    count_launch();
+                } else {
                     conv_s2d_split_kernel<0, 0><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
+                    count_launch();
+                }
                 conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s,
                                                                             sp.s, 1, tot, rt);
-                count_launch(2);
+                count_launch();
             }
             const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh2, 1, 1, 1,
                            out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};

@@ -232,7 +232,8 @@ struct GemmArgs {
     uint32_t rows_per_img;
     uint32_t ksteps;          // 32-deep MMA steps covering K (conv: covering one kernel row's KR bytes)
     // fused elementwise epilogue on the narrowed word v (bit 1: v = sat16(v + resid at the
-    // output's index), then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
+    // output's index); bit 2: v = sat16(v + resid[col]), a bias row broadcast over the
+    // rows; then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
     uint32_t epi;
     const int16_t* resid;
 };
@@ -452,14 +453,9 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
         uint32_t j = 0;
         for (uint64_t t = cid; t < total; t += ncl, ++j) {
             const uint32_t buf = j % NBUF, use = j / NBUF;
-            // One lane waits; the verdict is broadcast so that the .sync.aligned
-            // TMEM loads below are executed by the whole warp or not at all.
-            uint32_t ok = 0;
-            if (lane == 0) ok = (mbar_wait(smem_u32(&accf_b[buf]), use & 1u, wc) && !*abort_flag) ? 1u : 0u;
-            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
-            __syncwarp();
-            if (!ok) break;
-            tc_fence_after();
+            // Everything that does not depend on the accumulator is fetched before the
+            // wait, while the tile's MMAs run: the row's output offset, its row term and
+            // the epilogue's addends (residual words or the bias row), packed in pairs.
             const Tile tc = decode_tile<TBN, CG>(g, t, rank);
             bool valid;
             uint64_t rt_idx, o_off;
@@ -483,6 +479,27 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                 }
             }
             const uint32_t rt = valid ? (uint32_t)__ldg(g.rowterm + rt_idx) : 0u;
+            uint32_t addv[HALF / 2];                      // addend pairs (even column in the low half)
+            if (g.epi & 6u) {
+                const bool res = (g.epi & 2u) != 0u;
+                const int16_t* src = res ? g.resid + o_off : g.resid;
+                const uint64_t step = res ? g.ldc : 1u;
+#pragma unroll
+                for (uint32_t q = 0; q < HALF / 2; ++q) {
+                    const uint32_t col = tc.n0 + cbase + 2 * q;
+                    const uint32_t a0 = valid && col < g.cols ? (uint16_t)__ldg(src + (uint64_t)col * step) : 0u;
+                    const uint32_t a1 = valid && col + 1 < g.cols ? (uint16_t)__ldg(src + (uint64_t)(col + 1) * step) : 0u;
+                    addv[q] = a0 | (a1 << 16);
+                }
+            }
+            // One lane waits; the verdict is broadcast so that the .sync.aligned
+            // TMEM loads below are executed by the whole warp or not at all.
+            uint32_t ok = 0;
+            if (lane == 0) ok = (mbar_wait(smem_u32(&accf_b[buf]), use & 1u, wc) && !*abort_flag) ? 1u : 0u;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            __syncwarp();
+            if (!ok) break;
+            tc_fence_after();
             const int32_t* ct = g.colterm + (uint64_t)tc.bb * g.cols;
             // Drain: acc = 2^16*HH + 2^8*(HL + LH) + LL + rowterm + colterm, narrowed
             // and packed two int16 per word (even column in the low half).
@@ -522,29 +539,14 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
             }
             if (!valid) continue;
             int16_t* orow = g.out + o_off;
-            if (g.epi == 1u) {
+            // VectorOP ADD (saturating) and RELU on both halfwords of each pair
+            if (g.epi & 6u) {
 #pragma unroll
-                for (uint32_t q = 0; q < HALF / 2; ++q) pk[q] = __vmaxs2(pk[q], 0u);   // ReLU on both halfwords
-            } else if (g.epi) {
-                const int16_t* rrow = g.resid + o_off;
+                for (uint32_t q = 0; q < HALF / 2; ++q) pk[q] = __vaddss2(pk[q], addv[q]);
+            }
+            if (g.epi & 1u) {
 #pragma unroll
-                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
-                    const uint32_t col0 = tc.n0 + cbase + c0;
-                    if (col0 >= g.cols) break;
-#pragma unroll
-                    for (int k = 0; k < (int)CW; k += 2) {
-                        int32_t v0 = (int16_t)(pk[(c0 + k) / 2] & 0xFFFFu), v1 = (int16_t)(pk[(c0 + k) / 2] >> 16);
-                        if (g.epi & 2u) {
-                            if (col0 + k < g.cols) v0 = sat16(v0 + (int32_t)rrow[(uint64_t)(col0 + k) * g.ldc]);
-                            if (col0 + k + 1 < g.cols) v1 = sat16(v1 + (int32_t)rrow[(uint64_t)(col0 + k + 1) * g.ldc]);
-                        }
-                        if (g.epi & 1u) {
-                            v0 = max(v0, 0);
-                            v1 = max(v1, 0);
-                        }
-                        pk[(c0 + k) / 2] = (uint32_t)(uint16_t)v0 | ((uint32_t)(uint16_t)v1 << 16);
-                    }
-                }
+                for (uint32_t q = 0; q < HALF / 2; ++q) pk[q] = __vmaxs2(pk[q], 0u);
             }
 #pragma unroll
             for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
@@ -710,10 +712,11 @@ __global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict
 // <= 32) take the k products q = lane, lane + G, ...; their int32 wrap sums
 // meet by shuffle (addition mod 2^32 is order-free, so the result is the exact
 // reference sum) and one narrowing follows (MatmulKernel.cpp:204-218).
+// epi: bit 1 adds bias[j] (saturating), bit 0 applies ReLU, after the narrowing.
 __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b,
                                                             int16_t* __restrict__ c, uint32_t n, uint32_t k, uint32_t m,
                                                             uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, uint64_t total,
-                                                            uint32_t G) {
+                                                            uint32_t G, uint32_t epi, const int16_t* __restrict__ bias) {
     const uint64_t nm = (uint64_t)n * m;
     const uint32_t g = threadIdx.x & (G - 1);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / G;
@@ -730,7 +733,12 @@ __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __res
         if (live)
             for (uint32_t q = g; q < k; q += G) acc += (uint32_t)((int32_t)__ldg(ar + q) * (int32_t)__ldg(bc + (uint64_t)q * m));
         for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-        if (live && g == 0) c[z * c_bs + (uint64_t)i * m + j] = narrow_acc(acc);
+        if (live && g == 0) {
+            int32_t v = narrow_acc(acc);
+            if (epi & 2u) v = sat16(v + (int32_t)__ldg(bias + j));
+            if (epi & 1u) v = max(v, 0);
+            c[z * c_bs + (uint64_t)i * m + j] = (int16_t)v;
+        }
     }
 }
 
@@ -1038,39 +1046,51 @@ using namespace cm;
 // ---------------------------------------------------------------------------
 // MatmulKernel entry (MatmulKernel.h:68-79)
 // ---------------------------------------------------------------------------
-extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
-                               unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
-                               unsigned c_batch_stride, cm_stream_t stream) {
+namespace {
+// MatMul with an optional fused epilogue (epi bit 1: + bias[j] saturating, bit 0: ReLU).
+int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m, unsigned batch,
+                unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride, unsigned epi,
+                const int16_t* bias, cudaStream_t s) {
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
+    if (epi > 3u) return set_error(CM_EINVAL, "cm_matmul_fused: epilogue %u (0..3)", epi);
+    if ((epi & 2u) && !bias) return set_error(CM_EINVAL, "cm_matmul_fused: null bias");
     if (n == 0 || m == 0 || batch == 0) return CM_OK;
     if (!c || (k > 0 && (!a || !b))) return set_error(CM_EINVAL, "cm_matmul: null buffer");
-    cudaStream_t s = (cudaStream_t)stream;
     if (batch > 1 && (uint64_t)c_batch_stride < (uint64_t)n * m) {
         // Output slices of different batch steps overlap; the reference's batch
         // loop runs in order (MatmulKernel.cpp:108-112), so later steps win.
         if (c_batch_stride == 0) {
             const uint64_t last = batch - 1;
-            return cm_matmul_async(a ? a + last * a_batch_stride : a, b ? b + last * b_batch_stride : b, c, n, k,
-                                   m, 1, a_batch_stride, b_batch_stride, 0, stream);
+            return matmul_impl(a ? a + last * a_batch_stride : a, b ? b + last * b_batch_stride : b, c, n, k, m, 1,
+                               a_batch_stride, b_batch_stride, 0, epi, bias, s);
         }
         for (uint64_t bi = 0; bi < batch; ++bi) {
-            rc = cm_matmul_async(a ? a + bi * a_batch_stride : a, b ? b + bi * b_batch_stride : b,
-                                 c + bi * c_batch_stride, n, k, m, 1, a_batch_stride, b_batch_stride, 0, stream);
+            rc = matmul_impl(a ? a + bi * a_batch_stride : a, b ? b + bi * b_batch_stride : b, c + bi * c_batch_stride,
+                             n, k, m, 1, a_batch_stride, b_batch_stride, 0, epi, bias, s);
             if (rc) return rc;
         }
         return CM_OK;
     }
-    if (k == 0) return fill_zero(cx, c, batch, n, m, m, c_batch_stride, s);
+    if (k == 0) {
+        // empty sums: every word is 0, then the epilogue's VectorOP calls in place
+        rc = fill_zero(cx, c, batch, n, m, m, c_batch_stride, s);
+        for (uint64_t bi = 0; !rc && epi && bi < batch; ++bi) {
+            int16_t* cz = c + bi * c_batch_stride;
+            if (epi & 2u) rc = cm_vectorop_async(cz, bias, cz, m, CM_OP_ADD, n, m, 0, s);
+            if (!rc && (epi & 1u)) rc = cm_vectorop_async(cz, nullptr, cz, n * m, CM_OP_RELU, 1, 0, 0, s);
+        }
+        return rc;
+    }
     const unsigned __int128 macs = (unsigned __int128)batch * n * m * k;
     const uint64_t total = (uint64_t)batch * n * m;
     if (macs <= cx->direct_max_macs) {
         {
             ProfScope ps_(PK_GEMM, s);
             const uint32_t G = direct_lanes(cx, total, k);
-            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(a, b, c, n, k, m, a_batch_stride,
-                                                                               b_batch_stride, c_batch_stride, total, G);
+            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(
+                a, b, c, n, k, m, a_batch_stride, b_batch_stride, c_batch_stride, total, G, epi, bias);
         }
         count_launch();
         cudaError_t e = cudaGetLastError();
@@ -1098,12 +1118,38 @@ extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, u
     if (!rc) {
         GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, 1, c_batch_stride, batch};
         p.b_packed = packed ? 1u : 0u;
+        p.epi = (epi & 1u) | ((epi & 2u) << 1);   // the kernel's bias-row bit is 4
+        p.resid = (epi & 2u) ? bias : nullptr;
         rc = gemm_launch(cx, p, s);
     }
     scratch_free(scratch, s);
     if (rc) return rc;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul");
+}
+}  // namespace
+
+extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                               unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                               unsigned c_batch_stride, cm_stream_t stream) {
+    return matmul_impl(a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, 0u, nullptr,
+                       (cudaStream_t)stream);
+}
+
+extern "C" int cm_matmul_fused_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k,
+                                     unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                                     unsigned c_batch_stride, unsigned epilogue, const int16_t* bias,
+                                     cm_stream_t stream) {
+    return matmul_impl(a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, epilogue, bias,
+                       (cudaStream_t)stream);
+}
+
+extern "C" int cm_matmul_fused(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                               unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                               unsigned c_batch_stride, unsigned epilogue, const int16_t* bias) {
+    int rc = cm_matmul_fused_async(a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, epilogue,
+                                   bias, nullptr);
+    return rc ? rc : finish_sync(nullptr);
 }
 
 extern "C" int cm_matmul(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,

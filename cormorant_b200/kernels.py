@@ -106,6 +106,20 @@ def ConvKernelFused(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h,
     check(L.cm_conv_fused(*args) if stream is None else L.cm_conv_fused_async(*args, _stream(stream)))
 
 
+def MatmulKernelFused(a, b, c, n, k, m, batch=1, a_batch_stride=None, b_batch_stride=None, c_batch_stride=None,
+                      epilogue=EPI_ADD, bias=None, stream=None) -> None:
+    """MatmulKernel followed by VectorOP ADD of a bias row broadcast over the n rows
+    (size m, outer n, a_inc m, b_inc 0) and/or RELU, fused into the GEMM's epilogue
+    (cm_matmul_fused).  Not a reference kernel: the word-for-word result of the
+    scheduler's Gemm decomposition MatMul -> Add(bias) (graph.py:83-188) -> [Relu]."""
+    a_bs = n * k if a_batch_stride is None else a_batch_stride
+    b_bs = k * m if b_batch_stride is None else b_batch_stride
+    c_bs = n * m if c_batch_stride is None else c_batch_stride
+    L = lib()
+    args = (_addr(a), _addr(b), _addr(c), n, k, m, batch, a_bs, b_bs, c_bs, int(epilogue), _addr(bias))
+    check(L.cm_matmul_fused(*args) if stream is None else L.cm_matmul_fused_async(*args, _stream(stream)))
+
+
 def PoolingKernel(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
                   pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, lp_order=2, count_include_pad=0,
                   stream=None) -> None:

@@ -43,6 +43,7 @@ class Net:
     nodes: list = field(default_factory=list)        # (kind, args...) -- see execute()
     aliases: dict = field(default_factory=dict)      # Reshape: name -> name
     macs_per_image: int = 0
+    source_kinds: tuple = ()                         # kernel kinds of the call list before fusion
 
     def buf(self, name: str, words: int) -> str:
         self.buffers[name] = int(words)
@@ -192,19 +193,27 @@ def _inputs(node) -> list:
     kind = node[0]
     if kind == "conv":
         names = [node[1], node[2], node[3]] + ([node[7]] if len(node) > 7 else [])
-    elif kind in ("vectorop", "matmul"):
+    elif kind == "matmul":
+        names = [node[1], node[2]] + ([node[6]] if len(node) > 6 else [])
+    elif kind == "vectorop":
         names = [node[1], node[2]]
     else:
         names = [node[1]]
     return [n for n in names if n is not None]
 
 
-def fuse(net: Net, residual: bool = True) -> Net:
+def output_of(node) -> str:
+    return node[4] if node[0] == "conv" else node[3] if node[0] in ("vectorop", "matmul") else node[2]
+
+
+def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
     """The call list with Conv -> Relu chains and (residual=True) Conv -> Add and
     Conv -> Add -> Relu chains folded into one conv call with a fused epilogue
-    (cm_conv_fused): the same words, without writing and re-reading the intermediate
-    tensors.  A chain is folded only when each intermediate result has no other reader
-    (and is not the network output)."""
+    (cm_conv_fused), and (gemm=True) the Gemm decomposition MatMul -> Add(bias row) and
+    MatMul -> [Add(bias row)] -> Relu folded into one cm_matmul_fused call: the same
+    words, without writing and re-reading the intermediate tensors.  A chain is folded
+    only when each intermediate result has no other reader (and is not the network
+    output)."""
     R = net.resolve
     reads: dict = {}
     for node in net.nodes:
@@ -242,13 +251,30 @@ def fuse(net: Net, residual: bool = True) -> Net:
                     out.append(("conv", x, wn, bn, nxt[3], args, 2, other))
                     i += 2
                 continue
+        if gemm and node[0] == "matmul" and len(node) == 5 and i + 1 < len(nodes) and reads.get(R(node[3]), 0) == 1:
+            _, a, b, c, args = node
+            n, _, m, batch = args[:4]
+            c, nxt = R(c), nodes[i + 1]
+            if (batch == 1 and nxt[0] == "vectorop" and tuple(nxt[4]) == (m, OP_ADD, n, m, 0)
+                    and R(nxt[1]) == c and nxt[2] is not None and R(nxt[2]) != c):
+                y, epi, step = nxt[3], 2, 2
+                if i + 2 < len(nodes) and reads.get(R(y), 0) == 1 and relu_of(nodes[i + 2], R(y)):
+                    y, epi, step = nodes[i + 2][3], 3, 3
+                out.append(("matmul", a, b, y, args, epi, nxt[2]))
+                i += step
+                continue
+            if batch == 1 and relu_of(nxt, c):
+                out.append(("matmul", a, b, nxt[3], args, 1, None))
+                i += 2
+                continue
         out.append(node)
         i += 1
-    used = {R(n) for node in out for n in _inputs(node)} | {R(node[4] if node[0] == "conv" else node[3] if node[0] in ("vectorop", "matmul") else node[2]) for node in out}
+    used = {R(n) for node in out for n in _inputs(node)} | {R(output_of(node)) for node in out}
     used |= {R(net.input), R(net.output)}
     fused = Net(net.name + "+fused", net.batch, net.input, net.output,
                 buffers={k: v for k, v in net.buffers.items() if k in used}, consts=dict(net.consts), nodes=out,
-                aliases=dict(net.aliases), macs_per_image=net.macs_per_image)
+                aliases=dict(net.aliases), macs_per_image=net.macs_per_image,
+                source_kinds=net.source_kinds or tuple(sorted({n[0] for n in net.nodes})))
     return fused
 
 
@@ -258,7 +284,7 @@ def execute(net: Net, backend, bufs: dict) -> None:
     backend offers vectorop(a, b, c, size, op, outer, a_inc, b_inc),
     matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars),
     pool(x, y, *17 scalars) and, for fused call lists, conv_fused(x, w, bias, y, *17
-    scalars, epilogue, resid)."""
+    scalars, epilogue, resid) and matmul_fused(a, b, c, *7 scalars, epilogue, bias)."""
     R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
     for node in net.nodes:
         kind = node[0]
@@ -274,6 +300,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "pool":
             _, x, y, args = node
             backend.pool(R(x), R(y), *args)
+        elif kind == "matmul" and len(node) > 5:
+            _, a, bb, c, args, epi, bias = node
+            backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
         elif kind == "matmul":
             _, a, bb, c, args = node
             backend.matmul(R(a), R(bb), R(c), *args)
@@ -294,6 +323,10 @@ class GpuBackend:
 
     def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
         self.k.MatmulKernel(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, stream=self.stream)
+
+    def matmul_fused(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epi, bias):
+        self.k.MatmulKernelFused(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi, bias=bias,
+                                 stream=self.stream)
 
     def conv(self, x, w, bias, y, *args):
         self.k.ConvKernel(x, w, bias, y, *args, stream=self.stream)

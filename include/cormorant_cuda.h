@@ -138,6 +138,22 @@ int cm_matmul_noalloc(const int16_t* a, const int16_t* b, int16_t* c, unsigned n
                       unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
                       unsigned c_batch_stride, cm_stream_t stream);
 
+/* ---- MatMul with a fused bias / ReLU epilogue (no reference counterpart) -----------
+ * The same product as cm_matmul, then on every narrowed output word v of row r, column j:
+ *   epilogue bit 1: v = sat16(v + bias[j])   (VectorOP ADD, size m, outer n, a_inc m, b_inc 0:
+ *                                             the bias row broadcast over the rows)
+ *   epilogue bit 0: v = max(v, 0)            (VectorOP RELU)
+ * 0 = plain cm_matmul, 1 = MatMul+Relu, 2 = MatMul+Add, 3 = MatMul+Add+Relu: the scheduler's
+ * Gemm decomposition (MatMul then the broadcast bias Add, graph.py:83-188) and a following
+ * Relu, word for word, in one launch.  The same bias row serves every batch step. */
+int cm_matmul_fused(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
+                    unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                    unsigned c_batch_stride, unsigned epilogue, const int16_t* bias);
+int cm_matmul_fused_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k,
+                          unsigned m, unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
+                          unsigned c_batch_stride, unsigned epilogue, const int16_t* bias,
+                          cm_stream_t stream);
+
 /* run_matmul_at(): the same call with element offsets applied to each buffer. */
 int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, unsigned b_off, int16_t* c,
                  unsigned c_off, unsigned n, unsigned k, unsigned m, unsigned batch,

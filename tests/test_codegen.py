@@ -85,7 +85,8 @@ def test_emitted_api_and_weight_files(tmp_path):
         assert sym in h, sym
     src = (tmp_path / "src/inference.c").read_text()
     assert src.count("cm_conv_fused_async(") == 2             # Conv+Relu twice
-    assert src.count("cm_matmul_async(") == 3 and src.count("cm_pool_async(") == 2
+    assert src.count("cm_matmul_fused_async(") == 3 and src.count("cm_pool_async(") == 2   # Gemm(+Relu) x 3
+    assert "cm_vectorop_async(" not in src
     assert src.count("CHECK(cm_synchronize(NULL));") == 1
     # weights above the threshold go to .dat files (raw little-endian words), the rest inline
     for name, arr in net.consts.items():

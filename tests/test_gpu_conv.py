@@ -72,6 +72,11 @@ REF_CASES = [
     (2, 3, 35, 29, 40, 7, 7, 2, 2, 1, 1, 3, 2, 3, 1, 1, 0),
     (1, 4, 33, 33, 100, 5, 5, 2, 2, 1, 1, 2, 2, 2, 2, 1, 0),
     (2, 2, 26, 26, 16, 4, 4, 4, 4, 1, 1, 1, 1, 1, 1, 1, 0),
+    # maps with H*W not a multiple of 4: whole image in shared memory (odd word count, no
+    # padding, asymmetric padding) and one whose image is too large for it
+    (3, 37, 9, 7, 70, 3, 3, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+    (2, 200, 5, 5, 130, 3, 3, 1, 1, 1, 1, 2, 1, 0, 1, 1, 0),
+    (1, 1100, 7, 7, 8, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),
 ]
 
 
@@ -94,6 +99,20 @@ def run(cm, port, case, dist, seed):
 @pytest.mark.parametrize("dist", ["q8", "full"])
 def test_cases(cm, port, case, dist):
     run(cm, port, case, dist, seed=sum(case) * 13 + (dist == "full"))
+
+
+def test_small_map_unaligned_input(cm, port):
+    """A 7x7 input that starts 2 bytes past a 4-byte boundary (the whole-image split then
+    reads 2-byte words)."""
+    N, C, H, W, M = 3, 96, 7, 7, 80
+    rng = np.random.default_rng(77)
+    x = rand16(rng, N * C * H * W)
+    w = rand16(rng, M * C * 9)
+    b = rand16(rng, M)
+    xd = dev(np.concatenate([np.zeros(1, np.int16), x]))[1:]
+    y = empty(N * M * H * W)
+    cm.ConvKernel(xd, dev(w), dev(b), y, N, C, H, W, M, H, W, 3, 3, 1, 1, 1, 1, 1, 1)
+    assert_same(host(y), port.conv(x, w, b, N, C, H, W, M, H, W, 3, 3, 1, 1, 1, 1, 1, 1), "unaligned 7x7")
 
 
 @pytest.mark.parametrize("w_val,b_val,sat", [(256, 32767, 32767), (-256, -32768, -32768)])

@@ -128,3 +128,41 @@ def test_sweep_shapes(cm, port, n, k, m, batch):
     want = port.matmul_rows(an, bn, n, k, m, n * k, k * m, bidx, ridx)
     got = host(c).reshape(batch, n, m)[bidx, ridx]
     assert_same(got, want, f"sweep {n}x{k}x{m} b{batch} sampled rows")
+
+
+FUSED_SHAPES = [(1, 400, 120, 1), (1, 84, 10, 1), (7, 13, 5, 1), (129, 130, 131, 2), (256, 512, 1000, 1),
+                (300, 17, 64, 3), (64, 0, 19, 2)]
+
+
+@pytest.mark.parametrize("n,k,m,batch", FUSED_SHAPES)
+@pytest.mark.parametrize("epi", [1, 2, 3])
+def test_fused_bias_relu_epilogue(cm, port, n, k, m, batch, epi):
+    """cm_matmul_fused == the reference sequence MatMul -> Add(bias row: size m, outer n,
+    a_inc m, b_inc 0) -> Relu, word for word, per batch step; full-range words so the
+    bias add saturates both ways."""
+    rng = np.random.default_rng(n * 131 + k * 7 + m + 1000 * epi)
+    a = rand16(rng, max(batch * n * k, 1))
+    b = rand16(rng, max(batch * k * m, 1))
+    bias = rand16(rng, m, -32768, 32768)
+    c = empty(batch * n * m)
+    cm.kernels.MatmulKernelFused(dev(a), dev(b), c, n, k, m, batch, epilogue=epi, bias=dev(bias))
+    want = port.matmul(a, b, n, k, m, batch)[: batch * n * m] if k else np.zeros(batch * n * m, np.int16)
+    for z in range(batch):
+        t = want[z * n * m:(z + 1) * n * m]
+        if epi & 2:
+            t = port.vectorop(t, bias, m, 0, n, m, 0, c=t.copy())[: n * m]
+        if epi & 1:
+            t = port.vectorop(t, None, n * m, 4, 1, 0, 0)[: n * m]
+        want[z * n * m:(z + 1) * n * m] = t
+    assert_same(host(c), want, f"fused {n}x{k}x{m} b{batch} epi{epi}")
+
+
+def test_fused_rejects_bad_epilogue(cm):
+    from cormorant_b200 import CormorantError
+    c = empty(16)
+    with pytest.raises(CormorantError):
+        cm.kernels.MatmulKernelFused(dev(np.ones(16, np.int16)), dev(np.ones(16, np.int16)), c, 4, 4, 4,
+                                     epilogue=2, bias=None)
+    with pytest.raises(CormorantError):
+        cm.kernels.MatmulKernelFused(dev(np.ones(16, np.int16)), dev(np.ones(16, np.int16)), c, 4, 4, 4,
+                                     epilogue=4, bias=dev(np.ones(4, np.int16)))

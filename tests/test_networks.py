@@ -22,6 +22,16 @@ class OracleBackend:
     def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
         c[:] = self.chk.matmul(a, b, n, k, m, batch, a_bs, b_bs, c_bs)[: c.size]
 
+    def matmul_fused(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epi, bias):
+        """The reference call sequence MatMul -> [Add(bias row)] -> [Relu] on the checker."""
+        t = np.zeros(c.size, np.int16)
+        self.matmul(a, b, t, n, k, m, batch, a_bs, b_bs, c_bs)
+        if epi & 2:
+            t = self.chk.vectorop(t, bias, m, networks.OP_ADD, n, m, 0, c=t.copy())[: c.size]
+        if epi & 1:
+            t = self.chk.vectorop(t, None, c.size, networks.OP_RELU, 1, 0, 0)[: c.size]
+        c[:] = t
+
     def conv(self, x, w, bias, y, *args):
         y[:] = self.chk.conv(x, w, bias, *args)[: y.size]
 
@@ -104,15 +114,22 @@ def test_resnet18_batch256_sampled_images(cm, port):
 
 
 def test_fusion_pass_shapes():
-    """Conv -> Relu (and with residual=True Conv -> Add -> Relu) chains fold; nothing else changes."""
-    rn = networks.fuse(networks.resnet18(batch=1), residual=True)
-    kinds = [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else None) for n in rn.nodes]
-    assert kinds.count(("conv", 1)) == 9 and kinds.count(("conv", 3)) == 8 and kinds.count(("conv", None)) == 3
-    assert kinds.count(("vectorop", None)) == 1          # the classifier's bias add stays
-    rn = networks.fuse(networks.resnet18(batch=1), residual=False)
-    kinds = [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else None) for n in rn.nodes]
-    assert kinds.count(("conv", 1)) == 9 and kinds.count(("conv", None)) == 11 and kinds.count(("vectorop", None)) == 17
+    """Conv -> Relu (with residual=True also Conv -> Add -> Relu) and (gemm=True) MatMul ->
+    Add(bias row) -> [Relu] chains fold; nothing else changes."""
+    def kinds(net):
+        return [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else n[5] if n[0] == "matmul" and len(n) > 5 else None)
+                for n in net.nodes]
+    rn = kinds(networks.fuse(networks.resnet18(batch=1), residual=True))
+    assert rn.count(("conv", 1)) == 9 and rn.count(("conv", 3)) == 8 and rn.count(("conv", None)) == 3
+    assert rn.count(("matmul", 2)) == 1 and rn.count(("vectorop", None)) == 0    # classifier: MatMul+Add
+    rn = kinds(networks.fuse(networks.resnet18(batch=1), residual=False, gemm=False))
+    assert rn.count(("conv", 1)) == 9 and rn.count(("conv", None)) == 11 and rn.count(("vectorop", None)) == 17
+    assert rn.count(("matmul", None)) == 1
     ln = networks.fuse(networks.lenet5())
+    assert kinds(ln) == [("conv", 1), ("pool", None), ("conv", 1), ("pool", None), ("matmul", 3), ("matmul", 3),
+                         ("matmul", 2)]
+    assert ln.source_kinds == ("conv", "matmul", "pool", "vectorop")
+    ln = networks.fuse(networks.lenet5(), gemm=False)
     assert [n[0] for n in ln.nodes].count("vectorop") == 5 and all(len(n) == 8 for n in ln.nodes if n[0] == "conv")
 
 
