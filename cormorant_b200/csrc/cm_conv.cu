@@ -388,6 +388,53 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
     }
 }
 
+// Separable form for rows of at least 16 outputs: block = output row oh of image n
+// (grid (out_h, images)).  The kh input rows of S it covers are summed column by column
+// into shared memory (coalesced loads), then each output adds kw column sums: about
+// kh*Wp/out_w + kw reads per output instead of kh*kw, and no divisions.
+constexpr uint32_t kRowtermThreads = 128;
+
+__global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(const int32_t* __restrict__ S, uint32_t Hp,
+                                                                          uint32_t Wp, uint32_t out_h, uint32_t out_w,
+                                                                          uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
+                                                                          uint32_t dh, int32_t* __restrict__ rowterm) {
+    extern __shared__ uint32_t colsum[];
+    const uint32_t oh = blockIdx.x, n = blockIdx.y;
+    const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp;
+    const uint32_t need = (out_w - 1) * sw + kw;
+    for (uint32_t c = threadIdx.x; c < need; c += blockDim.x) {
+        uint32_t v = 0;
+        for (uint32_t r = 0; r < kh; ++r) v += (uint32_t)__ldg(b + (uint64_t)r * dh * Wp + c);
+        colsum[c] = v;
+    }
+    __syncthreads();
+    int32_t* out = rowterm + ((uint64_t)n * out_h + oh) * out_w;
+    for (uint32_t ow = threadIdx.x; ow < out_w; ow += blockDim.x) {
+        uint32_t sum = 0;
+        for (uint32_t q = 0; q < kw; ++q) sum += colsum[ow * sw + q];
+        out[ow] = (int32_t)(sum * 128u);
+    }
+}
+
+// Row terms of nb images (S: [nb][Hp][Wp], rt: [nb][out_h][out_w]).
+void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t Wp, uint32_t out_h, uint32_t out_w,
+                    uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t dh, uint32_t nb, int32_t* rt,
+                    cudaStream_t s) {
+    const uint64_t need_bytes = ((uint64_t)(out_w - 1) * sw + kw) * 4;
+    if (out_w >= 16 && need_bytes <= 48u * 1024u) {
+        for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
+            const uint32_t bz = std::min(65535u, nb - b0);
+            conv_rowterm_rows_kernel<<<dim3(out_h, bz), kRowtermThreads, (size_t)need_bytes, s>>>(
+                S + (uint64_t)b0 * Hp * Wp, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, rt + (uint64_t)b0 * out_h * out_w);
+            count_launch();
+        }
+    } else {
+        const uint64_t tot = (uint64_t)nb * out_h * out_w;
+        conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(S, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, tot, rt);
+        count_launch();
+    }
+}
+
 // weights [M][C][kh][kw] -> N-major planes: tap k = (c, r, s) of output channel m
 // goes to row k' = r*KR_pad + s*Cp + c, element (p, k', m) at
 // planes[p*plane + k'*pitch + m] -- [2][Kt][M_pad] (pitch M_pad, plane Kt*M_pad)
@@ -977,7 +1024,6 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
             const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
             const NhwcGeom ng{in_ch, in_h, in_w, ip.Cp, ip.Hp, ip.Wp, pad_top, pad_left, nb};
-            const uint64_t tot = (uint64_t)nb * P;
             {
                 ProfScope ps_(PK_SPLIT, s);
                 const uint64_t HW = (uint64_t)in_h * in_w;
@@ -1024,9 +1070,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
                         count_launch();
                     }
                 }
-                conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h,
-                                                                            stride_w, dilation_h, tot, rt);
-                count_launch();
+                rowterm_launch(cx, S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, nb, rt, s);
             }
             const ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
                            out_h, out_w, log2u(ip.bw), log2u(ip.bh), log2u(ip.bn)};
@@ -1082,7 +1126,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
             const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
             const S2dGeom sg{in_ch, in_h, in_w, sp.s, sp.C2, vp.Cp, vp.Hp, vp.Wp, pad_top, pad_left, sp.Hpo, sp.Wpo, nb};
-            const uint64_t vtot = (uint64_t)nb * vp.Hp * vp.Wp, tot = (uint64_t)nb * P;
+            const uint64_t vtot = (uint64_t)nb * vp.Hp * vp.Wp;
             {
                 ProfScope ps_(PK_SPLIT, s);
                 const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
@@ -1102,9 +1146,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
                     conv_s2d_split_kernel<0, 0><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
                     count_launch();
                 }
-                conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s,
-                                                                            sp.s, 1, tot, rt);
-                count_launch();
+                rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
             }
             const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh2, 1, 1, 1,
                            out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};

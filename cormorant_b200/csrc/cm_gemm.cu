@@ -214,6 +214,14 @@ __device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[W]) {
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Two raw accumulators narrowed as saturate_cast does (floor by 8 bits: arithmetic
+// shift; clamp to int16) and packed, `lo` in the low half: one cvt.pack.sat per pair.
+__device__ __forceinline__ uint32_t narrow_pack(uint32_t lo, uint32_t hi) {
+    uint32_t d;
+    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(d) : "r"((int32_t)hi >> 8), "r"((int32_t)lo >> 8));
+    return d;
+}
+
 constexpr uint32_t GROUP_M = 8;
 
 struct GemmArgs {
@@ -236,6 +244,9 @@ struct GemmArgs {
     // rows; then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
     uint32_t epi;
     const int16_t* resid;
+    // divisors of the tile decode (set by launch_persistent): tiles per batch step, tiles
+    // per row-tile group, conv tiles per image and per tile row
+    FastDiv fd_z, fd_group, fd_hw, fd_w;
 };
 
 struct Tile {
@@ -250,27 +261,34 @@ struct Tile {
 template <int TBN, int CG>
 __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint32_t rank) {
     Tile c;
-    const uint64_t per_z = (uint64_t)g.tiles_mc * g.tiles_n;
-    c.z = (uint32_t)(t / per_z);
-    const uint32_t local_t = (uint32_t)(t - (uint64_t)c.z * per_z);
-    const uint32_t per_group = GROUP_M * g.tiles_n;
-    const uint32_t group = local_t / per_group;
+    // t < batch * tiles_mc * tiles_n < 2^32 (checked at launch): 32-bit multiply-high divisions
+    const uint32_t t32 = (uint32_t)t;
+    c.z = g.fd_z.div(t32);
+    const uint32_t local_t = t32 - c.z * g.fd_z.d;
+    const uint32_t group = g.fd_group.div(local_t);
     const uint32_t first_m = group * GROUP_M;
-    const uint32_t gsize = min(GROUP_M, g.tiles_mc - first_m);
-    const uint32_t local = local_t - group * per_group;
-    const uint32_t tm = (first_m + local % gsize) * CG + rank;
+    const uint32_t local = local_t - group * g.fd_group.d;
+    uint32_t tmq, tnq;
+    if (g.tiles_mc - first_m >= GROUP_M) {           // a full group: power-of-two size
+        tmq = local % GROUP_M;
+        tnq = local / GROUP_M;
+    } else {                                         // the last, partial group
+        const uint32_t gsize = g.tiles_mc - first_m;
+        tnq = local / gsize;
+        tmq = local - tnq * gsize;
+    }
+    const uint32_t tm = (first_m + tmq) * CG + rank;
     c.m0 = tm * BM;
-    c.n0 = (local / gsize) * TBN;
+    c.n0 = tnq * TBN;
     c.ba = g.a_batches == 1 ? 0u : c.z;
     c.bb = g.b_batches == 1 ? 0u : c.z;
     c.cw0 = c.ch0 = c.cn0 = 0;
     if (g.conv) {
-        const uint32_t t_hw = g.tiles_w * g.tiles_h;
-        const uint32_t tn = tm / t_hw, rem = tm - tn * t_hw;
-        const uint32_t th = rem / g.tiles_w;
+        const uint32_t tn = g.fd_hw.div(tm), rem = tm - tn * g.fd_hw.d;
+        const uint32_t th = g.fd_w.div(rem);
         c.cn0 = tn << g.bn_log;
         c.ch0 = th << g.bh_log;
-        c.cw0 = (rem - th * g.tiles_w) << g.bw_log;
+        c.cw0 = (rem - th * g.fd_w.d) << g.bw_log;
     }
     return c;
 }
@@ -509,9 +527,22 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
             for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
                 const uint32_t col0 = tc.n0 + cbase + c0;
                 if (col0 < g.cols) {
-                    uint32_t p[CW], q[CW];
+                    uint32_t p[CW], q[CW], cv[CW];
                     tmem_ld<CW>(tl + c0, p);
                     tmem_ld<CW>(tl + TBN + c0, q);
+                    // column terms: four 16-byte loads for a full, aligned chunk
+                    if (col0 + CW <= g.cols && ((uintptr_t)(ct + col0) & 15u) == 0) {
+                        const int4* c4 = (const int4*)(ct + col0);
+#pragma unroll
+                        for (int v = 0; v < (int)CW / 4; ++v) {
+                            const int4 x = __ldg(c4 + v);
+                            cv[4 * v] = (uint32_t)x.x; cv[4 * v + 1] = (uint32_t)x.y;
+                            cv[4 * v + 2] = (uint32_t)x.z; cv[4 * v + 3] = (uint32_t)x.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k) cv[k] = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
+                    }
                     tmem_ld_wait();
 #pragma unroll
                     for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
@@ -522,13 +553,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                     tmem_ld<CW>(tl + 3 * TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int k = 0; k < (int)CW; k += 2) {
-                        const uint32_t ca = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
-                        const uint32_t cb = col0 + k + 1 < g.cols ? (uint32_t)__ldg(ct + col0 + k + 1) : 0u;
-                        const uint16_t lo = (uint16_t)narrow_acc(p[k] + q[k] + rt + ca);
-                        const uint16_t hi = (uint16_t)narrow_acc(p[k + 1] + q[k + 1] + rt + cb);
-                        pk[(c0 + k) / 2] = (uint32_t)lo | ((uint32_t)hi << 16);
-                    }
+                    for (int k = 0; k < (int)CW; k += 2)
+                        pk[(c0 + k) / 2] = narrow_pack(p[k] + q[k] + rt + cv[k], p[k + 1] + q[k + 1] + rt + cv[k + 1]);
                 }
             }
             tc_fence_before();
@@ -556,10 +582,17 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                 if (g.ldc != 1) {
                     // column-strided output (conv: y[m][p] with rows = pixels): each
                     // store is coalesced across the warp's consecutive rows
+                    if (col0 + CW <= g.cols) {
+                        int16_t* d = orow + (uint64_t)col0 * g.ldc;
 #pragma unroll
-                    for (int k = 0; k < (int)CW; ++k)
-                        if (col0 + k < g.cols)
-                            orow[(uint64_t)(col0 + k) * g.ldc] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
+                        for (int k = 0; k < (int)CW; ++k, d += g.ldc)
+                            *d = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
+                    } else {
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k)
+                            if (col0 + k < g.cols)
+                                orow[(uint64_t)(col0 + k) * g.ldc] = (int16_t)(uint16_t)(pk[(c0 + k) / 2] >> (16 * (k & 1)));
+                    }
                 } else if (col0 + CW <= g.cols && ((uintptr_t)dst & 15u) == 0) {
                     uint4* d4 = (uint4*)dst;
 #pragma unroll
@@ -810,6 +843,8 @@ int make_nmajor_map(CUtensorMap* m, const int8_t* base, uint32_t cols, uint32_t 
 // pixel stride being Cp bytes.  Box {128, bw*sw, bh*sh, bn, 1} with traversal
 // strides {1, sw, sh, 1, 1} = 128 pixels x 128 bytes of K.  Every in-range
 // (pixel, k) address stays inside the buffer plus (kw-1)*Cp bytes of slack.
+// (No L2 promotion: the box rows are 128 bytes and overlap their neighbours; measured
+// slightly faster than 256-byte promotion on the ResNet-18 layers.)
 int make_conv_map(CUtensorMap* m, const ConvA& c) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
@@ -823,7 +858,7 @@ int make_conv_map(CUtensorMap* m, const ConvA& c) {
     const cuuint32_t box[5] = {(cuuint32_t)BK, bw * c.sw, bh * c.sh, bn, 1};
     const cuuint32_t estr[5] = {1, c.sw, c.sh, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void*)c.planes, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled (conv) failed (%d)", (int)r);
     return CM_OK;
@@ -873,7 +908,12 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     g.tiles_mc = (g.tiles_m + CG - 1) / CG;
     const uint64_t total = (uint64_t)g.batch * g.tiles_mc * g.tiles_n;
     if (total == 0) return CM_OK;
-    if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 32)) return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    if ((uint64_t)g.tiles_m * g.tiles_n >= (1ull << 32) || total >= (1ull << 32))
+        return set_error(CM_EUNSUPPORTED, "GEMM tile grid too large");
+    g.fd_z = FastDiv(g.tiles_mc * g.tiles_n);
+    g.fd_group = FastDiv(GROUP_M * g.tiles_n);
+    g.fd_hw = FastDiv(g.conv ? g.tiles_w * g.tiles_h : 1u);
+    g.fd_w = FastDiv(g.conv ? g.tiles_w : 1u);
     const unsigned clusters = (unsigned)std::min<uint64_t>(total, (uint64_t)per_sm_clusters);
     g.status = cx->status; g.timeout_ns = cx->timeout_ns;
     cudaError_t e;
