@@ -38,6 +38,21 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// The same test, letting the thread sleep in hardware until the phase completes or
+// about `hint_ns` pass (instead of returning at once), so waiting warps do not spin
+// through issue slots.
+__device__ __forceinline__ bool mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
 struct WaitCtl {
     volatile int* abort;   // shared flag: some role gave up
     int* status;           // device status word
@@ -49,8 +64,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, const W
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try(bar, parity)) return true;
-        if ((it & 63u) == 0) {
+        if (mbar_try_sleep(bar, parity, 20000u)) return true;
+        if ((it & 7u) == 0) {
             if (*w.abort) return false;
             if (gtimer() - t0 > w.timeout_ns) {
                 atomicCAS(w.status, 0, CM_ETIMEOUT);
