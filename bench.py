@@ -440,13 +440,18 @@ class NetworkBench:
         self.fused = not UNFUSED
         if self.fused:                                           # Conv->Relu (/ Conv->Add->Relu) folded
             self.net = networks.fuse(self.net, residual=FUSE_RESIDUAL)
+        self.planes = self.fused and PLANES and which != "lenet"
+        if self.planes:                                          # conv outputs produced as the next convs' operand
+            self.net = networks.chain(self.net)
         self.units_total = float(self.batch_total)
         self.units_local = float(self.local)
         self.dom_units_local = 8.0 * self.net.macs_per_image * self.local   # int8 ops (4 MMAs x 2 per MAC)
 
     def config(self, world):
         calls = ("reference call list, Conv->Relu" + (" and Conv->Add->Relu" if FUSE_RESIDUAL else "")
-                 + " chains folded into cm_conv_fused" if self.fused else "reference call list, one C-ABI call per node")
+                 + " and Gemm(MatMul->Add)->Relu chains folded into cm_conv_fused / cm_matmul_fused"
+                 + ("; conv outputs read by convs written as plane images (cm_conv_planes)" if self.planes else "")
+                 if self.fused else "reference call list, one C-ABI call per node")
         if self.which == "lenet":
             return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
                     "parallelism": f"replicas only: one batch-1 stream per GPU ({world})", "calls": calls,
@@ -549,6 +554,7 @@ class NetworkBench:
 
 UNFUSED = False      # --unfused: networks run node by node
 FUSE_RESIDUAL = True   # --no-fuse-residual: fold Conv->Relu only
+PLANES = True          # --no-planes: every conv splits its own input
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -719,12 +725,15 @@ def main():
                     help="lenet/resnet: fold Conv->Relu only (keep the residual Add / Relu passes)")
     ap.add_argument("--unfused", action="store_true",
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
+    ap.add_argument("--no-planes", action="store_true",
+                    help="resnet: no plane images between convs (each conv splits its NCHW input)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
     args = ap.parse_args()
-    global UNFUSED, FUSE_RESIDUAL
+    global UNFUSED, FUSE_RESIDUAL, PLANES
     UNFUSED = args.unfused
     FUSE_RESIDUAL = not args.no_fuse_residual
+    PLANES = not args.no_planes
     if args.int8_peak:
         return int8_peak()
     if args.shape:

@@ -23,6 +23,7 @@
 // Depthwise conv (is_depthwise = 1, ConvKernel.cpp:251-319) is a per-channel
 // kh x kw stencil: CUDA cores, one thread per output pixel, int32 wrap sum.
 #include <algorithm>
+#include <new>
 
 #include "cm_gemm.cuh"
 
@@ -369,6 +370,18 @@ __global__ void __launch_bounds__(256) conv_nhwc_border_kernel(NhwcGeom g, int8_
         *(uint4*)(planes + plane + o) = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
         if (run == 0) S[pix] = (int32_t)(0u - 128u * g.C);
     }
+}
+
+// S of a plane image before its producer adds the channel sums: 0 at the image's
+// pixels, -128*C on the frame (x = 0 in every channel).  Grid (x: columns, y: rows,
+// z: images).
+__global__ void __launch_bounds__(256) planes_reset_S_kernel(int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
+                                                             uint32_t H, uint32_t W, uint32_t pt, uint32_t pl,
+                                                             int32_t frame) {
+    const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x, h = blockIdx.y, n = blockIdx.z;
+    if (w >= Wp) return;
+    const bool inside = h >= pt && h < pt + H && w >= pl && w < pl + W;
+    S[((uint64_t)n * Hp + h) * Wp + w] = inside ? 0 : frame;
 }
 
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
@@ -934,9 +947,101 @@ __global__ void __launch_bounds__(256) conv_s2d_weights_kernel(const int16_t* __
 
 using namespace cm;
 
+// A channels-last plane image of an activation x [n][C][H][W]: hi / lo' planes
+// [2][n][Hp][Wp][Cp] (Hp = pt + H + pb, Wp = pl + W + pr, Cp = C rounded up to 16)
+// and per-pixel channel sums S [n][Hp][Wp] = sum_c (x - 128); the frame and the
+// channels past C hold x = 0.  It is the A operand of every implicit-GEMM conv
+// that reads x, so a conv whose GEMM epilogue writes it spares its consumers the
+// split pass.
+struct cm_planes {
+    int8_t* planes = nullptr;
+    int32_t* S = nullptr;
+    uint64_t plane_pitch = 0;   // bytes from the hi plane to the lo plane
+    uint32_t n = 0, C = 0, H = 0, W = 0, Cp = 0, Hp = 0, Wp = 0, pt = 0, pl = 0;
+    int device = -1;
+};
+
 namespace {
 
-int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch, unsigned in_ch,
+// The path a standard conv call takes, in the order conv_core tests them.
+enum ConvPath { CP_DEPTHWISE, CP_BIAS_FILL, CP_DIRECT, CP_TOO_LONG, CP_IMPLICIT, CP_S2D, CP_EXPLICIT };
+
+ConvPath conv_path(uint64_t direct_max_macs, unsigned batch, unsigned in_ch, unsigned out_ch, unsigned out_h,
+                   unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                   unsigned dilation_w, unsigned is_depthwise, ImplicitPlan* ip) {
+    if (is_depthwise) return CP_DEPTHWISE;
+    const uint64_t K64 = (uint64_t)in_ch * kh * kw;
+    if (K64 == 0) return CP_BIAS_FILL;
+    const uint64_t total = (uint64_t)batch * out_ch * out_h * out_w;
+    if ((unsigned __int128)total * K64 <= direct_max_macs) return CP_DIRECT;
+    if (K64 > kMaxGemmK) return CP_TOO_LONG;
+    if (plan_implicit(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, ip)) return CP_IMPLICIT;
+    S2dPlan sp;
+    if (plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp)) return CP_S2D;
+    return CP_EXPLICIT;
+}
+
+// Whether plane image `xp` can be the A operand of an implicit conv with plan `ip`:
+// the same tensor, and a frame at least as wide as the conv's padded extent.
+bool planes_fit(const cm_planes* xp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned pad_top,
+                unsigned pad_left, const ImplicitPlan& ip) {
+    // (a box reads up to one kernel row past the last pixel: the image keeps 64 KB of slack)
+    return xp && ip.KR <= 65536u && xp->n == batch && xp->C == in_ch && xp->H == in_h && xp->W == in_w && xp->Cp == ip.Cp &&
+           xp->pt >= pad_top && xp->pl >= pad_left && (uint64_t)(xp->pt - pad_top) + ip.Hp <= xp->Hp &&
+           (uint64_t)(xp->pl - pad_left) + ip.Wp <= xp->Wp;
+}
+
+// x (NCHW words) -> plane image yp, by the split kernels (producers whose GEMM does
+// not write the image itself).  The frame was written when yp was created.
+int planes_from_tensor(const Context* cx, const int16_t* x, cm_planes* yp, cudaStream_t s) {
+    const uint64_t HW = (uint64_t)yp->H * yp->W;
+    const uint64_t img_plane = (uint64_t)yp->Hp * yp->Wp * yp->Cp;
+    const NhwcGeom ng{yp->C, yp->H, yp->W, yp->Cp, yp->Hp, yp->Wp, yp->pt, yp->pl, yp->n};
+    const bool quads = HW % 4 == 0 && ((uintptr_t)x & 7u) == 0 && HW < (1ull << 31);
+    const uint32_t gx = quads ? (uint32_t)((HW / 4 + 63) / 64) : (uint32_t)(((uint64_t)yp->Hp * yp->Wp + kNhwcPix - 1) / kNhwcPix);
+    ProfScope ps_(PK_SPLIT, s);
+    for (uint32_t b0 = 0; b0 < yp->n; b0 += 65535u) {
+        const uint32_t bz = std::min(65535u, yp->n - b0);
+        const int16_t* xb = x + (uint64_t)b0 * yp->C * HW;
+        int8_t* pb = yp->planes + (uint64_t)b0 * img_plane;
+        int32_t* Sb = yp->S + (uint64_t)b0 * yp->Hp * yp->Wp;
+        if (quads) conv_nhwc_split4_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+        else conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+        count_launch();
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv planes split");
+}
+
+// Clears the channel sums of plane image yp (images [n0, n0 + nb)) before a GEMM
+// epilogue adds into them.
+int planes_reset(cm_planes* yp, cudaStream_t s) {
+    for (uint32_t b0 = 0; b0 < yp->n; b0 += 65535u) {
+        const uint32_t bz = std::min(65535u, yp->n - b0);
+        planes_reset_S_kernel<<<dim3((yp->Wp + 255) / 256, yp->Hp, bz), 256, 0, s>>>(
+            yp->S + (uint64_t)b0 * yp->Hp * yp->Wp, yp->Hp, yp->Wp, yp->H, yp->W, yp->pt, yp->pl,
+            (int32_t)(0u - 128u * yp->C));
+        count_launch();
+    }
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv planes reset");
+}
+
+// The GEMM epilogue's view of plane image yp from image n0 on.
+PlaneOut plane_out(cm_planes* yp, uint64_t n0) {
+    PlaneOut o;
+    o.planes = yp->planes + n0 * yp->Hp * yp->Wp * yp->Cp;
+    o.S = yp->S + n0 * yp->Hp * yp->Wp;
+    o.plane_pitch = yp->plane_pitch;
+    o.Hp = yp->Hp; o.Wp = yp->Wp; o.Cp = yp->Cp; o.pt = yp->pt; o.pl = yp->pl;
+    return o;
+}
+
+// xv: a plane image that fits this conv's implicit plan (read instead of x); po:
+// the output's plane image, written by the GEMM epilogue (implicit / space-to-depth
+// paths only; y may then be null).
+int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, const int16_t* bias, int16_t* y,
+              cm_planes* po, unsigned batch, unsigned in_ch,
               unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
               unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
               unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epi, const int16_t* resid,
@@ -946,7 +1051,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
     if (rc) return rc;
     const uint64_t P = (uint64_t)out_h * out_w;
     if (batch == 0 || out_ch == 0 || P == 0) return CM_OK;
-    if (!y || (has_bias && !bias)) return set_error(CM_EINVAL, "cm_conv: null buffer");
+    if ((!y && !po) || (has_bias && !bias)) return set_error(CM_EINVAL, "cm_conv: null buffer");
     if (P >= (1ull << 31)) return set_error(CM_EUNSUPPORTED, "cm_conv: output plane too large");
     cudaStream_t s = (cudaStream_t)stream;
     const uint64_t total = (uint64_t)batch * out_ch * P;
@@ -978,7 +1083,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         cudaError_t e = cudaGetLastError();
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv bias fill");
     }
-    if (!x || !weight) return set_error(CM_EINVAL, "cm_conv: null buffer");
+    if ((!x && !xv) || !weight) return set_error(CM_EINVAL, "cm_conv: null buffer");
     if ((unsigned __int128)total * K64 <= cx->direct_max_macs) {
         DwArgs a{in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
                  has_bias ? 1u : 0u};
@@ -1004,12 +1109,12 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         const uint64_t img_plane = (uint64_t)ip.Hp * ip.Wp * ip.Cp;
         uint64_t chunk = kNhwcBudget / (2 * img_plane);
         if (chunk == 0) chunk = 1;
-        if (chunk > batch) chunk = batch;
+        if (chunk > batch || xv) chunk = batch;           // a plane image holds every image already
         if (chunk > (1u << 24)) chunk = 1u << 24;
         const uint64_t w_bytes = ((uint64_t)ip.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
         const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
-        const uint64_t a_bytes = (2 * chunk * img_plane + ip.KR + 256 + 255) & ~255ull;   // + slack past the last pixel
-        const uint64_t s_bytes = (chunk * ip.Hp * ip.Wp * 4 + 255) & ~255ull;
+        const uint64_t a_bytes = xv ? 0 : (2 * chunk * img_plane + ip.KR + 256 + 255) & ~255ull;   // + slack past the last pixel
+        const uint64_t s_bytes = xv ? 0 : (chunk * ip.Hp * ip.Wp * 4 + 255) & ~255ull;
         const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
         void* scratch = nullptr;
         rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + s_bytes + rt_bytes, s);
@@ -1021,10 +1126,17 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         int32_t* rt = (int32_t*)((int8_t*)S + s_bytes);
         rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch, w_plane,
                           w_bytes, wpl, ct, s);
+        if (!rc && po) rc = planes_reset(po, s);
+        // a plane image read in place: the conv's padded window starts (dt, dl) into its frame
+        const uint32_t dt = xv ? xv->pt - pad_top : 0u, dl = xv ? xv->pl - pad_left : 0u;
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
             const uint32_t nb = (uint32_t)((batch - n0) < chunk ? (batch - n0) : chunk);
             const NhwcGeom ng{in_ch, in_h, in_w, ip.Cp, ip.Hp, ip.Wp, pad_top, pad_left, nb};
-            {
+            if (xv) {
+                ProfScope ps_(PK_SPLIT, s);
+                rowterm_launch(cx, xv->S + (uint64_t)dt * xv->Wp + dl, xv->Hp, xv->Wp, out_h, out_w, kh, kw, stride_h,
+                               stride_w, dilation_h, nb, rt, s);
+            } else {
                 ProfScope ps_(PK_SPLIT, s);
                 const uint64_t HW = (uint64_t)in_h * in_w;
                 const bool quads = HW % 4 == 0 && ((uintptr_t)x & 7u) == 0 && HW < (1ull << 31);
@@ -1072,14 +1184,23 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
                 }
                 rowterm_launch(cx, S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, nb, rt, s);
             }
-            const ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
-                           out_h, out_w, log2u(ip.bw), log2u(ip.bh), log2u(ip.bn)};
+            ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
+                     out_h, out_w, log2u(ip.bw), log2u(ip.bh), log2u(ip.bn)};
+            if (xv) {
+                // the plane image's own layout; boxes may read its whole frame past the plan's extent
+                ca.planes = xv->planes + ((uint64_t)dt * xv->Wp + dl) * xv->Cp;
+                ca.Hp = xv->Hp - dt; ca.Wp = xv->Wp - dl;
+                ca.row_pitch = (uint64_t)xv->Wp * xv->Cp;
+                ca.img_pitch = (uint64_t)xv->Hp * xv->Wp * xv->Cp;
+                ca.plane_pitch = xv->plane_pitch;
+            }
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, ip.Kt, ip.Kt, M_pad, rt, ct,
-                       y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
+                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
+            if (po) p.po = plane_out(po, n0);
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -1116,6 +1237,7 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
         int32_t* rt = (int32_t*)((int8_t*)So + s_bytes);
         // column terms from the original weights (real taps, bias), planes of the virtual kernel
         rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, 0, 0, 0, 0, 0, nullptr, ct, s);
+        if (!rc && po) rc = planes_reset(po, s);
         if (!rc) {
             ProfScope ps_(PK_SPLIT, s);
             const uint64_t wtot = (uint64_t)vp.Kt * out_ch;
@@ -1151,11 +1273,12 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
             const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh2, 1, 1, 1,
                            out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, vp.Kt, vp.Kt, M_pad, rt, ct,
-                       y + n0 * (uint64_t)out_ch * P, 0, P, (uint64_t)out_ch * P, 1};
+                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
+            if (po) p.po = plane_out(po, n0);
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -1233,6 +1356,55 @@ int conv_impl(const int16_t* x, const int16_t* weight, const int16_t* bias, int1
     return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv");
 }
 
+// Conv with optional plane images on either side: xp replaces x when this conv's
+// path is the implicit GEMM and xp's frame covers its padding (else x is read and
+// must be given); yp receives the output as a plane image -- written by the GEMM
+// epilogue on the implicit and space-to-depth paths, by the split kernels from y
+// (or a scratch copy of it when y is null) otherwise.
+int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, const int16_t* bias, int16_t* y,
+              cm_planes* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+              unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
+              unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
+              unsigned is_depthwise, unsigned epi, const int16_t* resid, cm_stream_t stream) {
+    if (!xp && !yp)
+        return conv_core(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+                         stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi,
+                         resid, stream);
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if ((xp && xp->device != cx->device) || (yp && yp->device != cx->device))
+        return set_error(CM_EINVAL, "cm_conv: plane image of another device");
+    if (yp && (yp->n != batch || yp->C != out_ch || yp->H != out_h || yp->W != out_w))
+        return set_error(CM_EINVAL, "cm_conv: output plane image is %ux%ux%ux%u, the output %ux%ux%ux%u", yp->n, yp->C,
+                         yp->H, yp->W, batch, out_ch, out_h, out_w);
+    ImplicitPlan ip;
+    const ConvPath path = conv_path(cx->direct_max_macs, batch, in_ch, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                                    dilation_h, dilation_w, is_depthwise, &ip);
+    const cm_planes* xv = path == CP_IMPLICIT && planes_fit(xp, batch, in_ch, in_h, in_w, pad_top, pad_left, ip) ? xp : nullptr;
+    if (!xv && !x && path != CP_BIAS_FILL)
+        return set_error(CM_EINVAL, "cm_conv: x is null and this conv cannot read the plane image (not an implicit-GEMM "
+                                    "conv, or the image's tensor or frame does not match)");
+    const bool epi_writes = yp && (path == CP_IMPLICIT || path == CP_S2D);
+    if (!yp || epi_writes)
+        return conv_core(x, xv, weight, bias, y, epi_writes ? yp : nullptr, batch, in_ch, in_h, in_w, out_ch, out_h,
+                         out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias,
+                         is_depthwise, epi, resid, stream);
+    cudaStream_t s = (cudaStream_t)stream;
+    int16_t* yw = y;
+    void* tmp = nullptr;
+    if (!yw) {
+        rc = scratch_alloc(&tmp, ((uint64_t)batch * out_ch * out_h * out_w * 2 + 255) & ~255ull, s);
+        if (rc) return rc;
+        yw = (int16_t*)tmp;
+    }
+    rc = conv_core(x, xv, weight, bias, yw, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
+                   stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi, resid, stream);
+    if (!rc) rc = planes_from_tensor(cx, yw, yp, s);
+    if (tmp) scratch_free(tmp, s);
+    return rc;
+}
+
 }  // namespace
 
 extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
@@ -1240,8 +1412,9 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
                              unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
                              unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
                              unsigned has_bias, unsigned is_depthwise, cm_stream_t stream) {
-    return conv_impl(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
-                     dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, 0u, nullptr, stream);
+    return conv_impl(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+                     stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, 0u, nullptr,
+                     stream);
 }
 
 extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
@@ -1252,8 +1425,9 @@ extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, cons
                                    const int16_t* resid, cm_stream_t stream) {
     if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_fused: epilogue must be 0..3");
     if ((epilogue & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv_fused: residual buffer is null");
-    return conv_impl(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
-                     dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue, resid, stream);
+    return conv_impl(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+                     stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue,
+                     resid, stream);
 }
 
 extern "C" int cm_conv_fused(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
@@ -1274,5 +1448,105 @@ extern "C" int cm_conv(const int16_t* x, const int16_t* weight, const int16_t* b
                        unsigned is_depthwise) {
     int rc = cm_conv_async(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
                            stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Plane images (no reference counterpart): a conv's output written directly as
+// the next implicit-GEMM conv's A operand
+// ---------------------------------------------------------------------------
+extern "C" cm_planes_t* cm_planes_create(unsigned batch, unsigned channels, unsigned h, unsigned w, unsigned pad_top,
+                                         unsigned pad_left, unsigned pad_bottom, unsigned pad_right) {
+    const Context* cx;
+    if (enter(&cx)) return nullptr;
+    if (batch == 0 || channels == 0 || h == 0 || w == 0) {
+        set_error(CM_EINVAL, "cm_planes_create: empty tensor");
+        return nullptr;
+    }
+    const uint64_t Cp = (channels + 15ull) & ~15ull, Hp = (uint64_t)pad_top + h + pad_bottom,
+                   Wp = (uint64_t)pad_left + w + pad_right;
+    if (Cp > 8192 || Hp * Wp >= (1ull << 31) || (uint64_t)batch * Hp * Wp * Cp >= (1ull << 40)) {
+        set_error(CM_EUNSUPPORTED, "cm_planes_create: image too large");
+        return nullptr;
+    }
+    cm_planes* p = new (std::nothrow) cm_planes();
+    if (!p) return nullptr;
+    p->n = batch; p->C = channels; p->H = h; p->W = w; p->Cp = (uint32_t)Cp; p->Hp = (uint32_t)Hp; p->Wp = (uint32_t)Wp;
+    p->pt = pad_top; p->pl = pad_left; p->device = cx->device;
+    p->plane_pitch = (uint64_t)batch * Hp * Wp * Cp;
+    // slack past the lo plane: a conv box reads up to a kernel row (kw * Cp bytes) past a pixel
+    const uint64_t slack = 65536 + 256;
+    cudaError_t e = cudaMalloc(&p->planes, 2 * p->plane_pitch + slack);
+    if (e == cudaSuccess) e = cudaMalloc(&p->S, (uint64_t)batch * Hp * Wp * 4);
+    // x = 0 everywhere (hi 0, lo' 0x80): the frame and the channels past C keep it for good
+    if (e == cudaSuccess) e = cudaMemset(p->planes, 0, p->plane_pitch);
+    if (e == cudaSuccess) e = cudaMemset(p->planes + p->plane_pitch, 0x80, p->plane_pitch + slack);
+    if (e == cudaSuccess && planes_reset(p, nullptr) != CM_OK) e = cudaErrorUnknown;
+    if (e == cudaSuccess) e = cudaStreamSynchronize(nullptr);
+    if (e != cudaSuccess) {
+        cuda_error(e, "cm_planes_create");
+        cudaFree(p->planes);
+        cudaFree(p->S);
+        delete p;
+        return nullptr;
+    }
+    return p;
+}
+
+extern "C" void cm_planes_destroy(cm_planes_t* p) {
+    if (!p) return;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    cudaSetDevice(p->device);
+    cudaFree(p->planes);
+    cudaFree(p->S);
+    if (cur >= 0) cudaSetDevice(cur);
+    delete p;
+}
+
+extern "C" int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                                   unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                                   unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                                   unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned* frame) {
+    (void)has_bias;
+    const Context* c = ctx();
+    const uint64_t limit = c ? c->direct_max_macs : (1ull << 22);
+    ImplicitPlan ip;
+    if (batch == 0 || out_ch == 0 || (uint64_t)out_h * out_w == 0 ||
+        conv_path(limit, batch, in_ch, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w,
+                  is_depthwise, &ip) != CP_IMPLICIT)
+        return 0;
+    if (frame) {
+        frame[0] = pad_top;
+        frame[1] = pad_left;
+        frame[2] = ip.Hp > (uint64_t)pad_top + in_h ? ip.Hp - pad_top - in_h : 0u;
+        frame[3] = ip.Wp > (uint64_t)pad_left + in_w ? ip.Wp - pad_left - in_w : 0u;
+    }
+    return 1;
+}
+
+extern "C" int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
+                                    int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h,
+                                    unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh,
+                                    unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                                    unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
+                                    unsigned is_depthwise, unsigned epilogue, const int16_t* resid, cm_stream_t stream) {
+    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_planes: epilogue must be 0..3");
+    if ((epilogue & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv_planes: residual buffer is null");
+    if (!y && !yp) return set_error(CM_EINVAL, "cm_conv_planes: neither y nor an output plane image");
+    return conv_impl(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
+                     stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue, resid,
+                     stream);
+}
+
+extern "C" int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
+                              int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w,
+                              unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
+                              unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w,
+                              unsigned pad_top, unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
+                              unsigned epilogue, const int16_t* resid) {
+    int rc = cm_conv_planes_async(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+                                  stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise,
+                                  epilogue, resid, nullptr);
     return rc ? rc : finish_sync(nullptr);
 }

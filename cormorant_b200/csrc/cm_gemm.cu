@@ -244,6 +244,11 @@ struct GemmArgs {
     // rows; then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
     uint32_t epi;
     const int16_t* resid;
+    // conv mode: output also written as a channels-last plane image (see PlaneOut)
+    int8_t* po;
+    int32_t* po_S;
+    uint64_t po_plane;
+    uint32_t po_Hp, po_Wp, po_Cp, po_pt, po_pl;
     // divisors of the tile decode (set by launch_persistent): tiles per batch step, tiles
     // per row-tile group, conv tiles per image and per tile row
     FastDiv fd_z, fd_group, fd_hw, fd_w;
@@ -564,7 +569,6 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                 else mbar_arrive(smem_u32(&acce_b[buf]));
             }
             if (!valid) continue;
-            int16_t* orow = g.out + o_off;
             // VectorOP ADD (saturating) and RELU on both halfwords of each pair
             if (g.epi & 6u) {
 #pragma unroll
@@ -574,6 +578,47 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
 #pragma unroll
                 for (uint32_t q = 0; q < HALF / 2; ++q) pk[q] = __vmaxs2(pk[q], 0u);
             }
+            if (g.po) {
+                // the output row as channels-last hi / lo' planes of the next conv's input,
+                // 16 channels per 16-byte store, and its channel sum added into S
+                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
+                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
+                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                const uint64_t pix = ((uint64_t)n * g.po_Hp + oh + g.po_pt) * g.po_Wp + ow + g.po_pl;
+                int32_t sum = 0;
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
+                    const uint32_t col0 = tc.n0 + cbase + c0;
+                    if (col0 >= g.cols) break;
+                    const uint32_t live = min(CW, g.cols - col0);   // channels past the output hold x = 0
+                    uint32_t hw[CW / 4], lw[CW / 4];
+#pragma unroll
+                    for (uint32_t q = 0; q < CW / 4; ++q) {
+                        uint32_t a = pk[(c0 + 4 * q) / 2], b = pk[(c0 + 4 * q) / 2 + 1];
+                        if (4 * q + 4 > live) {
+                            const uint32_t k0 = 4 * q;
+                            if (k0 + 0 >= live) a &= 0xFFFF0000u;
+                            if (k0 + 1 >= live) a &= 0x0000FFFFu;
+                            if (k0 + 2 >= live) b &= 0xFFFF0000u;
+                            if (k0 + 3 >= live) b &= 0x0000FFFFu;
+                        }
+                        hw[q] = __byte_perm(a, b, 0x7531);
+                        lw[q] = __byte_perm(a, b, 0x6420) ^ 0x80808080u;
+                        sum += (int32_t)(int16_t)(a & 0xFFFFu) + (int32_t)(int16_t)(a >> 16) +
+                               (int32_t)(int16_t)(b & 0xFFFFu) + (int32_t)(int16_t)(b >> 16);
+                    }
+                    sum -= 128 * (int32_t)live;
+                    int8_t* dst = g.po + pix * g.po_Cp + col0;
+#pragma unroll
+                    for (uint32_t q = 0; q < CW / 16; ++q) {
+                        *(uint4*)(dst + 16 * q) = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+                        *(uint4*)(dst + g.po_plane + 16 * q) = make_uint4(lw[4 * q], lw[4 * q + 1], lw[4 * q + 2], lw[4 * q + 3]);
+                    }
+                }
+                atomicAdd(g.po_S + pix, sum);
+            }
+            if (!g.out) continue;
+            int16_t* orow = g.out + o_off;
 #pragma unroll
             for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
                 const uint32_t col0 = tc.n0 + cbase + c0;
@@ -852,9 +897,12 @@ int make_conv_map(CUtensorMap* m, const ConvA& c) {
     const uint32_t bw = 1u << c.bw_log, bh = 1u << c.bh_log, bn = 1u << c.bn_log;
     if (bw * bh * bn != (uint32_t)BM || bw * c.sw > 256 || bh * c.sh > 256 || c.sw > 8 || c.sh > 8)
         return set_error(CM_EINVAL, "conv tile shape");
-    const uint64_t row = (uint64_t)c.Wp * c.Cp, img = row * c.Hp;
+    const uint64_t row = c.row_pitch ? c.row_pitch : (uint64_t)c.Wp * c.Cp;
+    const uint64_t img = c.img_pitch ? c.img_pitch : row * c.Hp;
+    const uint64_t plane = c.plane_pitch ? c.plane_pitch : img * c.nimg;
+    if ((row | img | plane) & 15u) return set_error(CM_EINVAL, "conv plane pitches misaligned");
     const cuuint64_t dims[5] = {c.KR, c.Wp, c.Hp, c.nimg, 2};
-    const cuuint64_t strides[4] = {(cuuint64_t)c.Cp, (cuuint64_t)row, (cuuint64_t)img, (cuuint64_t)img * c.nimg};
+    const cuuint64_t strides[4] = {(cuuint64_t)c.Cp, (cuuint64_t)row, (cuuint64_t)img, (cuuint64_t)plane};
     const cuuint32_t box[5] = {(cuuint32_t)BK, bw * c.sw, bh * c.sh, bn, 1};
     const cuuint32_t estr[5] = {1, c.sw, c.sh, 1, 1};
     CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void*)c.planes, dims, strides, box, estr,
@@ -1013,6 +1061,8 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.rowterm = p.rowterm; g.colterm = p.colterm;
     g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
     g.epi = p.epi; g.resid = p.resid;
+    g.po = p.po.planes; g.po_S = p.po.S; g.po_plane = p.po.plane_pitch;
+    g.po_Hp = p.po.Hp; g.po_Wp = p.po.Wp; g.po_Cp = p.po.Cp; g.po_pt = p.po.pt; g.po_pl = p.po.pl;
     if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
     return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);
 }

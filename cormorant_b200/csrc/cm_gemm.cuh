@@ -25,10 +25,27 @@ namespace cm {
 // bh rows (stride sh), bn images} at (kb*128, ow0*sw, oh0*sh + r*dh, n0).
 // Tile rows are (image, row, column) in that order with bw*bh*bn = 128,
 // all three powers of two.
+// Hp and Wp are the extents the boxes may read (rows and columns past them read as
+// zero); the pitches give the layout, so a view into a larger plane image (a
+// channels-last image with a wider padding frame) is a shifted base pointer with
+// the image's own pitches.  Pitches of 0 mean the dense layout of these extents.
 struct ConvA {
     const int8_t* planes;
     uint32_t nimg, Cp, Hp, Wp, KR, KR_pad, kh, sh, sw, dh;
     uint32_t out_h, out_w, bw_log, bh_log, bn_log;
+    uint64_t row_pitch = 0, img_pitch = 0, plane_pitch = 0;   // bytes
+};
+
+// Channels-last plane image written by a conv GEMM's epilogue (the consumer convs'
+// A operand, produced without a separate split pass): output pixel (n, oh, ow),
+// channel c -> hi byte at planes[((n*Hp + oh + pt)*Wp + ow + pl)*Cp + c], lo' byte
+// plane_pitch further, and S[(n*Hp + oh + pt)*Wp + ow + pl] += x - 128 (atomic;
+// the producer clears S first).
+struct PlaneOut {
+    int8_t* planes = nullptr;
+    int32_t* S = nullptr;
+    uint64_t plane_pitch = 0;
+    uint32_t Hp = 0, Wp = 0, Cp = 0, pt = 0, pl = 0;
 };
 
 struct GemmPlan {
@@ -53,6 +70,8 @@ struct GemmPlan {
     // bit 0 = ReLU -- VectorOP ADD / RELU applied to the narrowed words
     uint32_t epi = 0;
     const int16_t* resid = nullptr;
+    // conv mode: also write the output as a plane image (out may then be null)
+    PlaneOut po;
 };
 
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude

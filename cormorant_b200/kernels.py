@@ -106,6 +106,61 @@ def ConvKernelFused(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h,
     check(L.cm_conv_fused(*args) if stream is None else L.cm_conv_fused_async(*args, _stream(stream)))
 
 
+class PlaneImage:
+    """A conv input held as channels-last int8 hi/lo planes with its padding frame
+    (cm_planes_create): written by a producing conv's GEMM epilogue, read in place of
+    the NCHW tensor by implicit-GEMM convs.  Not a reference object."""
+
+    def __init__(self, batch, channels, h, w, frame=(0, 0, 0, 0)):
+        self.shape = (int(batch), int(channels), int(h), int(w))
+        self.frame = tuple(int(f) for f in frame)
+        self.ptr = lib().cm_planes_create(*self.shape, *self.frame)
+        if not self.ptr:
+            msg = lib().cm_last_error()
+            raise CormorantError(-5, (msg or b"cm_planes_create failed").decode(errors="replace"))
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            lib().cm_planes_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def conv_plane_frame(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1, dilation_h=1,
+                     dilation_w=1, pad_top=0, pad_left=0, has_bias=1, is_depthwise=0):
+    """The padding frame (top, left, bottom, right) a conv with these arguments needs
+    in a PlaneImage it reads, or None when it reads its NCHW input instead."""
+    import ctypes as C
+    fr = (C.c_uint * 4)()
+    ok = lib().cm_conv_plane_frame(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                                   dilation_h, dilation_w, pad_top, pad_left, int(has_bias), int(is_depthwise), fr)
+    return tuple(int(v) for v in fr) if ok else None
+
+
+def _planes(p) -> int | None:
+    return None if p is None else p.ptr
+
+
+def ConvKernelPlanes(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1,
+                     stride_w=1, dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=None, is_depthwise=0,
+                     epilogue=EPI_NONE, resid=None, stream=None) -> None:
+    """ConvKernelFused with plane images (cm_conv_planes): `xp` (a PlaneImage or None)
+    is read instead of `x` when this conv can; `yp` receives the output, and `y` may
+    then be None."""
+    if has_bias is None:
+        has_bias = int(bias is not None)
+    L = lib()
+    args = (_addr(x), _planes(xp), _addr(weight), _addr(bias), _addr(y), _planes(yp), batch, in_ch, in_h, in_w,
+            out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
+            int(has_bias), int(is_depthwise), int(epilogue), _addr(resid))
+    check(L.cm_conv_planes(*args) if stream is None else L.cm_conv_planes_async(*args, _stream(stream)))
+
+
 def MatmulKernelFused(a, b, c, n, k, m, batch=1, a_batch_stride=None, b_batch_stride=None, c_batch_stride=None,
                       epilogue=EPI_ADD, bias=None, stream=None) -> None:
     """MatmulKernel followed by VectorOP ADD of a bias row broadcast over the n rows

@@ -44,6 +44,7 @@ class Net:
     aliases: dict = field(default_factory=dict)      # Reshape: name -> name
     macs_per_image: int = 0
     source_kinds: tuple = ()                         # kernel kinds of the call list before fusion
+    planes: dict = field(default_factory=dict)       # plane image -> (batch, C, H, W, frame)
 
     def buf(self, name: str, words: int) -> str:
         self.buffers[name] = int(words)
@@ -193,6 +194,8 @@ def _inputs(node) -> list:
     kind = node[0]
     if kind == "conv":
         names = [node[1], node[2], node[3]] + ([node[7]] if len(node) > 7 else [])
+        if len(node) > 8 and node[1] is None:
+            names[0] = node[8]                       # read from its plane image only
     elif kind == "matmul":
         names = [node[1], node[2]] + ([node[6]] if len(node) > 6 else [])
     elif kind == "vectorop":
@@ -203,7 +206,72 @@ def _inputs(node) -> list:
 
 
 def output_of(node) -> str:
-    return node[4] if node[0] == "conv" else node[3] if node[0] in ("vectorop", "matmul") else node[2]
+    if node[0] == "conv":
+        return node[4] if node[4] is not None else node[9]
+    return node[3] if node[0] in ("vectorop", "matmul") else node[2]
+
+
+def chain(net: Net, frame_fn=None) -> Net:
+    """The call list with conv outputs that feed implicit-GEMM convs produced as plane
+    images (cm_conv_planes): the producing conv's GEMM epilogue writes the consumers'
+    channels-last operand, so their split pass disappears.  `frame_fn(args)` gives the
+    padding frame a conv reads its input with, or None when it reads the NCHW tensor
+    (default: the library's cm_conv_plane_frame).  The NCHW output is still written
+    when anything else reads it (a residual Add, a pool, a conv that cannot read plane
+    images, the network output).  Conv nodes become
+    ("conv", x, w, bias, y, args, epilogue, resid, xp, yp) with x / y None when unused."""
+    if frame_fn is None:
+        from . import kernels
+        frame_fn = lambda args: kernels.conv_plane_frame(*args)  # noqa: E731
+    R = net.resolve
+    nodes = [n if n[0] != "conv" or len(n) > 6 else (*n, 0, None) for n in net.nodes]
+    readers: dict = {}
+    for j, node in enumerate(nodes):
+        for k, name in enumerate(_inputs(node)):
+            role = "x" if node[0] == "conv" and k == 0 else "other"
+            readers.setdefault(R(name), []).append((j, role))
+    readers.setdefault(R(net.output), []).append((-1, "other"))
+    xp_of: dict = {}                                  # consumer node -> plane image
+    produce: dict = {}                                # producer node -> (plane image, keep y)
+    planes: dict = {}
+    for i, node in enumerate(nodes):
+        if node[0] != "conv":
+            continue
+        y = R(node[4])
+        frames = [(j, frame_fn(nodes[j][5])) for j, role in readers.get(y, []) if role == "x"]
+        usable = [(j, f) for j, f in frames if f is not None]
+        if not usable:
+            continue
+        frame = tuple(max(f[k] for _, f in usable) for k in range(4))
+        pname = y + "@planes"
+        a = node[5]
+        planes[pname] = (net.batch, a[4], a[5], a[6], frame)
+        keep_y = len(usable) < len(readers[y])
+        produce[i] = (pname, keep_y)
+        for j, _ in usable:
+            xp_of[j] = (pname, keep_y)
+    out = []
+    for i, node in enumerate(nodes):
+        if node[0] != "conv":
+            out.append(node)
+            continue
+        _, x, wn, bn, y, args, epi, resid = node
+        xp = None
+        if i in xp_of:
+            xp, keep = xp_of[i]
+            x = x if keep else None
+        yp = None
+        if i in produce:
+            yp, keep = produce[i]
+            y = y if keep else None
+        out.append(("conv", x, wn, bn, y, args, epi, resid, xp, yp))
+    used = {R(n) for node in out for n in _inputs(node) if n in net.buffers or n in net.aliases}
+    used |= {R(output_of(node)) for node in out if output_of(node) in net.buffers or output_of(node) in net.aliases}
+    used |= {R(net.input), R(net.output)}
+    return Net(net.name + "+planes", net.batch, net.input, net.output,
+               buffers={k: v for k, v in net.buffers.items() if k in used}, consts=dict(net.consts), nodes=out,
+               aliases=dict(net.aliases), macs_per_image=net.macs_per_image,
+               source_kinds=net.source_kinds or tuple(sorted({n[0] for n in net.nodes})), planes=planes)
 
 
 def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
@@ -288,7 +356,10 @@ def execute(net: Net, backend, bufs: dict) -> None:
     R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
     for node in net.nodes:
         kind = node[0]
-        if kind == "conv" and len(node) > 6:
+        if kind == "conv" and len(node) > 8:
+            _, x, wn, bn, y, args, epi, resid, xp, yp = node
+            backend.conv_planes(R(x), R(xp), R(wn), R(bn), R(y), R(yp), *args, epi, R(resid))
+        elif kind == "conv" and len(node) > 6:
             _, x, wn, bn, y, args, epi, resid = node
             backend.conv_fused(R(x), R(wn), R(bn), R(y), *args, epi, R(resid))
         elif kind == "conv":
@@ -335,6 +406,10 @@ class GpuBackend:
         *geo, epi, resid = args
         self.k.ConvKernelFused(x, w, bias, y, *geo, epilogue=epi, resid=resid, stream=self.stream)
 
+    def conv_planes(self, x, xp, w, bias, y, yp, *args):
+        *geo, epi, resid = args
+        self.k.ConvKernelPlanes(x, xp, w, bias, y, yp, *geo, epilogue=epi, resid=resid, stream=self.stream)
+
     def pool(self, x, y, *args):
         self.k.PoolingKernel(x, y, *args, stream=self.stream)
 
@@ -347,6 +422,10 @@ def gpu_buffers(net: Net, x=None):
         bufs[name] = torch.empty(max(words, 1), dtype=torch.int16, device="cuda")
     for name, arr in net.consts.items():
         bufs[name] = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
+    if net.planes:
+        from .kernels import PlaneImage
+        for name, (n, c, h, w, frame) in net.planes.items():
+            bufs[name] = PlaneImage(n, c, h, w, frame)
     if x is not None:
         bufs[net.input].copy_(torch.from_numpy(np.ascontiguousarray(x, np.int16)))
     return bufs

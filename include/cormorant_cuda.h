@@ -195,6 +195,47 @@ int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* 
                         unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
                         const int16_t* resid, cm_stream_t stream);
 
+/* ---- Plane images: conv outputs produced as the next conv's operand ----------------
+ * (no reference counterpart; results are those of the plain calls, word for word)
+ * The tensor-core conv reads its input x [batch][C][H][W] as channels-last int8 hi/lo
+ * planes with the spatial padding written out, which a split pass normally builds
+ * from x on every call.  A cm_planes_t holds that form of one tensor; a conv whose
+ * output feeds such convs can write it directly from its GEMM epilogue, and the
+ * consumers read it instead of x:
+ *   cm_planes_create     -- a plane image of a [batch][channels][h][w] tensor with the
+ *                           given frame (rows / columns of padding on each side);
+ *                           needs cm_init; NULL on failure (cm_last_error)
+ *   cm_conv_plane_frame  -- 1 if a conv with these arguments reads its input from a
+ *                           plane image (its tensor-core implicit-GEMM path, at the
+ *                           current cm_set_direct_limit), filling frame[4] = the
+ *                           padding {top, left, bottom, right} it needs; else 0
+ *   cm_conv_planes       -- cm_conv_fused with plane images: xp (may be NULL) replaces x
+ *                           when the conv reads plane images and xp's tensor matches and
+ *                           its frame covers the needed padding (otherwise x is read,
+ *                           and a NULL x is CM_EINVAL); yp (may be NULL) receives the
+ *                           output, y may then be NULL.  A consumer whose padding is
+ *                           smaller than the frame reads the image in place. */
+typedef struct cm_planes cm_planes_t;
+cm_planes_t* cm_planes_create(unsigned batch, unsigned channels, unsigned h, unsigned w, unsigned pad_top,
+                              unsigned pad_left, unsigned pad_bottom, unsigned pad_right);
+void cm_planes_destroy(cm_planes_t* planes);
+int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                        unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                        unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                        unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned* frame);
+int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
+                   int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w,
+                   unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
+                   unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w,
+                   unsigned pad_top, unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
+                   unsigned epilogue, const int16_t* resid);
+int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
+                         int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h,
+                         unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh,
+                         unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                         unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
+                         unsigned is_depthwise, unsigned epilogue, const int16_t* resid, cm_stream_t stream);
+
 /* ---- PoolingKernel -------------------------------------------------------------
  * pool_type CM_POOL_MAX / AVG / LP (any value >= 2 is LP); lp_order 1 = sum|x|,
  * any other value = sqrt(sum x^2); count_include_pad selects the AVG divisor. */

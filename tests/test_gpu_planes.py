@@ -1,0 +1,132 @@
+"""Plane images (cm_conv_planes): a conv's output written by its GEMM epilogue as the
+channels-last operand of the implicit-GEMM convs that read it.  Not a reference kernel:
+every consumer's output must equal the reference call sequence producer -> consumer run
+on NCHW tensors by the oracle, word for word."""
+import numpy as np
+import pytest
+
+from tests._util import assert_same, dev, empty, host, rand16
+
+pytestmark = pytest.mark.gpu
+
+
+def osz(n, k, s, p):
+    return (n + 2 * p - k) // s + 1
+
+
+def geo(N, C, H, W, M, k, s, p):
+    return (N, C, H, W, M, osz(H, k, s, p), osz(W, k, s, p), k, k, s, s, 1, 1, p, p, 1, 0)
+
+
+def oracle(port, x, w, b, g, epi=0, resid=None):
+    size = g[0] * g[4] * g[5] * g[6]
+    y = port.conv(x, w, b, *g)[:size]
+    if epi & 2:
+        y = port.vectorop(y, resid, size, 0, 1, 0, 0)[:size]
+    if epi & 1:
+        y = port.vectorop(y, None, size, 4, 1, 0, 0)[:size]
+    return y
+
+
+def weights(rng, g):
+    return rand16(rng, g[4] * g[1] * g[7] * g[8], -256, 256), rand16(rng, g[4], -256, 256)
+
+
+# (producer N, C, H, W, M, k, s, p), (consumer M, k, s, p), producer epilogue
+CASES = [
+    ((3, 64, 14, 14, 64, 3, 1, 1), (64, 3, 1, 1), 1),      # 64-column producer tiles
+    ((3, 64, 14, 14, 128, 3, 1, 1), (128, 3, 1, 1), 1),    # 128-column tiles on CTA pairs
+    ((2, 32, 16, 16, 40, 3, 1, 1), (24, 3, 1, 1), 0),      # 40 channels: a partial 16-channel chunk
+    ((4, 128, 28, 28, 64, 3, 1, 1), (96, 1, 2, 0), 1),     # consumer padding smaller than the frame
+    ((2, 128, 28, 28, 64, 3, 1, 1), (96, 3, 2, 1), 1),     # stride-2 consumer
+    ((2, 3, 64, 64, 64, 7, 2, 3), (64, 3, 1, 1), 1),       # space-to-depth producer (stem form)
+    ((5, 64, 7, 7, 96, 3, 1, 1), (80, 3, 1, 1), 1),        # 7x7 maps, tile rows past the images
+]
+
+
+@pytest.mark.parametrize("prod,cons,epi", CASES)
+@pytest.mark.parametrize("keep_y", [False, True])
+def test_producer_consumer(cm, port, prod, cons, epi, keep_y):
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(sum(prod) * 31 + sum(cons) + epi)
+    g1 = geo(*prod)
+    N, M1, oh, ow = g1[0], g1[4], g1[5], g1[6]
+    g2 = geo(N, M1, oh, ow, *cons)
+    frame = kernels.conv_plane_frame(*g2)
+    assert frame is not None, "consumer must read plane images"
+    x = rand16(rng, N * g1[1] * g1[2] * g1[3], -1024, 1024)
+    w1, b1 = weights(rng, g1)
+    w2, b2 = weights(rng, g2)
+    y1_want = oracle(port, x, w1, b1, g1, epi)
+    y2_want = oracle(port, y1_want, w2, b2, g2)
+    P = kernels.PlaneImage(N, M1, oh, ow, frame)
+    y1 = empty(y1_want.size) if keep_y else None
+    kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), y1, P, *g1, epilogue=epi)
+    y2 = empty(y2_want.size)
+    kernels.ConvKernelPlanes(None, P, dev(w2), dev(b2), y2, None, *g2)
+    if keep_y:
+        assert_same(host(y1), y1_want, f"producer y {prod}")
+    assert_same(host(y2), y2_want, f"consumer {prod} -> {cons}")
+
+
+def test_producer_on_cuda_core_path_and_residual(cm, port):
+    """A producer on the CUDA-core path fills the image by a split pass; a consumer with a
+    residual epilogue and its own plane output chains a third conv."""
+    from cormorant_b200 import _lib, kernels
+    L = _lib.lib()
+    rng = np.random.default_rng(5)
+    g1 = geo(2, 16, 12, 12, 64, 3, 1, 1)
+    g2 = geo(2, 64, 12, 12, 64, 3, 1, 1)
+    x = rand16(rng, 2 * 16 * 144)
+    w1, b1 = weights(rng, g1)
+    w2, b2 = weights(rng, g2)
+    w3, b3 = weights(rng, g2)
+    r = rand16(rng, 2 * 64 * 144)
+    y1 = oracle(port, x, w1, b1, g1, 1)
+    y2 = oracle(port, y1, w2, b2, g2, 3, r)
+    y3 = oracle(port, y2, w3, b3, g2, 1)
+    fr = kernels.conv_plane_frame(*g2)
+    P1, P2 = kernels.PlaneImage(2, 64, 12, 12, fr), kernels.PlaneImage(2, 64, 12, 12, fr)
+    old = L.cm_set_direct_limit(1 << 40)                  # producer on the CUDA-core path
+    try:
+        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P1, *g1, epilogue=1)
+    finally:
+        L.cm_set_direct_limit(0)                          # the rest on the tensor cores
+    try:
+        got2 = empty(y2.size)
+        kernels.ConvKernelPlanes(None, P1, dev(w2), dev(b2), got2, P2, *g2, epilogue=3, resid=dev(r))
+        got3 = empty(y3.size)
+        kernels.ConvKernelPlanes(None, P2, dev(w3), dev(b3), got3, None, *g2, epilogue=1)
+    finally:
+        L.cm_set_direct_limit(old)
+    assert_same(host(got2), y2, "residual consumer")
+    assert_same(host(got3), y3, "third conv")
+
+
+def test_unusable_image_needs_x(cm, port):
+    """A conv that cannot read the image (column dilation: not the implicit path, or a
+    frame too narrow) falls back to x, and without x reports CM_EINVAL."""
+    from cormorant_b200 import CormorantError, kernels
+    rng = np.random.default_rng(9)
+    g1 = geo(2, 64, 14, 14, 64, 3, 1, 1)
+    x = rand16(rng, 2 * 64 * 196)
+    w1, b1 = weights(rng, g1)
+    y1 = oracle(port, x, w1, b1, g1)
+    P = kernels.PlaneImage(2, 64, 14, 14, (0, 0, 0, 0))  # no frame: a padded consumer cannot use it
+    kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1)
+    g2 = geo(2, 64, 14, 14, 64, 3, 1, 1)
+    w2, b2 = weights(rng, g2)
+    with pytest.raises(CormorantError):
+        kernels.ConvKernelPlanes(None, P, dev(w2), dev(b2), empty(2 * 64 * 196), None, *g2)
+    y2 = empty(2 * 64 * 196)
+    kernels.ConvKernelPlanes(dev(y1), P, dev(w2), dev(b2), y2, None, *g2)   # falls back to x
+    assert_same(host(y2), oracle(port, y1, w2, b2, g2), "fallback to x")
+    # column dilation: explicit im2col path reads x only
+    g3 = (2, 64, 14, 14, 32, 14, 12, 3, 3, 1, 1, 1, 2, 1, 1, 1, 0)
+    from cormorant_b200 import kernels as k
+    assert k.conv_plane_frame(*g3) is None
+    w3, b3 = rand16(rng, 32 * 64 * 9, -256, 256), rand16(rng, 32, -256, 256)
+    with pytest.raises(CormorantError):
+        kernels.ConvKernelPlanes(None, P, dev(w3), dev(b3), empty(2 * 32 * 14 * 12), None, *g3)
+    with pytest.raises(CormorantError):                  # output image of another shape
+        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, kernels.PlaneImage(2, 64, 7, 7), *g1)

@@ -45,6 +45,17 @@ class OracleBackend:
             t = self.chk.vectorop(t, None, y.size, networks.OP_RELU, 1, 0, 0)[: y.size]
         y[:] = t
 
+    def conv_planes(self, x, xp, w, bias, y, yp, *args):
+        """A plane image on the checker is the NCHW tensor itself."""
+        *geo, epi, resid = args
+        src = x if x is not None else xp
+        out = np.zeros(geo[0] * geo[4] * geo[5] * geo[6], np.int16)
+        self.conv_fused(src, w, bias, out, *geo, epi, resid)
+        if y is not None:
+            y[:] = out
+        if yp is not None:
+            yp[:] = out
+
     def pool(self, x, y, *args):
         y[:] = self.chk.pool(x, *args)[: y.size]
 
@@ -52,6 +63,8 @@ class OracleBackend:
 def cpu_buffers(net, x):
     bufs = {name: np.zeros(max(w, 1), np.int16) for name, w in net.buffers.items()}
     bufs.update({name: np.asarray(a, np.int16) for name, a in net.consts.items()})
+    for name, (n, c, h, w, _) in net.planes.items():
+        bufs[name] = np.zeros(n * c * h * w, np.int16)
     bufs[net.input][:] = x
     return bufs
 
@@ -180,3 +193,48 @@ def test_resnet18_fused_batch256_sampled_images(cm, port):
     networks.execute(small, OracleBackend(port), want)
     got = np.concatenate([logits[0], logits[255]])
     assert_same(got, want[small.resolve(small.output)], "fused resnet18 logits of images 0 and 255")
+
+
+def test_chain_pass_resnet_structure():
+    """Conv outputs read by implicit-GEMM convs become plane images; NCHW outputs stay only
+    where a residual, a pool or the network output reads them."""
+    net = networks.chain(networks.fuse(networks.resnet18(batch=2)))
+    convs = [n for n in net.nodes if n[0] == "conv"]
+    assert len(convs) == 20 and len(net.planes) == 15
+    assert sum(1 for n in convs if n[8] is not None) == 18      # every conv but the stem and layer 1's first
+    assert sum(1 for n in convs if n[1] is None) == 14          # inputs read only from plane images
+    assert sum(1 for n in convs if n[4] is None) == 11          # outputs written only as plane images
+    assert all(n[8] is not None for n in convs if n[1] is None)
+    assert all(n[9] is not None for n in convs if n[4] is None)
+    for name, (b, c, h, w, frame) in net.planes.items():
+        assert b == 2 and len(frame) == 4 and min(frame) >= 0
+    assert networks.chain(networks.fuse(networks.lenet5())).planes == {}    # batch-1 convs read NCHW
+
+
+def test_chained_call_list_equals_reference_sequence_on_cpu(port):
+    """The plane-chained ResNet call list, replayed on the checker (a plane image = its
+    NCHW tensor), gives the unchained list's logits."""
+    net = networks.resnet18(batch=1)
+    fn = networks.chain(networks.fuse(net), frame_fn=lambda a: (1, 1, 1, 1) if a[7] > 1 and a[9] == 1 else None)
+    x = networks.make_input(net)
+    a, b = cpu_buffers(net, x), cpu_buffers(fn, x)
+    networks.execute(net, OracleBackend(port), a)
+    networks.execute(fn, OracleBackend(port), b)
+    assert_same(b[fn.resolve(fn.output)], a[net.resolve(net.output)], "chained resnet logits")
+
+
+@pytest.mark.gpu
+def test_resnet18_chained_batch4_every_output(cm, port):
+    """Plane images on the GPU: every NCHW tensor the chained list still writes, and the
+    logits, equal the oracle's."""
+    import torch
+    net = networks.chain(networks.fuse(networks.resnet18(batch=4)))
+    assert net.planes
+    x = networks.make_input(net)
+    want = cpu_buffers(net, x)
+    networks.execute(net, OracleBackend(port), want)
+    bufs = networks.gpu_buffers(net, x)
+    networks.execute(net, networks.GpuBackend(), bufs)
+    torch.cuda.synchronize()
+    for name in net.buffers:
+        assert_same(bufs[name].cpu().numpy()[: net.buffers[name]], want[name][: net.buffers[name]], f"resnet {name}")
