@@ -373,15 +373,18 @@ __global__ void __launch_bounds__(256) conv_nhwc_border_kernel(NhwcGeom g, int8_
 }
 
 // S of a plane image before its producer adds the channel sums: 0 at the image's
-// pixels, -128*C on the frame (x = 0 in every channel).  Grid (x: columns, y: rows,
-// z: images).
-__global__ void __launch_bounds__(256) planes_reset_S_kernel(int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
-                                                             uint32_t H, uint32_t W, uint32_t pt, uint32_t pl,
-                                                             int32_t frame) {
-    const uint32_t w = blockIdx.x * blockDim.x + threadIdx.x, h = blockIdx.y, n = blockIdx.z;
-    if (w >= Wp) return;
-    const bool inside = h >= pt && h < pt + H && w >= pl && w < pl + W;
-    S[((uint64_t)n * Hp + h) * Wp + w] = inside ? 0 : frame;
+// pixels, -128*C on the frame (x = 0 in every channel).  Grid-stride over the
+// n*Hp*Wp words (multiply-high divisions by Wp and Hp).
+__global__ void __launch_bounds__(256) planes_reset_S_kernel(int32_t* __restrict__ S, uint64_t total, FastDiv fwp,
+                                                             FastDiv fhp, uint32_t H, uint32_t W, uint32_t pt,
+                                                             uint32_t pl, int32_t frame) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+        // rows of one image chunk stay below 2^31 words (checked by the caller)
+        const uint32_t row = fwp.div((uint32_t)t), w = (uint32_t)t - row * fwp.d;
+        const uint32_t h = row - fhp.div(row) * fhp.d;
+        const bool inside = h >= pt && h < pt + H && w >= pl && w < pl + W;
+        S[t] = inside ? 0 : frame;
+    }
 }
 
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
@@ -401,28 +404,32 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
     }
 }
 
-// Separable form for rows of at least 16 outputs: block = output row oh of image n
-// (grid (out_h, images)).  The kh input rows of S it covers are summed column by column
-// into shared memory (coalesced loads), then each output adds kw column sums: about
-// kh*Wp/out_w + kw reads per output instead of kh*kw, and no divisions.
+// Separable form for rows of at least 16 outputs: warp = output row oh of image n
+// (4 rows per block, grid (ceil(out_h / 4), images)).  Its lanes sum the kh input rows
+// of S column by column into the warp's slice of shared memory (coalesced loads), then
+// each output adds kw column sums: about kh*Wp/out_w + kw reads per output instead of
+// kh*kw, no divisions, and no block-wide barrier.
 constexpr uint32_t kRowtermThreads = 128;
 
 __global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(const int32_t* __restrict__ S, uint32_t Hp,
                                                                           uint32_t Wp, uint32_t out_h, uint32_t out_w,
                                                                           uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
                                                                           uint32_t dh, int32_t* __restrict__ rowterm) {
-    extern __shared__ uint32_t colsum[];
-    const uint32_t oh = blockIdx.x, n = blockIdx.y;
-    const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp;
+    extern __shared__ uint32_t colsum_all[];
+    const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    const uint32_t oh = blockIdx.x * (kRowtermThreads / 32) + warp, n = blockIdx.y;
+    if (oh >= out_h) return;
     const uint32_t need = (out_w - 1) * sw + kw;
-    for (uint32_t c = threadIdx.x; c < need; c += blockDim.x) {
+    uint32_t* colsum = colsum_all + warp * need;
+    const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp;
+    for (uint32_t c = lane; c < need; c += 32) {
         uint32_t v = 0;
         for (uint32_t r = 0; r < kh; ++r) v += (uint32_t)__ldg(b + (uint64_t)r * dh * Wp + c);
         colsum[c] = v;
     }
-    __syncthreads();
+    __syncwarp();
     int32_t* out = rowterm + ((uint64_t)n * out_h + oh) * out_w;
-    for (uint32_t ow = threadIdx.x; ow < out_w; ow += blockDim.x) {
+    for (uint32_t ow = lane; ow < out_w; ow += 32) {
         uint32_t sum = 0;
         for (uint32_t q = 0; q < kw; ++q) sum += colsum[ow * sw + q];
         out[ow] = (int32_t)(sum * 128u);
@@ -433,11 +440,11 @@ __global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(cons
 void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t Wp, uint32_t out_h, uint32_t out_w,
                     uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t dh, uint32_t nb, int32_t* rt,
                     cudaStream_t s) {
-    const uint64_t need_bytes = ((uint64_t)(out_w - 1) * sw + kw) * 4;
+    const uint64_t need_bytes = ((uint64_t)(out_w - 1) * sw + kw) * 4 * (kRowtermThreads / 32);
     if (out_w >= 16 && need_bytes <= 48u * 1024u) {
         for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
             const uint32_t bz = std::min(65535u, nb - b0);
-            conv_rowterm_rows_kernel<<<dim3(out_h, bz), kRowtermThreads, (size_t)need_bytes, s>>>(
+            conv_rowterm_rows_kernel<<<dim3((out_h + 3) / 4, bz), kRowtermThreads, (size_t)need_bytes, s>>>(
                 S + (uint64_t)b0 * Hp * Wp, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, rt + (uint64_t)b0 * out_h * out_w);
             count_launch();
         }
@@ -1016,10 +1023,14 @@ int planes_from_tensor(const Context* cx, const int16_t* x, cm_planes* yp, cudaS
 // Clears the channel sums of plane image yp (images [n0, n0 + nb)) before a GEMM
 // epilogue adds into them.
 int planes_reset(cm_planes* yp, cudaStream_t s) {
-    for (uint32_t b0 = 0; b0 < yp->n; b0 += 65535u) {
-        const uint32_t bz = std::min(65535u, yp->n - b0);
-        planes_reset_S_kernel<<<dim3((yp->Wp + 255) / 256, yp->Hp, bz), 256, 0, s>>>(
-            yp->S + (uint64_t)b0 * yp->Hp * yp->Wp, yp->Hp, yp->Wp, yp->H, yp->W, yp->pt, yp->pl,
+    const Context* cx = ctx();
+    const uint64_t img = (uint64_t)yp->Hp * yp->Wp;
+    const uint32_t per = (uint32_t)std::max<uint64_t>(1, ((1ull << 31) / img));   // images per launch: words < 2^31
+    for (uint32_t b0 = 0; b0 < yp->n; b0 += per) {
+        const uint32_t nb = std::min(per, yp->n - b0);
+        const uint64_t total = nb * img;
+        planes_reset_S_kernel<<<grid_for(cx, total, 256, 4), 256, 0, s>>>(
+            yp->S + (uint64_t)b0 * img, total, FastDiv(yp->Wp), FastDiv(yp->Hp), yp->H, yp->W, yp->pt, yp->pl,
             (int32_t)(0u - 128u * yp->C));
         count_launch();
     }
