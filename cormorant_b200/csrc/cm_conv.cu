@@ -1050,9 +1050,10 @@ PlaneOut plane_out(cm_planes* yp, uint64_t n0) {
 
 // xv: a plane image that fits this conv's implicit plan (read instead of x); po:
 // the output's plane image, written by the GEMM epilogue (implicit / space-to-depth
-// paths only; y may then be null).
+// paths only; y may then be null); rp: the residual's plane image (same paths; resid
+// may then be null).
 int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, const int16_t* bias, int16_t* y,
-              cm_planes* po, unsigned batch, unsigned in_ch,
+              cm_planes* po, const cm_planes* rp, unsigned batch, unsigned in_ch,
               unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
               unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
               unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epi, const int16_t* resid,
@@ -1212,6 +1213,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
             if (po) p.po = plane_out(po, n0);
+            if (rp) p.rp = plane_out(const_cast<cm_planes*>(rp), n0);
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -1290,6 +1292,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
             if (po) p.po = plane_out(po, n0);
+            if (rp) p.rp = plane_out(const_cast<cm_planes*>(rp), n0);
             rc = gemm_launch(cx, p, s);
         }
         scratch_free(scratch, s);
@@ -1376,9 +1379,10 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
               cm_planes* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
               unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
               unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
-              unsigned is_depthwise, unsigned epi, const int16_t* resid, cm_stream_t stream) {
-    if (!xp && !yp)
-        return conv_core(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+              unsigned is_depthwise, unsigned epi, const int16_t* resid, const cm_planes* rp, cm_stream_t stream) {
+    if (!(epi & 2u)) rp = nullptr;
+    if (!xp && !yp && !rp)
+        return conv_core(x, nullptr, weight, bias, y, nullptr, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                          stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi,
                          resid, stream);
     const Context* cx;
@@ -1389,6 +1393,8 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
     if (yp && (yp->n != batch || yp->C != out_ch || yp->H != out_h || yp->W != out_w))
         return set_error(CM_EINVAL, "cm_conv: output plane image is %ux%ux%ux%u, the output %ux%ux%ux%u", yp->n, yp->C,
                          yp->H, yp->W, batch, out_ch, out_h, out_w);
+    if (rp && (rp->device != cx->device || rp->n != batch || rp->C != out_ch || rp->H != out_h || rp->W != out_w))
+        return set_error(CM_EINVAL, "cm_conv: residual plane image does not match the output");
     ImplicitPlan ip;
     const ConvPath path = conv_path(cx->direct_max_macs, batch, in_ch, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
                                     dilation_h, dilation_w, is_depthwise, &ip);
@@ -1396,9 +1402,14 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
     if (!xv && !x && path != CP_BIAS_FILL)
         return set_error(CM_EINVAL, "cm_conv: x is null and this conv cannot read the plane image (not an implicit-GEMM "
                                     "conv, or the image's tensor or frame does not match)");
-    const bool epi_writes = yp && (path == CP_IMPLICIT || path == CP_S2D);
+    const bool gemm_epi = path == CP_IMPLICIT || path == CP_S2D;   // epilogue in the tensor-core GEMM
+    const cm_planes* rv = gemm_epi ? rp : nullptr;
+    if (rp && !rv && !resid)
+        return set_error(CM_EINVAL, "cm_conv: resid is null and this conv cannot read the residual plane image");
+    if (!rv && (epi & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv: residual buffer is null");
+    const bool epi_writes = yp && gemm_epi;
     if (!yp || epi_writes)
-        return conv_core(x, xv, weight, bias, y, epi_writes ? yp : nullptr, batch, in_ch, in_h, in_w, out_ch, out_h,
+        return conv_core(x, xv, weight, bias, y, epi_writes ? yp : nullptr, rv, batch, in_ch, in_h, in_w, out_ch, out_h,
                          out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias,
                          is_depthwise, epi, resid, stream);
     cudaStream_t s = (cudaStream_t)stream;
@@ -1409,7 +1420,7 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
         if (rc) return rc;
         yw = (int16_t*)tmp;
     }
-    rc = conv_core(x, xv, weight, bias, yw, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
+    rc = conv_core(x, xv, weight, bias, yw, nullptr, rv, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
                    stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi, resid, stream);
     if (!rc) rc = planes_from_tensor(cx, yw, yp, s);
     if (tmp) scratch_free(tmp, s);
@@ -1425,7 +1436,7 @@ extern "C" int cm_conv_async(const int16_t* x, const int16_t* weight, const int1
                              unsigned has_bias, unsigned is_depthwise, cm_stream_t stream) {
     return conv_impl(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                      stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, 0u, nullptr,
-                     stream);
+                     nullptr, stream);
 }
 
 extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
@@ -1438,7 +1449,7 @@ extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, cons
     if ((epilogue & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv_fused: residual buffer is null");
     return conv_impl(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                      stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue,
-                     resid, stream);
+                     resid, nullptr, stream);
 }
 
 extern "C" int cm_conv_fused(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
@@ -1541,13 +1552,14 @@ extern "C" int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, con
                                     unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh,
                                     unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
                                     unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
-                                    unsigned is_depthwise, unsigned epilogue, const int16_t* resid, cm_stream_t stream) {
+                                    unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
+                                    const cm_planes_t* resid_planes, cm_stream_t stream) {
     if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_planes: epilogue must be 0..3");
-    if ((epilogue & 2u) && !resid) return set_error(CM_EINVAL, "cm_conv_planes: residual buffer is null");
+    if ((epilogue & 2u) && !resid && !resid_planes) return set_error(CM_EINVAL, "cm_conv_planes: residual buffer is null");
     if (!y && !yp) return set_error(CM_EINVAL, "cm_conv_planes: neither y nor an output plane image");
     return conv_impl(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
                      stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue, resid,
-                     stream);
+                     resid_planes, stream);
 }
 
 extern "C" int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
@@ -1555,9 +1567,9 @@ extern "C" int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int
                               unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
                               unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w,
                               unsigned pad_top, unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
-                              unsigned epilogue, const int16_t* resid) {
+                              unsigned epilogue, const int16_t* resid, const cm_planes_t* resid_planes) {
     int rc = cm_conv_planes_async(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                                   stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise,
-                                  epilogue, resid, nullptr);
+                                  epilogue, resid, resid_planes, nullptr);
     return rc ? rc : finish_sync(nullptr);
 }

@@ -244,6 +244,11 @@ struct GemmArgs {
     // rows; then bit 0: v = max(v, 0)) -- VectorOP ADD / RELU semantics
     uint32_t epi;
     const int16_t* resid;
+    // conv mode: the residual (epi bit 1) read from a plane image of the output's shape
+    // instead of `resid`
+    const int8_t* rpl;
+    uint64_t rpl_plane;
+    uint32_t rpl_Hp, rpl_Wp, rpl_Cp, rpl_pt, rpl_pl;
     // conv mode: output also written as a channels-last plane image (see PlaneOut)
     int8_t* po;
     int32_t* po_S;
@@ -503,7 +508,31 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
             }
             const uint32_t rt = valid ? (uint32_t)__ldg(g.rowterm + rt_idx) : 0u;
             uint32_t addv[HALF / 2];                      // addend pairs (even column in the low half)
-            if (g.epi & 6u) {
+            if ((g.epi & 2u) && g.rpl) {
+                // residual words rebuilt from its plane image: per 16 channels one 16-byte hi
+                // run and one lo' run, x = 256*hi + lo' + 128, pairs assembled by byte permutes
+                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
+                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
+                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                const uint64_t pix = ((uint64_t)n * g.rpl_Hp + oh + g.rpl_pt) * g.rpl_Wp + ow + g.rpl_pl;
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < HALF; c0 += 16) {
+                    const uint32_t col0 = tc.n0 + cbase + c0;
+                    uint4 hv = make_uint4(0, 0, 0, 0), lv = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+                    if (valid && col0 < g.cols) {
+                        const int8_t* src = g.rpl + pix * g.rpl_Cp + col0;
+                        hv = __ldg((const uint4*)src);
+                        lv = __ldg((const uint4*)(src + g.rpl_plane));
+                    }
+                    const uint32_t h4[4] = {hv.x, hv.y, hv.z, hv.w};
+                    const uint32_t l4[4] = {lv.x ^ 0x80808080u, lv.y ^ 0x80808080u, lv.z ^ 0x80808080u, lv.w ^ 0x80808080u};
+#pragma unroll
+                    for (uint32_t q = 0; q < 4; ++q) {
+                        addv[c0 / 2 + 2 * q] = __byte_perm(l4[q], h4[q], 0x5140);
+                        addv[c0 / 2 + 2 * q + 1] = __byte_perm(l4[q], h4[q], 0x7362);
+                    }
+                }
+            } else if (g.epi & 6u) {
                 const bool res = (g.epi & 2u) != 0u;
                 const int16_t* src = res ? g.resid + o_off : g.resid;
                 const uint64_t step = res ? g.ldc : 1u;
@@ -1062,6 +1091,8 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
     g.epi = p.epi; g.resid = p.resid;
     g.po = p.po.planes; g.po_S = p.po.S; g.po_plane = p.po.plane_pitch;
+    g.rpl = p.rp.planes; g.rpl_plane = p.rp.plane_pitch;
+    g.rpl_Hp = p.rp.Hp; g.rpl_Wp = p.rp.Wp; g.rpl_Cp = p.rp.Cp; g.rpl_pt = p.rp.pt; g.rpl_pl = p.rp.pl;
     g.po_Hp = p.po.Hp; g.po_Wp = p.po.Wp; g.po_Cp = p.po.Cp; g.po_pt = p.po.pt; g.po_pl = p.po.pl;
     if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
     return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);

@@ -72,6 +72,8 @@ struct GemmPlan {
     const int16_t* resid = nullptr;
     // conv mode: also write the output as a plane image (out may then be null)
     PlaneOut po;
+    // conv mode: read the residual from this plane image (same shape as the output)
+    PlaneOut rp;
 };
 
 constexpr uint32_t kMaxGemmK = 65535;  // per-accumulator sums stay below 2^31 in magnitude

@@ -148,16 +148,17 @@ def _planes(p) -> int | None:
 
 def ConvKernelPlanes(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1,
                      stride_w=1, dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=None, is_depthwise=0,
-                     epilogue=EPI_NONE, resid=None, stream=None) -> None:
+                     epilogue=EPI_NONE, resid=None, resid_planes=None, stream=None) -> None:
     """ConvKernelFused with plane images (cm_conv_planes): `xp` (a PlaneImage or None)
     is read instead of `x` when this conv can; `yp` receives the output, and `y` may
-    then be None."""
+    then be None; `resid_planes` (a PlaneImage of the output's shape) supplies the
+    residual instead of `resid` when this conv reads plane images."""
     if has_bias is None:
         has_bias = int(bias is not None)
     L = lib()
     args = (_addr(x), _planes(xp), _addr(weight), _addr(bias), _addr(y), _planes(yp), batch, in_ch, in_h, in_w,
             out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
-            int(has_bias), int(is_depthwise), int(epilogue), _addr(resid))
+            int(has_bias), int(is_depthwise), int(epilogue), _addr(resid), _planes(resid_planes))
     check(L.cm_conv_planes(*args) if stream is None else L.cm_conv_planes_async(*args, _stream(stream)))
 
 

@@ -196,6 +196,8 @@ def _inputs(node) -> list:
         names = [node[1], node[2], node[3]] + ([node[7]] if len(node) > 7 else [])
         if len(node) > 8 and node[1] is None:
             names[0] = node[8]                       # read from its plane image only
+        if len(node) > 10 and node[7] is None and node[10] is not None:
+            names[3] = node[10]                      # residual from its plane image only
     elif kind == "matmul":
         names = [node[1], node[2]] + ([node[6]] if len(node) > 6 else [])
     elif kind == "vectorop":
@@ -214,59 +216,72 @@ def output_of(node) -> str:
 def chain(net: Net, frame_fn=None) -> Net:
     """The call list with conv outputs that feed implicit-GEMM convs produced as plane
     images (cm_conv_planes): the producing conv's GEMM epilogue writes the consumers'
-    channels-last operand, so their split pass disappears.  `frame_fn(args)` gives the
-    padding frame a conv reads its input with, or None when it reads the NCHW tensor
-    (default: the library's cm_conv_plane_frame).  The NCHW output is still written
-    when anything else reads it (a residual Add, a pool, a conv that cannot read plane
-    images, the network output).  Conv nodes become
-    ("conv", x, w, bias, y, args, epilogue, resid, xp, yp) with x / y None when unused."""
+    channels-last operand, so their split pass disappears, and a residual those convs
+    add comes from its plane image too.  `frame_fn(args)` gives the padding frame a
+    conv reads its input with, or None when it reads the NCHW tensor (default: the
+    library's cm_conv_plane_frame).  The NCHW output is still written when anything
+    else reads it (a pool, a vector op, a conv that cannot read plane images, the
+    network output).  Conv nodes become
+    ("conv", x, w, bias, y, args, epilogue, resid, xp, yp, rp) with x / y / resid None
+    when unused."""
     if frame_fn is None:
         from . import kernels
         frame_fn = lambda args: kernels.conv_plane_frame(*args)  # noqa: E731
     R = net.resolve
     nodes = [n if n[0] != "conv" or len(n) > 6 else (*n, 0, None) for n in net.nodes]
-    readers: dict = {}
+    reads_planes = {j: frame_fn(n[5]) for j, n in enumerate(nodes) if n[0] == "conv"}
+    produced = {R(n[4]): i for i, n in enumerate(nodes) if n[0] == "conv"}
+    uses: dict = {}                                   # tensor -> [(node, role)]
     for j, node in enumerate(nodes):
-        for k, name in enumerate(_inputs(node)):
-            role = "x" if node[0] == "conv" and k == 0 else "other"
-            readers.setdefault(R(name), []).append((j, role))
-    readers.setdefault(R(net.output), []).append((-1, "other"))
-    xp_of: dict = {}                                  # consumer node -> plane image
-    produce: dict = {}                                # producer node -> (plane image, keep y)
-    planes: dict = {}
-    for i, node in enumerate(nodes):
-        if node[0] != "conv":
+        if node[0] == "conv":
+            uses.setdefault(R(node[1]), []).append((j, "x"))
+            for name in (node[2], node[3]):
+                if name is not None:
+                    uses.setdefault(R(name), []).append((j, "other"))
+            if node[7] is not None:
+                uses.setdefault(R(node[7]), []).append((j, "resid"))
+        else:
+            for name in _inputs(node):
+                uses.setdefault(R(name), []).append((j, "other"))
+    uses.setdefault(R(net.output), []).append((-1, "other"))
+    xp_of, rp_of, keep_of, planes = {}, {}, {}, {}
+    for y, i in produced.items():
+        readers = uses.get(y, [])
+        x_ok = [(j, reads_planes[j]) for j, role in readers if role == "x" and reads_planes[j] is not None]
+        r_ok = [j for j, role in readers if role == "resid" and reads_planes[j] is not None]
+        if not x_ok and not r_ok:
             continue
-        y = R(node[4])
-        frames = [(j, frame_fn(nodes[j][5])) for j, role in readers.get(y, []) if role == "x"]
-        usable = [(j, f) for j, f in frames if f is not None]
-        if not usable:
-            continue
-        frame = tuple(max(f[k] for _, f in usable) for k in range(4))
+        frame = tuple(max([f[k] for _, f in x_ok] + [0]) for k in range(4))
         pname = y + "@planes"
-        a = node[5]
+        a = nodes[i][5]
         planes[pname] = (net.batch, a[4], a[5], a[6], frame)
-        keep_y = len(usable) < len(readers[y])
-        produce[i] = (pname, keep_y)
-        for j, _ in usable:
+        served = {(j, "x") for j, _ in x_ok} | {(j, "resid") for j in r_ok}
+        keep_y = any((j, role) not in served for j, role in readers)
+        keep_of[i] = (pname, keep_y)
+        for j, _ in x_ok:
             xp_of[j] = (pname, keep_y)
+        for j in r_ok:
+            rp_of[j] = (pname, keep_y)
     out = []
     for i, node in enumerate(nodes):
         if node[0] != "conv":
             out.append(node)
             continue
         _, x, wn, bn, y, args, epi, resid = node
-        xp = None
+        xp = yp = rp = None
         if i in xp_of:
             xp, keep = xp_of[i]
             x = x if keep else None
-        yp = None
-        if i in produce:
-            yp, keep = produce[i]
+        if i in rp_of:
+            rp, keep = rp_of[i]
+            resid = resid if keep else None
+        if i in keep_of:
+            yp, keep = keep_of[i]
             y = y if keep else None
-        out.append(("conv", x, wn, bn, y, args, epi, resid, xp, yp))
-    used = {R(n) for node in out for n in _inputs(node) if n in net.buffers or n in net.aliases}
-    used |= {R(output_of(node)) for node in out if output_of(node) in net.buffers or output_of(node) in net.aliases}
+        out.append(("conv", x, wn, bn, y, args, epi, resid, xp, yp, rp))
+    names = set(net.buffers) | set(net.aliases)
+    used = {R(n) for node in out for n in _inputs(node) if n in names}
+    used |= {R(output_of(node)) for node in out if output_of(node) in names}
     used |= {R(net.input), R(net.output)}
     return Net(net.name + "+planes", net.batch, net.input, net.output,
                buffers={k: v for k, v in net.buffers.items() if k in used}, consts=dict(net.consts), nodes=out,
@@ -357,8 +372,8 @@ def execute(net: Net, backend, bufs: dict) -> None:
     for node in net.nodes:
         kind = node[0]
         if kind == "conv" and len(node) > 8:
-            _, x, wn, bn, y, args, epi, resid, xp, yp = node
-            backend.conv_planes(R(x), R(xp), R(wn), R(bn), R(y), R(yp), *args, epi, R(resid))
+            _, x, wn, bn, y, args, epi, resid, xp, yp, rp = node
+            backend.conv_planes(R(x), R(xp), R(wn), R(bn), R(y), R(yp), *args, epi, R(resid), R(rp))
         elif kind == "conv" and len(node) > 6:
             _, x, wn, bn, y, args, epi, resid = node
             backend.conv_fused(R(x), R(wn), R(bn), R(y), *args, epi, R(resid))
@@ -407,8 +422,9 @@ class GpuBackend:
         self.k.ConvKernelFused(x, w, bias, y, *geo, epilogue=epi, resid=resid, stream=self.stream)
 
     def conv_planes(self, x, xp, w, bias, y, yp, *args):
-        *geo, epi, resid = args
-        self.k.ConvKernelPlanes(x, xp, w, bias, y, yp, *geo, epilogue=epi, resid=resid, stream=self.stream)
+        *geo, epi, resid, rp = args
+        self.k.ConvKernelPlanes(x, xp, w, bias, y, yp, *geo, epilogue=epi, resid=resid, resid_planes=rp,
+                                stream=self.stream)
 
     def pool(self, x, y, *args):
         self.k.PoolingKernel(x, y, *args, stream=self.stream)

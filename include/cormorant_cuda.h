@@ -214,7 +214,11 @@ int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* 
  *                           its frame covers the needed padding (otherwise x is read,
  *                           and a NULL x is CM_EINVAL); yp (may be NULL) receives the
  *                           output, y may then be NULL.  A consumer whose padding is
- *                           smaller than the frame reads the image in place. */
+ *                           smaller than the frame reads the image in place.
+ *                           resid_planes (may be NULL): a plane image of the residual
+ *                           (epilogue bit 1) with the output's shape, read instead of
+ *                           resid by convs that read plane images (resid may then be
+ *                           NULL; others need resid). */
 typedef struct cm_planes cm_planes_t;
 cm_planes_t* cm_planes_create(unsigned batch, unsigned channels, unsigned h, unsigned w, unsigned pad_top,
                               unsigned pad_left, unsigned pad_bottom, unsigned pad_right);
@@ -228,13 +232,14 @@ int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int16_t* weigh
                    unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
                    unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w,
                    unsigned pad_top, unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
-                   unsigned epilogue, const int16_t* resid);
+                   unsigned epilogue, const int16_t* resid, const cm_planes_t* resid_planes);
 int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
                          int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h,
                          unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh,
                          unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
                          unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
-                         unsigned is_depthwise, unsigned epilogue, const int16_t* resid, cm_stream_t stream);
+                         unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
+                         const cm_planes_t* resid_planes, cm_stream_t stream);
 
 /* ---- PoolingKernel -------------------------------------------------------------
  * pool_type CM_POOL_MAX / AVG / LP (any value >= 2 is LP); lp_order 1 = sum|x|,

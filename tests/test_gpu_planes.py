@@ -130,3 +130,36 @@ def test_unusable_image_needs_x(cm, port):
         kernels.ConvKernelPlanes(None, P, dev(w3), dev(b3), empty(2 * 32 * 14 * 12), None, *g3)
     with pytest.raises(CormorantError):                  # output image of another shape
         kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, kernels.PlaneImage(2, 64, 7, 7), *g1)
+
+
+def test_residual_from_plane_image(cm, port):
+    """Conv -> Add(residual) -> Relu with the residual read from its plane image (the
+    block input of a residual block): no NCHW copy of the residual is needed; a conv that
+    cannot read plane images needs the NCHW residual."""
+    from cormorant_b200 import CormorantError, _lib, kernels
+    rng = np.random.default_rng(21)
+    for (N, C, H) in ((3, 64, 14), (2, 128, 28)):
+        g0 = geo(N, 16, H, H, C, 3, 1, 1)
+        g1 = geo(N, C, H, H, C, 3, 1, 1)
+        x = rand16(rng, N * 16 * H * H)
+        w0, b0 = weights(rng, g0)
+        w1, b1 = weights(rng, g1)
+        r = oracle(port, x, w0, b0, g0, 1)                 # the block input
+        want = oracle(port, r, w1, b1, g1, 3, r)           # conv(r) + r, then Relu
+        R = kernels.PlaneImage(N, C, H, H, kernels.conv_plane_frame(*g1))
+        kernels.ConvKernelPlanes(dev(x), None, dev(w0), dev(b0), None, R, *g0, epilogue=1)
+        got = empty(want.size)
+        kernels.ConvKernelPlanes(None, R, dev(w1), dev(b1), got, None, *g1, epilogue=3, resid=None, resid_planes=R)
+        assert_same(host(got), want, f"residual from planes {N}x{C}x{H}")
+    L = _lib.lib()
+    old = L.cm_set_direct_limit(1 << 40)                  # the consumer on the CUDA-core path
+    try:
+        with pytest.raises(CormorantError):
+            kernels.ConvKernelPlanes(dev(r), None, dev(w1), dev(b1), empty(want.size), None, *g1, epilogue=3,
+                                     resid=None, resid_planes=R)
+        got = empty(want.size)
+        kernels.ConvKernelPlanes(dev(r), None, dev(w1), dev(b1), got, None, *g1, epilogue=3, resid=dev(r),
+                                 resid_planes=R)
+    finally:
+        L.cm_set_direct_limit(old)
+    assert_same(host(got), want, "NCHW residual on the CUDA-core path")

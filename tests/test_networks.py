@@ -47,10 +47,10 @@ class OracleBackend:
 
     def conv_planes(self, x, xp, w, bias, y, yp, *args):
         """A plane image on the checker is the NCHW tensor itself."""
-        *geo, epi, resid = args
+        *geo, epi, resid, rp = args
         src = x if x is not None else xp
         out = np.zeros(geo[0] * geo[4] * geo[5] * geo[6], np.int16)
-        self.conv_fused(src, w, bias, out, *geo, epi, resid)
+        self.conv_fused(src, w, bias, out, *geo, epi, resid if resid is not None else rp)
         if y is not None:
             y[:] = out
         if yp is not None:
@@ -200,12 +200,14 @@ def test_chain_pass_resnet_structure():
     where a residual, a pool or the network output reads them."""
     net = networks.chain(networks.fuse(networks.resnet18(batch=2)))
     convs = [n for n in net.nodes if n[0] == "conv"]
-    assert len(convs) == 20 and len(net.planes) == 15
+    assert len(convs) == 20 and len(net.planes) == 18
     assert sum(1 for n in convs if n[8] is not None) == 18      # every conv but the stem and layer 1's first
-    assert sum(1 for n in convs if n[1] is None) == 14          # inputs read only from plane images
-    assert sum(1 for n in convs if n[4] is None) == 11          # outputs written only as plane images
+    assert sum(1 for n in convs if n[1] is None) == 18          # inputs read only from plane images
+    assert sum(1 for n in convs if n[4] is None) == 18          # outputs written only as plane images
+    assert sum(1 for n in convs if n[10] is not None) == 7      # residuals read from plane images
     assert all(n[8] is not None for n in convs if n[1] is None)
     assert all(n[9] is not None for n in convs if n[4] is None)
+    assert set(net.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}   # NCHW tensors left
     for name, (b, c, h, w, frame) in net.planes.items():
         assert b == 2 and len(frame) == 4 and min(frame) >= 0
     assert networks.chain(networks.fuse(networks.lenet5())).planes == {}    # batch-1 convs read NCHW
