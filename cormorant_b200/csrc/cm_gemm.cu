@@ -621,6 +621,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                     if (col0 >= g.cols) break;
                     const uint32_t live = min(CW, g.cols - col0);   // channels past the output hold x = 0
                     uint32_t hw[CW / 4], lw[CW / 4];
+                    int32_t sh = 0, sl = 0;
 #pragma unroll
                     for (uint32_t q = 0; q < CW / 4; ++q) {
                         uint32_t a = pk[(c0 + 4 * q) / 2], b = pk[(c0 + 4 * q) / 2 + 1];
@@ -633,10 +634,12 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                         }
                         hw[q] = __byte_perm(a, b, 0x7531);
                         lw[q] = __byte_perm(a, b, 0x6420) ^ 0x80808080u;
-                        sum += (int32_t)(int16_t)(a & 0xFFFFu) + (int32_t)(int16_t)(a >> 16) +
-                               (int32_t)(int16_t)(b & 0xFFFFu) + (int32_t)(int16_t)(b >> 16);
+                        // x - 128 = 256*hi + lo': byte sums of both planes (signed)
+                        sh = __dp4a((int)hw[q], 0x01010101, sh);
+                        sl = __dp4a((int)lw[q], 0x01010101, sl);
                     }
-                    sum -= 128 * (int32_t)live;
+                    // masked channels hold x = 0 (lo' = -128) and are not part of the sum
+                    sum += 256 * sh + sl + 128 * (int32_t)(CW - live);
                     int8_t* dst = g.po + pix * g.po_Cp + col0;
 #pragma unroll
                     for (uint32_t q = 0; q < CW / 16; ++q) {
