@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_conv_fused_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p, _p]),
     "cm_planes_create": (_p, [_u] * 8),
     "cm_planes_destroy": (None, [_p]),
+    "cm_planes_fill": (C.c_int, [_p, _p]),
+    "cm_planes_fill_async": (C.c_int, [_p, _p, _p]),
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),

@@ -1573,3 +1573,17 @@ extern "C" int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int
                                   epilogue, resid, resid_planes, nullptr);
     return rc ? rc : finish_sync(nullptr);
 }
+
+extern "C" int cm_planes_fill_async(cm_planes_t* p, const int16_t* x, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!p || !x) return set_error(CM_EINVAL, "cm_planes_fill: null argument");
+    if (p->device != cx->device) return set_error(CM_EINVAL, "cm_planes_fill: plane image of another device");
+    return planes_from_tensor(cx, x, p, (cudaStream_t)stream);
+}
+
+extern "C" int cm_planes_fill(cm_planes_t* p, const int16_t* x) {
+    int rc = cm_planes_fill_async(p, x, nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}

@@ -142,6 +142,13 @@ def conv_plane_frame(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, str
     return tuple(int(v) for v in fr) if ok else None
 
 
+def PlanesFill(planes, x, stream=None) -> None:
+    """Split the NCHW tensor x into plane image `planes` (cm_planes_fill)."""
+    L = lib()
+    check(L.cm_planes_fill(planes.ptr, _addr(x)) if stream is None
+          else L.cm_planes_fill_async(planes.ptr, _addr(x), _stream(stream)))
+
+
 def _planes(p) -> int | None:
     return None if p is None else p.ptr
 

@@ -202,7 +202,7 @@ def _inputs(node) -> list:
         names = [node[1], node[2]] + ([node[6]] if len(node) > 6 else [])
     elif kind == "vectorop":
         names = [node[1], node[2]]
-    else:
+    else:                                            # pool, planes
         names = [node[1]]
     return [n for n in names if n is not None]
 
@@ -210,7 +210,7 @@ def _inputs(node) -> list:
 def output_of(node) -> str:
     if node[0] == "conv":
         return node[4] if node[4] is not None else node[9]
-    return node[3] if node[0] in ("vectorop", "matmul") else node[2]
+    return node[3] if node[0] in ("vectorop", "matmul") else node[2]   # pool, planes: node[2]
 
 
 def chain(net: Net, frame_fn=None) -> Net:
@@ -223,7 +223,9 @@ def chain(net: Net, frame_fn=None) -> Net:
     else reads it (a pool, a vector op, a conv that cannot read plane images, the
     network output).  Conv nodes become
     ("conv", x, w, bias, y, args, epilogue, resid, xp, yp, rp) with x / y / resid None
-    when unused."""
+    when unused.  A tensor no conv produced (a pool output, the input) that convs read at
+    least twice as an operand or residual gets one ("planes", x, image) split pass right
+    after its producer."""
     if frame_fn is None:
         from . import kernels
         frame_fn = lambda args: kernels.conv_plane_frame(*args)  # noqa: E731
@@ -245,6 +247,25 @@ def chain(net: Net, frame_fn=None) -> Net:
                 uses.setdefault(R(name), []).append((j, "other"))
     uses.setdefault(R(net.output), []).append((-1, "other"))
     xp_of, rp_of, keep_of, planes = {}, {}, {}, {}
+    fills: dict = {}                                  # node index (-1: the input) -> [(tensor, image)]
+    others = {R(output_of(n)): j for j, n in enumerate(nodes) if n[0] != "conv"}
+    others.setdefault(R(net.input), -1)
+    for y, i in others.items():
+        readers = uses.get(y, [])
+        x_ok = [(j, reads_planes[j]) for j, role in readers if role == "x" and reads_planes[j] is not None]
+        r_ok = [j for j, role in readers if role == "resid" and reads_planes[j] is not None]
+        if not x_ok or len(x_ok) + len(r_ok) < 2:
+            continue
+        frame = tuple(max(f[k] for _, f in x_ok) for k in range(4))
+        pname = y + "@planes"
+        j0 = x_ok[0][0]
+        a = nodes[j0][5]
+        planes[pname] = (net.batch, a[1], a[2], a[3], frame)
+        fills.setdefault(i, []).append((y, pname))
+        for j, _ in x_ok:
+            xp_of[j] = (pname, True)
+        for j in r_ok:
+            rp_of[j] = (pname, True)
     for y, i in produced.items():
         readers = uses.get(y, [])
         x_ok = [(j, reads_planes[j]) for j, role in readers if role == "x" and reads_planes[j] is not None]
@@ -262,10 +283,11 @@ def chain(net: Net, frame_fn=None) -> Net:
             xp_of[j] = (pname, keep_y)
         for j in r_ok:
             rp_of[j] = (pname, keep_y)
-    out = []
+    out = [("planes", y, pname) for y, pname in fills.get(-1, [])]
     for i, node in enumerate(nodes):
         if node[0] != "conv":
             out.append(node)
+            out.extend(("planes", y, pname) for y, pname in fills.get(i, []))
             continue
         _, x, wn, bn, y, args, epi, resid = node
         xp = yp = rp = None
@@ -386,6 +408,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "pool":
             _, x, y, args = node
             backend.pool(R(x), R(y), *args)
+        elif kind == "planes":
+            _, x, p = node
+            backend.planes_fill(R(x), R(p))
         elif kind == "matmul" and len(node) > 5:
             _, a, bb, c, args, epi, bias = node
             backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
@@ -428,6 +453,9 @@ class GpuBackend:
 
     def pool(self, x, y, *args):
         self.k.PoolingKernel(x, y, *args, stream=self.stream)
+
+    def planes_fill(self, x, p):
+        self.k.PlanesFill(p, x, stream=self.stream)
 
 
 def gpu_buffers(net: Net, x=None):

@@ -223,6 +223,10 @@ typedef struct cm_planes cm_planes_t;
 cm_planes_t* cm_planes_create(unsigned batch, unsigned channels, unsigned h, unsigned w, unsigned pad_top,
                               unsigned pad_left, unsigned pad_bottom, unsigned pad_right);
 void cm_planes_destroy(cm_planes_t* planes);
+/* x [batch][channels][h][w] (NCHW words) -> plane image p: the split pass a conv would run,
+ * for a tensor no conv produced (a pool output, the network input) that several convs read. */
+int cm_planes_fill(cm_planes_t* p, const int16_t* x);
+int cm_planes_fill_async(cm_planes_t* p, const int16_t* x, cm_stream_t stream);
 int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
                         unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
                         unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,

@@ -163,3 +163,22 @@ def test_residual_from_plane_image(cm, port):
     finally:
         L.cm_set_direct_limit(old)
     assert_same(host(got), want, "NCHW residual on the CUDA-core path")
+
+
+@pytest.mark.parametrize("N,C,H,W", [(3, 64, 14, 14), (2, 40, 7, 9), (2, 64, 56, 56)])
+def test_planes_fill_then_conv_and_residual(cm, port, N, C, H, W):
+    """cm_planes_fill splits an NCHW tensor no conv produced (a pool output) into a plane
+    image; a conv reads it as its operand and as its residual."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(N * C + H)
+    g = geo(N, C, H, W, C, 3, 1, 1)
+    x = rand16(rng, N * C * H * W, -2048, 2048)
+    w, b = weights(rng, g)
+    want = oracle(port, x, w, b, g, 3, x)
+    P = kernels.PlaneImage(N, C, H, W, kernels.conv_plane_frame(*g) or (1, 1, 1, 1))
+    kernels.PlanesFill(P, dev(x))
+    got = empty(want.size)
+    if kernels.conv_plane_frame(*g) is None:
+        pytest.skip("this conv runs on the CUDA-core path")
+    kernels.ConvKernelPlanes(None, P, dev(w), dev(b), got, None, *g, epilogue=3, resid=None, resid_planes=P)
+    assert_same(host(got), want, f"fill {N}x{C}x{H}x{W}")

@@ -59,6 +59,9 @@ class OracleBackend:
     def pool(self, x, y, *args):
         y[:] = self.chk.pool(x, *args)[: y.size]
 
+    def planes_fill(self, x, p):
+        p[:] = x[: p.size]
+
 
 def cpu_buffers(net, x):
     bufs = {name: np.zeros(max(w, 1), np.int16) for name, w in net.buffers.items()}
@@ -200,11 +203,12 @@ def test_chain_pass_resnet_structure():
     where a residual, a pool or the network output reads them."""
     net = networks.chain(networks.fuse(networks.resnet18(batch=2)))
     convs = [n for n in net.nodes if n[0] == "conv"]
-    assert len(convs) == 20 and len(net.planes) == 18
-    assert sum(1 for n in convs if n[8] is not None) == 18      # every conv but the stem and layer 1's first
+    assert len(convs) == 20 and len(net.planes) == 19
+    assert [n[1] for n in net.nodes if n[0] == "planes"] == ["pool5"]   # the max pool's output, split once
+    assert sum(1 for n in convs if n[8] is not None) == 19      # every conv but the stem
     assert sum(1 for n in convs if n[1] is None) == 18          # inputs read only from plane images
     assert sum(1 for n in convs if n[4] is None) == 18          # outputs written only as plane images
-    assert sum(1 for n in convs if n[10] is not None) == 7      # residuals read from plane images
+    assert sum(1 for n in convs if n[10] is not None) == 8      # residuals read from plane images
     assert all(n[8] is not None for n in convs if n[1] is None)
     assert all(n[9] is not None for n in convs if n[4] is None)
     assert set(net.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}   # NCHW tensors left
