@@ -522,6 +522,16 @@ class NetworkBench:
         self.e2e_graph = None
         self.e2e_path = ("pinned host input -> device copy -> the call list through the C ABI (ConvKernel, VectorOPKernel, "
                          "PoolingKernel, MatmulKernel) -> logits copied to pinned host")
+        self.copy_stream = None
+        if self.which != "lenet":
+            # two device input buffers: step i+1's input crosses PCIe on a copy stream while
+            # step i computes; a copy waits until the forward that last read its buffer is done
+            self.copy_stream = torch.cuda.Stream()
+            self.xbufs = [self.bufs[self.net.input], torch.empty_like(self.bufs[self.net.input])]
+            self.copied = [torch.cuda.Event(), torch.cuda.Event()]
+            self.consumed = [None, None]
+            self.e2e_i = 0
+            self.e2e_path += "; the next step's input copy overlaps this step's compute (copy stream, two input buffers)"
         if self.which == "lenet":
             self.e2e_path += "; captured once as a CUDA graph and replayed per image"
             # batch 1 is host-launch-bound: the whole step (pinned H2D copy, the call
@@ -544,8 +554,41 @@ class NetworkBench:
     def e2e_step(self):
         if self.e2e_graph is not None:
             self.e2e_graph.replay()
+        elif self.copy_stream is not None:
+            self._e2e_pipelined()
         else:
             self._e2e_body()
+
+    def e2e_start(self, start_event):
+        """Timed region starts: the first input copy is issued inside it."""
+        if self.copy_stream is not None:
+            self.copy_stream.wait_event(start_event)
+            self._issue_copy(self.e2e_i)
+
+    def _issue_copy(self, i):
+        import torch
+        b = i % 2
+        with torch.cuda.stream(self.copy_stream):
+            if self.consumed[b] is not None:
+                self.copy_stream.wait_event(self.consumed[b])
+            self.xbufs[b].copy_(self.hx, non_blocking=True)
+            self.copied[b].record(self.copy_stream)
+
+    def _e2e_pipelined(self):
+        import torch
+        from cormorant_b200 import networks
+        i = self.e2e_i
+        b = i % 2
+        self._issue_copy(i + 1)                              # the next step's input, overlapped
+        cur = torch.cuda.current_stream()
+        cur.wait_event(self.copied[b])
+        self.bufs[self.net.input] = self.xbufs[b]
+        networks.execute(self.net, networks.GpuBackend(cur), self.bufs)
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.consumed[b] = ev
+        self.hy.copy_(self.bufs[self.net.resolve(self.net.output)], non_blocking=True)
+        self.e2e_i = i + 1
 
     def e2e_release(self):
         self.e2e_graph = None
@@ -888,6 +931,8 @@ def main():
         e_steps = K if args.config == "lenet" else max(1, min(K, 3))
         es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         es.record()
+        if hasattr(wl, "e2e_start"):
+            wl.e2e_start(es)
         for _ in range(e_steps):
             wl.e2e_step()
         ee.record()
