@@ -90,7 +90,9 @@ def plan_layout(net: Net) -> Layout:
     live: dict = {}
     for i, node in enumerate(net.nodes):
         y = R(_output(node))
-        if y not in io and y not in net.consts:
+        if node[0] == "conv" and node[4] is not None:
+            y = R(node[4])                   # the NCHW output (a plane image output is separate)
+        if y not in io and y not in net.consts and y not in net.planes:
             first, last = live.get(y, (i, i))
             live[y] = (min(first, i), max(last, i))
         for name in _inputs(node):
@@ -103,6 +105,8 @@ def plan_layout(net: Net) -> Layout:
     top = 0
     for i, node in enumerate(net.nodes):
         y = R(_output(node))
+        if node[0] == "conv" and node[4] is not None:
+            y = R(node[4])
         if y in live and y not in acts and live[y][0] == i:
             words = _align(max(net.buffers[y], 1))
             pos, placed = 0, None
@@ -169,6 +173,13 @@ class _Emitter:
         self.in_c, self.out_c = self.R(net.input), self.R(net.output)
 
     # ---- buffer expressions --------------------------------------------------
+    @staticmethod
+    def _pvar(name: str) -> str:
+        return "p_" + "".join(ch if ch.isalnum() or ch == "_" else "_" for ch in name)
+
+    def _planes(self, name: str | None) -> str:
+        return "NULL" if name is None else self._pvar(name)
+
     def _buf(self, name: str | None) -> str:
         if name is None:
             return "NULL"
@@ -274,6 +285,19 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
     # ---- inference.c ---------------------------------------------------------
     def _call(self, i: int, node) -> str:
         kind = node[0]
+        if kind == "conv" and len(node) > 8:
+            _, x, wn, bn, y, args, epi, resid, xp, yp, rp = node
+            a = ", ".join(f"{int(v)}u" for v in args)
+            what = "Conv" + ("+Add" if epi & 2 else "") + ("+Relu" if epi & 1 else "")
+            dst = " and ".join(v for v in (self.R(y) if y else None, yp) if v)
+            return (f"    /* {i}: {what} -> {dst} */\n"
+                    f"    CHECK(cm_conv_planes_async({self._dev(x)}, {self._planes(xp)}, {self._dev(wn)}, {self._dev(bn)}, "
+                    f"{self._dev(y, False)}, {self._planes(yp)},\n        {a}, {int(epi)}u, {self._dev(resid)}, "
+                    f"{self._planes(rp)}, NULL));")
+        if kind == "planes":
+            _, x, pn = node
+            return (f"    /* {i}: {self.R(x)} -> plane image {pn} */\n"
+                    f"    CHECK(cm_planes_fill_async({self._planes(pn)}, {self._dev(x)}, NULL));")
         if kind == "conv":
             _, x, wn, bn, y, args = node[:6]
             epi, resid = (node[6], node[7]) if len(node) > 6 else (0, None)
@@ -336,6 +360,13 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             f"        return 1;\n    }}"
             for _, k, p in self.kernels[1:])
         calls = "\n".join(self._call(i, n) for i, n in enumerate(net.nodes))
+        pdecl = "\n".join(f"static cm_planes_t *{self._pvar(n)} = NULL;   /* {b}x{c}x{h}x{w}, frame {fr} */"
+                          for n, (b, c, h, w, fr) in net.planes.items())
+        pcreate = "\n".join(
+            f"    {self._pvar(n)} = cm_planes_create({b}u, {c}u, {h}u, {w}u, {fr[0]}u, {fr[1]}u, {fr[2]}u, {fr[3]}u);\n"
+            f"    if (!{self._pvar(n)}) goto fail;"
+            for n, (b, c, h, w, fr) in net.planes.items())
+        pdestroy = "\n".join(f"    cm_planes_destroy({self._pvar(n)});\n    {self._pvar(n)} = NULL;" for n in net.planes)
         loader = _LOAD_WEIGHT if large else ""
         return f"""/*
  * inference.c -- generated for network '{net.name}' (batch {net.batch}, {len(net.nodes)} kernel calls).
@@ -362,6 +393,8 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
 static inference_buf_t *g_wpool = NULL;   /* {L.weight_words} words */
 static inference_buf_t *g_apool = NULL;   /* {L.act_words} words */
 {views}
+/* ---- plane images: conv outputs kept in the next convs' operand form (cm_conv_planes) ---- */
+{pdecl}
 
 {loader}int inference_init({params})
 {{
@@ -380,6 +413,7 @@ static inference_buf_t *g_apool = NULL;   /* {L.act_words} words */
 {wviews}
 {aviews}
 {fills}
+{pcreate}
     if (cm_buf_sync_to_device(g_wpool) != CM_OK) goto fail;
     return 0;
 fail:
@@ -389,6 +423,7 @@ fail:
 
 void inference_deinit(void)
 {{
+{pdestroy}
     if (g_apool) inference_buf_release(g_apool);
     if (g_wpool) inference_buf_release(g_wpool);
     g_apool = g_wpool = NULL;

@@ -25,9 +25,28 @@ NETS = {
 }
 
 
-def _net(name, fused):
+MODES = ["plain", "fused", "planes"]
+
+
+def _net(name, mode):
     net = NETS[name]()
-    return networks.fuse(net) if fused else net
+    if mode == "plain":
+        return net
+    net = networks.fuse(net)
+    return networks.chain(net) if mode == "planes" else net
+
+
+def _nchw_outputs(net):
+    outs = set()
+    for n in net.nodes:
+        if n[0] == "planes":
+            continue
+        if n[0] == "conv":
+            if n[4] is not None:
+                outs.add(net.resolve(n[4]))
+        else:
+            outs.add(net.resolve(codegen._output(n)))
+    return outs
 
 
 def _expected(net, port):
@@ -36,14 +55,14 @@ def _expected(net, port):
     return bufs[net.resolve(net.output)].copy()
 
 
-@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("name", list(NETS))
-def test_layout_never_overlaps_live_tensors(name, fused):
+def test_layout_never_overlaps_live_tensors(name, mode):
     """Two intermediates that are live at the same node never share a word of the pool."""
-    net = _net(name, fused)
+    net = _net(name, mode)
     L = codegen.plan_layout(net)
     io = {net.resolve(net.input), net.resolve(net.output)}
-    inter = {net.resolve(codegen._output(n)) for n in net.nodes} - io
+    inter = _nchw_outputs(net) - io
     assert set(L.acts) == inter
     items = list(L.acts.items())
     for name_a, (oa, wa) in items:
@@ -119,11 +138,11 @@ def test_ramp_input_matches_reference_fill():
 
 
 @pytest.mark.skipif(not LIB.exists(), reason="libcormorant_cuda.so not built")
-@pytest.mark.parametrize("fused", [False, True])
-def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, fused):
+@pytest.mark.parametrize("mode", MODES)
+def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, mode):
     """gcc -Wall -Wextra -Werror over the generated sources, linked against the library;
     with no GPU visible inference_init reports the failure and the test binary exits 1."""
-    net = _net("resnet18_b2", fused)
+    net = _net("resnet18_b2", mode)
     codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
     exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
     import torch
@@ -135,10 +154,10 @@ def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, fused):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("mode", MODES)
 @pytest.mark.parametrize("name", list(NETS))
-def test_generated_project_bit_exact_on_gpu(tmp_path, port, name, fused):
-    net = _net(name, fused)
+def test_generated_project_bit_exact_on_gpu(tmp_path, port, name, mode):
+    net = _net(name, mode)
     exp = _expected(net, port)
     codegen.emit_project(net, tmp_path, expected=exp)
     exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
@@ -163,3 +182,11 @@ def test_generated_project_reports_missing_weights_and_mismatch(tmp_path, port):
     os.remove(tmp_path / "weights" / f"{big}.dat")
     r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300)
     assert r.returncode == 1 and "cannot open weight file" in r.stderr
+
+
+def test_chained_project_uses_plane_images(tmp_path):
+    net = _net("resnet18_b2", "planes")
+    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
+    src = (tmp_path / "src/inference.c").read_text()
+    assert src.count("cm_planes_create(") == len(net.planes) == src.count("cm_planes_destroy(")
+    assert src.count("cm_conv_planes_async(") == 20 and src.count("cm_planes_fill_async(") == 1
