@@ -52,6 +52,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_planes_destroy": (None, [_p]),
     "cm_planes_fill": (C.c_int, [_p, _p]),
     "cm_planes_fill_async": (C.c_int, [_p, _p, _p]),
+    "cm_pool_planes": (C.c_int, [_p, _p] + [_u] * 17),
+    "cm_pool_planes_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),

@@ -294,6 +294,11 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
                     f"    CHECK(cm_conv_planes_async({self._dev(x)}, {self._planes(xp)}, {self._dev(wn)}, {self._dev(bn)}, "
                     f"{self._dev(y, False)}, {self._planes(yp)},\n        {a}, {int(epi)}u, {self._dev(resid)}, "
                     f"{self._planes(rp)}, NULL));")
+        if kind == "poolp":
+            _, xp, yp, args = node
+            a = ", ".join(f"{int(v)}u" for v in args)
+            return (f"    /* {i}: Pool {xp} -> {yp} (plane images) */\n"
+                    f"    CHECK(cm_pool_planes_async({self._planes(xp)}, {self._planes(yp)},\n        {a}, NULL));")
         if kind == "planes":
             _, x, pn = node
             return (f"    /* {i}: {self.R(x)} -> plane image {pn} */\n"

@@ -387,6 +387,74 @@ __global__ void __launch_bounds__(256) planes_reset_S_kernel(int32_t* __restrict
     }
 }
 
+// MaxPool from plane image to plane image: thread = output pixel, all its channels in
+// 16-channel groups.  Each in-image tap contributes one 16-byte hi run and one lo' run,
+// rebuilt into word pairs and reduced with __vmaxs2; taps outside the image are the
+// pool's padding, which never wins (it holds -32768, PoolingKernel's kAccMin), so a
+// window with no tap inside gives -32768.  The output pixel's channels are written as
+// hi / lo' runs (channels past C as x = 0) and its channel sum to S directly.
+struct PoolPlanesGeo {
+    uint32_t in_h, in_w, out_h, out_w, ph, pw, sh, sw, pt, pl, dh, dw, C, Cp;
+    uint32_t xHp, xWp, xpt, xpl, yHp, yWp, ypt, ypl;
+    uint64_t x_plane, y_plane;
+};
+
+__global__ void __launch_bounds__(256) pool_max_planes_kernel(const int8_t* __restrict__ xin, int8_t* __restrict__ yout,
+                                                              int32_t* __restrict__ yS, PoolPlanesGeo g, uint64_t total,
+                                                              FastDiv fd_ow, FastDiv fd_oh) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+        // t < 2^32 (checked by the caller)
+        const uint32_t row = fd_ow.div((uint32_t)t), ow = (uint32_t)t - row * fd_ow.d;
+        const uint32_t n = fd_oh.div(row), oh = row - n * fd_oh.d;
+        const int32_t ih0 = (int32_t)(oh * g.sh) - (int32_t)g.pt, iw0 = (int32_t)(ow * g.sw) - (int32_t)g.pl;
+        const uint64_t ypix = ((uint64_t)n * g.yHp + oh + g.ypt) * g.yWp + ow + g.ypl;
+        int32_t sum = 0;
+        for (uint32_t c0 = 0; c0 < g.Cp; c0 += 16) {
+            uint32_t acc[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[k] = 0x80008000u;
+            for (uint32_t r = 0; r < g.ph; ++r) {
+                const int32_t ih = ih0 + (int32_t)(r * g.dh);
+                if (ih < 0 || ih >= (int32_t)g.in_h) continue;
+                for (uint32_t q = 0; q < g.pw; ++q) {
+                    const int32_t iw = iw0 + (int32_t)(q * g.dw);
+                    if (iw < 0 || iw >= (int32_t)g.in_w) continue;
+                    const uint64_t xpix = ((uint64_t)n * g.xHp + (uint32_t)ih + g.xpt) * g.xWp + (uint32_t)iw + g.xpl;
+                    const int8_t* src = xin + xpix * g.Cp + c0;
+                    const uint4 hv = __ldg((const uint4*)src), lv = __ldg((const uint4*)(src + g.x_plane));
+                    const uint32_t h4[4] = {hv.x, hv.y, hv.z, hv.w};
+                    const uint32_t l4[4] = {lv.x ^ 0x80808080u, lv.y ^ 0x80808080u, lv.z ^ 0x80808080u, lv.w ^ 0x80808080u};
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        acc[2 * k] = __vmaxs2(acc[2 * k], __byte_perm(l4[k], h4[k], 0x5140));
+                        acc[2 * k + 1] = __vmaxs2(acc[2 * k + 1], __byte_perm(l4[k], h4[k], 0x7362));
+                    }
+                }
+            }
+            const uint32_t live = c0 < g.C ? min(16u, g.C - c0) : 0u;
+            uint32_t hw[4], lw[4];
+            int32_t shi = 0, slo = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                uint32_t a = acc[2 * k], b = acc[2 * k + 1];
+                if (4u * k + 0 >= live) a &= 0xFFFF0000u;
+                if (4u * k + 1 >= live) a &= 0x0000FFFFu;
+                if (4u * k + 2 >= live) b &= 0xFFFF0000u;
+                if (4u * k + 3 >= live) b &= 0x0000FFFFu;
+                hw[k] = __byte_perm(a, b, 0x7531);
+                lw[k] = __byte_perm(a, b, 0x6420) ^ 0x80808080u;
+                shi = __dp4a((int)hw[k], 0x01010101, shi);
+                slo = __dp4a((int)lw[k], 0x01010101, slo);
+            }
+            sum += 256 * shi + slo + 128 * (int32_t)(16u - live);
+            int8_t* dst = yout + ypix * g.Cp + c0;
+            *(uint4*)dst = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(dst + g.y_plane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+        yS[ypix] = sum;
+    }
+}
+
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
 __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
                                                            uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw,
@@ -1585,5 +1653,50 @@ extern "C" int cm_planes_fill_async(cm_planes_t* p, const int16_t* x, cm_stream_
 
 extern "C" int cm_planes_fill(cm_planes_t* p, const int16_t* x) {
     int rc = cm_planes_fill_async(p, x, nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
+extern "C" int cm_pool_planes_async(const cm_planes_t* xp, cm_planes_t* yp, unsigned batch, unsigned channels,
+                                    unsigned in_h, unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h,
+                                    unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top,
+                                    unsigned pad_left, unsigned dil_h, unsigned dil_w, unsigned pool_type,
+                                    unsigned lp_order, unsigned count_include_pad, cm_stream_t stream) {
+    (void)lp_order;
+    (void)count_include_pad;
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!xp || !yp) return set_error(CM_EINVAL, "cm_pool_planes: null plane image");
+    if (pool_type != CM_POOL_MAX) return set_error(CM_EUNSUPPORTED, "cm_pool_planes: MAX pooling only");
+    if (xp->device != cx->device || yp->device != cx->device)
+        return set_error(CM_EINVAL, "cm_pool_planes: plane image of another device");
+    if (xp->n != batch || xp->C != channels || xp->H != in_h || xp->W != in_w || yp->n != batch ||
+        yp->C != channels || yp->H != out_h || yp->W != out_w || xp->Cp != yp->Cp)
+        return set_error(CM_EINVAL, "cm_pool_planes: plane images do not match the pool's tensors");
+    const uint64_t total = (uint64_t)batch * out_h * out_w;
+    if (total == 0) return CM_OK;
+    if (total >= (1ull << 32)) return set_error(CM_EUNSUPPORTED, "cm_pool_planes: output too large");
+    PoolPlanesGeo g{in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w, pad_top, pad_left, dil_h, dil_w,
+                    channels, xp->Cp, xp->Hp, xp->Wp, xp->pt, xp->pl, yp->Hp, yp->Wp, yp->pt, yp->pl,
+                    xp->plane_pitch, yp->plane_pitch};
+    cudaStream_t s = (cudaStream_t)stream;
+    {
+        ProfScope ps_(PK_POOL, s);
+        pool_max_planes_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(xp->planes, yp->planes, yp->S, g, total,
+                                                                        FastDiv(out_w), FastDiv(out_h));
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_pool_planes");
+}
+
+extern "C" int cm_pool_planes(const cm_planes_t* xp, cm_planes_t* yp, unsigned batch, unsigned channels,
+                              unsigned in_h, unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h,
+                              unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                              unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                              unsigned count_include_pad) {
+    int rc = cm_pool_planes_async(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
+                                  stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad,
+                                  nullptr);
     return rc ? rc : finish_sync(nullptr);
 }

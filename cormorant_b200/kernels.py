@@ -149,6 +149,16 @@ def PlanesFill(planes, x, stream=None) -> None:
           else L.cm_planes_fill_async(planes.ptr, _addr(x), _stream(stream)))
 
 
+def PoolingKernelPlanes(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
+                        pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, lp_order=2, count_include_pad=0,
+                        stream=None) -> None:
+    """PoolingKernel (MAX only) from plane image xp to plane image yp (cm_pool_planes)."""
+    L = lib()
+    args = (_planes(xp), _planes(yp), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+            pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
+    check(L.cm_pool_planes(*args) if stream is None else L.cm_pool_planes_async(*args, _stream(stream)))
+
+
 def _planes(p) -> int | None:
     return None if p is None else p.ptr
 

@@ -213,26 +213,28 @@ def output_of(node) -> str:
     return node[3] if node[0] in ("vectorop", "matmul") else node[2]   # pool, planes: node[2]
 
 
-def chain(net: Net, frame_fn=None) -> Net:
+def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
     """The call list with conv outputs that feed implicit-GEMM convs produced as plane
     images (cm_conv_planes): the producing conv's GEMM epilogue writes the consumers'
     channels-last operand, so their split pass disappears, and a residual those convs
     add comes from its plane image too.  `frame_fn(args)` gives the padding frame a
     conv reads its input with, or None when it reads the NCHW tensor (default: the
     library's cm_conv_plane_frame).  The NCHW output is still written when anything
-    else reads it (a pool, a vector op, a conv that cannot read plane images, the
-    network output).  Conv nodes become
+    else reads it (a vector op, a non-MAX pool, a conv that cannot read plane images,
+    the network output).  Conv nodes become
     ("conv", x, w, bias, y, args, epilogue, resid, xp, yp, rp) with x / y / resid None
-    when unused.  A tensor no conv produced (a pool output, the input) that convs read at
-    least twice as an operand or residual gets one ("planes", x, image) split pass right
-    after its producer."""
+    when unused.  With pool_planes=True a MAX pool between a conv and plane-reading convs
+    runs plane image to plane image: ("poolp", xp, yp, args) (off by default: on
+    ResNet-18's stem it measured slower than the NCHW pool plus one split).  A tensor no
+    conv produced (the input, a pool
+    output kept NCHW) that convs read at least twice as an operand or residual gets one
+    ("planes", x, image) split pass right after its producer."""
     if frame_fn is None:
         from . import kernels
         frame_fn = lambda args: kernels.conv_plane_frame(*args)  # noqa: E731
     R = net.resolve
     nodes = [n if n[0] != "conv" or len(n) > 6 else (*n, 0, None) for n in net.nodes]
     reads_planes = {j: frame_fn(n[5]) for j, n in enumerate(nodes) if n[0] == "conv"}
-    produced = {R(n[4]): i for i, n in enumerate(nodes) if n[0] == "conv"}
     uses: dict = {}                                   # tensor -> [(node, role)]
     for j, node in enumerate(nodes):
         if node[0] == "conv":
@@ -242,52 +244,73 @@ def chain(net: Net, frame_fn=None) -> Net:
                     uses.setdefault(R(name), []).append((j, "other"))
             if node[7] is not None:
                 uses.setdefault(R(node[7]), []).append((j, "resid"))
+        elif node[0] == "pool" and node[3][14] == 0:
+            uses.setdefault(R(node[1]), []).append((j, "maxpool"))
         else:
             for name in _inputs(node):
                 uses.setdefault(R(name), []).append((j, "other"))
     uses.setdefault(R(net.output), []).append((-1, "other"))
-    xp_of, rp_of, keep_of, planes = {}, {}, {}, {}
-    fills: dict = {}                                  # node index (-1: the input) -> [(tensor, image)]
-    others = {R(output_of(n)): j for j, n in enumerate(nodes) if n[0] != "conv"}
-    others.setdefault(R(net.input), -1)
-    for y, i in others.items():
-        readers = uses.get(y, [])
+    produced = {R(n[4]): i for i, n in enumerate(nodes) if n[0] == "conv"}
+
+    def plane_readers(t):
+        """(x readers with their frames, residual readers) that can take t's plane image."""
+        readers = uses.get(t, [])
         x_ok = [(j, reads_planes[j]) for j, role in readers if role == "x" and reads_planes[j] is not None]
         r_ok = [j for j, role in readers if role == "resid" and reads_planes[j] is not None]
+        return x_ok, r_ok
+
+    # MAX pools that can run plane to plane: conv input, output read only by plane-reading convs
+    poolp = {}
+    for j, node in enumerate(nodes):
+        if not pool_planes or node[0] != "pool" or node[3][14] != 0 or R(node[1]) not in produced:
+            continue
+        u = R(node[2])
+        x_ok, r_ok = plane_readers(u)
+        if (x_ok or r_ok) and len(x_ok) + len(r_ok) == len(uses.get(u, [])):
+            poolp[j] = (x_ok, r_ok)
+    xp_of, rp_of, keep_of, planes, fills = {}, {}, {}, {}, {}
+
+    def image(t, a, x_ok, r_ok, keep):
+        frame = tuple(max([f[k] for _, f in x_ok] + [0]) for k in range(4))
+        pname = t + "@planes"
+        planes[pname] = (net.batch, a[0], a[1], a[2], frame)
+        for j, _ in x_ok:
+            xp_of[j] = (pname, keep)
+        for j in r_ok:
+            rp_of[j] = (pname, keep)
+        return pname
+
+    for t, i in produced.items():
+        readers = uses.get(t, [])
+        x_ok, r_ok = plane_readers(t)
+        pools = [j for j, role in readers if role == "maxpool" and j in poolp]
+        if not x_ok and not r_ok and not pools:
+            continue
+        served = {(j, "x") for j, _ in x_ok} | {(j, "resid") for j in r_ok} | {(j, "maxpool") for j in pools}
+        keep = any((j, role) not in served for j, role in readers)
+        a = nodes[i][5]
+        keep_of[i] = (image(t, (a[4], a[5], a[6]), x_ok, r_ok, keep), keep)
+    pool_io = {}
+    for j, (x_ok, r_ok) in poolp.items():
+        node = nodes[j]
+        t, u, a = R(node[1]), R(node[2]), node[3]
+        pool_io[j] = (keep_of[produced[t]][0], image(u, (a[1], a[4], a[5]), x_ok, r_ok, False))
+    others = {R(output_of(n)): j for j, n in enumerate(nodes) if n[0] != "conv" and j not in poolp}
+    others.setdefault(R(net.input), -1)
+    for t, i in others.items():
+        x_ok, r_ok = plane_readers(t)
         if not x_ok or len(x_ok) + len(r_ok) < 2:
             continue
-        frame = tuple(max(f[k] for _, f in x_ok) for k in range(4))
-        pname = y + "@planes"
-        j0 = x_ok[0][0]
-        a = nodes[j0][5]
-        planes[pname] = (net.batch, a[1], a[2], a[3], frame)
-        fills.setdefault(i, []).append((y, pname))
-        for j, _ in x_ok:
-            xp_of[j] = (pname, True)
-        for j in r_ok:
-            rp_of[j] = (pname, True)
-    for y, i in produced.items():
-        readers = uses.get(y, [])
-        x_ok = [(j, reads_planes[j]) for j, role in readers if role == "x" and reads_planes[j] is not None]
-        r_ok = [j for j, role in readers if role == "resid" and reads_planes[j] is not None]
-        if not x_ok and not r_ok:
-            continue
-        frame = tuple(max([f[k] for _, f in x_ok] + [0]) for k in range(4))
-        pname = y + "@planes"
-        a = nodes[i][5]
-        planes[pname] = (net.batch, a[4], a[5], a[6], frame)
-        served = {(j, "x") for j, _ in x_ok} | {(j, "resid") for j in r_ok}
-        keep_y = any((j, role) not in served for j, role in readers)
-        keep_of[i] = (pname, keep_y)
-        for j, _ in x_ok:
-            xp_of[j] = (pname, keep_y)
-        for j in r_ok:
-            rp_of[j] = (pname, keep_y)
-    out = [("planes", y, pname) for y, pname in fills.get(-1, [])]
+        a = nodes[x_ok[0][0]][5]
+        fills.setdefault(i, []).append((t, image(t, (a[1], a[2], a[3]), x_ok, r_ok, True)))
+    out = [("planes", t, pname) for t, pname in fills.get(-1, [])]
     for i, node in enumerate(nodes):
+        if i in pool_io:
+            out.append(("poolp", pool_io[i][0], pool_io[i][1], node[3]))
+            continue
         if node[0] != "conv":
             out.append(node)
-            out.extend(("planes", y, pname) for y, pname in fills.get(i, []))
+            out.extend(("planes", t, pname) for t, pname in fills.get(i, []))
             continue
         _, x, wn, bn, y, args, epi, resid = node
         xp = yp = rp = None
@@ -411,6 +434,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "planes":
             _, x, p = node
             backend.planes_fill(R(x), R(p))
+        elif kind == "poolp":
+            _, xp, yp, args = node
+            backend.pool_planes(R(xp), R(yp), *args)
         elif kind == "matmul" and len(node) > 5:
             _, a, bb, c, args, epi, bias = node
             backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
@@ -456,6 +482,9 @@ class GpuBackend:
 
     def planes_fill(self, x, p):
         self.k.PlanesFill(p, x, stream=self.stream)
+
+    def pool_planes(self, xp, yp, *args):
+        self.k.PoolingKernelPlanes(xp, yp, *args, stream=self.stream)
 
 
 def gpu_buffers(net: Net, x=None):

@@ -227,6 +227,18 @@ void cm_planes_destroy(cm_planes_t* planes);
  * for a tensor no conv produced (a pool output, the network input) that several convs read. */
 int cm_planes_fill(cm_planes_t* p, const int16_t* x);
 int cm_planes_fill_async(cm_planes_t* p, const int16_t* x, cm_stream_t stream);
+/* PoolingKernel (MAX only) from plane image xp to plane image yp, the same words as
+ * cm_pool on the NCHW tensors: a conv -> max pool -> conv chain stays in plane form. */
+int cm_pool_planes(const cm_planes_t* xp, cm_planes_t* yp, unsigned batch, unsigned channels, unsigned in_h,
+                   unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                   unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                   unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                   unsigned count_include_pad);
+int cm_pool_planes_async(const cm_planes_t* xp, cm_planes_t* yp, unsigned batch, unsigned channels,
+                         unsigned in_h, unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h,
+                         unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top,
+                         unsigned pad_left, unsigned dil_h, unsigned dil_w, unsigned pool_type,
+                         unsigned lp_order, unsigned count_include_pad, cm_stream_t stream);
 int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
                         unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
                         unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,

@@ -39,7 +39,7 @@ def _net(name, mode):
 def _nchw_outputs(net):
     outs = set()
     for n in net.nodes:
-        if n[0] == "planes":
+        if n[0] in ("planes", "poolp"):
             continue
         if n[0] == "conv":
             if n[4] is not None:
@@ -190,3 +190,11 @@ def test_chained_project_uses_plane_images(tmp_path):
     src = (tmp_path / "src/inference.c").read_text()
     assert src.count("cm_planes_create(") == len(net.planes) == src.count("cm_planes_destroy(")
     assert src.count("cm_conv_planes_async(") == 20 and src.count("cm_planes_fill_async(") == 1
+
+
+@pytest.mark.skipif(not LIB.exists(), reason="libcormorant_cuda.so not built")
+def test_plane_pool_project_compiles(tmp_path):
+    net = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True)
+    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
+    assert (tmp_path / "src/inference.c").read_text().count("cm_pool_planes_async(") == 1
+    codegen.compile_project(tmp_path, INCLUDE, LIB)

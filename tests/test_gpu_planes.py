@@ -182,3 +182,41 @@ def test_planes_fill_then_conv_and_residual(cm, port, N, C, H, W):
         pytest.skip("this conv runs on the CUDA-core path")
     kernels.ConvKernelPlanes(None, P, dev(w), dev(b), got, None, *g, epilogue=3, resid=None, resid_planes=P)
     assert_same(host(got), want, f"fill {N}x{C}x{H}x{W}")
+
+
+def _identity_readback(kernels, P, N, C, H, W):
+    """The NCHW words of plane image P: a 1x1 conv with identity weights (1.0 = 256) reads it."""
+    import torch
+    from cormorant_b200 import _lib
+    w = np.zeros((C, C), np.int16)
+    np.fill_diagonal(w, 256)
+    g = (N, C, H, W, C, H, W, 1, 1, 1, 1, 1, 1, 0, 0, 0, 0)
+    L = _lib.lib()
+    old = L.cm_set_direct_limit(0)                        # the tensor-core path, whatever the size
+    try:
+        assert kernels.conv_plane_frame(*g) is not None
+        y = empty(N * C * H * W)
+        kernels.ConvKernelPlanes(None, P, dev(w.reshape(-1)), None, y, None, *g)
+        torch.cuda.synchronize()
+    finally:
+        L.cm_set_direct_limit(old)
+    return host(y)
+
+
+@pytest.mark.parametrize("N,H,W,k,s,p,d", [(4, 112, 112, 3, 2, 1, 1), (3, 30, 26, 3, 2, 1, 2), (8, 20, 20, 2, 2, 1, 1),
+                                           (16, 9, 13, 3, 1, 1, 1), (40, 4, 4, 5, 3, 2, 1)])
+def test_max_pool_plane_to_plane(cm, port, N, H, W, k, s, p, d):
+    """cm_pool_planes equals cm_pool's MAX on the NCHW tensors, windows with no tap in the
+    image included (they give -32768); read back through an identity 1x1 conv."""
+    from cormorant_b200 import kernels
+    C = 64
+    rng = np.random.default_rng(N + H + k)
+    x = rand16(rng, N * C * H * W)
+    oh, ow = (H + 2 * p - d * (k - 1) - 1) // s + 1, (W + 2 * p - d * (k - 1) - 1) // s + 1
+    pa = (N, C, H, W, oh, ow, k, k, s, s, p, p, d, d, 0, 2, 0)
+    want = port.pool(x, *pa)[: N * C * oh * ow]
+    X = kernels.PlaneImage(N, C, H, W)
+    kernels.PlanesFill(X, dev(x))
+    Y = kernels.PlaneImage(N, C, oh, ow)
+    kernels.PoolingKernelPlanes(X, Y, *pa)
+    assert_same(_identity_readback(kernels, Y, N, C, oh, ow), want, f"max pool planes {pa}")

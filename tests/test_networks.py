@@ -62,6 +62,9 @@ class OracleBackend:
     def planes_fill(self, x, p):
         p[:] = x[: p.size]
 
+    def pool_planes(self, xp, yp, *args):
+        self.pool(xp, yp, *args)
+
 
 def cpu_buffers(net, x):
     bufs = {name: np.zeros(max(w, 1), np.int16) for name, w in net.buffers.items()}
@@ -212,6 +215,9 @@ def test_chain_pass_resnet_structure():
     assert all(n[8] is not None for n in convs if n[1] is None)
     assert all(n[9] is not None for n in convs if n[4] is None)
     assert set(net.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}   # NCHW tensors left
+    pp = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True)
+    assert [n[0] for n in pp.nodes[:2]] == ["conv", "poolp"] and len(pp.planes) == 20
+    assert set(pp.buffers) == {"x", "relu86", "pool87", "gemm92"}
     for name, (b, c, h, w, frame) in net.planes.items():
         assert b == 2 and len(frame) == 4 and min(frame) >= 0
     assert networks.chain(networks.fuse(networks.lenet5())).planes == {}    # batch-1 convs read NCHW
@@ -230,11 +236,12 @@ def test_chained_call_list_equals_reference_sequence_on_cpu(port):
 
 
 @pytest.mark.gpu
-def test_resnet18_chained_batch4_every_output(cm, port):
+@pytest.mark.parametrize("pool_planes", [False, True])
+def test_resnet18_chained_batch4_every_output(cm, port, pool_planes):
     """Plane images on the GPU: every NCHW tensor the chained list still writes, and the
     logits, equal the oracle's."""
     import torch
-    net = networks.chain(networks.fuse(networks.resnet18(batch=4)))
+    net = networks.chain(networks.fuse(networks.resnet18(batch=4)), pool_planes=pool_planes)
     assert net.planes
     x = networks.make_input(net)
     want = cpu_buffers(net, x)
