@@ -455,7 +455,8 @@ class NetworkBench:
         if self.which == "lenet":
             return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
                     "parallelism": f"replicas only: one batch-1 stream per GPU ({world})", "calls": calls,
-                    "launches": "whole call list captured once as a CUDA graph and replayed"}
+                    "launches": ("whole call list run as one kernel launch (cm_calls), captured as a CUDA graph"
+                                 if ONE_LAUNCH else "whole call list captured once as a CUDA graph and replayed")}
         return {"workload": "resnet18-shaped (BASELINE configs[3])", "batch": 256,
                 "input": "256x3x224x224 uniform [0,1)", "macs_per_image": self.net.macs_per_image, "calls": calls,
                 "parallelism": f"batch-sharded over {world} GPU(s)", "l2": "inputs larger than L2 (77 MB input, 1.1 GB activations)"}
@@ -472,13 +473,14 @@ class NetworkBench:
             s.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(s):
                 for _ in range(3):            # warm: module loading and attribute setup happen outside capture
-                    networks.execute(self.net, networks.GpuBackend(s), self.bufs)
+                    networks.execute(self.net, networks.GpuBackend(s, one_launch=ONE_LAUNCH), self.bufs)
             torch.cuda.current_stream().wait_stream(s)
             torch.cuda.synchronize()
             l0 = cm.launch_count()
             self.graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.graph):
-                networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream()), self.bufs)
+                networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH),
+                                 self.bufs)
             self.launches_per_step = cm.launch_count() - l0
             torch.cuda.synchronize()
 
@@ -548,7 +550,7 @@ class NetworkBench:
         import torch
         from cormorant_b200 import networks
         self.bufs[self.net.input].copy_(self.hx, non_blocking=True)
-        networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream()), self.bufs)
+        networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH), self.bufs)
         self.hy.copy_(self.bufs[self.net.resolve(self.net.output)], non_blocking=True)
 
     def e2e_step(self):
@@ -598,6 +600,7 @@ class NetworkBench:
 UNFUSED = False      # --unfused: networks run node by node
 FUSE_RESIDUAL = True   # --no-fuse-residual: fold Conv->Relu only
 PLANES = True          # --no-planes: every conv splits its own input
+ONE_LAUNCH = False     # --one-launch: lenet's whole call list as one cm_calls launch (slower on B200)
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -768,15 +771,18 @@ def main():
                     help="lenet/resnet: fold Conv->Relu only (keep the residual Add / Relu passes)")
     ap.add_argument("--unfused", action="store_true",
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
+    ap.add_argument("--one-launch", action="store_true",
+                    help="lenet: the whole call list in one single-CTA launch (cm_calls) instead of one launch per call")
     ap.add_argument("--no-planes", action="store_true",
                     help="resnet: no plane images between convs (each conv splits its NCHW input)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
     args = ap.parse_args()
-    global UNFUSED, FUSE_RESIDUAL, PLANES
+    global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH
     UNFUSED = args.unfused
     FUSE_RESIDUAL = not args.no_fuse_residual
     PLANES = not args.no_planes
+    ONE_LAUNCH = args.one_launch
     if args.int8_peak:
         return int8_peak()
     if args.shape:

@@ -57,6 +57,9 @@ SIGNATURES: dict[str, tuple] = {
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),
+    "cm_calls_supported": (C.c_int, [_p, _u]),
+    "cm_calls": (C.c_int, [_p, _u]),
+    "cm_calls_async": (C.c_int, [_p, _u, _p]),
     "cm_pool": (C.c_int, [_p, _p] + [_u] * 17),
     "cm_pool_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
     "cm_buf_alloc": (_p, [_u]),

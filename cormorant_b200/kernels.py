@@ -159,6 +159,47 @@ def PoolingKernelPlanes(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_
     check(L.cm_pool_planes(*args) if stream is None else L.cm_pool_planes_async(*args, _stream(stream)))
 
 
+CALL_VECTOROP, CALL_MATMUL, CALL_CONV, CALL_POOL = 0, 1, 2, 3
+CALLS_MAX = 24
+
+
+def _call_struct():
+    import ctypes as C
+
+    class CmCall(C.Structure):                       # cm_call_t (include/cormorant_cuda.h)
+        _fields_ = [("kind", C.c_uint), ("epilogue", C.c_uint), ("in0", C.c_void_p), ("in1", C.c_void_p),
+                    ("in2", C.c_void_p), ("resid", C.c_void_p), ("out", C.c_void_p), ("args", C.c_uint * 17)]
+    return CmCall
+
+
+_CmCall = None
+
+
+def call_array(calls):
+    """A cm_call_t array from (kind, epilogue, in0, in1, in2, resid, out, args) tuples
+    (buffers as tensors or device addresses)."""
+    global _CmCall
+    if _CmCall is None:
+        _CmCall = _call_struct()
+    arr = (_CmCall * len(calls))()
+    for d, (kind, epi, in0, in1, in2, resid, out, args) in zip(arr, calls):
+        d.kind, d.epilogue = int(kind), int(epi)
+        d.in0, d.in1, d.in2, d.resid, d.out = _addr(in0), _addr(in1), _addr(in2), _addr(resid), _addr(out)
+        for k, v in enumerate(args):
+            d.args[k] = int(v)
+    return arr
+
+
+def calls_supported(arr) -> bool:
+    return bool(lib().cm_calls_supported(arr, len(arr)))
+
+
+def RunCalls(arr, stream=None) -> None:
+    """The whole small call list in one launch (cm_calls)."""
+    L = lib()
+    check(L.cm_calls(arr, len(arr)) if stream is None else L.cm_calls_async(arr, len(arr), _stream(stream)))
+
+
 def _planes(p) -> int | None:
     return None if p is None else p.ptr
 

@@ -406,6 +406,33 @@ def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
     return fused
 
 
+def calls_of(net: Net, bufs: dict):
+    """The call list as (kind, epilogue, in0, in1, in2, resid, out, args) tuples for
+    cm_calls, or None when a node has no one-launch form (plane images)."""
+    from . import kernels as k
+    R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
+    out = []
+    for node in net.nodes:
+        kind = node[0]
+        if kind == "conv" and len(node) <= 8:
+            _, x, wn, bn, y, args = node[:6]
+            epi, resid = (node[6], node[7]) if len(node) > 6 else (0, None)
+            out.append((k.CALL_CONV, epi, R(x), R(wn), R(bn), R(resid), R(y), args))
+        elif kind == "matmul":
+            _, a, b, c, args = node[:5]
+            epi, bias = (node[5], node[6]) if len(node) > 5 else (0, None)
+            out.append((k.CALL_MATMUL, epi, R(a), R(b), R(bias), None, R(c), args))
+        elif kind == "pool":
+            _, x, y, args = node
+            out.append((k.CALL_POOL, 0, R(x), None, None, None, R(y), args))
+        elif kind == "vectorop":
+            _, a, b, c, args = node
+            out.append((k.CALL_VECTOROP, 0, R(a), R(b), None, None, R(c), args))
+        else:
+            return None
+    return out
+
+
 def execute(net: Net, backend, bufs: dict) -> None:
     """Run every node of `net` on `backend` over `bufs` (name -> backend buffer).
 
@@ -413,6 +440,8 @@ def execute(net: Net, backend, bufs: dict) -> None:
     matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars),
     pool(x, y, *17 scalars) and, for fused call lists, conv_fused(x, w, bias, y, *17
     scalars, epilogue, resid) and matmul_fused(a, b, c, *7 scalars, epilogue, bias)."""
+    if getattr(backend, "one_launch", False) and backend.run_list(net, bufs):
+        return
     R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
     for node in net.nodes:
         kind = node[0]
@@ -450,10 +479,30 @@ def execute(net: Net, backend, bufs: dict) -> None:
 class GpuBackend:
     """The four kernels of libcormorant_cuda.so on one CUDA stream (asynchronous)."""
 
-    def __init__(self, stream=None):
+    def __init__(self, stream=None, one_launch: bool = False):
         from . import kernels
         self.k = kernels
         self.stream = stream
+        # one_launch: a call list that cm_calls accepts (small batch-1 networks) runs as
+        # one kernel launch instead of one launch per call
+        self.one_launch = one_launch
+        self._lists: dict = {}
+
+    def run_list(self, net, bufs) -> bool:
+        key = (id(net), id(bufs))
+        if key not in self._lists:
+            calls = calls_of(net, bufs)
+            arr = None
+            if calls is not None and 0 < len(calls) <= self.k.CALLS_MAX:
+                arr = self.k.call_array(calls)
+                if not self.k.calls_supported(arr):
+                    arr = None
+            self._lists[key] = arr
+        arr = self._lists[key]
+        if arr is None:
+            return False
+        self.k.RunCalls(arr, stream=self.stream)
+        return True
 
     def vectorop(self, a, b, c, size, op, outer, a_inc, b_inc):
         self.k.VectorOPKernel(a, b, c, size, op, outer, a_inc, b_inc, stream=self.stream)

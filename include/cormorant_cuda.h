@@ -257,6 +257,36 @@ int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t*
                          unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
                          const cm_planes_t* resid_planes, cm_stream_t stream);
 
+/* ---- Small call lists in one launch (no reference counterpart) ----------------------
+ * A list of small kernel calls -- a batch-1 network, bound by launch latency -- run as ONE
+ * CTA that executes them in order, with the results of the entry points named below,
+ * word for word.  Supported: CM_CALL_CONV (cm_conv_fused's arguments: args = its 17
+ * scalars, epilogue 0..3, in0 x, in1 weight, in2 bias, resid), CM_CALL_MATMUL
+ * (cm_matmul_fused: args = its 7 scalars, epilogue 0..3, in0 a, in1 b, in2 bias row),
+ * CM_CALL_POOL (cm_pool with pool_type MAX: args = its 17 scalars, in0 x) and
+ * CM_CALL_VECTOROP (cm_vectorop except DIV: args = size, op, outer, a_inc, b_inc, in0 a,
+ * in1 b); at most 2^20 outputs and 2^22 multiply-accumulates per call, no overlapping
+ * output rows.  cm_calls_supported says whether a list qualifies (1) or not (0);
+ * cm_calls_async refuses a list that does not with CM_EUNSUPPORTED. */
+#define CM_CALL_VECTOROP 0u
+#define CM_CALL_MATMUL   1u
+#define CM_CALL_CONV     2u
+#define CM_CALL_POOL     3u
+#define CM_CALLS_MAX     24u
+typedef struct cm_call {
+    unsigned kind;           /* CM_CALL_* */
+    unsigned epilogue;       /* conv / matmul: the fused epilogue bits */
+    const int16_t* in0;
+    const int16_t* in1;
+    const int16_t* in2;
+    const int16_t* resid;
+    int16_t* out;
+    unsigned args[17];       /* the entry point's scalar arguments, in its order */
+} cm_call_t;
+int cm_calls_supported(const cm_call_t* calls, unsigned count);
+int cm_calls(const cm_call_t* calls, unsigned count);
+int cm_calls_async(const cm_call_t* calls, unsigned count, cm_stream_t stream);
+
 /* ---- PoolingKernel -------------------------------------------------------------
  * pool_type CM_POOL_MAX / AVG / LP (any value >= 2 is LP); lp_order 1 = sum|x|,
  * any other value = sqrt(sum x^2); count_include_pad selects the AVG divisor. */

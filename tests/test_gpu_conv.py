@@ -183,3 +183,40 @@ def test_conv_fused_epilogue(cm, port, case, epi):
     if epi & 1:
         want = port.vectorop(want, None, size, 4, 1, 0, 0)[:size]
     assert_same(host(y), want, f"fused {case} epi {epi}")
+
+
+ONE_LAUNCH_CASES = [
+    (1, 1, 28, 28, 6, 5, 5, 1, 1, 1, 1, 2, 2, 2, 2, 1, 0),
+    (2, 6, 14, 14, 16, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),
+    (3, 5, 13, 11, 7, 2, 3, 3, 2, 2, 3, 1, 2, 0, 1, 1, 0),
+    (1, 8, 8, 8, 8, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 0, 1),
+]
+
+
+@pytest.mark.parametrize("case", ONE_LAUNCH_CASES)
+@pytest.mark.parametrize("epi", [0, 3])
+def test_one_launch_conv_and_pool_match_entries(cm, port, case, epi):
+    """cm_calls' conv (with the fused epilogue) and MAX pool equal cm_conv_fused / cm_pool."""
+    from cormorant_b200 import kernels
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    rng = np.random.default_rng(sum(case) + epi)
+    x = rand16(rng, N * C * H * W)
+    w = rand16(rng, M * (1 if dwm else C) * kh * kw)
+    b = rand16(rng, M)
+    r = rand16(rng, N * M * oh * ow)
+    args = (N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)
+    y1, y2 = empty(N * M * oh * ow), empty(N * M * oh * ow)
+    cm.ConvKernelFused(dev(x), dev(w), dev(b) if hb else None, y1, *args, epilogue=epi, resid=dev(r) if epi else None)
+    ph = (oh + 1) // 2
+    pool_args = (N, M, oh, ow, ph, (ow + 1) // 2, 3, 3, 2, 2, 1, 1, 1, 1, 0, 2, 0)
+    p1 = empty(N * M * ph * ((ow + 1) // 2))
+    p2 = empty(p1.numel())
+    cm.PoolingKernel(y1, p1, *pool_args)
+    arr = kernels.call_array([(kernels.CALL_CONV, epi, dev(x), dev(w), dev(b) if hb else None,
+                               dev(r) if epi else None, y2, args),
+                              (kernels.CALL_POOL, 0, y2, None, None, None, p2, pool_args)])
+    assert kernels.calls_supported(arr)
+    kernels.RunCalls(arr)
+    assert_same(host(y2), host(y1), f"one-launch conv {case} epi {epi}")
+    assert_same(host(p2), host(p1), f"one-launch pool after {case}")

@@ -103,3 +103,20 @@ def test_sweep_size(cm, port, op):
     c = empty(n)
     cm.VectorOPKernel(dev(a), dev(b), c, n, op)
     assert_same(host(c), port.vectorop(a, b, n, op), f"sweep op={op}")
+
+
+@pytest.mark.parametrize("op", [0, 1, 2, 4, 5, 7])
+def test_one_launch_vectorop_matches_entry(cm, port, op):
+    """cm_calls' VectorOP equals cm_vectorop (broadcast rows with gaps included)."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(op + 40)
+    size, outer, a_inc, b_inc = 37, 5, 41, 3
+    a = rand16(rng, outer * a_inc + size, -32768, 32768)
+    b = rand16(rng, outer * b_inc + size, -32768, 32768)
+    c1, c2 = empty(outer * (a_inc + b_inc) + size), empty(outer * (a_inc + b_inc) + size)
+    c1.fill_(0)
+    c2.fill_(0)
+    cm.VectorOPKernel(dev(a), dev(b), c1, size, op, outer, a_inc, b_inc)
+    kernels.RunCalls(kernels.call_array([(kernels.CALL_VECTOROP, 0, dev(a), dev(b), None, None, c2,
+                                          (size, op, outer, a_inc, b_inc))]))
+    assert_same(host(c2), host(c1), f"one-launch vectorop {op}")

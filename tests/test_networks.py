@@ -251,3 +251,38 @@ def test_resnet18_chained_batch4_every_output(cm, port, pool_planes):
     torch.cuda.synchronize()
     for name in net.buffers:
         assert_same(bufs[name].cpu().numpy()[: net.buffers[name]], want[name][: net.buffers[name]], f"resnet {name}")
+
+
+def test_one_launch_call_list_qualifies_on_cpu():
+    """LeNet's folded call list runs in one cm_calls launch; ResNet-18's does not (too large)."""
+    from cormorant_b200 import kernels
+    net = networks.fuse(networks.lenet5())
+    fake = {n: 256 * (i + 1) for i, n in enumerate(list(net.buffers) + list(net.consts))}
+    arr = kernels.call_array(networks.calls_of(net, fake))
+    assert len(arr) == 7 and kernels.calls_supported(arr)
+    rn = networks.fuse(networks.resnet18(batch=1))
+    calls = networks.calls_of(rn, {n: 256 for n in list(rn.buffers) + list(rn.consts)})
+    assert len(calls) > kernels.CALLS_MAX or not kernels.calls_supported(kernels.call_array(calls[:24]))
+    # a DIV or an AVG pool is refused
+    bad = [(kernels.CALL_VECTOROP, 0, 256, 512, None, None, 768, (16, 3, 1, 0, 0))]
+    assert not kernels.calls_supported(kernels.call_array(bad))
+    bad = [(kernels.CALL_POOL, 0, 256, None, None, None, 768, (1, 1, 4, 4, 2, 2, 2, 2, 2, 2, 0, 0, 1, 1, 1, 2, 0))]
+    assert not kernels.calls_supported(kernels.call_array(bad))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("batch", [1, 3])
+def test_lenet_one_launch_every_activation(cm, port, batch):
+    import torch
+    net = networks.fuse(networks.lenet5(batch=batch))
+    x = networks.make_input(net)
+    want = cpu_buffers(net, x)
+    networks.execute(net, OracleBackend(port), want)
+    bufs = networks.gpu_buffers(net, x)
+    l0 = cm.launch_count()
+    be = networks.GpuBackend(one_launch=True)
+    networks.execute(net, be, bufs)
+    torch.cuda.synchronize()
+    assert cm.launch_count() - l0 == 1
+    for name in net.buffers:
+        assert_same(bufs[name].cpu().numpy()[: net.buffers[name]], want[name][: net.buffers[name]], f"lenet {name}")
