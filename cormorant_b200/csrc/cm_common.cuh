@@ -21,6 +21,7 @@ struct Context {
     uint64_t direct_max_macs = 1ull << 22;
     // 128-column GEMM tiles run on CTA pairs (tcgen05 cta_group::2); CM_GEMM_PAIRS=0 turns it off
     int gemm_pairs = 1;
+    int gemm_wa = 1;          // weights-as-A GEMM for conv outputs of at most 64 channels
 };
 
 Context* ctx();                      // nullptr before cm_init

@@ -825,18 +825,47 @@ bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint
 // channel sums of the padded original image) and the column terms come from the
 // original weights.
 
+//
+// Row stacking (T = 2): virtual pixel (h', w') also carries the channels of virtual
+// pixel (h' + 1, w'), channels (t, th, tw, c), so one kernel row of the stacked image
+// spans two virtual kernel rows -- a stride-1 conv with kernel rows 2 apart (dilation 2)
+// and ceil(kh2 / 2) of them.  For the stem that is 24 channels (32 with padding) x 4
+// taps = one full 128-byte K block per stacked row: 2 K blocks per tile instead of 4
+// half-empty ones, the same MMA steps.  A tile's time there goes by its K blocks (each
+// a round of TMA boxes), not by their bytes.
+
 struct S2dPlan {
     uint32_t s, C2, kh2, kw2, Hpo, Wpo;
+    uint32_t T = 1, kh3 = 0;   // row stacking; kh3 = stacked kernel rows (dilation T)
     ImplicitPlan ip;
 };
 
 bool plan_s2d(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
-              uint32_t dh, uint32_t dw, S2dPlan* sp) {
+              uint32_t dh, uint32_t dw, S2dPlan* sp, uint32_t T = 1) {
     if (sh != sw || sh < 2 || sh > 4 || dh != 1 || dw != 1 || C == 0 || kh == 0 || kw == 0) return false;
     const uint32_t s = sh, C2 = s * s * C;
     if (C2 > 64) return false;
     const uint32_t kh2 = (kh + s - 1) / s, kw2 = (kw + s - 1) / s;
     ImplicitPlan ip;
+    if (T == 2) {
+        if (2 * C2 > 64 || kh2 < 2) return false;
+        const uint32_t kh3 = (kh2 + 1) / 2;
+        const uint64_t Cp = (2ull * C2 + 15ull) & ~15ull, KR = (uint64_t)kw2 * Cp, KR_pad = (KR + 127) & ~127ull;
+        const uint64_t Hp = (uint64_t)out_h + kh2 - 1, Wp = (uint64_t)out_w + kw2 - 1;
+        if (Hp * Wp >= (1ull << 31)) return false;
+        uint32_t bw = std::min<uint32_t>(pow2_ceil(out_w), 128);
+        uint32_t bh = std::min<uint32_t>(pow2_ceil(out_h), 128 / bw);
+        ip.Cp = (uint32_t)Cp; ip.Hp = (uint32_t)Hp; ip.Wp = (uint32_t)Wp;
+        ip.KR = (uint32_t)KR; ip.KR_pad = (uint32_t)KR_pad; ip.Kt = (uint32_t)(KR_pad * kh3);
+        ip.bw = bw; ip.bh = bh; ip.bn = 128 / (bw * bh);
+        const uint64_t steps = (uint64_t)kh3 * ((KR + 31) / 32) * 32;
+        if (steps > 2ull * C * kh * kw) return false;
+        sp->s = s; sp->C2 = C2; sp->kh2 = kh2; sp->kw2 = kw2;
+        sp->Hpo = ip.Hp * s; sp->Wpo = ip.Wp * s;
+        sp->T = 2; sp->kh3 = kh3;
+        sp->ip = ip;
+        return true;
+    }
     if (!plan_implicit(C2, out_h, out_w, kh2, kw2, 1, 1, 1, 1, &ip)) {
         // plan_implicit's waste rule counts the virtual taps as real; re-plan without it
         const uint64_t Cp = (C2 + 15ull) & ~15ull, KR = (uint64_t)kw2 * Cp, KR_pad = (KR + 127) & ~127ull;
@@ -853,6 +882,7 @@ bool plan_s2d(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t 
     if (steps > 2ull * C * kh * kw) return false;
     sp->s = s; sp->C2 = C2; sp->kh2 = kh2; sp->kw2 = kw2;
     sp->Hpo = ip.Hp * s; sp->Wpo = ip.Wp * s;
+    sp->T = 1; sp->kh3 = kh2;
     sp->ip = ip;
     return true;
 }
@@ -919,20 +949,22 @@ __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __re
 constexpr uint32_t kS2dRowThreads = 128;
 constexpr uint32_t kS2dRowSmem = 32u * 1024u;
 
-template <int S_, int C_>
+// T_ = 2: the block also stages virtual row hv + 1 and writes its channels after those of
+// row hv (row stacking); So is written for row hv only.
+template <int S_, int C_, int T_ = 1>
 __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int16_t* __restrict__ x, S2dGeom g,
                                                                         int8_t* __restrict__ planes,
                                                                         int32_t* __restrict__ So) {
-    static_assert(S_ >= 2 && S_ * S_ * C_ <= 64, "space-to-depth channels");
-    constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (C2 + 15u) / 16u * 16u;
-    extern __shared__ __align__(16) int16_t rowbuf[];      // [S_ * C_][W]
+    static_assert(S_ >= 2 && T_ * S_ * S_ * C_ <= 64, "space-to-depth channels");
+    constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (T_ * C2 + 15u) / 16u * 16u;
+    extern __shared__ __align__(16) int16_t rowbuf[];      // [T_ * S_ * C_][W]
     const uint32_t hv = blockIdx.x, n = blockIdx.y;
     const uint32_t W = g.W;
     const int16_t* xn = x + (uint64_t)n * C_ * g.H * W;
     const bool pairs = (W & 1u) == 0 && (((uintptr_t)x) & 3u) == 0;
 #pragma unroll
-    for (uint32_t r = 0; r < (uint32_t)(S_ * C_); ++r) {
-        const uint32_t th = r / C_, c = r % C_;
+    for (uint32_t r = 0; r < (uint32_t)(T_ * S_ * C_); ++r) {
+        const uint32_t th = r / C_, c = r % C_;           // th < T_*S_: input row S_*hv + th
         const int32_t ih = (int32_t)(S_ * hv + th) - (int32_t)g.pt;
         int16_t* dst = rowbuf + r * W;
         if (ih >= 0 && ih < (int32_t)g.H) {
@@ -954,7 +986,7 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
 #pragma unroll
         for (uint32_t q = 0; q < CPC / 4; ++q) { hw[q] = 0; lw[q] = 0x80808080u; }
 #pragma unroll
-        for (uint32_t th = 0; th < (uint32_t)S_; ++th) {
+        for (uint32_t th = 0; th < (uint32_t)(T_ * S_); ++th) {   // th >= S_: stacked row hv + 1
             int32_t sums[S_];
 #pragma unroll
             for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) {
@@ -972,12 +1004,14 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
                 }
                 sums[tw] = sum;
             }
-            int32_t* so = So + ((uint64_t)n * g.Hpo + S_ * hv + th) * g.Wpo + S_ * wv;
-            if constexpr (S_ == 2) {
-                *(int2*)so = make_int2(sums[0], sums[1]);
-            } else {
+            if (th < (uint32_t)S_) {
+                int32_t* so = So + ((uint64_t)n * g.Hpo + S_ * hv + th) * g.Wpo + S_ * wv;
+                if constexpr (S_ == 2) {
+                    *(int2*)so = make_int2(sums[0], sums[1]);
+                } else {
 #pragma unroll
-                for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) so[tw] = sums[tw];
+                    for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) so[tw] = sums[tw];
+                }
             }
         }
         int8_t* dst = planes + (((uint64_t)n * g.Hs + hv) * g.Ws + wv) * g.Cp;
@@ -993,19 +1027,22 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
 // Virtual weights -> N-major planes (layout as conv_weights_kernel): row
 // k' = r'*KR_pad + u'*Cp + (th*s + tw)*C + c holds w[m][c][s*r' + th][s*u' + tw], zero past
 // the original kernel.  Thread per (k', m); the weights are small.
+// With row stacking (T = 2) channel c2 = (t, th, tw, c) of stacked kernel row r2 is
+// virtual kernel row T*r2 + t.
 __global__ void __launch_bounds__(256) conv_s2d_weights_kernel(const int16_t* __restrict__ w, uint32_t M, uint32_t C,
                                                                uint32_t kh, uint32_t kw, uint32_t s, uint32_t kw2,
                                                                uint32_t Cp, uint32_t KR_pad, uint32_t Kt, uint32_t pitch,
-                                                               uint64_t plane, int8_t* __restrict__ planes) {
+                                                               uint64_t plane, int8_t* __restrict__ planes, uint32_t T) {
     const uint64_t total = (uint64_t)Kt * M;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint32_t kp = (uint32_t)(t / M), m = (uint32_t)(t - (uint64_t)kp * M);
         const uint32_t r2 = kp / KR_pad, rem = kp - r2 * KR_pad;
         const uint32_t u2 = rem / Cp, c2 = rem - u2 * Cp;
         int8_t hi = 0, lo = 0;
-        if (u2 < kw2 && c2 < s * s * C) {
-            const uint32_t blk = c2 / C, c = c2 - blk * C, th = blk / s, tw = blk - th * s;
-            const uint32_t r = s * r2 + th, q = s * u2 + tw;
+        if (u2 < kw2 && c2 < T * s * s * C) {
+            const uint32_t st = c2 / (s * s * C), c2b = c2 - st * (s * s * C);
+            const uint32_t blk = c2b / C, c = c2b - blk * C, th = blk / s, tw = blk - th * s;
+            const uint32_t r = s * (T * r2 + st) + th, q = s * u2 + tw;
             if (r < kh && q < kw) {
                 const int16_t v = __ldg(w + (((uint64_t)m * C + c) * kh + r) * kw + q);
                 hi = (int8_t)(v >> 8);
@@ -1292,6 +1329,12 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
 
     S2dPlan sp;
     if (plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp)) {
+        // row stacking where the row-staged split kernel serves it and it saves K blocks
+        S2dPlan sp2;
+        if (stride_h == 2 && in_ch == 3 && 4ull * in_ch * in_w * 2 <= kS2dRowSmem &&
+            plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp2, 2) &&
+            sp2.kh3 * (sp2.ip.KR_pad / 128) < sp.kh3 * (sp.ip.KR_pad / 128))
+            sp = sp2;
         const ImplicitPlan& vp = sp.ip;
         const uint32_t M_pad = pad_c(out_ch);
         const bool packed = out_ch <= 64;
@@ -1323,7 +1366,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             ProfScope ps_(PK_SPLIT, s);
             const uint64_t wtot = (uint64_t)vp.Kt * out_ch;
             conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
-                                                                              vp.Cp, vp.KR_pad, vp.Kt, w_pitch, w_plane, wpl);
+                                                                              vp.Cp, vp.KR_pad, vp.Kt, w_pitch, w_plane, wpl,
+                                                                              sp.T);
             count_launch();
         }
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
@@ -1333,8 +1377,15 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             {
                 ProfScope ps_(PK_SPLIT, s);
                 const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
-                const uint64_t row_smem = (uint64_t)sp.s * in_ch * in_w * 2;
-                if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
+                const uint64_t row_smem = (uint64_t)sp.T * sp.s * in_ch * in_w * 2;
+                if (sp.T == 2) {
+                    for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
+                        const uint32_t bz = std::min(65535u, nb - b0);
+                        conv_s2d_rows_kernel<2, 3, 2><<<dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s>>>(
+                            xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so);
+                        count_launch();
+                    }
+                } else if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
                     for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                         const uint32_t bz = std::min(65535u, nb - b0);
                         // images b0..: shift the input, planes and So bases; the plane stride stays the chunk's
@@ -1351,7 +1402,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 }
                 rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
             }
-            const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh2, 1, 1, 1,
+            const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh3, 1, 1, sp.T,
                            out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, vp.Kt, vp.Kt, M_pad, rt, ct,
                        y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};

@@ -14,20 +14,20 @@
 // Each accumulator's magnitude stays below K * 2^15, so K <= 65535 never
 // overflows an int32 on the way.
 //
-// Kernel (one 128x128 output tile per CTA, 192 threads, 1 CTA per SM):
-//   warp 0   TMA producer: per K block of 128, one 4-D box {128 k, 128 rows, 2 planes,
-//            1 batch} of the K-major A planes and one box {128 n, 128 k, 2 planes,
-//            1 batch} of the N-major B planes (32 KB each, 128-byte swizzle),
-//            3-stage ring guarded by full/empty mbarriers.  No multicast.
+// Kernel (persistent, 1 CTA per SM or a CTA pair per 2 SMs, 576 threads):
+//   warp 0   TMA producer: per K block of 128, the A planes' box (hi, lo') and the B
+//            planes' box into a stage of a ring guarded by full/empty mbarriers.
+//            No multicast.
 //   warp 1   allocates all 512 TMEM columns; lane 0 issues the MMAs and commits.
-//            The B box lands as two N-major 128-column atoms [Bh | Bl] = one
-//            256-column operand, so each 32-deep K step is two M=128, N=256 MMAs:
-//            Ah x [Bh|Bl] -> (HH | HL) and Al x [Bh|Bl] -> (LH | LL), four
-//            128-column int32 accumulators.
-//            N=256 halves the shared-memory operand reads per MAC against N=128,
-//            which is what bounds this kernel (TMA writes share the bandwidth).
-//   warps 2-5 epilogue: tcgen05.ld 32 lanes x 32 columns of each accumulator,
-//            recombine, narrow, store int16 rows.
+//            128-column tiles: the B box lands as two N-major 128-column atoms
+//            [Bh | Bl] = one 256-column operand, so each 32-deep K step is two M=128,
+//            N=256 MMAs: Ah x [Bh|Bl] -> (HH | HL) and Al x [Bh|Bl] -> (LH | LL), four
+//            128-column int32 accumulators (CTA pairs: M = 256, one B plane per CTA).
+//            64-column tiles keep B packed ([64 hi | 64 lo] per K row, N = 128) with
+//            double-buffered accumulators, or swap the operands (weights as A, N = 256:
+//            see Cfg).
+//   warps 2-17 epilogue: tcgen05.ld of the accumulators, recombine, narrow, fused
+//            VectorOP epilogue, store int16 (or the next conv's plane image).
 // Every mbarrier wait is bounded by %globaltimer; on expiry the kernel records
 // CM_ETIMEOUT in the status word and winds down instead of hanging.
 #include <cuda.h>
@@ -54,9 +54,19 @@ constexpr uint32_t TMEM_COLS = 512;
 // at most 64 columns): B is stored packed, each K row = [64 hi | 64 lo] bytes, so
 // one 128-byte atom is the whole [Bh | Bl] operand (16 KB); the four 64-column
 // accumulators take 256 TMEM columns and are double-buffered.
-template <int TBN, int CG = 1>
+//
+// WA ("weights as A", conv outputs of at most 64 channels): the roles swap so that the
+// MMA is N = 256 wide.  A = the weight tile, 128 K-major rows (channel m's hi plane in
+// row 2m, its lo' plane in row 2m + 1); B = the activation tile, K-major, its 128 hi
+// rows followed by its 128 lo' rows (the two plane boxes are adjacent in shared
+// memory).  One MMA per 32-deep step writes all four products of 64 channels x 128
+// pixels into 256 accumulator columns (pixels of the hi plane, then of the lo' plane),
+// double-buffered.  An M = 128, N = 128 MMA takes as long as an N = 256 one, so the
+// packed form's two N = 128 MMAs per step ran the tensor pipe at half rate.
+template <int TBN, int CG = 1, bool WA = false>
 struct Cfg {
     static_assert(CG == 1 || TBN == 128, "CTA pairs use 128-column tiles");
+    static_assert(!WA || (TBN == 64 && CG == 1), "weights-as-A tiles hold 64 channels");
     // a CTA pair holds one B plane per CTA (Bh in the even CTA, Bl in the odd one)
     static constexpr int B_TILE = CG == 2 ? PLANE_TILE : (TBN == 128 ? 2 * PLANE_TILE : PLANE_TILE);
     static constexpr int STAGE = OPERAND_TILE + B_TILE;
@@ -67,11 +77,14 @@ struct Cfg {
     // with short mainloops: conv tiles with few K blocks, fused residual reads)
     static constexpr int EPI_WARPS = 16;
     static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-    static constexpr uint32_t MMA_N = 2 * TBN;         // [Bh | Bl]
-    // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16), M = 128 * CG, N = MMA_N.
-    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((MMA_N >> 3) << 17) |
+    static constexpr uint32_t MMA_N = WA ? 256u : 2 * TBN;   // [Bh | Bl], or WA: [hi pixels | lo' pixels]
+    // Instruction descriptor: D s32, A s8 K-major, B s8 N-major (bit 16; K-major for WA),
+    // M = 128 * CG, N = MMA_N.
+    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | (WA ? 0u : (1u << 16)) | ((MMA_N >> 3) << 17) |
                                       ((uint32_t)((BM * CG) >> 4) << 24);
-    static constexpr int SMEM_USED = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+    // WA: a 16 x 16 int16 transpose buffer per epilogue warp, after the barriers
+    static constexpr int XPOSE_BYTES = WA ? EPI_WARPS * 512 : 0;
+    static constexpr int SMEM_USED = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/ + XPOSE_BYTES;
     static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
     static_assert(NBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
 };
@@ -321,10 +334,10 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
 // single-CTA kernel is bound by.  All TMA completions and epilogue releases go to the
 // even CTA's barriers; its MMA commits arrive on both CTAs' barriers (multicast
 // commit).  No TMA multicast is used.
-template <int TBN, int CG>
-__global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
+template <int TBN, int CG, bool WA = false>
+__global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
-    using C = Cfg<TBN, CG>;
+    using C = Cfg<TBN, CG, WA>;
     constexpr int STAGES = C::STAGES, NBUF = C::NBUF;
     constexpr uint32_t HALF = TBN / (C::EPI_WARPS / 4);  // columns per epilogue warp
     constexpr uint32_t CW = 16;                           // columns per TMEM load
@@ -413,7 +426,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                         } else {
                             tma_load_4d(smem_u32(st), &tmA, full, (int)(kb * BK), (int)tc.m0, 0, (int)tc.ba);
                         }
-                        tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), 0, (int)tc.bb);
+                        if (WA) tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)(kb * BK), 0, 0, 0);   // weight rows
+                        else tma_load_4d(smem_u32(st + OPERAND_TILE), &tmB, full, (int)tc.n0, (int)(kb * BK), 0, (int)tc.bb);
                     }
                 }
             }
@@ -449,7 +463,10 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
                         const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
                         const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x [Bh | Bl]
                         const uint32_t acc = (kb | kk) != 0u;
-                        if (CG == 2) {
+                        if (WA) {
+                            // weights (A) x [hi pixels | lo' pixels] (B, 256 K-major rows)
+                            umma_i8(d, sdesc(b0 + kk * 32), ah, C::IDESC, acc);
+                        } else if (CG == 2) {
                             umma_i8_pair(d, ah, bhl, C::IDESC, acc);            // -> HH | HL (both CTAs)
                             umma_i8_pair(d + 2 * TBN, al, bhl, C::IDESC, acc);  // -> LH | LL
                         } else {
@@ -472,6 +489,182 @@ __global__ void __launch_bounds__(Cfg<TBN, CG>::THREADS, 1)
             volatile int never = 0;
             WaitCtl drain{&never, g.status, g.timeout_ns};
             mbar_wait(smem_u32(done_b), 0, drain);
+        }
+    } else if constexpr (WA) {
+        // Outputs go to a plane image only (the host sends no NCHW output here).
+        // TMEM lane = weight row: channel ch = 16*quarter + lane/2, hi plane in the even
+        // lane, lo' plane in the odd one; columns = tile pixels (products with the pixels'
+        // hi plane in columns 0..127, with their lo' plane in 128..255).  Per pixel
+        // acc = 2^16*HH + 2^8*(HL + LH) + LL: the even lane holds HH and HL, the odd lane LH
+        // and LL; of each 16-pixel chunk the even lane finishes pixels 0-7 and the odd lane
+        // pixels 8-15, each taking its partner's partial sums by one shuffle per pixel.
+        const uint32_t quarter = warp & 3u;
+        const uint32_t cgrp = (warp - 2) >> 2;               // tile pixels 32*cgrp .. +31
+        const uint32_t odd = lane & 1u;
+        const uint32_t ch = 16u * quarter + (lane >> 1);
+        const uint32_t m1 = odd ? 256u : 65536u, m2 = odd ? 1u : 256u;
+        int16_t* xb = (int16_t*)(smem + STAGES * C::STAGE + 256) + (warp - 2) * 256;
+        const uint32_t bwm = (1u << g.bw_log) - 1u, bhm = (1u << g.bh_log) - 1u, bsh = g.bw_log + g.bh_log;
+        const bool cvalid = ch < g.cols;
+        const uint32_t ct = cvalid ? (uint32_t)__ldg(g.colterm + ch) : 0u;
+        const bool prl = (g.epi & 2u) && g.rpl;               // residual read from a plane image
+        // channels 8*odd .. +7 of this quarter in the pixel-major phase
+        const uint32_t cl0 = 16u * quarter + 8u * odd;
+        const uint32_t live = g.cols > cl0 ? min(8u, g.cols - cl0) : 0u;
+        const bool qlive = 16u * quarter < g.cols;
+        uint32_t j = 0;
+        for (uint64_t t = cid; t < total; t += ncl, ++j) {
+            const uint32_t buf = j % NBUF, use = j / NBUF;
+            const Tile tc = decode_tile<TBN, CG>(g, t, rank);
+            // this thread's two runs of 8 pixels (tile pixels i0 .. i0+7, one image row: bw >= 8),
+            // their row terms and residual words, fetched while the tile's MMAs run
+            uint32_t nv[2];
+            uint64_t ooff[2];
+            uint32_t rt[2][8];
+            uint4 rs[2];
+#pragma unroll
+            for (uint32_t h = 0; h < 2; ++h) {
+                const uint32_t i0 = 32u * cgrp + 16u * h + 8u * odd;
+                const uint32_t ow = tc.cw0 + (i0 & bwm);
+                const uint32_t oh = tc.ch0 + ((i0 >> g.bw_log) & bhm);
+                const uint32_t n = tc.cn0 + (i0 >> bsh);
+                nv[h] = (oh < g.out_h && n < g.nimg && ow < g.out_w) ? min(8u, g.out_w - ow) : 0u;
+                const uint64_t pix = (uint64_t)oh * g.out_w + ow;
+                const uint64_t ri = (uint64_t)n * g.out_h * g.out_w + pix;
+                ooff[h] = (uint64_t)n * g.out_bs + pix;
+                if (nv[h] == 8u && (ri & 3u) == 0) {
+                    const int4 a = __ldg((const int4*)(g.rowterm + ri)), b = __ldg((const int4*)(g.rowterm + ri + 4));
+                    rt[h][0] = (uint32_t)a.x; rt[h][1] = (uint32_t)a.y; rt[h][2] = (uint32_t)a.z; rt[h][3] = (uint32_t)a.w;
+                    rt[h][4] = (uint32_t)b.x; rt[h][5] = (uint32_t)b.y; rt[h][6] = (uint32_t)b.z; rt[h][7] = (uint32_t)b.w;
+                } else {
+#pragma unroll
+                    for (uint32_t k = 0; k < 8; ++k) rt[h][k] = k < nv[h] ? (uint32_t)__ldg(g.rowterm + ri + k) : 0u;
+                }
+                rs[h] = make_uint4(0, 0, 0, 0);
+                if ((g.epi & 2u) && !g.rpl && cvalid && nv[h]) {
+                    const int16_t* src = g.resid + ooff[h] + (uint64_t)ch * g.ldc;
+                    if (nv[h] == 8u && ((uintptr_t)src & 15u) == 0) {
+                        rs[h] = __ldg((const uint4*)src);
+                    } else {
+                        uint32_t w4[4] = {0, 0, 0, 0};
+#pragma unroll
+                        for (uint32_t k = 0; k < 8; ++k)
+                            if (k < nv[h]) w4[k / 2] |= (uint32_t)(uint16_t)__ldg(src + k) << (16 * (k & 1));
+                        rs[h] = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    }
+                }
+            }
+            // a residual plane image: this lane's pixel-major runs (8 channels of pixel lane/2
+            // of each chunk), as hi and lo' bytes
+            uint2 rh[2], rl[2];
+#pragma unroll
+            for (uint32_t h = 0; h < 2; ++h) {
+                rh[h] = make_uint2(0, 0);
+                rl[h] = make_uint2(0x80808080u, 0x80808080u);
+                if (prl && live) {
+                    const uint32_t i = 32u * cgrp + 16u * h + (lane >> 1);
+                    const uint32_t ow = tc.cw0 + (i & bwm), oh = tc.ch0 + ((i >> g.bw_log) & bhm), n = tc.cn0 + (i >> bsh);
+                    if (ow < g.out_w && oh < g.out_h && n < g.nimg) {
+                        const int8_t* src =
+                            g.rpl + (((uint64_t)n * g.rpl_Hp + oh + g.rpl_pt) * g.rpl_Wp + ow + g.rpl_pl) * g.rpl_Cp + cl0;
+                        rh[h] = __ldg((const uint2*)src);
+                        rl[h] = __ldg((const uint2*)(src + g.rpl_plane));
+                    }
+                }
+            }
+            uint32_t ok = 0;
+            if (lane == 0) ok = (mbar_wait(smem_u32(&accf_b[buf]), use & 1u, wc) && !*abort_flag) ? 1u : 0u;
+            ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+            __syncwarp();
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t tl = tmem + buf * C::ACC_COLS + ((quarter * 32u) << 16) + 32u * cgrp;
+            uint32_t v[2][4];
+#pragma unroll
+            for (uint32_t h = 0; h < 2; ++h) {
+                uint32_t dh[16], dl[16];
+                tmem_ld16(tl + 16u * h, dh);
+                tmem_ld16(tl + 128u + 16u * h, dl);
+                tmem_ld_wait();
+                uint32_t acc[8];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const uint32_t p0 = dh[k] * m1 + dl[k] * m2, p1 = dh[k + 8] * m1 + dl[k + 8] * m2;
+                    const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, odd ? p0 : p1, 1);
+                    acc[k] = (odd ? p1 : p0) + other + rt[h][k] + ct;
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[h][q] = narrow_pack(acc[2 * q], acc[2 * q + 1]);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(&acce_b[buf]));   // buffer free for the next tile
+            if (!prl) {
+                // channel-major: residual words (NCHW), ReLU
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    if (g.epi & 2u) {
+                        v[h][0] = __vaddss2(v[h][0], rs[h].x); v[h][1] = __vaddss2(v[h][1], rs[h].y);
+                        v[h][2] = __vaddss2(v[h][2], rs[h].z); v[h][3] = __vaddss2(v[h][3], rs[h].w);
+                    }
+                    if (g.epi & 1u) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) v[h][q] = __vmaxs2(v[h][q], 0u);
+                    }
+                }
+            }
+            {
+                // pixel-major: each 16-pixel x 16-channel chunk through the warp's buffer;
+                // lane -> pixel lane/2 of the chunk, channels cl0 .. cl0+7
+#pragma unroll
+                for (uint32_t h = 0; h < 2; ++h) {
+                    __syncwarp();
+#pragma unroll
+                    for (uint32_t k = 0; k < 8; ++k)
+                        xb[(8u * odd + k) * 16u + (lane >> 1)] = (int16_t)(uint16_t)(v[h][k / 2] >> (16 * (k & 1)));
+                    __syncwarp();
+                    const uint4 w = *(const uint4*)(xb + (lane >> 1) * 16u + 8u * odd);
+                    uint32_t pw[4] = {w.x, w.y, w.z, w.w};
+                    const uint32_t i = 32u * cgrp + 16u * h + (lane >> 1);
+                    const uint32_t ow = tc.cw0 + (i & bwm), oh = tc.ch0 + ((i >> g.bw_log) & bhm), n = tc.cn0 + (i >> bsh);
+                    const bool pv = ow < g.out_w && oh < g.out_h && n < g.nimg;
+                    if (prl) {
+                        const uint32_t h4[2] = {rh[h].x, rh[h].y}, l4[2] = {rl[h].x ^ 0x80808080u, rl[h].y ^ 0x80808080u};
+#pragma unroll
+                        for (uint32_t q = 0; q < 2; ++q) {
+                            pw[2 * q] = __vaddss2(pw[2 * q], __byte_perm(l4[q], h4[q], 0x5140));
+                            pw[2 * q + 1] = __vaddss2(pw[2 * q + 1], __byte_perm(l4[q], h4[q], 0x7362));
+                        }
+                        if (g.epi & 1u) {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) pw[q] = __vmaxs2(pw[q], 0u);
+                        }
+                    }
+                    {
+                        const uint64_t pix = ((uint64_t)n * g.po_Hp + oh + g.po_pt) * g.po_Wp + ow + g.po_pl;
+                        int32_t sum = 0;
+                        if (pv && qlive) {
+                            // channels past the output hold x = 0 (hi 0, lo' -128), not in the sum
+#pragma unroll
+                            for (uint32_t q = 0; q < 4; ++q) {
+                                if (2 * q >= live) pw[q] &= 0xFFFF0000u;
+                                if (2 * q + 1 >= live) pw[q] &= 0x0000FFFFu;
+                            }
+                            const uint32_t h0 = __byte_perm(pw[0], pw[1], 0x7531), h1 = __byte_perm(pw[2], pw[3], 0x7531);
+                            const uint32_t l0 = __byte_perm(pw[0], pw[1], 0x6420) ^ 0x80808080u;
+                            const uint32_t l1 = __byte_perm(pw[2], pw[3], 0x6420) ^ 0x80808080u;
+                            const int sh = __dp4a((int)h1, 0x01010101, __dp4a((int)h0, 0x01010101, 0));
+                            const int sl = __dp4a((int)l1, 0x01010101, __dp4a((int)l0, 0x01010101, 0));
+                            sum = 256 * sh + sl + 128 * (int32_t)(8u - live);
+                            int8_t* dst = g.po + pix * g.po_Cp + cl0;
+                            *(uint2*)dst = make_uint2(h0, h1);
+                            *(uint2*)(dst + g.po_plane) = make_uint2(l0, l1);
+                        }
+                        sum += __shfl_xor_sync(0xFFFFFFFFu, sum, 1);
+                        if (!odd && pv && qlive) atomicAdd(g.po_S + pix, sum);
+                    }
+                }
+            }
         }
     } else {
         const uint32_t quarter = warp & 3u;
@@ -961,25 +1154,65 @@ int make_packed_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t bat
     return CM_OK;
 }
 
-template <int TBN, int CG>
+// Weights-as-A operand: [128][Kt] int8, row 2m = channel m's hi plane, row 2m + 1 its
+// lo' plane, K contiguous (Kt a multiple of 128).
+int make_wa_map(CUtensorMap* m, const int8_t* base, uint32_t Kt) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)base & 15u) != 0 || Kt % BK != 0) return set_error(CM_EINVAL, "weight rows misaligned");
+    const cuuint64_t dims[4] = {Kt, 128, 1, 1};
+    const cuuint64_t strides[3] = {Kt, (cuuint64_t)Kt * 128, (cuuint64_t)Kt * 128};
+    const cuuint32_t box[4] = {(cuuint32_t)BK, 128, 1, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, (void*)base, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled (weight rows) failed (%d)", (int)r);
+    return CM_OK;
+}
+
+// Packed weight planes [Kt][64 hi | 64 lo] -> weight rows [128][Kt] (row 2m + p = byte
+// p*64 + m of every K row).  Block = 128 K rows through shared memory.
+__global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __restrict__ packed, uint32_t Kt,
+                                                             int8_t* __restrict__ rows) {
+    __shared__ uint32_t tile[128][33];            // [k][byte / 4] of the packed rows
+    const uint32_t k0 = blockIdx.x * 128;
+    for (uint32_t q = threadIdx.x; q < 128 * 8; q += 256) {
+        const uint32_t k = q / 8, seg = q % 8;
+        const uint4 v = __ldg((const uint4*)(packed + (uint64_t)(k0 + k) * 128 + seg * 16));
+        tile[k][4 * seg] = v.x; tile[k][4 * seg + 1] = v.y; tile[k][4 * seg + 2] = v.z; tile[k][4 * seg + 3] = v.w;
+    }
+    __syncthreads();
+    for (uint32_t q = threadIdx.x; q < 128 * 8; q += 256) {
+        const uint32_t R = q / 8, seg = q % 8;    // output row, 16-byte run of K
+        const uint32_t byte = (R & 1u) * 64 + (R >> 1);
+        uint32_t w[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (uint32_t b = 0; b < 16; ++b)
+            w[b / 4] |= ((tile[seg * 16 + b][byte / 4] >> (8 * (byte % 4))) & 0xFFu) << (8 * (b % 4));
+        *(uint4*)(rows + (uint64_t)R * Kt + k0 + seg * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+}
+
+template <int TBN, int CG, bool WA = false>
 int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s) {
     static int per_sm_clusters = -1;   // co-resident clusters of CG CTAs (one CTA per SM)
     if (per_sm_clusters < 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
         int n = cx->sm_count / CG;
         if (CG > 1) {
-            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * n);
-            q.blockDim = dim3(Cfg<TBN, CG>::THREADS);
+            q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
             q.dynamicSmemBytes = SMEM_BYTES;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             q.attrs = &at; q.numAttrs = 1;
             int m = 0;
-            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG>, &q) == cudaSuccess && m > 0) n = m;
+            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG, WA>, &q) == cudaSuccess && m > 0) n = m;
             cudaGetLastError();
         }
         per_sm_clusters = n;
@@ -1000,19 +1233,19 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            gemm_q88_kernel<TBN, CG><<<clusters, Cfg<TBN, CG>::THREADS, SMEM_BYTES, s>>>(ta, tb, g);
+            gemm_q88_kernel<TBN, CG, WA><<<clusters, Cfg<TBN, CG, WA>::THREADS, SMEM_BYTES, s>>>(ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * clusters);
-            q.blockDim = dim3(Cfg<TBN, CG>::THREADS);
+            q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
             q.dynamicSmemBytes = SMEM_BYTES;
             q.stream = s;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             q.attrs = &at; q.numAttrs = 1;
-            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG>, ta, tb, g);
+            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG, WA>, ta, tb, g);
         }
     }
     count_launch();
@@ -1097,6 +1330,25 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.rpl = p.rp.planes; g.rpl_plane = p.rp.plane_pitch;
     g.rpl_Hp = p.rp.Hp; g.rpl_Wp = p.rp.Wp; g.rpl_Cp = p.rp.Cp; g.rpl_pt = p.rp.pt; g.rpl_pl = p.rp.pl;
     g.po_Hp = p.po.Hp; g.po_Wp = p.po.Wp; g.po_Cp = p.po.Cp; g.po_pt = p.po.pt; g.po_pl = p.po.pl;
+    // Weights as A (one N = 256 MMA per step) for outputs written only as a plane image: its
+    // channel-major epilogue goes through a shared-memory transpose for the image, but the
+    // plain NCHW epilogue of the packed form is the cheaper one (ResNet-18 stem: 346 against
+    // 383 us; layer-1 plane outputs: 181 against 189 us).
+    if (p.b_packed && cx->gemm_wa && c.bw_log >= 3 && !(p.epi & 4u) && p.po.planes && !p.out) {
+        // the packed planes regrouped as weight rows
+        void* wr = nullptr;
+        rc = scratch_alloc(&wr, (size_t)p.K * 128, s);
+        if (rc) return rc;
+        {
+            ProfScope ps_(PK_SPLIT, s);
+            packed_to_rows_kernel<<<p.K / 128, 256, 0, s>>>(p.b_planes, p.K, (int8_t*)wr);
+        }
+        count_launch();
+        rc = make_wa_map(&tb, (const int8_t*)wr, p.K);
+        if (!rc) rc = launch_persistent<64, 1, true>(cx, ta, tb, g, s);
+        scratch_free(wr, s);
+        return rc;
+    }
     if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
     return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);
 }

@@ -168,6 +168,8 @@ int cm_init(const char* instance) {
     if (tmo && *tmo) c.timeout_ns = (uint64_t)strtoull(tmo, nullptr, 10) * 1000000ull;
     const char* gp = getenv("CM_GEMM_PAIRS");
     if (gp && *gp) c.gemm_pairs = atoi(gp) != 0;
+    const char* gw = getenv("CM_GEMM_WA");
+    if (gw && *gw) c.gemm_wa = atoi(gw) != 0;
     const char* dm = getenv("CM_DIRECT_MAX_MACS");
     if (dm && *dm) c.direct_max_macs = (uint64_t)strtoull(dm, nullptr, 10);
     g_ctx = c;

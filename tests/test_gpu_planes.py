@@ -184,6 +184,31 @@ def test_planes_fill_then_conv_and_residual(cm, port, N, C, H, W):
     assert_same(host(got), want, f"fill {N}x{C}x{H}x{W}")
 
 
+@pytest.mark.parametrize("C,M", [(64, 64), (32, 44)])
+@pytest.mark.parametrize("res", ["nchw", "planes"])
+def test_plane_only_output_with_residual(cm, port, C, M, res):
+    """A conv of at most 64 output channels whose output is only a plane image (the
+    weights-as-A GEMM form) with a fused residual Add + Relu, the residual as NCHW words
+    or as its own plane image: the image holds the reference sequence's words (read back
+    through an identity 1x1 conv, which also checks its channel sums)."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(C * 7 + M + len(res))
+    N, H, W = 2, 28, 28
+    g1 = geo(N, C, H, W, M, 3, 1, 1)
+    x = rand16(rng, N * C * H * W, -1024, 1024)
+    w1, b1 = weights(rng, g1)
+    r = rand16(rng, N * M * H * W, -4096, 4096)
+    want = oracle(port, x, w1, b1, g1, 3, r)
+    P = kernels.PlaneImage(N, M, H, W, kernels.conv_plane_frame(*geo(N, M, H, W, 64, 3, 1, 1)))
+    if res == "planes":
+        R = kernels.PlaneImage(N, M, H, W, (0, 0, 0, 0))
+        kernels.PlanesFill(R, dev(r))
+        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1, epilogue=3, resid=None, resid_planes=R)
+    else:
+        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1, epilogue=3, resid=dev(r))
+    assert_same(_identity_readback(kernels, P, N, M, H, W), want, f"plane-only output, {res} residual, M={M}")
+
+
 def _identity_readback(kernels, P, N, C, H, W):
     """The NCHW words of plane image P: a 1x1 conv with identity weights (1.0 = 256) reads it."""
     import torch
