@@ -813,6 +813,32 @@ bool plan_implicit(uint32_t C, uint32_t out_h, uint32_t out_w, uint32_t kh, uint
     return true;
 }
 
+// Tile shape (bw x bh x bn = 128 output pixels: columns, rows, images; powers of two) with
+// the fewest padded pixels over nimg images -- 16 x 8 for a 112-wide map, 8 x 8 x 2
+// images for 56, 1 x 1 x 128 images for 7 x 7 -- instead of bw = the width rounded up (a
+// 14 x 14 map in 16 x 8 tiles computes 31 % padding).  A tile's time goes by its K blocks
+// whatever its shape.  Ties go to the wider tile (coalesced output runs), then to the
+// taller one (fewer images: neighbouring rows share input rows in L2); a conv writing
+// NCHW words counts tiles narrower than 8 columns (scattered 2-byte stores) a quarter
+// dearer.  TMA box extents: bw*sw, bh*sh <= 256.
+void pick_tiles(uint32_t out_h, uint32_t out_w, uint32_t sh, uint32_t sw, uint64_t nimg, bool nchw_out,
+                uint32_t* bw_out, uint32_t* bh_out, uint32_t* bn_out) {
+    double best = -1.0;
+    for (uint32_t bw = 1; bw <= 128; bw *= 2) {
+        if (bw * sw > 256) break;
+        for (uint32_t bh = 1; bw * bh <= 128; bh *= 2) {
+            if (bh * sh > 256) break;
+            const uint32_t bn = 128 / (bw * bh);
+            double cost = (double)((out_w + bw - 1) / bw * bw) * (double)((out_h + bh - 1) / bh * bh) *
+                          (double)((nimg + bn - 1) / bn * bn);
+            if (nchw_out && bw < 8 && bw < out_w) cost *= 1.25;
+            if (best < 0 || cost < best || (cost == best && (bw > *bw_out || (bw == *bw_out && bh > *bh_out)))) {
+                best = cost; *bw_out = bw; *bh_out = bh; *bn_out = bn;
+            }
+        }
+    }
+}
+
 // ---- space-to-depth form of strided convolutions with few input channels -----
 // A conv with stride s in both directions equals a stride-1 conv over the input
 // regrouped into s x s blocks: virtual pixel (h', w') holds channels (th, tw, c) =
@@ -1301,8 +1327,10 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 }
                 rowterm_launch(cx, S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, nb, rt, s);
             }
+            uint32_t bw, bh, bn;
+            pick_tiles(out_h, out_w, stride_h, stride_w, nb, y != nullptr, &bw, &bh, &bn);
             ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
-                     out_h, out_w, log2u(ip.bw), log2u(ip.bh), log2u(ip.bn)};
+                     out_h, out_w, log2u(bw), log2u(bh), log2u(bn)};
             if (xv) {
                 // the plane image's own layout; boxes may read its whole frame past the plan's extent
                 ca.planes = xv->planes + ((uint64_t)dt * xv->Wp + dl) * xv->Cp;
@@ -1402,8 +1430,10 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 }
                 rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
             }
+            uint32_t bw, bh, bn;
+            pick_tiles(out_h, out_w, 1, 1, nb, y != nullptr, &bw, &bh, &bn);
             const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh3, 1, 1, sp.T,
-                           out_h, out_w, log2u(vp.bw), log2u(vp.bh), log2u(vp.bn)};
+                           out_h, out_w, log2u(bw), log2u(bh), log2u(bn)};
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, vp.Kt, vp.Kt, M_pad, rt, ct,
                        y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
