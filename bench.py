@@ -459,7 +459,9 @@ class NetworkBench:
                                  if ONE_LAUNCH else "whole call list captured once as a CUDA graph and replayed")}
         return {"workload": "resnet18-shaped (BASELINE configs[3])", "batch": 256,
                 "input": "256x3x224x224 uniform [0,1)", "macs_per_image": self.net.macs_per_image, "calls": calls,
-                "parallelism": f"batch-sharded over {world} GPU(s)", "l2": "inputs larger than L2 (77 MB input, 1.1 GB activations)"}
+                "parallelism": f"batch-sharded over {world} GPU(s)", "l2": "inputs larger than L2 (77 MB input, 1.1 GB activations)",
+                "launches": ("whole call list captured once as a CUDA graph and replayed" if GRAPH
+                             else "one launch per kernel from the host")}
 
     def setup(self):
         import torch
@@ -467,22 +469,46 @@ class NetworkBench:
         self.x = networks.make_input(self.net)
         self.bufs = networks.gpu_buffers(self.net, self.x)
         self.graph = None
-        if self.which == "lenet":
-            import cormorant_b200 as cm
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                for _ in range(3):            # warm: module loading and attribute setup happen outside capture
-                    networks.execute(self.net, networks.GpuBackend(s, one_launch=ONE_LAUNCH), self.bufs)
-            torch.cuda.current_stream().wait_stream(s)
-            torch.cuda.synchronize()
-            l0 = cm.launch_count()
-            self.graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(self.graph):
-                networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH),
-                                 self.bufs)
-            self.launches_per_step = cm.launch_count() - l0
-            torch.cuda.synchronize()
+        if GRAPH and self.local > 0:
+            self.graph, self.launches_per_step = self._capture(self.bufs)
+
+    def _capture(self, bufs):
+        """The whole call list captured once as a CUDA graph (its scratch allocations become
+        graph memory nodes); returns (graph, kernel launches per replay)."""
+        import torch
+        import cormorant_b200 as cm
+        from cormorant_b200 import networks
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):            # warm: module loading and attribute setup happen outside capture
+                networks.execute(self.net, networks.GpuBackend(s, one_launch=ONE_LAUNCH), bufs)
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        l0 = cm.launch_count()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH), bufs)
+        n = cm.launch_count() - l0
+        torch.cuda.synchronize()
+        return g, n
+
+    def profile_dominant(self, cm, stream, iters):
+        """Device time (ms) and launch count of the GEMM kernel over `iters` eager passes, from
+        CUDA events around each launch (a graph replay carries no per-launch events)."""
+        import ctypes as C
+        import torch
+        from cormorant_b200 import networks
+        L = cm.lib()
+        torch.cuda.synchronize()
+        L.cm_profile_begin()
+        for _ in range(iters):
+            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+        torch.cuda.synchronize()
+        L.cm_profile_end()
+        ms, cnt = C.c_double(), C.c_uint64()
+        L.cm_profile_read(self.dominant.encode(), C.byref(ms), C.byref(cnt))
+        return ms.value, cnt.value
 
     def step(self, cm, stream):
         from cormorant_b200 import networks
@@ -534,6 +560,14 @@ class NetworkBench:
             self.consumed = [None, None]
             self.e2e_i = 0
             self.e2e_path += "; the next step's input copy overlaps this step's compute (copy stream, two input buffers)"
+            self.e2e_graphs = None
+            if GRAPH:
+                # one graph of the call list per input buffer; the copies stay outside the graphs
+                self.e2e_graphs = []
+                for b in range(2):
+                    self.bufs[self.net.input] = self.xbufs[b]
+                    self.e2e_graphs.append(self._capture(self.bufs)[0])
+                self.e2e_path += "; the call list replayed as a CUDA graph (one per input buffer)"
         if self.which == "lenet":
             self.e2e_path += "; captured once as a CUDA graph and replayed per image"
             # batch 1 is host-launch-bound: the whole step (pinned H2D copy, the call
@@ -585,7 +619,10 @@ class NetworkBench:
         cur = torch.cuda.current_stream()
         cur.wait_event(self.copied[b])
         self.bufs[self.net.input] = self.xbufs[b]
-        networks.execute(self.net, networks.GpuBackend(cur), self.bufs)
+        if self.e2e_graphs is not None:
+            self.e2e_graphs[b].replay()
+        else:
+            networks.execute(self.net, networks.GpuBackend(cur), self.bufs)
         ev = torch.cuda.Event()
         ev.record(cur)
         self.consumed[b] = ev
@@ -594,6 +631,7 @@ class NetworkBench:
 
     def e2e_release(self):
         self.e2e_graph = None
+        self.e2e_graphs = None
         self.bufs = None
 
 
@@ -601,6 +639,7 @@ UNFUSED = False      # --unfused: networks run node by node
 FUSE_RESIDUAL = True   # --no-fuse-residual: fold Conv->Relu only
 PLANES = True          # --no-planes: every conv splits its own input
 ONE_LAUNCH = False     # --one-launch: lenet's whole call list as one cm_calls launch (slower on B200)
+GRAPH = True           # --no-graph: the network configs launch every kernel from the host each step
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -773,13 +812,16 @@ def main():
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
     ap.add_argument("--one-launch", action="store_true",
                     help="lenet: the whole call list in one single-CTA launch (cm_calls) instead of one launch per call")
+    ap.add_argument("--no-graph", action="store_true",
+                    help="network configs: launch every kernel from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-planes", action="store_true",
                     help="resnet: no plane images between convs (each conv splits its NCHW input)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
     args = ap.parse_args()
-    global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH
+    global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH, GRAPH
     UNFUSED = args.unfused
+    GRAPH = not args.no_graph
     FUSE_RESIDUAL = not args.no_fuse_residual
     PLANES = not args.no_planes
     ONE_LAUNCH = args.one_launch
@@ -888,6 +930,13 @@ def main():
     import ctypes as C
     dms, dcnt = C.c_double(), C.c_uint64()
     L.cm_profile_read(wl.dominant.encode(), C.byref(dms), C.byref(dcnt))
+    dom_note = ""
+    if getattr(wl, "graph", None) is not None and wl.dominant == "gemm_q88":
+        # graph replays carry no per-launch events: the GEMM's launch durations come from K
+        # eager passes right after the timed region
+        dms.value, dcnt.value = wl.profile_dominant(cm, stream, K)
+        dom_note = ("; GEMM launch durations from CUDA events around each launch over K eager passes right "
+                    "after the timed region (which replays a CUDA graph)")
     dom_ms = max_over_ranks(dms.value)
     elapsed_ms = max_over_ranks(elapsed_ms)
     ms_per_step = elapsed_ms / K
@@ -916,7 +965,7 @@ def main():
                          f"2 x {peaks['source']} bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} "
                          f"{peaks[which]} TF/s (dense int8 rate is twice bf16 on B200); traffic = DRAM bytes of "
                          + ("one 4096^3 x 64 launch" if args.config == "matmul" else "one layer-1 3x3 conv GEMM launch")
-                         + " (ncu, profiles/)")}
+                         + " (ncu, profiles/)" + dom_note)}
     else:
         achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e9 if dms.value > 0 else 0.0
         peak = peaks["hbm_gbs"]
