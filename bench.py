@@ -468,9 +468,15 @@ class NetworkBench:
         from cormorant_b200 import networks
         self.x = networks.make_input(self.net)
         self.bufs = networks.gpu_buffers(self.net, self.x)
+        # the network's conv weights prepared once (constants of the call list)
+        self.wcache = networks.prepare_weights(self.net, self.bufs) if PREPARED and self.local > 0 else {}
         self.graph = None
         if GRAPH and self.local > 0:
             self.graph, self.launches_per_step = self._capture(self.bufs)
+
+    def _backend(self, stream):
+        from cormorant_b200 import networks
+        return networks.GpuBackend(stream, one_launch=ONE_LAUNCH, weights=self.wcache)
 
     def _capture(self, bufs):
         """The whole call list captured once as a CUDA graph (its scratch allocations become
@@ -482,13 +488,13 @@ class NetworkBench:
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
             for _ in range(3):            # warm: module loading and attribute setup happen outside capture
-                networks.execute(self.net, networks.GpuBackend(s, one_launch=ONE_LAUNCH), bufs)
+                networks.execute(self.net, self._backend(s), bufs)
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
         l0 = cm.launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH), bufs)
+            networks.execute(self.net, self._backend(torch.cuda.current_stream()), bufs)
         n = cm.launch_count() - l0
         torch.cuda.synchronize()
         return g, n
@@ -503,7 +509,7 @@ class NetworkBench:
         torch.cuda.synchronize()
         L.cm_profile_begin()
         for _ in range(iters):
-            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+            networks.execute(self.net, self._backend(stream), self.bufs)
         torch.cuda.synchronize()
         L.cm_profile_end()
         ms, cnt = C.c_double(), C.c_uint64()
@@ -515,7 +521,7 @@ class NetworkBench:
         if self.graph is not None:
             self.graph.replay()
         elif self.local > 0:
-            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+            networks.execute(self.net, self._backend(stream), self.bufs)
 
     def per_part(self, cm, stream, iters):
         import ctypes as C
@@ -524,7 +530,7 @@ class NetworkBench:
         L = cm.lib()
         L.cm_profile_begin()
         for _ in range(iters):
-            networks.execute(self.net, networks.GpuBackend(stream), self.bufs)
+            networks.execute(self.net, self._backend(stream), self.bufs)
         torch.cuda.synchronize()
         L.cm_profile_end()
         out = {}
@@ -537,11 +543,13 @@ class NetworkBench:
     def release(self):
         self.bufs = None
         self.graph = None
+        self.wcache = {}
 
     def e2e_setup(self):
         import torch
         from cormorant_b200 import networks
         self.bufs = networks.gpu_buffers(self.net)
+        self.wcache = networks.prepare_weights(self.net, self.bufs) if PREPARED else {}
         self.hx = torch.from_numpy(self.x.copy()).pin_memory()
         out_words = self.net.buffers[self.net.resolve(self.net.output)]
         self.hy = torch.empty(out_words, dtype=torch.int16).pin_memory()
@@ -584,7 +592,7 @@ class NetworkBench:
         import torch
         from cormorant_b200 import networks
         self.bufs[self.net.input].copy_(self.hx, non_blocking=True)
-        networks.execute(self.net, networks.GpuBackend(torch.cuda.current_stream(), one_launch=ONE_LAUNCH), self.bufs)
+        networks.execute(self.net, self._backend(torch.cuda.current_stream()), self.bufs)
         self.hy.copy_(self.bufs[self.net.resolve(self.net.output)], non_blocking=True)
 
     def e2e_step(self):
@@ -622,7 +630,7 @@ class NetworkBench:
         if self.e2e_graphs is not None:
             self.e2e_graphs[b].replay()
         else:
-            networks.execute(self.net, networks.GpuBackend(cur), self.bufs)
+            networks.execute(self.net, self._backend(cur), self.bufs)
         ev = torch.cuda.Event()
         ev.record(cur)
         self.consumed[b] = ev
@@ -633,6 +641,7 @@ class NetworkBench:
         self.e2e_graph = None
         self.e2e_graphs = None
         self.bufs = None
+        self.wcache = {}
 
 
 UNFUSED = False      # --unfused: networks run node by node
@@ -640,6 +649,7 @@ FUSE_RESIDUAL = True   # --no-fuse-residual: fold Conv->Relu only
 PLANES = True          # --no-planes: every conv splits its own input
 ONE_LAUNCH = False     # --one-launch: lenet's whole call list as one cm_calls launch (slower on B200)
 GRAPH = True           # --no-graph: the network configs launch every kernel from the host each step
+PREPARED = True        # --no-prepared: every conv call prepares its weight planes again
 
 WORKLOADS = {"matmul": MatmulSweep, "vectorop": VectorOPSweep, "pool": PoolSweep,
              "lenet": lambda r, w: NetworkBench(r, w, "lenet"), "resnet": lambda r, w: NetworkBench(r, w, "resnet")}
@@ -812,6 +822,8 @@ def main():
                     help="lenet/resnet: run the reference call list node by node (no Conv->Relu/Add folding)")
     ap.add_argument("--one-launch", action="store_true",
                     help="lenet: the whole call list in one single-CTA launch (cm_calls) instead of one launch per call")
+    ap.add_argument("--no-prepared", action="store_true",
+                    help="network configs: prepare the conv weight planes in every call instead of once")
     ap.add_argument("--no-graph", action="store_true",
                     help="network configs: launch every kernel from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-planes", action="store_true",
@@ -819,9 +831,10 @@ def main():
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
     args = ap.parse_args()
-    global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH, GRAPH
+    global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH, GRAPH, PREPARED
     UNFUSED = args.unfused
     GRAPH = not args.no_graph
+    PREPARED = not args.no_prepared
     FUSE_RESIDUAL = not args.no_fuse_residual
     PLANES = not args.no_planes
     ONE_LAUNCH = args.one_launch
@@ -983,7 +996,7 @@ def main():
         wl.e2e_step()                      # warm-up pass
         torch.cuda.synchronize()
         barrier()
-        e_steps = K if args.config == "lenet" else max(1, min(K, 3))
+        e_steps = K if args.config in ("lenet", "resnet") else max(1, min(K, 3))
         es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         es.record()
         if hasattr(wl, "e2e_start"):

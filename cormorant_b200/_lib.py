@@ -57,6 +57,10 @@ SIGNATURES: dict[str, tuple] = {
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),
+    "cm_conv_weights_create": (C.c_int, [_p, _p] + [_u] * 17 + [C.POINTER(_p)]),
+    "cm_conv_weights_destroy": (None, [_p]),
+    "cm_conv_prepared": (C.c_int, [_p] * 5 + [_u, _p, _p]),
+    "cm_conv_prepared_async": (C.c_int, [_p] * 5 + [_u, _p, _p, _p]),
     "cm_calls_supported": (C.c_int, [_p, _u]),
     "cm_calls": (C.c_int, [_p, _u]),
     "cm_calls_async": (C.c_int, [_p, _u, _p]),

@@ -1179,16 +1179,49 @@ PlaneOut plane_out(cm_planes* yp, uint64_t n0) {
     return o;
 }
 
+// The space-to-depth plan conv_core uses: row stacking where the row-staged split kernel
+// serves it and it saves K blocks.
+bool choose_s2d(uint32_t in_ch, uint32_t in_w, uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw, uint32_t sh,
+                uint32_t sw, uint32_t dh, uint32_t dw, S2dPlan* sp) {
+    if (!plan_s2d(in_ch, out_h, out_w, kh, kw, sh, sw, dh, dw, sp)) return false;
+    S2dPlan sp2;
+    if (sh == 2 && in_ch == 3 && 4ull * in_ch * in_w * 2 <= kS2dRowSmem &&
+        plan_s2d(in_ch, out_h, out_w, kh, kw, sh, sw, dh, dw, &sp2, 2) &&
+        sp2.kh3 * (sp2.ip.KR_pad / 128) < sp->kh3 * (sp->ip.KR_pad / 128))
+        *sp = sp2;
+    return true;
+}
+
+}  // namespace
+
+// Conv weights prepared once (cm_conv_weights_create): the weight planes and column terms
+// the tensor-core paths read, built for one geometry, so calls with constant weights skip
+// the per-call preparation.
+struct cm_conv_weights {
+    const int16_t* weight = nullptr;
+    const int16_t* bias = nullptr;
+    unsigned g[17] = {};               // batch .. is_depthwise, as the conv entry points take them
+    int path = -1;                     // cm::ConvPath the planes were built for
+    int8_t* planes = nullptr;          // conv_weights layout of that path
+    int32_t* colterm = nullptr;
+    int8_t* rows = nullptr;            // <= 64 channels: the weights-as-A rows [128][Kt]
+    void* mem = nullptr;
+    int device = -1;
+};
+
+namespace {
+
 // xv: a plane image that fits this conv's implicit plan (read instead of x); po:
 // the output's plane image, written by the GEMM epilogue (implicit / space-to-depth
 // paths only; y may then be null); rp: the residual's plane image (same paths; resid
 // may then be null).
+// pw: prepared weight planes and column terms of this geometry's path (null: built here).
 int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, const int16_t* bias, int16_t* y,
               cm_planes* po, const cm_planes* rp, unsigned batch, unsigned in_ch,
               unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,
               unsigned stride_h, unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
               unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epi, const int16_t* resid,
-              cm_stream_t stream) {
+              cm_stream_t stream, const cm_conv_weights* pw = nullptr) {
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
@@ -1254,21 +1287,23 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         if (chunk == 0) chunk = 1;
         if (chunk > batch || xv) chunk = batch;           // a plane image holds every image already
         if (chunk > (1u << 24)) chunk = 1u << 24;
-        const uint64_t w_bytes = ((uint64_t)ip.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
-        const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+        // prepared weights (pw) replace the per-call weight planes and column terms
+        const uint64_t w_bytes = pw ? 0 : ((uint64_t)ip.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+        const uint64_t ct_bytes = pw ? 0 : ((uint64_t)out_ch * 4 + 255) & ~255ull;
         const uint64_t a_bytes = xv ? 0 : (2 * chunk * img_plane + ip.KR + 256 + 255) & ~255ull;   // + slack past the last pixel
         const uint64_t s_bytes = xv ? 0 : (chunk * ip.Hp * ip.Wp * 4 + 255) & ~255ull;
         const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
         void* scratch = nullptr;
         rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + s_bytes + rt_bytes, s);
         if (rc) return rc;
-        int8_t* wpl = (int8_t*)scratch;
-        int32_t* ct = (int32_t*)(wpl + w_bytes);
-        int8_t* apl = (int8_t*)ct + ct_bytes;
+        int8_t* wpl = pw ? pw->planes : (int8_t*)scratch;
+        int32_t* ct = pw ? pw->colterm : (int32_t*)((int8_t*)scratch + w_bytes);
+        int8_t* apl = (int8_t*)scratch + w_bytes + ct_bytes;
         int32_t* S = (int32_t*)(apl + a_bytes);
         int32_t* rt = (int32_t*)((int8_t*)S + s_bytes);
-        rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch, w_plane,
-                          w_bytes, wpl, ct, s);
+        if (!pw)
+            rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch,
+                              w_plane, w_bytes, wpl, ct, s);
         if (!rc && po) rc = planes_reset(po, s);
         // a plane image read in place: the conv's padded window starts (dt, dl) into its frame
         const uint32_t dt = xv ? xv->pt - pad_top : 0u, dl = xv ? xv->pl - pad_left : 0u;
@@ -1343,6 +1378,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                        y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
+            p.wa_rows = pw ? pw->rows : nullptr;
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
             if (po) p.po = plane_out(po, n0);
@@ -1356,13 +1392,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     }
 
     S2dPlan sp;
-    if (plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp)) {
-        // row stacking where the row-staged split kernel serves it and it saves K blocks
-        S2dPlan sp2;
-        if (stride_h == 2 && in_ch == 3 && 4ull * in_ch * in_w * 2 <= kS2dRowSmem &&
-            plan_s2d(in_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp2, 2) &&
-            sp2.kh3 * (sp2.ip.KR_pad / 128) < sp.kh3 * (sp.ip.KR_pad / 128))
-            sp = sp2;
+    if (choose_s2d(in_ch, in_w, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp)) {
         const ImplicitPlan& vp = sp.ip;
         const uint32_t M_pad = pad_c(out_ch);
         const bool packed = out_ch <= 64;
@@ -1374,23 +1404,23 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         if (chunk == 0) chunk = 1;
         if (chunk > batch) chunk = batch;
         if (chunk > (1u << 24)) chunk = 1u << 24;
-        const uint64_t w_bytes = ((uint64_t)vp.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
-        const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+        const uint64_t w_bytes = pw ? 0 : ((uint64_t)vp.Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+        const uint64_t ct_bytes = pw ? 0 : ((uint64_t)out_ch * 4 + 255) & ~255ull;
         const uint64_t a_bytes = (2 * chunk * img_plane + vp.KR + 256 + 255) & ~255ull;
         const uint64_t s_bytes = (chunk * img_so * 4 + 255) & ~255ull;
         const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
         void* scratch = nullptr;
         rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + s_bytes + rt_bytes, s);
         if (rc) return rc;
-        int8_t* wpl = (int8_t*)scratch;
-        int32_t* ct = (int32_t*)(wpl + w_bytes);
-        int8_t* apl = (int8_t*)ct + ct_bytes;
+        int8_t* wpl = pw ? pw->planes : (int8_t*)scratch;
+        int32_t* ct = pw ? pw->colterm : (int32_t*)((int8_t*)scratch + w_bytes);
+        int8_t* apl = (int8_t*)scratch + w_bytes + ct_bytes;
         int32_t* So = (int32_t*)(apl + a_bytes);
         int32_t* rt = (int32_t*)((int8_t*)So + s_bytes);
         // column terms from the original weights (real taps, bias), planes of the virtual kernel
-        rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, 0, 0, 0, 0, 0, nullptr, ct, s);
+        if (!pw) rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, 0, 0, 0, 0, 0, nullptr, ct, s);
         if (!rc && po) rc = planes_reset(po, s);
-        if (!rc) {
+        if (!rc && !pw) {
             ProfScope ps_(PK_SPLIT, s);
             const uint64_t wtot = (uint64_t)vp.Kt * out_ch;
             conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
@@ -1438,6 +1468,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                        y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
+            p.wa_rows = pw ? pw->rows : nullptr;
             p.epi = epi;
             p.resid = resid ? resid + n0 * (uint64_t)out_ch * P : nullptr;
             if (po) p.po = plane_out(po, n0);
@@ -1461,20 +1492,22 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     if (chunk == 0) chunk = 1;
     if (chunk > batch) chunk = batch;
     if (chunk * P >= (1ull << 31)) chunk = ((1ull << 31) - 1) / P;
-    const uint64_t w_bytes = ((uint64_t)K * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
-    const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+    const uint64_t w_bytes = pw ? 0 : ((uint64_t)K * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+    const uint64_t ct_bytes = pw ? 0 : ((uint64_t)out_ch * 4 + 255) & ~255ull;
     const uint64_t a_bytes = (chunk * per_img + 255) & ~255ull;
     const uint64_t rt_bytes = (chunk * P * 4 + 255) & ~255ull;
     void* scratch = nullptr;
     rc = scratch_alloc(&scratch, w_bytes + ct_bytes + a_bytes + rt_bytes, s);
     if (rc) return rc;
-    int8_t* wpl = (int8_t*)scratch;
-    int32_t* ct = (int32_t*)(wpl + w_bytes);
-    int8_t* apl = (int8_t*)ct + ct_bytes;
+    int8_t* wpl = pw ? pw->planes : (int8_t*)scratch;
+    int32_t* ct = pw ? pw->colterm : (int32_t*)((int8_t*)scratch + w_bytes);
+    int8_t* apl = (int8_t*)scratch + w_bytes + ct_bytes;
     int32_t* rt = (int32_t*)(apl + a_bytes);
 
     // natural tap order: kh = kw = 1, C = Cp = KR_pad = K
-    rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, K, 1, 1, K, K, w_pitch, w_plane, w_bytes, wpl, ct, s);
+    if (!pw)
+        rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, K, 1, 1, K, K, w_pitch, w_plane, w_bytes, wpl, ct,
+                          s);
     const ConvGeom geo{in_ch, in_h, in_w, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left};
     // shared-memory window im2col when one block's window (C x kh rows x the columns
     // 128 pixels span) fits; the direct gather otherwise
@@ -1528,12 +1561,13 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
               cm_planes* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
               unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
               unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
-              unsigned is_depthwise, unsigned epi, const int16_t* resid, const cm_planes* rp, cm_stream_t stream) {
+              unsigned is_depthwise, unsigned epi, const int16_t* resid, const cm_planes* rp, cm_stream_t stream,
+              const cm_conv_weights* pw = nullptr) {
     if (!(epi & 2u)) rp = nullptr;
     if (!xp && !yp && !rp)
         return conv_core(x, nullptr, weight, bias, y, nullptr, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                          stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi,
-                         resid, stream);
+                         resid, stream, pw);
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
@@ -1560,7 +1594,7 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
     if (!yp || epi_writes)
         return conv_core(x, xv, weight, bias, y, epi_writes ? yp : nullptr, rv, batch, in_ch, in_h, in_w, out_ch, out_h,
                          out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias,
-                         is_depthwise, epi, resid, stream);
+                         is_depthwise, epi, resid, stream, pw);
     cudaStream_t s = (cudaStream_t)stream;
     int16_t* yw = y;
     void* tmp = nullptr;
@@ -1570,7 +1604,7 @@ int conv_impl(const int16_t* x, const cm_planes* xp, const int16_t* weight, cons
         yw = (int16_t*)tmp;
     }
     rc = conv_core(x, xv, weight, bias, yw, nullptr, rv, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
-                   stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi, resid, stream);
+                   stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epi, resid, stream, pw);
     if (!rc) rc = planes_from_tensor(cx, yw, yp, s);
     if (tmp) scratch_free(tmp, s);
     return rc;
@@ -1779,5 +1813,132 @@ extern "C" int cm_pool_planes(const cm_planes_t* xp, cm_planes_t* yp, unsigned b
     int rc = cm_pool_planes_async(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
                                   stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad,
                                   nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
+// ---------------------------------------------------------------------------
+// Prepared conv weights (no reference counterpart): the tensor-core paths' weight planes,
+// column terms and weights-as-A rows built once for one geometry.
+// ---------------------------------------------------------------------------
+extern "C" int cm_conv_weights_create(const int16_t* weight, const int16_t* bias, unsigned batch, unsigned in_ch,
+                                      unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w,
+                                      unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
+                                      unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
+                                      unsigned has_bias, unsigned is_depthwise, cm_conv_weights_t** out) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!out) return set_error(CM_EINVAL, "cm_conv_weights_create: null result pointer");
+    *out = nullptr;
+    if (has_bias && !bias) return set_error(CM_EINVAL, "cm_conv_weights_create: null bias");
+    const uint64_t K64 = (uint64_t)in_ch * kh * kw;
+    if (K64 > 0 && !weight) return set_error(CM_EINVAL, "cm_conv_weights_create: null weight");
+    cm_conv_weights* w = new (std::nothrow) cm_conv_weights;
+    if (!w) return set_error(CM_ENOMEM, "cm_conv_weights_create: out of host memory");
+    w->weight = weight;
+    w->bias = has_bias ? bias : nullptr;
+    const unsigned g[17] = {batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                            dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise};
+    std::copy(g, g + 17, w->g);
+    w->device = cx->device;
+    ImplicitPlan ip;
+    const ConvPath path = (batch == 0 || out_ch == 0 || (uint64_t)out_h * out_w == 0)
+                              ? CP_BIAS_FILL
+                              : conv_path(cx->direct_max_macs, batch, in_ch, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                                          dilation_h, dilation_w, is_depthwise, &ip);
+    w->path = (int)path;
+    const uint32_t M_pad = pad_c(out_ch);
+    const bool packed = out_ch <= 64;
+    uint32_t Kt = 0;
+    S2dPlan sp;
+    if (path == CP_IMPLICIT) Kt = ip.Kt;
+    else if (path == CP_S2D && choose_s2d(in_ch, in_w, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, &sp))
+        Kt = sp.ip.Kt;
+    else if (path == CP_EXPLICIT) Kt = (uint32_t)K64;
+    if (Kt == 0) {                  // nothing to prepare on this path: calls read weight and bias
+        w->path = path == CP_S2D ? -1 : (int)path;
+        *out = w;
+        return CM_OK;
+    }
+    const uint64_t w_bytes = ((uint64_t)Kt * (packed ? 128 : 2 * M_pad) + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)out_ch * 4 + 255) & ~255ull;
+    const bool rows = packed && path != CP_EXPLICIT;      // the weights-as-A form is a conv-mode GEMM
+    const uint64_t r_bytes = rows ? ((uint64_t)Kt * 128 + 255) & ~255ull : 0;
+    cudaError_t e = cudaMalloc(&w->mem, w_bytes + ct_bytes + r_bytes);
+    if (e != cudaSuccess) { delete w; return cuda_error(e, "cm_conv_weights_create: cudaMalloc"); }
+    w->planes = (int8_t*)w->mem;
+    w->colterm = (int32_t*)((int8_t*)w->mem + w_bytes);
+    w->rows = rows ? (int8_t*)w->mem + w_bytes + ct_bytes : nullptr;
+    cudaStream_t s = nullptr;
+    const uint32_t w_pitch = packed ? 128u : M_pad;
+    if (path == CP_IMPLICIT) {
+        rc = conv_weights(cx, weight, w->bias, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch,
+                          packed ? 64u : (uint64_t)Kt * M_pad, w_bytes, w->planes, w->colterm, s);
+    } else if (path == CP_S2D) {
+        rc = conv_weights(cx, weight, w->bias, out_ch, in_ch, kh, kw, 0, 0, 0, 0, 0, nullptr, w->colterm, s);
+        if (!rc) {
+            const ImplicitPlan& vp = sp.ip;
+            const uint64_t wtot = (uint64_t)Kt * out_ch;
+            conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
+                                                                              vp.Cp, vp.KR_pad, Kt, w_pitch,
+                                                                              packed ? 64u : (uint64_t)Kt * M_pad, w->planes,
+                                                                              sp.T);
+            count_launch();
+        }
+    } else {
+        rc = conv_weights(cx, weight, w->bias, out_ch, (uint32_t)K64, 1, 1, (uint32_t)K64, (uint32_t)K64, w_pitch,
+                          packed ? 64u : (uint64_t)Kt * M_pad, w_bytes, w->planes, w->colterm, s);
+    }
+    if (!rc && rows) rc = weights_to_rows(cx, w->planes, Kt, w->rows, s);
+    if (!rc) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) rc = cuda_error(e, "cm_conv_weights_create");
+    }
+    if (rc) {
+        cudaFree(w->mem);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return CM_OK;
+}
+
+extern "C" void cm_conv_weights_destroy(cm_conv_weights_t* w) {
+    if (!w) return;
+    if (w->mem) {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (w->device >= 0 && cur != w->device) cudaSetDevice(w->device);
+        cudaFree(w->mem);
+        if (cur >= 0 && cur != w->device) cudaSetDevice(cur);
+    }
+    delete w;
+}
+
+extern "C" int cm_conv_prepared_async(const cm_conv_weights_t* w, const int16_t* x, const cm_planes_t* xp, int16_t* y,
+                                      cm_planes_t* yp, unsigned epilogue, const int16_t* resid,
+                                      const cm_planes_t* resid_planes, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!w) return set_error(CM_EINVAL, "cm_conv_prepared: null prepared weights");
+    if (w->device != cx->device) return set_error(CM_EINVAL, "cm_conv_prepared: weights prepared on another device");
+    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_prepared: epilogue %u (0..3)", epilogue);
+    const unsigned* g = w->g;
+    // the planes serve only the path they were built for (the direct-path limit may have
+    // changed since); otherwise this call prepares its own from weight and bias
+    ImplicitPlan ip;
+    const ConvPath path = (g[0] == 0 || g[4] == 0 || (uint64_t)g[5] * g[6] == 0)
+                              ? CP_BIAS_FILL
+                              : conv_path(cx->direct_max_macs, g[0], g[1], g[4], g[5], g[6], g[7], g[8], g[9], g[10], g[11],
+                                          g[12], g[16], &ip);
+    const cm_conv_weights* pw = (w->planes && (int)path == w->path) ? w : nullptr;
+    return conv_impl(x, xp, w->weight, w->bias, y, yp, g[0], g[1], g[2], g[3], g[4], g[5], g[6], g[7], g[8], g[9], g[10],
+                     g[11], g[12], g[13], g[14], g[15], g[16], epilogue, resid, resid_planes, stream, pw);
+}
+
+extern "C" int cm_conv_prepared(const cm_conv_weights_t* w, const int16_t* x, const cm_planes_t* xp, int16_t* y,
+                                cm_planes_t* yp, unsigned epilogue, const int16_t* resid, const cm_planes_t* resid_planes) {
+    int rc = cm_conv_prepared_async(w, x, xp, y, yp, epilogue, resid, resid_planes, nullptr);
     return rc ? rc : finish_sync(nullptr);
 }

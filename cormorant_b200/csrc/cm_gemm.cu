@@ -1335,22 +1335,32 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     // plain NCHW epilogue of the packed form is the cheaper one (ResNet-18 stem: 346 against
     // 383 us; layer-1 plane outputs: 181 against 189 us).
     if (p.b_packed && cx->gemm_wa && c.bw_log >= 3 && !(p.epi & 4u) && p.po.planes && !p.out) {
-        // the packed planes regrouped as weight rows
+        // the packed planes regrouped as weight rows (prepared already, or here)
         void* wr = nullptr;
-        rc = scratch_alloc(&wr, (size_t)p.K * 128, s);
-        if (rc) return rc;
-        {
-            ProfScope ps_(PK_SPLIT, s);
-            packed_to_rows_kernel<<<p.K / 128, 256, 0, s>>>(p.b_planes, p.K, (int8_t*)wr);
+        if (!p.wa_rows) {
+            rc = scratch_alloc(&wr, (size_t)p.K * 128, s);
+            if (rc) return rc;
+            rc = weights_to_rows(cx, p.b_planes, p.K, (int8_t*)wr, s);
         }
-        count_launch();
-        rc = make_wa_map(&tb, (const int8_t*)wr, p.K);
+        if (!rc) rc = make_wa_map(&tb, p.wa_rows ? p.wa_rows : (const int8_t*)wr, p.K);
         if (!rc) rc = launch_persistent<64, 1, true>(cx, ta, tb, g, s);
-        scratch_free(wr, s);
+        if (wr) scratch_free(wr, s);
         return rc;
     }
     if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
     return pairs ? launch_persistent<128, 2>(cx, ta, tb, g, s) : launch_persistent<128, 1>(cx, ta, tb, g, s);
+}
+
+int weights_to_rows(const Context* cx, const int8_t* packed, uint32_t Kt, int8_t* rows, cudaStream_t s) {
+    (void)cx;
+    if (Kt == 0 || Kt % 128 != 0) return set_error(CM_EINVAL, "weight rows: K = %u", Kt);
+    {
+        ProfScope ps_(PK_SPLIT, s);
+        packed_to_rows_kernel<<<Kt / 128, 256, 0, s>>>(packed, Kt, rows);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "weight rows");
 }
 
 int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld, uint32_t rows, uint32_t K,

@@ -63,6 +63,8 @@ struct GemmPlan {
     // B planes packed for one 64-column tile: [b_batches][K][128] int8, each K row
     // = [64 hi | 64 lo] (cols <= 64; C_pad unused).
     uint32_t b_packed = 0;
+    // packed B already regrouped as weights-as-A rows [128][K] (prepared weights), or null
+    const int8_t* wa_rows = nullptr;
     // rows_per_img != 0 (plain mode): row = n*rows_per_img + p is written to
     // out[n*out_bs + p + col*ldc] (conv output pixels of several images, NCHW)
     uint32_t rows_per_img = 0;
@@ -84,6 +86,10 @@ inline uint32_t pad_c(uint32_t C) { return (C + 15u) & ~15u; }
 // Launch the tcgen05 GEMM (all arguments device-resident, stream-ordered).
 int gemm_launch(const Context* cx, const GemmPlan& g, cudaStream_t s);
 int gemm_launch_conv(const Context* cx, const GemmPlan& g, cudaStream_t s);
+
+// Packed weight planes [Kt][64 hi | 64 lo] -> weights-as-A rows [128][Kt] (row 2m + p =
+// byte p*64 + m of every K row); Kt a multiple of 128.
+int weights_to_rows(const Context* cx, const int8_t* packed, uint32_t Kt, int8_t* rows, cudaStream_t s);
 
 // Split int16 rows into hi/lo planes + row terms:
 //   element (bt, r, k) = src[bt*src_bs + r*ld + k], r < rows, k < K, bt < nbt;

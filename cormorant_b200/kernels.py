@@ -220,6 +220,46 @@ def ConvKernelPlanes(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_c
     check(L.cm_conv_planes(*args) if stream is None else L.cm_conv_planes_async(*args, _stream(stream)))
 
 
+class ConvWeights:
+    """Conv weights prepared once for one call geometry (cm_conv_weights_create): the
+    weight planes and column terms the tensor-core paths read, so repeated calls with
+    constant weights (a network's parameters) skip that preparation.  `weight` and `bias`
+    must keep the values they had at creation and stay allocated.  Not a reference
+    object."""
+
+    def __init__(self, weight, bias, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1,
+                 dilation_h=1, dilation_w=1, pad_top=0, pad_left=0, has_bias=None, is_depthwise=0):
+        import ctypes as C
+        if has_bias is None:
+            has_bias = int(bias is not None)
+        self.geometry = (batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h,
+                         dilation_w, pad_top, pad_left, int(has_bias), int(is_depthwise))
+        self._keep = (weight, bias)            # the buffers the prepared calls still read
+        out = C.c_void_p()
+        self.ptr = None
+        check(lib().cm_conv_weights_create(_addr(weight), _addr(bias), *self.geometry, C.byref(out)))
+        self.ptr = out.value
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            lib().cm_conv_weights_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def ConvKernelPrepared(w, x, xp, y, yp, epilogue=EPI_NONE, resid=None, resid_planes=None, stream=None) -> None:
+    """The conv of ConvWeights `w`'s geometry (cm_conv_prepared): cm_conv_planes' inputs,
+    outputs and epilogue, without the per-call weight preparation."""
+    L = lib()
+    args = (w.ptr, _addr(x), _planes(xp), _addr(y), _planes(yp), int(epilogue), _addr(resid), _planes(resid_planes))
+    check(L.cm_conv_prepared(*args) if stream is None else L.cm_conv_prepared_async(*args, _stream(stream)))
+
+
 def MatmulKernelFused(a, b, c, n, k, m, batch=1, a_batch_stride=None, b_batch_stride=None, c_batch_stride=None,
                       epilogue=EPI_ADD, bias=None, stream=None) -> None:
     """MatmulKernel followed by VectorOP ADD of a bias row broadcast over the n rows

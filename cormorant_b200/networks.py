@@ -479,10 +479,13 @@ def execute(net: Net, backend, bufs: dict) -> None:
 class GpuBackend:
     """The four kernels of libcormorant_cuda.so on one CUDA stream (asynchronous)."""
 
-    def __init__(self, stream=None, one_launch: bool = False):
+    def __init__(self, stream=None, one_launch: bool = False, weights: dict | None = None):
         from . import kernels
         self.k = kernels
         self.stream = stream
+        # weights: prepared conv weights (prepare_weights) looked up by the call's weight and
+        # bias buffers and geometry; convs without an entry prepare their weights per call
+        self.weights = weights or {}
         # one_launch: a call list that cm_calls accepts (small batch-1 networks) runs as
         # one kernel launch instead of one launch per call
         self.one_launch = one_launch
@@ -514,17 +517,32 @@ class GpuBackend:
         self.k.MatmulKernelFused(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi, bias=bias,
                                  stream=self.stream)
 
+    def _prepared(self, w, bias, geo):
+        return self.weights.get(weights_key(w, bias, geo)) if self.weights else None
+
     def conv(self, x, w, bias, y, *args):
-        self.k.ConvKernel(x, w, bias, y, *args, stream=self.stream)
+        pw = self._prepared(w, bias, args)
+        if pw is not None:
+            self.k.ConvKernelPrepared(pw, x, None, y, None, stream=self.stream)
+        else:
+            self.k.ConvKernel(x, w, bias, y, *args, stream=self.stream)
 
     def conv_fused(self, x, w, bias, y, *args):
         *geo, epi, resid = args
-        self.k.ConvKernelFused(x, w, bias, y, *geo, epilogue=epi, resid=resid, stream=self.stream)
+        pw = self._prepared(w, bias, geo)
+        if pw is not None:
+            self.k.ConvKernelPrepared(pw, x, None, y, None, epilogue=epi, resid=resid, stream=self.stream)
+        else:
+            self.k.ConvKernelFused(x, w, bias, y, *geo, epilogue=epi, resid=resid, stream=self.stream)
 
     def conv_planes(self, x, xp, w, bias, y, yp, *args):
         *geo, epi, resid, rp = args
-        self.k.ConvKernelPlanes(x, xp, w, bias, y, yp, *geo, epilogue=epi, resid=resid, resid_planes=rp,
-                                stream=self.stream)
+        pw = self._prepared(w, bias, geo)
+        if pw is not None:
+            self.k.ConvKernelPrepared(pw, x, xp, y, yp, epilogue=epi, resid=resid, resid_planes=rp, stream=self.stream)
+        else:
+            self.k.ConvKernelPlanes(x, xp, w, bias, y, yp, *geo, epilogue=epi, resid=resid, resid_planes=rp,
+                                    stream=self.stream)
 
     def pool(self, x, y, *args):
         self.k.PoolingKernel(x, y, *args, stream=self.stream)
@@ -534,6 +552,32 @@ class GpuBackend:
 
     def pool_planes(self, xp, yp, *args):
         self.k.PoolingKernelPlanes(xp, yp, *args, stream=self.stream)
+
+
+def weights_key(w, bias, geo) -> tuple:
+    """Lookup key of a conv call's prepared weights: its weight and bias buffers and the 17
+    geometry scalars."""
+    def addr(t):
+        return 0 if t is None else (t.data_ptr() if hasattr(t, "data_ptr") else int(t))
+    return (addr(w), addr(bias), tuple(int(v) for v in geo))
+
+
+def prepare_weights(net: Net, bufs: dict) -> dict:
+    """Prepared weights (kernels.ConvWeights) of every conv in the call list, built once
+    from the device buffers `bufs` (gpu_buffers) holds: pass the result to GpuBackend so
+    that runs skip the per-call weight preparation.  The network's weights are constants;
+    the buffers must keep their values while the result is used."""
+    from . import kernels
+    R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
+    out = {}
+    for node in net.nodes:
+        if node[0] != "conv":
+            continue
+        w, b, geo = R(node[2]), R(node[3]), node[5]
+        key = weights_key(w, b, geo)
+        if key not in out:
+            out[key] = kernels.ConvWeights(w, b, *geo)
+    return out
 
 
 def gpu_buffers(net: Net, x=None):

@@ -257,6 +257,30 @@ int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t*
                          unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
                          const cm_planes_t* resid_planes, cm_stream_t stream);
 
+/* ---- Prepared conv weights (no reference counterpart) ---------------------------------
+ * A network's conv weights do not change between runs, but every conv call turns them into
+ * the GEMM's weight planes and column terms again (one to three small launches per call).
+ * cm_conv_weights_create does that once for one call's geometry (the scalars of cm_conv_planes
+ * from batch to is_depthwise, the same meaning) and keeps the result on the device;
+ * cm_conv_prepared[_async] then runs that conv (cm_conv_planes' x, xp, y, yp, epilogue, resid,
+ * resid_planes) without the preparation.  Results are cm_conv_planes' words as long as weight
+ * and bias still hold the values they held at creation: the prepared planes are a snapshot,
+ * while convs small enough for the CUDA-core paths (and depthwise convs) read weight and bias
+ * at each call, so both buffers must stay allocated.  Creation runs on the default stream and
+ * waits for it (not inside a stream capture).  Destroy frees the planes. */
+typedef struct cm_conv_weights cm_conv_weights_t;
+int cm_conv_weights_create(const int16_t* weight, const int16_t* bias, unsigned batch, unsigned in_ch,
+                           unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w,
+                           unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                           unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
+                           unsigned is_depthwise, cm_conv_weights_t** out);
+void cm_conv_weights_destroy(cm_conv_weights_t* w);
+int cm_conv_prepared(const cm_conv_weights_t* w, const int16_t* x, const cm_planes_t* xp, int16_t* y,
+                     cm_planes_t* yp, unsigned epilogue, const int16_t* resid, const cm_planes_t* resid_planes);
+int cm_conv_prepared_async(const cm_conv_weights_t* w, const int16_t* x, const cm_planes_t* xp, int16_t* y,
+                           cm_planes_t* yp, unsigned epilogue, const int16_t* resid,
+                           const cm_planes_t* resid_planes, cm_stream_t stream);
+
 /* ---- Small call lists in one launch (no reference counterpart) ----------------------
  * A list of small kernel calls -- a batch-1 network, bound by launch latency -- run as ONE
  * CTA that executes them in order, with the results of the entry points named below,

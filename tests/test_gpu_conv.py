@@ -185,6 +185,59 @@ def test_conv_fused_epilogue(cm, port, case, epi):
     assert_same(host(y), want, f"fused {case} epi {epi}")
 
 
+PREPARED = [REF_CASES[i] for i in (4, 13, 19, 20, 21, 24, 25, 34, 36, 39, 42)]
+
+
+@pytest.mark.parametrize("case", PREPARED)
+@pytest.mark.parametrize("epi", [0, 3])
+def test_prepared_weights_match_reference(cm, port, case, epi):
+    """cm_conv_prepared with weights prepared once (every conv path: CUDA-core small and
+    depthwise convs, implicit GEMM, space-to-depth, explicit im2col) equals the reference
+    conv (+ residual Add + Relu), word for word, over repeated calls."""
+    from cormorant_b200 import kernels
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    rng = np.random.default_rng(sum(case) * 3 + epi)
+    x = rand16(rng, N * C * H * W, -2048, 2048)
+    w = rand16(rng, M * (1 if dwm else C) * kh * kw, -512, 512)
+    bias = rand16(rng, M, -2048, 2048)
+    r = rand16(rng, N * M * oh * ow)
+    size = N * M * oh * ow
+    want = port.conv(x, w, bias if hb else None, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)[:size]
+    if epi & 2:
+        want = port.vectorop(want, r, size, 0, 1, 0, 0)[:size]
+    if epi & 1:
+        want = port.vectorop(want, None, size, 4, 1, 0, 0)[:size]
+    wd, bd = dev(w), dev(bias) if hb else None
+    pw = kernels.ConvWeights(wd, bd, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)
+    for rep in range(2):
+        y = empty(size)
+        kernels.ConvKernelPrepared(pw, dev(x), None, y, None, epilogue=epi, resid=dev(r) if epi & 2 else None)
+        assert_same(host(y), want, f"prepared {case} epi {epi} call {rep}")
+    pw.close()
+
+
+def test_prepared_weights_follow_the_direct_limit(cm, port):
+    """A conv prepared for the tensor-core path and then called with the CUDA-core limit
+    raised past it takes the CUDA-core path with the live weights: the same words."""
+    from cormorant_b200 import _lib, kernels
+    case = (2, 64, 14, 14, 64, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0)
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    rng = np.random.default_rng(5)
+    x, w, bias = rand16(rng, N * C * H * W), rand16(rng, M * C * 9, -512, 512), rand16(rng, M)
+    want = port.conv(x, w, bias, N, C, H, W, M, H, W, 3, 3, 1, 1, 1, 1, 1, 1, 1, 0)[: N * M * H * W]
+    L = _lib.lib()
+    old = L.cm_set_direct_limit(0)
+    try:
+        pw = kernels.ConvWeights(dev(w), dev(bias), N, C, H, W, M, H, W, 3, 3, 1, 1, 1, 1, 1, 1, 1, 0)
+        L.cm_set_direct_limit(1 << 40)
+        y = empty(N * M * H * W)
+        kernels.ConvKernelPrepared(pw, dev(x), None, y, None)
+    finally:
+        L.cm_set_direct_limit(old)
+    assert_same(host(y), want, "prepared weights, CUDA-core path at call time")
+
+
 ONE_LAUNCH_CASES = [
     (1, 1, 28, 28, 6, 5, 5, 1, 1, 1, 1, 2, 2, 2, 2, 1, 0),
     (2, 6, 14, 14, 16, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0, 1, 0),

@@ -186,7 +186,8 @@ def test_planes_fill_then_conv_and_residual(cm, port, N, C, H, W):
 
 @pytest.mark.parametrize("C,M", [(64, 64), (32, 44)])
 @pytest.mark.parametrize("res", ["nchw", "planes"])
-def test_plane_only_output_with_residual(cm, port, C, M, res):
+@pytest.mark.parametrize("prepared", [False, True])
+def test_plane_only_output_with_residual(cm, port, C, M, res, prepared):
     """A conv of at most 64 output channels whose output is only a plane image (the
     weights-as-A GEMM form) with a fused residual Add + Relu, the residual as NCHW words
     or as its own plane image: the image holds the reference sequence's words (read back
@@ -200,12 +201,17 @@ def test_plane_only_output_with_residual(cm, port, C, M, res):
     r = rand16(rng, N * M * H * W, -4096, 4096)
     want = oracle(port, x, w1, b1, g1, 3, r)
     P = kernels.PlaneImage(N, M, H, W, kernels.conv_plane_frame(*geo(N, M, H, W, 64, 3, 1, 1)))
+    R = None
     if res == "planes":
         R = kernels.PlaneImage(N, M, H, W, (0, 0, 0, 0))
         kernels.PlanesFill(R, dev(r))
-        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1, epilogue=3, resid=None, resid_planes=R)
+    rd = None if R is not None else dev(r)
+    if prepared:                                   # the weights-as-A rows built once
+        wd, bd = dev(w1), dev(b1)
+        pw = kernels.ConvWeights(wd, bd, *g1)
+        kernels.ConvKernelPrepared(pw, dev(x), None, None, P, epilogue=3, resid=rd, resid_planes=R)
     else:
-        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1, epilogue=3, resid=dev(r))
+        kernels.ConvKernelPlanes(dev(x), None, dev(w1), dev(b1), None, P, *g1, epilogue=3, resid=rd, resid_planes=R)
     assert_same(_identity_readback(kernels, P, N, M, H, W), want, f"plane-only output, {res} residual, M={M}")
 
 

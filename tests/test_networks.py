@@ -236,10 +236,10 @@ def test_chained_call_list_equals_reference_sequence_on_cpu(port):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("pool_planes", [False, True])
-def test_resnet18_chained_batch4_every_output(cm, port, pool_planes):
+@pytest.mark.parametrize("pool_planes,prepared", [(False, False), (True, False), (False, True)])
+def test_resnet18_chained_batch4_every_output(cm, port, pool_planes, prepared):
     """Plane images on the GPU: every NCHW tensor the chained list still writes, and the
-    logits, equal the oracle's."""
+    logits, equal the oracle's (also with the conv weights prepared once)."""
     import torch
     net = networks.chain(networks.fuse(networks.resnet18(batch=4)), pool_planes=pool_planes)
     assert net.planes
@@ -247,7 +247,10 @@ def test_resnet18_chained_batch4_every_output(cm, port, pool_planes):
     want = cpu_buffers(net, x)
     networks.execute(net, OracleBackend(port), want)
     bufs = networks.gpu_buffers(net, x)
-    networks.execute(net, networks.GpuBackend(), bufs)
+    weights = networks.prepare_weights(net, bufs) if prepared else None
+    if prepared:
+        assert len(weights) == sum(1 for n in net.nodes if n[0] == "conv")
+    networks.execute(net, networks.GpuBackend(weights=weights), bufs)
     torch.cuda.synchronize()
     for name in net.buffers:
         assert_same(bufs[name].cpu().numpy()[: net.buffers[name]], want[name][: net.buffers[name]], f"resnet {name}")
