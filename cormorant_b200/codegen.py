@@ -161,8 +161,11 @@ static int _load_weight(inference_buf_t *buf, const char *name)
 
 
 class _Emitter:
-    def __init__(self, net: Net, lib_path: str | None):
+    def __init__(self, net: Net, lib_path: str | None, prepared: bool = False):
         self.net = net
+        # prepared: every conv's weight planes built once by inference_init
+        # (cm_conv_weights_create) and the calls made through cm_conv_prepared_async
+        self.prepared = prepared
         self.R = net.resolve
         self.layout = plan_layout(net)
         # one init parameter per kernel of the unfused call list, as the reference's
@@ -285,6 +288,19 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
     # ---- inference.c ---------------------------------------------------------
     def _call(self, i: int, node) -> str:
         kind = node[0]
+        if kind == "conv" and self.prepared:
+            x, y, resid, xp, yp, rp = node[1], node[4], None, None, None, None
+            epi = 0
+            if len(node) > 6:
+                epi, resid = node[6], node[7]
+            if len(node) > 8:
+                xp, yp, rp = node[8], node[9], node[10]
+            what = "Conv" + ("+Add" if epi & 2 else "") + ("+Relu" if epi & 1 else "")
+            dst = " and ".join(v for v in (self.R(y) if y else None, yp) if v)
+            return (f"    /* {i}: {what} -> {dst} (weights prepared by inference_init) */\n"
+                    f"    CHECK(cm_conv_prepared_async(g_cw[{self._conv_index[i]}], {self._dev(x)}, {self._planes(xp)}, "
+                    f"{self._dev(y, False)}, {self._planes(yp)},\n        {int(epi)}u, {self._dev(resid)}, "
+                    f"{self._planes(rp)}, NULL));")
         if kind == "conv" and len(node) > 8:
             _, x, wn, bn, y, args, epi, resid, xp, yp, rp = node
             a = ", ".join(f"{int(v)}u" for v in args)
@@ -364,7 +380,18 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             f"        fprintf(stderr, \"inference_init: {k} instance '%s' differs from '%s'\\n\", {p}, {first});\n"
             f"        return 1;\n    }}"
             for _, k, p in self.kernels[1:])
+        convs = [i for i, n in enumerate(net.nodes) if n[0] == "conv"] if self.prepared else []
+        self._conv_index = {i: j for j, i in enumerate(convs)}
         calls = "\n".join(self._call(i, n) for i, n in enumerate(net.nodes))
+        cwdecl = (f"/* ---- conv weights prepared once (cm_conv_weights_create) ---- */\n"
+                  f"static cm_conv_weights_t *g_cw[{len(convs)}];\n") if convs else ""
+        cwcreate = "\n".join(
+            f"    if (cm_conv_weights_create({self._dev(net.nodes[i][2])}, {self._dev(net.nodes[i][3])},\n"
+            f"            {', '.join(f'{int(v)}u' for v in net.nodes[i][5])}, &g_cw[{j}]) != CM_OK) {{\n"
+            f"        fprintf(stderr, \"inference_init: preparing conv {i}: %s\\n\", cm_last_error());\n"
+            f"        goto fail;\n    }}"
+            for j, i in enumerate(convs))
+        cwdestroy = "\n".join(f"    cm_conv_weights_destroy(g_cw[{j}]);\n    g_cw[{j}] = NULL;" for j in range(len(convs)))
         pdecl = "\n".join(f"static cm_planes_t *{self._pvar(n)} = NULL;   /* {b}x{c}x{h}x{w}, frame {fr} */"
                           for n, (b, c, h, w, fr) in net.planes.items())
         pcreate = "\n".join(
@@ -400,7 +427,7 @@ static inference_buf_t *g_apool = NULL;   /* {L.act_words} words */
 {views}
 /* ---- plane images: conv outputs kept in the next convs' operand form (cm_conv_planes) ---- */
 {pdecl}
-
+{cwdecl}
 {loader}int inference_init({params})
 {{
 {same}
@@ -420,6 +447,7 @@ static inference_buf_t *g_apool = NULL;   /* {L.act_words} words */
 {fills}
 {pcreate}
     if (cm_buf_sync_to_device(g_wpool) != CM_OK) goto fail;
+{cwcreate}
     return 0;
 fail:
     inference_deinit();
@@ -428,6 +456,7 @@ fail:
 
 void inference_deinit(void)
 {{
+{cwdestroy}
 {pdestroy}
     if (g_apool) inference_buf_release(g_apool);
     if (g_wpool) inference_buf_release(g_wpool);
@@ -571,13 +600,15 @@ target_link_libraries(test_inference PRIVATE inference)
 """
 
 
-def emit_project(net: Net, out_dir, expected: np.ndarray | None = None, lib_path: str | None = None) -> dict:
+def emit_project(net: Net, out_dir, expected: np.ndarray | None = None, lib_path: str | None = None,
+                 prepared: bool = False) -> dict:
     """Write the generated project for `net` under out_dir and return {relative path: bytes written}.
 
     expected: the network output for the ramp input (word i = i & 0xFFFF), as int16; when
     given, test/test_inference.c and (above LARGE_EXPECTED_THRESHOLD words)
-    expected/<output>.dat are written."""
-    em = _Emitter(net, lib_path)
+    expected/<output>.dat are written.  prepared: inference_init builds every conv's weight
+    planes once (cm_conv_weights_create) and inference_run calls cm_conv_prepared_async."""
+    em = _Emitter(net, lib_path, prepared)
     out = Path(out_dir)
     files = {"include/inference.h": em.header().encode(), "src/inference.c": em.source().encode(),
              "CMakeLists.txt": em.cmake().encode()}

@@ -25,7 +25,7 @@ NETS = {
 }
 
 
-MODES = ["plain", "fused", "planes"]
+MODES = ["plain", "fused", "planes", "prepared"]
 
 
 def _net(name, mode):
@@ -33,7 +33,7 @@ def _net(name, mode):
     if mode == "plain":
         return net
     net = networks.fuse(net)
-    return networks.chain(net) if mode == "planes" else net
+    return networks.chain(net) if mode in ("planes", "prepared") else net
 
 
 def _nchw_outputs(net):
@@ -143,7 +143,7 @@ def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, mode):
     """gcc -Wall -Wextra -Werror over the generated sources, linked against the library;
     with no GPU visible inference_init reports the failure and the test binary exits 1."""
     net = _net("resnet18_b2", mode)
-    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
+    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16), prepared=mode == "prepared")
     exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
     import torch
     if torch.cuda.is_available():
@@ -159,7 +159,7 @@ def test_project_compiles_and_fails_cleanly_without_gpu(tmp_path, mode):
 def test_generated_project_bit_exact_on_gpu(tmp_path, port, name, mode):
     net = _net(name, mode)
     exp = _expected(net, port)
-    codegen.emit_project(net, tmp_path, expected=exp)
+    codegen.emit_project(net, tmp_path, expected=exp, prepared=mode == "prepared")
     exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
     r = subprocess.run([str(exe), "20"], capture_output=True, text=True, timeout=600, cwd=tmp_path)
     assert r.returncode == 0, r.stdout + r.stderr
@@ -198,3 +198,17 @@ def test_plane_pool_project_compiles(tmp_path):
     codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
     assert (tmp_path / "src/inference.c").read_text().count("cm_pool_planes_async(") == 1
     codegen.compile_project(tmp_path, INCLUDE, LIB)
+
+
+def test_prepared_project_builds_weights_once(tmp_path):
+    """prepared=True: inference_init creates one cm_conv_weights_t per conv (after the weight
+    pool reaches the device), inference_run calls cm_conv_prepared_async for every conv,
+    inference_deinit destroys them."""
+    net = _net("resnet18_b2", "prepared")
+    codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16), prepared=True)
+    src = (tmp_path / "src/inference.c").read_text()
+    nconv = sum(1 for n in net.nodes if n[0] == "conv")
+    assert src.count("cm_conv_weights_create(") == nconv == src.count("cm_conv_prepared_async(")
+    assert src.count("cm_conv_weights_destroy(") == nconv
+    assert "cm_conv_planes_async(" not in src and "cm_conv_fused_async(" not in src
+    assert src.index("cm_buf_sync_to_device(g_wpool)") < src.index("cm_conv_weights_create(")
