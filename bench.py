@@ -195,6 +195,15 @@ class MatmulSweep:
                 continue
             cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, stream=stream)
 
+    def gather_outputs(self):
+        """(local output shard, items over all ranks, words per item) of each output of a step."""
+        import torch
+        out = []
+        for (n, k, m, b), (_, _, _, B), t in zip(self.shapes, self.sweep, self.bufs):
+            c = t[2] if t is not None else torch.empty(0, dtype=torch.int16, device="cuda")
+            out.append((c, B, n * m))
+        return out
+
     def per_part(self, cm, stream, iters):
         """Per-shape device times of the GEMM and split kernels (a separate profiled pass)."""
         out = []
@@ -290,6 +299,9 @@ class VectorOPSweep:
         for op in VOP_OPS:
             cm.VectorOPKernel(self.a, self.b, self.c, self.n, op, stream=stream)
 
+    def gather_outputs(self):
+        return [(self.c, VOP_N, 1) for _ in VOP_OPS]
+
     def per_part(self, cm, stream, iters):
         import ctypes as C
         import torch
@@ -372,6 +384,10 @@ class PoolSweep:
     def step(self, cm, stream):
         for c in POOL_SWEEP:
             self._one(cm, c, stream)
+
+    def gather_outputs(self):
+        N, C, H, W = POOL_SHAPE
+        return [(self.y[: self.nb * C * c[-2] * c[-1]], N, C * c[-2] * c[-1]) for c in POOL_SWEEP]
 
     def per_part(self, cm, stream, iters):
         import ctypes as C_
@@ -498,6 +514,13 @@ class NetworkBench:
         n = cm.launch_count() - l0
         torch.cuda.synchronize()
         return g, n
+
+    def gather_outputs(self):
+        """ResNet: the logits of every image; LeNet runs replicas (nothing to gather)."""
+        if self.which == "lenet":
+            return []
+        out = self.bufs[self.net.resolve(self.net.output)]
+        return [(out[: self.local * 1000], self.batch_total, 1000)]
 
     def profile_dominant(self, cm, stream, iters):
         """Device time (ms) and launch count of the GEMM kernel over `iters` eager passes, from
@@ -986,6 +1009,35 @@ def main():
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(wl.dominant),
                 "kernel": wl.dominant, "note": f"algorithmic bytes / kernel time on rank 0; of {peaks['source']}"}
 
+    # N > 1: the outputs stay sharded in `value`; end to end, a caller that wants every
+    # output on every GPU adds one NCCL all-gather of them per step (NVLink / NVSwitch)
+    gather = None
+    gspec = wl.gather_outputs() if (world > 1 and hasattr(wl, "gather_outputs")) else []
+    if gspec:
+        from cormorant_b200 import sharding
+        gather_bytes = 0
+        for t, total, per_item in gspec:                # warm the collectives once
+            sharding.gather_batches(t, total, per_item)
+        torch.cuda.synchronize()
+        barrier()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record(stream)
+        for t, total, per_item in gspec:
+            full = sharding.gather_batches(t, total, per_item)
+            gather_bytes += full.numel() * 2
+            del full
+        ge.record(stream)
+        torch.cuda.synchronize()
+        g_ms = max_over_ranks(gs.elapsed_time(ge))
+        gv = wl.units_total / ((ms_per_step + g_ms) * 1e-3)
+        if args.config == "matmul":
+            gv /= 1e9
+        gather = {"ms_per_step": g_ms, "bytes_per_step": gather_bytes, "value_with_gather": gv, "unit": wl.unit,
+                  "note": "every output of one step all-gathered to every rank (NCCL all_gather over NVLink / "
+                          "NVSwitch, max over ranks); value_with_gather = units / (ms_per_step + gather ms); "
+                          "gathering to every GPU is bound by each GPU's NVLink ingress, so it does not scale "
+                          "with N"}
+        torch.cuda.empty_cache()
     per_part = wl.per_part(cm, stream, max(2, min(K, 5))) if (args.per_part and rank == 0) else None
     wl.release()
     torch.cuda.empty_cache()
@@ -1031,6 +1083,8 @@ def main():
                 if wl.dominant == "gemm_q88" else "q8.8 int16 (ap_fixed<16,8>), int32 / IEEE f32 epilogue",
                 "data": "synthetic (seeded)", "config": wl.config(world), "roofline": roof,
                 "cpu_baseline": cpu_line, "e2e": e2e, "gpu_launches": launches_total, "clocks": clocks}
+        if gather is not None:
+            line["gather"] = gather
         if per_part is not None:
             line["per_part"] = per_part
         print(json.dumps(line))

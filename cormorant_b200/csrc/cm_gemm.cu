@@ -194,20 +194,6 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-#define CM_R32(i) "=r"(r[i])
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-        : CM_R32(0), CM_R32(1), CM_R32(2), CM_R32(3), CM_R32(4), CM_R32(5), CM_R32(6), CM_R32(7), CM_R32(8),
-          CM_R32(9), CM_R32(10), CM_R32(11), CM_R32(12), CM_R32(13), CM_R32(14), CM_R32(15), CM_R32(16),
-          CM_R32(17), CM_R32(18), CM_R32(19), CM_R32(20), CM_R32(21), CM_R32(22), CM_R32(23), CM_R32(24),
-          CM_R32(25), CM_R32(26), CM_R32(27), CM_R32(28), CM_R32(29), CM_R32(30), CM_R32(31)
-        : "r"(taddr));
-}
-#undef CM_R32
-
 #define CM_R16(i) "=r"(r[i])
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -219,11 +205,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 #undef CM_R16
 
-template <int W>
-__device__ __forceinline__ void tmem_ld(uint32_t taddr, uint32_t (&r)[W]) {
-    if constexpr (W == 32) tmem_ld32(taddr, r);
-    else tmem_ld16(taddr, r);
-}
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -755,8 +736,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                 const uint32_t col0 = tc.n0 + cbase + c0;
                 if (col0 < g.cols) {
                     uint32_t p[CW], q[CW], cv[CW];
-                    tmem_ld<CW>(tl + c0, p);
-                    tmem_ld<CW>(tl + TBN + c0, q);
+                    tmem_ld16(tl + c0, p);
+                    tmem_ld16(tl + TBN + c0, q);
                     // column terms: four 16-byte loads for a full, aligned chunk
                     if (col0 + CW <= g.cols && ((uintptr_t)(ct + col0) & 15u) == 0) {
                         const int4* c4 = (const int4*)(ct + col0);
@@ -773,11 +754,11 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                     tmem_ld_wait();
 #pragma unroll
                     for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
-                    tmem_ld<CW>(tl + 2 * TBN + c0, q);
+                    tmem_ld16(tl + 2 * TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
                     for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] + q[k]) << 8;
-                    tmem_ld<CW>(tl + 3 * TBN + c0, q);
+                    tmem_ld16(tl + 3 * TBN + c0, q);
                     tmem_ld_wait();
 #pragma unroll
                     for (int k = 0; k < (int)CW; k += 2)

@@ -182,7 +182,7 @@ __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restr
             // Window reduction of output row q (tile offset b); compile-time windows
             // gather all taps first and reduce them as a tree to keep chains short.
             auto reduce = [&](uint32_t b) -> uint32_t {
-                if (PH && PW) {
+                if constexpr (PH > 0 && PW > 0) {
                     int32_t v[(PH * PW > 0) ? PH * PW : 1];
 #pragma unroll
                     for (uint32_t r = 0; r < (uint32_t)PH; ++r)
@@ -749,6 +749,41 @@ __device__ __forceinline__ void reduce_word(uint32_t& acc, int32_t v) {
 
 // Global pools: warp per plane.  Sums are formed on raw words and scaled by
 // 2^8 afterwards (the same value mod 2^32); MAX keeps the largest word.
+// Global pools of small planes (hw <= 512, e.g. the 7x7 maps before a classifier): a warp
+// per plane would leave most lanes idle and chain its few loads; instead a block stages
+// `ppb` consecutive planes (one contiguous run) in shared memory with coalesced 4-byte
+// loads and thread t reduces plane t.  Same sums (mod 2^32) and maxima as the warp kernel.
+template <int TYPE>
+__global__ void __launch_bounds__(256) pool_global_small_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
+                                                                uint64_t planes, uint32_t hw) {
+    extern __shared__ __align__(16) int16_t sbuf[];     // blockDim.x planes x hw words
+    const uint32_t ppb = blockDim.x, tid = threadIdx.x;
+    for (uint64_t p0 = (uint64_t)blockIdx.x * ppb; p0 < planes; p0 += (uint64_t)gridDim.x * ppb) {
+        const uint32_t np = planes - p0 < ppb ? (uint32_t)(planes - p0) : ppb;
+        const uint32_t words = np * hw;
+        const int16_t* src = x + p0 * hw;
+        if (((uintptr_t)src & 3u) == 0) {
+            const uint32_t* s4 = (const uint32_t*)src;
+            for (uint32_t i = tid; i < words / 2; i += ppb) ((uint32_t*)sbuf)[i] = __ldcs(s4 + i);
+            if ((words & 1u) && tid == 0) sbuf[words - 1] = src[words - 1];
+        } else {
+            for (uint32_t i = tid; i < words; i += ppb) sbuf[i] = __ldcs(src + i);
+        }
+        __syncthreads();
+        if (tid < np) {
+            uint32_t acc = (TYPE == P_MAX) ? 0xFFFF8000u : 0u;
+            const int16_t* v = sbuf + tid * hw;
+            for (uint32_t k = 0; k < hw; ++k) reduce_word<TYPE>(acc, v[k]);
+            uint32_t a;
+            if (TYPE == P_MAX) a = (uint32_t)((int32_t)acc * 256);
+            else if (TYPE == P_LP2) a = acc;
+            else a = acc * 256u;
+            y[p0 + tid] = finalize<TYPE>(a, hw);
+        }
+        __syncthreads();
+    }
+}
+
 template <int TYPE>
 __global__ void __launch_bounds__(256) pool_global_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                           uint64_t planes, uint32_t hw) {
@@ -803,6 +838,19 @@ template <int TYPE>
 int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, const PoolP& p0, bool global,
            cudaStream_t s) {
     if (global) {
+        const uint64_t hw = (uint64_t)p0.in_h * p0.in_w;
+        if (hw > 0 && hw <= 512) {
+            // planes per block: a power of two in [32, 256] with at most 32 KB staged
+            uint32_t ppb = 256;
+            while (ppb > 32 && (uint64_t)ppb * hw * 2 > 32768) ppb /= 2;
+            const unsigned grid = grid_for(cx, planes, ppb, 2048 / ppb);
+            {
+                ProfScope ps_(PK_POOL, s);
+                pool_global_small_kernel<TYPE><<<grid, ppb, (size_t)ppb * hw * 2, s>>>(x, y, planes, (uint32_t)hw);
+            }
+            count_launch();
+            return CM_OK;
+        }
         const unsigned grid = grid_for(cx, planes * 32, 256, 8);
         {
             ProfScope ps_(PK_POOL, s);

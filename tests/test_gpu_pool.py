@@ -69,6 +69,18 @@ def test_global(cm, port, hw, typ):
     run_case(cm, port, x, N, C, H, W, H, W, 1, 1, 0, 0, 1, 1, 0, *typ)
 
 
+@pytest.mark.parametrize("hw", [(7, 7), (14, 14), (5, 3), (16, 32)])
+@pytest.mark.parametrize("typ", TYPES)
+def test_global_many_small_planes(cm, port, hw, typ):
+    """Global pools of many small planes (the ResNet classifier's 7x7 input): several
+    blocks of staged planes, a partial last block, odd word counts."""
+    H, W = hw
+    N, C = 3, 700
+    rng = np.random.default_rng(H * 100 + W + typ[0])
+    x = rand16(rng, N * C * H * W)
+    run_case(cm, port, x, N, C, H, W, H, W, 1, 1, 0, 0, 1, 1, 0, *typ)
+
+
 def test_empty_window(cm, port):
     x = rand16(np.random.default_rng(3), 2 * 3 * 4 * 4)
     for t in (0, 1, 2):
