@@ -2,7 +2,7 @@
 """Benchmark of the Cormorant Q8.8 kernels on B200 -- prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config matmul|vectorop|pool]
+                    [--config matmul|vectorop|pool|resnet|lenet]
 
 Default workload (the metric's configuration): the
 batched MatMul sweep, raw int16 uniform [-1024, 1024):
@@ -11,10 +11,16 @@ One step = one pass over the sweep.  metric = Q8.8 GOPS = 2*n*k*m*batch / time
 (the reference bench's definition, inference-scheduler/bench_src/bench_matmul.c).
 --config vectorop: the 2^28-element sweep of the six ops, GB/s = ports*size*2B / time.
 --config pool: the seven pooling variants on [256,64,112,112], GB/s = (x+y bytes) / time.
+--config resnet / lenet: the ResNet-18-shaped network at batch 256 and LeNet-5 at batch 1,
+images/s; the call list (folded epilogues, plane images, conv weights prepared once) is
+captured as one CUDA graph and replayed per step (--no-graph, --no-prepared, --no-planes,
+--unfused select the slower forms).
 
 Multi-GPU (torchrun, one rank per GPU): every workload is sharded by batch
 (VectorOP by contiguous element range); no collective runs in the timed
 region; the total work is fixed, so scaling is "strong".  Time = max over ranks.
+The line adds "gather": one NCCL all-gather of a step's outputs to every rank, timed
+after the timed region.
 
 --impl reference times the reference's own CPU implementation (the unmodified
 reference kernels compiled against oracle/'s shim, oracle/_ref; else the C
