@@ -456,12 +456,37 @@ __global__ void __launch_bounds__(256) pool_max_planes_kernel(const int8_t* __re
 }
 
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
+// The channel sums of a conv's OUTPUT plane image cleared (0 inside the image, the frame's
+// value on the frame) by the launch that computes the conv's row terms from its INPUT
+// image, instead of a launch of its own: images [0, nimg) of S [nimg][Hp][Wp].
+struct SumsReset {
+    int32_t* S = nullptr;
+    uint32_t nimg = 0, Hp = 0, Wp = 0, H = 0, W = 0, pt = 0, pl = 0;
+    int32_t frame = 0;
+};
+
+__device__ __forceinline__ void sums_reset_image(const SumsReset& z, uint32_t n, uint32_t first_row, uint32_t row_step,
+                                                 uint32_t first_col, uint32_t col_step) {
+    int32_t* S = z.S + (uint64_t)n * z.Hp * z.Wp;
+    for (uint32_t h = first_row; h < z.Hp; h += row_step) {
+        const bool row_in = h >= z.pt && h < z.pt + z.H;
+        for (uint32_t w = first_col; w < z.Wp; w += col_step)
+            S[(uint64_t)h * z.Wp + w] = row_in && w >= z.pl && w < z.pl + z.W ? 0 : z.frame;
+    }
+}
+
 __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
                                                            uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw,
                                                            uint32_t sh, uint32_t sw, uint32_t dh, uint64_t total,
-                                                           int32_t* __restrict__ rowterm) {
+                                                           int32_t* __restrict__ rowterm, SumsReset z) {
+    // blocks past the row-term grid clear the output image's sums, one image at a time
+    if (z.S && blockIdx.x >= gridDim.x - z.nimg) {
+        sums_reset_image(z, blockIdx.x - (gridDim.x - z.nimg), threadIdx.x / 32, blockDim.x / 32, threadIdx.x % 32, 32);
+        return;
+    }
+    const uint64_t nthreads = (uint64_t)(gridDim.x - (z.S ? z.nimg : 0)) * blockDim.x;
     const uint64_t P = (uint64_t)out_h * out_w;
-    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
+    for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += nthreads) {
         const uint64_t n = t / P, p = t - n * P;
         const uint32_t oh = (uint32_t)(p / out_w), ow = (uint32_t)(p - (uint64_t)oh * out_w);
         const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp + (uint64_t)ow * sw;
@@ -482,9 +507,15 @@ constexpr uint32_t kRowtermThreads = 128;
 __global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(const int32_t* __restrict__ S, uint32_t Hp,
                                                                           uint32_t Wp, uint32_t out_h, uint32_t out_w,
                                                                           uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
-                                                                          uint32_t dh, int32_t* __restrict__ rowterm) {
+                                                                          uint32_t dh, int32_t* __restrict__ rowterm,
+                                                                          SumsReset z) {
     extern __shared__ uint32_t colsum_all[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+    // the last block column clears image blockIdx.y of the output image's sums
+    if (z.S && blockIdx.x == gridDim.x - 1) {
+        sums_reset_image(z, blockIdx.y, warp, kRowtermThreads / 32, lane, 32);
+        return;
+    }
     const uint32_t oh = blockIdx.x * (kRowtermThreads / 32) + warp, n = blockIdx.y;
     if (oh >= out_h) return;
     const uint32_t need = (out_w - 1) * sw + kw;
@@ -505,20 +536,25 @@ __global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(cons
 }
 
 // Row terms of nb images (S: [nb][Hp][Wp], rt: [nb][out_h][out_w]).
+// z.S != null: the same launch clears the output image's sums for these nb images (z.nimg = nb).
 void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t Wp, uint32_t out_h, uint32_t out_w,
                     uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t dh, uint32_t nb, int32_t* rt,
-                    cudaStream_t s) {
+                    cudaStream_t s, SumsReset z = SumsReset{}) {
     const uint64_t need_bytes = ((uint64_t)(out_w - 1) * sw + kw) * 4 * (kRowtermThreads / 32);
     if (out_w >= 16 && need_bytes <= 48u * 1024u) {
         for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
             const uint32_t bz = std::min(65535u, nb - b0);
-            conv_rowterm_rows_kernel<<<dim3((out_h + 3) / 4, bz), kRowtermThreads, (size_t)need_bytes, s>>>(
-                S + (uint64_t)b0 * Hp * Wp, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, rt + (uint64_t)b0 * out_h * out_w);
+            SumsReset zb = z;
+            if (zb.S) { zb.S += (uint64_t)b0 * zb.Hp * zb.Wp; zb.nimg = bz; }
+            conv_rowterm_rows_kernel<<<dim3((out_h + 3) / 4 + (zb.S ? 1u : 0u), bz), kRowtermThreads, (size_t)need_bytes, s>>>(
+                S + (uint64_t)b0 * Hp * Wp, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, rt + (uint64_t)b0 * out_h * out_w, zb);
             count_launch();
         }
     } else {
         const uint64_t tot = (uint64_t)nb * out_h * out_w;
-        conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8), 256, 0, s>>>(S, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, tot, rt);
+        if (z.S) z.nimg = nb;
+        conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8) + (z.S ? nb : 0u), 256, 0, s>>>(S, Hp, Wp, out_h, out_w, kh, kw, sh,
+                                                                                        sw, dh, tot, rt, z);
         count_launch();
     }
 }
@@ -1304,7 +1340,9 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         if (!pw)
             rc = conv_weights(cx, weight, has_bias ? bias : nullptr, out_ch, in_ch, kh, kw, ip.Cp, ip.KR_pad, w_pitch,
                               w_plane, w_bytes, wpl, ct, s);
-        if (!rc && po) rc = planes_reset(po, s);
+        // a plane-image input runs in one chunk: its row-term launch also clears the output
+        // image's sums; otherwise a reset launch of its own
+        if (!rc && po && !xv) rc = planes_reset(po, s);
         // a plane image read in place: the conv's padded window starts (dt, dl) into its frame
         const uint32_t dt = xv ? xv->pt - pad_top : 0u, dl = xv ? xv->pl - pad_left : 0u;
         for (uint64_t n0 = 0; !rc && n0 < batch; n0 += chunk) {
@@ -1312,8 +1350,10 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             const NhwcGeom ng{in_ch, in_h, in_w, ip.Cp, ip.Hp, ip.Wp, pad_top, pad_left, nb};
             if (xv) {
                 ProfScope ps_(PK_SPLIT, s);
+                SumsReset z;
+                if (po) z = SumsReset{po->S, nb, po->Hp, po->Wp, po->H, po->W, po->pt, po->pl, (int32_t)(0u - 128u * po->C)};
                 rowterm_launch(cx, xv->S + (uint64_t)dt * xv->Wp + dl, xv->Hp, xv->Wp, out_h, out_w, kh, kw, stride_h,
-                               stride_w, dilation_h, nb, rt, s);
+                               stride_w, dilation_h, nb, rt, s, z);
             } else {
                 ProfScope ps_(PK_SPLIT, s);
                 const uint64_t HW = (uint64_t)in_h * in_w;
