@@ -1865,11 +1865,11 @@ extern "C" int cm_conv_weights_create(const int16_t* weight, const int16_t* bias
                                       unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
                                       unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
                                       unsigned has_bias, unsigned is_depthwise, cm_conv_weights_t** out) {
+    if (out) *out = nullptr;                // null on every failure
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
     if (!out) return set_error(CM_EINVAL, "cm_conv_weights_create: null result pointer");
-    *out = nullptr;
     if (has_bias && !bias) return set_error(CM_EINVAL, "cm_conv_weights_create: null bias");
     const uint64_t K64 = (uint64_t)in_ch * kh * kw;
     if (K64 > 0 && !weight) return set_error(CM_EINVAL, "cm_conv_weights_create: null weight");

@@ -267,7 +267,8 @@ int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t*
  * and bias still hold the values they held at creation: the prepared planes are a snapshot,
  * while convs small enough for the CUDA-core paths (and depthwise convs) read weight and bias
  * at each call, so both buffers must stay allocated.  Creation runs on the default stream and
- * waits for it (not inside a stream capture).  Destroy frees the planes. */
+ * waits for it (not inside a stream capture); *out is null unless it returns CM_OK.
+ * Destroy frees the planes (null is accepted). */
 typedef struct cm_conv_weights cm_conv_weights_t;
 int cm_conv_weights_create(const int16_t* weight, const int16_t* bias, unsigned batch, unsigned in_ch,
                            unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w,

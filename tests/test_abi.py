@@ -46,6 +46,13 @@ def test_calls_before_init_report_enoinit():
     assert L.cm_matmul(None, None, None, 1, 1, 1, 1, 0, 0, 0) == _lib.CM_ENOINIT
     assert L.cm_conv(None, None, None, None, *([1] * 17)) == _lib.CM_ENOINIT
     assert L.cm_pool(None, None, *([1] * 17)) == _lib.CM_ENOINIT
+    # the prepared-weights entries refuse the same way and leave the result pointer null
+    import ctypes as C
+    out = C.c_void_p(12345)
+    assert L.cm_conv_weights_create(None, None, *([1] * 17), C.byref(out)) == _lib.CM_ENOINIT
+    assert out.value is None
+    assert L.cm_conv_prepared(None, None, None, None, None, 0, None, None) == _lib.CM_ENOINIT
+    L.cm_conv_weights_destroy(None)                       # null is accepted
     assert b"cm_init" in L.cm_last_error()
 
 
