@@ -2,25 +2,36 @@
 """Benchmark of the Cormorant Q8.8 kernels on B200 -- prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config matmul|vectorop|pool|resnet|lenet]
+                    [--config all|matmul|vectorop|pool|resnet|lenet]
 
-Default workload (the metric's configuration): the
-batched MatMul sweep, raw int16 uniform [-1024, 1024):
-    B=64 x {256^3, 1024^3, 4096^3}  +  B=8 x (8192x4096)(4096x11008).
-One step = one pass over the sweep.  metric = Q8.8 GOPS = 2*n*k*m*batch / time
-(the reference bench's definition, inference-scheduler/bench_src/bench_matmul.c).
---config vectorop: the 2^28-element sweep of the six ops, GB/s = ports*size*2B / time.
---config pool: the seven pooling variants on [256,64,112,112], GB/s = (x+y bytes) / time.
---config resnet / lenet: the ResNet-18-shaped network at batch 256 and LeNet-5 at batch 1,
-images/s; the call list (folded epilogues, plane images, conv weights prepared once) is
-captured as one CUDA graph and replayed per step (--no-graph, --no-prepared, --no-planes,
---unfused select the slower forms).
+Default (--config all): every BASELINE config is measured; the line's own keys are the
+headline workload, BASELINE.json configs[1] (the metric's configuration): the batched
+MatMul sweep, raw int16 uniform [-1024, 1024),
+    B=64 x {256^3, 1024^3, 4096^3}  +  B=8 x (8192x4096)(4096x11008),
+one step = one pass over the sweep, metric = Q8.8 GOPS = 2*n*k*m*batch / time (the
+reference bench's definition, inference-scheduler/bench_src/bench_matmul.c:82-101).
+"configs" holds one record per config, each measured the same way (value, ms_per_step,
+roofline of its dominant kernel, e2e through the reference-facing API, cpu_baseline,
+clocks, per-part breakdown):
+  matmul    the headline again;
+  lenet     LeNet-5 batch 1, images/s (one step = one inference, CUDA-graph replay);
+  vectorop  the 2^28-element sweep of the six ops, GB/s = ports*size*2B / time
+            (bench_vectorop.c:92-95);
+  pool      the seven pooling variants on [256,64,112,112], GB/s = (x+y bytes) / time
+            (bench_pool.c:223-224);
+  resnet    the ResNet-18-shaped network at batch 256, images/s; the call list (folded
+            epilogues, plane images, conv weights prepared once) captured as one CUDA graph
+            and replayed per step (--no-graph, --no-prepared, --no-planes, --unfused select
+            the slower forms).
+Sub-configs whose step is short time K x STEP_MULT steps so that each timed region lasts a
+few hundred ms.  GEMM configs measure the int8 tensor pipe's ceiling (cm_int8_mma_rate) and
+cuBLASLt's int8 rate just before their timed region: the roofline's peak.
 
 Multi-GPU (torchrun, one rank per GPU): every workload is sharded by batch
 (VectorOP by contiguous element range); no collective runs in the timed
 region; the total work is fixed, so scaling is "strong".  Time = max over ranks.
-The line adds "gather": one NCCL all-gather of a step's outputs to every rank, timed
-after the timed region.
+Each record adds "gather": one step's outputs gathered to rank 0 (grouped NCCL
+send/recv into offsets) and all-gathered to every rank, each timed on the device.
 
 --impl reference times the reference's own CPU implementation (the unmodified
 reference kernels compiled against oracle/'s shim, oracle/_ref; else the C
@@ -240,8 +251,12 @@ class MatmulSweep:
         self.bufs = []
 
     # ---- end to end through the reference-facing API (cm_buf_* + run_matmul) ----
+    e2e_path = ("per shape: cm_buf_sync_to_device_async(A, B) -> run_matmul (cm_matmul_async) -> "
+                "cm_buf_sync_from_device_async(C), pinned host mirrors; uploads, kernels and downloads on three "
+                "streams, so shape i+1's upload and shape i-1's download overlap shape i's GEMM (runtime.CopyOverlap)")
+
     def e2e_setup(self):
-        from cormorant_b200.runtime import InferenceBuf
+        from cormorant_b200.runtime import CopyOverlap, InferenceBuf
         import numpy as np
         self.e2e = []
         rng = np.random.default_rng(99 + self.rank)
@@ -257,20 +272,26 @@ class MatmulSweep:
             self.e2e.append((n, k, m, b, A, B, Cb))
             self.h2d += 2 * (b * n * k + b * k * m)
             self.d2h += 2 * b * n * m
+        self.pipe = CopyOverlap()
+
+    def e2e_start(self, start_event):
+        self.pipe.start(start_event)
 
     def e2e_step(self):
         from cormorant_b200.runtime import run_matmul
         for (n, k, m, b, A, B, Cb) in self.e2e:
-            A.sync_to_device()
-            B.sync_to_device()
-            run_matmul(A, B, Cb, n, k, m, b, n * k, k * m, n * m)
-            Cb.sync_from_device()
+            self.pipe.call([A, B], [Cb], lambda s, n=n, k=k, m=m, b=b, A=A, B=B, Cb=Cb:
+                           run_matmul(A, B, Cb, n, k, m, b, n * k, k * m, n * m, stream=s))
+
+    def e2e_finish(self):
+        self.pipe.join()
 
     def e2e_release(self):
         for t in self.e2e:
             for buf in t[4:]:
                 buf.free()
         self.e2e = []
+        self.pipe = None
 
 
 class VectorOPSweep:
@@ -329,28 +350,44 @@ class VectorOPSweep:
     def release(self):
         self.a = self.b = self.c = None
 
+    e2e_path = ("per op: cm_buf_sync_to_device_async(a[, b]) -> run_op (cm_vectorop_async) -> "
+                "cm_buf_sync_from_device_async(c), pinned host mirrors; consecutive ops use two buffer sets so one "
+                "op's copies overlap the next op's kernel (runtime.CopyOverlap)")
+
     def e2e_setup(self):
-        from cormorant_b200.runtime import InferenceBuf
+        from cormorant_b200.runtime import CopyOverlap, InferenceBuf
         import numpy as np
         rng = np.random.default_rng(5 + self.rank)
-        self.A, self.B, self.C = (InferenceBuf.alloc(self.n) for _ in range(3))
-        fill(self.A.ptr(), rng, -32768, 32768)
-        fill(self.B.ptr(), rng, 1, 32768)
+        self.sets = []
+        for _ in range(2):
+            A, B, C = (InferenceBuf.alloc(self.n) for _ in range(3))
+            fill(A.ptr(), rng, -32768, 32768)
+            fill(B.ptr(), rng, 1, 32768)
+            self.sets.append((A, B, C))
         self.h2d = sum((2 if op < 4 else 1) * self.n * 2 for op in VOP_OPS)
         self.d2h = len(VOP_OPS) * self.n * 2
+        self.pipe = CopyOverlap()
+
+    def e2e_start(self, start_event):
+        self.pipe.start(start_event)
 
     def e2e_step(self):
         from cormorant_b200.runtime import run_op
-        for op in VOP_OPS:
-            self.A.sync_to_device()
-            if op < 4:
-                self.B.sync_to_device()
-            run_op(self.A, self.B if op < 4 else None, self.C, self.n, op, 1, 0, 0)
-            self.C.sync_from_device()
+        for i, op in enumerate(VOP_OPS):
+            A, B, C = self.sets[i % 2]
+            ins = [A, B] if op < 4 else [A]
+            self.pipe.call(ins, [C], lambda s, op=op, A=A, B=B, C=C:
+                           run_op(A, B if op < 4 else None, C, self.n, op, 1, 0, 0, stream=s))
+
+    def e2e_finish(self):
+        self.pipe.join()
 
     def e2e_release(self):
-        for b in (self.A, self.B, self.C):
-            b.free()
+        for t in self.sets:
+            for b in t:
+                b.free()
+        self.sets = []
+        self.pipe = None
 
 
 class PoolSweep:
@@ -417,29 +454,47 @@ class PoolSweep:
     def release(self):
         self.x = self.y = None
 
+    e2e_path = ("per variant: cm_buf_sync_to_device_async(x) -> run_pool (cm_pool_async) -> "
+                "cm_buf_sync_from_device_async(y), pinned host mirrors; consecutive variants use two buffer pairs so "
+                "one variant's copies overlap the next variant's kernel (runtime.CopyOverlap)")
+
     def e2e_setup(self):
-        from cormorant_b200.runtime import InferenceBuf
+        from cormorant_b200.runtime import CopyOverlap, InferenceBuf
         import numpy as np
         N, C, H, W = POOL_SHAPE
         rng = np.random.default_rng(8 + self.rank)
-        self.X = InferenceBuf.alloc(self.nb * C * H * W)
-        self.Y = InferenceBuf.alloc(self.nb * C * 56 * 56)
-        fill(self.X.ptr(), rng, -2048, 2048)
+        self.X = [InferenceBuf.alloc(self.nb * C * H * W) for _ in range(2)]
+        self.Y = [InferenceBuf.alloc(self.nb * C * 56 * 56) for _ in range(2)]
+        for x in self.X:
+            fill(x.ptr(), rng, -2048, 2048)
+        # one output view per (variant, buffer): the variant's output words only
+        self.Yv = [[InferenceBuf.init_view(y, 0, self.nb * C * c[12] * c[13]) for y in self.Y] for c in POOL_SWEEP]
         self.h2d = len(POOL_SWEEP) * self.nb * C * H * W * 2
         self.d2h = sum(self.nb * C * c[12] * c[13] * 2 for c in POOL_SWEEP)
+        self.pipe = CopyOverlap()
+
+    def e2e_start(self, start_event):
+        self.pipe.start(start_event)
 
     def e2e_step(self):
-        from cormorant_b200.runtime import InferenceBuf, run_pool
+        from cormorant_b200.runtime import run_pool
         N, C, H, W = POOL_SHAPE
-        for c in POOL_SWEEP:
+        for i, c in enumerate(POOL_SWEEP):
             _, ph, pw, sh, sw, pt, pl, dh, dw, t, lp, cip, oh, ow = c
-            self.X.sync_to_device()
-            run_pool(self.X, self.Y, self.nb, C, H, W, oh, ow, ph, pw, sh, sw, pt, pl, dh, dw, t, lp, cip)
-            InferenceBuf.init_view(self.Y, 0, self.nb * C * oh * ow).sync_from_device()
+            X, Yv = self.X[i % 2], self.Yv[i][i % 2]
+            self.pipe.call([X], [Yv], lambda s, X=X, Yv=Yv, c=c:
+                           run_pool(X, Yv, self.nb, C, H, W, c[12], c[13], c[1], c[2], c[3], c[4], c[5], c[6], c[7],
+                                    c[8], c[9], c[10], c[11], stream=s))
+
+    def e2e_finish(self):
+        self.pipe.join()
 
     def e2e_release(self):
-        self.X.free()
-        self.Y.free()
+        self.Yv = []
+        for b in self.X + self.Y:
+            b.free()
+        self.X = self.Y = []
+        self.pipe = None
 
 
 class NetworkBench:
@@ -730,7 +785,8 @@ def _cpu_worker(args):
         bufs[net.input][:] = x
         R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
         dt = 0.0
-        for node in net.nodes:
+        reps = 50 if config == "lenet" else 1       # a LeNet-5 inference is ~1 ms of CPU
+        for node in [nd for _ in range(reps) for nd in net.nodes]:
             nk = node[0]
             t0 = time.perf_counter()
             scale = 1.0
@@ -757,7 +813,7 @@ def _cpu_worker(args):
                 _, an, bn, cn, a = node
                 R(cn)[:] = chk.matmul(R(an), R(bn), *a)[: R(cn).size]
             dt += (time.perf_counter() - t0) * scale
-        units = 1.0
+        units = float(reps)
     else:
         N, C, H, W = POOL_SHAPE
         nb, cs = 1, 8
@@ -775,7 +831,7 @@ SAMPLE_TEXT = {
     "matmul": "4 output rows of one batch item per sweep shape per worker process (reference MatmulKernel with n=4)",
     "vectorop": "2^20 elements per op per worker process",
     "pool": "one image x 8 channels of [.,64,112,112] per variant per worker process",
-    "lenet": "one whole LeNet-5 inference (batch 1) per worker process",
+    "lenet": "50 whole LeNet-5 inferences (batch 1) per worker process, kernel time summed per worker",
     "resnet": ("one ResNet-18 image per worker process; each conv layer computes 8 of its output channels "
                "(the reference's TILE_M) and its time is scaled by out_ch / 8; pools and vector ops run in full"),
 }
@@ -795,8 +851,9 @@ def cpu_sample(config: str, workers: int, pool=None):
         pool.join()
     units = sum(r[0] for r in res)
     kind = res[0][2]
-    if config == "resnet":
-        # scaled per-image estimates: the workers run in parallel, each at 1/dt images per second
+    if config in ("resnet", "lenet"):
+        # per-worker rates (kernel time only, summed over the call list; ResNet's conv times are
+        # scaled estimates): the workers run in parallel, each at units/dt images per second
         rate = sum(r[0] / r[1] for r in res)
         return rate, 1.0, kind
     return units, wall, kind
@@ -808,29 +865,279 @@ def cpu_units_to_value(config, units, seconds):
     return units / seconds                 # GB/s (units already in GB) or images/s
 
 
-def int8_peak() -> int:
-    """Library int8 reference point: torch._int_mm (cuBLASLt, s8 x s8 -> s32) at 8192^3."""
+def int8_ceiling(cm, seconds: float = 0.4) -> dict:
+    """The int8 tensor-pipe ceiling of this GPU, measured now (before a GEMM config's timed region):
+    the GEMM's own MMA stream with its operands resident in shared memory (cm_int8_mma_rate, CTA
+    pairs and single CTAs: no memory traffic, so nothing but the pipe bounds it), and cuBLASLt's
+    int8 GEMM (torch._int_mm 8192^3, s8 x s8 -> s32) as a library reference point."""
+    import ctypes as C
     import torch
+    from cormorant_b200 import _lib
+    L = cm.lib()
+    out = {}
+    for pairs, key in ((1, "mma_pairs_tops"), (0, "mma_single_tops")):
+        tops, ms = C.c_double(), C.c_double()
+        _lib.check(L.cm_int8_mma_rate(pairs, 16384, C.byref(tops), C.byref(ms)))
+        out[key] = round(tops.value, 1)
     n = 8192
     a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda")
     b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
-    for _ in range(5):
+    for _ in range(3):
         torch._int_mm(a, b)
     torch.cuda.synchronize()
-    best, tot, it = 1e9, 0.0, 0
-    t_end = time.time() + 4.0
+    best, t_end = 1e9, time.time() + seconds
     while time.time() < t_end:
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
         torch._int_mm(a, b)
-        e.record()
+        e_.record()
         torch.cuda.synchronize()
-        ms = s.elapsed_time(e)
-        best, tot, it = min(best, ms), tot + ms, it + 1
-    ops = 2.0 * n ** 3
-    print(json.dumps({"int8_mm_tops_burst": ops / (best * 1e-3) / 1e12, "int8_mm_tops_sustained": ops / (tot / it * 1e-3) / 1e12,
-                      "iters": it, "how": "torch._int_mm 8192^3 s8xs8->s32, best and mean over 4 s"}))
+        best = min(best, s_.elapsed_time(e_))
+    out["cublaslt_int8_tops"] = round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1)
+    out["ceiling_tops"] = max(out["mma_pairs_tops"], out["mma_single_tops"])
+    del a, b
+    torch.cuda.empty_cache()
+    return out
+
+
+def int8_peak() -> int:
+    """--int8-peak: print the int8 ceiling measurements and exit."""
+    import torch
+    import cormorant_b200 as cm
+    torch.cuda.set_device(0)
+    cm.init("0")
+    print(json.dumps({**int8_ceiling(cm, seconds=4.0),
+                      "how": "cm_int8_mma_rate (the GEMM's MMAs on resident operands; pairs = cta_group::2) and "
+                             "torch._int_mm 8192^3 s8xs8->s32 (best over 4 s)"}))
     return 0
+
+
+# Sub-configs of the default run time more steps than K where one step is short, so that
+# each timed region lasts a few hundred ms (enough nvidia-smi clock samples).
+STEP_MULT = {"matmul": 1, "resnet": 5, "vectorop": 10, "pool": 20, "lenet": 500}
+ALL_CONFIGS = ["matmul", "lenet", "vectorop", "pool", "resnet"]
+
+
+class Env:
+    """Per-process plumbing shared by the configs of one run."""
+
+    def __init__(self, args, world, rank, local, cm, cpool, workers):
+        import torch
+        self.args, self.world, self.rank, self.local = args, world, rank, local
+        self.cm, self.L = cm, cm.lib()
+        self.cpool, self.workers = cpool, workers
+        self.peaks = load_peaks()
+        self.stream = torch.cuda.current_stream()
+        self.cpu_warm = False
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def reduce(self, x: float, op: str) -> float:
+        if self.world == 1:
+            return x
+        import torch
+        import torch.distributed as dist
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+        return float(t.item())
+
+
+def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
+    """One config on every rank: setup, W warm-up steps, K timed steps (barrier + synchronize on both
+    sides, CUDA events, max over ranks), the dominant kernel's roofline, the output gathers (N > 1),
+    the per-part breakdown, the end-to-end run through the reference-facing API and the CPU baseline
+    (rank 0 at N = 1).  Returns rank 0's record (None on other ranks)."""
+    import ctypes as C
+    import torch
+    cm, L, world, rank, stream = env.cm, env.L, env.world, env.rank, env.stream
+    wl = WORKLOADS[name](rank, world)
+    wl.setup()
+    torch.cuda.synchronize()
+    for _ in range(W):
+        wl.step(cm, stream)
+    torch.cuda.synchronize()
+    env.barrier()
+
+    ceiling = int8_ceiling(cm) if wl.dominant == "gemm_q88" and name != "lenet" else None
+    env.barrier()
+    sampler = ClockSampler(gpu_indices(world)) if rank == 0 else None
+    time.sleep(0.3 if sampler else 0.0)
+    env.barrier()
+    torch.cuda.synchronize()
+    lc0 = L.cm_launch_count()
+    L.cm_profile_begin()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for _ in range(K):
+        wl.step(cm, stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    L.cm_profile_end()
+    env.barrier()
+    clocks = sampler.stop() if sampler else None
+    launches = L.cm_launch_count() - lc0
+    elapsed_ms = start.elapsed_time(end)
+    dms, dcnt = C.c_double(), C.c_uint64()
+    L.cm_profile_read(wl.dominant.encode(), C.byref(dms), C.byref(dcnt))
+    dom_note = ""
+    if getattr(wl, "graph", None) is not None and wl.dominant == "gemm_q88" and name != "lenet":
+        # graph replays carry no per-launch events: the GEMM's launch durations come from K
+        # eager passes right after the timed region
+        dms.value, dcnt.value = wl.profile_dominant(cm, stream, K)
+        dom_note = ("; GEMM launch durations from CUDA events around each launch over K eager passes right "
+                    "after the timed region (which replays a CUDA graph)")
+    elapsed_ms = env.reduce(elapsed_ms, "max")
+    ms_per_step = elapsed_ms / K
+    scale = 1e9 if name == "matmul" else 1.0
+    value = wl.units_total / (ms_per_step * 1e-3) / scale
+    if getattr(wl, "graph", None) is not None:
+        launches = wl.launches_per_step * K        # graph replays launch the captured kernels
+    launches_total = int(env.reduce(float(launches), "sum"))
+
+    peaks = env.peaks
+    if name == "lenet":
+        roof = {"bound": "launch", "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
+                "kernel": "whole network, CUDA graph",
+                "note": "0.83 MOPs per image: latency-bound; no roofline fraction (too small)"}
+    elif wl.dominant == "gemm_q88":
+        achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e12 if dms.value > 0 else 0.0
+        which = "bf16_sustained" if elapsed_ms > 1500.0 else "bf16"
+        proxy = 2.0 * peaks[which]
+        peak = ceiling["ceiling_tops"]
+        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"gemm_q88:{name}"),
+                "kernel": "gemm_q88_kernel",
+                "int8_ceiling": ceiling,
+                "int8_measured_tops": ceiling["cublaslt_int8_tops"],
+                "frac_of_cublaslt_int8": round(achieved / ceiling["cublaslt_int8_tops"], 4),
+                "proxy_2x_bf16": round(proxy, 1), "frac_of_proxy": round(achieved / proxy, 4),
+                "note": ("achieved = int8 tensor ops (4 s8 MMAs per Q8.8 multiply-add, 2 ops each) of the GEMM "
+                         "launches / their CUDA-event time on rank 0; peak = the int8 tensor pipe's ceiling "
+                         "measured in this run just before the timed region (cm_int8_mma_rate: the GEMM's MMA "
+                         "stream on shared-memory-resident operands, best of CTA pairs and single CTAs); also "
+                         f"against cuBLASLt's int8 GEMM (a library rate, not a ceiling) and 2 x the {peaks['source']} "
+                         f"bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} rate {peaks[which]} TF/s; "
+                         "traffic = DRAM bytes of "
+                         + ("one 4096^3 x 64 launch" if name == "matmul" else "one layer-1 3x3 conv GEMM launch")
+                         + " (ncu, profiles/)" + dom_note)}
+    else:
+        achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e9 if dms.value > 0 else 0.0
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": profile_traffic(wl.dominant),
+                "kernel": wl.dominant,
+                "note": f"algorithmic bytes / kernel CUDA-event time on rank 0; peak = {peaks['source']} HBM copy rate"}
+
+    gather = measure_gathers(wl, env, ms_per_step, scale) if world > 1 else None
+    per_part = wl.per_part(cm, stream, max(2, min(K, 5))) if (detail and rank == 0) else None
+    wl.release()
+    torch.cuda.empty_cache()
+
+    e2e = None
+    if not env.args.no_e2e:
+        wl.e2e_setup()
+        wl.e2e_step()                      # warm-up pass
+        if hasattr(wl, "e2e_finish"):
+            wl.e2e_finish()
+        torch.cuda.synchronize()
+        env.barrier()
+        e_steps = K if name in ("lenet", "resnet") else max(1, min(K, 3))
+        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        es.record()
+        if hasattr(wl, "e2e_start"):
+            wl.e2e_start(es)
+        for _ in range(e_steps):
+            wl.e2e_step()
+        if hasattr(wl, "e2e_finish"):
+            wl.e2e_finish()
+        ee.record()
+        torch.cuda.synchronize()
+        e_ms = env.reduce(es.elapsed_time(ee) / e_steps, "max")
+        e2e = {"value": wl.units_total / (e_ms * 1e-3) / scale, "unit": wl.unit, "ms_per_step": e_ms,
+               "steps": e_steps,
+               "h2d_bytes_per_step": int(env.reduce(float(wl.h2d), "sum")),
+               "d2h_bytes_per_step": int(env.reduce(float(wl.d2h), "sum")),
+               "path": getattr(wl, "e2e_path", "cm_buf_sync_to_device -> run_* (cm_* C ABI) -> "
+                                                "cm_buf_sync_from_device, pinned host mirrors")}
+        wl.e2e_release()
+        torch.cuda.empty_cache()
+
+    cpu_line = None
+    if env.cpool is not None:
+        if not env.cpu_warm:
+            cpu_sample(name, env.workers, env.cpool)     # warm: the workers load the reference kernels
+            env.cpu_warm = True
+        u, sec, kind = cpu_sample(name, env.workers, env.cpool)
+        cpu_line = {"value": cpu_units_to_value(name, u, sec), "unit": wl.unit, "cores": env.workers, "kind": kind,
+                    "sample": SAMPLE_TEXT[name] + f"; {sec:.1f} s wall on {env.workers} processes"}
+    if rank != 0:
+        return None
+    rec = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": K, "warmup": W,
+           "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+           "dtype": "q8.8 int16 (ap_fixed<16,8>); s8 tcgen05 MMA, s32 accumulate"
+           if wl.dominant == "gemm_q88" and name != "lenet" else "q8.8 int16 (ap_fixed<16,8>), int32 / IEEE f32 epilogue",
+           "data": "synthetic (seeded)", "config": wl.config(world), "roofline": roof,
+           "cpu_baseline": cpu_line, "e2e": e2e, "gpu_launches": launches_total, "clocks": clocks}
+    if gather is not None:
+        rec["gather"] = gather
+    if per_part is not None:
+        rec["per_part"] = per_part
+    return rec
+
+
+def measure_gathers(wl, env: Env, ms_per_step: float, scale: float) -> dict | None:
+    """N > 1: the outputs stay sharded in `value`.  A caller that wants them together adds, per step,
+    either a gather to rank 0 (every rank sends its shard, rank 0 receives each into its offset) or an
+    all-gather to every rank, both over NCCL (NVLink / NVSwitch).  Each is timed on the device over one
+    step's outputs (max over ranks) after a warm-up pass."""
+    import torch
+    from cormorant_b200 import sharding
+    spec = wl.gather_outputs() if hasattr(wl, "gather_outputs") else []
+    if not spec:
+        return None
+    world, rank, stream = env.world, env.rank, env.stream
+    res = {}
+    for kind in ("to_root", "all_gather"):
+        outs = []
+        for t, total, per_item in spec:
+            if kind == "to_root":
+                outs.append(torch.empty(total * per_item, dtype=torch.int16, device="cuda") if rank == 0 else None)
+            else:
+                outs.append(torch.empty(total * per_item, dtype=torch.int16, device="cuda"))
+
+        def run():
+            for (t, total, per_item), o in zip(spec, outs):
+                if kind == "to_root":
+                    sharding.gather_to_root(t, total, per_item, root=0, out=o)
+                else:
+                    sharding.gather_batches(t, total, per_item, out=o)
+        run()                                           # warm the communicators
+        torch.cuda.synchronize()
+        env.barrier()
+        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        gs.record(stream)
+        run()
+        ge.record(stream)
+        torch.cuda.synchronize()
+        g_ms = env.reduce(gs.elapsed_time(ge), "max")
+        full_bytes = sum(total * per_item * 2 for _, total, per_item in spec)
+        # bytes that cross NVLink into one receiving GPU: every shard but its own
+        ingress = sum((total - sharding.shard_range(total, 0, world)[1]) * per_item * 2 for _, total, per_item in spec)
+        res[kind] = {"ms_per_step": g_ms, "bytes_per_step": full_bytes, "ingress_bytes_per_gpu": ingress,
+                     "ingress_gbs": round(ingress / (g_ms * 1e-3) / 1e9, 1) if g_ms > 0 else None,
+                     "value_with_gather": wl.units_total / ((ms_per_step + g_ms) * 1e-3) / scale}
+        del outs
+        torch.cuda.empty_cache()
+        env.barrier()
+    res["unit"] = wl.unit
+    res["note"] = ("to_root: every rank sends its shard of one step's outputs and rank 0 receives each straight into "
+                   "its offset (NCCL grouped send/recv); all_gather: every output to every rank "
+                   "(all_gather_into_tensor into a preallocated output); value_with_gather = units / (ms_per_step + "
+                   "gather ms), gather not overlapped; one GPU's NVLink ingress bounds both, so neither scales with N")
+    return res
 
 
 # --------------------------------------------------------------------------------------
@@ -840,7 +1147,9 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", choices=sorted(WORKLOADS), default="matmul")
+    ap.add_argument("--config", choices=["all"] + sorted(WORKLOADS), default="all",
+                    help="all (default): the MatMul sweep as the headline line plus every BASELINE config in "
+                         "'configs'; or one config alone")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-workers", type=int, default=0)
@@ -858,7 +1167,7 @@ def main():
     ap.add_argument("--no-planes", action="store_true",
                     help="resnet: no plane images between convs (each conv splits its NCHW input)")
     ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
-    ap.add_argument("--int8-peak", action="store_true", help="measure cuBLASLt int8 GEMM (torch._int_mm) and exit")
+    ap.add_argument("--int8-peak", action="store_true", help="measure the int8 ceilings (MMA stream, cuBLASLt) and exit")
     args = ap.parse_args()
     global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH, GRAPH, PREPARED
     UNFUSED = args.unfused
@@ -871,6 +1180,9 @@ def main():
         return int8_peak()
     if args.shape:
         MatmulSweep.sweep = [tuple(int(v) for v in args.shape.split(","))]
+        if args.config == "all":
+            args.config = "matmul"
+    names = ALL_CONFIGS if args.config == "all" else [args.config]
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -882,27 +1194,34 @@ def main():
     if args.impl == "reference":
         if rank != 0:
             return 0
-        wl = WORKLOADS[args.config](0, 1)
         import multiprocessing as mp
         pool = mp.get_context("spawn").Pool(workers)
-        for _ in range(W):
-            cpu_sample(args.config, workers, pool)
-        vals, kind = [], "port"
-        t_all = 0.0
-        for _ in range(K):
-            u, s, kind = cpu_sample(args.config, workers, pool)
-            vals.append(cpu_units_to_value(args.config, u, s))
-            t_all += s
+        recs = {}
+        for i, name in enumerate(names):
+            wl = WORKLOADS[name](0, 1)
+            # the headline config takes W + K samples; the others 1 + 3 (a ResNet sample is ~10 s of CPU)
+            w_, k_ = (W, K) if i == 0 else (1, 3)
+            for _ in range(w_):
+                cpu_sample(name, workers, pool)
+            vals, kind, t_all = [], "port", 0.0
+            for _ in range(k_):
+                u, sec, kind = cpu_sample(name, workers, pool)
+                vals.append(cpu_units_to_value(name, u, sec))
+                t_all += sec
+            v = statistics.median(vals)
+            recs[name] = {"impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": args.gpus,
+                          "steps": k_, "warmup": w_, "ms_per_step": t_all / k_ * 1e3, "higher_is_better": True,
+                          "scaling": "strong", "vs_baseline": None,
+                          "dtype": "ap_fixed<16,8> C-simulation on host cores",
+                          "data": "synthetic", "config": wl.config(1),
+                          "cpu_baseline": {"value": v, "unit": wl.unit, "cores": workers, "kind": kind,
+                                           "sample": SAMPLE_TEXT[name]},
+                          "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
         pool.close()
         pool.join()
-        v = statistics.median(vals)
-        line = {"impl": "reference", "metric": wl.metric, "value": v, "unit": wl.unit, "n_gpus": args.gpus,
-                "steps": K, "warmup": W, "ms_per_step": t_all / K * 1e3, "higher_is_better": True,
-                "scaling": "strong", "vs_baseline": None, "dtype": "ap_fixed<16,8> C-simulation on host cores",
-                "data": "synthetic", "config": wl.config(1),
-                "cpu_baseline": {"value": v, "unit": wl.unit, "cores": workers, "kind": kind,
-                                 "sample": SAMPLE_TEXT[args.config]},
-                "e2e": {"value": v, "unit": wl.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+        line = dict(recs[names[0]])
+        if len(names) > 1:
+            line["configs"] = recs
         print(json.dumps(line))
         return 0
 
@@ -915,184 +1234,27 @@ def main():
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device(f"cuda:{local}"))
     import cormorant_b200 as cm
     cm.init(str(local))
-    L = cm.lib()
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
-
-    def max_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
-
-    def sum_over_ranks(x: float) -> float:
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
 
     # The CPU baseline pool is spawned before heavy GPU work (rank 0, N = 1 only).
-    cpu_line = None
-    want_cpu = (rank == 0 and world == 1 and not args.no_cpu_baseline)
     cpool = None
-    if want_cpu:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import multiprocessing as mp
         cpool = mp.get_context("spawn").Pool(workers)
-
-    wl = WORKLOADS[args.config](rank, world)
-    wl.setup()
-    stream = torch.cuda.current_stream()
-    torch.cuda.synchronize()
-    for _ in range(W):
-        wl.step(cm, stream)
-    torch.cuda.synchronize()
-    barrier()
-
-    sampler = ClockSampler(gpu_indices(world)) if rank == 0 else None
-    time.sleep(0.3 if sampler else 0.0)
-    barrier()
-    torch.cuda.synchronize()
-    lc0 = L.cm_launch_count()
-    L.cm_profile_begin()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    start.record(stream)
-    for _ in range(K):
-        wl.step(cm, stream)
-    end.record(stream)
-    torch.cuda.synchronize()
-    L.cm_profile_end()
-    barrier()
-    clocks = sampler.stop() if sampler else None
-    launches = L.cm_launch_count() - lc0
-    elapsed_ms = start.elapsed_time(end)
-    import ctypes as C
-    dms, dcnt = C.c_double(), C.c_uint64()
-    L.cm_profile_read(wl.dominant.encode(), C.byref(dms), C.byref(dcnt))
-    dom_note = ""
-    if getattr(wl, "graph", None) is not None and wl.dominant == "gemm_q88":
-        # graph replays carry no per-launch events: the GEMM's launch durations come from K
-        # eager passes right after the timed region
-        dms.value, dcnt.value = wl.profile_dominant(cm, stream, K)
-        dom_note = ("; GEMM launch durations from CUDA events around each launch over K eager passes right "
-                    "after the timed region (which replays a CUDA graph)")
-    dom_ms = max_over_ranks(dms.value)
-    elapsed_ms = max_over_ranks(elapsed_ms)
-    ms_per_step = elapsed_ms / K
-    value = wl.units_total / (ms_per_step * 1e-3)
-    if args.config == "matmul":
-        value /= 1e9
-    if getattr(wl, "graph", None) is not None:
-        launches = wl.launches_per_step * K        # graph replays launch the captured kernels
-    launches_total = int(sum_over_ranks(float(launches)))
-
-    peaks = load_peaks()
-    # achieved on the dominant kernel (rank 0): algorithmic units of all its launches / their device time
-    if args.config == "lenet":
-        roof = {"bound": "launch", "achieved": None, "peak": None, "unit": None, "frac": None, "traffic": None,
-                "kernel": "whole network, CUDA graph",
-                "note": "0.83 MOPs per image: latency-bound; no roofline fraction (too small)"}
-    elif wl.dominant == "gemm_q88":
-        achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e12 if dms.value > 0 else 0.0
-        # burst figure for a timed region of about a second or less, sustained beyond
-        which = "bf16_sustained" if elapsed_ms > 1500.0 else "bf16"
-        peak = 2.0 * peaks[which]
-        roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TFLOP/s",
-                "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"gemm_q88:{args.config}"),
-                "kernel": "gemm_q88_kernel",
-                "note": (f"int8 tensor ops (4 s8 MMAs per Q8.8 MAC, x2 ops per MAC) per second on rank 0; peak = "
-                         f"2 x {peaks['source']} bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} "
-                         f"{peaks[which]} TF/s (dense int8 rate is twice bf16 on B200); traffic = DRAM bytes of "
-                         + ("one 4096^3 x 64 launch" if args.config == "matmul" else "one layer-1 3x3 conv GEMM launch")
-                         + " (ncu, profiles/)" + dom_note)}
-    else:
-        achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e9 if dms.value > 0 else 0.0
-        peak = peaks["hbm_gbs"]
-        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": profile_traffic(wl.dominant),
-                "kernel": wl.dominant, "note": f"algorithmic bytes / kernel time on rank 0; of {peaks['source']}"}
-
-    # N > 1: the outputs stay sharded in `value`; end to end, a caller that wants every
-    # output on every GPU adds one NCCL all-gather of them per step (NVLink / NVSwitch)
-    gather = None
-    gspec = wl.gather_outputs() if (world > 1 and hasattr(wl, "gather_outputs")) else []
-    if gspec:
-        from cormorant_b200 import sharding
-        gather_bytes = 0
-        for t, total, per_item in gspec:                # warm the collectives once
-            sharding.gather_batches(t, total, per_item)
-        torch.cuda.synchronize()
-        barrier()
-        gs, ge = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        gs.record(stream)
-        for t, total, per_item in gspec:
-            full = sharding.gather_batches(t, total, per_item)
-            gather_bytes += full.numel() * 2
-            del full
-        ge.record(stream)
-        torch.cuda.synchronize()
-        g_ms = max_over_ranks(gs.elapsed_time(ge))
-        gv = wl.units_total / ((ms_per_step + g_ms) * 1e-3)
-        if args.config == "matmul":
-            gv /= 1e9
-        gather = {"ms_per_step": g_ms, "bytes_per_step": gather_bytes, "value_with_gather": gv, "unit": wl.unit,
-                  "note": "every output of one step all-gathered to every rank (NCCL all_gather over NVLink / "
-                          "NVSwitch, max over ranks); value_with_gather = units / (ms_per_step + gather ms); "
-                          "gathering to every GPU is bound by each GPU's NVLink ingress, so it does not scale "
-                          "with N"}
-        torch.cuda.empty_cache()
-    per_part = wl.per_part(cm, stream, max(2, min(K, 5))) if (args.per_part and rank == 0) else None
-    wl.release()
-    torch.cuda.empty_cache()
-
-    e2e = None
-    if not args.no_e2e:
-        wl.e2e_setup()
-        wl.e2e_step()                      # warm-up pass
-        torch.cuda.synchronize()
-        barrier()
-        e_steps = K if args.config in ("lenet", "resnet") else max(1, min(K, 3))
-        es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        es.record()
-        if hasattr(wl, "e2e_start"):
-            wl.e2e_start(es)
-        for _ in range(e_steps):
-            wl.e2e_step()
-        ee.record()
-        torch.cuda.synchronize()
-        e_ms = max_over_ranks(es.elapsed_time(ee) / e_steps)
-        ev = wl.units_total / (e_ms * 1e-3)
-        if args.config == "matmul":
-            ev /= 1e9
-        e2e = {"value": ev, "unit": wl.unit, "ms_per_step": e_ms,
-               "h2d_bytes_per_step": int(sum_over_ranks(float(wl.h2d))),
-               "d2h_bytes_per_step": int(sum_over_ranks(float(wl.d2h))),
-               "path": getattr(wl, "e2e_path", "cm_buf_sync_to_device -> run_* (cm_* C ABI) -> cm_buf_sync_from_device, "
-                                                "pinned host mirrors")}
-        wl.e2e_release()
-
-    if want_cpu:
-        cpu_sample(args.config, workers, cpool)     # warm
-        u, s, kind = cpu_sample(args.config, workers, cpool)
+    env = Env(args, world, rank, local, cm, cpool, workers)
+    recs = {}
+    for i, name in enumerate(names):
+        mult = 1 if i == 0 or len(names) == 1 else STEP_MULT[name]
+        if name == "lenet" and len(names) == 1:
+            mult = STEP_MULT["lenet"]
+        recs[name] = measure(name, env, K * mult, W, detail=args.per_part or len(names) > 1)
+        env.barrier()
+    if cpool is not None:
         cpool.close()
         cpool.join()
-        cpu_line = {"value": cpu_units_to_value(args.config, u, s), "unit": wl.unit, "cores": workers, "kind": kind,
-                    "sample": SAMPLE_TEXT[args.config] + f"; {s:.1f} s wall on {workers} processes"}
-
     if rank == 0:
-        line = {"metric": wl.metric, "value": value, "unit": wl.unit, "n_gpus": world, "steps": K, "warmup": W,
-                "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-                "dtype": "q8.8 int16 (ap_fixed<16,8>); s8 tcgen05 MMA, s32 accumulate"
-                if wl.dominant == "gemm_q88" else "q8.8 int16 (ap_fixed<16,8>), int32 / IEEE f32 epilogue",
-                "data": "synthetic (seeded)", "config": wl.config(world), "roofline": roof,
-                "cpu_baseline": cpu_line, "e2e": e2e, "gpu_launches": launches_total, "clocks": clocks}
-        if gather is not None:
-            line["gather"] = gather
-        if per_part is not None:
-            line["per_part"] = per_part
+        line = dict(recs[names[0]])
+        if len(names) > 1:
+            line["configs"] = {n: recs[n] for n in names}
         print(json.dumps(line))
     if world > 1:
         dist.barrier()

@@ -33,6 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_set_direct_limit": (C.c_uint64, [C.c_uint64]),
     "cm_version": (C.c_char_p, []),
     "cm_selftest_wait_timeout": (C.c_int, [_u]),
+    "cm_int8_mma_rate": (C.c_int, [_u, _u, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "cm_profile_begin": (C.c_int, []),
     "cm_profile_end": (C.c_int, []),
     "cm_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
@@ -76,6 +77,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_buf_init_view": (None, [_p, _p, _u, _u]),
     "cm_buf_sync_to_device": (C.c_int, [_p]),
     "cm_buf_sync_from_device": (C.c_int, [_p]),
+    "cm_buf_sync_to_device_async": (C.c_int, [_p, _p]),
+    "cm_buf_sync_from_device_async": (C.c_int, [_p, _p]),
 }
 
 

@@ -871,6 +871,93 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
 }
 
 // ---------------------------------------------------------------------------
+// int8 tensor-pipe rate (a measurement; no reference counterpart)
+// ---------------------------------------------------------------------------
+// The GEMM's main loop with the operand traffic taken away: every CTA (CG = 1) or
+// CTA pair (CG = 2) issues `iters` rounds of the same MMAs on one operand stage that
+// stays in shared memory (hashed bytes, so the data are not trivially zero), into
+// the same TMEM accumulators.  The rate reached is the int8 tensor pipe's own
+// ceiling at the clocks of the moment: the denominator of the GEMM's roofline.
+template <int CG>
+__global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* status, uint64_t timeout_ns) {
+    using C = Cfg<128, CG>;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* done_b = (uint64_t*)(smem + C::STAGE);
+    volatile uint32_t* tmem_slot = (volatile uint32_t*)(done_b + 1);
+    volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+    const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
+    for (uint32_t i = threadIdx.x; i < (uint32_t)C::STAGE / 4; i += blockDim.x) {
+        uint32_t x = (i + 1u) * 0x9E3779B1u ^ (blockIdx.x * 0x85EBCA77u);
+        x ^= x >> 15;
+        x *= 0x2C1B3C6Du;
+        x ^= x >> 12;
+        ((uint32_t*)smem)[i] = x;
+    }
+    // the operand bytes were written through the generic proxy; the MMAs read them
+    // through the async proxy
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(done_b), 1);
+        *abort_flag = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 1) {
+        if (CG == 2) {
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32((const void*)tmem_slot)),
+                         "r"(TMEM_COLS)
+                         : "memory");
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+        }
+        tc_fence_before();
+    }
+    __syncthreads();
+    if (CG == 2) cluster_sync_all();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    if (warp == 0 && lane == 0 && rank == 0) {
+        const uint32_t a0 = smem_u32(smem), b0 = a0 + OPERAND_TILE;
+        for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+            for (uint32_t kk = 0; kk < BK / 32; ++kk) {
+                const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
+                const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);
+                const uint32_t acc = (it | kk) != 0u;
+                if (CG == 2) {
+                    umma_i8_pair(tmem, ah, bhl, C::IDESC, acc);
+                    umma_i8_pair(tmem + 256, al, bhl, C::IDESC, acc);
+                } else {
+                    umma_i8(tmem, ah, bhl, C::IDESC, acc);
+                    umma_i8(tmem + 256, al, bhl, C::IDESC, acc);
+                }
+            }
+        }
+        // arrives on `done` in both CTAs of a pair once every MMA above has completed
+        if (CG == 2) umma_commit_pair(smem_u32(done_b), 0x3);
+        else umma_commit(smem_u32(done_b));
+    }
+    if (threadIdx.x == 0) {
+        const WaitCtl wc{abort_flag, status, timeout_ns};
+        mbar_wait(smem_u32(done_b), 0, wc);
+    }
+    __syncthreads();
+    if (CG == 2) cluster_sync_all();
+    if (warp == 1) {
+        tc_fence_after();
+        if (CG == 2)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
 // split pre-passes
 // ---------------------------------------------------------------------------
 
@@ -1565,6 +1652,19 @@ int noalloc_scratch(int device, void** out) {
 // One batch-step range [bi0, bi0 + nb) of a matmul, all scratch in `base`.
 int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_t* b, int16_t* c, uint32_t n,
                 uint32_t k, uint32_t m, uint32_t nb, uint32_t a_bs, uint32_t b_bs, uint64_t c_bs, cudaStream_t s) {
+    const unsigned __int128 macs = (unsigned __int128)nb * n * m * k;
+    if (macs <= cx->direct_max_macs) {
+        // launch-bound sizes: the one-kernel CUDA-core path, which needs no scratch at all
+        const uint64_t total = (uint64_t)nb * n * m;
+        {
+            ProfScope ps_(PK_GEMM, s);
+            const uint32_t G = direct_lanes(cx, total, k);
+            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(a, b, c, n, k, m, a_bs, b_bs, c_bs,
+                                                                                 total, G, 0u, nullptr);
+        }
+        count_launch();
+        return CM_OK;
+    }
     const uint32_t a_batches = a_bs == 0 ? 1u : nb;
     const uint32_t b_batches = b_bs == 0 ? 1u : nb;
     const uint64_t K_pad = pad_k(k);
@@ -1628,4 +1728,64 @@ extern "C" int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, 
                             unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride) {
     return cm_matmul(a ? a + a_off : a, b ? b + b_off : b, c ? c + c_off : c, n, k, m, batch, a_batch_stride,
                      b_batch_stride, c_batch_stride);
+}
+
+// ---------------------------------------------------------------------------
+// cm_int8_mma_rate: the int8 tensor pipe's ceiling, measured (no reference counterpart)
+// ---------------------------------------------------------------------------
+extern "C" int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!tops || !ms) return set_error(CM_EINVAL, "cm_int8_mma_rate: null output");
+    if (iters == 0 || iters > (1u << 16)) return set_error(CM_EINVAL, "cm_int8_mma_rate: iters 1..65536");
+    if (pairs > 1) return set_error(CM_EINVAL, "cm_int8_mma_rate: pairs is 0 or 1");
+    const int CG = pairs ? 2 : 1;
+    const void* fn = pairs ? (const void*)mma_rate_kernel<2> : (const void*)mma_rate_kernel<1>;
+    // the whole per-CTA shared memory, so that one CTA runs per SM, as in the GEMM
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(mma rate)");
+    int ctas = cx->sm_count;
+    cudaLaunchConfig_t q{};
+    q.blockDim = dim3(128);
+    q.dynamicSmemBytes = SMEM_BYTES;
+    cudaLaunchAttribute at{};
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+    q.attrs = &at; q.numAttrs = 1;
+    if (CG == 2) {
+        q.gridDim = dim3(cx->sm_count);
+        int m = 0;
+        if (cudaOccupancyMaxActiveClusters(&m, (void*)fn, &q) == cudaSuccess && m > 0) ctas = 2 * m;
+        else ctas = cx->sm_count & ~1;
+        cudaGetLastError();
+    }
+    q.gridDim = dim3(ctas);
+    cudaStream_t s = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if ((e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking)) != cudaSuccess) return cuda_error(e, "stream");
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    q.stream = s;
+    // one untimed launch (module load, clocks up), then the timed one
+    for (int pass = 0; pass < 2 && !rc; ++pass) {
+        if (pass == 1) cudaEventRecord(e0, s);
+        e = pairs ? cudaLaunchKernelEx(&q, mma_rate_kernel<2>, iters, cx->status, cx->timeout_ns)
+                  : cudaLaunchKernelEx(&q, mma_rate_kernel<1>, iters, cx->status, cx->timeout_ns);
+        count_launch();
+        if (e != cudaSuccess) rc = cuda_error(e, "mma rate launch");
+    }
+    cudaEventRecord(e1, s);
+    if (!rc) rc = finish_sync((cm_stream_t)s);
+    float t = 0.f;
+    if (!rc && (e = cudaEventElapsedTime(&t, e0, e1)) != cudaSuccess) rc = cuda_error(e, "mma rate events");
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(s);
+    if (rc) return rc;
+    // per CTA and round: 4 K steps x 2 MMAs x 128 rows x 256 columns x 32 deep, 2 ops per MAC
+    const double ops = (double)ctas * iters * 4.0 * 2.0 * 128.0 * 256.0 * 32.0 * 2.0;
+    *ms = t;
+    *tops = t > 0.f ? ops / (t * 1e-3) / 1e12 : 0.0;
+    return CM_OK;
 }

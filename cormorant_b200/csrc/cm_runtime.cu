@@ -311,4 +311,20 @@ int cm_buf_sync_from_device(cm_buf_t* b) {
     return e == cudaSuccess ? CM_OK : cuda_error(e, "sync_from_device");
 }
 
+int cm_buf_sync_to_device_async(cm_buf_t* b, cm_stream_t stream) {
+    if (!b) return set_error(CM_EINVAL, "null buffer");
+    cudaSetDevice(b->device);
+    cudaError_t e = cudaMemcpyAsync((void*)(uintptr_t)b->dev, b->virt, (size_t)b->count * 2, cudaMemcpyHostToDevice,
+                                    (cudaStream_t)stream);
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "sync_to_device_async");
+}
+
+int cm_buf_sync_from_device_async(cm_buf_t* b, cm_stream_t stream) {
+    if (!b) return set_error(CM_EINVAL, "null buffer");
+    cudaSetDevice(b->device);
+    cudaError_t e = cudaMemcpyAsync(b->virt, (void*)(uintptr_t)b->dev, (size_t)b->count * 2, cudaMemcpyDeviceToHost,
+                                    (cudaStream_t)stream);
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "sync_from_device_async");
+}
+
 }  // extern "C"

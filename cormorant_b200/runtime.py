@@ -9,7 +9,8 @@ reference programs the DMA physical address); views alias a slice of an owner.
 mirror the static helpers the reference code generator emits
 (_source.py:174-421): same names, same argument order, blocking until the
 kernel is done.  They raise ``CormorantError`` where the reference helpers
-(void) had no error path.
+(void) had no error path.  An optional trailing ``stream`` enqueues the call on
+that CUDA stream instead (the ``_async`` entry) and returns at once.
 """
 from __future__ import annotations
 
@@ -65,11 +66,21 @@ class InferenceBuf:
     def count(self) -> int:
         return int(self._p.contents.count)
 
-    def sync_to_device(self) -> None:
-        check(lib().cm_buf_sync_to_device(self._p))
+    def sync_to_device(self, stream=None) -> None:
+        """Host mirror -> device.  With `stream` (a torch.cuda.Stream or a raw cudaStream_t
+        address) the copy is enqueued there and the call returns at once."""
+        if stream is None:
+            check(lib().cm_buf_sync_to_device(self._p))
+        else:
+            check(lib().cm_buf_sync_to_device_async(self._p, _stream_ptr(stream)))
 
-    def sync_from_device(self) -> None:
-        check(lib().cm_buf_sync_from_device(self._p))
+    def sync_from_device(self, stream=None) -> None:
+        """Device -> host mirror; with `stream`, enqueued there (read the mirror after the
+        stream has reached it)."""
+        if stream is None:
+            check(lib().cm_buf_sync_from_device(self._p))
+        else:
+            check(lib().cm_buf_sync_from_device_async(self._p, _stream_ptr(stream)))
 
     def retain(self) -> None:
         lib().cm_buf_retain(self._p)
@@ -83,31 +94,105 @@ class InferenceBuf:
         self._p = None
 
 
+def _stream_ptr(stream) -> int:
+    return int(getattr(stream, "cuda_stream", stream) or 0)
+
+
 def _dev(buf: InferenceBuf | None, off: int = 0) -> int | None:
     return None if buf is None else buf.phys() + off * InferenceBuf.BYTES_PER_ELEM
 
 
-def run_op(a, b, c, size, op, outer, a_inc, b_inc) -> None:
-    check(lib().cm_vectorop(_dev(a), _dev(b), _dev(c), size, op, outer, a_inc, b_inc))
+def run_op(a, b, c, size, op, outer, a_inc, b_inc, stream=None) -> None:
+    args = (_dev(a), _dev(b), _dev(c), size, op, outer, a_inc, b_inc)
+    check(lib().cm_vectorop(*args) if stream is None else lib().cm_vectorop_async(*args, _stream_ptr(stream)))
 
 
-def run_matmul(a, b, c, n, k, m, batch, a_stride, b_stride, c_stride) -> None:
-    check(lib().cm_matmul(_dev(a), _dev(b), _dev(c), n, k, m, batch, a_stride, b_stride, c_stride))
+def run_matmul(a, b, c, n, k, m, batch, a_stride, b_stride, c_stride, stream=None) -> None:
+    args = (_dev(a), _dev(b), _dev(c), n, k, m, batch, a_stride, b_stride, c_stride)
+    check(lib().cm_matmul(*args) if stream is None else lib().cm_matmul_async(*args, _stream_ptr(stream)))
 
 
-def run_matmul_at(a, a_off, b, b_off, c, c_off, n, k, m, batch, a_stride, b_stride, c_stride) -> None:
-    check(lib().cm_matmul(_dev(a, a_off), _dev(b, b_off), _dev(c, c_off), n, k, m, batch, a_stride, b_stride,
-                          c_stride))
+def run_matmul_at(a, a_off, b, b_off, c, c_off, n, k, m, batch, a_stride, b_stride, c_stride, stream=None) -> None:
+    args = (_dev(a, a_off), _dev(b, b_off), _dev(c, c_off), n, k, m, batch, a_stride, b_stride, c_stride)
+    check(lib().cm_matmul(*args) if stream is None else lib().cm_matmul_async(*args, _stream_ptr(stream)))
 
 
 def run_conv(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
-             dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise) -> None:
-    check(lib().cm_conv(_dev(x), _dev(weight), _dev(bias), _dev(y), batch, in_ch, in_h, in_w, out_ch, out_h, out_w,
-                        kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias,
-                        is_depthwise))
+             dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, stream=None) -> None:
+    args = (_dev(x), _dev(weight), _dev(bias), _dev(y), batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
+            stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise)
+    check(lib().cm_conv(*args) if stream is None else lib().cm_conv_async(*args, _stream_ptr(stream)))
 
 
 def run_pool(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w, pad_top,
-             pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad) -> None:
-    check(lib().cm_pool(_dev(x), _dev(y), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
-                        stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad))
+             pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad, stream=None) -> None:
+    args = (_dev(x), _dev(y), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+            pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
+    check(lib().cm_pool(*args) if stream is None else lib().cm_pool_async(*args, _stream_ptr(stream)))
+
+
+class CopyOverlap:
+    """Runs calls shaped like the reference's inference_run() -- copy the inputs to
+    the device, run the kernel, copy the outputs back (_source.py:643-791) -- with
+    the copies of one call overlapping the kernels of the others.
+
+    Input copies go on an upload stream and output copies on a download stream
+    (host-to-device and device-to-host use separate copy engines), kernels run on
+    the caller's stream, and CUDA events order every reuse of a buffer: an upload
+    into a buffer waits for the last kernel that read it, a kernel writing a buffer
+    waits for the last download of it.  Calls whose buffers are distinct overlap;
+    calls that share a buffer are ordered.  Buffers are ``InferenceBuf`` objects; views
+    of one owner count as that owner.
+    """
+
+    @staticmethod
+    def _key(b) -> int:
+        return id(b._keep) if b._keep is not None else id(b)
+
+    def __init__(self):
+        import torch
+        self._torch = torch
+        self.up = torch.cuda.Stream()
+        self.down = torch.cuda.Stream()
+        self._read = {}      # buffer -> event of the last kernel that read it
+        self._drained = {}   # buffer -> event of the last download of it
+
+    def start(self, event) -> None:
+        """Copies issued from now on start no earlier than `event` (a recorded CUDA event)."""
+        self.up.wait_event(event)
+        self.down.wait_event(event)
+
+    def call(self, inputs, outputs, run) -> None:
+        """Upload `inputs`, then `run(stream)` on the current stream, then download `outputs`."""
+        torch = self._torch
+        cur = torch.cuda.current_stream()
+        for b in inputs:
+            ev = self._read.get(self._key(b))
+            if ev is not None:
+                self.up.wait_event(ev)
+            b.sync_to_device(self.up)
+        up_done = torch.cuda.Event()
+        up_done.record(self.up)
+        cur.wait_event(up_done)
+        for b in outputs:
+            ev = self._drained.get(self._key(b))
+            if ev is not None:
+                cur.wait_event(ev)
+        run(cur)
+        ran = torch.cuda.Event()
+        ran.record(cur)
+        for b in inputs:
+            self._read[self._key(b)] = ran
+        self.down.wait_event(ran)
+        for b in outputs:
+            b.sync_from_device(self.down)
+        down_done = torch.cuda.Event()
+        down_done.record(self.down)
+        for b in outputs:
+            self._drained[self._key(b)] = down_done
+
+    def join(self) -> None:
+        """Make the current stream wait for every copy issued so far."""
+        cur = self._torch.cuda.current_stream()
+        cur.wait_stream(self.up)
+        cur.wait_stream(self.down)

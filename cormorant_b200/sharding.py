@@ -2,9 +2,11 @@
 
 Every Cormorant kernel call is independent per batch item (per image, per
 batched-GEMM slice; VectorOP per element range), so ranks take contiguous
-shards and run with no communication.  Only when a caller needs the whole
-output on every rank is it gathered, over NCCL (NVLink/NVSwitch) on GPUs or
-gloo on CPU.
+shards and run with no communication.  Only when a caller needs the outputs
+together are they gathered: to every rank (``gather_batches``, an all-gather)
+or to one rank (``gather_to_root``: every other rank sends its shard and the
+root receives each into its offset of the full output, one grouped set of
+point-to-point transfers), over NCCL (NVLink / NVSwitch) on GPUs or gloo on CPU.
 """
 from __future__ import annotations
 
@@ -18,25 +20,87 @@ def shard_range(total: int, rank: int, world: int) -> tuple[int, int]:
     return lo, hi - lo
 
 
-def gather_batches(local, total: int, per_item: int, group=None):
+def _bytes(t):
+    # neither NCCL nor gloo has an int16 type; the gathers only move bytes
+    import torch
+    return t.reshape(-1).view(torch.uint8)
+
+
+def _check_local(local, total, per_item, rank, world):
+    lo, cnt = shard_range(total, rank, world)
+    if local.numel() != cnt * per_item:
+        raise ValueError(f"rank {rank}: expected {cnt * per_item} words, got {local.numel()}")
+    return lo, cnt
+
+
+def gather_batches(local, total: int, per_item: int, group=None, out=None):
     """All-gather rank shards of a [count * per_item] tensor into the full [total * per_item] tensor.
 
-    Shards may differ in length by one item; they are padded to the largest shard for the
-    collective and trimmed afterwards.  Returns the full tensor on every rank.
+    Equal shards (total divisible by the world size) are gathered straight into `out`
+    (allocated if not given) by one all-gather; unequal ones are padded to the largest
+    shard for the collective and trimmed.  Returns the full tensor on every rank.
     """
     import torch
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    _check_local(local, total, per_item, rank, world)
+    if out is None:
+        out = torch.empty(total * per_item, dtype=local.dtype, device=local.device)
+    elif out.numel() != total * per_item or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous tensor of {total * per_item} words")
+    if total % world == 0:
+        dist.all_gather_into_tensor(_bytes(out), _bytes(local.contiguous()), group=group)
+        return out
     counts = [shard_range(total, r, world)[1] for r in range(world)]
     cmax = max(counts)
-    rank = dist.get_rank(group)
-    if local.numel() != counts[rank] * per_item:
-        raise ValueError(f"rank {rank}: expected {counts[rank] * per_item} words, got {local.numel()}")
     padded = torch.zeros(cmax * per_item, dtype=local.dtype, device=local.device)
     padded[: local.numel()] = local.reshape(-1)
-    # neither NCCL nor gloo has an int16 type; an all-gather only moves bytes
-    wire = padded.view(torch.uint8)
-    parts = [torch.empty_like(wire) for _ in range(world)]
-    dist.all_gather(parts, wire, group=group)
-    return torch.cat([p.view(local.dtype)[: c * per_item] for p, c in zip(parts, counts)])
+    parts = [torch.empty(cmax * per_item * local.element_size(), dtype=torch.uint8, device=local.device)
+             for _ in range(world)]
+    dist.all_gather(parts, _bytes(padded), group=group)
+    flat = out.reshape(-1)
+    for r, (p, c) in enumerate(zip(parts, counts)):
+        lo = shard_range(total, r, world)[0]
+        flat[lo * per_item:(lo + c) * per_item] = p.view(local.dtype)[: c * per_item]
+    return out
+
+
+def gather_to_root(local, total: int, per_item: int, root: int = 0, group=None, out=None):
+    """Gather rank shards into the full output on `root` only.
+
+    Every other rank sends its shard; the root posts one receive per rank straight
+    into that rank's offset of `out` (allocated on the root if not given) and copies
+    its own shard in place.  Returns the full tensor on the root and None elsewhere.
+    Shards may be unequal.
+    """
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    _check_local(local, total, per_item, rank, world)
+    if not 0 <= root < world:
+        raise ValueError(f"bad root {root} of {world}")
+    ops = []
+    if rank == root:
+        if out is None:
+            out = torch.empty(total * per_item, dtype=local.dtype, device=local.device)
+        elif out.numel() != total * per_item or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous tensor of {total * per_item} words")
+        flat = out.reshape(-1)
+        lo, cnt = shard_range(total, rank, world)
+        flat[lo * per_item:(lo + cnt) * per_item] = local.reshape(-1)
+        for r in range(world):
+            lo_r, cnt_r = shard_range(total, r, world)
+            if r != root and cnt_r:
+                peer = r if group is None else dist.get_global_rank(group, r)
+                ops.append(dist.P2POp(dist.irecv, _bytes(flat[lo_r * per_item:(lo_r + cnt_r) * per_item]), peer, group))
+    elif local.numel():
+        peer = root if group is None else dist.get_global_rank(group, root)
+        ops.append(dist.P2POp(dist.isend, _bytes(local.contiguous()), peer, group))
+    if ops:
+        for req in dist.batch_isend_irecv(ops):
+            req.wait()
+    return out if rank == root else None

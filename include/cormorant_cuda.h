@@ -92,6 +92,16 @@ const char* cm_version(void);
  * (the status word is read and cleared), and the library stays usable. */
 int cm_selftest_wait_timeout(unsigned timeout_ms);
 
+/* ---- int8 tensor-pipe ceiling (a measurement; no reference counterpart) --------
+ * Runs the MatMul GEMM's MMA stream (tcgen05.mma kind::i8, M = 128 per CTA,
+ * N = 256, 32 deep) with its operands resident in shared memory -- no memory
+ * traffic -- on every SM: one CTA per SM (pairs = 0) or CTA pairs with
+ * cta_group::2 (pairs = 1), `iters` (1..65536) rounds of 8 MMAs each, after one
+ * untimed launch.  Returns the int8 ops per second reached (TOPS, 2 ops per
+ * multiply-add) and the timed launch's device time in ms: the roofline
+ * denominator of the Q8.8 GEMM, measured at the clocks of the moment. */
+int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms);
+
 /* ---- device timing of this library's launches (no reference counterpart) --
  * Between cm_profile_begin and cm_profile_end every kernel launch is bracketed
  * by CUDA events on its own stream.  cm_profile_read waits for those events
@@ -129,6 +139,8 @@ int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, 
  * CM_EINVAL; the need is, in bytes (each term rounded up to 256):
  *   A_b*2*n*K16 + B_b*2*k*M16 + A_b*n*4 + B_b*m*4,
  *   K16, M16 = k, m rounded up to 16, A_b = (a_batch_stride ? batch : 1), B_b likewise.
+ * Calls of at most cm_set_direct_limit multiply-accumulates run on the one-kernel
+ * CUDA-core path, as cm_matmul does, and use no scratch.
  * The first call on a device looks up the array's device address (once per
  * device, with that device current); make that first call before any stream
  * capture.  All calls share the one array: calls that can overlap on the GPU
@@ -350,6 +362,13 @@ void      cm_buf_init_view(cm_buf_t* view, cm_buf_t* base, unsigned offset_elems
                            unsigned count_elems);
 int       cm_buf_sync_to_device(cm_buf_t* buf);
 int       cm_buf_sync_from_device(cm_buf_t* buf);
+/* Stream-ordered twins of the two syncs (no reference counterpart: the reference's
+ * syncs are cache maintenance on one shared DDR): one cudaMemcpyAsync between the
+ * pinned mirror and the device buffer, enqueued on `stream`, so that a caller can
+ * overlap the copies of one call with the kernels of another.  Wait with
+ * cm_synchronize(stream) or any later work ordered after it on the GPU. */
+int       cm_buf_sync_to_device_async(cm_buf_t* buf, cm_stream_t stream);
+int       cm_buf_sync_from_device_async(cm_buf_t* buf, cm_stream_t stream);
 
 #ifdef __cplusplus
 }

@@ -3,10 +3,13 @@ memory while running (a run loop that must not allocate after initialisation, or
 code whose GPU memory is owned by another allocator).  It keeps its scratch in a
 fixed device array inside the library instead of calling cudaMalloc.
 
-Checked through the C ABI against the regular cm_matmul on two calls in a row
-(different shapes and data, so a stale array from the first call would show),
-bit-exact like every MatMul test, plus the clear rejection of a call whose
-scratch need exceeds the array.  Named test_zz_* so pytest collects it last.
+Checked through the C ABI, bit-exact like every MatMul test, against the oracle's
+MatMul and against the regular cm_matmul, on calls in a row with different shapes and
+data (so a stale array from an earlier call would show): partial tiles, A broadcast,
+outputs of at most 64 columns, overlapping output slices (c_batch_stride < n*m, later
+batch steps win) and c_batch_stride = 0, a launch-bound call that needs no scratch at
+all; plus the clear rejection of a call whose scratch need exceeds the array.  Named
+test_zz_* so pytest collects it last.
 """
 import ctypes as C
 
@@ -15,8 +18,23 @@ import pytest
 
 pytestmark = pytest.mark.gpu
 
+# (n, k, m, batch, a_batch_stride is zero, c_batch_stride or None for n*m)
+CASES = [
+    (300, 1000, 200, 3, False, None),     # partial tiles, both strides advance
+    (257, 513, 129, 4, True, None),       # A broadcast
+    (300, 257, 40, 3, False, None),       # m <= 64
+    (129, 1000, 64, 2, False, None),      # m = 64
+    (200, 300, 150, 3, False, 200 * 150 // 2),   # overlapping output slices
+    (130, 140, 150, 3, False, 0),         # every batch step on the same output
+    (7, 13, 5, 2, False, None),           # launch-bound: no scratch needed
+]
 
-def test_noalloc_matches_cm_matmul_twice():
+
+def _p(t):
+    return C.c_void_p(t.data_ptr())
+
+
+def test_noalloc_matches_oracle_and_cm_matmul(port):
     import torch
 
     import cormorant_b200 as cm
@@ -25,23 +43,26 @@ def test_noalloc_matches_cm_matmul_twice():
     cm.init("0")
     L = lib()
     gen = torch.Generator().manual_seed(314)
-    # (n, k, m, batch, a_batch_stride-is-zero): partial tiles, both strides, A broadcast
-    for (n, k, m, batch, a_bcast) in [(300, 1000, 200, 3, False), (257, 513, 129, 4, True)]:
+    for (n, k, m, batch, a_bcast, c_bs) in CASES:
+        c_bs = n * m if c_bs is None else c_bs
         a = torch.randint(-32768, 32768, ((1 if a_bcast else batch) * n * k,), dtype=torch.int32, generator=gen)
         b = torch.randint(-32768, 32768, (batch * k * m,), dtype=torch.int32, generator=gen)
-        a = a.to(torch.int16).cuda()
-        b = b.to(torch.int16).cuda()
+        a16, b16 = a.to(torch.int16), b.to(torch.int16)
         a_bs = 0 if a_bcast else n * k
-        want = torch.full((batch * n * m,), -23131, dtype=torch.int16, device="cuda")
-        got = torch.full((batch * n * m,), -23131, dtype=torch.int16, device="cuda")
-        assert L.cm_matmul(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(want.data_ptr()),
-                           n, k, m, batch, a_bs, k * m, n * m) == 0, L.cm_last_error()
-        rc = L.cm_matmul_noalloc(C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), C.c_void_p(got.data_ptr()),
-                                 n, k, m, batch, a_bs, k * m, n * m, None)
+        out_words = (batch - 1) * c_bs + n * m
+        want = torch.full((out_words,), -23131, dtype=torch.int16, device="cuda")
+        got = torch.full((out_words,), -23131, dtype=torch.int16, device="cuda")
+        ad, bd = a16.cuda(), b16.cuda()
+        assert L.cm_matmul(_p(ad), _p(bd), _p(want), n, k, m, batch, a_bs, k * m, c_bs) == 0, L.cm_last_error()
+        rc = L.cm_matmul_noalloc(_p(ad), _p(bd), _p(got), n, k, m, batch, a_bs, k * m, c_bs, None)
         assert rc == 0, L.cm_last_error()
         assert L.cm_synchronize(None) == 0, L.cm_last_error()
         g, w = got.cpu().numpy(), want.cpu().numpy()
-        assert np.array_equal(g, w), f"{int((g != w).sum())} words differ for {(n, k, m, batch)}"
+        o = port.matmul(a16.numpy(), b16.numpy(), n, k, m, batch, a_bs, k * m, c_bs,
+                        c=np.full(out_words, -23131, np.int16))
+        case = (n, k, m, batch, a_bs, c_bs)
+        assert np.array_equal(g, o), f"{int((g != o).sum())} words differ from the oracle for {case}"
+        assert np.array_equal(g, w), f"{int((g != w).sum())} words differ from cm_matmul for {case}"
 
 
 def test_noalloc_rejects_oversized_calls():
@@ -55,7 +76,6 @@ def test_noalloc_rejects_oversized_calls():
     n = k = m = 4096          # planes alone need 2 * 2 * 4096 * 4096 bytes = 64 MiB, plus terms
     a = torch.zeros(n * k, dtype=torch.int16, device="cuda")
     c = torch.zeros(n * m, dtype=torch.int16, device="cuda")
-    rc = L.cm_matmul_noalloc(C.c_void_p(a.data_ptr()), C.c_void_p(a.data_ptr()), C.c_void_p(c.data_ptr()),
-                             n, k, m, 1, n * k, k * m, n * m, None)
+    rc = L.cm_matmul_noalloc(_p(a), _p(a), _p(c), n, k, m, 1, n * k, k * m, n * m, None)
     assert rc == CM_EINVAL
     assert b"scratch" in L.cm_last_error()
