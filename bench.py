@@ -171,6 +171,14 @@ class MatmulSweep:
     dominant = "gemm_q88"
 
     sweep = MATMUL_SWEEP
+    strides = None          # --shape n,k,m,batch,a_bs,b_bs,c_bs: explicit batch strides (row-strided form)
+
+    def _st(self, n, k, m):
+        return self.strides if self.strides is not None else (n * k, k * m, n * m)
+
+    def _words(self, n, k, m, b):
+        a_bs, b_bs, c_bs = self._st(n, k, m)
+        return (b - 1) * a_bs + n * k, (b - 1) * b_bs + k * m, (b - 1) * c_bs + n * m
 
     def __init__(self, rank, world):
         self.rank, self.world = rank, world
@@ -185,7 +193,9 @@ class MatmulSweep:
 
     def config(self, world):
         if self.sweep is not MATMUL_SWEEP:
-            return {"workload": "matmul single shape " + ",".join(map(str, self.sweep[0])) + " (n,k,m,batch)",
+            return {"workload": "matmul single shape " + ",".join(map(str, self.sweep[0])) + " (n,k,m,batch)"
+                    + ("" if self.strides is None else " strides " + ",".join(map(str, self.strides))
+                       + " (a_bs,b_bs,c_bs)"),
                     "inputs": "raw int16 uniform [-1024,1024)", "parallelism": f"batch-sharded over {world} GPU(s)"}
         return {"workload": "matmul_sweep (BASELINE configs[1])",
                 "shapes": "B=64 x {256,1024,4096}^3 + B=8 x 8192x4096x11008 (n x k x m)",
@@ -201,16 +211,17 @@ class MatmulSweep:
             if b == 0:
                 self.bufs.append(None)
                 continue
-            a = torch.randint(-1024, 1024, (b * n * k,), dtype=torch.int16, device="cuda", generator=g)
-            bb = torch.randint(-1024, 1024, (b * k * m,), dtype=torch.int16, device="cuda", generator=g)
-            c = torch.empty(b * n * m, dtype=torch.int16, device="cuda")
+            wa, wb, wc = self._words(n, k, m, b)
+            a = torch.randint(-1024, 1024, (wa,), dtype=torch.int16, device="cuda", generator=g)
+            bb = torch.randint(-1024, 1024, (wb,), dtype=torch.int16, device="cuda", generator=g)
+            c = torch.empty(wc, dtype=torch.int16, device="cuda")
             self.bufs.append((a, bb, c))
 
     def step(self, cm, stream):
         for (n, k, m, b), t in zip(self.shapes, self.bufs):
             if t is None:
                 continue
-            cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, stream=stream)
+            cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, *self._st(n, k, m), stream=stream)
 
     def gather_outputs(self):
         """(local output shard, items over all ranks, words per item) of each output of a step."""
@@ -232,7 +243,7 @@ class MatmulSweep:
                 continue
             L.cm_profile_begin()
             for _ in range(iters):
-                cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, stream=stream)
+                cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, *self._st(n, k, m), stream=stream)
             torch.cuda.synchronize()
             L.cm_profile_end()
             res = {}
@@ -264,14 +275,15 @@ class MatmulSweep:
         for (n, k, m, b) in self.shapes:
             if b == 0:
                 continue
-            A = InferenceBuf.alloc(b * n * k)
-            B = InferenceBuf.alloc(b * k * m)
-            Cb = InferenceBuf.alloc(b * n * m)
+            wa, wb, wc = self._words(n, k, m, b)
+            A = InferenceBuf.alloc(wa)
+            B = InferenceBuf.alloc(wb)
+            Cb = InferenceBuf.alloc(wc)
             fill(A.ptr(), rng, -1024, 1024)
             fill(B.ptr(), rng, -1024, 1024)
             self.e2e.append((n, k, m, b, A, B, Cb))
-            self.h2d += 2 * (b * n * k + b * k * m)
-            self.d2h += 2 * b * n * m
+            self.h2d += 2 * (wa + wb)
+            self.d2h += 2 * wc
         self.pipe = CopyOverlap()
 
     def e2e_start(self, start_event):
@@ -281,7 +293,7 @@ class MatmulSweep:
         from cormorant_b200.runtime import run_matmul
         for (n, k, m, b, A, B, Cb) in self.e2e:
             self.pipe.call([A, B], [Cb], lambda s, n=n, k=k, m=m, b=b, A=A, B=B, Cb=Cb:
-                           run_matmul(A, B, Cb, n, k, m, b, n * k, k * m, n * m, stream=s))
+                           run_matmul(A, B, Cb, n, k, m, b, *self._st(n, k, m), stream=s))
 
     def e2e_finish(self):
         self.pipe.join()
@@ -1166,7 +1178,8 @@ def main():
                     help="network configs: launch every kernel from the host instead of replaying a CUDA graph")
     ap.add_argument("--no-planes", action="store_true",
                     help="resnet: no plane images between convs (each conv splits its NCHW input)")
-    ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch case instead of the sweep")
+    ap.add_argument("--shape", default="", help="matmul only: one n,k,m,batch[,a_bs,b_bs,c_bs] case instead "
+                                                "of the sweep")
     ap.add_argument("--int8-peak", action="store_true", help="measure the int8 ceilings (MMA stream, cuBLASLt) and exit")
     args = ap.parse_args()
     global UNFUSED, FUSE_RESIDUAL, PLANES, ONE_LAUNCH, GRAPH, PREPARED
@@ -1179,7 +1192,11 @@ def main():
     if args.int8_peak:
         return int8_peak()
     if args.shape:
-        MatmulSweep.sweep = [tuple(int(v) for v in args.shape.split(","))]
+        v = tuple(int(x) for x in args.shape.split(","))
+        if len(v) not in (4, 7):
+            ap.error("--shape takes n,k,m,batch or n,k,m,batch,a_bs,b_bs,c_bs")
+        MatmulSweep.sweep = [v[:4]]
+        MatmulSweep.strides = v[4:] if len(v) == 7 else None
         if args.config == "all":
             args.config = "matmul"
     names = ALL_CONFIGS if args.config == "all" else [args.config]

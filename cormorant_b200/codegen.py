@@ -350,6 +350,14 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             return (f"    /* {i}: MatMul -> {self.R(c_)} */\n"
                     f"    CHECK(cm_matmul_async({self._dev(a_)}, {self._dev(b_)}, {self._dev(c_, False)}, "
                     f"{a}, NULL));")
+        if kind == "matmul_at":
+            # run_matmul_at (_source.py:261-299): element offsets added to the three bases
+            _, a_, b_, c_, args = node
+            ao, bo, co = (int(v) for v in args[:3])
+            a = ", ".join(f"{int(v)}u" for v in args[3:])
+            return (f"    /* {i}: MatMul at +{ao}, +{bo}, +{co} -> {self.R(c_)} */\n"
+                    f"    CHECK(cm_matmul_async({self._dev(a_)} + {ao}u, {self._dev(b_)} + {bo}u, "
+                    f"{self._dev(c_, False)} + {co}u, {a}, NULL));")
         if kind == "pool":
             _, x, y, args = node
             a = ", ".join(f"{int(v)}u" for v in args)

@@ -1501,6 +1501,38 @@ using namespace cm;
 // MatmulKernel entry (MatmulKernel.h:68-79)
 // ---------------------------------------------------------------------------
 namespace {
+// `rows` rows of A (row r at a + r*lda) times the shared B [k][m], row r of the result at
+// c + r*ldc_row: one tensor-core GEMM over all rows (fused epilogue as in matmul_impl).
+int matmul_rows_impl(const Context* cx, const int16_t* a, const int16_t* b, int16_t* c, uint32_t rows, uint32_t k,
+                     uint32_t m, uint64_t lda, uint64_t ldc_row, unsigned epi, const int16_t* bias, cudaStream_t s) {
+    const uint64_t K_pad = pad_k(k);
+    const bool packed = m <= 64;
+    const uint64_t a_bytes = (2ull * rows * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)k * (packed ? 128 : 2 * pad_c(m)) + 255) & ~255ull;
+    const uint64_t rt_bytes = ((uint64_t)rows * 4 + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)m * 4 + 255) & ~255ull;
+    void* scratch = nullptr;
+    int rc = scratch_alloc(&scratch, a_bytes + b_bytes + rt_bytes + ct_bytes, s);
+    if (rc) return rc;
+    int8_t* ap = (int8_t*)scratch;
+    int8_t* bp = ap + a_bytes;
+    int32_t* rt = (int32_t*)(bp + b_bytes);
+    int32_t* ct = (int32_t*)((uint8_t*)rt + rt_bytes);
+    rc = split_rows(cx, a, 0, lda, rows, k, 1, ap, rt, nullptr, s);
+    if (!rc) rc = split_kn(cx, b, 0, m, m, k, 1, bp, ct, s, packed);
+    if (!rc) {
+        GemmPlan p{ap, rows, 1, bp, m, 1, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, ldc_row, 1, 0, 1};
+        p.b_packed = packed ? 1u : 0u;
+        p.epi = (epi & 1u) | ((epi & 2u) << 1);   // the kernel's bias-row bit is 4
+        p.resid = (epi & 2u) ? bias : nullptr;
+        rc = gemm_launch(cx, p, s);
+    }
+    scratch_free(scratch, s);
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul (row-strided)");
+}
+
 // MatMul with an optional fused epilogue (epi bit 1: + bias[j] saturating, bit 0: ReLU).
 int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m, unsigned batch,
                 unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride, unsigned epi,
@@ -1551,6 +1583,15 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul direct");
     }
     if (k > kMaxGemmK) return set_error(CM_EUNSUPPORTED, "cm_matmul: k = %u exceeds %u", k, kMaxGemmK);
+    if (n == 1 && batch > 1 && b_batch_stride == 0) {
+        // Row-strided form (the reference scheduler's MatMul over gapped buffers,
+        // inference-scheduler/src/nodes.py:785-801): `batch` one-row products with the
+        // same B, A rows a_batch_stride apart and output rows c_batch_stride apart
+        // (>= m here: overlapping rows took the ordered path above).  As batch steps
+        // every 128-row tile would hold one row; folded, they are the rows of ONE GEMM
+        // with those row pitches.
+        return matmul_rows_impl(cx, a, b, c, batch, k, m, a_batch_stride, c_batch_stride, epi, bias, s);
+    }
     const uint32_t a_batches = a_batch_stride == 0 ? 1u : batch;
     const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;
     const uint64_t K_pad = pad_k(k);

@@ -1,23 +1,19 @@
 """The two whole-network configurations of the benchmark, as kernel-call lists.
 
 The reference compiles an ONNX graph into a sequence of run_op / run_matmul /
-run_conv / run_pool calls over one buffer pool (inference-scheduler/src/nodes.py,
-src/codegen/_source.py).  `onnx` is not needed here: each network below is
-written directly as the call list the scheduler derives for it:
-
-* Conv  -> ConvKernel (bias as a conv input: has_bias = 1)        nodes.py:956-1119
-* Relu  -> VectorOPKernel(op=RELU, outer=1), b not read              nodes.py:414-453
-* Add   -> VectorOPKernel(op=ADD) over the whole tensor (residual)
-* MaxPool / GlobalAveragePool -> PoolingKernel (global = pool over H x W, stride 1, pad 0)
-                                                                      nodes.py:1274-1418
-* Reshape -> alias of the input buffer, no kernel                   nodes.py:1425-1493
-* Gemm(x[N,K], W[K,M], b[M]) -> MatMul(n=N, k=K, m=M, batch=1) then
-  Add(size=M, outer=N, a_inc=M, b_inc=0)  (Gemm -> MatMul + Add, graph.py:83-188)
+run_conv / run_pool calls over one buffer pool (inference-scheduler/src/graph.py,
+src/nodes.py, src/codegen/_source.py).  Each network here is built as the same
+operator graph (`lenet5_graph`, `resnet18_graph`: Conv with bias, Relu, MaxPool,
+residual Add, GlobalAveragePool, Reshape to [N, -1], Gemm) and its call list is
+derived by `scheduler.derive`, which restates the reference scheduler's argument
+derivation (Gemm -> MatMul + broadcast Add, Reshape -> buffer alias, alignment gaps
+and the row-strided MatMul form where a row width is not a multiple of 8 words).
 
 Each node is a plain tuple; `execute` walks the list on any backend that offers
 the four kernels (the GPU backend here; the tests replay the same list on the
-CPU oracle).  Weights are seeded synthetic data with the configurations' shapes
-and distributions.
+CPU oracle).  `fuse` and `chain` rewrite a list into its fused / plane-image forms.
+Weights are seeded synthetic data with the configurations' shapes and
+distributions.
 """
 from __future__ import annotations
 
@@ -45,6 +41,7 @@ class Net:
     macs_per_image: int = 0
     source_kinds: tuple = ()                         # kernel kinds of the call list before fusion
     planes: dict = field(default_factory=dict)       # plane image -> (batch, C, H, W, frame)
+    layouts: dict = field(default_factory=dict)      # tensor -> scheduler.Layout (buffers with alignment gaps)
 
     def buf(self, name: str, words: int) -> str:
         self.buffers[name] = int(words)
@@ -65,123 +62,130 @@ def q88_round(v: np.ndarray) -> np.ndarray:
     return np.clip(np.round(np.clip(v, -128.0, 127.99609375) * 256.0), -32768, 32767).astype(np.int16)
 
 
-class _Builder:
-    def __init__(self, net: Net, rng: np.random.Generator, weight_fn):
-        self.net, self.rng, self.weight_fn = net, rng, weight_fn
+class _GraphBuilder:
+    """Builds the ONNX-shaped operator graph of a network (scheduler.Graph); the call list
+    is then derived from it exactly as the reference scheduler derives it."""
+
+    def __init__(self, name: str, batch: int, x_shape, weight_fn):
+        from .scheduler import Graph
+        self.g = Graph(name)
+        self.g.add("x", (batch,) + tuple(x_shape))
+        self.g.inputs = ["x"]
+        self.weight_fn = weight_fn
         self.count = 0
 
     def _name(self, kind: str) -> str:
         self.count += 1
         return f"{kind}{self.count}"
 
-    def conv(self, x, c, h, w, m, k, s, p, bias=True):
-        n = self.net.batch
-        oh, ow = conv_out(h, k, s, p), conv_out(w, k, s, p)
+    def _op(self, op_type, inputs, outputs, **attrs):
+        from .scheduler import infer_shapes
+        self.g.op(op_type, inputs, outputs, **attrs)
+        infer_shapes(self.g)
+
+    def conv(self, x, m, k, s, p, bias=True):
+        c = self.g.tensors[x].shape[1]
         wn, bn = self._name("W"), self._name("B")
-        self.net.consts[wn] = self.weight_fn((m, c, k, k), c * k * k)
-        self.net.consts[bn] = self.weight_fn((m,), None) if bias else np.zeros(m, np.int16)
-        y = self.net.buf(self._name("conv"), n * m * oh * ow)
-        self.net.nodes.append(("conv", x, wn, bn if bias else None, y,
-                               (n, c, h, w, m, oh, ow, k, k, s, s, 1, 1, p, p, int(bias), 0)))
-        self.net.macs_per_image += m * oh * ow * c * k * k
-        return y, m, oh, ow
-
-    def relu(self, x, words):
-        y = self.net.buf(self._name("relu"), words)
-        self.net.nodes.append(("vectorop", x, None, y, (words, OP_RELU, 1, 0, 0)))
+        self.g.add(wn, (m, c, k, k), self.weight_fn((m, c, k, k), c * k * k))
+        ins = [x, wn]
+        if bias:
+            self.g.add(bn, (m,), self.weight_fn((m,), None))
+            ins.append(bn)
+        y = self._name("conv")
+        self._op("Conv", ins, [y], kernel_shape=(k, k), strides=(s, s), pads=(p, p, p, p))
         return y
 
-    def add(self, a, b, words):
-        y = self.net.buf(self._name("add"), words)
-        self.net.nodes.append(("vectorop", a, b, y, (words, OP_ADD, 1, 0, 0)))
+    def relu(self, x):
+        y = self._name("relu")
+        self._op("Relu", [x], [y])
         return y
 
-    def pool(self, x, c, h, w, k, s, p, kind, global_=False):
-        n = self.net.batch
-        if global_:
-            oh = ow = 1
-            args = (n, c, h, w, 1, 1, h, w, 1, 1, 0, 0, 1, 1, kind, 2, 0)
-        else:
-            oh, ow = conv_out(h, k, s, p), conv_out(w, k, s, p)
-            args = (n, c, h, w, oh, ow, k, k, s, s, p, p, 1, 1, kind, 2, 0)
-        y = self.net.buf(self._name("pool"), n * c * oh * ow)
-        self.net.nodes.append(("pool", x, y, args))
-        return y, oh, ow
+    def add(self, a, b):
+        y = self._name("add")
+        self._op("Add", [a, b], [y])
+        return y
 
-    def reshape(self, x):
-        y = self._name("reshape")
-        self.net.aliases[y] = x
+    def maxpool(self, x, k, s, p):
+        y = self._name("pool")
+        self._op("MaxPool", [x], [y], kernel_shape=(k, k), strides=(s, s), pads=(p, p, p, p))
+        return y
+
+    def global_avgpool(self, x):
+        y = self._name("pool")
+        self._op("GlobalAveragePool", [x], [y])
+        return y
+
+    def flatten(self, x):
+        """Reshape to [N, -1] (the shape given as a constant int64 input, as ONNX does)."""
+        y, sh = self._name("reshape"), self._name("shape")
+        self.g.add(sh, (2,), np.array([self.g.tensors[x].shape[0], -1], np.int64))
+        self._op("Reshape", [x, sh], [y])
         return y
 
     def gemm(self, x, k, m):
-        n = self.net.batch
         wn, bn = self._name("W"), self._name("B")
-        self.net.consts[wn] = self.weight_fn((k, m), k)
-        self.net.consts[bn] = self.weight_fn((m,), None)
-        t = self.net.buf(self._name("mm"), n * m)
-        self.net.nodes.append(("matmul", x, wn, t, (n, k, m, 1, n * k, k * m, n * m)))
-        y = self.net.buf(self._name("gemm"), n * m)
-        self.net.nodes.append(("vectorop", t, bn, y, (m, OP_ADD, n, m, 0)))
-        self.net.macs_per_image += k * m
+        self.g.add(wn, (k, m), self.weight_fn((k, m), k))
+        self.g.add(bn, (m,), self.weight_fn((m,), None))
+        y = self._name("gemm")
+        self._op("Gemm", [x, wn, bn], [y])
         return y
 
+    def finish(self, out: str):
+        self.g.outputs = [out]
+        return self.g
 
-def lenet5(batch: int = 1, seed: int = 42) -> Net:
-    """BASELINE config 0: LeNet-5-style CNN, 1x1x28x28 input uniform [0,1) (RNE to Q8.8);
-    weights and biases uniform [-0.5, 0.5) rounded down to a multiple of 1/256."""
+
+def lenet5_graph(batch: int = 1, seed: int = 42):
+    """BASELINE config 0 as an operator graph: LeNet-5-style CNN, 1x1x28x28 input; weights
+    and biases uniform [-0.5, 0.5) rounded down to a multiple of 1/256."""
     rng = np.random.default_rng(seed)
-    net = Net("lenet5", batch, "x", "")
-    net.buf("x", batch * 28 * 28)
     wfn = lambda shape, fan_in: q88_floor(rng.uniform(-0.5, 0.5, size=shape)).reshape(-1)  # noqa: E731
-    b = _Builder(net, rng, wfn)
-    y, c, h, w = b.conv("x", 1, 28, 28, 6, 5, 1, 2)
-    y = b.relu(y, batch * c * h * w)
-    y, h, w = b.pool(y, c, h, w, 2, 2, 0, 0)
-    y, c, h, w = b.conv(y, 6, h, w, 16, 5, 1, 0)
-    y = b.relu(y, batch * c * h * w)
-    y, h, w = b.pool(y, c, h, w, 2, 2, 0, 0)
-    y = b.reshape(y)                                          # [N, 400]
-    y = b.gemm(y, 400, 120)
-    y = b.relu(y, batch * 120)
-    y = b.gemm(y, 120, 84)
-    y = b.relu(y, batch * 84)
-    net.output = b.gemm(y, 84, 10)
-    return net
+    b = _GraphBuilder("lenet5", batch, (1, 28, 28), wfn)
+    y = b.maxpool(b.relu(b.conv("x", 6, 5, 1, 2)), 2, 2, 0)
+    y = b.maxpool(b.relu(b.conv(y, 16, 5, 1, 0)), 2, 2, 0)
+    y = b.flatten(y)                                           # [N, 400]
+    y = b.relu(b.gemm(y, 400, 120))
+    y = b.relu(b.gemm(y, 120, 84))
+    return b.finish(b.gemm(y, 84, 10))
 
 
-def resnet18(batch: int = 256, seed: int = 42, num_classes: int = 1000) -> Net:
-    """ResNet-18-shaped plain CNN (no normalisation layers), 3x224x224
-    input uniform [0,1) (RNE to Q8.8); He-scaled normal weights N(0, 2/fan_in) and
-    N(0, 0.01^2) biases, rounded to Q8.8."""
+def resnet18_graph(batch: int = 256, seed: int = 42, num_classes: int = 1000):
+    """BASELINE config 3 as an operator graph: ResNet-18-shaped plain CNN (no normalisation
+    layers), 3x224x224 input; He-scaled normal weights N(0, 2/fan_in) and N(0, 0.01^2)
+    biases, rounded to Q8.8."""
     rng = np.random.default_rng(seed)
-    net = Net("resnet18", batch, "x", "")
-    net.buf("x", batch * 3 * 224 * 224)
 
     def wfn(shape, fan_in):
         sd = np.sqrt(2.0 / fan_in) if fan_in else 0.01
         return q88_round(rng.normal(0.0, sd, size=shape)).reshape(-1)
 
-    b = _Builder(net, rng, wfn)
-    y, c, h, w = b.conv("x", 3, 224, 224, 64, 7, 2, 3)
-    y = b.relu(y, batch * c * h * w)
-    y, h, w = b.pool(y, c, h, w, 3, 2, 1, 0)                 # 56 x 56
+    b = _GraphBuilder("resnet18", batch, (3, 224, 224), wfn)
+    y = b.maxpool(b.relu(b.conv("x", 64, 7, 2, 3)), 3, 2, 1)   # 56 x 56
+    c = 64
     for width, stride in ((64, 1), (128, 2), (256, 2), (512, 2)):
         for blk in range(2):
             s = stride if blk == 0 else 1
-            t, c2, h2, w2 = b.conv(y, c, h, w, width, 3, s, 1)
-            t = b.relu(t, batch * c2 * h2 * w2)
-            t, c2, h2, w2 = b.conv(t, c2, h2, w2, width, 3, 1, 1)
-            if s != 1 or c != width:
-                sc, _, _, _ = b.conv(y, c, h, w, width, 1, s, 0)
-            else:
-                sc = y
-            y = b.add(t, sc, batch * c2 * h2 * w2)
-            y = b.relu(y, batch * c2 * h2 * w2)
-            c, h, w = c2, h2, w2
-    y, _, _ = b.pool(y, c, h, w, h, 1, 0, 1, global_=True)   # [N, 512, 1, 1]
-    y = b.reshape(y)
-    net.output = b.gemm(y, 512, num_classes)
-    return net
+            t = b.relu(b.conv(y, width, 3, s, 1))
+            t = b.conv(t, width, 3, 1, 1)
+            sc = b.conv(y, width, 1, s, 0) if (s != 1 or c != width) else y
+            y = b.relu(b.add(t, sc))
+            c = width
+    y = b.flatten(b.global_avgpool(y))                         # [N, 512]
+    return b.finish(b.gemm(y, 512, num_classes))
+
+
+def lenet5(batch: int = 1, seed: int = 42) -> Net:
+    """LeNet-5's call list, derived from its graph as the reference
+    scheduler derives it (scheduler.derive)."""
+    from .scheduler import derive
+    return derive(lenet5_graph(batch, seed))
+
+
+def resnet18(batch: int = 256, seed: int = 42, num_classes: int = 1000) -> Net:
+    """the ResNet-18-shaped network's call list, derived from its graph
+    as the reference scheduler derives it (scheduler.derive)."""
+    from .scheduler import derive
+    return derive(resnet18_graph(batch, seed, num_classes))
 
 
 def make_input(net: Net, seed: int = 7) -> np.ndarray:
@@ -198,7 +202,7 @@ def _inputs(node) -> list:
             names[0] = node[8]                       # read from its plane image only
         if len(node) > 10 and node[7] is None and node[10] is not None:
             names[3] = node[10]                      # residual from its plane image only
-    elif kind == "matmul":
+    elif kind in ("matmul", "matmul_at"):
         names = [node[1], node[2]] + ([node[6]] if len(node) > 6 else [])
     elif kind == "vectorop":
         names = [node[1], node[2]]
@@ -210,7 +214,7 @@ def _inputs(node) -> list:
 def output_of(node) -> str:
     if node[0] == "conv":
         return node[4] if node[4] is not None else node[9]
-    return node[3] if node[0] in ("vectorop", "matmul") else node[2]   # pool, planes: node[2]
+    return node[3] if node[0] in ("vectorop", "matmul", "matmul_at") else node[2]   # pool, planes: node[2]
 
 
 def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
@@ -381,9 +385,15 @@ def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
                 continue
         if gemm and node[0] == "matmul" and len(node) == 5 and i + 1 < len(nodes) and reads.get(R(node[3]), 0) == 1:
             _, a, b, c, args = node
-            n, _, m, batch = args[:4]
+            n, _, m, batch, _, b_bs, c_bs = args
             c, nxt = R(c), nodes[i + 1]
-            if (batch == 1 and nxt[0] == "vectorop" and tuple(nxt[4]) == (m, OP_ADD, n, m, 0)
+            # the output as rows of m words at a pitch: one matrix (batch 1), or the
+            # row-strided form (n = 1, B shared, one row per batch step c_bs apart)
+            rows, pitch = (n, m) if batch == 1 else ((batch, c_bs) if n == 1 and b_bs == 0 else (0, 0))
+            # the Gemm's bias Add: the bias row broadcast over those rows (at one row the
+            # scheduler emits a plain whole-tensor Add)
+            bias_forms = {(m, OP_ADD, rows, pitch, 0)} | ({(m, OP_ADD, 1, 0, 0)} if rows == 1 else set())
+            if (rows and nxt[0] == "vectorop" and tuple(nxt[4]) in bias_forms
                     and R(nxt[1]) == c and nxt[2] is not None and R(nxt[2]) != c):
                 y, epi, step = nxt[3], 2, 2
                 if i + 2 < len(nodes) and reads.get(R(y), 0) == 1 and relu_of(nodes[i + 2], R(y)):
@@ -391,7 +401,7 @@ def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
                 out.append(("matmul", a, b, y, args, epi, nxt[2]))
                 i += step
                 continue
-            if batch == 1 and relu_of(nxt, c):
+            if rows and relu_of(nxt, c):
                 out.append(("matmul", a, b, nxt[3], args, 1, None))
                 i += 2
                 continue
@@ -437,7 +447,8 @@ def execute(net: Net, backend, bufs: dict) -> None:
     """Run every node of `net` on `backend` over `bufs` (name -> backend buffer).
 
     backend offers vectorop(a, b, c, size, op, outer, a_inc, b_inc),
-    matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), conv(x, w, bias, y, *17 scalars),
+    matmul(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs), matmul_at(a, b, c, a_off, b_off, c_off,
+    n, k, m, batch, a_bs, b_bs, c_bs) (the reference's run_matmul_at), conv(x, w, bias, y, *17 scalars),
     pool(x, y, *17 scalars) and, for fused call lists, conv_fused(x, w, bias, y, *17
     scalars, epilogue, resid) and matmul_fused(a, b, c, *7 scalars, epilogue, bias)."""
     if getattr(backend, "one_launch", False) and backend.run_list(net, bufs):
@@ -472,6 +483,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "matmul":
             _, a, bb, c, args = node
             backend.matmul(R(a), R(bb), R(c), *args)
+        elif kind == "matmul_at":
+            _, a, bb, c, args = node
+            backend.matmul_at(R(a), R(bb), R(c), *args)
         else:
             raise ValueError(kind)
 
@@ -512,6 +526,11 @@ class GpuBackend:
 
     def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
         self.k.MatmulKernel(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, stream=self.stream)
+
+    def matmul_at(self, a, b, c, a_off, b_off, c_off, n, k, m, batch, a_bs, b_bs, c_bs):
+        # run_matmul_at: the element offsets move the three base addresses
+        self.k.MatmulKernel(a.reshape(-1)[a_off:], b.reshape(-1)[b_off:], c.reshape(-1)[c_off:], n, k, m, batch,
+                            a_bs, b_bs, c_bs, stream=self.stream)
 
     def matmul_fused(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epi, bias):
         self.k.MatmulKernelFused(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi, bias=bias,
@@ -581,11 +600,13 @@ def prepare_weights(net: Net, bufs: dict) -> dict:
 
 
 def gpu_buffers(net: Net, x=None):
-    """Device buffers for every activation and constant of `net` (torch int16 tensors)."""
+    """Device buffers for every activation and constant of `net` (torch int16 tensors),
+    zeroed: the alignment gaps of strided buffers are never written by the kernels and
+    hold 0, as the reference's zero-filled buffer pool does."""
     import torch
     bufs = {}
     for name, words in net.buffers.items():
-        bufs[name] = torch.empty(max(words, 1), dtype=torch.int16, device="cuda")
+        bufs[name] = torch.zeros(max(words, 1), dtype=torch.int16, device="cuda")
     for name, arr in net.consts.items():
         bufs[name] = torch.from_numpy(np.ascontiguousarray(arr)).cuda()
     if net.planes:

@@ -212,3 +212,49 @@ def test_prepared_project_builds_weights_once(tmp_path):
     assert src.count("cm_conv_weights_destroy(") == nconv
     assert "cm_conv_planes_async(" not in src and "cm_conv_fused_async(" not in src
     assert src.index("cm_buf_sync_to_device(g_wpool)") < src.index("cm_conv_weights_create(")
+
+
+# ---- the reference scheduler's own files (tests/golden/make_calllists.py) ----------
+REFPROJ = ROOT / "tests" / "golden" / "refproj_lenet5"
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_weight_files_equal_the_reference_scheduler(tmp_path, batch):
+    """weights/*.dat of the generated project are byte for byte the files the reference
+    scheduler writes for the same network (CodeGenerator.generate_weight_dat)."""
+    codegen.emit_project(networks.lenet5(batch), tmp_path)
+    ref = sorted((REFPROJ / "weights").glob("*.dat"))
+    ours = sorted((tmp_path / "weights").glob("*.dat"))
+    assert ref and [p.name for p in ours] == [p.name for p in ref]
+    for a, b in zip(ours, ref):
+        assert a.read_bytes() == b.read_bytes(), a.name
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_reference_expected_output_equals_the_oracle(port, batch):
+    """The expected words of the reference's generated test (its fixed-point simulator on
+    the ramp input, alignment gaps as zeros) equal the oracle's run of the derived call list."""
+    net = networks.lenet5(batch)
+    want = np.load(REFPROJ / f"expected_lenet5_b{batch}.npy")
+    got = _expected(net, port)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", ["plain", "fused"])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_reference_files_run_unchanged_on_gpu(tmp_path, batch, mode):
+    """The reference scheduler's weights/*.dat and its expected output words drive the
+    generated CUDA project unchanged: our weight files are replaced by the reference's and
+    the test binary compares the network output with the reference's expected words."""
+    net = networks.lenet5(batch)
+    if mode == "fused":
+        net = networks.fuse(net)
+    want = np.load(REFPROJ / f"expected_lenet5_b{batch}.npy")
+    codegen.emit_project(net, tmp_path, expected=want)
+    for f in (REFPROJ / "weights").glob("*.dat"):
+        (tmp_path / "weights" / f.name).write_bytes(f.read_bytes())
+    exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
+    r = subprocess.run([str(exe), "3"], capture_output=True, text=True, timeout=300, cwd=tmp_path)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "test_inference PASSED" in r.stdout

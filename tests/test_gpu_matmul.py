@@ -166,3 +166,46 @@ def test_fused_rejects_bad_epilogue(cm):
     with pytest.raises(CormorantError):
         cm.kernels.MatmulKernelFused(dev(np.ones(16, np.int16)), dev(np.ones(16, np.int16)), c, 4, 4, 4,
                                      epilogue=4, bias=dev(np.ones(4, np.int16)))
+
+
+# Row-strided form (the reference scheduler's MatMul over gapped buffers, nodes.py:785-801):
+# n = 1, B shared, `batch` rows of A a_bs apart, output rows c_bs apart.  Folded into one
+# GEMM of `batch` rows on the tensor-core path.
+ROW_STRIDED = [(84, 10, 3, 88, 16), (120, 84, 3, 120, 88), (13, 70, 300, 20, 72), (257, 64, 129, 264, 64),
+               (40, 200, 517, 40, 203), (1000, 33, 260, 1001, 40)]
+
+
+@pytest.mark.parametrize("k,m,rows,a_bs,c_bs", ROW_STRIDED)
+@pytest.mark.parametrize("epi", [0, 3])
+def test_row_strided_rows(cm, port, k, m, rows, a_bs, c_bs, epi):
+    rng = np.random.default_rng(k * 7 + m + rows)
+    a = rand16(rng, (rows - 1) * a_bs + k, -1024, 1024)
+    b = rand16(rng, k * m, -1024, 1024)
+    bias = rand16(rng, m, -4096, 4096)
+    init = np.full((rows - 1) * c_bs + m, -23131, np.int16)
+    c = dev(init)
+    if epi:
+        cm.kernels.MatmulKernelFused(dev(a), dev(b), c, 1, k, m, rows, a_bs, 0, c_bs, epilogue=epi, bias=dev(bias))
+    else:
+        cm.MatmulKernel(dev(a), dev(b), c, 1, k, m, rows, a_bs, 0, c_bs)
+    want = port.matmul(a, b, 1, k, m, rows, a_bs, 0, c_bs, c=init.copy())
+    if epi & 2:
+        want = port.vectorop(want, bias, m, 0, rows, c_bs, 0, c=want.copy())
+    if epi & 1:
+        for r in range(rows):          # ReLU on the data words of each row; gap words untouched
+            seg = want[r * c_bs:r * c_bs + m]
+            want[r * c_bs:r * c_bs + m] = np.maximum(seg, 0)
+    assert_same(host(c), want, f"row-strided k={k} m={m} rows={rows} a_bs={a_bs} c_bs={c_bs} epi={epi}")
+
+
+@pytest.mark.big
+def test_row_strided_full_size(cm, port):
+    """4096 gapped rows x K = 512 x M = 1000 (rows 520 and 1008 words apart), whole output."""
+    k, m, rows, a_bs, c_bs = 512, 1000, 4096, 520, 1008
+    rng = np.random.default_rng(77)
+    a = rand16(rng, (rows - 1) * a_bs + k, -1024, 1024)
+    b = rand16(rng, k * m, -1024, 1024)
+    init = np.full((rows - 1) * c_bs + m, -23131, np.int16)
+    c = dev(init)
+    cm.MatmulKernel(dev(a), dev(b), c, 1, k, m, rows, a_bs, 0, c_bs)
+    assert_same(host(c), port.matmul(a, b, 1, k, m, rows, a_bs, 0, c_bs, c=init.copy()), "row-strided 4096x512x1000")

@@ -20,14 +20,21 @@ class OracleBackend:
         c[:] = self.chk.vectorop(a, b, size, op, outer, a_inc, b_inc, c=c.copy())[: c.size]
 
     def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
-        c[:] = self.chk.matmul(a, b, n, k, m, batch, a_bs, b_bs, c_bs)[: c.size]
+        # written in place: words between output rows (alignment gaps) keep their values
+        c[:] = self.chk.matmul(a, b, n, k, m, batch, a_bs, b_bs, c_bs, c=c.copy())[: c.size]
+
+    def matmul_at(self, a, b, c, a_off, b_off, c_off, n, k, m, batch, a_bs, b_bs, c_bs):
+        view = c[c_off:]
+        self.matmul(a[a_off:], b[b_off:], view, n, k, m, batch, a_bs, b_bs, c_bs)
 
     def matmul_fused(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epi, bias):
-        """The reference call sequence MatMul -> [Add(bias row)] -> [Relu] on the checker."""
-        t = np.zeros(c.size, np.int16)
+        """The reference call sequence MatMul -> [Add(bias row)] -> [Relu] on the checker;
+        the output rows are one n x m matrix, or one row per batch step c_bs apart."""
+        t = c.copy()
         self.matmul(a, b, t, n, k, m, batch, a_bs, b_bs, c_bs)
+        rows, pitch = (n, m) if batch == 1 else (batch, c_bs)
         if epi & 2:
-            t = self.chk.vectorop(t, bias, m, networks.OP_ADD, n, m, 0, c=t.copy())[: c.size]
+            t = self.chk.vectorop(t, bias, m, networks.OP_ADD, rows, pitch, 0, c=t.copy())[: c.size]
         if epi & 1:
             t = self.chk.vectorop(t, None, c.size, networks.OP_RELU, 1, 0, 0)[: c.size]
         c[:] = t
@@ -289,3 +296,48 @@ def test_lenet_one_launch_every_activation(cm, port, batch):
     assert cm.launch_count() - l0 == 1
     for name in net.buffers:
         assert_same(bufs[name].cpu().numpy()[: net.buffers[name]], want[name][: net.buffers[name]], f"lenet {name}")
+
+
+# ---- the scheduler edge-case graphs (tests/golden/scheduler_graphs.py) ------------
+def _edge_graphs():
+    from tests.golden.scheduler_graphs import GRAPHS
+    return {k: f for k, f in GRAPHS.items() if not k.startswith(("lenet", "resnet"))}
+
+
+@pytest.mark.parametrize("name", sorted(_edge_graphs()))
+def test_edge_graph_reference_cpu_equals_port(port, name):
+    """The derived call lists of the edge-case graphs (broadcast gaps, MatMul batch forms and
+    outer loop, row-strided MatMul, conv and pool forms) on the C restatement and on the
+    reference's own kernels: every buffer equal."""
+    if not oracle.have_ref():
+        pytest.skip("oracle/_ref not built")
+    from cormorant_b200 import scheduler
+    net = scheduler.derive(_edge_graphs()[name]())
+    x = np.random.default_rng(3).integers(-1024, 1024, net.buffers[net.input]).astype(np.int16)
+    a, b = cpu_buffers(net, x), cpu_buffers(net, x)
+    networks.execute(net, OracleBackend(port), a)
+    networks.execute(net, OracleBackend(oracle.ref()), b)
+    for buf in net.buffers:
+        assert_same(a[buf], b[buf], f"{name} buffer {buf}")
+
+
+@pytest.mark.gpu
+@pytest.mark.usefixtures("mac_path")
+@pytest.mark.parametrize("fused", [False, True])
+@pytest.mark.parametrize("name", sorted(_edge_graphs()))
+def test_edge_graph_gpu_every_buffer(cm, port, name, fused):
+    """The same call lists (and their fused forms) through the C ABI on the GPU, every buffer
+    bit-exact against the oracle, on both MatMul / Conv paths."""
+    import torch
+    from cormorant_b200 import scheduler
+    net = scheduler.derive(_edge_graphs()[name]())
+    if fused:
+        net = networks.fuse(net)
+    x = np.random.default_rng(3).integers(-1024, 1024, net.buffers[net.input]).astype(np.int16)
+    want = cpu_buffers(net, x)
+    networks.execute(net, OracleBackend(port), want)
+    bufs = networks.gpu_buffers(net, x)
+    networks.execute(net, networks.GpuBackend(), bufs)
+    torch.cuda.synchronize()
+    for buf in net.buffers:
+        assert_same(bufs[buf].cpu().numpy(), want[buf], f"{name} buffer {buf}")
