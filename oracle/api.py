@@ -14,7 +14,22 @@ import numpy as np
 
 ORACLE_DIR = Path(__file__).resolve().parent
 REF_DIR = ORACLE_DIR / "_ref"
-REFERENCE_TREE = Path(os.environ.get("CM_REFERENCE_TREE", "/root/reference"))
+
+
+def _reference_tree() -> Path | None:
+    """Where the reference tree is: CM_REFERENCE_TREE, else the reference_path that
+    BASELINE.json (the repository's description of its reference) records; None when
+    neither names an existing directory."""
+    loc = os.environ.get("CM_REFERENCE_TREE")
+    if not loc:
+        meta = ORACLE_DIR.parent / "BASELINE.json"
+        if meta.exists():
+            import json
+            loc = json.loads(meta.read_text()).get("reference_path")
+    return Path(loc) if loc and Path(loc).is_dir() else None
+
+
+REFERENCE_TREE = _reference_tree()
 
 _u = C.c_uint
 _p16 = C.POINTER(C.c_int16)
@@ -24,10 +39,15 @@ def build(with_ref: bool | None = None) -> None:
     """Compile liboracle.so and, when the reference tree is present, _ref/."""
     targets = ["port"]
     if with_ref is None:
-        with_ref = (REFERENCE_TREE / "kernels").is_dir()
+        with_ref = REFERENCE_TREE is not None and (REFERENCE_TREE / "kernels").is_dir()
     if with_ref:
+        if REFERENCE_TREE is None:
+            raise FileNotFoundError("the reference tree is not known: set CM_REFERENCE_TREE")
         targets += ["ref", "reftests"]
-    subprocess.run(["make", "-s", "-C", str(ORACLE_DIR), f"REF={REFERENCE_TREE}", *targets], check=True)
+    cmd = ["make", "-s", "-C", str(ORACLE_DIR), *targets]
+    if with_ref:
+        cmd.insert(4, f"REF={REFERENCE_TREE}")
+    subprocess.run(cmd, check=True)
 
 
 def have_ref() -> bool:
