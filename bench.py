@@ -223,6 +223,13 @@ class MatmulSweep:
                 continue
             cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, *self._st(n, k, m), stream=stream)
 
+    def step_into(self, cm, stream, outs):
+        """The step with output i written at device address outs[i] (the root's buffers)."""
+        for (n, k, m, b), t, o in zip(self.shapes, self.bufs, outs):
+            if t is None:
+                continue
+            cm.MatmulKernel(t[0], t[1], o, n, k, m, b, *self._st(n, k, m), stream=stream)
+
     def gather_outputs(self):
         """(local output shard, items over all ranks, words per item) of each output of a step."""
         import torch
@@ -338,6 +345,10 @@ class VectorOPSweep:
         for op in VOP_OPS:
             cm.VectorOPKernel(self.a, self.b, self.c, self.n, op, stream=stream)
 
+    def step_into(self, cm, stream, outs):
+        for op, o in zip(VOP_OPS, outs):
+            cm.VectorOPKernel(self.a, self.b, o, self.n, op, stream=stream)
+
     def gather_outputs(self):
         return [(self.c, VOP_N, 1) for _ in VOP_OPS]
 
@@ -430,11 +441,15 @@ class PoolSweep:
         self.x = torch.randint(-2048, 2048, (self.nb * C * H * W,), dtype=torch.int16, device="cuda", generator=g)
         self.y = torch.empty(self.nb * C * 56 * 56, dtype=torch.int16, device="cuda")
 
-    def _one(self, cm, c, stream):
+    def _one(self, cm, c, stream, y=None):
         N, C, H, W = POOL_SHAPE
         _, ph, pw, sh, sw, pt, pl, dh, dw, t, lp, cip, oh, ow = c
-        cm.PoolingKernel(self.x, self.y, self.nb, C, H, W, oh, ow, ph, pw, sh, sw, pt, pl, dh, dw, t, lp, cip,
-                         stream=stream)
+        cm.PoolingKernel(self.x, self.y if y is None else y, self.nb, C, H, W, oh, ow, ph, pw, sh, sw, pt, pl, dh,
+                         dw, t, lp, cip, stream=stream)
+
+    def step_into(self, cm, stream, outs):
+        for c, o in zip(POOL_SWEEP, outs):
+            self._one(cm, c, stream, o)
 
     def step(self, cm, stream):
         for c in POOL_SWEEP:
@@ -588,6 +603,14 @@ class NetworkBench:
         torch.cuda.synchronize()
         return g, n
 
+    def step_into(self, cm, stream, outs):
+        """The call list with the network output at outs[0], replayed as its own CUDA graph."""
+        if getattr(self, "_into", None) is None or self._into[0] != outs[0]:
+            bufs = dict(self.bufs)
+            bufs[self.net.resolve(self.net.output)] = int(outs[0])
+            self._into = (outs[0], self._capture(bufs)[0])
+        self._into[1].replay()
+
     def gather_outputs(self):
         """ResNet: the logits of every image; LeNet runs replicas (nothing to gather)."""
         if self.which == "lenet":
@@ -639,6 +662,7 @@ class NetworkBench:
     def release(self):
         self.bufs = None
         self.graph = None
+        self._into = None
         self.wcache = {}
 
     def e2e_setup(self):
@@ -1043,7 +1067,7 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
                 "kernel": wl.dominant,
                 "note": f"algorithmic bytes / kernel CUDA-event time on rank 0; peak = {peaks['source']} HBM copy rate"}
 
-    gather = measure_gathers(wl, env, ms_per_step, scale) if world > 1 else None
+    gather = measure_gathers(wl, env, ms_per_step, scale, K) if world > 1 else None
     per_part = wl.per_part(cm, stream, max(2, min(K, 5))) if (detail and rank == 0) else None
     wl.release()
     torch.cuda.empty_cache()
@@ -1100,18 +1124,28 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
     return rec
 
 
-def measure_gathers(wl, env: Env, ms_per_step: float, scale: float) -> dict | None:
-    """N > 1: the outputs stay sharded in `value`.  A caller that wants them together adds, per step,
-    either a gather to rank 0 (every rank sends its shard, rank 0 receives each into its offset) or an
-    all-gather to every rank, both over NCCL (NVLink / NVSwitch).  Each is timed on the device over one
-    step's outputs (max over ranks) after a warm-up pass."""
+def measure_gathers(wl, env: Env, ms_per_step: float, scale: float, K: int) -> dict | None:
+    """N > 1: the outputs stay sharded in `value`.  A caller that wants them together on one GPU
+    (or every GPU) gets them three ways, each timed on the device (max over ranks):
+      fused_to_root  every rank's kernels write their output shard straight into rank 0's buffers
+                     (sharding.RootOutputs: CUDA-IPC-mapped, plain stores over NVLink while the
+                     kernels run); K whole steps timed, gather included;
+      to_root        after the step, every rank sends its shards and rank 0 receives each into its
+                     offset (grouped NCCL send/recv);
+      all_gather     after the step, every output to every rank (NCCL all_gather_into_tensor).
+    The fused form's root output is checked word for word against the NCCL gather of the same
+    step's last output."""
     import torch
     from cormorant_b200 import sharding
     spec = wl.gather_outputs() if hasattr(wl, "gather_outputs") else []
     if not spec:
         return None
     world, rank, stream = env.world, env.rank, env.stream
-    res = {}
+    full_bytes = sum(total * per_item * 2 for _, total, per_item in spec)
+    # bytes that cross NVLink into the receiving GPU: every shard but its own
+    ingress = sum((total - sharding.shard_range(total, 0, world)[1]) * per_item * 2 for _, total, per_item in spec)
+    res = {"unit": wl.unit, "bytes_per_step": full_bytes, "ingress_bytes_per_gpu": ingress}
+    last_nccl = None
     for kind in ("to_root", "all_gather"):
         outs = []
         for t, total, per_item in spec:
@@ -1135,20 +1169,43 @@ def measure_gathers(wl, env: Env, ms_per_step: float, scale: float) -> dict | No
         ge.record(stream)
         torch.cuda.synchronize()
         g_ms = env.reduce(gs.elapsed_time(ge), "max")
-        full_bytes = sum(total * per_item * 2 for _, total, per_item in spec)
-        # bytes that cross NVLink into one receiving GPU: every shard but its own
-        ingress = sum((total - sharding.shard_range(total, 0, world)[1]) * per_item * 2 for _, total, per_item in spec)
-        res[kind] = {"ms_per_step": g_ms, "bytes_per_step": full_bytes, "ingress_bytes_per_gpu": ingress,
-                     "ingress_gbs": round(ingress / (g_ms * 1e-3) / 1e9, 1) if g_ms > 0 else None,
+        res[kind] = {"ms_per_step": g_ms, "ingress_gbs": round(ingress / (g_ms * 1e-3) / 1e9, 1) if g_ms > 0 else None,
                      "value_with_gather": wl.units_total / ((ms_per_step + g_ms) * 1e-3) / scale}
+        if kind == "to_root" and rank == 0:
+            last_nccl = outs[-1]
         del outs
-        torch.cuda.empty_cache()
         env.barrier()
-    res["unit"] = wl.unit
-    res["note"] = ("to_root: every rank sends its shard of one step's outputs and rank 0 receives each straight into "
-                   "its offset (NCCL grouped send/recv); all_gather: every output to every rank "
-                   "(all_gather_into_tensor into a preallocated output); value_with_gather = units / (ms_per_step + "
-                   "gather ms), gather not overlapped; one GPU's NVLink ingress bounds both, so neither scales with N")
+    if hasattr(wl, "step_into"):
+        ro = sharding.RootOutputs([total * per_item for _, total, per_item in spec])
+        addrs = [ro.address(i, sharding.shard_range(total, rank, world)[0] * per_item)
+                 for i, (_, total, per_item) in enumerate(spec)]
+        for _ in range(2):                              # warm (a network captures its graph)
+            wl.step_into(env.cm, stream, addrs)
+        torch.cuda.synchronize()
+        env.barrier()
+        fs, fe = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        fs.record(stream)
+        for _ in range(K):
+            wl.step_into(env.cm, stream, addrs)
+        fe.record(stream)
+        torch.cuda.synchronize()
+        env.barrier()
+        f_ms = env.reduce(fs.elapsed_time(fe), "max") / K
+        same = None
+        if rank == 0:
+            same = bool(torch.equal(ro.tensors[-1], last_nccl))
+        res["fused_to_root"] = {"ms_per_step": f_ms,
+                                "ingress_gbs": round(ingress / (f_ms * 1e-3) / 1e9, 1) if f_ms > 0 else None,
+                                "value_with_gather": wl.units_total / (f_ms * 1e-3) / scale,
+                                "steps": K, "matches_nccl_gather": same}
+        ro.close()
+    del last_nccl
+    torch.cuda.empty_cache()
+    env.barrier()
+    res["note"] = ("value_with_gather = units / time of a step whose outputs end up on rank 0 (fused_to_root: the "
+                   "kernels write there directly, K steps timed; to_root / all_gather: ms_per_step + the NCCL "
+                   "collective's ms); ingress_gbs = bytes arriving at one GPU / that time; the receiving GPU's "
+                   "NVLink ingress bounds every form")
     return res
 
 

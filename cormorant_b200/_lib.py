@@ -67,6 +67,9 @@ SIGNATURES: dict[str, tuple] = {
     "cm_calls_async": (C.c_int, [_p, _u, _p]),
     "cm_pool": (C.c_int, [_p, _p] + [_u] * 17),
     "cm_pool_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
+    "cm_ipc_export": (C.c_int, [_p, _p]),
+    "cm_ipc_open": (C.c_int, [_p, C.POINTER(_p)]),
+    "cm_ipc_close": (C.c_int, [_p]),
     "cm_buf_alloc": (_p, [_u]),
     "cm_buf_free": (None, [_p]),
     "cm_buf_retain": (None, [_p]),

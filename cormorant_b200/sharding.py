@@ -104,3 +104,64 @@ def gather_to_root(local, total: int, per_item: int, root: int = 0, group=None, 
         for req in dist.batch_isend_irecv(ops):
             req.wait()
     return out if rank == root else None
+
+
+class RootOutputs:
+    """Full-size output buffers held by the root rank, written by every rank's kernels.
+
+    The gather fused into the producing kernels: the root allocates each output in full
+    and exports it (cm_ipc_export); every other rank maps it (cm_ipc_open) and passes
+    `address(i, first_item)` -- the mapped buffer advanced to its shard -- as the output
+    of its MatMul / VectorOP / Pooling calls.  The kernels' ordinary stores then put each
+    output word straight into the root GPU's memory over NVLink while the kernel runs: no
+    collective, no copy after the kernels.  `sizes` are the outputs' word counts (every
+    item of every rank); `tensors` holds them on the root (None elsewhere).  The data are
+    complete on the root once every rank has synchronized its kernels (then a barrier).
+    Call close() on every rank before the process group goes away.
+    """
+
+    def __init__(self, sizes, root: int = 0, group=None):
+        import ctypes as C
+        import torch
+        import torch.distributed as dist
+        from ._lib import check, lib
+        self.rank = dist.get_rank(group)
+        self.root, self.group = root, group
+        L = lib()
+        self.tensors, handles = None, None
+        if self.rank == root:
+            self.tensors = [torch.empty(max(int(w), 1), dtype=torch.int16, device="cuda") for w in sizes]
+            handles = []
+            for t in self.tensors:
+                h = (C.c_ubyte * 80)()
+                check(L.cm_ipc_export(C.c_void_p(t.data_ptr()), h))
+                handles.append(bytes(h))
+        box = [handles]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, root) if group is not None else root,
+                                   group=group)
+        self._opened = []
+        if self.rank == root:
+            self.ptrs = [t.data_ptr() for t in self.tensors]
+        else:
+            self.ptrs = []
+            for hb in box[0]:
+                h = (C.c_ubyte * 80).from_buffer_copy(hb)
+                p = C.c_void_p()
+                check(L.cm_ipc_open(h, C.byref(p)))
+                self._opened.append(p.value)
+                self.ptrs.append(p.value)
+
+    def address(self, i: int, word_offset: int) -> int:
+        """Device address (valid in this process) of word `word_offset` of output i."""
+        return int(self.ptrs[i]) + 2 * int(word_offset)
+
+    def close(self) -> None:
+        """Unmap on the importing ranks, then a barrier, so the root frees its buffers only
+        after every mapping is gone."""
+        import torch.distributed as dist
+        from ._lib import check, lib
+        for p in self._opened:
+            check(lib().cm_ipc_close(p))
+        self._opened, self.ptrs = [], []
+        dist.barrier(group=self.group)
+        self.tensors = None

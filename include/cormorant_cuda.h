@@ -338,6 +338,27 @@ int cm_pool_async(const int16_t* x, int16_t* y, unsigned batch, unsigned channel
                   unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
                   unsigned count_include_pad, cm_stream_t stream);
 
+/* ---- outputs written across GPUs (no reference counterpart) -----------------------
+ * The batch-sharded multi-GPU drivers (one process per GPU) gather a step's outputs
+ * on one GPU by letting every rank's kernels write their shard straight into that
+ * GPU's buffers: the root exports a device buffer (cm_ipc_export), every other rank
+ * maps it (cm_ipc_open, CUDA IPC; peer access over NVLink / NVSwitch enabled as
+ * needed) and passes the mapped address, offset to its shard, as the output of
+ * cm_matmul / cm_vectorop / cm_pool.  Those kernels write outputs with ordinary
+ * stores only, so each word crosses NVLink once, while it is computed.  The
+ * exporter keeps the buffer alive until every importer has called cm_ipc_close.
+ * Ordering across processes is the caller's (e.g. a barrier after each rank's
+ * cm_synchronize). */
+typedef struct cm_ipc_handle {
+    unsigned char handle[64];   /* cudaIpcMemHandle_t of the allocation holding the buffer */
+    uint64_t      offset;       /* bytes from the allocation's start to the buffer */
+    int           device;       /* the exporting process's device ordinal */
+    int           reserved;
+} cm_ipc_handle_t;
+int cm_ipc_export(const void* dev_ptr, cm_ipc_handle_t* handle);
+int cm_ipc_open(const cm_ipc_handle_t* handle, void** dev_ptr);
+int cm_ipc_close(void* dev_ptr);
+
 /* ---- buffers: mirror of inference_buf_* (_buf_impl.py:25-236) ------------------
  * An owner buffer is a device allocation plus a pinned host mirror of the same
  * size; views alias a slice of an owner.  `virt` is the host mirror, `dev` the
