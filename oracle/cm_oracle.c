@@ -184,6 +184,17 @@ static void mm_range(void* p, uint64_t lo, uint64_t hi) {
 void orc_matmul(const int16_t* a, const int16_t* b, int16_t* c, uint32_t n, uint32_t k, uint32_t m,
                 uint32_t batch, uint32_t a_batch_stride, uint32_t b_batch_stride,
                 uint32_t c_batch_stride) {
+    if (batch > 1 && (uint64_t)c_batch_stride < (uint64_t)n * m) {
+        /* output slices of different batch steps overlap: the reference's batch loop runs in
+           order and later steps overwrite earlier ones (:108-112), so the steps run one after
+           another here too (rows of one step never overlap) */
+        for (uint32_t bi = 0; bi < batch; ++bi) {
+            mm_ctx x = {a + (uint64_t)bi * a_batch_stride, b + (uint64_t)bi * b_batch_stride,
+                        c + (uint64_t)bi * c_batch_stride, n, k, m, 0, 0, 0, NULL, NULL, NULL};
+            par_for(n, mm_range, &x);
+        }
+        return;
+    }
     mm_ctx x = {a, b, c, n, k, m, a_batch_stride, b_batch_stride, c_batch_stride, NULL, NULL, NULL};
     par_for((uint64_t)batch * n, mm_range, &x);
 }

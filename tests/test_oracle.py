@@ -180,3 +180,19 @@ def test_fast_matmul_matches_port(port):
     for (n, k, m) in [(17, 300, 9), (5, 4096, 7), (64, 64, 64)]:
         a, b = rand16(rng, n * k), rand16(rng, k * m)
         assert_same(fast.matmul_2d(a.reshape(n, k), b.reshape(k, m)), port.matmul(a, b, n, k, m), "fast")
+
+
+@pytest.mark.skipif(not oracle.have_ref(), reason="oracle/_ref not built")
+@pytest.mark.parametrize("c_bs", [0, 7, 15000, 29999])
+def test_overlapping_batch_outputs_follow_batch_order(port, c_bs):
+    """c_batch_stride < n*m: output slices of different batch steps overlap and the
+    reference's batch loop lets later steps win; the threaded restatement must keep that
+    order (sizes large enough that the work is split across threads)."""
+    n, k, m, batch = 200, 300, 150, 3
+    rng = np.random.default_rng(c_bs)
+    a = rng.integers(-32768, 32768, batch * n * k).astype(np.int16)
+    b = rng.integers(-32768, 32768, batch * k * m).astype(np.int16)
+    init = np.full((batch - 1) * c_bs + n * m, -23131, np.int16)
+    got = port.matmul(a, b, n, k, m, batch, n * k, k * m, c_bs, c=init.copy())
+    want = oracle.ref().matmul(a, b, n, k, m, batch, n * k, k * m, c_bs, c=init.copy())
+    assert np.array_equal(got, want)
