@@ -22,6 +22,10 @@ struct Context {
     // 128-column GEMM tiles run on CTA pairs (tcgen05 cta_group::2); CM_GEMM_PAIRS=0 turns it off
     int gemm_pairs = 1;
     int gemm_wa = 1;          // weights-as-A GEMM for conv outputs of at most 64 channels
+    // large MatMul calls split batch chunk j+1 on this stream while chunk j's GEMM runs on
+    // the caller's (CM_MATMUL_OVERLAP=0 at cm_init turns it off)
+    cudaStream_t aux_stream = nullptr;
+    int matmul_overlap = 1;
 };
 
 Context* ctx();                      // nullptr before cm_init

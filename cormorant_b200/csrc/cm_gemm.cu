@@ -34,6 +34,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "cm_async.cuh"
 #include "cm_gemm.cuh"
@@ -44,8 +45,10 @@ namespace {
 constexpr int BM = 128, BK = 128;
 constexpr int PLANE_TILE = BM * BK;                 // 16 KB: one plane of a 128 x 128 operand tile
 constexpr int OPERAND_TILE = 2 * PLANE_TILE;        // A hi + lo = 32 KB
-// The whole per-CTA maximum is requested (1 CTA per SM either way), so every
-// operand descriptor stays inside this CTA's own allocation with margin.
+// The per-CTA maximum of dynamic shared memory.  A GEMM CTA requests only what its
+// configuration uses (Cfg::SMEM_LAUNCH, 190-205 KB: still one GEMM CTA per SM), which
+// leaves room beside it for a small CTA of another kernel -- the split pre-pass of the
+// next batch chunk of a large MatMul runs there while this chunk's GEMM computes.
 constexpr int SMEM_BYTES = 232448;
 constexpr uint32_t TMEM_COLS = 512;
 
@@ -85,7 +88,9 @@ struct Cfg {
     // WA: a 16 x 16 int16 transpose buffer per epilogue warp, after the barriers
     static constexpr int XPOSE_BYTES = WA ? EPI_WARPS * 512 : 0;
     static constexpr int SMEM_USED = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/ + XPOSE_BYTES;
-    static_assert(SMEM_USED <= SMEM_BYTES, "shared memory budget");
+    static constexpr int SMEM_LAUNCH = (SMEM_USED + 1023) / 1024 * 1024;
+    static_assert(SMEM_LAUNCH <= SMEM_BYTES, "shared memory budget");
+    static_assert(2 * SMEM_LAUNCH > SMEM_BYTES, "one GEMM CTA per SM");
     static_assert(NBUF * ACC_COLS <= TMEM_COLS, "TMEM budget");
 };
 
@@ -1266,7 +1271,8 @@ template <int TBN, int CG, bool WA = false>
 int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s) {
     static int per_sm_clusters = -1;   // co-resident clusters of CG CTAs (one CTA per SM)
     if (per_sm_clusters < 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             Cfg<TBN, CG, WA>::SMEM_LAUNCH);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
         int n = cx->sm_count / CG;
         if (CG > 1) {
@@ -1274,7 +1280,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * n);
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
-            q.dynamicSmemBytes = SMEM_BYTES;
+            q.dynamicSmemBytes = Cfg<TBN, CG, WA>::SMEM_LAUNCH;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
@@ -1301,13 +1307,13 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            gemm_q88_kernel<TBN, CG, WA><<<clusters, Cfg<TBN, CG, WA>::THREADS, SMEM_BYTES, s>>>(ta, tb, g);
+            gemm_q88_kernel<TBN, CG, WA><<<clusters, Cfg<TBN, CG, WA>::THREADS, Cfg<TBN, CG, WA>::SMEM_LAUNCH, s>>>(ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * clusters);
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
-            q.dynamicSmemBytes = SMEM_BYTES;
+            q.dynamicSmemBytes = Cfg<TBN, CG, WA>::SMEM_LAUNCH;
             q.stream = s;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
@@ -1435,10 +1441,11 @@ int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
                uint32_t nbt, int8_t* planes, int32_t* rowterm, const int16_t* bias, cudaStream_t s) {
     const uint64_t total = (uint64_t)rows * nbt;
     if (total == 0) return CM_OK;
-    const unsigned grid = grid_for(cx, total * 32, 256, 16);
+    // 128-thread blocks (48 registers a thread): one fits on an SM beside a GEMM CTA
+    const unsigned grid = grid_for(cx, total * 32, 128, 16);
     {
         ProfScope ps_(PK_SPLIT, s);
-        split_rows_kernel<<<grid, 256, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
+        split_rows_kernel<<<grid, 128, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
     }
     count_launch();
     return CM_OK;
@@ -1461,7 +1468,8 @@ int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld
     if (e != cudaSuccess) return cuda_error(e, "memset colterm");
     if (K == 0) return CM_OK;
     const uint32_t vec_threads = (cols + 7) / 8;
-    const uint32_t block = std::min<uint32_t>(256, (vec_threads + 31) / 32 * 32);
+    // at most 128 threads (64 registers a thread): one block fits on an SM beside a GEMM CTA
+    const uint32_t block = std::min<uint32_t>(128, (vec_threads + 31) / 32 * 32);
     const uint32_t gx = (vec_threads + block - 1) / block;
     const uint32_t k_chunk = pick_k_chunk(K, (uint64_t)gx * nbt, cx->sm_count);
     const uint32_t C_pad = packed ? 128u : pad_c(cols);
@@ -1533,6 +1541,78 @@ int matmul_rows_impl(const Context* cx, const int16_t* a, const int16_t* b, int1
     return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul (row-strided)");
 }
 
+// A large batched MatMul as `chunks` batch chunks whose split pre-passes run on the
+// context's side stream, chunk j + 1's while chunk j's GEMM runs on the caller's stream:
+// the splits are HBM-bound, the GEMM tensor-bound, and the GEMM CTAs leave room on every
+// SM for one split CTA (their shared-memory request and the splits' 128-thread blocks are
+// sized for it).  Two plane buffers per advancing operand alternate between chunks; a
+// broadcast operand (batch stride 0) is split once.  Events order every reuse; the
+// caller's stream waits for the side stream before the scratch is released, so the call
+// is stream-ordered on `s` like the one-shot path (and captures into a graph the same way).
+int matmul_chunked(const Context* cx, const int16_t* a, const int16_t* b, int16_t* c, uint32_t n, uint32_t k,
+                   uint32_t m, uint32_t batch, uint32_t a_bs, uint32_t b_bs, uint32_t c_bs, unsigned epi,
+                   const int16_t* bias, cudaStream_t s, uint32_t chunks) {
+    const uint32_t cb = (batch + chunks - 1) / chunks;
+    chunks = (batch + cb - 1) / cb;
+    const bool a_adv = a_bs != 0, b_adv = b_bs != 0;
+    const uint64_t K_pad = pad_k(k);
+    const bool packed = m <= 64;
+    const uint64_t a_bytes = ((uint64_t)(a_adv ? cb : 1) * 2 * n * K_pad + 255) & ~255ull;
+    const uint64_t b_bytes = ((uint64_t)(b_adv ? cb : 1) * k * (packed ? 128 : 2 * pad_c(m)) + 255) & ~255ull;
+    const uint64_t rt_bytes = ((uint64_t)(a_adv ? cb : 1) * n * 4 + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)(b_adv ? cb : 1) * m * 4 + 255) & ~255ull;
+    const int na = a_adv ? 2 : 1, nbuf = b_adv ? 2 : 1;
+    void* scratch = nullptr;
+    int rc = scratch_alloc(&scratch, na * (a_bytes + rt_bytes) + nbuf * (b_bytes + ct_bytes), s);
+    if (rc) return rc;
+    uint8_t* q = (uint8_t*)scratch;
+    int8_t* A[2] = {nullptr, nullptr};
+    int8_t* B[2] = {nullptr, nullptr};
+    int32_t* RT[2] = {nullptr, nullptr};
+    int32_t* CT[2] = {nullptr, nullptr};
+    for (int i = 0; i < na; ++i) { A[i] = (int8_t*)q; q += a_bytes; RT[i] = (int32_t*)q; q += rt_bytes; }
+    for (int i = 0; i < nbuf; ++i) { B[i] = (int8_t*)q; q += b_bytes; CT[i] = (int32_t*)q; q += ct_bytes; }
+    cudaStream_t aux = cx->aux_stream;
+    std::vector<cudaEvent_t> ev(2 * chunks + 2, nullptr);
+    for (auto& e : ev)
+        if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) rc = set_error(CM_ECUDA, "event");
+    cudaEvent_t ev_start = ev[2 * chunks], ev_join = ev[2 * chunks + 1];
+    if (!rc) {
+        cudaEventRecord(ev_start, s);
+        cudaStreamWaitEvent(aux, ev_start, 0);      // the inputs are ready when the caller's stream is
+        if (!a_adv) rc = split_rows(cx, a, 0, k, n, k, 1, A[0], RT[0], nullptr, aux);
+        if (!rc && !b_adv) rc = split_kn(cx, b, 0, m, m, k, 1, B[0], CT[0], aux, packed);
+    }
+    for (uint32_t j = 0; j < chunks && !rc; ++j) {
+        const uint32_t z0 = j * cb, nb = std::min(cb, batch - z0), buf = j & 1u;
+        if (j >= 2) cudaStreamWaitEvent(aux, ev[2 * (j - 2) + 1], 0);   // chunk j-2's GEMM has read the buffers
+        if (a_adv) rc = split_rows(cx, a + (uint64_t)z0 * a_bs, a_bs, k, n, k, nb, A[buf], RT[buf], nullptr, aux);
+        if (!rc && b_adv) rc = split_kn(cx, b + (uint64_t)z0 * b_bs, b_bs, m, m, k, nb, B[buf], CT[buf], aux, packed);
+        if (rc) break;
+        cudaEventRecord(ev[2 * j], aux);
+        cudaStreamWaitEvent(s, ev[2 * j], 0);
+        const uint32_t ia = a_adv ? buf : 0u, ib = b_adv ? buf : 0u;
+        GemmPlan p{A[ia], n, a_adv ? nb : 1u, B[ib], m, b_adv ? nb : 1u, k, (uint32_t)K_pad, pad_c(m), RT[ia], CT[ib],
+                   c + (uint64_t)z0 * c_bs, m, 1, c_bs, nb};
+        p.b_packed = packed ? 1u : 0u;
+        p.epi = (epi & 1u) | ((epi & 2u) << 1);   // the kernel's bias-row bit is 4
+        p.resid = (epi & 2u) ? bias : nullptr;
+        rc = gemm_launch(cx, p, s);
+        cudaEventRecord(ev[2 * j + 1], s);
+    }
+    // join the side stream before the scratch goes back to the pool (also on an error path)
+    if (ev_join) {
+        cudaEventRecord(ev_join, aux);
+        cudaStreamWaitEvent(s, ev_join, 0);
+    }
+    for (auto& e : ev)
+        if (e) cudaEventDestroy(e);
+    scratch_free(scratch, s);
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul (chunked)");
+}
+
 // MatMul with an optional fused epilogue (epi bit 1: + bias[j] saturating, bit 0: ReLU).
 int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m, unsigned batch,
                 unsigned a_batch_stride, unsigned b_batch_stride, unsigned c_batch_stride, unsigned epi,
@@ -1591,6 +1671,14 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
         // every 128-row tile would hold one row; folded, they are the rows of ONE GEMM
         // with those row pitches.
         return matmul_rows_impl(cx, a, b, c, batch, k, m, a_batch_stride, c_batch_stride, epi, bias, s);
+    }
+    if (cx->matmul_overlap && batch >= 2) {
+        // large calls: batch chunks of >= 2^33 multiply-adds, at most 8
+        const uint64_t by_work = (uint64_t)(macs >> 33);
+        const uint32_t chunks = (uint32_t)std::min<uint64_t>(std::min<uint64_t>(batch, 8), by_work);
+        if (chunks >= 2)
+            return matmul_chunked(cx, a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, epi,
+                                  bias, s, chunks);
     }
     const uint32_t a_batches = a_batch_stride == 0 ? 1u : batch;
     const uint32_t b_batches = b_batch_stride == 0 ? 1u : batch;

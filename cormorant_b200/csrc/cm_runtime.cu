@@ -144,6 +144,7 @@ int cm_init(const char* instance) {
     if (g_ready) {
         cudaSetDevice(g_ctx.device);
         cudaFree(g_ctx.status);
+        if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
         g_ready = false;
     }
     e = cudaSetDevice(dev);
@@ -172,6 +173,13 @@ int cm_init(const char* instance) {
     if (gw && *gw) c.gemm_wa = atoi(gw) != 0;
     const char* dm = getenv("CM_DIRECT_MAX_MACS");
     if (dm && *dm) c.direct_max_macs = (uint64_t)strtoull(dm, nullptr, 10);
+    const char* mo = getenv("CM_MATMUL_OVERLAP");
+    if (mo && *mo) c.matmul_overlap = atoi(mo) != 0;
+    e = cudaStreamCreateWithFlags(&c.aux_stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        cudaFree(c.status);
+        return cuda_error(e, "cudaStreamCreate(aux)");
+    }
     g_ctx = c;
     g_ready = true;
     return CM_OK;
@@ -183,6 +191,7 @@ int cm_release(void) {
     cudaSetDevice(g_ctx.device);
     cudaDeviceSynchronize();
     cudaFree(g_ctx.status);
+    if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
     g_ready = false;
     return CM_OK;
 }

@@ -209,3 +209,43 @@ def test_row_strided_full_size(cm, port):
     c = dev(init)
     cm.MatmulKernel(dev(a), dev(b), c, 1, k, m, rows, a_bs, 0, c_bs)
     assert_same(host(c), port.matmul(a, b, 1, k, m, rows, a_bs, 0, c_bs, c=init.copy()), "row-strided 4096x512x1000")
+
+
+# Large calls run as batch chunks, each chunk's split overlapping the previous chunk's GEMM
+# (at least 2^33 multiply-adds a chunk): broadcast operands, gapped outputs, the fused
+# epilogue.  Checked on sampled rows, the last row of the last batch step included.
+CHUNKED = [(1024, 1024, 512, 48, "a"), (1024, 1024, 512, 48, "b"), (768, 2048, 384, 40, None),
+           (512, 1024, 40, 160, None)]
+
+
+@pytest.mark.big
+@pytest.mark.parametrize("n,k,m,batch,bcast", CHUNKED)
+@pytest.mark.parametrize("epi", [0, 3])
+def test_chunked_batches(cm, port, n, k, m, batch, bcast, epi):
+    rng = np.random.default_rng(n + k + m + batch + epi)
+    a_bs = 0 if bcast == "a" else n * k
+    b_bs = 0 if bcast == "b" else k * m
+    c_bs = n * m + 24                                   # a gap after every output slice
+    a = rand16(rng, (batch - 1) * a_bs + n * k, -1024, 1024)
+    b = rand16(rng, (batch - 1) * b_bs + k * m, -1024, 1024)
+    bias = rand16(rng, m, -4096, 4096)
+    init = np.full((batch - 1) * c_bs + n * m, -23131, np.int16)
+    c = dev(init)
+    if epi:
+        cm.kernels.MatmulKernelFused(dev(a), dev(b), c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi,
+                                     bias=dev(bias))
+    else:
+        cm.MatmulKernel(dev(a), dev(b), c, n, k, m, batch, a_bs, b_bs, c_bs)
+    got = host(c)
+    bidx = rng.integers(0, batch, 64)
+    ridx = rng.integers(0, n, 64)
+    bidx[0], ridx[0] = batch - 1, n - 1
+    want = port.matmul_rows(a, b, n, k, m, a_bs, b_bs, bidx, ridx)
+    if epi & 2:
+        want = np.clip(want.astype(np.int32) + bias.astype(np.int32), -32768, 32767).astype(np.int16)
+    if epi & 1:
+        want = np.maximum(want, 0)
+    rows = np.stack([got[z * c_bs + r * m: z * c_bs + (r + 1) * m] for z, r in zip(bidx, ridx)])
+    assert_same(rows, want, f"chunked {n}x{k}x{m} b{batch} bcast={bcast} epi={epi}")
+    gaps = np.concatenate([got[z * c_bs + n * m:(z + 1) * c_bs] for z in range(batch - 1)])
+    assert (gaps == -23131).all()                       # the words between slices stay untouched
