@@ -630,6 +630,12 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
         }
     }
 
+    // AVG: this strip's reciprocals for rows whose PH taps are all inside the plane (all
+    // but the first and last output rows), kept in registers
+    float inv_in[V];
+#pragma unroll
+    for (int v = 0; v < V; ++v) inv_in[v] = TYPE == P_AVG ? inv_tab[p.cip ? PH * PW : PH * vc[v]] : 0.0f;
+
     uint32_t k = 0;
     for (uint64_t plane = blockIdx.x; plane < planes; plane += gridDim.x, ++k) {
         const uint32_t b = k % kPlaneBufs;
@@ -686,7 +692,17 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
                         vr += (ih >= 0 && ih < (int32_t)in_h);
                     }
                 }
-                int16_t out[V];
+                // Results before the int16 narrowing.  With at most 3 x 3 taps the Q16.16
+                // accumulator (the word sum a times 2^8) cannot wrap, and the reference's
+                // power-of-two scales are exact, so (PoolingKernel.cpp:168-172, 253-263):
+                //   AVG  floor(rn(float(acc) * 2^-16 * inv) at 2^-16) >> 8 = floor(rn(a * inv)),
+                //        inv = rn(1 / denom)
+                //   LP2  floor(sqrt_rn(rn(acc)) * 2^8) >> 8 = floor(sqrt_rn(rn(acc))) with acc the
+                //        wrapped sum of squares (negative -> NaN -> 0); a root >= 2^15 wraps the
+                //        Q16.16 word (AP_WRAP) and narrows to -32768
+                //   LP1  the sum of |x|, MAX the largest word
+                // then one saturating pack per pair of outputs.
+                int32_t res[V];
 #pragma unroll
                 for (int v = 0; v < V; ++v) {
                     int32_t a = ring[0][v];
@@ -696,27 +712,25 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
                         else a = (int32_t)((uint32_t)a + (uint32_t)ring[r][v]);
                     }
                     if (TYPE == P_AVG) {
-                        // float(acc) * 2^-16 * (1/denom), floored at 2^-16: the power-of-two
-                        // scales are exact, so this is floor(rn(float(a * 256) * (1/denom)))
-                        const float f = __fmul_rn(__int2float_rn((int32_t)((uint32_t)a * 256u)),
-                                                  inv_tab[p.cip ? PH * PW : vr * vc[v]]);
-                        out[v] = narrow_acc(f >= 2147483648.0f ? 0x80000000u : (uint32_t)__float2int_rd(f));
+                        const float inv = (p.cip || vr == (uint32_t)PH) ? inv_in[v] : inv_tab[vr * vc[v]];
+                        res[v] = __float2int_rd(__fmul_rn(__int2float_rn(a), inv));
+                    } else if (TYPE == P_LP2) {
+                        const int32_t q = __float2int_rz(__fsqrt_rn(__int2float_rn(a)));   // NaN -> 0
+                        res[v] = q >= 32768 ? -32768 : q;
                     } else {
-                        uint32_t acc;
-                        if (TYPE == P_MAX) acc = (uint32_t)(a * 256);
-                        else if (TYPE == P_LP2) acc = (uint32_t)a;
-                        else acc = (uint32_t)a * 256u;
-                        out[v] = finalize<TYPE>(acc, 0);
+                        res[v] = a;
                     }
                 }
                 int16_t* dst = yp + (uint64_t)oh * p.out_w + ow0;
                 if (nv == (uint32_t)V && V == 4 && ((uintptr_t)dst & 7u) == 0) {
-                    *(uint2*)dst = make_uint2((uint32_t)(uint16_t)out[0] | ((uint32_t)(uint16_t)out[1 % V] << 16),
-                                              (uint32_t)(uint16_t)out[2 % V] | ((uint32_t)(uint16_t)out[3 % V] << 16));
+                    uint32_t lo, hi;
+                    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(lo) : "r"(res[1 % V]), "r"(res[0]));
+                    asm("cvt.pack.sat.s16.s32 %0, %1, %2;" : "=r"(hi) : "r"(res[3 % V]), "r"(res[2 % V]));
+                    *(uint2*)dst = make_uint2(lo, hi);
                 } else {
 #pragma unroll
                     for (int v = 0; v < V; ++v)
-                        if ((uint32_t)v < nv) dst[v] = out[v];
+                        if ((uint32_t)v < nv) dst[v] = sat16(res[v]);
                 }
             }
         }
