@@ -223,12 +223,17 @@ class MatmulSweep:
                 continue
             cm.MatmulKernel(t[0], t[1], t[2], n, k, m, b, *self._st(n, k, m), stream=stream)
 
-    def step_into(self, cm, stream, outs):
-        """The step with output i written at device address outs[i] (the root's buffers)."""
-        for (n, k, m, b), t, o in zip(self.shapes, self.bufs, outs):
+    def step_into(self, cm, stream, outs, before=None, after=None):
+        """The step with output i written at device address outs[i]; before(i) / after(i)
+        run around output i's kernels."""
+        for i, ((n, k, m, b), t, o) in enumerate(zip(self.shapes, self.bufs, outs)):
             if t is None:
                 continue
+            if before:
+                before(i)
             cm.MatmulKernel(t[0], t[1], o, n, k, m, b, *self._st(n, k, m), stream=stream)
+            if after:
+                after(i)
 
     def gather_outputs(self):
         """(local output shard, items over all ranks, words per item) of each output of a step."""
@@ -345,9 +350,13 @@ class VectorOPSweep:
         for op in VOP_OPS:
             cm.VectorOPKernel(self.a, self.b, self.c, self.n, op, stream=stream)
 
-    def step_into(self, cm, stream, outs):
-        for op, o in zip(VOP_OPS, outs):
+    def step_into(self, cm, stream, outs, before=None, after=None):
+        for i, (op, o) in enumerate(zip(VOP_OPS, outs)):
+            if before:
+                before(i)
             cm.VectorOPKernel(self.a, self.b, o, self.n, op, stream=stream)
+            if after:
+                after(i)
 
     def gather_outputs(self):
         return [(self.c, VOP_N, 1) for _ in VOP_OPS]
@@ -447,9 +456,13 @@ class PoolSweep:
         cm.PoolingKernel(self.x, self.y if y is None else y, self.nb, C, H, W, oh, ow, ph, pw, sh, sw, pt, pl, dh,
                          dw, t, lp, cip, stream=stream)
 
-    def step_into(self, cm, stream, outs):
-        for c, o in zip(POOL_SWEEP, outs):
+    def step_into(self, cm, stream, outs, before=None, after=None):
+        for i, (c, o) in enumerate(zip(POOL_SWEEP, outs)):
+            if before:
+                before(i)
             self._one(cm, c, stream, o)
+            if after:
+                after(i)
 
     def step(self, cm, stream):
         for c in POOL_SWEEP:
@@ -603,13 +616,17 @@ class NetworkBench:
         torch.cuda.synchronize()
         return g, n
 
-    def step_into(self, cm, stream, outs):
+    def step_into(self, cm, stream, outs, before=None, after=None):
         """The call list with the network output at outs[0], replayed as its own CUDA graph."""
         if getattr(self, "_into", None) is None or self._into[0] != outs[0]:
             bufs = dict(self.bufs)
             bufs[self.net.resolve(self.net.output)] = int(outs[0])
             self._into = (outs[0], self._capture(bufs)[0])
+        if before:
+            before(0)
         self._into[1].replay()
+        if after:
+            after(0)
 
     def gather_outputs(self):
         """ResNet: the logits of every image; LeNet runs replicas (nothing to gather)."""
@@ -683,6 +700,7 @@ class NetworkBench:
             # two device input buffers: step i+1's input crosses PCIe on a copy stream while
             # step i computes; a copy waits until the forward that last read its buffer is done
             self.copy_stream = torch.cuda.Stream()
+            self.copy_times = []
             self.xbufs = [self.bufs[self.net.input], torch.empty_like(self.bufs[self.net.input])]
             self.copied = [torch.cuda.Event(), torch.cuda.Event()]
             self.consumed = [None, None]
@@ -735,8 +753,23 @@ class NetworkBench:
         with torch.cuda.stream(self.copy_stream):
             if self.consumed[b] is not None:
                 self.copy_stream.wait_event(self.consumed[b])
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(self.copy_stream)
             self.xbufs[b].copy_(self.hx, non_blocking=True)
+            t1.record(self.copy_stream)
             self.copied[b].record(self.copy_stream)
+            self.copy_times.append((t0, t1))
+
+    def e2e_extra(self):
+        """The input copies' own device time (host -> device over PCIe): how much of a step
+        the copy takes when the host is busy or idle."""
+        if not getattr(self, "copy_times", None):
+            return {}
+        ms = [a.elapsed_time(b) for a, b in self.copy_times[1:]] or [0.0]
+        med = sorted(ms)[len(ms) // 2]
+        return {"h2d_copy_ms_median": round(med, 4), "h2d_copy_ms_max": round(max(ms), 4),
+                "h2d_gbs_median": round(self.hx.numel() * 2 / (med * 1e-3) / 1e9, 1) if med > 0 else None}
 
     def _e2e_pipelined(self):
         import torch
@@ -1098,6 +1131,8 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
                "d2h_bytes_per_step": int(env.reduce(float(wl.d2h), "sum")),
                "path": getattr(wl, "e2e_path", "cm_buf_sync_to_device -> run_* (cm_* C ABI) -> "
                                                 "cm_buf_sync_from_device, pinned host mirrors")}
+        if hasattr(wl, "e2e_extra"):
+            e2e.update(wl.e2e_extra())
         wl.e2e_release()
         torch.cuda.empty_cache()
 
@@ -1133,8 +1168,11 @@ def measure_gathers(wl, env: Env, ms_per_step: float, scale: float, K: int) -> d
       to_root        after the step, every rank sends its shards and rank 0 receives each into its
                      offset (grouped NCCL send/recv);
       all_gather     after the step, every output to every rank (NCCL all_gather_into_tensor).
-    The fused form's root output is checked word for word against the NCCL gather of the same
-    step's last output."""
+      copy_to_root   the other ranks compute each output into their own memory and push it to
+                     rank 0 with one copy-engine cudaMemcpyAsync (cm_copy_async, NVLink) on a copy
+                     stream while the next output computes; K whole steps timed.
+    The fused and copy forms' root output is checked word for word against the NCCL gather of
+    the same step's last output."""
     import torch
     from cormorant_b200 import sharding
     spec = wl.gather_outputs() if hasattr(wl, "gather_outputs") else []
@@ -1198,12 +1236,64 @@ def measure_gathers(wl, env: Env, ms_per_step: float, scale: float, K: int) -> d
                                 "ingress_gbs": round(ingress / (f_ms * 1e-3) / 1e9, 1) if f_ms > 0 else None,
                                 "value_with_gather": wl.units_total / (f_ms * 1e-3) / scale,
                                 "steps": K, "matches_nccl_gather": same}
+        # copy engines: the other ranks compute output i into their own memory, then push it to
+        # rank 0 with one cudaMemcpyAsync on a copy stream while output i+1 computes
+        import ctypes as C
+        L = env.L
+        locs = None
+        if rank == 0:
+            outs = addrs
+        else:
+            locs = [torch.empty(max(sharding.shard_range(total, rank, world)[1] * per_item, 1), dtype=torch.int16,
+                                device="cuda") for _, total, per_item in spec]
+            outs = [t.data_ptr() for t in locs]
+        cstream = torch.cuda.Stream()
+        copied = [None] * len(spec)
+
+        def before(i):
+            if copied[i] is not None:
+                stream.wait_event(copied[i])      # last step's push of this buffer is done
+
+        def after(i):
+            if rank == 0:
+                return
+            _, total, per_item = spec[i]
+            ev = torch.cuda.Event()
+            ev.record(stream)
+            cstream.wait_event(ev)
+            nbytes = sharding.shard_range(total, rank, world)[1] * per_item * 2
+            L.cm_copy_async(C.c_void_p(addrs[i]), C.c_void_p(outs[i]), nbytes, C.c_void_p(cstream.cuda_stream))
+            done = torch.cuda.Event()
+            done.record(cstream)
+            copied[i] = done
+        for _ in range(2):
+            wl.step_into(env.cm, stream, outs, before, after)
+        stream.wait_stream(cstream)
+        torch.cuda.synchronize()
+        env.barrier()
+        cs_, ce_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        cs_.record(stream)
+        cstream.wait_event(cs_)
+        for _ in range(K):
+            wl.step_into(env.cm, stream, outs, before, after)
+        stream.wait_stream(cstream)
+        ce_.record(stream)
+        torch.cuda.synchronize()
+        env.barrier()
+        c_ms = env.reduce(cs_.elapsed_time(ce_), "max") / K
+        same = bool(torch.equal(ro.tensors[-1], last_nccl)) if rank == 0 else None
+        res["copy_to_root"] = {"ms_per_step": c_ms,
+                               "ingress_gbs": round(ingress / (c_ms * 1e-3) / 1e9, 1) if c_ms > 0 else None,
+                               "value_with_gather": wl.units_total / (c_ms * 1e-3) / scale,
+                               "steps": K, "matches_nccl_gather": same}
+        outs = locs = None
         ro.close()
     del last_nccl
     torch.cuda.empty_cache()
     env.barrier()
     res["note"] = ("value_with_gather = units / time of a step whose outputs end up on rank 0 (fused_to_root: the "
-                   "kernels write there directly, K steps timed; to_root / all_gather: ms_per_step + the NCCL "
+                   "kernels write there directly; copy_to_root: copy-engine pushes overlapped with the next output's "
+                   "kernels; both K steps timed; to_root / all_gather: ms_per_step + the NCCL "
                    "collective's ms); ingress_gbs = bytes arriving at one GPU / that time; the receiving GPU's "
                    "NVLink ingress bounds every form")
     return res

@@ -70,6 +70,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_ipc_export": (C.c_int, [_p, _p]),
     "cm_ipc_open": (C.c_int, [_p, C.POINTER(_p)]),
     "cm_ipc_close": (C.c_int, [_p]),
+    "cm_copy_async": (C.c_int, [_p, _p, C.c_size_t, _p]),
     "cm_buf_alloc": (_p, [_u]),
     "cm_buf_free": (None, [_p]),
     "cm_buf_retain": (None, [_p]),

@@ -8,7 +8,9 @@
 // memory with ordinary stores, so each output word crosses NVLink once, while
 // the kernel that computes it runs, and no SM time is spent on a copy.  Only
 // plain stores reach the peer's memory: no TMA (bulk or tensor) copy and no
-// library kernel is given a peer address.
+// library kernel is given a peer address.  Alternatively a rank computes into
+// its own memory and pushes each finished output with cm_copy_async (one
+// cudaMemcpyAsync, a copy engine over NVLink) while its next output computes.
 #include <cuda.h>
 
 #include <cstring>
@@ -112,4 +114,14 @@ extern "C" int cm_ipc_close(void* dev_ptr) {
         if (e != cudaSuccess) return cuda_error(e, "cudaIpcCloseMemHandle");
     }
     return CM_OK;
+}
+
+extern "C" int cm_copy_async(void* dst, const void* src, size_t bytes, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (bytes == 0) return CM_OK;
+    if (!dst || !src) return set_error(CM_EINVAL, "cm_copy_async: null pointer");
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_copy_async");
 }

@@ -358,6 +358,10 @@ typedef struct cm_ipc_handle {
 int cm_ipc_export(const void* dev_ptr, cm_ipc_handle_t* handle);
 int cm_ipc_open(const cm_ipc_handle_t* handle, void** dev_ptr);
 int cm_ipc_close(void* dev_ptr);
+/* One device-to-device copy enqueued on `stream` (a copy engine; `dst` or `src` may be
+ * a cm_ipc_open mapping of a peer GPU's buffer): pushes a finished output shard to the
+ * root while the next kernels run. */
+int cm_copy_async(void* dst, const void* src, size_t bytes, cm_stream_t stream);
 
 /* ---- buffers: mirror of inference_buf_* (_buf_impl.py:25-236) ------------------
  * An owner buffer is a device allocation plus a pinned host mirror of the same

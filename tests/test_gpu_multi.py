@@ -1,7 +1,8 @@
 """The fused gather on 2 GPUs (skipped with fewer): every rank's MatMul, VectorOP and
 Pooling kernels write their batch shard straight into rank 0's full-size output buffers
 (sharding.RootOutputs, CUDA IPC over NVLink), and rank 0's buffers must equal the oracle
-word for word; the NCCL gathers (to rank 0, to every rank) are checked the same way.
+word for word; the copy-engine push (cm_copy_async into the mapped buffer) and the NCCL
+gathers (to rank 0, to every rank) are checked the same way.
 
 Run as spawned child processes, one per GPU, NCCL on 127.0.0.1 with NVLS off and a short
 process-group timeout; the parent waits with a limit and reports each rank's verdict."""
@@ -62,6 +63,18 @@ def _worker(rank, port, q):
             if rank == 0:
                 want = port_.matmul(a, b, n, k, m, B)
                 verdicts.append(("matmul fused", np.array_equal(ro.tensors[0].cpu().numpy(), want)))
+                ro.tensors[0].fill_(-23131)
+            dist.barrier()
+            # the copy-engine push: every rank copies its local shard into the root's buffer
+            import ctypes as C
+            from cormorant_b200._lib import check, lib
+            s = torch.cuda.Stream()
+            check(lib().cm_copy_async(C.c_void_p(ro.address(0, lo * n * m)), C.c_void_p(local.data_ptr()),
+                                      cnt * n * m * 2, C.c_void_p(s.cuda_stream)))
+            s.synchronize()
+            dist.barrier()
+            if rank == 0:
+                verdicts.append(("matmul copy push", np.array_equal(ro.tensors[0].cpu().numpy(), want)))
                 verdicts.append(("matmul to_root", np.array_equal(full_root.cpu().numpy(), want)))
             verdicts.append(("matmul all_gather", port_ is None or np.array_equal(full_all.cpu().numpy(), want)))
             ro.close()
