@@ -15,8 +15,8 @@ already carries every intermediate shape, computed by cormorant_b200.scheduler's
 shape rules), and helper / numpy_helper build and read the same plain objects.  For
 every scheduled node the text of the reference's emit_call(layouts) is parsed into
 (kernel, buffer names, scalar arguments), with the broadcast CHUNK / CHUNK_STRIDE
-macros given the values generate_header() defines for them; buffer allocations are
-CodeGenerator's layouts.  Graphs the reference refuses record its SchedulerError.
+macros given the values generate_header() defines for them; buffer allocations and layouts
+(numel, alloc, n_chunks, chunk, stride) are CodeGenerator's.  Graphs the reference refuses record its SchedulerError.
 
 For LeNet-5 (batch 1 and 3) the reference's weights/<name>.dat files of the weights
 above its 4096-word threshold (generate_weight_dat) and the expected output words of
@@ -234,6 +234,7 @@ def main():
                    if isinstance(sn, src.nodes.ReshapeNode)}
         rec = {"calls": _calls_of(gen, src),
                "allocs": {k: v.alloc for k, v in gen._layouts.items()},
+               "layouts": {k: [v.numel, v.alloc, v.n_chunks, v.chunk, v.stride] for k, v in gen._layouts.items()},
                "aliases": aliases,
                "input": og.input_tensors[0].onnx_name, "output": og.output_tensors[0].onnx_name}
         result["graphs"][name] = rec

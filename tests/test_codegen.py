@@ -258,3 +258,43 @@ def test_reference_files_run_unchanged_on_gpu(tmp_path, batch, mode):
     r = subprocess.run([str(exe), "3"], capture_output=True, text=True, timeout=300, cwd=tmp_path)
     assert r.returncode == 0, r.stdout + r.stderr
     assert "test_inference PASSED" in r.stdout
+
+
+def _net_from_reference_list(name):
+    """A Net whose calls, buffer sizes and constant layouts are the reference scheduler's own
+    (calllists.json), with the graph's constant words placed in those layouts; nothing comes
+    from scheduler.derive."""
+    import json
+    from cormorant_b200.networks import Net
+    from cormorant_b200.scheduler import Layout, _const_words, infer_shapes
+    from tests.golden.scheduler_graphs import GRAPHS
+    ref = json.loads((ROOT / "tests" / "golden" / "calllists.json").read_text())["graphs"][name]
+    g = GRAPHS[name]()
+    infer_shapes(g)
+    net = Net(name + "+reference-list", int(g.tensors[ref["input"]].shape[0]), ref["input"], ref["output"])
+    net.aliases = dict(ref["aliases"])
+    for t, lay in ref["layouts"].items():
+        if t in net.aliases:
+            continue
+        if t in g.tensors and g.tensors[t].is_const:
+            net.consts[t] = _const_words(g.tensors[t], Layout(*lay))
+        else:
+            net.buffers[t] = lay[1]
+    kinds = {"vectorop": 3, "matmul": 3, "matmul_at": 3, "conv": 4, "pool": 2}
+    for kind, names, args in ref["calls"]:
+        net.nodes.append((kind, *names[:kinds[kind]], tuple(args)))
+    return net
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", ["lenet5_b3", "matmul_gapped", "matmul_outer", "broadcast_aligned"])
+def test_project_from_the_reference_node_list_on_gpu(tmp_path, port, name):
+    """The reference scheduler's own call list (not scheduler.derive's) emitted as a CUDA
+    project, compiled and run: output equal to the oracle's run of the same list."""
+    net = _net_from_reference_list(name)
+    exp = _expected(net, port)
+    codegen.emit_project(net, tmp_path, expected=exp)
+    exe = codegen.compile_project(tmp_path, INCLUDE, LIB)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=300, cwd=tmp_path)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "test_inference PASSED" in r.stdout

@@ -58,6 +58,8 @@ def test_allocations_equal_the_reference_layouts(name):
     net = scheduler.derive(GRAPHS[name]())
     got = {k: L.alloc for k, L in net.layouts.items()}
     assert got == want
+    layouts = GOLDEN["graphs"][name]["layouts"]
+    assert {k: [L.numel, L.alloc, L.n_chunks, L.chunk, L.stride] for k, L in net.layouts.items()} == layouts
     # buffers and constants are sized by those allocations
     for k, words in net.buffers.items():
         assert words == want[k]
