@@ -1673,8 +1673,10 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
         return matmul_rows_impl(cx, a, b, c, batch, k, m, a_batch_stride, c_batch_stride, epi, bias, s);
     }
     if (cx->matmul_overlap && batch >= 2) {
-        // large calls: batch chunks of >= 2^33 multiply-adds, at most 8
-        const uint64_t by_work = (uint64_t)(macs >> 33);
+        // large calls: batch chunks of >= 2^37 multiply-adds, at most 8 (smaller chunks lose
+        // more to the extra launches than the overlap gains: a GEMM under the power cap runs
+        // slower beside a concurrent split, so only the large ones gain)
+        const uint64_t by_work = (uint64_t)(macs >> 37);
         const uint32_t chunks = (uint32_t)std::min<uint64_t>(std::min<uint64_t>(batch, 8), by_work);
         if (chunks >= 2)
             return matmul_chunked(cx, a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, epi,

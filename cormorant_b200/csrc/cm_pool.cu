@@ -698,8 +698,8 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
                 //   AVG  floor(rn(float(acc) * 2^-16 * inv) at 2^-16) >> 8 = floor(rn(a * inv)),
                 //        inv = rn(1 / denom)
                 //   LP2  floor(sqrt_rn(rn(acc)) * 2^8) >> 8 = floor(sqrt_rn(rn(acc))) with acc the
-                //        wrapped sum of squares (negative -> NaN -> 0); a root >= 2^15 wraps the
-                //        Q16.16 word (AP_WRAP) and narrows to -32768
+                //        wrapped sum of squares (negative -> NaN -> 0); the root's value is at
+                //        most 181, so the Q16.16 word never wraps and the narrowing saturates
                 //   LP1  the sum of |x|, MAX the largest word
                 // then one saturating pack per pair of outputs.
                 int32_t res[V];
@@ -715,8 +715,7 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
                         const float inv = (p.cip || vr == (uint32_t)PH) ? inv_in[v] : inv_tab[vr * vc[v]];
                         res[v] = __float2int_rd(__fmul_rn(__int2float_rn(a), inv));
                     } else if (TYPE == P_LP2) {
-                        const int32_t q = __float2int_rz(__fsqrt_rn(__int2float_rn(a)));   // NaN -> 0
-                        res[v] = q >= 32768 ? -32768 : q;
+                        res[v] = __float2int_rz(__fsqrt_rn(__int2float_rn(a)));   // NaN -> 0
                     } else {
                         res[v] = a;
                     }

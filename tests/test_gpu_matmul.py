@@ -212,10 +212,10 @@ def test_row_strided_full_size(cm, port):
 
 
 # Large calls run as batch chunks, each chunk's split overlapping the previous chunk's GEMM
-# (at least 2^33 multiply-adds a chunk): broadcast operands, gapped outputs, the fused
+# (at least 2^37 multiply-adds a chunk): broadcast operands, gapped outputs, the fused
 # epilogue.  Checked on sampled rows, the last row of the last batch step included.
-CHUNKED = [(1024, 1024, 512, 48, "a"), (1024, 1024, 512, 48, "b"), (768, 2048, 384, 40, None),
-           (512, 1024, 40, 160, None)]
+CHUNKED = [(2048, 2048, 2048, 48, "a"), (2048, 2048, 2048, 48, "b"), (4096, 2048, 1536, 24, None),
+           (8192, 2048, 2048, 8, None)]
 
 
 @pytest.mark.big
