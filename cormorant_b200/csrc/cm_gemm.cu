@@ -64,8 +64,8 @@ constexpr uint32_t TMEM_COLS = 512;
 // rows followed by its 128 lo' rows (the two plane boxes are adjacent in shared
 // memory).  One MMA per 32-deep step writes all four products of 64 channels x 128
 // pixels into 256 accumulator columns (pixels of the hi plane, then of the lo' plane),
-// double-buffered.  An M = 128, N = 128 MMA takes as long as an N = 256 one, so the
-// packed form's two N = 128 MMAs per step ran the tensor pipe at half rate.
+// double-buffered: half the MMA instructions of the packed form's two N = 128 MMAs per
+// step (the tensor pipe runs N = 128 at the same rate per multiply-add).
 template <int TBN, int CG = 1, bool WA = false>
 struct Cfg {
     static_assert(CG == 1 || TBN == 128, "CTA pairs use 128-column tiles");
