@@ -26,6 +26,9 @@ struct Context {
     // the caller's (CM_MATMUL_OVERLAP=0 at cm_init turns it off)
     cudaStream_t aux_stream = nullptr;
     int matmul_overlap = 1;
+    // implicit-GEMM convs with packed weights read one input window per K block
+    // (CM_CONV_WINDOW=0 at cm_init turns it off)
+    int conv_window = 1;
 };
 
 Context* ctx();                      // nullptr before cm_init

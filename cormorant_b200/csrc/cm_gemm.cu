@@ -256,6 +256,11 @@ struct GemmArgs {
     // divisors of the tile decode (set by launch_persistent): tiles per batch step, tiles
     // per row-tile group, conv tiles per image and per tile row
     FastDiv fd_z, fd_group, fd_hw, fd_w;
+    // conv window form (win != 0): tile rows are (row, image, column); per K block one TMA
+    // box brings the input window of all kh kernel rows (bh + (kh-1)*dh rows of bn images,
+    // both planes: win_bytes, the lo' plane win_plane bytes after the hi plane) and kernel
+    // row r reads it win_roff*r bytes in; the packed weights (w_bytes) stay resident
+    uint32_t win, win_stages, win_bytes, win_plane, win_roff, w_bytes, kh;
 };
 
 struct Tile {
@@ -302,6 +307,20 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
     return c;
 }
 
+// Output pixel (n, oh, ow) of tile row i of a conv tile: rows are (image, row, column),
+// or (row, image, column) in the window form.
+__device__ __forceinline__ void conv_pixel(const GemmArgs& g, const Tile& tc, uint32_t i, uint32_t& n, uint32_t& oh,
+                                           uint32_t& ow) {
+    ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
+    if (g.win) {
+        n = tc.cn0 + ((i >> g.bw_log) & ((1u << g.bn_log) - 1u));
+        oh = tc.ch0 + (i >> (g.bw_log + g.bn_log));
+    } else {
+        oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
+        n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+    }
+}
+
 // Persistent kernel: one CTA per SM (CG = 1), or one CTA pair per two SMs
 // (CG = 2, a 2-CTA cluster), walking tiles cluster, +clusters, ...
 //   warp 0      TMA producer (continuous stage ring across tiles)
@@ -320,23 +339,31 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
 // single-CTA kernel is bound by.  All TMA completions and epilogue releases go to the
 // even CTA's barriers; its MMA commits arrive on both CTAs' barriers (multicast
 // commit).  No TMA multicast is used.
-template <int TBN, int CG, bool WA = false>
+template <int TBN, int CG, bool WA = false, bool WIN = false>
 __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
     using C = Cfg<TBN, CG, WA>;
-    constexpr int STAGES = C::STAGES, NBUF = C::NBUF;
+    static_assert(!WIN || (TBN == 64 && CG == 1 && !WA), "the window form runs packed 64-column tiles");
+    constexpr int NBUF = C::NBUF;
     constexpr uint32_t HALF = TBN / (C::EPI_WARPS / 4);  // columns per epilogue warp
     constexpr uint32_t CW = 16;                           // columns per TMEM load
+    // the window form's stage count and size come with the launch; its resident weights
+    // come first in shared memory
+    const uint32_t STAGES = WIN ? g.win_stages : (uint32_t)C::STAGES;
+    const uint32_t STAGE_B = WIN ? g.win_bytes : (uint32_t)C::STAGE;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + STAGES * C::STAGE);
-    // bars: [0,S) full, [S,2S) empty, [2S,2S+NBUF) acc_full, [2S+NBUF,2S+2NBUF) acc_empty, then done
+    uint8_t* stg = WIN ? smem + g.w_bytes : smem;
+    uint64_t* bars = (uint64_t*)(stg + STAGES * STAGE_B);
+    // bars: [0,S) full, [S,2S) empty, [2S,2S+NBUF) acc_full, [2S+NBUF,2S+2NBUF) acc_empty, then
+    // done, then (window form) the resident weights' barrier
     uint64_t* full_b = bars;
     uint64_t* empty_b = bars + STAGES;
     uint64_t* accf_b = bars + 2 * STAGES;
     uint64_t* acce_b = accf_b + NBUF;
     uint64_t* done_b = acce_b + NBUF;
-    volatile uint32_t* tmem_slot = (volatile uint32_t*)(done_b + 1);
+    uint64_t* wbar = done_b + 1;
+    volatile uint32_t* tmem_slot = (volatile uint32_t*)(wbar + 1);
     volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
     const uint32_t warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -347,7 +374,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     constexpr uint16_t kPairMask = 0x3;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (uint32_t s = 0; s < STAGES; ++s) {
             mbar_init(smem_u32(&full_b[s]), 1);
             mbar_init(smem_u32(&empty_b[s]), 1);
         }
@@ -356,6 +383,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             mbar_init(smem_u32(&acce_b[b]), C::EPI_WARPS * CG);
         }
         mbar_init(smem_u32(done_b), 1);
+        mbar_init(smem_u32(wbar), 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -379,7 +407,34 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     const uint32_t tmem = *tmem_slot;
     const WaitCtl wc{abort_flag, g.status, g.timeout_ns};
 
-    if (warp == 0) {
+    if (WIN && warp == 0) {
+        if (lane == 0) {
+            // the packed weights once, then per tile and K block one window box (both planes)
+            mbar_expect_tx(smem_u32(wbar), g.w_bytes);
+            for (uint32_t j = 0; j < g.w_bytes / (uint32_t)PLANE_TILE; ++j)
+                tma_load_4d(smem_u32(smem + j * PLANE_TILE), &tmB, smem_u32(wbar), 0, (int)(j * BK), 0, 0);
+            uint32_t it = 0;
+            for (uint64_t t = cid; t < total && !*abort_flag; t += ncl) {
+                const Tile tc = decode_tile<TBN, CG>(g, t, rank);
+                for (uint32_t kb = 0; kb < g.kb_per_r; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(smem_u32(&empty_b[s]), (round & 1u) ^ 1u, wc)) break;
+                    const uint32_t full = smem_u32(&full_b[s]);
+                    mbar_expect_tx(full, STAGE_B);
+                    tma_load_5d(smem_u32(stg + s * STAGE_B), &tmA, full, (int)(kb * BK), (int)(tc.cw0 * g.sw),
+                                (int)tc.cn0, (int)(tc.ch0 * g.sh), 0);
+                }
+            }
+            // let the copies still in flight land before the CTA exits
+            volatile int never = 0;
+            WaitCtl drain{&never, g.status, g.timeout_ns};
+            mbar_wait(smem_u32(wbar), 0, drain);
+            if (*abort_flag) {
+                const uint32_t first = it > STAGES ? it - STAGES : 0u;
+                for (uint32_t k = first; k < it; ++k) mbar_wait(smem_u32(&full_b[k % STAGES]), (k / STAGES) & 1u, drain);
+            }
+        }
+    } else if (warp == 0) {
         if (lane == 0) {
             uint32_t it = 0;
             for (uint64_t t = cid; t < total && !*abort_flag; t += ncl) {
@@ -387,7 +442,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                 for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(smem_u32(&empty_b[s]), (round & 1u) ^ 1u, wc)) break;
-                    uint8_t* st = smem + s * C::STAGE;
+                    uint8_t* st = stg + s * STAGE_B;
                     if (CG == 2) {
                         const uint32_t full = map_to_rank(smem_u32(&full_b[s]), 0);   // the pair leader's barrier
                         if (leader) mbar_expect_tx(smem_u32(&full_b[s]), CG * C::STAGE);
@@ -420,11 +475,50 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             if (*abort_flag && leader) {
                 // let copies already in flight land before the CTA exits (a pair's copies
                 // all complete on the leader's barriers)
-                const uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0u;
+                const uint32_t first = it > STAGES ? it - STAGES : 0u;
                 volatile int never = 0;
                 WaitCtl drain{&never, g.status, g.timeout_ns};
                 for (uint32_t k = first; k < it; ++k) mbar_wait(smem_u32(&full_b[k % STAGES]), (k / STAGES) & 1u, drain);
             }
+        }
+    } else if (WIN && warp == 1) {
+        if (lane == 0) {
+            uint32_t it = 0, j = 0;
+            const WaitCtl wcw = wc;
+            bool ok = mbar_wait(smem_u32(wbar), 0, wcw);     // resident weights landed
+            tc_fence_after();
+            const uint32_t wbase = smem_u32(smem);
+            for (uint64_t t = cid; ok && t < total; t += ncl, ++j) {
+                const uint32_t buf = j % NBUF, use = j / NBUF;
+                if (!mbar_wait(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, wc)) break;
+                tc_fence_after();
+                const uint32_t d = tmem + buf * C::ACC_COLS;
+                for (uint32_t kb = 0; kb < g.kb_per_r; ++kb, ++it) {
+                    const uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(smem_u32(&full_b[s]), round & 1u, wc)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(stg + s * STAGE_B);
+                    // 32-deep steps of this block that hold any tap (the rest are zero)
+                    const uint32_t steps = min(BK / 32u, g.ksteps - kb * (BK / 32));
+                    for (uint32_t r = 0; r < g.kh; ++r) {
+                        const uint32_t ar = a0 + r * g.win_roff;                               // kernel row r's input rows
+                        const uint32_t br = wbase + (r * g.kb_per_r + kb) * (uint32_t)PLANE_TILE; // its weights
+                        for (uint32_t kk = 0; kk < steps; ++kk) {
+                            const uint64_t ah = sdesc(ar + kk * 32), al = sdesc(ar + g.win_plane + kk * 32);
+                            const uint64_t bhl = sdesc_n(br + kk * 32 * 128);
+                            const uint32_t acc = (kb | r | kk) != 0u;
+                            umma_i8(d, ah, bhl, C::IDESC, acc);                 // -> HH | HL
+                            umma_i8(d + 2 * TBN, al, bhl, C::IDESC, acc);       // -> LH | LL
+                        }
+                    }
+                    umma_commit(smem_u32(&empty_b[s]));   // frees the window once these MMAs have read it
+                }
+                if (ok) umma_commit(smem_u32(&accf_b[buf]));
+            }
+            umma_commit(smem_u32(done_b));
+            volatile int never = 0;
+            WaitCtl drain{&never, g.status, g.timeout_ns};
+            mbar_wait(smem_u32(done_b), 0, drain);
         }
     } else if (warp == 1) {
         if (lane == 0 && leader) {
@@ -439,7 +533,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(smem_u32(&full_b[s]), round & 1u, wc)) { ok = false; break; }
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(smem + s * C::STAGE);
+                    const uint32_t a0 = smem_u32(stg + s * STAGE_B);
                     const uint32_t b0 = a0 + OPERAND_TILE;
                     // 32-deep steps of this block that hold any tap (the rest are zero in A and B)
                     const uint32_t steps = g.conv ? g.ksteps - (kb % g.kb_per_r) * (BK / 32) : g.ksteps - kb * (BK / 32);
@@ -667,9 +761,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             bool valid;
             uint64_t rt_idx, o_off;
             if (g.conv) {
-                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
-                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
-                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                uint32_t n, oh, ow;
+                conv_pixel(g, tc, i, n, oh, ow);
                 valid = ow < g.out_w && oh < g.out_h && n < g.nimg;
                 const uint64_t pix = (uint64_t)oh * g.out_w + ow;
                 rt_idx = (uint64_t)n * g.out_h * g.out_w + pix;
@@ -690,9 +783,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             if ((g.epi & 2u) && g.rpl) {
                 // residual words rebuilt from its plane image: per 16 channels one 16-byte hi
                 // run and one lo' run, x = 256*hi + lo' + 128, pairs assembled by byte permutes
-                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
-                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
-                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                uint32_t n, oh, ow;
+                conv_pixel(g, tc, i, n, oh, ow);
                 const uint64_t pix = ((uint64_t)n * g.rpl_Hp + oh + g.rpl_pt) * g.rpl_Wp + ow + g.rpl_pl;
 #pragma unroll
                 for (uint32_t c0 = 0; c0 < HALF; c0 += 16) {
@@ -789,9 +881,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             if (g.po) {
                 // the output row as channels-last hi / lo' planes of the next conv's input,
                 // 16 channels per 16-byte store, and its channel sum added into S
-                const uint32_t ow = tc.cw0 + (i & ((1u << g.bw_log) - 1u));
-                const uint32_t oh = tc.ch0 + ((i >> g.bw_log) & ((1u << g.bh_log) - 1u));
-                const uint32_t n = tc.cn0 + (i >> (g.bw_log + g.bh_log));
+                uint32_t n, oh, ow;
+                conv_pixel(g, tc, i, n, oh, ow);
                 const uint64_t pix = ((uint64_t)n * g.po_Hp + oh + g.po_pt) * g.po_Wp + ow + g.po_pl;
                 int32_t sum = 0;
 #pragma unroll
@@ -1210,6 +1301,32 @@ int make_conv_map(CUtensorMap* m, const ConvA& c) {
     return CM_OK;
 }
 
+// The window form's operand: dims (K bytes of a kernel row, columns, images, rows, plane)
+// so that one box {128 k, bw columns (stride sw), bn images, `rows` rows, 2 planes} lands
+// as [plane][row][image][column][128 bytes] -- for every kernel row r, the 128 tile rows
+// (row, image, column) start r*dh*bn*bw rows into each plane.
+int make_conv_window_map(CUtensorMap* m, const ConvA& c, uint32_t rows) {
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    if (((uintptr_t)c.planes & 15u) != 0 || (c.Cp & 15u) != 0) return set_error(CM_EINVAL, "conv plane buffer misaligned");
+    const uint32_t bw = 1u << c.bw_log, bn = 1u << c.bn_log;
+    if (bw * (1u << c.bh_log) * bn != (uint32_t)BM || bw * c.sw > 256 || rows > 256 || c.sw > 8)
+        return set_error(CM_EINVAL, "conv window shape");
+    const uint64_t row = c.row_pitch ? c.row_pitch : (uint64_t)c.Wp * c.Cp;
+    const uint64_t img = c.img_pitch ? c.img_pitch : row * c.Hp;
+    const uint64_t plane = c.plane_pitch ? c.plane_pitch : img * c.nimg;
+    if ((row | img | plane) & 15u) return set_error(CM_EINVAL, "conv plane pitches misaligned");
+    const cuuint64_t dims[5] = {c.KR, c.Wp, c.nimg, c.Hp, 2};
+    const cuuint64_t strides[4] = {(cuuint64_t)c.Cp, (cuuint64_t)img, (cuuint64_t)row, (cuuint64_t)plane};
+    const cuuint32_t box[5] = {(cuuint32_t)BK, bw * c.sw, bn, rows, 2};
+    const cuuint32_t estr[5] = {1, c.sw, 1, 1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, (void*)c.planes, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(CM_ECUDA, "cuTensorMapEncodeTiled (conv window) failed (%d)", (int)r);
+    return CM_OK;
+}
+
 // B planes packed for 64-column tiles: [batches][K][128] int8, each K row =
 // [64 hi | 64 lo] bytes of one column tile; box {128, 128 k, 1, 1}.
 int make_packed_map(CUtensorMap* m, const int8_t* base, uint32_t K, uint32_t batches) {
@@ -1267,16 +1384,20 @@ __global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __res
     }
 }
 
-template <int TBN, int CG, bool WA = false>
-int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s) {
+template <int TBN, int CG, bool WA = false, bool WIN = false>
+int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s,
+                      size_t win_smem = 0) {
     static int per_sm_clusters = -1;   // co-resident clusters of CG CTAs (one CTA per SM)
+    // the window form's shared memory depends on the call (resident weights + windows)
+    const size_t smem = WIN ? win_smem : (size_t)Cfg<TBN, CG, WA>::SMEM_LAUNCH;
     if (per_sm_clusters < 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             Cfg<TBN, CG, WA>::SMEM_LAUNCH);
+        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA, WIN>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             WIN ? SMEM_BYTES : Cfg<TBN, CG, WA>::SMEM_LAUNCH);
         if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
         int n = cx->sm_count / CG;
         if (CG > 1) {
-            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA, WIN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * n);
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
@@ -1286,7 +1407,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             q.attrs = &at; q.numAttrs = 1;
             int m = 0;
-            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG, WA>, &q) == cudaSuccess && m > 0) n = m;
+            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG, WA, WIN>, &q) == cudaSuccess && m > 0) n = m;
             cudaGetLastError();
         }
         per_sm_clusters = n;
@@ -1307,19 +1428,19 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            gemm_q88_kernel<TBN, CG, WA><<<clusters, Cfg<TBN, CG, WA>::THREADS, Cfg<TBN, CG, WA>::SMEM_LAUNCH, s>>>(ta, tb, g);
+            gemm_q88_kernel<TBN, CG, WA, WIN><<<clusters, Cfg<TBN, CG, WA>::THREADS, smem, s>>>(ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * clusters);
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
-            q.dynamicSmemBytes = Cfg<TBN, CG, WA>::SMEM_LAUNCH;
+            q.dynamicSmemBytes = smem;
             q.stream = s;
             cudaLaunchAttribute at{};
             at.id = cudaLaunchAttributeClusterDimension;
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             q.attrs = &at; q.numAttrs = 1;
-            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG, WA>, ta, tb, g);
+            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG, WA, WIN>, ta, tb, g);
         }
     }
     count_launch();
@@ -1404,6 +1525,27 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.rpl = p.rp.planes; g.rpl_plane = p.rp.plane_pitch;
     g.rpl_Hp = p.rp.Hp; g.rpl_Wp = p.rp.Wp; g.rpl_Cp = p.rp.Cp; g.rpl_pt = p.rp.pt; g.rpl_pl = p.rp.pl;
     g.po_Hp = p.po.Hp; g.po_Wp = p.po.Wp; g.po_Cp = p.po.Cp; g.po_pt = p.po.pt; g.po_pl = p.po.pl;
+    // Window form (packed weights, stride 1 down the rows, tiles at least 8 columns wide): one
+    // TMA box per K block brings the input rows of all kh kernel rows, which read it at row
+    // offsets, and the packed weights stay resident -- a quarter to a third of the TMA bytes
+    // of one box per kernel row, which bounded these GEMMs (their K-block rounds, not the
+    // tensor pipe, set the pace).
+    if (p.b_packed && cx->conv_window && c.sh == 1 && c.bw_log >= 3 && !(p.epi & 4u)) {
+        const uint32_t bw = 1u << c.bw_log, bn = 1u << c.bn_log;
+        const uint32_t rows = (1u << c.bh_log) + (c.kh - 1) * c.dh;
+        const uint64_t win_bytes = 2ull * BK * bw * bn * rows;
+        const uint64_t w_bytes = (uint64_t)p.K * 128;
+        const uint64_t avail = (uint64_t)SMEM_BYTES - 1024 - 256;
+        if (rows <= 256 && w_bytes + 2 * win_bytes <= avail) {
+            const uint32_t stages = (uint32_t)std::min<uint64_t>(4, (avail - w_bytes) / win_bytes);
+            CUtensorMap tw;
+            rc = make_conv_window_map(&tw, c, rows);
+            if (rc) return rc;
+            g.win = 1; g.win_stages = stages; g.win_bytes = (uint32_t)win_bytes; g.win_plane = (uint32_t)(win_bytes / 2);
+            g.win_roff = c.dh * bn * bw * BK; g.w_bytes = (uint32_t)w_bytes; g.kh = c.kh;
+            return launch_persistent<64, 1, false, true>(cx, tw, tb, g, s, (size_t)(w_bytes + stages * win_bytes + 1024 + 256));
+        }
+    }
     // Weights as A (one N = 256 MMA per step) for outputs written only as a plane image: its
     // channel-major epilogue goes through a shared-memory transpose for the image, but the
     // plain NCHW epilogue of the packed form is the cheaper one (ResNet-18 stem: 346 against

@@ -175,6 +175,8 @@ int cm_init(const char* instance) {
     if (dm && *dm) c.direct_max_macs = (uint64_t)strtoull(dm, nullptr, 10);
     const char* mo = getenv("CM_MATMUL_OVERLAP");
     if (mo && *mo) c.matmul_overlap = atoi(mo) != 0;
+    const char* cw = getenv("CM_CONV_WINDOW");
+    if (cw && *cw) c.conv_window = atoi(cw) != 0;
     e = cudaStreamCreateWithFlags(&c.aux_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         cudaFree(c.status);
