@@ -199,6 +199,83 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
     asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Window-form MMA issue.  One thread issues all of a CTA's MMAs, and at M = 128,
+// N = 128 (about 70 tensor cycles a step) its instruction stream, not the tensor
+// pipe, set the pace: a loop with runtime bounds, a stage index taken modulo a
+// runtime stage count and descriptors rebuilt per MMA issued one MMA every ~130
+// cycles.  So descriptors advance by constant increments (the start-address field
+// holds address / 16, and every operand lies below 2^18 bytes, so the additions
+// never carry out of it), the stage ring advances without divisions, and the tile
+// shapes of the shipped networks issue from fully unrolled code (ResNet-18: 3x3
+// 64-channel convs, 3 rows x 2 K blocks, 2 steps in the last; the row-stacked
+// space-to-depth stem, 2 rows x 1 block of 4 steps); other shapes take the loop.
+// ---------------------------------------------------------------------------
+struct WinIssue {
+    uint64_t da0, db0;       // descriptors of stage 0's window and of the resident weights
+    uint32_t stb16;          // one stage, in descriptor units
+    uint32_t roff;           // kernel row offset inside a window, in descriptor units
+    uint32_t wpl;            // lo' plane offset inside a window, in descriptor units
+    uint32_t stages;
+};
+
+constexpr uint32_t kWinAStep = 32 >> 4;               // 32 K bytes of a K-major row
+constexpr uint32_t kWinBStep = (32 * 128) >> 4;       // 32 K rows of 128 N bytes
+constexpr uint32_t kWinBBlock = PLANE_TILE >> 4;      // one 128-deep weight block
+
+// one 32-deep step: A's hi and lo' planes against [Bh | Bl]
+template <uint32_t NOFF, uint32_t IDESC>
+__device__ __forceinline__ void win_step(uint32_t d, uint64_t ah, uint64_t al, uint64_t bhl, uint32_t acc) {
+    umma_i8(d, ah, bhl, IDESC, acc);           // -> HH | HL
+    umma_i8(d + NOFF, al, bhl, IDESC, acc);    // -> LH | LL
+}
+
+// The K blocks of one tile.  Each block is one window stage holding all kernel rows;
+// its MMAs free the stage once they have read it.  KH = 0: shape from the arguments.
+template <uint32_t KH, uint32_t KBR, uint32_t LAST, uint32_t NOFF, uint32_t IDESC>
+__device__ __forceinline__ bool win_tile(uint32_t d, const WinIssue& w, uint32_t kh, uint32_t kbr, uint32_t last,
+                                         uint32_t& s, uint32_t& phase, uint64_t* full_b, uint64_t* empty_b,
+                                         const WaitCtl& wc) {
+    constexpr uint32_t BKS = BK / 32;
+    if constexpr (KH != 0) {
+#pragma unroll
+        for (uint32_t kb = 0; kb < KBR; ++kb) {
+            if (!mbar_wait(smem_u32(&full_b[s]), phase, wc)) return false;
+            tc_fence_after();
+            const uint64_t da = w.da0 + s * w.stb16;
+#pragma unroll
+            for (uint32_t r = 0; r < KH; ++r) {
+                const uint64_t ar = da + r * w.roff, br = w.db0 + (r * KBR + kb) * kWinBBlock;
+#pragma unroll
+                for (uint32_t kk = 0; kk < (kb + 1 == KBR ? LAST : BKS); ++kk)
+                    win_step<NOFF, IDESC>(d, ar + kk * kWinAStep, ar + w.wpl + kk * kWinAStep, br + kk * kWinBStep,
+                                          (kb | r | kk) != 0u);
+            }
+            umma_commit(smem_u32(&empty_b[s]));
+            if (++s == w.stages) { s = 0; phase ^= 1u; }
+        }
+    } else {
+        for (uint32_t kb = 0; kb < kbr; ++kb) {
+            if (!mbar_wait(smem_u32(&full_b[s]), phase, wc)) return false;
+            tc_fence_after();
+            const uint64_t da = w.da0 + s * w.stb16;
+            const uint32_t steps = kb + 1u == kbr ? last : BKS;     // 32-deep steps holding any tap
+            for (uint32_t r = 0; r < kh; ++r) {
+                const uint64_t ar = da + r * w.roff, br = w.db0 + (r * kbr + kb) * kWinBBlock;
+                const uint32_t first = (kb | r) != 0u;
+#pragma unroll
+                for (uint32_t kk = 0; kk < BKS; ++kk)
+                    if (kk < steps)
+                        win_step<NOFF, IDESC>(d, ar + kk * kWinAStep, ar + w.wpl + kk * kWinAStep, br + kk * kWinBStep,
+                                              kk ? 1u : first);
+            }
+            umma_commit(smem_u32(&empty_b[s]));
+            if (++s == w.stages) { s = 0; phase ^= 1u; }
+        }
+    }
+    return true;
+}
+
 #define CM_R16(i) "=r"(r[i])
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
@@ -483,36 +560,24 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
         }
     } else if (WIN && warp == 1) {
         if (lane == 0) {
-            uint32_t it = 0, j = 0;
+            uint32_t j = 0, s = 0, phase = 0;
             const WaitCtl wcw = wc;
             bool ok = mbar_wait(smem_u32(wbar), 0, wcw);     // resident weights landed
             tc_fence_after();
-            const uint32_t wbase = smem_u32(smem);
+            const WinIssue w{sdesc(smem_u32(stg)), sdesc_n(smem_u32(smem)), STAGE_B >> 4, g.win_roff >> 4,
+                             g.win_plane >> 4, STAGES};
+            const uint32_t kh = g.kh, kbr = g.kb_per_r;
+            const uint32_t last = g.ksteps - (kbr - 1u) * (BK / 32u);   // 32-deep steps in a row's last block
+            const uint32_t shape = kh == 3 && kbr == 2 && last == 2 ? 1u : kh == 2 && kbr == 1 && last == 4 ? 2u : 0u;
+            constexpr uint32_t NOFF = 2 * TBN, ID = C::IDESC;
             for (uint64_t t = cid; ok && t < total; t += ncl, ++j) {
                 const uint32_t buf = j % NBUF, use = j / NBUF;
                 if (!mbar_wait(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, wc)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * C::ACC_COLS;
-                for (uint32_t kb = 0; kb < g.kb_per_r; ++kb, ++it) {
-                    const uint32_t s = it % STAGES, round = it / STAGES;
-                    if (!mbar_wait(smem_u32(&full_b[s]), round & 1u, wc)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint32_t a0 = smem_u32(stg + s * STAGE_B);
-                    // 32-deep steps of this block that hold any tap (the rest are zero)
-                    const uint32_t steps = min(BK / 32u, g.ksteps - kb * (BK / 32));
-                    for (uint32_t r = 0; r < g.kh; ++r) {
-                        const uint32_t ar = a0 + r * g.win_roff;                               // kernel row r's input rows
-                        const uint32_t br = wbase + (r * g.kb_per_r + kb) * (uint32_t)PLANE_TILE; // its weights
-                        for (uint32_t kk = 0; kk < steps; ++kk) {
-                            const uint64_t ah = sdesc(ar + kk * 32), al = sdesc(ar + g.win_plane + kk * 32);
-                            const uint64_t bhl = sdesc_n(br + kk * 32 * 128);
-                            const uint32_t acc = (kb | r | kk) != 0u;
-                            umma_i8(d, ah, bhl, C::IDESC, acc);                 // -> HH | HL
-                            umma_i8(d + 2 * TBN, al, bhl, C::IDESC, acc);       // -> LH | LL
-                        }
-                    }
-                    umma_commit(smem_u32(&empty_b[s]));   // frees the window once these MMAs have read it
-                }
+                if (shape == 1) ok = win_tile<3, 2, 2, NOFF, ID>(d, w, kh, kbr, last, s, phase, full_b, empty_b, wc);
+                else if (shape == 2) ok = win_tile<2, 1, 4, NOFF, ID>(d, w, kh, kbr, last, s, phase, full_b, empty_b, wc);
+                else ok = win_tile<0, 0, 0, NOFF, ID>(d, w, kh, kbr, last, s, phase, full_b, empty_b, wc);
                 if (ok) umma_commit(smem_u32(&accf_b[buf]));
             }
             umma_commit(smem_u32(done_b));
