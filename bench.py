@@ -274,16 +274,23 @@ class MatmulSweep:
         self.bufs = []
 
     # ---- end to end through the reference-facing API (cm_buf_* + run_matmul) ----
-    e2e_path = ("per shape: cm_buf_sync_to_device_async(A, B) -> run_matmul (cm_matmul_async) -> "
-                "cm_buf_sync_from_device_async(C), pinned host mirrors; uploads, kernels and downloads on three "
-                "streams, so shape i+1's upload and shape i-1's download overlap shape i's GEMM (runtime.CopyOverlap)")
+    e2e_path = ("per batch chunk of a shape: views of the shape's A, B and C buffers (cm_buf_init_view) -> "
+                "cm_buf_sync_to_device_async(A, B) -> run_matmul (cm_matmul_async) -> cm_buf_sync_from_device_async(C), "
+                "pinned host mirrors; uploads, kernels and downloads on three streams (runtime.CopyOverlap), chunks "
+                "of at most ~270 MB of upload in Johnson order for the upload -> download flow (chunks whose upload "
+                "is smaller than their download first, by increasing upload, then the rest by decreasing download), "
+                "so the download stream starts after the first chunk instead of after the largest shape")
+
+    E2E_CHUNK_BYTES = 270 << 20          # upload bytes per chunk, at most (one batch item at least)
 
     def e2e_setup(self):
         from cormorant_b200.runtime import CopyOverlap, InferenceBuf
         import numpy as np
-        self.e2e = []
+        self.e2e = []          # owner buffers per shape
+        self.e2e_calls = []    # (n, k, m, items, a_bs, b_bs, c_bs, A view, B view, C view)
         rng = np.random.default_rng(99 + self.rank)
         self.h2d = self.d2h = 0
+        jobs = []
         for (n, k, m, b) in self.shapes:
             if b == 0:
                 continue
@@ -293,9 +300,24 @@ class MatmulSweep:
             Cb = InferenceBuf.alloc(wc)
             fill(A.ptr(), rng, -1024, 1024)
             fill(B.ptr(), rng, -1024, 1024)
-            self.e2e.append((n, k, m, b, A, B, Cb))
+            self.e2e.append((A, B, Cb))
             self.h2d += 2 * (wa + wb)
             self.d2h += 2 * wc
+            a_bs, b_bs, c_bs = self._st(n, k, m)
+            # batch chunks as views; explicit strides (which may overlap items) run whole
+            per_up = 2 * (a_bs + b_bs)
+            items = b if self.strides is not None else max(1, min(b, self.E2E_CHUNK_BYTES // per_up))
+            for i0 in range(0, b, items):
+                c = min(items, b - i0)
+                views = (InferenceBuf.init_view(A, i0 * a_bs, (c - 1) * a_bs + n * k),
+                         InferenceBuf.init_view(B, i0 * b_bs, (c - 1) * b_bs + k * m),
+                         InferenceBuf.init_view(Cb, i0 * c_bs, (c - 1) * c_bs + n * m))
+                up = 2 * (views[0].count() + views[1].count())
+                down = 2 * views[2].count()
+                jobs.append((up, down, (n, k, m, c, a_bs, b_bs, c_bs) + views))
+        first = sorted((j for j in jobs if j[0] < j[1]), key=lambda j: j[0])
+        rest = sorted((j for j in jobs if j[0] >= j[1]), key=lambda j: -j[1])
+        self.e2e_calls = [j[2] for j in first + rest]
         self.pipe = CopyOverlap()
 
     def e2e_start(self, start_event):
@@ -303,17 +325,17 @@ class MatmulSweep:
 
     def e2e_step(self):
         from cormorant_b200.runtime import run_matmul
-        # largest output first: the last shape's download is the part of a step nothing hides
-        for (n, k, m, b, A, B, Cb) in sorted(self.e2e, key=lambda t: -t[6].count()):
-            self.pipe.call([A, B], [Cb], lambda s, n=n, k=k, m=m, b=b, A=A, B=B, Cb=Cb:
-                           run_matmul(A, B, Cb, n, k, m, b, *self._st(n, k, m), stream=s))
+        for (n, k, m, c, a_bs, b_bs, c_bs, A, B, Cb) in self.e2e_calls:
+            self.pipe.call([A, B], [Cb], lambda s, n=n, k=k, m=m, c=c, st=(a_bs, b_bs, c_bs), A=A, B=B, Cb=Cb:
+                           run_matmul(A, B, Cb, n, k, m, c, *st, stream=s))
 
     def e2e_finish(self):
         self.pipe.join()
 
     def e2e_release(self):
+        self.e2e_calls = []
         for t in self.e2e:
-            for buf in t[4:]:
+            for buf in t:
                 buf.free()
         self.e2e = []
         self.pipe = None

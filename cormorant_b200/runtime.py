@@ -141,21 +141,37 @@ class CopyOverlap:
     the caller's stream, and CUDA events order every reuse of a buffer: an upload
     into a buffer waits for the last kernel that read it, a kernel writing a buffer
     waits for the last download of it.  Calls whose buffers are distinct overlap;
-    calls that share a buffer are ordered.  Buffers are ``InferenceBuf`` objects; views
-    of one owner count as that owner.
+    calls that share a buffer are ordered.  Buffers are ``InferenceBuf`` objects; a
+    view is the element range it aliases in its owner, so views of one owner that do
+    not overlap (batch chunks of one large buffer) are independent, and a view and
+    its owner are ordered.
     """
 
     @staticmethod
-    def _key(b) -> int:
-        return id(b._keep) if b._keep is not None else id(b)
+    def _range(b) -> tuple:
+        """(owner identity, first element, end element) of the words `b` covers."""
+        if b._keep is None:
+            return id(b), 0, b.count()
+        start = (b.phys() - b._keep.phys()) // InferenceBuf.BYTES_PER_ELEM
+        return id(b._keep), start, start + b.count()
+
+    @staticmethod
+    def _record(table: dict, rng: tuple, event) -> None:
+        entries = table.setdefault(rng[0], [])
+        entries[:] = [e for e in entries if (e[0], e[1]) != (rng[1], rng[2])]
+        entries.append((rng[1], rng[2], event))
+
+    @staticmethod
+    def _overlapping(table: dict, rng: tuple):
+        return [ev for (s, e, ev) in table.get(rng[0], ()) if s < rng[2] and rng[1] < e]
 
     def __init__(self):
         import torch
         self._torch = torch
         self.up = torch.cuda.Stream()
         self.down = torch.cuda.Stream()
-        self._read = {}      # buffer -> event of the last kernel that read it
-        self._drained = {}   # buffer -> event of the last download of it
+        self._read = {}      # owner -> [(start, end, event of the last kernel that read the range)]
+        self._drained = {}   # owner -> [(start, end, event of the last download of the range)]
 
     def start(self, event) -> None:
         """Copies issued from now on start no earlier than `event` (a recorded CUDA event)."""
@@ -167,29 +183,29 @@ class CopyOverlap:
         torch = self._torch
         cur = torch.cuda.current_stream()
         for b in inputs:
-            ev = self._read.get(self._key(b))
-            if ev is not None:
+            rng = self._range(b)
+            # the last kernel that read the range, and the download of a result written there
+            for ev in self._overlapping(self._read, rng) + self._overlapping(self._drained, rng):
                 self.up.wait_event(ev)
             b.sync_to_device(self.up)
         up_done = torch.cuda.Event()
         up_done.record(self.up)
         cur.wait_event(up_done)
         for b in outputs:
-            ev = self._drained.get(self._key(b))
-            if ev is not None:
+            for ev in self._overlapping(self._drained, self._range(b)):
                 cur.wait_event(ev)
         run(cur)
         ran = torch.cuda.Event()
         ran.record(cur)
         for b in inputs:
-            self._read[self._key(b)] = ran
+            self._record(self._read, self._range(b), ran)
         self.down.wait_event(ran)
         for b in outputs:
             b.sync_from_device(self.down)
         down_done = torch.cuda.Event()
         down_done.record(self.down)
         for b in outputs:
-            self._drained[self._key(b)] = down_done
+            self._record(self._drained, self._range(b), down_done)
 
     def join(self) -> None:
         """Make the current stream wait for every copy issued so far."""

@@ -86,6 +86,46 @@ def test_copy_overlap_sequence(cm, port):
         Y.free()
 
 
+def test_copy_overlap_views(cm, port):
+    """A batched MatMul run as batch chunks through views of its owners (the bench's e2e
+    form: disjoint views of one owner overlap each other), then, in the next step, once
+    over the whole owners (a call on an owner is ordered after its views' copies and
+    kernels), then chunked again; every read-back equals the oracle."""
+    import torch
+    from cormorant_b200.runtime import CopyOverlap, InferenceBuf, run_matmul
+    n, k, m, batch, items = 96, 160, 72, 7, 2
+    rng = np.random.default_rng(23)
+    A, B, Cb = InferenceBuf.alloc(batch * n * k), InferenceBuf.alloc(batch * k * m), InferenceBuf.alloc(batch * n * m)
+    chunks = []
+    for i0 in range(0, batch, items):
+        c = min(items, batch - i0)
+        chunks.append((c, InferenceBuf.init_view(A, i0 * n * k, c * n * k), InferenceBuf.init_view(B, i0 * k * m, c * k * m),
+                       InferenceBuf.init_view(Cb, i0 * n * m, c * n * m)))
+    try:
+        pipe = CopyOverlap()
+        start = torch.cuda.Event()
+        start.record()
+        pipe.start(start)
+        for step, whole in enumerate((False, True, False)):
+            a, b = rand16(rng, A.count(), -1024, 1024), rand16(rng, B.count(), -1024, 1024)
+            torch.cuda.synchronize()
+            A.ptr()[:] = a
+            B.ptr()[:] = b
+            Cb.ptr()[:] = -23131
+            if whole:
+                pipe.call([A, B], [Cb], lambda s: run_matmul(A, B, Cb, n, k, m, batch, n * k, k * m, n * m, stream=s))
+            else:
+                for (c, Av, Bv, Cv) in chunks:
+                    pipe.call([Av, Bv], [Cv], lambda s, c=c, Av=Av, Bv=Bv, Cv=Cv:
+                              run_matmul(Av, Bv, Cv, n, k, m, c, n * k, k * m, n * m, stream=s))
+            pipe.join()
+            torch.cuda.synchronize()
+            assert_same(Cb.ptr().copy(), port.matmul(a, b, n, k, m, batch), f"step {step} whole={whole}")
+    finally:
+        for x in (A, B, Cb):
+            x.free()
+
+
 @pytest.mark.parametrize("pairs", [0, 1])
 def test_int8_mma_rate(cm, pairs):
     """The ceiling measurement runs, returns a plausible rate and leaves the library usable."""
