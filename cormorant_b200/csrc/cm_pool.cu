@@ -635,6 +635,10 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
     float inv_in[V];
 #pragma unroll
     for (int v = 0; v < V; ++v) inv_in[v] = TYPE == P_AVG ? inv_tab[p.cip ? PH * PW : PH * vc[v]] : 0.0f;
+    // output rows whose PH taps all lie inside the plane: oh_in0 <= oh <= oh_in1
+    constexpr int32_t oh_in0 = (PT + SH - 1) / SH;
+    const int32_t last_ok = (int32_t)p.in_h - 1 + PT - (PH - 1) * DH;
+    const int32_t oh_in1 = last_ok < 0 ? -1 : last_ok / SH;
 
     uint32_t k = 0;
     for (uint64_t plane = blockIdx.x; plane < planes; plane += gridDim.x, ++k) {
@@ -683,8 +687,9 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
 #pragma unroll
                     for (int i = 0; i < NEW; ++i) hrow((int32_t)(oh * SH) - PT + (PH - NEW + i) * DH, ring[PH - NEW + i]);
                 }
+                const bool inner = (int32_t)oh >= oh_in0 && (int32_t)oh <= oh_in1;
                 uint32_t vr = PH;
-                if (TYPE == P_AVG && !p.cip) {
+                if (TYPE == P_AVG && !p.cip && !inner) {
                     vr = 0;
 #pragma unroll
                     for (int r = 0; r < PH; ++r) {
@@ -712,7 +717,7 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
                         else a = (int32_t)((uint32_t)a + (uint32_t)ring[r][v]);
                     }
                     if (TYPE == P_AVG) {
-                        const float inv = (p.cip || vr == (uint32_t)PH) ? inv_in[v] : inv_tab[vr * vc[v]];
+                        const float inv = (p.cip || inner || vr == (uint32_t)PH) ? inv_in[v] : inv_tab[vr * vc[v]];
                         res[v] = __float2int_rd(__fmul_rn(__int2float_rn(a), inv));
                     } else if (TYPE == P_LP2) {
                         res[v] = __float2int_rz(__fsqrt_rn(__int2float_rn(a)));   // NaN -> 0
