@@ -1003,35 +1003,44 @@ __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __re
     }
 }
 
-// Row form of the same conversion for fixed S_, C_: block = virtual row hv of one image
-// (grid (Hs, images)).  The S_ x C_ input rows it covers are staged in shared memory with
-// coalesced loads (rows outside the image as zeros), then thread wv converts virtual pixel
-// (hv, wv): no divisions, shared-memory reads, So written as one S_-word run per
-// original row.  S_*C_*W words fit in kS2dRowSmem.
+// Row form of the same conversion for fixed S_, C_: block = RB_ consecutive virtual rows
+// hv0 .. hv0 + RB_ - 1 of one image (grid (ceil(Hs / RB_), images)).  The input rows they
+// cover, (RB_ - 1) * S_ + T_ * S_ per channel, are staged in shared memory once with
+// coalesced loads (16-byte loads when rows are 16-byte aligned; rows outside the image as
+// zeros), so rows shared by consecutive virtual rows are read once; then each thread
+// converts virtual pixels (hv, wv): shared-memory reads, So written as one S_-word run per
+// original row.  The staged rows fit in kS2dRowSmem.
 constexpr uint32_t kS2dRowThreads = 128;
 constexpr uint32_t kS2dRowSmem = 32u * 1024u;
 
-// T_ = 2: the block also stages virtual row hv + 1 and writes its channels after those of
-// row hv (row stacking); So is written for row hv only.
-template <int S_, int C_, int T_ = 1>
+// input rows per channel a band of rb virtual rows stages
+__host__ __device__ constexpr uint32_t s2d_band_rows(uint32_t s, uint32_t t, uint32_t rb) { return (rb - 1) * s + t * s; }
+
+// T_ = 2: a virtual pixel also carries virtual row hv + 1 and writes its channels after
+// those of row hv (row stacking); So is written for row hv only.
+template <int S_, int C_, int T_ = 1, int RB_ = 1>
 __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int16_t* __restrict__ x, S2dGeom g,
                                                                         int8_t* __restrict__ planes,
                                                                         int32_t* __restrict__ So) {
     static_assert(S_ >= 2 && T_ * S_ * S_ * C_ <= 64, "space-to-depth channels");
     constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (T_ * C2 + 15u) / 16u * 16u;
-    extern __shared__ __align__(16) int16_t rowbuf[];      // [T_ * S_ * C_][W]
-    const uint32_t hv = blockIdx.x, n = blockIdx.y;
+    constexpr uint32_t RPC = s2d_band_rows(S_, T_, RB_);      // staged input rows per channel
+    extern __shared__ __align__(16) int16_t rowbuf[];      // [RPC][C_][W]
+    const uint32_t hv0 = blockIdx.x * RB_, n = blockIdx.y;
     const uint32_t W = g.W;
     const int16_t* xn = x + (uint64_t)n * C_ * g.H * W;
+    const bool quads = (W & 7u) == 0 && (((uintptr_t)x) & 15u) == 0;
     const bool pairs = (W & 1u) == 0 && (((uintptr_t)x) & 3u) == 0;
-#pragma unroll
-    for (uint32_t r = 0; r < (uint32_t)(T_ * S_ * C_); ++r) {
-        const uint32_t th = r / C_, c = r % C_;           // th < T_*S_: input row S_*hv + th
-        const int32_t ih = (int32_t)(S_ * hv + th) - (int32_t)g.pt;
+    for (uint32_t r = 0; r < RPC * (uint32_t)C_; ++r) {
+        const uint32_t lr = r / C_, c = r % C_;            // local row lr: input row S_*hv0 + lr - pt
+        const int32_t ih = (int32_t)(S_ * hv0 + lr) - (int32_t)g.pt;
         int16_t* dst = rowbuf + r * W;
         if (ih >= 0 && ih < (int32_t)g.H) {
             const int16_t* src = xn + ((uint64_t)c * g.H + (uint32_t)ih) * W;
-            if (pairs) {
+            if (quads) {
+                for (uint32_t i = threadIdx.x; i < W / 8; i += blockDim.x)
+                    ((uint4*)dst)[i] = __ldg((const uint4*)src + i);
+            } else if (pairs) {
                 for (uint32_t i = threadIdx.x; i < W / 2; i += blockDim.x)
                     ((uint32_t*)dst)[i] = __ldg((const uint32_t*)src + i);
             } else {
@@ -1043,12 +1052,16 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
     }
     __syncthreads();
     const uint64_t plane = (uint64_t)g.nimg * g.Hs * g.Ws * g.Cp;
-    for (uint32_t wv = threadIdx.x; wv < g.Ws; wv += blockDim.x) {
+    const uint32_t rows = min((uint32_t)RB_, g.Hs - hv0);
+    for (uint32_t item = threadIdx.x; item < rows * g.Ws; item += blockDim.x) {
+        const uint32_t i = item / g.Ws, wv = item - i * g.Ws;
+        const uint32_t hv = hv0 + i;
         uint32_t hw[CPC / 4], lw[CPC / 4];
 #pragma unroll
         for (uint32_t q = 0; q < CPC / 4; ++q) { hw[q] = 0; lw[q] = 0x80808080u; }
 #pragma unroll
         for (uint32_t th = 0; th < (uint32_t)(T_ * S_); ++th) {   // th >= S_: stacked row hv + 1
+            const int16_t* lrow = rowbuf + (S_ * i + th) * C_ * W;
             int32_t sums[S_];
 #pragma unroll
             for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) {
@@ -1058,7 +1071,7 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
 #pragma unroll
                 for (uint32_t c = 0; c < (uint32_t)C_; ++c) {
                     const uint32_t c2 = (th * S_ + tw) * C_ + c;
-                    const int16_t v = in ? rowbuf[(th * C_ + c) * W + (uint32_t)iw] : (int16_t)0;
+                    const int16_t v = in ? lrow[c * W + (uint32_t)iw] : (int16_t)0;
                     sum += (int32_t)v - 128;
                     const uint32_t q = c2 >> 2, sh = 8 * (c2 & 3);
                     hw[q] |= (uint32_t)(uint8_t)(v >> 8) << sh;
@@ -1477,10 +1490,20 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
                 const uint64_t row_smem = (uint64_t)sp.T * sp.s * in_ch * in_w * 2;
                 if (sp.T == 2) {
+                    // bands of 4 virtual rows when their input rows fit, else 2, else 1
+                    const uint64_t row_bytes = (uint64_t)in_ch * in_w * 2;
+                    const uint32_t rb = s2d_band_rows(2, 2, 4) * row_bytes <= kS2dRowSmem ? 4u
+                                        : s2d_band_rows(2, 2, 2) * row_bytes <= kS2dRowSmem ? 2u : 1u;
+                    const size_t band_smem = (size_t)(s2d_band_rows(2, 2, rb) * row_bytes);
+                    const uint32_t gx = (vp.Hp + rb - 1) / rb;
                     for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                         const uint32_t bz = std::min(65535u, nb - b0);
-                        conv_s2d_rows_kernel<2, 3, 2><<<dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s>>>(
-                            xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so);
+                        const int16_t* xb = xc + (uint64_t)b0 * in_ch * in_h * in_w;
+                        int8_t* pb = apl + (uint64_t)b0 * img_plane;
+                        int32_t* sb = So + (uint64_t)b0 * img_so;
+                        if (rb == 4) conv_s2d_rows_kernel<2, 3, 2, 4><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
+                        else if (rb == 2) conv_s2d_rows_kernel<2, 3, 2, 2><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
+                        else conv_s2d_rows_kernel<2, 3, 2, 1><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
                         count_launch();
                     }
                 } else if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
