@@ -183,6 +183,7 @@ __device__ void run_vectorop(const CallArgs& c) {
 }
 
 __global__ void __launch_bounds__(kCallThreads, 1) calls_kernel(const __grid_constant__ CallList L) {
+    griddep_wait();
     extern __shared__ __align__(16) int16_t stage_smem[];
     for (uint32_t k = 0; k < L.count; ++k) {
         const CallArgs& c = L.c[k];
@@ -283,7 +284,7 @@ extern "C" int cm_calls_async(const cm_call_t* calls, unsigned count, cm_stream_
     }
     {
         ProfScope ps_(PK_CONV_AUX, s);
-        calls_kernel<<<1, kCallThreads, kStageBytes, s>>>(L);
+        launch_k(calls_kernel, 1, kCallThreads, kStageBytes, s, L);
     }
     count_launch();
     cudaError_t e = cudaGetLastError();

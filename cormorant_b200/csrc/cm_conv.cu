@@ -37,6 +37,7 @@ struct DwArgs {
 __global__ void __launch_bounds__(256) conv_depthwise_kernel(const int16_t* __restrict__ x, const int16_t* __restrict__ w,
                                                              const int16_t* __restrict__ bias, int16_t* __restrict__ y,
                                                              DwArgs a, uint64_t total) {
+    griddep_wait();
     const uint64_t ohw = (uint64_t)a.out_h * a.out_w;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t plane = t / ohw;            // n * M + m
@@ -72,6 +73,7 @@ __device__ __forceinline__ int16_t epilogue_word(int16_t v, uint32_t epi, const 
 
 __global__ void __launch_bounds__(256) conv_epilogue_kernel(int16_t* __restrict__ y, const int16_t* __restrict__ resid,
                                                             uint64_t total, uint32_t epi) {
+    griddep_wait();
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x)
         y[t] = epilogue_word(y[t], epi, resid, t);
 }
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
                                                           const int16_t* __restrict__ bias, int16_t* __restrict__ y,
                                                           DwArgs a, uint64_t total, uint32_t G, uint32_t epi,
                                                           const int16_t* __restrict__ resid) {
+    griddep_wait();
     const uint64_t ohw = (uint64_t)a.out_h * a.out_w;
     const uint32_t khw = a.kh * a.kw, rows = a.C * a.kh;
     const uint32_t g = threadIdx.x & (G - 1);
@@ -120,6 +123,7 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
 // Empty reduction (in_ch * kh * kw == 0): every output is bias (or 0).
 __global__ void conv_bias_fill_kernel(const int16_t* __restrict__ bias, int16_t* __restrict__ y, uint32_t M,
                                       uint64_t ohw, uint64_t total, uint32_t has_bias) {
+    griddep_wait();
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t m = (t / ohw) % M;
         y[t] = has_bias ? bias[m] : (int16_t)0;
@@ -146,6 +150,7 @@ constexpr uint32_t kNhwcPix = 256, kNhwcCh = 32;
 
 __global__ void __launch_bounds__(256) conv_nhwc_split_kernel(const int16_t* __restrict__ x, NhwcGeom g,
                                                               int8_t* __restrict__ planes, int32_t* __restrict__ S) {
+    griddep_wait();
     __shared__ int16_t tile[kNhwcCh][kNhwcPix + 2];
     const uint32_t n = blockIdx.y;
     const uint32_t HWp = g.Hp * g.Wp;
@@ -204,6 +209,7 @@ constexpr uint32_t kImgSplitSmem = 100u * 1024u;
 __global__ void __launch_bounds__(kImgSplitThreads) conv_nhwc_split_img_kernel(const int16_t* __restrict__ x, NhwcGeom g,
                                                                                int8_t* __restrict__ planes,
                                                                                int32_t* __restrict__ S) {
+    griddep_wait();
     extern __shared__ __align__(16) uint8_t img_smem[];
     const uint32_t HW = g.H * g.W, words = g.C * HW;
     int16_t* img = (int16_t*)img_smem;
@@ -256,6 +262,7 @@ __global__ void __launch_bounds__(kImgSplitThreads) conv_nhwc_split_img_kernel(c
 // position.  The padding frame is written by conv_nhwc_border_kernel.
 __global__ void __launch_bounds__(256) conv_nhwc_split4_kernel(const int16_t* __restrict__ x, NhwcGeom g,
                                                                int8_t* __restrict__ planes, int32_t* __restrict__ S) {
+    griddep_wait();
     __shared__ uint2 tile[kNhwcCh][64 + 1];                 // [channel][quad], 4 words per entry
     const uint32_t n = blockIdx.y;
     const uint32_t HW = g.H * g.W, nq = HW / 4;
@@ -343,6 +350,7 @@ __global__ void __launch_bounds__(256) conv_nhwc_split4_kernel(const int16_t* __
 // input, then the left / right margins of the input rows.
 __global__ void __launch_bounds__(256) conv_nhwc_border_kernel(NhwcGeom g, int8_t* __restrict__ planes,
                                                                int32_t* __restrict__ S) {
+    griddep_wait();
     const uint32_t n = blockIdx.y;
     const uint32_t HWp = g.Hp * g.Wp;
     const uint64_t plane = (uint64_t)g.nimg * HWp * g.Cp;
@@ -378,6 +386,7 @@ __global__ void __launch_bounds__(256) conv_nhwc_border_kernel(NhwcGeom g, int8_
 __global__ void __launch_bounds__(256) planes_reset_S_kernel(int32_t* __restrict__ S, uint64_t total, FastDiv fwp,
                                                              FastDiv fhp, uint32_t H, uint32_t W, uint32_t pt,
                                                              uint32_t pl, int32_t frame) {
+    griddep_wait();
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         // rows of one image chunk stay below 2^31 words (checked by the caller)
         const uint32_t row = fwp.div((uint32_t)t), w = (uint32_t)t - row * fwp.d;
@@ -402,6 +411,7 @@ struct PoolPlanesGeo {
 __global__ void __launch_bounds__(256) pool_max_planes_kernel(const int8_t* __restrict__ xin, int8_t* __restrict__ yout,
                                                               int32_t* __restrict__ yS, PoolPlanesGeo g, uint64_t total,
                                                               FastDiv fd_ow, FastDiv fd_oh) {
+    griddep_wait();
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         // t < 2^32 (checked by the caller)
         const uint32_t row = fd_ow.div((uint32_t)t), ow = (uint32_t)t - row * fd_ow.d;
@@ -479,6 +489,7 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
                                                            uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw,
                                                            uint32_t sh, uint32_t sw, uint32_t dh, uint64_t total,
                                                            int32_t* __restrict__ rowterm, SumsReset z) {
+    griddep_wait();
     // blocks past the row-term grid clear the output image's sums, one image at a time
     if (z.S && blockIdx.x >= gridDim.x - z.nimg) {
         sums_reset_image(z, blockIdx.x - (gridDim.x - z.nimg), threadIdx.x / 32, blockDim.x / 32, threadIdx.x % 32, 32);
@@ -509,6 +520,7 @@ __global__ void __launch_bounds__(kRowtermThreads) conv_rowterm_rows_kernel(cons
                                                                           uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw,
                                                                           uint32_t dh, int32_t* __restrict__ rowterm,
                                                                           SumsReset z) {
+    griddep_wait();
     extern __shared__ uint32_t colsum_all[];
     const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
     // the last block column clears image blockIdx.y of the output image's sums
@@ -546,14 +558,14 @@ void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t W
             const uint32_t bz = std::min(65535u, nb - b0);
             SumsReset zb = z;
             if (zb.S) { zb.S += (uint64_t)b0 * zb.Hp * zb.Wp; zb.nimg = bz; }
-            conv_rowterm_rows_kernel<<<dim3((out_h + 3) / 4 + (zb.S ? 1u : 0u), bz), kRowtermThreads, (size_t)need_bytes, s>>>(
+            launch_k(conv_rowterm_rows_kernel, dim3((out_h + 3) / 4 + (zb.S ? 1u : 0u), bz), kRowtermThreads, (size_t)need_bytes, s, 
                 S + (uint64_t)b0 * Hp * Wp, Hp, Wp, out_h, out_w, kh, kw, sh, sw, dh, rt + (uint64_t)b0 * out_h * out_w, zb);
             count_launch();
         }
     } else {
         const uint64_t tot = (uint64_t)nb * out_h * out_w;
         if (z.S) z.nimg = nb;
-        conv_rowterm_kernel<<<grid_for(cx, tot, 256, 8) + (z.S ? nb : 0u), 256, 0, s>>>(S, Hp, Wp, out_h, out_w, kh, kw, sh,
+        launch_k(conv_rowterm_kernel, grid_for(cx, tot, 256, 8) + (z.S ? nb : 0u), 256, 0, s, S, Hp, Wp, out_h, out_w, kh, kw, sh,
                                                                                         sw, dh, tot, rt, z);
         count_launch();
     }
@@ -573,6 +585,7 @@ __global__ void __launch_bounds__(256) conv_weights_kernel(const int16_t* __rest
                                                            uint32_t M, uint32_t C, uint32_t kh, uint32_t kw, uint32_t Cp,
                                                            uint32_t KR_pad, uint32_t pitch, uint64_t plane,
                                                            int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    griddep_wait();
     __shared__ int16_t tile[32][130];
     const uint32_t khw = kh * kw, K = C * khw;
     const uint32_t k0 = blockIdx.x * 128, m0 = blockIdx.y * 32;
@@ -632,7 +645,7 @@ int conv_weights(const Context* cx, const int16_t* weight, const int16_t* bias, 
     const dim3 grid((K + 127) / 128, (M + 31) / 32);
     {
         ProfScope ps_(PK_SPLIT, s);
-        conv_weights_kernel<<<grid, 256, 0, s>>>(weight, bias, M, C, kh, kw, Cp, KR_pad, pitch, plane, planes, colterm);
+        launch_k(conv_weights_kernel, grid, 256, 0, s, weight, bias, M, C, kh, kw, Cp, KR_pad, pitch, plane, planes, colterm);
     }
     count_launch();
     return CM_OK;
@@ -650,6 +663,7 @@ constexpr uint32_t kIcRows = 128, kIcSlice = 160, kIcPitch = kIcSlice + 16;
 __global__ void __launch_bounds__(kIcRows) im2col_rows_kernel(const int16_t* __restrict__ x, ConvGeom g, uint32_t P,
                                                               uint64_t rows, uint32_t K, uint32_t K_pad,
                                                               int8_t* __restrict__ planes, int32_t* __restrict__ rowterm) {
+    griddep_wait();
     __shared__ __align__(16) int8_t stage[2][kIcRows * kIcPitch];
     const uint64_t plane = rows * K_pad;
     const uint64_t r0 = (uint64_t)blockIdx.x * kIcRows;
@@ -717,6 +731,7 @@ __global__ void __launch_bounds__(kIcRows) im2col_win_kernel(const int16_t* __re
                                                              uint64_t rows, uint32_t K, uint32_t K_pad, uint32_t WC,
                                                              FastDiv fd_wc, FastDiv fd_kh, int8_t* __restrict__ planes,
                                                              int32_t* __restrict__ rowterm) {
+    griddep_wait();
     extern __shared__ __align__(16) uint8_t smem_dyn[];
     int8_t* stage0 = (int8_t*)smem_dyn;
     int8_t* stage1 = stage0 + kIcRows * kIcPitch;
@@ -962,6 +977,7 @@ struct S2dGeom {
 template <int S_, int C_>
 __global__ void __launch_bounds__(256) conv_s2d_split_kernel(const int16_t* __restrict__ x, S2dGeom g, uint64_t total,
                                                              int8_t* __restrict__ planes, int32_t* __restrict__ So) {
+    griddep_wait();
     constexpr uint32_t CPC = S_ > 0 ? ((uint32_t)(S_ * S_ * C_) + 15u) / 16u * 16u : 0u;
     const uint32_t S = S_ > 0 ? (uint32_t)S_ : g.s, CC = C_ > 0 ? (uint32_t)C_ : g.C;
     const uint32_t Cp = CPC ? CPC : g.Cp;
@@ -1022,6 +1038,7 @@ template <int S_, int C_, int T_ = 1, int RB_ = 1>
 __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int16_t* __restrict__ x, S2dGeom g,
                                                                         int8_t* __restrict__ planes,
                                                                         int32_t* __restrict__ So) {
+    griddep_wait();
     static_assert(S_ >= 2 && T_ * S_ * S_ * C_ <= 64, "space-to-depth channels");
     constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (T_ * C2 + 15u) / 16u * 16u;
     constexpr uint32_t RPC = s2d_band_rows(S_, T_, RB_);      // staged input rows per channel
@@ -1108,6 +1125,7 @@ __global__ void __launch_bounds__(256) conv_s2d_weights_kernel(const int16_t* __
                                                                uint32_t kh, uint32_t kw, uint32_t s, uint32_t kw2,
                                                                uint32_t Cp, uint32_t KR_pad, uint32_t Kt, uint32_t pitch,
                                                                uint64_t plane, int8_t* __restrict__ planes, uint32_t T) {
+    griddep_wait();
     const uint64_t total = (uint64_t)Kt * M;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint32_t kp = (uint32_t)(t / M), m = (uint32_t)(t - (uint64_t)kp * M);
@@ -1192,8 +1210,8 @@ int planes_from_tensor(const Context* cx, const int16_t* x, cm_planes* yp, cudaS
         const int16_t* xb = x + (uint64_t)b0 * yp->C * HW;
         int8_t* pb = yp->planes + (uint64_t)b0 * img_plane;
         int32_t* Sb = yp->S + (uint64_t)b0 * yp->Hp * yp->Wp;
-        if (quads) conv_nhwc_split4_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
-        else conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+        if (quads) launch_k(conv_nhwc_split4_kernel, dim3(gx, bz), 256, 0, s, xb, ng, pb, Sb);
+        else launch_k(conv_nhwc_split_kernel, dim3(gx, bz), 256, 0, s, xb, ng, pb, Sb);
         count_launch();
     }
     cudaError_t e = cudaGetLastError();
@@ -1209,7 +1227,7 @@ int planes_reset(cm_planes* yp, cudaStream_t s) {
     for (uint32_t b0 = 0; b0 < yp->n; b0 += per) {
         const uint32_t nb = std::min(per, yp->n - b0);
         const uint64_t total = nb * img;
-        planes_reset_S_kernel<<<grid_for(cx, total, 256, 4), 256, 0, s>>>(
+        launch_k(planes_reset_S_kernel, grid_for(cx, total, 256, 4), 256, 0, s, 
             yp->S + (uint64_t)b0 * img, total, FastDiv(yp->Wp), FastDiv(yp->Hp), yp->H, yp->W, yp->pt, yp->pl,
             (int32_t)(0u - 128u * yp->C));
         count_launch();
@@ -1289,8 +1307,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                  has_bias ? 1u : 0u};
         {
             ProfScope ps_(PK_CONV_AUX, s);
-            conv_depthwise_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total);
-            if (epi) conv_epilogue_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(y, resid, total, epi);
+            launch_k(conv_depthwise_kernel, grid_for(cx, total, 256, 8), 256, 0, s, x, weight, bias, y, a, total);
+            if (epi) launch_k(conv_epilogue_kernel, grid_for(cx, total, 256, 8), 256, 0, s, y, resid, total, epi);
         }
         count_launch(epi ? 2 : 1);
         cudaError_t e = cudaGetLastError();
@@ -1301,8 +1319,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     if (K64 == 0) {
         {
             ProfScope ps_(PK_CONV_AUX, s);
-            conv_bias_fill_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(bias, y, out_ch, P, total, has_bias ? 1u : 0u);
-            if (epi) conv_epilogue_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(y, resid, total, epi);
+            launch_k(conv_bias_fill_kernel, grid_for(cx, total, 256, 8), 256, 0, s, bias, y, out_ch, P, total, has_bias ? 1u : 0u);
+            if (epi) launch_k(conv_epilogue_kernel, grid_for(cx, total, 256, 8), 256, 0, s, y, resid, total, epi);
         }
         count_launch(epi ? 2 : 1);
         cudaError_t e = cudaGetLastError();
@@ -1315,7 +1333,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         {
             ProfScope ps_(PK_CONV_AUX, s);
             const uint32_t G = direct_lanes(cx, total, (uint64_t)in_ch * kh);
-            conv_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(x, weight, bias, y, a, total, G, epi, resid);
+            launch_k(conv_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, x, weight, bias, y, a, total, G, epi, resid);
         }
         count_launch();
         cudaError_t e = cudaGetLastError();
@@ -1391,13 +1409,13 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                     int8_t* pb = apl + (uint64_t)b0 * img_plane;
                     int32_t* Sb = S + (uint64_t)b0 * ip.Hp * ip.Wp;
                     if (quads) {
-                        conv_nhwc_split4_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+                        launch_k(conv_nhwc_split4_kernel, dim3(gx, bz), 256, 0, s, xb, ng, pb, Sb);
                         count_launch();
                     } else if (whole) {
-                        conv_nhwc_split_img_kernel<<<bz, kImgSplitThreads, (size_t)img_smem, s>>>(xb, ng, pb, Sb);
+                        launch_k(conv_nhwc_split_img_kernel, bz, kImgSplitThreads, (size_t)img_smem, s, xb, ng, pb, Sb);
                         count_launch();
                     } else {
-                        conv_nhwc_split_kernel<<<dim3(gx, bz), 256, 0, s>>>(xb, ng, pb, Sb);
+                        launch_k(conv_nhwc_split_kernel, dim3(gx, bz), 256, 0, s, xb, ng, pb, Sb);
                         count_launch();
                     }
                 }
@@ -1408,7 +1426,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                         NhwcGeom gb = ng;
                         const uint32_t bz = std::min(65535u, nb - b0);
                         // images b0.. of the chunk: shift the planes / S bases, keep the chunk's plane stride
-                        conv_nhwc_border_kernel<<<dim3(bx, bz), 256, 0, s>>>(gb, apl + (uint64_t)b0 * img_plane,
+                        launch_k(conv_nhwc_border_kernel, dim3(bx, bz), 256, 0, s, gb, apl + (uint64_t)b0 * img_plane,
                                                                             S + (uint64_t)b0 * ip.Hp * ip.Wp);
                         count_launch();
                     }
@@ -1476,7 +1494,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         if (!rc && !pw) {
             ProfScope ps_(PK_SPLIT, s);
             const uint64_t wtot = (uint64_t)vp.Kt * out_ch;
-            conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
+            launch_k(conv_s2d_weights_kernel, grid_for(cx, wtot, 256, 8), 256, 0, s, weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
                                                                               vp.Cp, vp.KR_pad, vp.Kt, w_pitch, w_plane, wpl,
                                                                               sp.T);
             count_launch();
@@ -1501,24 +1519,24 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                         const int16_t* xb = xc + (uint64_t)b0 * in_ch * in_h * in_w;
                         int8_t* pb = apl + (uint64_t)b0 * img_plane;
                         int32_t* sb = So + (uint64_t)b0 * img_so;
-                        if (rb == 4) conv_s2d_rows_kernel<2, 3, 2, 4><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
-                        else if (rb == 2) conv_s2d_rows_kernel<2, 3, 2, 2><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
-                        else conv_s2d_rows_kernel<2, 3, 2, 1><<<dim3(gx, bz), kS2dRowThreads, band_smem, s>>>(xb, sg, pb, sb);
+                        if (rb == 4) launch_k(conv_s2d_rows_kernel<2, 3, 2, 4>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
+                        else if (rb == 2) launch_k(conv_s2d_rows_kernel<2, 3, 2, 2>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
+                        else launch_k(conv_s2d_rows_kernel<2, 3, 2, 1>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
                         count_launch();
                     }
                 } else if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
                     for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                         const uint32_t bz = std::min(65535u, nb - b0);
                         // images b0..: shift the input, planes and So bases; the plane stride stays the chunk's
-                        conv_s2d_rows_kernel<2, 3><<<dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s>>>(
+                        launch_k(conv_s2d_rows_kernel<2, 3>, dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s, 
                             xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so);
                         count_launch();
                     }
                 } else if (sp.s == 2 && in_ch == 3) {
-                    conv_s2d_split_kernel<2, 3><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
+                    launch_k(conv_s2d_split_kernel<2, 3>, grid_for(cx, vtot, 256, 8), 256, 0, s, xc, sg, vtot, apl, So);
                     count_launch();
                 } else {
-                    conv_s2d_split_kernel<0, 0><<<grid_for(cx, vtot, 256, 8), 256, 0, s>>>(xc, sg, vtot, apl, So);
+                    launch_k(conv_s2d_split_kernel<0, 0>, grid_for(cx, vtot, 256, 8), 256, 0, s, xc, sg, vtot, apl, So);
                     count_launch();
                 }
                 rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
@@ -1593,10 +1611,10 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
             const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
             if (win_smem) {
                 const dim3 grid((out_w + kIcRows - 1) / kIcRows, out_h, nb);
-                im2col_win_kernel<<<grid, kIcRows, win_smem, s>>>(xc, geo, (uint32_t)P, rows, K, K_pad, WC, FastDiv(WC),
+                launch_k(im2col_win_kernel, grid, kIcRows, win_smem, s, xc, geo, (uint32_t)P, rows, K, K_pad, WC, FastDiv(WC),
                                                                   FastDiv(kh), apl, rt);
             } else {
-                im2col_rows_kernel<<<(unsigned)((rows + kIcRows - 1) / kIcRows), kIcRows, 0, s>>>(xc, geo, (uint32_t)P, rows,
+                launch_k(im2col_rows_kernel, (unsigned)((rows + kIcRows - 1) / kIcRows), kIcRows, 0, s, xc, geo, (uint32_t)P, rows,
                                                                                               K, K_pad, apl, rt);
             }
         }
@@ -1860,7 +1878,7 @@ extern "C" int cm_pool_planes_async(const cm_planes_t* xp, cm_planes_t* yp, unsi
     cudaStream_t s = (cudaStream_t)stream;
     {
         ProfScope ps_(PK_POOL, s);
-        pool_max_planes_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(xp->planes, yp->planes, yp->S, g, total,
+        launch_k(pool_max_planes_kernel, grid_for(cx, total, 256, 8), 256, 0, s, xp->planes, yp->planes, yp->S, g, total,
                                                                         FastDiv(out_w), FastDiv(out_h));
     }
     count_launch();
@@ -1942,7 +1960,7 @@ extern "C" int cm_conv_weights_create(const int16_t* weight, const int16_t* bias
         if (!rc) {
             const ImplicitPlan& vp = sp.ip;
             const uint64_t wtot = (uint64_t)Kt * out_ch;
-            conv_s2d_weights_kernel<<<grid_for(cx, wtot, 256, 8), 256, 0, s>>>(weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
+            launch_k(conv_s2d_weights_kernel, grid_for(cx, wtot, 256, 8), 256, 0, s, weight, out_ch, in_ch, kh, kw, sp.s, sp.kw2,
                                                                               vp.Cp, vp.KR_pad, Kt, w_pitch,
                                                                               packed ? 64u : (uint64_t)Kt * M_pad, w->planes,
                                                                               sp.T);

@@ -419,6 +419,8 @@ __device__ __forceinline__ void conv_pixel(const GemmArgs& g, const Tile& tc, ui
 template <int TBN, int CG, bool WA = false, bool WIN = false>
 __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
+    griddep_wait();
+    griddep_launch_dependents();   // all CTAs are resident: the next kernel may launch now
     using C = Cfg<TBN, CG, WA>;
     static_assert(!WIN || (TBN == 64 && CG == 1 && !WA), "the window form runs packed 64-column tiles");
     constexpr int NBUF = C::NBUF;
@@ -1041,6 +1043,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
 // ceiling at the clocks of the moment: the denominator of the GEMM's roofline.
 template <int CG>
 __global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* status, uint64_t timeout_ns) {
+    griddep_wait();
     using C = Cfg<128, CG>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -1131,6 +1134,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restri
                                                          uint32_t rows, uint32_t K, uint32_t K_pad, uint64_t nrows_total,
                                                          int8_t* __restrict__ planes, int32_t* __restrict__ rowterm,
                                                          const int16_t* __restrict__ bias) {
+    griddep_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     for (uint64_t t = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; t < nrows_total; t += warps) {
@@ -1181,6 +1185,7 @@ __global__ void __launch_bounds__(256) split_kn_kernel(const int16_t* __restrict
                                                        uint32_t cols, uint32_t K, uint32_t C_pad, uint32_t k_chunk,
                                                        uint64_t plane_off, uint64_t batch_pitch,
                                                        int8_t* __restrict__ planes, int32_t* __restrict__ colterm) {
+    griddep_wait();
     const uint32_t bt = blockIdx.z;
     const uint32_t c8 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
     if (c8 >= cols) return;
@@ -1249,6 +1254,7 @@ __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __res
                                                             int16_t* __restrict__ c, uint32_t n, uint32_t k, uint32_t m,
                                                             uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, uint64_t total,
                                                             uint32_t G, uint32_t epi, const int16_t* __restrict__ bias) {
+    griddep_wait();
     const uint64_t nm = (uint64_t)n * m;
     const uint32_t g = threadIdx.x & (G - 1);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / G;
@@ -1275,6 +1281,7 @@ __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __res
 }
 
 __global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
+    griddep_wait();
     const uint64_t rc = (uint64_t)rows * cols;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t z = t / rc, rem = t - z * rc;
@@ -1430,6 +1437,7 @@ int make_wa_map(CUtensorMap* m, const int8_t* base, uint32_t Kt) {
 // p*64 + m of every K row).  Block = 128 K rows through shared memory.
 __global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __restrict__ packed, uint32_t Kt,
                                                              int8_t* __restrict__ rows) {
+    griddep_wait();
     __shared__ uint32_t tile[128][33];            // [k][byte / 4] of the packed rows
     const uint32_t k0 = blockIdx.x * 128;
     for (uint32_t q = threadIdx.x; q < 128 * 8; q += 256) {
@@ -1493,7 +1501,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            gemm_q88_kernel<TBN, CG, WA, WIN><<<clusters, Cfg<TBN, CG, WA>::THREADS, smem, s>>>(ta, tb, g);
+            launch_k(gemm_q88_kernel<TBN, CG, WA, WIN>, clusters, Cfg<TBN, CG, WA>::THREADS, smem, s, ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
@@ -1501,10 +1509,12 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
             q.dynamicSmemBytes = smem;
             q.stream = s;
-            cudaLaunchAttribute at{};
-            at.id = cudaLaunchAttributeClusterDimension;
-            at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
-            q.attrs = &at; q.numAttrs = 1;
+            cudaLaunchAttribute at[2]{};
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = CG; at[0].val.clusterDim.y = 1; at[0].val.clusterDim.z = 1;
+            at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+            at[1].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
+            q.attrs = at; q.numAttrs = 2;
             e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG, WA, WIN>, ta, tb, g);
         }
     }
@@ -1637,7 +1647,7 @@ int weights_to_rows(const Context* cx, const int8_t* packed, uint32_t Kt, int8_t
     if (Kt == 0 || Kt % 128 != 0) return set_error(CM_EINVAL, "weight rows: K = %u", Kt);
     {
         ProfScope ps_(PK_SPLIT, s);
-        packed_to_rows_kernel<<<Kt / 128, 256, 0, s>>>(packed, Kt, rows);
+        launch_k(packed_to_rows_kernel, Kt / 128, 256, 0, s, packed, Kt, rows);
     }
     count_launch();
     cudaError_t e = cudaGetLastError();
@@ -1652,7 +1662,7 @@ int split_rows(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t 
     const unsigned grid = grid_for(cx, total * 32, 128, 16);
     {
         ProfScope ps_(PK_SPLIT, s);
-        split_rows_kernel<<<grid, 128, 0, s>>>(src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
+        launch_k(split_rows_kernel, grid, 128, 0, s, src, src_bs, ld, rows, K, pad_k(K), total, planes, rowterm, bias);
     }
     count_launch();
     return CM_OK;
@@ -1687,7 +1697,7 @@ int split_kn(const Context* cx, const int16_t* src, uint64_t src_bs, uint64_t ld
         const dim3 grid(gx, (K + k_chunk - 1) / k_chunk, nb);
         {
             ProfScope ps_(PK_SPLIT, s);
-            split_kn_kernel<<<grid, block, 0, s>>>(src + (uint64_t)b0 * src_bs, src_bs, ld, cols, K, C_pad, k_chunk,
+            launch_k(split_kn_kernel, grid, block, 0, s, src + (uint64_t)b0 * src_bs, src_bs, ld, cols, K, C_pad, k_chunk,
                                                   plane_off, batch_pitch, planes + (uint64_t)b0 * batch_pitch,
                                                   colterm + (uint64_t)b0 * cols);
         }
@@ -1702,7 +1712,7 @@ int fill_zero(const Context* cx, int16_t* out, uint32_t batch, uint32_t rows, ui
     if (total == 0) return CM_OK;
     {
         ProfScope ps_(PK_CONV_AUX, s);
-        fill_zero_kernel<<<grid_for(cx, total, 256, 8), 256, 0, s>>>(out, rows, cols, ldo, out_bs, total);
+        launch_k(fill_zero_kernel, grid_for(cx, total, 256, 8), 256, 0, s, out, rows, cols, ldo, out_bs, total);
     }
     count_launch();
     return CM_OK;
@@ -1862,7 +1872,7 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
         {
             ProfScope ps_(PK_GEMM, s);
             const uint32_t G = direct_lanes(cx, total, k);
-            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(
+            launch_k(matmul_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, 
                 a, b, c, n, k, m, a_batch_stride, b_batch_stride, c_batch_stride, total, G, epi, bias);
         }
         count_launch();
@@ -1997,7 +2007,7 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
         {
             ProfScope ps_(PK_GEMM, s);
             const uint32_t G = direct_lanes(cx, total, k);
-            matmul_direct_kernel<<<grid_for(cx, total * G, 256, 8), 256, 0, s>>>(a, b, c, n, k, m, a_bs, b_bs, c_bs,
+            launch_k(matmul_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs,
                                                                                  total, G, 0u, nullptr);
         }
         count_launch();

@@ -109,6 +109,7 @@ __device__ __forceinline__ void cp_async_wait1() { asm volatile("cp.async.wait_g
 template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PL>
 __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                           PoolP p, uint64_t items, uint32_t aligned) {
+    griddep_wait();
     extern __shared__ __align__(16) int16_t smem[];
     __shared__ float inv_tab[65];
     const uint32_t ph = PH ? PH : p.ph, pw = PW ? PW : p.pw;
@@ -368,6 +369,7 @@ __global__ void __launch_bounds__(256) pool_stream_kernel(const int16_t* __restr
 template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PT, int PL>
 __global__ void __launch_bounds__(256) pool_rows_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                         PoolP p, uint64_t total) {
+    griddep_wait();
     constexpr int V = 8 / SW;
     constexpr int SPAN = (V - 1) * SW + (PW - 1) * DW + 1;   // input columns under the strip
     constexpr int HR = SPAN - PL - 8 > 0 ? SPAN - PL - 8 : 0;
@@ -548,6 +550,7 @@ template <int TYPE, int PH, int PW, int SH, int SW, int DH, int DW, int PT, int 
 __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y, PoolP p,
                                                          uint64_t planes, uint32_t buf_bytes, uint32_t rows_bot,
                                                          int* status, uint64_t timeout_ns) {
+    griddep_wait();
     constexpr int V = 8 / SW;
     constexpr int SPAN = (V - 1) * SW + (PW - 1) * DW + 1;   // input columns under the strip
     constexpr int HR = SPAN - PL - 8 > 0 ? SPAN - PL - 8 : 0;
@@ -746,6 +749,7 @@ __global__ void __launch_bounds__(512) pool_plane_kernel(const int16_t* __restri
 template <int TYPE>
 __global__ void __launch_bounds__(256) pool_direct_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                           PoolP p, uint64_t total) {
+    griddep_wait();
     const uint64_t ohw = (uint64_t)p.out_h * p.out_w;
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (uint64_t)gridDim.x * blockDim.x) {
         const uint64_t plane = t / ohw;
@@ -774,6 +778,7 @@ __device__ __forceinline__ void reduce_word(uint32_t& acc, int32_t v) {
 template <int TYPE>
 __global__ void __launch_bounds__(256) pool_global_small_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                                 uint64_t planes, uint32_t hw) {
+    griddep_wait();
     extern __shared__ __align__(16) int16_t sbuf[];     // blockDim.x planes x hw words
     const uint32_t ppb = blockDim.x, tid = threadIdx.x;
     for (uint64_t p0 = (uint64_t)blockIdx.x * ppb; p0 < planes; p0 += (uint64_t)gridDim.x * ppb) {
@@ -805,6 +810,7 @@ __global__ void __launch_bounds__(256) pool_global_small_kernel(const int16_t* _
 template <int TYPE>
 __global__ void __launch_bounds__(256) pool_global_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
                                                           uint64_t planes, uint32_t hw) {
+    griddep_wait();
     const uint32_t lane = threadIdx.x & 31;
     const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
     for (uint64_t plane = (uint64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; plane < planes; plane += warps) {
@@ -864,7 +870,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
             const unsigned grid = grid_for(cx, planes, ppb, 2048 / ppb);
             {
                 ProfScope ps_(PK_POOL, s);
-                pool_global_small_kernel<TYPE><<<grid, ppb, (size_t)ppb * hw * 2, s>>>(x, y, planes, (uint32_t)hw);
+                launch_k(pool_global_small_kernel<TYPE>, grid, ppb, (size_t)ppb * hw * 2, s, x, y, planes, (uint32_t)hw);
             }
             count_launch();
             return CM_OK;
@@ -872,7 +878,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         const unsigned grid = grid_for(cx, planes * 32, 256, 8);
         {
             ProfScope ps_(PK_POOL, s);
-            pool_global_kernel<TYPE><<<grid, 256, 0, s>>>(x, y, planes, p0.in_h * p0.in_w);
+            launch_k(pool_global_kernel<TYPE>, grid, 256, 0, s, x, y, planes, p0.in_h * p0.in_w);
         }
         count_launch();
         return CM_OK;
@@ -930,7 +936,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         int per_sm = 1;                                                                                  \
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_, (int)threads, smem);                 \
         const uint64_t grid = std::min<uint64_t>(planes, (uint64_t)cx->sm_count * std::max(per_sm, 1)); \
-        k_<<<(unsigned)grid, threads, smem, s>>>(x, y, p, planes, buf_bytes, rows_bot, cx->status, cx->timeout_ns); \
+        launch_k(k_, (unsigned)grid, threads, smem, s, x, y, p, planes, buf_bytes, rows_bot, cx->status, cx->timeout_ns); \
     } while (0)
             if (spec == 0)
                 CM_PLANE_LAUNCH(3, 3, 2, 2, 1, 1, 1, 1);
@@ -953,11 +959,11 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         {
             ProfScope ps_(PK_POOL, s);
             if (spec == 0)
-                pool_rows_kernel<TYPE, 3, 3, 2, 2, 1, 1, 1, 1><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+                launch_k(pool_rows_kernel<TYPE, 3, 3, 2, 2, 1, 1, 1, 1>, (unsigned)blocks, 256, 0, s, x, y, p, total);
             else if (spec == 1)
-                pool_rows_kernel<TYPE, 3, 3, 2, 2, 2, 2, 1, 1><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+                launch_k(pool_rows_kernel<TYPE, 3, 3, 2, 2, 2, 2, 1, 1>, (unsigned)blocks, 256, 0, s, x, y, p, total);
             else
-                pool_rows_kernel<TYPE, 2, 2, 2, 2, 1, 1, 0, 0><<<(unsigned)blocks, 256, 0, s>>>(x, y, p, total);
+                launch_k(pool_rows_kernel<TYPE, 2, 2, 2, 2, 1, 1, 0, 0>, (unsigned)blocks, 256, 0, s, x, y, p, total);
         }
         count_launch();
         return CM_OK;
@@ -989,7 +995,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
     do {                                                                                                 \
         auto k_ = pool_stream_kernel<TYPE, PH_, PW_, SH_, SW_, DH_, DW_, PL_>;                          \
         cudaFuncSetAttribute(k_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);               \
-        k_<<<(unsigned)grid, 256, smem, s>>>(x, y, p, items, aligned);                                  \
+        launch_k(k_, (unsigned)grid, 256, smem, s, x, y, p, items, aligned);                                  \
     } while (0)
             if (spec == 0)
                 CM_POOL_LAUNCH(3, 3, 2, 2, 1, 1, 1);
@@ -1005,7 +1011,7 @@ int launch(const Context* cx, const int16_t* x, int16_t* y, uint64_t planes, con
         const uint64_t total = planes * p.out_h * p.out_w;
         {
             ProfScope ps_(PK_POOL, s);
-            pool_direct_kernel<TYPE><<<grid_for(cx, total, 256, 8), 256, 0, s>>>(x, y, p, total);
+            launch_k(pool_direct_kernel<TYPE>, grid_for(cx, total, 256, 8), 256, 0, s, x, y, p, total);
         }
     }
     count_launch();

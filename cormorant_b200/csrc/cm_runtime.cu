@@ -20,6 +20,8 @@ static thread_local char t_err[512] = "";
 
 Context* ctx() { return g_ready ? &g_ctx : nullptr; }
 
+int g_pdl = 1;   // programmatic dependent launch of the library's kernels (CM_PDL=0 at cm_init: off)
+
 int set_error(int code, const char* fmt, ...) {
     va_list ap;
     va_start(ap, fmt);
@@ -177,6 +179,8 @@ int cm_init(const char* instance) {
     if (mo && *mo) c.matmul_overlap = atoi(mo) != 0;
     const char* cw = getenv("CM_CONV_WINDOW");
     if (cw && *cw) c.conv_window = atoi(cw) != 0;
+    const char* pd = getenv("CM_PDL");
+    g_pdl = (pd && *pd) ? (atoi(pd) != 0) : 1;
     e = cudaStreamCreateWithFlags(&c.aux_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         cudaFree(c.status);

@@ -10,6 +10,7 @@ namespace cm {
 namespace {
 
 __global__ void selftest_wait_kernel(int* status, uint64_t timeout_ns) {
+    griddep_wait();
     __shared__ __align__(8) uint64_t bar;
     __shared__ int abort_flag;
     if (threadIdx.x == 0) {
@@ -35,7 +36,7 @@ extern "C" int cm_selftest_wait_timeout(unsigned timeout_ms) {
     int rc = enter(&cx);
     if (rc) return rc;
     if (timeout_ms == 0 || timeout_ms > 10000) return set_error(CM_EINVAL, "cm_selftest_wait_timeout: 1..10000 ms");
-    selftest_wait_kernel<<<1, 32>>>(cx->status, (uint64_t)timeout_ms * 1000000ull);
+    launch_k(selftest_wait_kernel, 1, 32, 0, (cudaStream_t)0, cx->status, (uint64_t)timeout_ms * 1000000ull);
     count_launch();
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return cuda_error(e, "selftest launch");

@@ -95,6 +95,7 @@ template <int OP, bool TWO_D>
 __global__ void __launch_bounds__(256) vop_vec_kernel(const uint4* __restrict__ a, const uint4* __restrict__ b,
                                                       uint4* __restrict__ c, uint64_t total, FastDiv nv,
                                                       uint64_t a_inc, uint64_t b_inc, uint64_t c_inc) {
+    griddep_wait();
     constexpr bool UNARY = (OP >= K_RELU);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t0 < total; t0 += stride * UNROLL) {
@@ -131,6 +132,7 @@ template <int OP>
 __global__ void __launch_bounds__(256) vop_general_kernel(const int16_t* __restrict__ a, const int16_t* __restrict__ b,
                                                           int16_t* __restrict__ c, uint64_t c_len, uint32_t size,
                                                           uint32_t outer, uint64_t a_inc, uint64_t b_inc, uint64_t c_inc) {
+    griddep_wait();
     constexpr bool UNARY = (OP >= K_RELU);
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t j = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; j < c_len; j += stride) {
@@ -158,7 +160,7 @@ int launch_general(const Context* cx, const VopCall& v, cudaStream_t s) {
     const unsigned grid = grid_for(cx, c_len, 256, 16);
     {
         ProfScope ps_(PK_VECTOROP, s);
-        vop_general_kernel<OP><<<grid, 256, 0, s>>>(v.a, v.b, v.c, c_len, v.size, v.outer, v.a_inc, v.b_inc, v.c_inc);
+        launch_k(vop_general_kernel<OP>, grid, 256, 0, s, v.a, v.b, v.c, c_len, v.size, v.outer, v.a_inc, v.b_inc, v.c_inc);
     }
     count_launch();
     return CM_OK;
@@ -173,12 +175,12 @@ int launch_vec(const Context* cx, const int16_t* a, const int16_t* b, int16_t* c
     if (rows == 1) {
         {
             ProfScope ps_(PK_VECTOROP, s);
-            vop_vec_kernel<OP, false><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total, FastDiv(1), 0, 0, 0);
+            launch_k(vop_vec_kernel<OP, false>, grid, 256, 0, s, (const uint4*)a, (const uint4*)b, (uint4*)c, total, FastDiv(1), 0, 0, 0);
         }
     } else {
         {
             ProfScope ps_(PK_VECTOROP, s);
-            vop_vec_kernel<OP, true><<<grid, 256, 0, s>>>((const uint4*)a, (const uint4*)b, (uint4*)c, total,
+            launch_k(vop_vec_kernel<OP, true>, grid, 256, 0, s, (const uint4*)a, (const uint4*)b, (uint4*)c, total,
                                                           FastDiv((uint32_t)nv), a_inc_v, b_inc_v, c_inc_v);
         }
     }
