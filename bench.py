@@ -968,9 +968,10 @@ def int8_ceiling(cm, seconds: float = 0.4) -> dict:
     L = cm.lib()
     out = {}
     for pairs, key in ((1, "mma_pairs_tops"), (0, "mma_single_tops")):
-        tops, ms = C.c_double(), C.c_double()
-        _lib.check(L.cm_int8_mma_rate(pairs, 16384, C.byref(tops), C.byref(ms)))
+        tops, ms, mhz = C.c_double(), C.c_double(), C.c_double()
+        _lib.check(L.cm_int8_mma_rate(pairs, 16384, C.byref(tops), C.byref(ms), C.byref(mhz)))
         out[key] = round(tops.value, 1)
+        out[key.replace("_tops", "_sm_mhz")] = round(mhz.value, 1)
     n = 8192
     a = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda")
     b = torch.randint(-128, 128, (n, n), dtype=torch.int8, device="cuda").t().contiguous().t()
@@ -986,7 +987,9 @@ def int8_ceiling(cm, seconds: float = 0.4) -> dict:
         torch.cuda.synchronize()
         best = min(best, s_.elapsed_time(e_))
     out["cublaslt_int8_tops"] = round(2.0 * n ** 3 / (best * 1e-3) / 1e12, 1)
-    out["ceiling_tops"] = max(out["mma_pairs_tops"], out["mma_single_tops"])
+    best = "mma_pairs" if out["mma_pairs_tops"] >= out["mma_single_tops"] else "mma_single"
+    out["ceiling_tops"] = out[best + "_tops"]
+    out["ceiling_sm_mhz"] = out[best + "_sm_mhz"]     # the SM clock the ceiling was measured at
     del a, b
     torch.cuda.empty_cache()
     return out
@@ -1098,18 +1101,31 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
         achieved = (wl.dom_units_local * K) / (dms.value * 1e-3) / 1e12 if dms.value > 0 else 0.0
         which = "bf16_sustained" if elapsed_ms > 1500.0 else "bf16"
         proxy = 2.0 * peaks[which]
-        peak = ceiling["ceiling_tops"]
+        burst = ceiling["ceiling_tops"]
+        # The ceiling is a burst measurement taken just before the timed region, at the SM
+        # clock the probe reports; the GEMM runs for seconds, under the power cap, at the
+        # clock the sampler saw.  The pipe's rate per clock is fixed, so the ceiling at the
+        # GEMM's clock is the burst figure x run clock / probe clock: frac is the fraction
+        # of the pipe's per-clock capacity, whatever the power cap does to the clock.
+        run_mhz = (clocks or {}).get("sm_mhz")
+        probe_mhz = ceiling.get("ceiling_sm_mhz")
+        scale_ = run_mhz / probe_mhz if run_mhz and probe_mhz else 1.0
+        peak = round(burst * scale_, 1)
         roof = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"gemm_q88:{name}"),
                 "kernel": "gemm_q88_kernel",
+                "peak_burst": burst, "frac_of_burst": round(achieved / burst, 4),
+                "peak_clock_scale": {"run_sm_mhz": run_mhz, "ceiling_sm_mhz": probe_mhz, "scale": round(scale_, 4)},
                 "int8_ceiling": ceiling,
                 "int8_measured_tops": ceiling["cublaslt_int8_tops"],
                 "frac_of_cublaslt_int8": round(achieved / ceiling["cublaslt_int8_tops"], 4),
                 "proxy_2x_bf16": round(proxy, 1), "frac_of_proxy": round(achieved / proxy, 4),
                 "note": ("achieved = int8 tensor ops (4 s8 MMAs per Q8.8 multiply-add, 2 ops each) of the GEMM "
-                         "launches / their CUDA-event time on rank 0; peak = the int8 tensor pipe's ceiling "
+                         "launches / their CUDA-event time on rank 0; peak_burst = the int8 tensor pipe's ceiling "
                          "measured in this run just before the timed region (cm_int8_mma_rate: the GEMM's MMA "
-                         "stream on shared-memory-resident operands, best of CTA pairs and single CTAs); also "
+                         "stream on shared-memory-resident operands, best of CTA pairs and single CTAs, at the SM "
+                         "clock it reports); peak = that ceiling at the timed region's median SM clock (burst x "
+                         "run clock / probe clock: the pipe's per-clock capacity at the clock the power cap left); also "
                          f"against cuBLASLt's int8 GEMM (a library rate, not a ceiling) and 2 x the {peaks['source']} "
                          f"bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} rate {peaks[which]} TF/s; "
                          "traffic = DRAM bytes of "

@@ -33,7 +33,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_set_direct_limit": (C.c_uint64, [C.c_uint64]),
     "cm_version": (C.c_char_p, []),
     "cm_selftest_wait_timeout": (C.c_int, [_u]),
-    "cm_int8_mma_rate": (C.c_int, [_u, _u, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "cm_int8_mma_rate": (C.c_int, [_u, _u, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "cm_profile_begin": (C.c_int, []),
     "cm_profile_end": (C.c_int, []),
     "cm_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),

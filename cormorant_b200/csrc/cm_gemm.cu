@@ -1042,7 +1042,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
 // the same TMEM accumulators.  The rate reached is the int8 tensor pipe's own
 // ceiling at the clocks of the moment: the denominator of the GEMM's roofline.
 template <int CG>
-__global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* status, uint64_t timeout_ns) {
+__global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* status, uint64_t timeout_ns,
+                                                          unsigned long long* clk) {
     griddep_wait();
     using C = Cfg<128, CG>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1085,6 +1086,12 @@ __global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* s
     if (CG == 2) cluster_sync_all();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // the SM clock over the stream: clock64 ticks against %globaltimer nanoseconds
+    unsigned long long c0 = 0, t0 = 0;
+    if (threadIdx.x == 0) {
+        asm volatile("mov.u64 %0, %%clock64;" : "=l"(c0));
+        t0 = gtimer();
+    }
     if (warp == 0 && lane == 0 && rank == 0) {
         const uint32_t a0 = smem_u32(smem), b0 = a0 + OPERAND_TILE;
         for (uint32_t it = 0; it < iters; ++it) {
@@ -1109,6 +1116,12 @@ __global__ void __launch_bounds__(128, 1) mma_rate_kernel(uint32_t iters, int* s
     if (threadIdx.x == 0) {
         const WaitCtl wc{abort_flag, status, timeout_ns};
         mbar_wait(smem_u32(done_b), 0, wc);
+        if (blockIdx.x == 0 && clk) {
+            unsigned long long c1;
+            asm volatile("mov.u64 %0, %%clock64;" : "=l"(c1));
+            clk[0] = c1 - c0;
+            clk[1] = gtimer() - t0;
+        }
     }
     __syncthreads();
     if (CG == 2) cluster_sync_all();
@@ -2081,7 +2094,7 @@ extern "C" int cm_matmul_at(const int16_t* a, unsigned a_off, const int16_t* b, 
 // ---------------------------------------------------------------------------
 // cm_int8_mma_rate: the int8 tensor pipe's ceiling, measured (no reference counterpart)
 // ---------------------------------------------------------------------------
-extern "C" int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms) {
+extern "C" int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms, double* sm_mhz) {
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
@@ -2115,11 +2128,13 @@ extern "C" int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, do
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     q.stream = s;
+    unsigned long long* clk = nullptr;           // CTA 0's clock64 ticks and nanoseconds
+    if ((e = cudaMalloc(&clk, 2 * sizeof(unsigned long long))) != cudaSuccess) rc = cuda_error(e, "cudaMalloc(mma rate)");
     // one untimed launch (module load, clocks up), then the timed one
     for (int pass = 0; pass < 2 && !rc; ++pass) {
         if (pass == 1) cudaEventRecord(e0, s);
-        e = pairs ? cudaLaunchKernelEx(&q, mma_rate_kernel<2>, iters, cx->status, cx->timeout_ns)
-                  : cudaLaunchKernelEx(&q, mma_rate_kernel<1>, iters, cx->status, cx->timeout_ns);
+        e = pairs ? cudaLaunchKernelEx(&q, mma_rate_kernel<2>, iters, cx->status, cx->timeout_ns, clk)
+                  : cudaLaunchKernelEx(&q, mma_rate_kernel<1>, iters, cx->status, cx->timeout_ns, clk);
         count_launch();
         if (e != cudaSuccess) rc = cuda_error(e, "mma rate launch");
     }
@@ -2127,10 +2142,14 @@ extern "C" int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, do
     if (!rc) rc = finish_sync((cm_stream_t)s);
     float t = 0.f;
     if (!rc && (e = cudaEventElapsedTime(&t, e0, e1)) != cudaSuccess) rc = cuda_error(e, "mma rate events");
+    unsigned long long hc[2] = {0, 0};
+    if (!rc && (e = cudaMemcpy(hc, clk, sizeof(hc), cudaMemcpyDeviceToHost)) != cudaSuccess) rc = cuda_error(e, "mma rate clock");
+    if (clk) cudaFree(clk);
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     cudaStreamDestroy(s);
     if (rc) return rc;
+    if (sm_mhz) *sm_mhz = hc[1] ? 1e3 * (double)hc[0] / (double)hc[1] : 0.0;
     // per CTA and round: 4 K steps x 2 MMAs x 128 rows x 256 columns x 32 deep, 2 ops per MAC
     const double ops = (double)ctas * iters * 4.0 * 2.0 * 128.0 * 256.0 * 32.0 * 2.0;
     *ms = t;

@@ -99,8 +99,11 @@ int cm_selftest_wait_timeout(unsigned timeout_ms);
  * cta_group::2 (pairs = 1), `iters` (1..65536) rounds of 8 MMAs each, after one
  * untimed launch.  Returns the int8 ops per second reached (TOPS, 2 ops per
  * multiply-add) and the timed launch's device time in ms: the roofline
- * denominator of the Q8.8 GEMM, measured at the clocks of the moment. */
-int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms);
+ * denominator of the Q8.8 GEMM, measured at the clocks of the moment.  `sm_mhz`
+ * (may be NULL) receives the SM clock over the timed stream (clock64 ticks per
+ * %globaltimer microsecond in CTA 0), so the ceiling can be scaled to the clock
+ * another measurement ran at. */
+int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms, double* sm_mhz);
 
 /* ---- device timing of this library's launches (no reference counterpart) --
  * Between cm_profile_begin and cm_profile_end every kernel launch is bracketed

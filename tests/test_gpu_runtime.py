@@ -131,10 +131,13 @@ def test_int8_mma_rate(cm, pairs):
     """The ceiling measurement runs, returns a plausible rate and leaves the library usable."""
     from cormorant_b200 import _lib
     L = _lib.lib()
-    tops, ms = C.c_double(), C.c_double()
-    _lib.check(L.cm_int8_mma_rate(pairs, 2048, C.byref(tops), C.byref(ms)))
+    tops, ms, mhz = C.c_double(), C.c_double(), C.c_double()
+    _lib.check(L.cm_int8_mma_rate(pairs, 2048, C.byref(tops), C.byref(ms), C.byref(mhz)))
     assert ms.value > 0.0
     # between a tenth of and twice the datasheet's dense int8 rate (4.5 POPS)
     assert 450.0 < tops.value < 9000.0, tops.value
-    assert L.cm_int8_mma_rate(pairs, 0, C.byref(tops), C.byref(ms)) == _lib.CM_EINVAL
-    assert L.cm_int8_mma_rate(2, 16, C.byref(tops), C.byref(ms)) == _lib.CM_EINVAL
+    # an SM clock between 300 MHz and the B200's 1965 MHz maximum (plus measurement slack)
+    assert 300.0 < mhz.value < 2100.0, mhz.value
+    _lib.check(L.cm_int8_mma_rate(pairs, 16, C.byref(tops), C.byref(ms), None))
+    assert L.cm_int8_mma_rate(pairs, 0, C.byref(tops), C.byref(ms), None) == _lib.CM_EINVAL
+    assert L.cm_int8_mma_rate(2, 16, C.byref(tops), C.byref(ms), None) == _lib.CM_EINVAL
