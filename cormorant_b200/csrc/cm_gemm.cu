@@ -1293,6 +1293,56 @@ __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __res
     }
 }
 
+// The same products for a few rows (n <= NR): a block owns 32 consecutive output columns
+// of one batch step (grid (ceil(m / 32), batch)); lane = column, so each load of a B row
+// reads 32 adjacent words, the block's 8 warps take every 8th k, the A words are
+// broadcast loads, and each lane keeps one int32 wrap sum per row.  The 8 partial sums
+// meet in shared memory (wrap addition: order-free) and warp 0 narrows, adds the
+// epilogue and stores.  Batch steps run in parallel: their output slices do not overlap
+// (overlapping ones take the in-order loop before the direct path).
+template <int NR>
+__global__ void __launch_bounds__(256) matmul_rows_direct_kernel(const int16_t* __restrict__ a,
+                                                                 const int16_t* __restrict__ b, int16_t* __restrict__ c,
+                                                                 uint32_t n, uint32_t k, uint32_t m, uint64_t a_bs,
+                                                                 uint64_t b_bs, uint64_t c_bs, uint32_t epi,
+                                                                 const int16_t* __restrict__ bias) {
+    griddep_wait();
+    __shared__ uint32_t part[8][NR][32];
+    const uint32_t lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
+    const uint32_t j = blockIdx.x * 32u + lane;
+    const uint64_t z = blockIdx.y;
+    const int16_t* A = a + z * a_bs;
+    const int16_t* B = b + z * b_bs + j;
+    uint32_t acc[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) acc[r] = 0;
+    if (j < m) {
+#pragma unroll 4
+        for (uint32_t q = w; q < k; q += 8) {
+            const int32_t bv = __ldg(B + (uint64_t)q * m);
+#pragma unroll
+            for (int r = 0; r < NR; ++r)
+                if ((uint32_t)r < n) acc[r] += (uint32_t)((int32_t)__ldg(A + (uint64_t)r * k + q) * bv);
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r) part[w][r][lane] = acc[r];
+    __syncthreads();
+    if (w == 0 && j < m) {
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+            if ((uint32_t)r >= n) break;
+            uint32_t s = part[0][r][lane];
+#pragma unroll
+            for (int x = 1; x < 8; ++x) s += part[x][r][lane];
+            int32_t v = narrow_acc(s);
+            if (epi & 2u) v = sat16(v + (int32_t)__ldg(bias + j));
+            if (epi & 1u) v = max(v, 0);
+            c[z * c_bs + (uint64_t)r * m + j] = (int16_t)v;
+        }
+    }
+}
+
 __global__ void fill_zero_kernel(int16_t* out, uint32_t rows, uint32_t cols, uint64_t ldo, uint64_t out_bs, uint64_t total) {
     griddep_wait();
     const uint64_t rc = (uint64_t)rows * cols;
@@ -1549,6 +1599,25 @@ uint32_t direct_lanes(const Context* cx, uint64_t outputs, uint64_t red) {
     while (G < 32 && outputs * G < want && 2ull * G <= red) G *= 2;
     return G;
 }
+
+// Direct MatMul launch: the row form for at most 8 rows, else the general one.
+void launch_matmul_direct(const Context* cx, const int16_t* a, const int16_t* b, int16_t* c, uint32_t n, uint32_t k,
+                          uint32_t m, uint32_t batch, uint64_t a_bs, uint64_t b_bs, uint64_t c_bs, uint32_t epi,
+                          const int16_t* bias, cudaStream_t s) {
+    if (n <= 8 && batch <= 65535u) {
+        const dim3 grid((m + 31) / 32, batch);
+        if (n == 1) launch_k(matmul_rows_direct_kernel<1>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else if (n == 2) launch_k(matmul_rows_direct_kernel<2>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else if (n <= 4) launch_k(matmul_rows_direct_kernel<4>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else launch_k(matmul_rows_direct_kernel<8>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        return;
+    }
+    const uint64_t total = (uint64_t)batch * n * m;
+    const uint32_t G = direct_lanes(cx, total, k);
+    launch_k(matmul_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, total,
+             G, epi, bias);
+}
+
 
 int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     if (p.conv) return gemm_launch_conv(cx, p, s);
@@ -1880,13 +1949,11 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
         return rc;
     }
     const unsigned __int128 macs = (unsigned __int128)batch * n * m * k;
-    const uint64_t total = (uint64_t)batch * n * m;
     if (macs <= cx->direct_max_macs) {
         {
             ProfScope ps_(PK_GEMM, s);
-            const uint32_t G = direct_lanes(cx, total, k);
-            launch_k(matmul_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, 
-                a, b, c, n, k, m, a_batch_stride, b_batch_stride, c_batch_stride, total, G, epi, bias);
+            launch_matmul_direct(cx, a, b, c, n, k, m, batch, a_batch_stride, b_batch_stride, c_batch_stride, epi, bias,
+                                 s);
         }
         count_launch();
         cudaError_t e = cudaGetLastError();
@@ -2016,12 +2083,9 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
     const unsigned __int128 macs = (unsigned __int128)nb * n * m * k;
     if (macs <= cx->direct_max_macs) {
         // launch-bound sizes: the one-kernel CUDA-core path, which needs no scratch at all
-        const uint64_t total = (uint64_t)nb * n * m;
         {
             ProfScope ps_(PK_GEMM, s);
-            const uint32_t G = direct_lanes(cx, total, k);
-            launch_k(matmul_direct_kernel, grid_for(cx, total * G, 256, 8), 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs,
-                                                                                 total, G, 0u, nullptr);
+            launch_matmul_direct(cx, a, b, c, n, k, m, nb, a_bs, b_bs, c_bs, 0u, nullptr, s);
         }
         count_launch();
         return CM_OK;

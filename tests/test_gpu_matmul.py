@@ -19,7 +19,11 @@ SHAPES = [(1, 1, 1, 1), (4, 256, 16, 1), (8, 256, 16, 1), (4, 512, 16, 1), (4, 2
           (4, 261, 16, 1), (4, 256, 19, 1), (6, 261, 19, 1), (7, 13, 5, 1), (5, 1, 17, 1), (1, 256, 16, 1),
           (4, 256, 1, 1), (12, 519, 33, 1), (128, 128, 128, 1), (129, 130, 131, 2), (255, 257, 383, 3),
           (1, 400, 120, 1), (1, 120, 84, 1), (1, 84, 10, 1), (256, 512, 1000, 1), (300, 17, 200, 4),
-          (64, 32, 64, 5), (33, 4096, 65, 1)]
+          (64, 32, 64, 5), (33, 4096, 65, 1),
+          # few-row direct form (lane = output column, warps split k): rows below the
+          # template's width, exactly 8 rows, widths off a multiple of 32, k < 8 (idle
+          # warps), a batch of 100 steps on the grid's y axis
+          (3, 7, 70, 3), (8, 1000, 33, 2), (2, 5, 100, 100), (1, 3, 31, 1)]
 
 
 @pytest.mark.parametrize("n,k,m,batch", SHAPES)
