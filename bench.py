@@ -596,7 +596,9 @@ class NetworkBench:
             return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
                     "parallelism": f"replicas only: one batch-1 stream per GPU ({world})", "calls": calls,
                     "launches": ("whole call list run as one kernel launch (cm_calls), captured as a CUDA graph"
-                                 if ONE_LAUNCH else "whole call list captured once as a CUDA graph and replayed")}
+                                 if ONE_LAUNCH else "whole call list captured once as a CUDA graph and replayed")
+                    + (f"; {self.SEQ_IMAGES} consecutive batch-1 inferences (each its whole call list, in order on"
+                       " one stream) per graph replay, so one host launch serves 8 images" if GRAPH else "")}
         return {"workload": "resnet18-shaped (BASELINE configs[3])", "batch": 256,
                 "input": "256x3x224x224 uniform [0,1)", "macs_per_image": self.net.macs_per_image, "calls": calls,
                 "parallelism": f"batch-sharded over {world} GPU(s)", "l2": "inputs larger than L2 (77 MB input, 1.1 GB activations)",
@@ -611,16 +613,25 @@ class NetworkBench:
         # the network's conv weights prepared once (constants of the call list)
         self.wcache = networks.prepare_weights(self.net, self.bufs) if PREPARED and self.local > 0 else {}
         self.graph = None
+        self.graph_seq = None
+        self.pending = 0
         if GRAPH and self.local > 0:
             self.graph, self.launches_per_step = self._capture(self.bufs)
+            if self.which == "lenet":
+                # batch-1 inferences take ~20 us each: one host graph launch per image would
+                # make the rate depend on how fast the host submits, so SEQ_IMAGES consecutive
+                # inferences (each its whole call list, in order on one stream) form one graph
+                self.graph_seq, _ = self._capture(self.bufs, reps=self.SEQ_IMAGES)
 
     def _backend(self, stream):
         from cormorant_b200 import networks
         return networks.GpuBackend(stream, one_launch=ONE_LAUNCH, weights=self.wcache)
 
-    def _capture(self, bufs):
+    SEQ_IMAGES = 8      # LeNet: consecutive inferences per replay of the device-timed graph
+
+    def _capture(self, bufs, reps=1):
         """The whole call list captured once as a CUDA graph (its scratch allocations become
-        graph memory nodes); returns (graph, kernel launches per replay)."""
+        graph memory nodes), `reps` times in a row; returns (graph, kernel launches per pass)."""
         import torch
         import cormorant_b200 as cm
         from cormorant_b200 import networks
@@ -634,8 +645,9 @@ class NetworkBench:
         l0 = cm.launch_count()
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
-            networks.execute(self.net, self._backend(torch.cuda.current_stream()), bufs)
-        n = cm.launch_count() - l0
+            for _ in range(reps):
+                networks.execute(self.net, self._backend(torch.cuda.current_stream()), bufs)
+        n = (cm.launch_count() - l0) // reps
         torch.cuda.synchronize()
         return g, n
 
@@ -677,10 +689,21 @@ class NetworkBench:
 
     def step(self, cm, stream):
         from cormorant_b200 import networks
-        if self.graph is not None:
+        if self.graph_seq is not None:
+            self.pending += 1
+            if self.pending == self.SEQ_IMAGES:
+                self.graph_seq.replay()
+                self.pending = 0
+        elif self.graph is not None:
             self.graph.replay()
         elif self.local > 0:
             networks.execute(self.net, self._backend(stream), self.bufs)
+
+    def step_flush(self, cm, stream):
+        """Steps not yet run by a multi-image replay run one by one."""
+        for _ in range(self.pending):
+            self.graph.replay()
+        self.pending = 0
 
     def per_part(self, cm, stream, iters):
         import ctypes as C
@@ -702,6 +725,7 @@ class NetworkBench:
     def release(self):
         self.bufs = None
         self.graph = None
+        self.graph_seq = None
         self._into = None
         self.wcache = {}
 
@@ -738,16 +762,23 @@ class NetworkBench:
                     self.e2e_graphs.append(self._capture(self.bufs)[0])
                 self.e2e_path += "; the call list replayed as a CUDA graph (one per input buffer)"
         if self.which == "lenet":
-            self.e2e_path += "; captured once as a CUDA graph and replayed per image"
-            # batch 1 is host-launch-bound: the whole step (pinned H2D copy, the call
-            # list, D2H copy of the logits) is captured once and replayed per image
+            # batch 1 is host-launch-bound: the whole step (pinned H2D copy, the call list,
+            # D2H copy of the logits) is captured once as a CUDA graph (also the remainder
+            # path), and E2E_IMAGES consecutive steps are captured as one pipelined graph
             for _ in range(3):
                 self._e2e_body()
             torch.cuda.synchronize()
+            self.want_y = self.hy.clone()                     # the logits of a plain step
             self.e2e_graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(self.e2e_graph):
                 self._e2e_body()
             torch.cuda.synchronize()
+            self._capture_pipelined_lenet()
+            self.e2e_path += (f"; {self.E2E_IMAGES} consecutive batch-1 inferences captured as one CUDA graph and replayed:"
+                              " each image's call list runs alone on the compute stream, image i+1's input copy"
+                              " (copy stream) overlaps image i's call list and image i's logits copy (a third"
+                              " stream) overlaps image i+1's; input and output buffers double-buffered, events"
+                              " order every reuse")
 
     def _e2e_body(self):
         import torch
@@ -756,13 +787,82 @@ class NetworkBench:
         networks.execute(self.net, self._backend(torch.cuda.current_stream()), self.bufs)
         self.hy.copy_(self.bufs[self.net.resolve(self.net.output)], non_blocking=True)
 
+    E2E_IMAGES = 8      # consecutive batch-1 inferences per pipelined LeNet graph
+
+    def _capture_pipelined_lenet(self):
+        """E2E_IMAGES steps as one graph: per image an upload on the copy stream into input
+        buffer b = i % 2, the call list on the capture stream (reading x_b, writing y_b), and
+        the logits download on the download stream; image i+2's upload waits for image i's
+        call list (x_b free), image i+2's call list for image i's download (y_b free)."""
+        import torch
+        from cormorant_b200 import networks
+        K = self.E2E_IMAGES
+        xin, yout = self.net.input, self.net.resolve(self.net.output)
+        xb = [self.bufs[xin], torch.empty_like(self.bufs[xin])]
+        yb = [self.bufs[yout], torch.empty_like(self.bufs[yout])]
+        self.hxs = [self.hx.clone().pin_memory() for _ in range(K)]
+        self.hys = [torch.empty_like(self.hy).pin_memory() for _ in range(K)]
+        up, down = torch.cuda.Stream(), torch.cuda.Stream()
+
+        def body():
+            main = torch.cuda.current_stream()
+            up.wait_stream(main)
+            down.wait_stream(main)
+            used, drained = [None, None], [None, None]
+            for i in range(K):
+                b = i % 2
+                with torch.cuda.stream(up):
+                    if used[b] is not None:
+                        up.wait_event(used[b])
+                    xb[b].copy_(self.hxs[i], non_blocking=True)
+                    ready = torch.cuda.Event()
+                    ready.record(up)
+                main.wait_event(ready)
+                if drained[b] is not None:
+                    main.wait_event(drained[b])
+                bufs = dict(self.bufs)
+                bufs[xin], bufs[yout] = xb[b], yb[b]
+                networks.execute(self.net, self._backend(main), bufs)
+                done = torch.cuda.Event()
+                done.record(main)
+                used[b] = done
+                with torch.cuda.stream(down):
+                    down.wait_event(done)
+                    self.hys[i].copy_(yb[b], non_blocking=True)
+                    fin = torch.cuda.Event()
+                    fin.record(down)
+                drained[b] = fin
+            main.wait_stream(up)
+            main.wait_stream(down)
+
+        for _ in range(2):
+            body()
+        torch.cuda.synchronize()
+        self.e2e_pipe_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.e2e_pipe_graph):
+            body()
+        torch.cuda.synchronize()
+        self.e2e_pending = 0
+
     def e2e_step(self):
-        if self.e2e_graph is not None:
+        if getattr(self, "e2e_pipe_graph", None) is not None:
+            self.e2e_pending += 1
+            if self.e2e_pending == self.E2E_IMAGES:
+                self.e2e_pipe_graph.replay()
+                self.e2e_pending = 0
+        elif self.e2e_graph is not None:
             self.e2e_graph.replay()
         elif self.copy_stream is not None:
             self._e2e_pipelined()
         else:
             self._e2e_body()
+
+    def e2e_finish(self):
+        """Steps not yet run by a pipelined replay run one by one."""
+        if getattr(self, "e2e_pipe_graph", None) is not None:
+            for _ in range(self.e2e_pending):
+                self.e2e_graph.replay()
+            self.e2e_pending = 0
 
     def e2e_start(self, start_event):
         """Timed region starts: the first input copy is issued inside it."""
@@ -786,7 +886,12 @@ class NetworkBench:
 
     def e2e_extra(self):
         """The input copies' own device time (host -> device over PCIe): how much of a step
-        the copy takes when the host is busy or idle."""
+        the copy takes when the host is busy or idle.  LeNet: whether every image's logits
+        copied back by the pipelined graph equal those of a plain step."""
+        if getattr(self, "e2e_pipe_graph", None) is not None:
+            import torch
+            torch.cuda.synchronize()
+            return {"outputs_match": all(bool(torch.equal(h, self.want_y)) for h in self.hys + [self.hy])}
         if not getattr(self, "copy_times", None):
             return {}
         ms = [a.elapsed_time(b) for a, b in self.copy_times[1:]] or [0.0]
@@ -815,6 +920,7 @@ class NetworkBench:
 
     def e2e_release(self):
         self.e2e_graph = None
+        self.e2e_pipe_graph = None
         self.e2e_graphs = None
         self.bufs = None
         self.wcache = {}
@@ -1053,6 +1159,8 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
     torch.cuda.synchronize()
     for _ in range(W):
         wl.step(cm, stream)
+    if hasattr(wl, "step_flush"):
+        wl.step_flush(cm, stream)
     torch.cuda.synchronize()
     env.barrier()
 
@@ -1068,6 +1176,8 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
     start.record(stream)
     for _ in range(K):
         wl.step(cm, stream)
+    if hasattr(wl, "step_flush"):
+        wl.step_flush(cm, stream)
     end.record(stream)
     torch.cuda.synchronize()
     L.cm_profile_end()
