@@ -55,7 +55,10 @@ SIGNATURES: dict[str, tuple] = {
     "cm_planes_fill_async": (C.c_int, [_p, _p, _p]),
     "cm_pool_planes": (C.c_int, [_p, _p] + [_u] * 17),
     "cm_pool_planes_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
+    "cm_pool_nhwc_planes": (C.c_int, [_p, _p] + [_u] * 15),
+    "cm_pool_nhwc_planes_async": (C.c_int, [_p, _p] + [_u] * 15 + [_p]),
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),
+    "cm_conv_writes_nhwc": (C.c_int, [_u] * 17),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),
     "cm_conv_weights_create": (C.c_int, [_p, _p] + [_u] * 17 + [C.POINTER(_p)]),

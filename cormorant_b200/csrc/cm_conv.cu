@@ -465,6 +465,73 @@ __global__ void __launch_bounds__(256) pool_max_planes_kernel(const int8_t* __re
     }
 }
 
+// MAX pool from a channels-last int16 tensor x [n][in_h][in_w][C] (C a multiple of 16) to
+// plane image y: thread = (output pixel, 16-channel group), the G = Cp / 16 groups of a
+// pixel on consecutive lanes.  Per tap two 16-byte loads of 16 words, a halfword-pair max
+// (identity -32768: a window with no tap in the image gives it, as the NCHW pool does),
+// then the hi / lo' split and the group's channel sum, the pixel's sum combined over its
+// groups by shuffles and stored once (no atomics).  Channels past C hold x = 0.
+__global__ void __launch_bounds__(256) pool_max_nhwc_planes_kernel(const int16_t* __restrict__ x,
+                                                                   int8_t* __restrict__ yout, int32_t* __restrict__ yS,
+                                                                   PoolPlanesGeo g, uint64_t total, uint32_t g_log,
+                                                                   FastDiv fd_ow, FastDiv fd_oh) {
+    griddep_wait();
+    const uint32_t G = 1u << g_log;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    // whole warps iterate together (the shuffles below need every lane of a pixel's groups)
+    for (uint64_t t0 = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t0 < (total + stride - 1) / stride * stride;
+         t0 += stride) {
+        const bool live_t = t0 < total;
+        const uint64_t t = live_t ? t0 : 0;          // t < 2^32 (checked by the caller)
+        const uint32_t pix = (uint32_t)t >> g_log, grp = (uint32_t)t & (G - 1u);
+        const uint32_t row = fd_ow.div(pix), ow = pix - row * fd_ow.d;
+        const uint32_t n = fd_oh.div(row), oh = row - n * fd_oh.d;
+        const uint32_t c0 = grp * 16u;
+        const int32_t ih0 = (int32_t)(oh * g.sh) - (int32_t)g.pt, iw0 = (int32_t)(ow * g.sw) - (int32_t)g.pl;
+        uint32_t acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = 0x80008000u;
+        const bool real = c0 < g.C;
+        if (live_t && real) {
+            for (uint32_t r = 0; r < g.ph; ++r) {
+                const int32_t ih = ih0 + (int32_t)(r * g.dh);
+                if (ih < 0 || ih >= (int32_t)g.in_h) continue;
+                for (uint32_t q = 0; q < g.pw; ++q) {
+                    const int32_t iw = iw0 + (int32_t)(q * g.dw);
+                    if (iw < 0 || iw >= (int32_t)g.in_w) continue;
+                    const uint4* src = (const uint4*)(x + (((uint64_t)n * g.in_h + (uint32_t)ih) * g.in_w + (uint32_t)iw) * g.C + c0);
+                    const uint4 v0 = __ldg(src), v1 = __ldg(src + 1);
+                    acc[0] = __vmaxs2(acc[0], v0.x); acc[1] = __vmaxs2(acc[1], v0.y);
+                    acc[2] = __vmaxs2(acc[2], v0.z); acc[3] = __vmaxs2(acc[3], v0.w);
+                    acc[4] = __vmaxs2(acc[4], v1.x); acc[5] = __vmaxs2(acc[5], v1.y);
+                    acc[6] = __vmaxs2(acc[6], v1.z); acc[7] = __vmaxs2(acc[7], v1.w);
+                }
+            }
+        }
+        uint32_t hw[4], lw[4];
+        int32_t shi = 0, slo = 0;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t a = real ? acc[2 * k] : 0u, b = real ? acc[2 * k + 1] : 0u;   // x = 0 past C
+            hw[k] = __byte_perm(a, b, 0x7531);
+            lw[k] = __byte_perm(a, b, 0x6420) ^ 0x80808080u;
+            shi = __dp4a((int)hw[k], 0x01010101, shi);
+            slo = __dp4a((int)lw[k], 0x01010101, slo);
+        }
+        // x - 128 = 256*hi + lo' summed over the group's channels; padding channels hold x = 0
+        // and are not part of the sum (their lo' bytes count -128 each: add it back)
+        int32_t sum = 256 * shi + slo + (real ? 0 : 128 * 16);
+        for (uint32_t o = G >> 1; o > 0; o >>= 1) sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
+        if (live_t) {
+            const uint64_t ypix = ((uint64_t)n * g.yHp + oh + g.ypt) * g.yWp + ow + g.ypl;
+            int8_t* dst = yout + ypix * g.Cp + c0;
+            *(uint4*)dst = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *(uint4*)(dst + g.y_plane) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            if (grp == 0) yS[ypix] = sum;
+        }
+    }
+}
+
 // rowterm of output pixel (n, oh, ow) = 128 * sum over its kh x kw taps of S.
 // The channel sums of a conv's OUTPUT plane image cleared (0 inside the image, the frame's
 // value on the frame) by the launch that computes the conv's row terms from its INPUT
@@ -1292,6 +1359,9 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     const Context* cx;
     int rc = enter(&cx);
     if (rc) return rc;
+    // epilogue bit 3: y is channels-last [batch][out_h][out_w][out_ch] (implicit-GEMM paths)
+    const bool nhwc = (epi & 8u) != 0 && y != nullptr;
+    epi &= 7u;
     const uint64_t P = (uint64_t)out_h * out_w;
     if (batch == 0 || out_ch == 0 || P == 0) return CM_OK;
     if ((!y && !po) || (has_bias && !bias)) return set_error(CM_EINVAL, "cm_conv: null buffer");
@@ -1299,6 +1369,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     cudaStream_t s = (cudaStream_t)stream;
     const uint64_t total = (uint64_t)batch * out_ch * P;
 
+    if (nhwc && (is_depthwise || (uint64_t)in_ch * kh * kw == 0))
+        return set_error(CM_EUNSUPPORTED, "cm_conv: channels-last output only on the implicit-GEMM paths");
     if (is_depthwise) {
         if (out_ch > in_ch)
             return set_error(CM_EINVAL, "cm_conv: depthwise needs out_ch <= in_ch (output channel m reads input channel m)");
@@ -1327,6 +1399,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
         return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv bias fill");
     }
     if ((!x && !xv) || !weight) return set_error(CM_EINVAL, "cm_conv: null buffer");
+    if (nhwc && (unsigned __int128)total * K64 <= cx->direct_max_macs)
+        return set_error(CM_EUNSUPPORTED, "cm_conv: channels-last output only on the implicit-GEMM paths");
     if ((unsigned __int128)total * K64 <= cx->direct_max_macs) {
         DwArgs a{in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left,
                  has_bias ? 1u : 0u};
@@ -1434,7 +1508,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 rowterm_launch(cx, S, ip.Hp, ip.Wp, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, nb, rt, s);
             }
             uint32_t bw, bh, bn;
-            pick_tiles(out_h, out_w, stride_h, stride_w, nb, y != nullptr, &bw, &bh, &bn);
+            pick_tiles(out_h, out_w, stride_h, stride_w, nb, y != nullptr && !nhwc, &bw, &bh, &bn);
             ConvA ca{apl, nb, ip.Cp, ip.Hp, ip.Wp, ip.KR, ip.KR_pad, kh, stride_h, stride_w, dilation_h,
                      out_h, out_w, log2u(bw), log2u(bh), log2u(bn)};
             if (xv) {
@@ -1446,7 +1520,8 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 ca.plane_pitch = xv->plane_pitch;
             }
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, ip.Kt, ip.Kt, M_pad, rt, ct,
-                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
+                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, nhwc ? out_ch : 0u, nhwc ? 1u : P,
+                       (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
             p.wa_rows = pw ? pw->rows : nullptr;
@@ -1542,11 +1617,12 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
             }
             uint32_t bw, bh, bn;
-            pick_tiles(out_h, out_w, 1, 1, nb, y != nullptr, &bw, &bh, &bn);
+            pick_tiles(out_h, out_w, 1, 1, nb, y != nullptr && !nhwc, &bw, &bh, &bn);
             const ConvA ca{apl, nb, vp.Cp, vp.Hp, vp.Wp, vp.KR, vp.KR_pad, sp.kh3, 1, 1, sp.T,
                            out_h, out_w, log2u(bw), log2u(bh), log2u(bn)};
             GemmPlan p{nullptr, 0, 1, wpl, out_ch, 1, vp.Kt, vp.Kt, M_pad, rt, ct,
-                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, 0, P, (uint64_t)out_ch * P, 1};
+                       y ? y + n0 * (uint64_t)out_ch * P : nullptr, nhwc ? out_ch : 0u, nhwc ? 1u : P,
+                       (uint64_t)out_ch * P, 1};
             p.conv = &ca;
             p.b_packed = packed ? 1u : 0u;
             p.wa_rows = pw ? pw->rows : nullptr;
@@ -1565,6 +1641,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
     // Explicit im2col: rows = output pixels of a chunk of images (K-major planes),
     // columns = output channels, K in the weight layout's (c, r, s) order.
     const uint32_t M_pad = pad_c(out_ch);
+    if (nhwc) return set_error(CM_EUNSUPPORTED, "cm_conv: channels-last output only on the implicit-GEMM paths");
     const bool packed = out_ch <= 64;
     const uint32_t w_pitch = packed ? 128u : M_pad;
     const uint64_t w_plane = packed ? 64u : (uint64_t)K * M_pad;
@@ -1811,6 +1888,20 @@ extern "C" int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h
     return 1;
 }
 
+extern "C" int cm_conv_writes_nhwc(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                                   unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                                   unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                                   unsigned pad_left, unsigned has_bias, unsigned is_depthwise) {
+    (void)in_h; (void)in_w; (void)pad_top; (void)pad_left; (void)has_bias;
+    const Context* c = ctx();
+    const uint64_t limit = c ? c->direct_max_macs : (1ull << 22);
+    ImplicitPlan ip;
+    if (batch == 0 || out_ch == 0 || (uint64_t)out_h * out_w == 0) return 0;
+    const ConvPath path = conv_path(limit, batch, in_ch, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h,
+                                    dilation_w, is_depthwise, &ip);
+    return path == CP_IMPLICIT || path == CP_S2D ? 1 : 0;
+}
+
 extern "C" int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
                                     int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h,
                                     unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh,
@@ -1818,7 +1909,7 @@ extern "C" int cm_conv_planes_async(const int16_t* x, const cm_planes_t* xp, con
                                     unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
                                     unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
                                     const cm_planes_t* resid_planes, cm_stream_t stream) {
-    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_planes: epilogue must be 0..3");
+    if ((epilogue & ~8u) > 3u) return set_error(CM_EINVAL, "cm_conv_planes: epilogue must be 0..3, plus 8 for channels-last y");
     if ((epilogue & 2u) && !resid && !resid_planes) return set_error(CM_EINVAL, "cm_conv_planes: residual buffer is null");
     if (!y && !yp) return set_error(CM_EINVAL, "cm_conv_planes: neither y nor an output plane image");
     return conv_impl(x, xp, weight, bias, y, yp, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
@@ -1894,6 +1985,49 @@ extern "C" int cm_pool_planes(const cm_planes_t* xp, cm_planes_t* yp, unsigned b
     int rc = cm_pool_planes_async(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
                                   stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad,
                                   nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
+extern "C" int cm_pool_nhwc_planes_async(const int16_t* x, cm_planes_t* yp, unsigned batch, unsigned channels,
+                                         unsigned in_h, unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h,
+                                         unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top,
+                                         unsigned pad_left, unsigned dil_h, unsigned dil_w, unsigned pool_type,
+                                         cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!x || !yp) return set_error(CM_EINVAL, "cm_pool_nhwc_planes: null buffer");
+    if (pool_type != CM_POOL_MAX) return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc_planes: MAX pooling only");
+    if (channels % 16u != 0) return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc_planes: channels must be a multiple of 16");
+    if (yp->device != cx->device) return set_error(CM_EINVAL, "cm_pool_nhwc_planes: plane image of another device");
+    if (yp->n != batch || yp->C != channels || yp->H != out_h || yp->W != out_w)
+        return set_error(CM_EINVAL, "cm_pool_nhwc_planes: the plane image does not match the pool's output");
+    uint32_t g_log = 0;
+    while ((16u << g_log) < yp->Cp) ++g_log;
+    if ((16u << g_log) != yp->Cp || g_log > 5)
+        return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc_planes: %u padded channels (16 x a power of two up to 512)", yp->Cp);
+    const uint64_t total = ((uint64_t)batch * out_h * out_w) << g_log;
+    if (total == 0) return CM_OK;
+    if (total >= (1ull << 32)) return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc_planes: output too large");
+    PoolPlanesGeo g{in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w, pad_top, pad_left, dil_h, dil_w,
+                    channels, yp->Cp, 0, 0, 0, 0, yp->Hp, yp->Wp, yp->pt, yp->pl, 0, yp->plane_pitch};
+    cudaStream_t s = (cudaStream_t)stream;
+    {
+        ProfScope ps_(PK_POOL, s);
+        launch_k(pool_max_nhwc_planes_kernel, grid_for(cx, total, 256, 8), 256, 0, s, x, yp->planes, yp->S, g, total,
+                 g_log, FastDiv(out_w), FastDiv(out_h));
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_pool_nhwc_planes");
+}
+
+extern "C" int cm_pool_nhwc_planes(const int16_t* x, cm_planes_t* yp, unsigned batch, unsigned channels, unsigned in_h,
+                                   unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                                   unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                                   unsigned dil_h, unsigned dil_w, unsigned pool_type) {
+    int rc = cm_pool_nhwc_planes_async(x, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h,
+                                       stride_w, pad_top, pad_left, dil_h, dil_w, pool_type, nullptr);
     return rc ? rc : finish_sync(nullptr);
 }
 
@@ -2004,7 +2138,7 @@ extern "C" int cm_conv_prepared_async(const cm_conv_weights_t* w, const int16_t*
     if (rc) return rc;
     if (!w) return set_error(CM_EINVAL, "cm_conv_prepared: null prepared weights");
     if (w->device != cx->device) return set_error(CM_EINVAL, "cm_conv_prepared: weights prepared on another device");
-    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_prepared: epilogue %u (0..3)", epilogue);
+    if ((epilogue & ~8u) > 3u) return set_error(CM_EINVAL, "cm_conv_prepared: epilogue %u (0..3, plus 8 for channels-last y)", epilogue);
     const unsigned* g = w->g;
     // the planes serve only the path they were built for (the direct-path limit may have
     // changed since); otherwise this call prepares its own from weight and bias

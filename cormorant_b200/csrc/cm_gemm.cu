@@ -833,7 +833,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                 valid = ow < g.out_w && oh < g.out_h && n < g.nimg;
                 const uint64_t pix = (uint64_t)oh * g.out_w + ow;
                 rt_idx = (uint64_t)n * g.out_h * g.out_w + pix;
-                o_off = (uint64_t)n * g.out_bs + pix;
+                o_off = (uint64_t)n * g.out_bs + pix * g.ldo;     // NCHW: ldo 1; channels-last: ldo = cols
             } else {
                 const uint32_t row = tc.m0 + i;
                 valid = row < g.rows;
@@ -1676,7 +1676,7 @@ int gemm_launch_conv(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.batch = 1; g.rows = 0; g.a_batches = 1; g.b_batches = 1;
     g.nimg = c.nimg; g.out_h = c.out_h; g.out_w = c.out_w; g.sw = c.sw; g.sh = c.sh; g.dh = c.dh;
     g.rowterm = p.rowterm; g.colterm = p.colterm;
-    g.out = p.out; g.ldo = 0; g.ldc = p.ldc; g.out_bs = p.out_bs;
+    g.out = p.out; g.ldo = p.ldo ? p.ldo : 1; g.ldc = p.ldc; g.out_bs = p.out_bs;   // ldo: output pixel stride
     g.epi = p.epi; g.resid = p.resid;
     g.po = p.po.planes; g.po_S = p.po.S; g.po_plane = p.po.plane_pitch;
     g.rpl = p.rp.planes; g.rpl_plane = p.rp.plane_pitch;

@@ -57,7 +57,8 @@ struct GemmPlan {
     int16_t* out; uint64_t ldo, ldc, out_bs;     // out[z*out_bs + row*ldo + col*ldc]
     uint32_t batch;
     // Conv implicit GEMM (a_planes, rows, a_batches, K_pad and batch unused):
-    // output pixel (n, oh, ow), channel col -> out[n*out_bs + (oh*out_w + ow) + col*ldc],
+    // output pixel (n, oh, ow), channel col -> out[n*out_bs + (oh*out_w + ow)*ldo + col*ldc]
+    // (ldo 0 means 1: NCHW with ldc = out_h*out_w; channels-last: ldo = cols, ldc = 1),
     // rowterm[n*out_h*out_w + oh*out_w + ow]; K = kh*KR_pad.
     const ConvA* conv = nullptr;
     // B planes packed for one 64-column tile: [b_batches][K][128] int8, each K row

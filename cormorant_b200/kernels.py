@@ -89,6 +89,7 @@ def ConvKernel(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_
 
 
 EPI_NONE, EPI_RELU, EPI_ADD, EPI_ADD_RELU = 0, 1, 2, 3
+EPI_NHWC = 8    # ConvKernelPlanes / ConvKernelPrepared: y channels-last [batch][out_h][out_w][out_ch]
 
 
 def ConvKernelFused(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1,
@@ -142,6 +143,13 @@ def conv_plane_frame(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, str
     return tuple(int(v) for v in fr) if ok else None
 
 
+def conv_writes_nhwc(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h=1, stride_w=1, dilation_h=1,
+                     dilation_w=1, pad_top=0, pad_left=0, has_bias=1, is_depthwise=0) -> bool:
+    """Whether a conv with these arguments can write a channels-last y (EPI_NHWC)."""
+    return bool(lib().cm_conv_writes_nhwc(batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w,
+                                          dilation_h, dilation_w, pad_top, pad_left, int(has_bias), int(is_depthwise)))
+
+
 def PlanesFill(planes, x, stream=None) -> None:
     """Split the NCHW tensor x into plane image `planes` (cm_planes_fill)."""
     L = lib()
@@ -157,6 +165,16 @@ def PoolingKernelPlanes(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_
     args = (_planes(xp), _planes(yp), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
             pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
     check(L.cm_pool_planes(*args) if stream is None else L.cm_pool_planes_async(*args, _stream(stream)))
+
+
+def PoolingKernelNhwcPlanes(x, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
+                            pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, stream=None) -> None:
+    """PoolingKernel (MAX only) from a channels-last tensor x [batch][in_h][in_w][channels]
+    (a conv output written under EPI_NHWC) to plane image yp (cm_pool_nhwc_planes)."""
+    L = lib()
+    args = (_addr(x), _planes(yp), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+            pad_top, pad_left, dil_h, dil_w, pool_type)
+    check(L.cm_pool_nhwc_planes(*args) if stream is None else L.cm_pool_nhwc_planes_async(*args, _stream(stream)))
 
 
 CALL_VECTOROP, CALL_MATMUL, CALL_CONV, CALL_POOL = 0, 1, 2, 3

@@ -22,6 +22,7 @@ from dataclasses import dataclass, field
 import numpy as np
 
 OP_ADD, OP_RELU = 0, 4
+EPI_NHWC = 8          # conv epilogue bit 3: y channels-last (cm_conv_planes)
 
 
 def conv_out(n: int, k: int, s: int, p: int, d: int = 1) -> int:
@@ -217,7 +218,7 @@ def output_of(node) -> str:
     return node[3] if node[0] in ("vectorop", "matmul", "matmul_at") else node[2]   # pool, planes: node[2]
 
 
-def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
+def chain(net: Net, frame_fn=None, pool_planes: bool = False, nhwc_fn=None, pool_nhwc: bool = True) -> Net:
     """The call list with conv outputs that feed implicit-GEMM convs produced as plane
     images (cm_conv_planes): the producing conv's GEMM epilogue writes the consumers'
     channels-last operand, so their split pass disappears, and a residual those convs
@@ -229,13 +230,21 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
     ("conv", x, w, bias, y, args, epilogue, resid, xp, yp, rp) with x / y / resid None
     when unused.  With pool_planes=True a MAX pool between a conv and plane-reading convs
     runs plane image to plane image: ("poolp", xp, yp, args) (off by default: on
-    ResNet-18's stem it measured slower than the NCHW pool plus one split).  A tensor no
-    conv produced (the input, a pool
+    ResNet-18's stem it measured slower than the NCHW pool plus one split).  With
+    pool_nhwc=True (default) a MAX pool that is the only reader of a conv's output, whose
+    own output only plane-reading convs read, and whose channels are a multiple of 16 (and
+    whose conv can write channels-last, `nhwc_fn(args)`, default the library's
+    cm_conv_writes_nhwc): the conv writes its output channels-last (epilogue bit 3) and
+    the pool reads that and writes the plane image, ("poolnp", x, yp, args) -- no NCHW
+    tensor, no split pass (ResNet-18's stem).  A tensor no conv produced (the input, a pool
     output kept NCHW) that convs read at least twice as an operand or residual gets one
     ("planes", x, image) split pass right after its producer."""
     if frame_fn is None:
         from . import kernels
         frame_fn = lambda args: kernels.conv_plane_frame(*args)  # noqa: E731
+    if nhwc_fn is None:
+        from . import kernels
+        nhwc_fn = lambda args: kernels.conv_writes_nhwc(*args)  # noqa: E731
     R = net.resolve
     nodes = [n if n[0] != "conv" or len(n) > 6 else (*n, 0, None) for n in net.nodes]
     reads_planes = {j: frame_fn(n[5]) for j, n in enumerate(nodes) if n[0] == "conv"}
@@ -263,10 +272,25 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
         r_ok = [j for j, role in readers if role == "resid" and reads_planes[j] is not None]
         return x_ok, r_ok
 
+    # MAX pools whose conv writes channels-last for them (the pool its only reader) and
+    # whose output only plane-reading convs read
+    poolnp, nhwc_convs = {}, set()
+    for j, node in enumerate(nodes):
+        if not pool_nhwc or node[0] != "pool" or node[3][14] != 0 or R(node[1]) not in produced:
+            continue
+        t, u = R(node[1]), R(node[2])
+        i = produced[t]
+        if uses.get(t) != [(j, "maxpool")] or node[3][1] % 16 or nodes[i][7] is not None or not nhwc_fn(nodes[i][5]):
+            continue
+        x_ok, r_ok = plane_readers(u)
+        if (x_ok or r_ok) and len(x_ok) + len(r_ok) == len(uses.get(u, [])):
+            poolnp[j] = (x_ok, r_ok)
+            nhwc_convs.add(i)
     # MAX pools that can run plane to plane: conv input, output read only by plane-reading convs
     poolp = {}
     for j, node in enumerate(nodes):
-        if not pool_planes or node[0] != "pool" or node[3][14] != 0 or R(node[1]) not in produced:
+        if (not pool_planes or j in poolnp or node[0] != "pool" or node[3][14] != 0
+                or R(node[1]) not in produced):
             continue
         u = R(node[2])
         x_ok, r_ok = plane_readers(u)
@@ -299,7 +323,13 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
         node = nodes[j]
         t, u, a = R(node[1]), R(node[2]), node[3]
         pool_io[j] = (keep_of[produced[t]][0], image(u, (a[1], a[4], a[5]), x_ok, r_ok, False))
-    others = {R(output_of(n)): j for j, n in enumerate(nodes) if n[0] != "conv" and j not in poolp}
+    pool_nhwc_io = {}
+    for j, (x_ok, r_ok) in poolnp.items():
+        node = nodes[j]
+        u, a = R(node[2]), node[3]
+        pool_nhwc_io[j] = (node[1], image(u, (a[1], a[4], a[5]), x_ok, r_ok, False))
+    others = {R(output_of(n)): j for j, n in enumerate(nodes)
+              if n[0] != "conv" and j not in poolp and j not in poolnp}
     others.setdefault(R(net.input), -1)
     for t, i in others.items():
         x_ok, r_ok = plane_readers(t)
@@ -311,6 +341,9 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
     for i, node in enumerate(nodes):
         if i in pool_io:
             out.append(("poolp", pool_io[i][0], pool_io[i][1], node[3]))
+            continue
+        if i in pool_nhwc_io:
+            out.append(("poolnp", pool_nhwc_io[i][0], pool_nhwc_io[i][1], node[3]))
             continue
         if node[0] != "conv":
             out.append(node)
@@ -327,6 +360,8 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False) -> Net:
         if i in keep_of:
             yp, keep = keep_of[i]
             y = y if keep else None
+        if i in nhwc_convs:
+            epi |= EPI_NHWC                              # y channels-last, read only by its pool
         out.append(("conv", x, wn, bn, y, args, epi, resid, xp, yp, rp))
     names = set(net.buffers) | set(net.aliases)
     used = {R(n) for node in out for n in _inputs(node) if n in names}
@@ -477,6 +512,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "poolp":
             _, xp, yp, args = node
             backend.pool_planes(R(xp), R(yp), *args)
+        elif kind == "poolnp":
+            _, x, yp, args = node
+            backend.pool_nhwc_planes(R(x), R(yp), *args)
         elif kind == "matmul" and len(node) > 5:
             _, a, bb, c, args, epi, bias = node
             backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
@@ -571,6 +609,9 @@ class GpuBackend:
 
     def pool_planes(self, xp, yp, *args):
         self.k.PoolingKernelPlanes(xp, yp, *args, stream=self.stream)
+
+    def pool_nhwc_planes(self, x, yp, *args):
+        self.k.PoolingKernelNhwcPlanes(x, yp, *args[:15], stream=self.stream)
 
 
 def weights_key(w, bias, geo) -> tuple:

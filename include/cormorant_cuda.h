@@ -233,7 +233,10 @@ int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* 
  *                           resid_planes (may be NULL): a plane image of the residual
  *                           (epilogue bit 1) with the output's shape, read instead of
  *                           resid by convs that read plane images (resid may then be
- *                           NULL; others need resid). */
+ *                           NULL; others need resid).  Epilogue bit 3 (value 8): y is
+ *                           channels-last, [batch][out_h][out_w][out_ch] (an NCHW resid
+ *                           is then read in that layout too); implicit-GEMM convs only,
+ *                           others return CM_EUNSUPPORTED. */
 typedef struct cm_planes cm_planes_t;
 cm_planes_t* cm_planes_create(unsigned batch, unsigned channels, unsigned h, unsigned w, unsigned pad_top,
                               unsigned pad_left, unsigned pad_bottom, unsigned pad_right);
@@ -254,10 +257,29 @@ int cm_pool_planes_async(const cm_planes_t* xp, cm_planes_t* yp, unsigned batch,
                          unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top,
                          unsigned pad_left, unsigned dil_h, unsigned dil_w, unsigned pool_type,
                          unsigned lp_order, unsigned count_include_pad, cm_stream_t stream);
+/* PoolingKernel (MAX only) from a channels-last tensor x [batch][in_h][in_w][channels]
+ * (a conv's y under epilogue bit 3; channels a multiple of 16) to plane image yp: the words
+ * of cm_pool on the NCHW tensors, in the form the next convs read.  A conv -> max pool ->
+ * conv chain then writes no NCHW tensor and runs no split pass. */
+int cm_pool_nhwc_planes(const int16_t* x, cm_planes_t* yp, unsigned batch, unsigned channels, unsigned in_h,
+                        unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                        unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left, unsigned dil_h,
+                        unsigned dil_w, unsigned pool_type);
+int cm_pool_nhwc_planes_async(const int16_t* x, cm_planes_t* yp, unsigned batch, unsigned channels,
+                              unsigned in_h, unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h,
+                              unsigned pool_w, unsigned stride_h, unsigned stride_w, unsigned pad_top,
+                              unsigned pad_left, unsigned dil_h, unsigned dil_w, unsigned pool_type,
+                              cm_stream_t stream);
 int cm_conv_plane_frame(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
                         unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
                         unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
                         unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned* frame);
+/* 1 if a conv with these arguments (at the current cm_set_direct_limit) runs on an
+ * implicit-GEMM path and can write a channels-last y (epilogue bit 3), else 0. */
+int cm_conv_writes_nhwc(unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                        unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                        unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                        unsigned pad_left, unsigned has_bias, unsigned is_depthwise);
 int cm_conv_planes(const int16_t* x, const cm_planes_t* xp, const int16_t* weight, const int16_t* bias,
                    int16_t* y, cm_planes_t* yp, unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w,
                    unsigned out_ch, unsigned out_h, unsigned out_w, unsigned kh, unsigned kw,

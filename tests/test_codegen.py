@@ -39,7 +39,7 @@ def _net(name, mode):
 def _nchw_outputs(net):
     outs = set()
     for n in net.nodes:
-        if n[0] in ("planes", "poolp"):
+        if n[0] in ("planes", "poolp", "poolnp"):
             continue
         if n[0] == "conv":
             if n[4] is not None:
@@ -185,16 +185,21 @@ def test_generated_project_reports_missing_weights_and_mismatch(tmp_path, port):
 
 
 def test_chained_project_uses_plane_images(tmp_path):
+    """The stem writes channels-last for the max pool, which writes the layer-1 convs'
+    plane image (cm_pool_nhwc_planes_async): no split pass remains."""
     net = _net("resnet18_b2", "planes")
     codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
     src = (tmp_path / "src/inference.c").read_text()
     assert src.count("cm_planes_create(") == len(net.planes) == src.count("cm_planes_destroy(")
-    assert src.count("cm_conv_planes_async(") == 20 and src.count("cm_planes_fill_async(") == 1
+    assert src.count("cm_conv_planes_async(") == 20 and src.count("cm_planes_fill_async(") == 0
+    assert src.count("cm_pool_nhwc_planes_async(") == 1
+    if LIB.exists():
+        codegen.compile_project(tmp_path, INCLUDE, LIB)
 
 
 @pytest.mark.skipif(not LIB.exists(), reason="libcormorant_cuda.so not built")
 def test_plane_pool_project_compiles(tmp_path):
-    net = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True)
+    net = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True, pool_nhwc=False)
     codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16))
     assert (tmp_path / "src/inference.c").read_text().count("cm_pool_planes_async(") == 1
     codegen.compile_project(tmp_path, INCLUDE, LIB)

@@ -251,3 +251,76 @@ def test_max_pool_plane_to_plane(cm, port, N, H, W, k, s, p, d):
     Y = kernels.PlaneImage(N, C, oh, ow)
     kernels.PoolingKernelPlanes(X, Y, *pa)
     assert_same(_identity_readback(kernels, Y, N, C, oh, ow), want, f"max pool planes {pa}")
+
+
+def _nchw_to_nhwc(t, n, c, h, w):
+    return np.ascontiguousarray(np.asarray(t)[: n * c * h * w].reshape(n, c, h, w).transpose(0, 2, 3, 1)).reshape(-1)
+
+
+@pytest.mark.parametrize("N,C,H,W,k,s,p,d,frame", [(4, 64, 112, 112, 3, 2, 1, 1, (1, 1, 1, 1)),
+                                                   (3, 32, 30, 26, 3, 2, 1, 2, (0, 0, 0, 0)),
+                                                   (2, 128, 20, 20, 2, 2, 1, 1, (1, 1, 1, 1)),
+                                                   (5, 64, 9, 13, 3, 1, 1, 1, (2, 1, 0, 3)),
+                                                   (40, 64, 4, 4, 5, 3, 2, 1, (0, 0, 0, 0))])
+def test_max_pool_nhwc_to_planes(cm, port, N, C, H, W, k, s, p, d, frame):
+    """cm_pool_nhwc_planes: the MAX pool of a channels-last tensor written as a plane image
+    (hi / lo' planes and channel sums, inside a frame) equals cm_pool's MAX on the NCHW
+    tensor, windows with no tap in the image included; read back through an identity 1x1
+    conv, whose row terms come from the image's channel sums."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(N * 31 + C + H + k)
+    x = rand16(rng, N * C * H * W)
+    oh, ow = (H + 2 * p - d * (k - 1) - 1) // s + 1, (W + 2 * p - d * (k - 1) - 1) // s + 1
+    pa = (N, C, H, W, oh, ow, k, k, s, s, p, p, d, d, 0, 2, 0)
+    want = port.pool(x, *pa)[: N * C * oh * ow]
+    Y = kernels.PlaneImage(N, C, oh, ow, frame)
+    kernels.PoolingKernelNhwcPlanes(dev(_nchw_to_nhwc(x, N, C, H, W)), Y, *pa[:15])
+    assert_same(_identity_readback(kernels, Y, N, C, oh, ow), want, f"max pool nhwc -> planes {pa} frame {frame}")
+
+
+def test_max_pool_nhwc_to_planes_refusals(cm):
+    """Channel counts other than 16 x a power of two, and pool types other than MAX, are refused."""
+    from cormorant_b200 import kernels
+    Y = kernels.PlaneImage(2, 48, 4, 4)
+    with pytest.raises(cm.CormorantError):
+        kernels.PoolingKernelNhwcPlanes(dev(np.zeros(2 * 8 * 8 * 48, np.int16)), Y, 2, 48, 8, 8, 4, 4, 2, 2, 2, 2)
+    Y2 = kernels.PlaneImage(2, 64, 4, 4)
+    with pytest.raises(cm.CormorantError):
+        kernels.PoolingKernelNhwcPlanes(dev(np.zeros(2 * 8 * 8 * 64, np.int16)), Y2, 2, 64, 8, 8, 4, 4, 2, 2, 2, 2,
+                                        pool_type=kernels.POOL_AVG)
+
+
+@pytest.mark.parametrize("g,epi", [(geo(2, 3, 64, 64, 64, 7, 2, 3), 1),       # space-to-depth stem form
+                                   (geo(3, 64, 14, 14, 64, 3, 1, 1), 0),      # 64-column window form
+                                   (geo(3, 64, 14, 14, 64, 3, 1, 1), 1),
+                                   (geo(2, 64, 14, 14, 128, 3, 1, 1), 1)])    # 128-column tiles on CTA pairs
+def test_conv_channels_last_output(cm, port, g, epi):
+    """Epilogue bit 3 (EPI_NHWC): y is the same words as the NCHW output, channels-last."""
+    from cormorant_b200 import kernels
+    import torch
+    rng = np.random.default_rng(sum(g) + epi)
+    x = rand16(rng, g[0] * g[1] * g[2] * g[3])
+    w, b = weights(rng, g)
+    assert kernels.conv_writes_nhwc(*g)
+    want = _nchw_to_nhwc(oracle(port, x, w, b, g, epi), g[0], g[4], g[5], g[6])
+    y = empty(g[0] * g[4] * g[5] * g[6])
+    kernels.ConvKernelPlanes(dev(x), None, dev(w), dev(b), y, None, *g, epilogue=epi | kernels.EPI_NHWC)
+    torch.cuda.synchronize()
+    assert_same(host(y), want, f"channels-last conv {g} epi {epi}")
+
+
+def test_conv_channels_last_refused_off_gemm_paths(cm, port):
+    """A conv on a CUDA-core path cannot write channels-last: CM_EUNSUPPORTED."""
+    from cormorant_b200 import _lib, kernels
+    g = geo(1, 4, 6, 6, 8, 3, 1, 1)
+    L = _lib.lib()
+    old = L.cm_set_direct_limit(1 << 26)                  # the direct path for this size
+    try:
+        assert not kernels.conv_writes_nhwc(*g)
+        rng = np.random.default_rng(3)
+        x = rand16(rng, 4 * 36)
+        w, b = weights(rng, g)
+        with pytest.raises(cm.CormorantError):
+            kernels.ConvKernelPlanes(dev(x), None, dev(w), dev(b), empty(8 * 36), None, *g, epilogue=kernels.EPI_NHWC)
+    finally:
+        L.cm_set_direct_limit(old)

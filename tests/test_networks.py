@@ -53,13 +53,14 @@ class OracleBackend:
         y[:] = t
 
     def conv_planes(self, x, xp, w, bias, y, yp, *args):
-        """A plane image on the checker is the NCHW tensor itself."""
+        """A plane image on the checker is the NCHW tensor itself; epilogue bit 3 writes y
+        channels-last ([batch][out_h][out_w][out_ch])."""
         *geo, epi, resid, rp = args
         src = x if x is not None else xp
         out = np.zeros(geo[0] * geo[4] * geo[5] * geo[6], np.int16)
-        self.conv_fused(src, w, bias, out, *geo, epi, resid if resid is not None else rp)
+        self.conv_fused(src, w, bias, out, *geo, epi & 3, resid if resid is not None else rp)
         if y is not None:
-            y[:] = out
+            y[:] = nchw_to_nhwc(out, geo[0], geo[4], geo[5], geo[6]) if epi & networks.EPI_NHWC else out
         if yp is not None:
             yp[:] = out
 
@@ -71,6 +72,19 @@ class OracleBackend:
 
     def pool_planes(self, xp, yp, *args):
         self.pool(xp, yp, *args)
+
+    def pool_nhwc_planes(self, x, yp, *args):
+        """MAX pool of a channels-last tensor into a plane image (= its NCHW tensor here)."""
+        n, c, h, w = args[:4]
+        self.pool(nhwc_to_nchw(x, n, c, h, w), yp, *args)
+
+
+def nchw_to_nhwc(t, n, c, h, w):
+    return np.ascontiguousarray(np.asarray(t)[: n * c * h * w].reshape(n, c, h, w).transpose(0, 2, 3, 1)).reshape(-1)
+
+
+def nhwc_to_nchw(t, n, c, h, w):
+    return np.ascontiguousarray(np.asarray(t)[: n * c * h * w].reshape(n, h, w, c).transpose(0, 3, 1, 2)).reshape(-1)
 
 
 def cpu_buffers(net, x):
@@ -210,19 +224,26 @@ def test_resnet18_fused_batch256_sampled_images(cm, port):
 
 def test_chain_pass_resnet_structure():
     """Conv outputs read by implicit-GEMM convs become plane images; NCHW outputs stay only
-    where a residual, a pool or the network output reads them."""
+    where a residual, a pool or the network output reads them.  The stem writes its output
+    channels-last for the max pool, which writes the layer-1 convs' plane image."""
     net = networks.chain(networks.fuse(networks.resnet18(batch=2)))
     convs = [n for n in net.nodes if n[0] == "conv"]
     assert len(convs) == 20 and len(net.planes) == 19
-    assert [n[1] for n in net.nodes if n[0] == "planes"] == ["pool5"]   # the max pool's output, split once
+    assert [n[0] for n in net.nodes[:2]] == ["conv", "poolnp"]
+    assert convs[0][6] == 1 | networks.EPI_NHWC and net.nodes[1][1:3] == ("relu4", "pool5@planes")
+    assert not [n for n in net.nodes if n[0] == "planes"]       # no split pass left
     assert sum(1 for n in convs if n[8] is not None) == 19      # every conv but the stem
-    assert sum(1 for n in convs if n[1] is None) == 18          # inputs read only from plane images
+    assert sum(1 for n in convs if n[1] is None) == 19          # inputs read only from plane images
     assert sum(1 for n in convs if n[4] is None) == 18          # outputs written only as plane images
     assert sum(1 for n in convs if n[10] is not None) == 8      # residuals read from plane images
+    assert sum(1 for n in convs if n[7] is not None) == 0       # no residual read as NCHW
     assert all(n[8] is not None for n in convs if n[1] is None)
     assert all(n[9] is not None for n in convs if n[4] is None)
-    assert set(net.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}   # NCHW tensors left
-    pp = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True)
+    assert set(net.buffers) == {"x", "relu4", "relu86", "pool87", "gemm92"}   # relu4 is channels-last
+    old = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_nhwc=False)
+    assert [n[1] for n in old.nodes if n[0] == "planes"] == ["pool5"]   # the max pool's output, split once
+    assert set(old.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}
+    pp = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_planes=True, pool_nhwc=False)
     assert [n[0] for n in pp.nodes[:2]] == ["conv", "poolp"] and len(pp.planes) == 20
     assert set(pp.buffers) == {"x", "relu86", "pool87", "gemm92"}
     for name, (b, c, h, w, frame) in net.planes.items():
@@ -234,7 +255,9 @@ def test_chained_call_list_equals_reference_sequence_on_cpu(port):
     """The plane-chained ResNet call list, replayed on the checker (a plane image = its
     NCHW tensor), gives the unchained list's logits."""
     net = networks.resnet18(batch=1)
-    fn = networks.chain(networks.fuse(net), frame_fn=lambda a: (1, 1, 1, 1) if a[7] > 1 and a[9] == 1 else None)
+    fn = networks.chain(networks.fuse(net), frame_fn=lambda a: (1, 1, 1, 1) if a[7] > 1 and a[9] == 1 else None,
+                        nhwc_fn=lambda a: a[7] == 7)
+    assert [n[0] for n in fn.nodes[:2]] == ["conv", "poolnp"]
     x = networks.make_input(net)
     a, b = cpu_buffers(net, x), cpu_buffers(fn, x)
     networks.execute(net, OracleBackend(port), a)
@@ -248,8 +271,9 @@ def test_resnet18_chained_batch4_every_output(cm, port, pool_planes, prepared):
     """Plane images on the GPU: every NCHW tensor the chained list still writes, and the
     logits, equal the oracle's (also with the conv weights prepared once)."""
     import torch
-    net = networks.chain(networks.fuse(networks.resnet18(batch=4)), pool_planes=pool_planes)
+    net = networks.chain(networks.fuse(networks.resnet18(batch=4)), pool_planes=pool_planes, pool_nhwc=not pool_planes)
     assert net.planes
+    assert [n[0] for n in net.nodes[:2]] == ["conv", "poolp" if pool_planes else "poolnp"]
     x = networks.make_input(net)
     want = cpu_buffers(net, x)
     networks.execute(net, OracleBackend(port), want)
