@@ -492,7 +492,32 @@ __global__ void __launch_bounds__(256) pool_max_nhwc_planes_kernel(const int16_t
 #pragma unroll
         for (int k = 0; k < 8; ++k) acc[k] = 0x80008000u;
         const bool real = c0 < g.C;
-        if (live_t && real) {
+        if (live_t && real && g.ph == 3 && g.pw == 3) {
+            // 3 x 3 windows (ResNet's stem pool): the taps' loads issued together, then the max
+            uint4 v[9][2];
+#pragma unroll
+            for (uint32_t r = 0; r < 3; ++r) {
+                const int32_t ih = ih0 + (int32_t)(r * g.dh);
+                const bool rin = ih >= 0 && ih < (int32_t)g.in_h;
+#pragma unroll
+                for (uint32_t q = 0; q < 3; ++q) {
+                    const int32_t iw = iw0 + (int32_t)(q * g.dw);
+                    v[3 * r + q][0] = v[3 * r + q][1] = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
+                    if (rin && iw >= 0 && iw < (int32_t)g.in_w) {
+                        const uint4* src = (const uint4*)(x + (((uint64_t)n * g.in_h + (uint32_t)ih) * g.in_w + (uint32_t)iw) * g.C + c0);
+                        v[3 * r + q][0] = __ldg(src);
+                        v[3 * r + q][1] = __ldg(src + 1);
+                    }
+                }
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < 9; ++k) {
+                acc[0] = __vmaxs2(acc[0], v[k][0].x); acc[1] = __vmaxs2(acc[1], v[k][0].y);
+                acc[2] = __vmaxs2(acc[2], v[k][0].z); acc[3] = __vmaxs2(acc[3], v[k][0].w);
+                acc[4] = __vmaxs2(acc[4], v[k][1].x); acc[5] = __vmaxs2(acc[5], v[k][1].y);
+                acc[6] = __vmaxs2(acc[6], v[k][1].z); acc[7] = __vmaxs2(acc[7], v[k][1].w);
+            }
+        } else if (live_t && real) {
             for (uint32_t r = 0; r < g.ph; ++r) {
                 const int32_t ih = ih0 + (int32_t)(r * g.dh);
                 if (ih < 0 || ih >= (int32_t)g.in_h) continue;
@@ -569,8 +594,20 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
         const uint32_t oh = (uint32_t)(p / out_w), ow = (uint32_t)(p - (uint64_t)oh * out_w);
         const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp + (uint64_t)ow * sw;
         uint32_t sum = 0;
-        for (uint32_t r = 0; r < kh; ++r)
-            for (uint32_t s = 0; s < kw; ++s) sum += (uint32_t)__ldg(b + (uint64_t)r * dh * Wp + s);
+        if (kh <= 3 && kw <= 3) {
+            // up to 3 x 3 taps: the loads issued together, then summed
+            uint32_t v[9];
+#pragma unroll
+            for (uint32_t r = 0; r < 3; ++r)
+#pragma unroll
+                for (uint32_t q = 0; q < 3; ++q)
+                    v[3 * r + q] = r < kh && q < kw ? (uint32_t)__ldg(b + (uint64_t)r * dh * Wp + q) : 0u;
+#pragma unroll
+            for (uint32_t k = 0; k < 9; ++k) sum += v[k];
+        } else {
+            for (uint32_t r = 0; r < kh; ++r)
+                for (uint32_t q = 0; q < kw; ++q) sum += (uint32_t)__ldg(b + (uint64_t)r * dh * Wp + q);
+        }
         rowterm[t] = (int32_t)(sum * 128u);
     }
 }
@@ -1115,16 +1152,40 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
     const int16_t* xn = x + (uint64_t)n * C_ * g.H * W;
     const bool quads = (W & 7u) == 0 && (((uintptr_t)x) & 15u) == 0;
     const bool pairs = (W & 1u) == 0 && (((uintptr_t)x) & 3u) == 0;
-    for (uint32_t r = 0; r < RPC * (uint32_t)C_; ++r) {
+    if (quads) {
+        // every 16-byte piece of every staged row is one item: each thread issues up to
+        // kBatch loads before its first shared-memory store, so the block's rows arrive in
+        // one memory round trip instead of one per row
+        constexpr uint32_t kBatch = 8;
+        const uint32_t per_row = W / 8, items = RPC * (uint32_t)C_ * per_row;
+        for (uint32_t base = 0; base < items; base += kBatch * blockDim.x) {
+            uint4 v[kBatch];
+#pragma unroll
+            for (uint32_t k = 0; k < kBatch; ++k) {
+                const uint32_t idx = base + k * blockDim.x + threadIdx.x;
+                v[k] = make_uint4(0, 0, 0, 0);
+                if (idx < items) {
+                    const uint32_t r = idx / per_row, i = idx - r * per_row;
+                    const uint32_t lr = r / C_, c = r % C_;
+                    const int32_t ih = (int32_t)(S_ * hv0 + lr) - (int32_t)g.pt;
+                    if (ih >= 0 && ih < (int32_t)g.H)
+                        v[k] = __ldg((const uint4*)(xn + ((uint64_t)c * g.H + (uint32_t)ih) * W) + i);
+                }
+            }
+#pragma unroll
+            for (uint32_t k = 0; k < kBatch; ++k) {
+                const uint32_t idx = base + k * blockDim.x + threadIdx.x;
+                if (idx < items) ((uint4*)rowbuf)[idx] = v[k];
+            }
+        }
+    }
+    for (uint32_t r = 0; !quads && r < RPC * (uint32_t)C_; ++r) {
         const uint32_t lr = r / C_, c = r % C_;            // local row lr: input row S_*hv0 + lr - pt
         const int32_t ih = (int32_t)(S_ * hv0 + lr) - (int32_t)g.pt;
         int16_t* dst = rowbuf + r * W;
         if (ih >= 0 && ih < (int32_t)g.H) {
             const int16_t* src = xn + ((uint64_t)c * g.H + (uint32_t)ih) * W;
-            if (quads) {
-                for (uint32_t i = threadIdx.x; i < W / 8; i += blockDim.x)
-                    ((uint4*)dst)[i] = __ldg((const uint4*)src + i);
-            } else if (pairs) {
+            if (pairs) {
                 for (uint32_t i = threadIdx.x; i < W / 2; i += blockDim.x)
                     ((uint32_t*)dst)[i] = __ldg((const uint32_t*)src + i);
             } else {
