@@ -1136,17 +1136,31 @@ constexpr uint32_t kS2dRowSmem = 32u * 1024u;
 // input rows per channel a band of rb virtual rows stages
 __host__ __device__ constexpr uint32_t s2d_band_rows(uint32_t s, uint32_t t, uint32_t rb) { return (rb - 1) * s + t * s; }
 
+// Row terms of the original conv computed by the split itself (S2dRt::rt != null, KH_ > 0:
+// the original kernel height; stride S_, dilation 1): output row oh = hv of the band reads
+// padded rows S_*oh .. S_*oh + KH_ - 1, so the band stages S_*(RB_ - 1) + KH_ rows when that
+// is more than the split needs, and So is not written.
+struct S2dRt {
+    int32_t* rt;                   // [nimg][out_h][out_w], as rowterm_launch writes it
+    uint32_t out_h, out_w, kw;
+};
+
+__host__ __device__ constexpr uint32_t s2d_stage_rows(uint32_t s, uint32_t t, uint32_t rb, uint32_t kh) {
+    return s2d_band_rows(s, t, rb) > (rb - 1) * s + kh ? s2d_band_rows(s, t, rb) : (rb - 1) * s + kh;
+}
+
 // T_ = 2: a virtual pixel also carries virtual row hv + 1 and writes its channels after
 // those of row hv (row stacking); So is written for row hv only.
-template <int S_, int C_, int T_ = 1, int RB_ = 1>
+template <int S_, int C_, int T_ = 1, int RB_ = 1, int KH_ = 0>
 __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int16_t* __restrict__ x, S2dGeom g,
                                                                         int8_t* __restrict__ planes,
-                                                                        int32_t* __restrict__ So) {
+                                                                        int32_t* __restrict__ So, S2dRt rtp) {
     griddep_wait();
     static_assert(S_ >= 2 && T_ * S_ * S_ * C_ <= 64, "space-to-depth channels");
     constexpr uint32_t C2 = (uint32_t)(S_ * S_ * C_), CPC = (T_ * C2 + 15u) / 16u * 16u;
-    constexpr uint32_t RPC = s2d_band_rows(S_, T_, RB_);      // staged input rows per channel
-    extern __shared__ __align__(16) int16_t rowbuf[];      // [RPC][C_][W]
+    constexpr uint32_t RPC = s2d_stage_rows(S_, T_, RB_, KH_);   // staged input rows per channel
+    const bool fused_rt = KH_ > 0 && rtp.rt != nullptr;
+    extern __shared__ __align__(16) int16_t rowbuf[];      // [RPC][C_][W], then (fused_rt) [RB_][Wpo] int32
     const uint32_t hv0 = blockIdx.x * RB_, n = blockIdx.y;
     const uint32_t W = g.W;
     const int16_t* xn = x + (uint64_t)n * C_ * g.H * W;
@@ -1224,7 +1238,7 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
                 }
                 sums[tw] = sum;
             }
-            if (th < (uint32_t)S_) {
+            if (th < (uint32_t)S_ && !fused_rt) {
                 int32_t* so = So + ((uint64_t)n * g.Hpo + S_ * hv + th) * g.Wpo + S_ * wv;
                 if constexpr (S_ == 2) {
                     *(int2*)so = make_int2(sums[0], sums[1]);
@@ -1240,6 +1254,36 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
             const uint32_t q = c0 / 4;
             *(uint4*)(dst + c0) = make_uint4(hw[q], hw[q + 1], hw[q + 2], hw[q + 3]);
             *(uint4*)(dst + plane + c0) = make_uint4(lw[q], lw[q + 1], lw[q + 2], lw[q + 3]);
+        }
+    }
+    if constexpr (KH_ > 0) {
+        if (fused_rt) {
+            // V[i][col] = sum over kernel rows r and channels c of (x - 128) at padded row
+            // S_*(hv0 + i) + r, padded column col (x = 0 outside the image); then
+            // rt = 128 * sum over q < kw of V[i][S_*ow + q] -- the box sums of So
+            int32_t* V = (int32_t*)(((uintptr_t)(rowbuf + RPC * (uint32_t)C_ * W) + 15u) & ~(uintptr_t)15u);
+            const uint32_t Wpo = g.Wpo;
+            for (uint32_t item = threadIdx.x; item < (uint32_t)RB_ * Wpo; item += blockDim.x) {
+                const uint32_t i = item / Wpo, col = item - i * Wpo;
+                const int32_t iw = (int32_t)col - (int32_t)g.pl;
+                int32_t v = -128 * KH_ * C_;
+                if (iw >= 0 && iw < (int32_t)W) {
+#pragma unroll
+                    for (uint32_t r = 0; r < (uint32_t)KH_; ++r)
+#pragma unroll
+                        for (uint32_t c = 0; c < (uint32_t)C_; ++c) v += rowbuf[((S_ * i + r) * C_ + c) * W + (uint32_t)iw];
+                }
+                V[item] = v;
+            }
+            __syncthreads();
+            const uint32_t rows_out = hv0 < rtp.out_h ? min((uint32_t)RB_, rtp.out_h - hv0) : 0u;
+            for (uint32_t item = threadIdx.x; item < rows_out * rtp.out_w; item += blockDim.x) {
+                const uint32_t i = item / rtp.out_w, ow = item - i * rtp.out_w;
+                const int32_t* vr = V + i * Wpo + S_ * ow;
+                uint32_t sum = 0;
+                for (uint32_t q = 0; q < rtp.kw; ++q) sum += (uint32_t)vr[q];
+                rtp.rt[((uint64_t)n * rtp.out_h + hv0 + i) * rtp.out_w + ow] = (int32_t)(sum * 128u);
+            }
         }
     }
 }
@@ -1643,29 +1687,42 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                 ProfScope ps_(PK_SPLIT, s);
                 const int16_t* xc = x + n0 * (uint64_t)in_ch * in_h * in_w;
                 const uint64_t row_smem = (uint64_t)sp.T * sp.s * in_ch * in_w * 2;
+                bool rt_done = false;
                 if (sp.T == 2) {
                     // bands of 4 virtual rows when their input rows fit, else 2, else 1
                     const uint64_t row_bytes = (uint64_t)in_ch * in_w * 2;
                     const uint32_t rb = s2d_band_rows(2, 2, 4) * row_bytes <= kS2dRowSmem ? 4u
                                         : s2d_band_rows(2, 2, 2) * row_bytes <= kS2dRowSmem ? 2u : 1u;
-                    const size_t band_smem = (size_t)(s2d_band_rows(2, 2, rb) * row_bytes);
+                    // the 7 x 7 stride-2 stem: the band also computes its output rows' row terms
+                    // (13 staged rows instead of 10, no So, no row-term launch)
+                    const uint64_t fused_smem = s2d_stage_rows(2, 2, 4, 7) * row_bytes + 16 + 4ull * 4 * sp.Wpo;
+                    const bool fuse_rt = rb == 4 && kh == 7 && kw <= 16 && dilation_h == 1 && dilation_w == 1 &&
+                                         fused_smem <= kS2dRowSmem;
+                    const size_t band_smem = fuse_rt ? (size_t)fused_smem : (size_t)(s2d_band_rows(2, 2, rb) * row_bytes);
                     const uint32_t gx = (vp.Hp + rb - 1) / rb;
                     for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                         const uint32_t bz = std::min(65535u, nb - b0);
                         const int16_t* xb = xc + (uint64_t)b0 * in_ch * in_h * in_w;
                         int8_t* pb = apl + (uint64_t)b0 * img_plane;
                         int32_t* sb = So + (uint64_t)b0 * img_so;
-                        if (rb == 4) launch_k(conv_s2d_rows_kernel<2, 3, 2, 4>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
-                        else if (rb == 2) launch_k(conv_s2d_rows_kernel<2, 3, 2, 2>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
-                        else launch_k(conv_s2d_rows_kernel<2, 3, 2, 1>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb);
+                        const S2dRt none{nullptr, 0, 0, 0};
+                        if (fuse_rt) {
+                            const S2dRt fr{rt + (uint64_t)b0 * P, out_h, out_w, kw};
+                            launch_k(conv_s2d_rows_kernel<2, 3, 2, 4, 7>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb, fr);
+                        }
+                        else if (rb == 4) launch_k(conv_s2d_rows_kernel<2, 3, 2, 4>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb, none);
+                        else if (rb == 2) launch_k(conv_s2d_rows_kernel<2, 3, 2, 2>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb, none);
+                        else launch_k(conv_s2d_rows_kernel<2, 3, 2, 1>, dim3(gx, bz), kS2dRowThreads, band_smem, s, xb, sg, pb, sb, none);
                         count_launch();
                     }
+                    rt_done = fuse_rt;
                 } else if (sp.s == 2 && in_ch == 3 && row_smem <= kS2dRowSmem && vp.Hp < (1u << 31)) {
                     for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
                         const uint32_t bz = std::min(65535u, nb - b0);
                         // images b0..: shift the input, planes and So bases; the plane stride stays the chunk's
                         launch_k(conv_s2d_rows_kernel<2, 3>, dim3(vp.Hp, bz), kS2dRowThreads, (size_t)row_smem, s, 
-                            xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so);
+                            xc + (uint64_t)b0 * in_ch * in_h * in_w, sg, apl + (uint64_t)b0 * img_plane, So + (uint64_t)b0 * img_so,
+                            S2dRt{nullptr, 0, 0, 0});
                         count_launch();
                     }
                 } else if (sp.s == 2 && in_ch == 3) {
@@ -1675,7 +1732,7 @@ int conv_core(const int16_t* x, const cm_planes* xv, const int16_t* weight, cons
                     launch_k(conv_s2d_split_kernel<0, 0>, grid_for(cx, vtot, 256, 8), 256, 0, s, xc, sg, vtot, apl, So);
                     count_launch();
                 }
-                rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
+                if (!rt_done) rowterm_launch(cx, So, sp.Hpo, sp.Wpo, out_h, out_w, kh, kw, sp.s, sp.s, 1, nb, rt, s);
             }
             uint32_t bw, bh, bn;
             pick_tiles(out_h, out_w, 1, 1, nb, y != nullptr && !nhwc, &bw, &bh, &bn);
