@@ -720,7 +720,69 @@ class NetworkBench:
             ms, cnt = C.c_double(), C.c_uint64()
             L.cm_profile_read(kind.encode(), C.byref(ms), C.byref(cnt))
             out[kind + "_ms"] = round(ms.value / iters, 4)
+        if self.which != "lenet":
+            try:
+                out["layers"] = self.per_layer(stream)
+            except Exception as e:          # a breakdown, never a reason to lose the record
+                out["layers"] = {"error": f"{type(e).__name__}: {e}"}
         return [out]
+
+    def per_layer(self, stream, passes: int = 3):
+        """Per-call roofline: CUDA events around every call of the
+        call list in eager passes (median over `passes`); conv / MatMul calls against the int8
+        pipe's ceiling at the timed region's clock (`self.roof_peak`, int8 TOPS), pools and
+        VectorOP against the measured HBM copy rate (`self.hbm_gbs`)."""
+        import torch
+        from cormorant_b200 import networks
+        be = self._backend(stream)
+        calls = []
+        for name in ("conv", "conv_fused", "conv_planes", "matmul", "matmul_fused", "pool", "pool_planes",
+                     "pool_nhwc_planes", "planes_fill", "vectorop"):
+            if not hasattr(be, name):
+                continue
+
+            def wrap(*a, _o=getattr(be, name), _n=name, **k):
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                _o(*a, **k)
+                e1.record(stream)
+                calls.append((_n, a, e0, e1))
+            setattr(be, name, wrap)
+        times = []
+        for _ in range(passes):
+            calls.clear()
+            networks.execute(self.net, be, self.bufs)
+            torch.cuda.synchronize()
+            times.append([c[2].elapsed_time(c[3]) for c in calls])
+        rows = []
+        for i, (name, a, _, _) in enumerate(calls):
+            ms = sorted(t[i] for t in times)[len(times) // 2]
+            rec = {"call": i, "kind": name, "us": round(ms * 1e3, 1)}
+            if name.startswith("conv"):
+                geo = a[6:23] if name == "conv_planes" else a[4:21]
+                b, ci, _, _, co, oh, ow, kh, kw = geo[:9]
+                dw = geo[16]
+                macs = b * co * oh * ow * kh * kw * (1 if dw else ci)
+                rec["shape"] = f"{kh}x{kw}/{geo[9]} {ci}->{co} {oh}x{ow}"
+                rec["int8_tops"] = round(8.0 * macs / (ms * 1e-3) / 1e12, 1)
+                if getattr(self, "roof_peak", None):
+                    rec["frac"] = round(rec["int8_tops"] / self.roof_peak, 3)
+            elif name.startswith("matmul"):
+                n, k, m, bt = a[3:7]
+                rec["shape"] = f"{n}x{k}x{m} b{bt}"
+                rec["int8_tops"] = round(8.0 * n * k * m * bt / (ms * 1e-3) / 1e12, 1)
+                if getattr(self, "roof_peak", None):
+                    rec["frac"] = round(rec["int8_tops"] / self.roof_peak, 3)
+            elif name.startswith("pool"):
+                args = a[2:]
+                b, c, ih, iw, oh, ow = args[:6]
+                nbytes = 2 * b * c * (ih * iw + oh * ow)
+                rec["shape"] = f"{args[6]}x{args[7]}/{args[8]} {c}ch {ih}x{iw}->{oh}x{ow}"
+                rec["gbs"] = round(nbytes / (ms * 1e-3) / 1e9, 1)
+                if getattr(self, "hbm_gbs", None):
+                    rec["frac"] = round(rec["gbs"] / self.hbm_gbs, 3)
+            rows.append(rec)
+        return rows
 
     def release(self):
         self.bufs = None
@@ -1250,6 +1312,8 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
                 "note": f"algorithmic bytes / kernel CUDA-event time on rank 0; peak = {peaks['source']} HBM copy rate"}
 
     gather = measure_gathers(wl, env, ms_per_step, scale, K) if world > 1 else None
+    wl.roof_peak = roof.get("peak") if roof.get("unit") == "TFLOP/s" else None
+    wl.hbm_gbs = peaks["hbm_gbs"]
     per_part = wl.per_part(cm, stream, max(2, min(K, 5))) if (detail and rank == 0) else None
     wl.release()
     torch.cuda.empty_cache()
