@@ -398,7 +398,26 @@ def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
         return (whole(node, net.buffers[y]) and node[4][1] == OP_ADD and node[2] is not None
                 and y in (R(node[1]), R(node[2])) and R(node[1]) != R(node[2]))
 
-    out, nodes, i = [], net.nodes, 0
+    nodes = list(net.nodes)
+    if residual:
+        # Conv D; Conv C; Add(C's output, D's output): the Add is folded into the conv that
+        # runs right before it.  When D has the longer reduction (a 3x3 conv against ResNet's
+        # 1x1 projection shortcut) and neither reads the other's output, C runs first, so the
+        # residual read sits in the epilogue of the conv whose mainloop hides it.  ADD is
+        # symmetric (sat16(a + b)): the words do not change.
+        for i in range(1, len(nodes) - 1):
+            d, c, nxt = nodes[i - 1], nodes[i], nodes[i + 1]
+            if not (d[0] == "conv" and c[0] == "conv" and len(d) == 6 and len(c) == 6):
+                continue
+            yd, yc = R(d[4]), R(c[4])
+            if not (add_with(nxt, yc) and add_with(nxt, yd) and reads.get(yd, 0) == 1 and reads.get(yc, 0) == 1):
+                continue
+            if yd in {R(n) for n in _inputs(c)} or yc in {R(n) for n in _inputs(d)}:
+                continue
+            red = lambda a: a[7] * a[8] * (1 if a[16] else a[1])     # noqa: E731  taps x channels per output
+            if red(d[5]) > red(c[5]):
+                nodes[i - 1], nodes[i] = c, d
+    out, i = [], 0
     while i < len(nodes):
         node = nodes[i]
         if node[0] == "conv" and len(node) == 6 and i + 1 < len(nodes) and reads.get(R(node[4]), 0) == 1:
