@@ -737,7 +737,7 @@ class NetworkBench:
         be = self._backend(stream)
         calls = []
         for name in ("conv", "conv_fused", "conv_planes", "matmul", "matmul_fused", "pool", "pool_planes",
-                     "pool_nhwc_planes", "planes_fill", "vectorop"):
+                     "pool_nhwc_planes", "pool_nhwc", "planes_fill", "vectorop"):
             if not hasattr(be, name):
                 continue
 

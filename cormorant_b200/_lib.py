@@ -55,6 +55,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_planes_fill_async": (C.c_int, [_p, _p, _p]),
     "cm_pool_planes": (C.c_int, [_p, _p] + [_u] * 17),
     "cm_pool_planes_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
+    "cm_pool_nhwc": (C.c_int, [_p, _p] + [_u] * 17),
+    "cm_pool_nhwc_async": (C.c_int, [_p, _p] + [_u] * 17 + [_p]),
     "cm_pool_nhwc_planes": (C.c_int, [_p, _p] + [_u] * 15),
     "cm_pool_nhwc_planes_async": (C.c_int, [_p, _p] + [_u] * 15 + [_p]),
     "cm_conv_plane_frame": (C.c_int, [_u] * 17 + [C.POINTER(_u)]),

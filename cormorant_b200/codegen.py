@@ -320,6 +320,11 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             a = ", ".join(f"{int(v)}u" for v in args[:15])
             return (f"    /* {i}: Pool {self.R(x)} (channels-last) -> {yp} (plane image) */\n"
                     f"    CHECK(cm_pool_nhwc_planes_async({self._dev(x)}, {self._planes(yp)},\n        {a}, NULL));")
+        if kind == "poolng":
+            _, x, y, args = node
+            a = ", ".join(f"{int(v)}u" for v in args)
+            return (f"    /* {i}: global Pool {self.R(x)} (channels-last) -> {self.R(y)} */\n"
+                    f"    CHECK(cm_pool_nhwc_async({self._dev(x)}, {self._dev(y, False)},\n        {a}, NULL));")
         if kind == "planes":
             _, x, pn = node
             return (f"    /* {i}: {self.R(x)} -> plane image {pn} */\n"

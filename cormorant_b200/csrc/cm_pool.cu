@@ -855,6 +855,72 @@ __global__ void __launch_bounds__(256) pool_global_kernel(const int16_t* __restr
     }
 }
 
+// Global pools of a channels-last tensor x [images][hw][C] (C a multiple of 8, x 16-byte
+// aligned): four adjacent threads take one (image, 8 consecutive channels) item, each the
+// pixels p = its lane mod 4, 4 + that, ... with one 16-byte load of 8 words per pixel (up to
+// 4 pixels' loads issued together); the four partial reductions meet by shuffles (sums mod
+// 2^32 and maxima are order-free), and the item's first thread applies the NCHW kernels'
+// finalize and stores the 8 results with one 16-byte store into y [image][C] (a global
+// pool's output is the same in both layouts).
+template <int TYPE>
+__global__ void __launch_bounds__(256) pool_global_nhwc_kernel(const int16_t* __restrict__ x, int16_t* __restrict__ y,
+                                                               uint64_t groups, uint32_t C, uint32_t hw) {
+    griddep_wait();
+    const uint32_t G = C / 8;
+    const uint32_t sl = threadIdx.x & 3u;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / 4;
+    // whole warps iterate together (the shuffles below need every lane of an item)
+    const uint64_t rounds = (groups + stride - 1) / stride;
+    uint64_t t = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / 4;
+    for (uint64_t r = 0; r < rounds; ++r, t += stride) {
+        const bool live = t < groups;
+        const uint64_t n = live ? t / G : 0;
+        const uint32_t c0 = live ? (uint32_t)(t - n * G) * 8u : 0u;
+        const uint4* src = (const uint4*)(x + n * hw * C + c0);
+        const uint32_t step = C / 8;                       // one pixel, in 16-byte units
+        uint32_t acc[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) acc[k] = (TYPE == P_MAX) ? 0xFFFF8000u : 0u;
+        for (uint32_t p0 = sl; live && p0 < hw; p0 += 16) {
+            uint4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (p0 + 4 * u < hw) v[u] = __ldcs(src + (uint64_t)(p0 + 4 * u) * step);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (p0 + 4 * u >= hw) break;
+                const uint32_t w[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    reduce_word<TYPE>(acc[2 * j], (int32_t)(int16_t)(w[j] & 0xFFFF));
+                    reduce_word<TYPE>(acc[2 * j + 1], (int32_t)(int16_t)(w[j] >> 16));
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+#pragma unroll
+            for (int o = 1; o < 4; o <<= 1) {
+                const uint32_t other = __shfl_xor_sync(0xFFFFFFFFu, acc[k], o);
+                if (TYPE == P_MAX) acc[k] = (uint32_t)max((int32_t)acc[k], (int32_t)other);
+                else acc[k] += other;
+            }
+        }
+        if (live && sl == 0) {
+            uint32_t out[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t a0, a1;
+                if (TYPE == P_MAX) { a0 = (uint32_t)((int32_t)acc[2 * j] * 256); a1 = (uint32_t)((int32_t)acc[2 * j + 1] * 256); }
+                else if (TYPE == P_LP2) { a0 = acc[2 * j]; a1 = acc[2 * j + 1]; }
+                else { a0 = acc[2 * j] * 256u; a1 = acc[2 * j + 1] * 256u; }
+                out[j] = (uint32_t)(uint16_t)finalize<TYPE>(a0, hw) | ((uint32_t)(uint16_t)finalize<TYPE>(a1, hw) << 16);
+            }
+            *(uint4*)(y + n * C + c0) = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+    }
+}
+
 // Per tile buffer (two per CTA): small enough for 8 resident CTAs per SM.
 constexpr size_t kSmemBudget = 16 * 1024;
 
@@ -1050,6 +1116,47 @@ extern "C" int cm_pool_async(const int16_t* x, int16_t* y, unsigned batch, unsig
     if (rc) return rc;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_pool launch");
+}
+
+extern "C" int cm_pool_nhwc_async(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+                                  unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                                  unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                                  unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                                  unsigned count_include_pad, cm_stream_t stream) {
+    (void)stride_h; (void)stride_w; (void)count_include_pad;
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    const uint64_t hw = (uint64_t)in_h * in_w;
+    if ((uint64_t)batch * channels == 0) return CM_OK;
+    if (!x || !y) return set_error(CM_EINVAL, "cm_pool_nhwc: null buffer");
+    const bool global = pad_top == 0 && pad_left == 0 && pool_h == in_h && pool_w == in_w && out_h == 1 && out_w == 1 &&
+                        (dil_h == 1 || pool_h <= 1) && (dil_w == 1 || pool_w <= 1) && hw > 0 && hw < (1ull << 31);
+    if (!global) return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc: global pools only (the window covers the whole plane)");
+    if (channels % 8u != 0 || ((uintptr_t)x & 15u) != 0 || ((uintptr_t)y & 15u) != 0)
+        return set_error(CM_EUNSUPPORTED, "cm_pool_nhwc: channels a multiple of 8 and 16-byte aligned buffers");
+    const uint64_t groups = (uint64_t)batch * (channels / 8u);
+    cudaStream_t s = (cudaStream_t)stream;
+    const unsigned grid = grid_for(cx, groups * 4, 256, 8);
+    {
+        ProfScope ps_(PK_POOL, s);
+        if (pool_type == CM_POOL_MAX) launch_k(pool_global_nhwc_kernel<P_MAX>, grid, 256, 0, s, x, y, groups, channels, (uint32_t)hw);
+        else if (pool_type == CM_POOL_AVG) launch_k(pool_global_nhwc_kernel<P_AVG>, grid, 256, 0, s, x, y, groups, channels, (uint32_t)hw);
+        else if (lp_order == 1u) launch_k(pool_global_nhwc_kernel<P_LP1>, grid, 256, 0, s, x, y, groups, channels, (uint32_t)hw);
+        else launch_k(pool_global_nhwc_kernel<P_LP2>, grid, 256, 0, s, x, y, groups, channels, (uint32_t)hw);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_pool_nhwc launch");
+}
+
+extern "C" int cm_pool_nhwc(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+                            unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                            unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left, unsigned dil_h,
+                            unsigned dil_w, unsigned pool_type, unsigned lp_order, unsigned count_include_pad) {
+    int rc = cm_pool_nhwc_async(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+                                pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad, nullptr);
+    return rc ? rc : finish_sync(nullptr);
 }
 
 extern "C" int cm_pool(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,

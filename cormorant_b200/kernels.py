@@ -167,6 +167,17 @@ def PoolingKernelPlanes(xp, yp, batch, channels, in_h, in_w, out_h, out_w, pool_
     check(L.cm_pool_planes(*args) if stream is None else L.cm_pool_planes_async(*args, _stream(stream)))
 
 
+def PoolingKernelNhwc(x, y, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
+                      pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, lp_order=2, count_include_pad=0,
+                      stream=None) -> None:
+    """PoolingKernel's global pools on a channels-last tensor x [batch][in_h][in_w][channels]
+    (a conv output written under EPI_NHWC); y [batch][channels] (cm_pool_nhwc)."""
+    L = lib()
+    args = (_addr(x), _addr(y), batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h, stride_w,
+            pad_top, pad_left, dil_h, dil_w, pool_type, lp_order, count_include_pad)
+    check(L.cm_pool_nhwc(*args) if stream is None else L.cm_pool_nhwc_async(*args, _stream(stream)))
+
+
 def PoolingKernelNhwcPlanes(x, yp, batch, channels, in_h, in_w, out_h, out_w, pool_h, pool_w, stride_h=1, stride_w=1,
                             pad_top=0, pad_left=0, dil_h=1, dil_w=1, pool_type=POOL_MAX, stream=None) -> None:
     """PoolingKernel (MAX only) from a channels-last tensor x [batch][in_h][in_w][channels]

@@ -236,7 +236,11 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False, nhwc_fn=None, pool
     whose conv can write channels-last, `nhwc_fn(args)`, default the library's
     cm_conv_writes_nhwc): the conv writes its output channels-last (epilogue bit 3) and
     the pool reads that and writes the plane image, ("poolnp", x, yp, args) -- no NCHW
-    tensor, no split pass (ResNet-18's stem).  A tensor no conv produced (the input, a pool
+    tensor, no split pass (ResNet-18's stem).  Likewise (pool_nhwc=True) a global pool that
+    is the only reader of a conv's output (channels a multiple of 8, the conv's residual,
+    if any, read from a plane image) takes that output channels-last: ("poolng", x, y,
+    args), cm_pool_nhwc (ResNet-18's last block before GlobalAveragePool: its conv stores
+    rows instead of scattered NCHW words).  A tensor no conv produced (the input, a pool
     output kept NCHW) that convs read at least twice as an operand or residual gets one
     ("planes", x, image) split pass right after its producer."""
     if frame_fn is None:
@@ -285,6 +289,20 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False, nhwc_fn=None, pool
         x_ok, r_ok = plane_readers(u)
         if (x_ok or r_ok) and len(x_ok) + len(r_ok) == len(uses.get(u, [])):
             poolnp[j] = (x_ok, r_ok)
+            nhwc_convs.add(i)
+    # global pools whose conv writes channels-last for them (the pool its only reader)
+    poolng = set()
+    for j, node in enumerate(nodes):
+        if not pool_nhwc or node[0] != "pool" or R(node[1]) not in produced:
+            continue
+        a, t = node[3], R(node[1])
+        i = produced[t]
+        glob = a[4] == 1 and a[5] == 1 and a[6] == a[2] and a[7] == a[3] and a[10] == 0 and a[11] == 0
+        res = nodes[i][7]
+        res_ok = res is None or i in plane_readers(R(res))[1]
+        if (glob and a[1] % 8 == 0 and len(uses.get(t, [])) == 1 and uses[t][0][0] == j and res_ok
+                and nhwc_fn(nodes[i][5])):
+            poolng.add(j)
             nhwc_convs.add(i)
     # MAX pools that can run plane to plane: conv input, output read only by plane-reading convs
     poolp = {}
@@ -344,6 +362,9 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False, nhwc_fn=None, pool
             continue
         if i in pool_nhwc_io:
             out.append(("poolnp", pool_nhwc_io[i][0], pool_nhwc_io[i][1], node[3]))
+            continue
+        if i in poolng:
+            out.append(("poolng", node[1], node[2], node[3]))
             continue
         if node[0] != "conv":
             out.append(node)
@@ -534,6 +555,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "poolnp":
             _, x, yp, args = node
             backend.pool_nhwc_planes(R(x), R(yp), *args)
+        elif kind == "poolng":
+            _, x, y, args = node
+            backend.pool_nhwc(R(x), R(y), *args)
         elif kind == "matmul" and len(node) > 5:
             _, a, bb, c, args, epi, bias = node
             backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
@@ -631,6 +655,9 @@ class GpuBackend:
 
     def pool_nhwc_planes(self, x, yp, *args):
         self.k.PoolingKernelNhwcPlanes(x, yp, *args[:15], stream=self.stream)
+
+    def pool_nhwc(self, x, y, *args):
+        self.k.PoolingKernelNhwc(x, y, *args, stream=self.stream)
 
 
 def weights_key(w, bias, geo) -> tuple:

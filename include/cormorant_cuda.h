@@ -362,6 +362,23 @@ int cm_pool_async(const int16_t* x, int16_t* y, unsigned batch, unsigned channel
                   unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
                   unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
                   unsigned count_include_pad, cm_stream_t stream);
+/* PoolingKernel's global pools (the window covers the whole plane: out 1x1, pool = in
+ * size, no padding) on a channels-last tensor x [batch][in_h][in_w][channels] -- a conv's
+ * y under epilogue bit 3 -- with cm_pool's arguments and words; y is [batch][channels].
+ * No reference counterpart: a conv whose only reader is a global pool (ResNet's last
+ * block before GlobalAveragePool) then writes channels-last rows instead of scattered NCHW
+ * words.  channels a multiple of 8, x and y 16-byte aligned; other pools and layouts
+ * return CM_EUNSUPPORTED. */
+int cm_pool_nhwc(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+                 unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                 unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                 unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                 unsigned count_include_pad);
+int cm_pool_nhwc_async(const int16_t* x, int16_t* y, unsigned batch, unsigned channels, unsigned in_h,
+                       unsigned in_w, unsigned out_h, unsigned out_w, unsigned pool_h, unsigned pool_w,
+                       unsigned stride_h, unsigned stride_w, unsigned pad_top, unsigned pad_left,
+                       unsigned dil_h, unsigned dil_w, unsigned pool_type, unsigned lp_order,
+                       unsigned count_include_pad, cm_stream_t stream);
 
 /* ---- outputs written across GPUs (no reference counterpart) -----------------------
  * The batch-sharded multi-GPU drivers (one process per GPU) gather a step's outputs

@@ -193,6 +193,7 @@ def test_chained_project_uses_plane_images(tmp_path):
     assert src.count("cm_planes_create(") == len(net.planes) == src.count("cm_planes_destroy(")
     assert src.count("cm_conv_planes_async(") == 20 and src.count("cm_planes_fill_async(") == 0
     assert src.count("cm_pool_nhwc_planes_async(") == 1
+    assert src.count("cm_pool_nhwc_async(") == 1                     # the global pool after the last block
     if LIB.exists():
         codegen.compile_project(tmp_path, INCLUDE, LIB)
 

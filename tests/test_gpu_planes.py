@@ -278,6 +278,31 @@ def test_max_pool_nhwc_to_planes(cm, port, N, C, H, W, k, s, p, d, frame):
     assert_same(_identity_readback(kernels, Y, N, C, oh, ow), want, f"max pool nhwc -> planes {pa} frame {frame}")
 
 
+@pytest.mark.parametrize("N,C,H,W,ptype,lp", [(256, 512, 7, 7, 1, 2), (5, 64, 7, 7, 0, 2), (3, 24, 9, 5, 2, 2),
+                                                (2, 40, 3, 3, 2, 1), (4, 8, 1, 1, 1, 2), (2, 16, 30, 30, 1, 2)])
+def test_global_pool_nhwc(cm, port, N, C, H, W, ptype, lp):
+    """cm_pool_nhwc: a global pool of a channels-last tensor gives cm_pool's words on the NCHW
+    tensor (AVG, MAX, LP2, LP1; pixel counts with and without a remainder of 7)."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(N + C + H + ptype)
+    x = rand16(rng, N * C * H * W)
+    pa = (N, C, H, W, 1, 1, H, W, 1, 1, 0, 0, 1, 1, ptype, lp, 0)
+    want = port.pool(x, *pa)[: N * C]
+    y = empty(N * C)
+    kernels.PoolingKernelNhwc(dev(_nchw_to_nhwc(x, N, C, H, W)), y, *pa)
+    assert_same(host(y), want, f"global pool nhwc {pa}")
+
+
+def test_global_pool_nhwc_refusals(cm):
+    """Only global pools, channels a multiple of 8."""
+    from cormorant_b200 import kernels
+    with pytest.raises(cm.CormorantError):      # not global: a 2 x 2 output
+        kernels.PoolingKernelNhwc(dev(np.zeros(2 * 4 * 4 * 8, np.int16)), empty(2 * 8 * 4), 2, 8, 4, 4, 2, 2, 2, 2, 2, 2)
+    with pytest.raises(cm.CormorantError):      # 12 channels
+        kernels.PoolingKernelNhwc(dev(np.zeros(2 * 4 * 4 * 12, np.int16)), empty(2 * 12), 2, 12, 4, 4, 1, 1, 4, 4,
+                                  pool_type=kernels.POOL_AVG)
+
+
 def test_max_pool_nhwc_to_planes_refusals(cm):
     """Channel counts other than 16 x a power of two, and pool types other than MAX, are refused."""
     from cormorant_b200 import kernels

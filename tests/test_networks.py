@@ -78,6 +78,11 @@ class OracleBackend:
         n, c, h, w = args[:4]
         self.pool(nhwc_to_nchw(x, n, c, h, w), yp, *args)
 
+    def pool_nhwc(self, x, y, *args):
+        """Global pool of a channels-last tensor (its [n][c] output is the same in both layouts)."""
+        n, c, h, w = args[:4]
+        self.pool(nhwc_to_nchw(x, n, c, h, w), y, *args)
+
 
 def nchw_to_nhwc(t, n, c, h, w):
     return np.ascontiguousarray(np.asarray(t)[: n * c * h * w].reshape(n, c, h, w).transpose(0, 2, 3, 1)).reshape(-1)
@@ -239,7 +244,9 @@ def test_chain_pass_resnet_structure():
     assert sum(1 for n in convs if n[7] is not None) == 0       # no residual read as NCHW
     assert all(n[8] is not None for n in convs if n[1] is None)
     assert all(n[9] is not None for n in convs if n[4] is None)
-    assert set(net.buffers) == {"x", "relu4", "relu86", "pool87", "gemm92"}   # relu4 is channels-last
+    assert set(net.buffers) == {"x", "relu4", "relu86", "pool87", "gemm92"}   # relu4, relu86 channels-last
+    assert [n[0] for n in net.nodes[-3:-1]] == ["conv", "poolng"]       # the last block's conv -> global pool
+    assert net.nodes[-3][6] == 3 | networks.EPI_NHWC and net.nodes[-2][1:3] == ("relu86", "pool87")
     old = networks.chain(networks.fuse(networks.resnet18(batch=2)), pool_nhwc=False)
     assert [n[1] for n in old.nodes if n[0] == "planes"] == ["pool5"]   # the max pool's output, split once
     assert set(old.buffers) == {"x", "relu4", "pool5", "relu86", "pool87", "gemm92"}
