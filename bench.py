@@ -579,7 +579,8 @@ class NetworkBench:
             self.metric = "ResNet-18-shaped images/s (batch 256)"
         self.fused = not UNFUSED
         if self.fused:                                           # Conv->Relu (/ Conv->Add->Relu) folded
-            self.net = networks.fuse(self.net, residual=FUSE_RESIDUAL)
+            # one cm_calls launch (--one-launch) takes the plain conv and pool calls
+            self.net = networks.fuse(self.net, residual=FUSE_RESIDUAL, conv_pool_macs=0 if ONE_LAUNCH else 1 << 22)
         self.planes = self.fused and PLANES and which != "lenet"
         if self.planes:                                          # conv outputs produced as the next convs' operand
             self.net = networks.chain(self.net)

@@ -49,6 +49,8 @@ SIGNATURES: dict[str, tuple] = {
     "cm_conv_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 17 + [_p]),
     "cm_conv_fused": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p]),
     "cm_conv_fused_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p, _p]),
+    "cm_conv_pool": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p] + [_u] * 17),
+    "cm_conv_pool_async": (C.c_int, [_p, _p, _p, _p] + [_u] * 18 + [_p] + [_u] * 17 + [_p]),
     "cm_planes_create": (_p, [_u] * 8),
     "cm_planes_destroy": (None, [_p]),
     "cm_planes_fill": (C.c_int, [_p, _p]),

@@ -288,6 +288,14 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
     # ---- inference.c ---------------------------------------------------------
     def _call(self, i: int, node) -> str:
         kind = node[0]
+        if kind == "convpool":
+            _, x, wn, bn, y, args, epi, resid, pargs = node
+            a = ", ".join(f"{int(v)}u" for v in args)
+            pa = ", ".join(f"{int(v)}u" for v in pargs)
+            what = "Conv" + ("+Add" if epi & 2 else "") + ("+Relu" if epi & 1 else "") + "+MaxPool"
+            return (f"    /* {i}: {what} -> {self.R(y)} (one launch) */\n"
+                    f"    CHECK(cm_conv_pool_async({self._dev(x)}, {self._dev(wn)}, {self._dev(bn)}, {self._dev(y, False)},\n"
+                    f"        {a}, {int(epi)}u, {self._dev(resid)},\n        {pa}, NULL));")
         if kind == "conv" and self.prepared:
             x, y, resid, xp, yp, rp = node[1], node[4], None, None, None, None
             epi = 0

@@ -120,6 +120,68 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
     }
 }
 
+// ConvKernel (+ its fused epilogue) followed by a MAX PoolingKernel on the conv's output, in
+// one CUDA-core launch for launch-bound sizes.  A pooled output word takes G x T lanes: T tap
+// slots (pool taps slot, slot + T, ...) of G lanes each; the G lanes of a slot split the conv
+// pixel's reduction (rows (c, r) as in conv_direct_kernel) and meet by shuffles, the slot's
+// first lane narrows the sum and applies the epilogue (resid at the conv output's index), and
+// the slots' maxima meet by shuffles.  Taps outside the conv output contribute the pool's
+// -128.0 padding, which is also where the maximum starts.  The conv output is never written.
+// Every lane runs the same loop counts (the shuffles need the whole warp).
+struct PoolGeo {
+    uint32_t out_h, out_w, ph, pw, sh, sw, pt, pl, dh, dw;
+};
+
+__global__ void __launch_bounds__(256) conv_pool_direct_kernel(const int16_t* __restrict__ x, const int16_t* __restrict__ w,
+                                                               const int16_t* __restrict__ bias, int16_t* __restrict__ y,
+                                                               DwArgs a, PoolGeo q, uint64_t total, uint32_t G,
+                                                               uint32_t T, uint32_t epi, const int16_t* __restrict__ resid) {
+    griddep_wait();
+    const uint64_t qhw = (uint64_t)q.out_h * q.out_w, chw = (uint64_t)a.out_h * a.out_w;
+    const uint32_t khw = a.kh * a.kw, rows = a.C * a.kh, taps = q.ph * q.pw;
+    const uint32_t L = G * T, li = threadIdx.x & (L - 1), g = li & (G - 1), slot = li / G;
+    const uint32_t tap_rounds = (taps + T - 1) / T;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x / L;
+    for (uint64_t t0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) / L; t0 < (total + stride - 1) / stride * stride;
+         t0 += stride) {
+        const bool live = t0 < total;
+        const uint64_t t = live ? t0 : 0;
+        const uint64_t plane = t / qhw;            // n * M + m
+        const uint64_t p = t - plane * qhw;
+        const uint64_t n = plane / a.M, m = plane - n * a.M;
+        const uint32_t qh = (uint32_t)(p / q.out_w), qw = (uint32_t)(p - (uint64_t)qh * q.out_w);
+        int32_t best = -32768;
+        for (uint32_t rd = 0; rd < tap_rounds; ++rd) {
+            const uint32_t tap = slot + rd * T;
+            const uint32_t pr = tap / q.pw, pc = tap - pr * q.pw;
+            const int64_t oh = (int64_t)qh * q.sh + (int64_t)pr * q.dh - (int64_t)q.pt;
+            const int64_t ow = (int64_t)qw * q.sw + (int64_t)pc * q.dw - (int64_t)q.pl;
+            const bool in = live && tap < taps && oh >= 0 && oh < (int64_t)a.out_h && ow >= 0 && ow < (int64_t)a.out_w;
+            uint32_t acc = 0;
+            for (uint32_t kr = g; in && kr < rows; kr += G) {
+                const uint32_t c = kr / a.kh, r = kr - c * a.kh;
+                const int64_t ih = oh * a.sh + (int64_t)r * a.dh - (int64_t)a.pt;
+                if (ih < 0 || ih >= (int64_t)a.H) continue;
+                const int16_t* xr = x + ((n * a.C + c) * (uint64_t)a.H + (uint64_t)ih) * a.W;
+                const int16_t* wr = w + (m * a.C + c) * (uint64_t)khw + (uint64_t)r * a.kw;
+                for (uint32_t s = 0; s < a.kw; ++s) {
+                    const int64_t iw = ow * a.sw + (int64_t)s * a.dw - (int64_t)a.pl;
+                    if (iw < 0 || iw >= (int64_t)a.W) continue;
+                    acc += (uint32_t)((int32_t)__ldg(xr + iw) * (int32_t)__ldg(wr + s));
+                }
+            }
+            for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+            if (in && g == 0) {
+                if (a.has_bias) acc += (uint32_t)((int32_t)bias[m] * 256);
+                const uint64_t ci = plane * chw + (uint64_t)oh * a.out_w + (uint64_t)ow;
+                best = max(best, (int32_t)epilogue_word(narrow_acc(acc), epi, resid, ci));
+            }
+        }
+        for (uint32_t o = G; o < L; o <<= 1) best = max(best, __shfl_xor_sync(0xFFFFFFFFu, best, o));
+        if (live && li == 0) y[t] = (int16_t)best;
+    }
+}
+
 // Empty reduction (in_ch * kh * kw == 0): every output is bias (or 0).
 __global__ void conv_bias_fill_kernel(const int16_t* __restrict__ bias, int16_t* __restrict__ y, uint32_t M,
                                       uint64_t ohw, uint64_t total, uint32_t has_bias) {
@@ -1909,6 +1971,66 @@ extern "C" int cm_conv_fused_async(const int16_t* x, const int16_t* weight, cons
     return conv_impl(x, nullptr, weight, bias, y, nullptr, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw,
                      stride_h, stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue,
                      resid, nullptr, stream);
+}
+
+extern "C" int cm_conv_pool_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y,
+                                  unsigned batch, unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch,
+                                  unsigned out_h, unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h,
+                                  unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
+                                  unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
+                                  const int16_t* resid, unsigned p_batch, unsigned p_channels, unsigned p_in_h,
+                                  unsigned p_in_w, unsigned p_out_h, unsigned p_out_w, unsigned pool_h, unsigned pool_w,
+                                  unsigned p_stride_h, unsigned p_stride_w, unsigned p_pad_top, unsigned p_pad_left,
+                                  unsigned p_dil_h, unsigned p_dil_w, unsigned pool_type, unsigned lp_order,
+                                  unsigned count_include_pad, cm_stream_t stream) {
+    (void)lp_order; (void)count_include_pad;
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (epilogue > 3u) return set_error(CM_EINVAL, "cm_conv_pool: epilogue must be 0..3");
+    if (p_batch != batch || p_channels != out_ch || p_in_h != out_h || p_in_w != out_w)
+        return set_error(CM_EINVAL, "cm_conv_pool: the pool's input is not the conv's output");
+    if (pool_type != CM_POOL_MAX) return set_error(CM_EUNSUPPORTED, "cm_conv_pool: MAX pooling only");
+    if (is_depthwise) return set_error(CM_EUNSUPPORTED, "cm_conv_pool: standard convs only");
+    const uint64_t total = (uint64_t)batch * out_ch * p_out_h * p_out_w;
+    if (total == 0) return CM_OK;
+    if (!x || !weight || !y || (has_bias && !bias) || ((epilogue & 2u) && !resid))
+        return set_error(CM_EINVAL, "cm_conv_pool: null buffer");
+    const DwArgs a{in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h, stride_w, dilation_h, dilation_w, pad_top,
+                   pad_left, has_bias ? 1u : 0u};
+    const PoolGeo q{p_out_h, p_out_w, pool_h, pool_w, p_stride_h, p_stride_w, p_pad_top, p_pad_left, p_dil_h, p_dil_w};
+    cudaStream_t s = (cudaStream_t)stream;
+    {
+        ProfScope ps_(PK_CONV_AUX, s);
+        // tap slots: the pool window's taps rounded up to a power of two; then reduction lanes
+        // while the slots x lanes stay within a warp
+        uint32_t T = 1;
+        while (T < (uint64_t)pool_h * pool_w && T < 32) T *= 2;
+        uint32_t G = direct_lanes(cx, total * T, (uint64_t)in_ch * kh);
+        while (G * T > 32) G /= 2;
+        launch_k(conv_pool_direct_kernel, grid_for(cx, total * G * T, 256, 8), 256, 0, s, x, weight, bias, y, a, q, total,
+                 G, T, epilogue, resid);
+    }
+    count_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_conv_pool");
+}
+
+extern "C" int cm_conv_pool(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
+                            unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h,
+                            unsigned out_w, unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w,
+                            unsigned dilation_h, unsigned dilation_w, unsigned pad_top, unsigned pad_left,
+                            unsigned has_bias, unsigned is_depthwise, unsigned epilogue, const int16_t* resid,
+                            unsigned p_batch, unsigned p_channels, unsigned p_in_h, unsigned p_in_w, unsigned p_out_h,
+                            unsigned p_out_w, unsigned pool_h, unsigned pool_w, unsigned p_stride_h,
+                            unsigned p_stride_w, unsigned p_pad_top, unsigned p_pad_left, unsigned p_dil_h,
+                            unsigned p_dil_w, unsigned pool_type, unsigned lp_order, unsigned count_include_pad) {
+    int rc = cm_conv_pool_async(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h, out_w, kh, kw, stride_h,
+                                stride_w, dilation_h, dilation_w, pad_top, pad_left, has_bias, is_depthwise, epilogue,
+                                resid, p_batch, p_channels, p_in_h, p_in_w, p_out_h, p_out_w, pool_h, pool_w,
+                                p_stride_h, p_stride_w, p_pad_top, p_pad_left, p_dil_h, p_dil_w, pool_type, lp_order,
+                                count_include_pad, nullptr);
+    return rc ? rc : finish_sync(nullptr);
 }
 
 extern "C" int cm_conv_fused(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,

@@ -107,6 +107,17 @@ def ConvKernelFused(x, weight, bias, y, batch, in_ch, in_h, in_w, out_ch, out_h,
     check(L.cm_conv_fused(*args) if stream is None else L.cm_conv_fused_async(*args, _stream(stream)))
 
 
+def ConvPoolKernel(x, weight, bias, y, conv_args, epilogue, resid, pool_args, stream=None) -> None:
+    """ConvKernel (+ the fused epilogue) followed by a MAX PoolingKernel of its output in one
+    launch (cm_conv_pool): conv_args are the conv's 17 scalars, pool_args the pool's 17
+    (cm_pool's order); y receives the pool's output.  Not a reference kernel: the words of
+    Conv -> [Add] -> [Relu] -> MaxPool."""
+    L = lib()
+    args = ((_addr(x), _addr(weight), _addr(bias), _addr(y)) + tuple(int(v) for v in conv_args)
+            + (int(epilogue), _addr(resid)) + tuple(int(v) for v in pool_args))
+    check(L.cm_conv_pool(*args) if stream is None else L.cm_conv_pool_async(*args, _stream(stream)))
+
+
 class PlaneImage:
     """A conv input held as channels-last int8 hi/lo planes with its padding frame
     (cm_planes_create): written by a producing conv's GEMM epilogue, read in place of

@@ -197,6 +197,8 @@ def make_input(net: Net, seed: int = 7) -> np.ndarray:
 
 def _inputs(node) -> list:
     kind = node[0]
+    if kind == "convpool":
+        return [n for n in (node[1], node[2], node[3], node[7]) if n is not None]
     if kind == "conv":
         names = [node[1], node[2], node[3]] + ([node[7]] if len(node) > 7 else [])
         if len(node) > 8 and node[1] is None:
@@ -213,6 +215,8 @@ def _inputs(node) -> list:
 
 
 def output_of(node) -> str:
+    if node[0] == "convpool":
+        return node[4]
     if node[0] == "conv":
         return node[4] if node[4] is not None else node[9]
     return node[3] if node[0] in ("vectorop", "matmul", "matmul_at") else node[2]   # pool, planes: node[2]
@@ -394,14 +398,16 @@ def chain(net: Net, frame_fn=None, pool_planes: bool = False, nhwc_fn=None, pool
                source_kinds=net.source_kinds or tuple(sorted({n[0] for n in net.nodes})), planes=planes)
 
 
-def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
+def fuse(net: Net, residual: bool = True, gemm: bool = True, conv_pool_macs: int = 1 << 22) -> Net:
     """The call list with Conv -> Relu chains and (residual=True) Conv -> Add and
     Conv -> Add -> Relu chains folded into one conv call with a fused epilogue
     (cm_conv_fused), and (gemm=True) the Gemm decomposition MatMul -> Add(bias row) and
     MatMul -> [Add(bias row)] -> Relu folded into one cm_matmul_fused call: the same
-    words, without writing and re-reading the intermediate tensors.  A chain is folded
-    only when each intermediate result has no other reader (and is not the network
-    output)."""
+    words, without writing and re-reading the intermediate tensors.  A conv of at most
+    `conv_pool_macs` multiply-adds (a launch-bound size) whose output only a MAX pool reads
+    becomes one ("convpool", x, w, bias, y, args, epi, resid, pool_args) call, cm_conv_pool
+    (0 turns it off).  A chain is folded only when each intermediate result has no other
+    reader (and is not the network output)."""
     R = net.resolve
     reads: dict = {}
     for node in net.nodes:
@@ -482,6 +488,23 @@ def fuse(net: Net, residual: bool = True, gemm: bool = True) -> Net:
                 continue
         out.append(node)
         i += 1
+    if conv_pool_macs:
+        folded, i = [], 0
+        while i < len(out):
+            node = out[i]
+            if node[0] == "conv" and i + 1 < len(out) and out[i + 1][0] == "pool":
+                args, p = node[5], out[i + 1]
+                pa, y = p[3], R(node[4])
+                macs = args[0] * args[4] * args[5] * args[6] * args[1] * args[7] * args[8]
+                if (R(p[1]) == y and reads.get(y, 0) == 1 and pa[14] == 0 and not args[16] and macs <= conv_pool_macs
+                        and tuple(pa[:4]) == (args[0], args[4], args[5], args[6])):
+                    epi, resid = (node[6], node[7]) if len(node) > 6 else (0, None)
+                    folded.append(("convpool", node[1], node[2], node[3], p[2], args, epi, resid, pa))
+                    i += 2
+                    continue
+            folded.append(node)
+            i += 1
+        out = folded
     used = {R(n) for node in out for n in _inputs(node)} | {R(output_of(node)) for node in out}
     used |= {R(net.input), R(net.output)}
     fused = Net(net.name + "+fused", net.batch, net.input, net.output,
@@ -558,6 +581,9 @@ def execute(net: Net, backend, bufs: dict) -> None:
         elif kind == "poolng":
             _, x, y, args = node
             backend.pool_nhwc(R(x), R(y), *args)
+        elif kind == "convpool":
+            _, x, wn, bn, y, args, epi, resid, pargs = node
+            backend.conv_pool(R(x), R(wn), R(bn), R(y), args, epi, R(resid), pargs)
         elif kind == "matmul" and len(node) > 5:
             _, a, bb, c, args, epi, bias = node
             backend.matmul_fused(R(a), R(bb), R(c), *args, epi, R(bias))
@@ -658,6 +684,9 @@ class GpuBackend:
 
     def pool_nhwc(self, x, y, *args):
         self.k.PoolingKernelNhwc(x, y, *args, stream=self.stream)
+
+    def conv_pool(self, x, w, bias, y, args, epi, resid, pargs):
+        self.k.ConvPoolKernel(x, w, bias, y, args, epi, resid, pargs, stream=self.stream)
 
 
 def weights_key(w, bias, geo) -> tuple:

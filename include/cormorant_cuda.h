@@ -209,6 +209,31 @@ int cm_conv_fused_async(const int16_t* x, const int16_t* weight, const int16_t* 
                         unsigned stride_w, unsigned dilation_h, unsigned dilation_w, unsigned pad_top,
                         unsigned pad_left, unsigned has_bias, unsigned is_depthwise, unsigned epilogue,
                         const int16_t* resid, cm_stream_t stream);
+/* ConvKernel (+ cm_conv_fused's epilogue) followed by a MAX PoolingKernel of its output, in one
+ * CUDA-core launch; the conv's 17 scalars and epilogue / resid as cm_conv_fused, then the pool's
+ * 17 scalars as cm_pool (its batch, channels, in_h, in_w must be the conv's batch, out_ch, out_h,
+ * out_w). y is the pool's output; the conv output is never written. The words of cm_conv_fused
+ * followed by cm_pool. No reference counterpart: for launch-bound networks (LeNet-5 batch 1),
+ * where a Conv -> Relu -> MaxPool chain whose intermediate has no other reader becomes one
+ * launch. MAX pools and standard (not depthwise) convs only, else CM_EUNSUPPORTED. */
+int cm_conv_pool(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
+                 unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w,
+                 unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                 unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias, unsigned is_depthwise,
+                 unsigned epilogue, const int16_t* resid, unsigned p_batch, unsigned p_channels, unsigned p_in_h,
+                 unsigned p_in_w, unsigned p_out_h, unsigned p_out_w, unsigned pool_h, unsigned pool_w,
+                 unsigned p_stride_h, unsigned p_stride_w, unsigned p_pad_top, unsigned p_pad_left,
+                 unsigned p_dil_h, unsigned p_dil_w, unsigned pool_type, unsigned lp_order,
+                 unsigned count_include_pad);
+int cm_conv_pool_async(const int16_t* x, const int16_t* weight, const int16_t* bias, int16_t* y, unsigned batch,
+                       unsigned in_ch, unsigned in_h, unsigned in_w, unsigned out_ch, unsigned out_h, unsigned out_w,
+                       unsigned kh, unsigned kw, unsigned stride_h, unsigned stride_w, unsigned dilation_h,
+                       unsigned dilation_w, unsigned pad_top, unsigned pad_left, unsigned has_bias,
+                       unsigned is_depthwise, unsigned epilogue, const int16_t* resid, unsigned p_batch,
+                       unsigned p_channels, unsigned p_in_h, unsigned p_in_w, unsigned p_out_h, unsigned p_out_w,
+                       unsigned pool_h, unsigned pool_w, unsigned p_stride_h, unsigned p_stride_w,
+                       unsigned p_pad_top, unsigned p_pad_left, unsigned p_dil_h, unsigned p_dil_w,
+                       unsigned pool_type, unsigned lp_order, unsigned count_include_pad, cm_stream_t stream);
 
 /* ---- Plane images: conv outputs produced as the next conv's operand ----------------
  * (no reference counterpart; results are those of the plain calls, word for word)

@@ -103,8 +103,8 @@ def test_emitted_api_and_weight_files(tmp_path):
                 "#define INFERENCE_X_SIZE  784u", f"#define INFERENCE_{out.upper()}_SIZE  10u"):
         assert sym in h, sym
     src = (tmp_path / "src/inference.c").read_text()
-    assert src.count("cm_conv_fused_async(") == 2             # Conv+Relu twice
-    assert src.count("cm_matmul_fused_async(") == 3 and src.count("cm_pool_async(") == 2   # Gemm(+Relu) x 3
+    assert src.count("cm_conv_pool_async(") == 2              # Conv+Relu+MaxPool twice, one launch each
+    assert src.count("cm_matmul_fused_async(") == 3 and src.count("cm_pool_async(") == 0   # Gemm(+Relu) x 3
     assert "cm_vectorop_async(" not in src
     assert src.count("CHECK(cm_synchronize(NULL));") == 1
     # weights above the threshold go to .dat files (raw little-endian words), the rest inline

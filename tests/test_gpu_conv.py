@@ -185,6 +185,53 @@ def test_conv_fused_epilogue(cm, port, case, epi):
     assert_same(host(y), want, f"fused {case} epi {epi}")
 
 
+# conv (N, C, H, W, M, kh, kw, sh, sw, dh, dw, pt, pl, pb, pr, bias) and MAX pool (ph, pw, sh, sw, pt, pl, dh, dw)
+CONV_POOL = [
+    ((1, 1, 28, 28, 6, 5, 5, 1, 1, 1, 1, 2, 2, 2, 2, 1), (2, 2, 2, 2, 0, 0, 1, 1)),     # LeNet conv1 + pool
+    ((1, 6, 14, 14, 16, 5, 5, 1, 1, 1, 1, 0, 0, 0, 0, 1), (2, 2, 2, 2, 0, 0, 1, 1)),    # LeNet conv2 + pool
+    ((3, 4, 13, 11, 5, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0), (3, 3, 2, 2, 1, 1, 1, 1)),     # overlapping padded windows
+    ((2, 3, 17, 15, 7, 3, 2, 2, 1, 2, 1, 2, 0, 1, 1, 1), (2, 3, 1, 2, 0, 1, 2, 1)),     # dilations, odd strides
+]
+
+
+@pytest.mark.parametrize("case", CONV_POOL)
+@pytest.mark.parametrize("epi", [0, 1, 3])
+def test_conv_pool_one_launch(cm, port, case, epi):
+    """cm_conv_pool == ConvKernel, then VectorOP ADD / RELU, then a MAX PoolingKernel, word for word."""
+    from cormorant_b200 import kernels
+    (N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb), (ph, pw, psh, psw, ppt, ppl, pdh, pdw) = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    qh, qw = osz(oh, ph, psh, pdh, ppt, ppt), osz(ow, pw, psw, pdw, ppl, ppl)
+    rng = np.random.default_rng(sum(case[0]) + sum(case[1]) + epi)
+    x = rand16(rng, N * C * H * W, -2048, 2048)
+    w = rand16(rng, M * C * kh * kw, -512, 512)
+    bias = rand16(rng, M, -2048, 2048)
+    r = rand16(rng, N * M * oh * ow)
+    conv_args = (N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, 0)
+    pool_args = (N, M, oh, ow, qh, qw, ph, pw, psh, psw, ppt, ppl, pdh, pdw, 0, 2, 0)
+    size = N * M * oh * ow
+    t = port.conv(x, w, bias, *conv_args)[:size]
+    if epi & 2:
+        t = port.vectorop(t, r, size, 0, 1, 0, 0)[:size]
+    if epi & 1:
+        t = port.vectorop(t, None, size, 4, 1, 0, 0)[:size]
+    want = port.pool(t, *pool_args)[: N * M * qh * qw]
+    y = empty(N * M * qh * qw)
+    kernels.ConvPoolKernel(dev(x), dev(w), dev(bias), y, conv_args, epi, dev(r), pool_args)
+    assert_same(host(y), want, f"conv+pool {case} epi {epi}")
+
+
+def test_conv_pool_refusals(cm):
+    """An AVG pool, or a pool whose input is not the conv's output, is refused."""
+    from cormorant_b200 import kernels
+    conv_args = (1, 1, 8, 8, 2, 8, 8, 3, 3, 1, 1, 1, 1, 1, 1, 0, 0)
+    x, w = dev(np.zeros(64, np.int16)), dev(np.zeros(18, np.int16))
+    with pytest.raises(cm.CormorantError):
+        kernels.ConvPoolKernel(x, w, None, empty(32), conv_args, 0, None, (1, 2, 8, 8, 4, 4, 2, 2, 2, 2, 0, 0, 1, 1, 1, 2, 0))
+    with pytest.raises(cm.CormorantError):
+        kernels.ConvPoolKernel(x, w, None, empty(32), conv_args, 0, None, (1, 2, 7, 8, 4, 4, 2, 2, 2, 2, 0, 0, 1, 1, 0, 2, 0))
+
+
 PREPARED = [REF_CASES[i] for i in (4, 13, 19, 20, 21, 24, 25, 34, 36, 39, 42)]
 
 

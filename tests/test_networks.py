@@ -78,6 +78,12 @@ class OracleBackend:
         n, c, h, w = args[:4]
         self.pool(nhwc_to_nchw(x, n, c, h, w), yp, *args)
 
+    def conv_pool(self, x, w, bias, y, args, epi, resid, pargs):
+        """Conv -> [Add] -> [Relu] -> MaxPool as the reference call sequence."""
+        t = np.zeros(args[0] * args[4] * args[5] * args[6], np.int16)
+        self.conv_fused(x, w, bias, t, *args, epi, resid)
+        self.pool(t, y, *pargs)
+
     def pool_nhwc(self, x, y, *args):
         """Global pool of a channels-last tensor (its [n][c] output is the same in both layouts)."""
         n, c, h, w = args[:4]
@@ -162,8 +168,8 @@ def test_fusion_pass_shapes():
     """Conv -> Relu (with residual=True also Conv -> Add -> Relu) and (gemm=True) MatMul ->
     Add(bias row) -> [Relu] chains fold; nothing else changes."""
     def kinds(net):
-        return [(n[0], n[6] if n[0] == "conv" and len(n) > 6 else n[5] if n[0] == "matmul" and len(n) > 5 else None)
-                for n in net.nodes]
+        return [(n[0], n[6] if n[0] in ("conv", "convpool") and len(n) > 6 else n[5] if n[0] == "matmul" and len(n) > 5
+                 else None) for n in net.nodes]
     rn = kinds(networks.fuse(networks.resnet18(batch=1), residual=True))
     assert rn.count(("conv", 1)) == 9 and rn.count(("conv", 3)) == 8 and rn.count(("conv", None)) == 3
     assert rn.count(("matmul", 2)) == 1 and rn.count(("vectorop", None)) == 0    # classifier: MatMul+Add
@@ -171,6 +177,8 @@ def test_fusion_pass_shapes():
     assert rn.count(("conv", 1)) == 9 and rn.count(("conv", None)) == 11 and rn.count(("vectorop", None)) == 17
     assert rn.count(("matmul", None)) == 1
     ln = networks.fuse(networks.lenet5())
+    assert kinds(ln) == [("convpool", 1), ("convpool", 1), ("matmul", 3), ("matmul", 3), ("matmul", 2)]
+    ln = networks.fuse(networks.lenet5(), conv_pool_macs=0)
     assert kinds(ln) == [("conv", 1), ("pool", None), ("conv", 1), ("pool", None), ("matmul", 3), ("matmul", 3),
                          ("matmul", 2)]
     assert ln.source_kinds == ("conv", "matmul", "pool", "vectorop")
@@ -297,7 +305,7 @@ def test_resnet18_chained_batch4_every_output(cm, port, pool_planes, prepared):
 def test_one_launch_call_list_qualifies_on_cpu():
     """LeNet's folded call list runs in one cm_calls launch; ResNet-18's does not (too large)."""
     from cormorant_b200 import kernels
-    net = networks.fuse(networks.lenet5())
+    net = networks.fuse(networks.lenet5(), conv_pool_macs=0)
     fake = {n: 256 * (i + 1) for i, n in enumerate(list(net.buffers) + list(net.consts))}
     arr = kernels.call_array(networks.calls_of(net, fake))
     assert len(arr) == 7 and kernels.calls_supported(arr)
@@ -315,7 +323,7 @@ def test_one_launch_call_list_qualifies_on_cpu():
 @pytest.mark.parametrize("batch", [1, 3])
 def test_lenet_one_launch_every_activation(cm, port, batch):
     import torch
-    net = networks.fuse(networks.lenet5(batch=batch))
+    net = networks.fuse(networks.lenet5(batch=batch), conv_pool_macs=0)
     x = networks.make_input(net)
     want = cpu_buffers(net, x)
     networks.execute(net, OracleBackend(port), want)

@@ -98,8 +98,8 @@ def test_gemm_bias_fuses_in_every_derived_form():
     the forms the scheduler emits: a whole-tensor Add at one row, the bias row broadcast
     over n rows, and the row-strided form over gapped rows."""
     for batch in (1, 3):
-        f = networks.fuse(networks.lenet5(batch))
+        f = networks.fuse(networks.lenet5(batch), conv_pool_macs=0)
         assert [n[0] for n in f.nodes] == ["conv", "pool", "conv", "pool", "matmul", "matmul", "matmul"]
         assert [n[5] for n in f.nodes[4:]] == [3, 3, 2]
-    f = networks.fuse(networks.lenet5(3))
+    f = networks.fuse(networks.lenet5(3), conv_pool_macs=0)
     assert f.nodes[5][4] == (1, 120, 84, 3, 120, 0, 88)    # row-strided, rows 88 words apart
