@@ -1257,6 +1257,11 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
         dms.value, dcnt.value = wl.profile_dominant(cm, stream, K)
         dom_note = ("; GEMM launch durations from CUDA events around each launch over K eager passes right "
                     "after the timed region (which replays a CUDA graph)")
+    # the SM clock the GEMM launches themselves ran at (cycle counter / global timer of each
+    # launch's first CTA), over the same launches as the durations
+    gemm_mhz = C.c_double(0.0)
+    if wl.dominant == "gemm_q88" and L.cm_profile_gemm_clock(C.byref(gemm_mhz)) != 0:
+        gemm_mhz.value = 0.0
     elapsed_ms = env.reduce(elapsed_ms, "max")
     ms_per_step = elapsed_ms / K
     scale = 1e9 if name == "matmul" else 1.0
@@ -1280,7 +1285,8 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
         # clock the sampler saw.  The pipe's rate per clock is fixed, so the ceiling at the
         # GEMM's clock is the burst figure x run clock / probe clock: frac is the fraction
         # of the pipe's per-clock capacity, whatever the power cap does to the clock.
-        run_mhz = (clocks or {}).get("sm_mhz")
+        sampled_mhz = (clocks or {}).get("sm_mhz")
+        run_mhz = round(gemm_mhz.value, 1) if gemm_mhz.value > 0 else sampled_mhz
         probe_mhz = ceiling.get("ceiling_sm_mhz")
         scale_ = run_mhz / probe_mhz if run_mhz and probe_mhz else 1.0
         peak = round(burst * scale_, 1)
@@ -1288,7 +1294,9 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
                 "frac": round(achieved / peak, 4), "traffic": profile_traffic(f"gemm_q88:{name}"),
                 "kernel": "gemm_q88_kernel",
                 "peak_burst": burst, "frac_of_burst": round(achieved / burst, 4),
-                "peak_clock_scale": {"run_sm_mhz": run_mhz, "ceiling_sm_mhz": probe_mhz, "scale": round(scale_, 4)},
+                "peak_clock_scale": {"run_sm_mhz": run_mhz, "ceiling_sm_mhz": probe_mhz, "scale": round(scale_, 4),
+                                     "gemm_sm_mhz": round(gemm_mhz.value, 1) if gemm_mhz.value > 0 else None,
+                                     "sampled_sm_mhz": sampled_mhz},
                 "int8_ceiling": ceiling,
                 "int8_measured_tops": ceiling["cublaslt_int8_tops"],
                 "frac_of_cublaslt_int8": round(achieved / ceiling["cublaslt_int8_tops"], 4),
@@ -1297,8 +1305,9 @@ def measure(name: str, env: Env, K: int, W: int, detail: bool) -> dict | None:
                          "launches / their CUDA-event time on rank 0; peak_burst = the int8 tensor pipe's ceiling "
                          "measured in this run just before the timed region (cm_int8_mma_rate: the GEMM's MMA "
                          "stream on shared-memory-resident operands, best of CTA pairs and single CTAs, at the SM "
-                         "clock it reports); peak = that ceiling at the timed region's median SM clock (burst x "
-                         "run clock / probe clock: the pipe's per-clock capacity at the clock the power cap left); also "
+                         "clock it reports); peak = that ceiling at the SM clock the GEMM launches ran at (their "
+                         "own cycle counter over the global timer; the sampled median when absent): burst x run "
+                         "clock / probe clock, the pipe's per-clock capacity at the clock the power cap left; also "
                          f"against cuBLASLt's int8 GEMM (a library rate, not a ceiling) and 2 x the {peaks['source']} "
                          f"bf16 {'sustained' if which == 'bf16_sustained' else 'burst'} rate {peaks[which]} TF/s; "
                          "traffic = DRAM bytes of "

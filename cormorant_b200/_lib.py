@@ -37,6 +37,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_profile_begin": (C.c_int, []),
     "cm_profile_end": (C.c_int, []),
     "cm_profile_read": (C.c_int, [C.c_char_p, C.POINTER(C.c_double), C.POINTER(C.c_uint64)]),
+    "cm_profile_gemm_clock": (C.c_int, [C.POINTER(C.c_double)]),
     "cm_vectorop": (C.c_int, [_p, _p, _p] + [_u] * 5),
     "cm_vectorop_async": (C.c_int, [_p, _p, _p] + [_u] * 5 + [_p]),
     "cm_matmul": (C.c_int, [_p, _p, _p] + [_u] * 7),

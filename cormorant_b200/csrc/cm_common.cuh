@@ -45,6 +45,10 @@ void scratch_free(void* p, cudaStream_t s);
 // Opt-in device timing of the library's own launches: CUDA events recorded on
 // the launch stream around each kernel while profiling is on (cm_profile_*).
 enum ProfKind { PK_GEMM = 0, PK_SPLIT, PK_VECTOROP, PK_POOL, PK_CONV_AUX, PK_COUNT };
+// Device counters {SM cycles, nanoseconds} that GEMM launches add their CTA 0 span to while
+// profiling is on (cm_profile_begin .. cm_profile_end); nullptr otherwise.
+unsigned long long* prof_gemm_clock();
+
 struct ProfScope {
     int kind; cudaStream_t s; cudaEvent_t a = nullptr;
     ProfScope(int k, cudaStream_t st);

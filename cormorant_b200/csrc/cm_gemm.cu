@@ -338,6 +338,8 @@ struct GemmArgs {
     // both planes: win_bytes, the lo' plane win_plane bytes after the hi plane) and kernel
     // row r reads it win_roff*r bytes in; the packed weights (w_bytes) stay resident
     uint32_t win, win_stages, win_bytes, win_plane, win_roff, w_bytes, kh;
+    // profiling: CTA 0 adds its {SM cycles, ns} from start to exit here (prof_gemm_clock)
+    unsigned long long* clk;
 };
 
 struct Tile {
@@ -421,6 +423,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
     griddep_wait();
     griddep_launch_dependents();   // all CTAs are resident: the next kernel may launch now
+    uint64_t clk_c0 = 0, clk_t0 = 0;
+    if (g.clk && blockIdx.x == 0 && threadIdx.x == 0) { clk_c0 = clock64(); clk_t0 = gtimer(); }
     using C = Cfg<TBN, CG, WA>;
     static_assert(!WIN || (TBN == 64 && CG == 1 && !WA), "the window form runs packed 64-column tiles");
     constexpr int NBUF = C::NBUF;
@@ -1022,6 +1026,10 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
         }
     }
     __syncthreads();
+    if (g.clk && blockIdx.x == 0 && threadIdx.x == 0) {
+        atomicAdd(g.clk, (unsigned long long)(clock64() - clk_c0));
+        atomicAdd(g.clk + 1, (unsigned long long)(gtimer() - clk_t0));
+    }
     // a pair's CTAs read each other's shared memory and barriers until here
     if (CG == 2) cluster_sync_all();
     if (warp == 1) {
@@ -1560,6 +1568,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     g.fd_w = FastDiv(g.conv ? g.tiles_w : 1u);
     const unsigned clusters = (unsigned)std::min<uint64_t>(total, (uint64_t)per_sm_clusters);
     g.status = cx->status; g.timeout_ns = cx->timeout_ns;
+    g.clk = prof_gemm_clock();
     cudaError_t e;
     {
         ProfScope ps_(PK_GEMM, s);

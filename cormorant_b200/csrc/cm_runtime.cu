@@ -92,6 +92,16 @@ ProfScope::~ProfScope() {
     g_prof_pairs.push_back({kind, a, b});
 }
 
+// the GEMM clock counters live in the status buffer, after the status word
+static unsigned long long* gemm_clock_words() {
+    return g_ready ? (unsigned long long*)((char*)g_ctx.status + 64) : nullptr;
+}
+
+unsigned long long* prof_gemm_clock() {
+    std::lock_guard<std::mutex> lk(g_prof_mu);
+    return g_prof_on ? gemm_clock_words() : nullptr;
+}
+
 int scratch_alloc(void** p, size_t bytes, cudaStream_t s) {
     *p = nullptr;
     if (bytes == 0) return CM_OK;
@@ -210,7 +220,19 @@ int cm_profile_begin(void) {
     std::lock_guard<std::mutex> lk(g_prof_mu);
     for (auto& pp : g_prof_pairs) { g_prof_free.push_back(pp.a); g_prof_free.push_back(pp.b); }
     g_prof_pairs.clear();
+    if (gemm_clock_words()) cudaMemset(gemm_clock_words(), 0, 2 * sizeof(unsigned long long));
     g_prof_on = true;
+    return CM_OK;
+}
+
+int cm_profile_gemm_clock(double* sm_mhz) {
+    if (!sm_mhz) return set_error(CM_EINVAL, "cm_profile_gemm_clock: null result");
+    *sm_mhz = 0.0;
+    if (!g_ready) return set_error(CM_ENOINIT, "cm_profile_gemm_clock: cm_init has not been called");
+    unsigned long long w[2] = {0, 0};
+    cudaError_t e = cudaMemcpy(w, gemm_clock_words(), sizeof w, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_error(e, "cm_profile_gemm_clock");
+    *sm_mhz = w[1] ? (double)w[0] / (double)w[1] * 1000.0 : 0.0;
     return CM_OK;
 }
 

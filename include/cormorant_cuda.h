@@ -113,6 +113,11 @@ int cm_int8_mma_rate(unsigned pairs, unsigned iters, double* tops, double* ms, d
 int cm_profile_begin(void);
 int cm_profile_end(void);
 int cm_profile_read(const char* kernel, double* total_ms, uint64_t* launches);
+/* The mean SM clock (MHz) of the tensor-core GEMM launches since cm_profile_begin (each launch
+ * times its first CTA with the SM cycle counter and the global nanosecond timer); 0 if none
+ * ran.  Synchronizes the device.  A measurement aid with no reference counterpart: the GEMM's
+ * roofline divides by the int8 pipe's per-clock ceiling at this clock. */
+int cm_profile_gemm_clock(double* sm_mhz);
 
 /* ---- VectorOPKernel ----------------------------------------------------------
  * c[o*(a_inc+b_inc) + i] = op(a[o*a_inc + i], b[o*b_inc + i]),  o < outer, i < size.
