@@ -82,6 +82,33 @@ __global__ void __launch_bounds__(256) conv_epilogue_kernel(int16_t* __restrict_
 // (G a power of two <= 32) taking the kernel rows (c, r) = lane, lane + G, ...;
 // the int32 wrap sums meet by shuffle, bias << 8 is added, one narrowing
 // follows (ConvKernel.cpp:160-230).
+// One kernel row of a direct conv tap sum: sum over s < kw of x[iw0 + s*dw] * w[s] (taps
+// outside the input row add nothing).  Up to 8 taps issue all their loads before the first
+// multiply, so a row costs one memory round trip instead of one per tap.
+__device__ __forceinline__ uint32_t row_dot(const int16_t* __restrict__ xr, const int16_t* __restrict__ wr, int64_t iw0,
+                                            const DwArgs& a) {
+    uint32_t acc = 0;
+    if (a.kw <= 8) {
+        int32_t xv[8], wv[8];
+#pragma unroll
+        for (uint32_t s = 0; s < 8; ++s) {
+            const int64_t iw = iw0 + (int64_t)s * a.dw;
+            const bool ok = s < a.kw && iw >= 0 && iw < (int64_t)a.W;
+            xv[s] = ok ? (int32_t)__ldg(xr + iw) : 0;
+            wv[s] = s < a.kw ? (int32_t)__ldg(wr + s) : 0;
+        }
+#pragma unroll
+        for (uint32_t s = 0; s < 8; ++s) acc += (uint32_t)(xv[s] * wv[s]);
+    } else {
+        for (uint32_t s = 0; s < a.kw; ++s) {
+            const int64_t iw = iw0 + (int64_t)s * a.dw;
+            if (iw < 0 || iw >= (int64_t)a.W) continue;
+            acc += (uint32_t)((int32_t)__ldg(xr + iw) * (int32_t)__ldg(wr + s));
+        }
+    }
+    return acc;
+}
+
 __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restrict__ x, const int16_t* __restrict__ w,
                                                           const int16_t* __restrict__ bias, int16_t* __restrict__ y,
                                                           DwArgs a, uint64_t total, uint32_t G, uint32_t epi,
@@ -106,11 +133,7 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
             if (ih < 0 || ih >= (int64_t)a.H) continue;
             const int16_t* xr = x + ((n * a.C + c) * (uint64_t)a.H + (uint64_t)ih) * a.W;
             const int16_t* wr = w + (m * a.C + c) * (uint64_t)khw + (uint64_t)r * a.kw;
-            for (uint32_t s = 0; s < a.kw; ++s) {
-                const int64_t iw = (int64_t)ow * a.sw + (int64_t)s * a.dw - (int64_t)a.pl;
-                if (iw < 0 || iw >= (int64_t)a.W) continue;
-                acc += (uint32_t)((int32_t)__ldg(xr + iw) * (int32_t)__ldg(wr + s));
-            }
+            acc += row_dot(xr, wr, (int64_t)ow * a.sw - (int64_t)a.pl, a);
         }
         for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
         if (live && g == 0) {
@@ -164,11 +187,7 @@ __global__ void __launch_bounds__(256) conv_pool_direct_kernel(const int16_t* __
                 if (ih < 0 || ih >= (int64_t)a.H) continue;
                 const int16_t* xr = x + ((n * a.C + c) * (uint64_t)a.H + (uint64_t)ih) * a.W;
                 const int16_t* wr = w + (m * a.C + c) * (uint64_t)khw + (uint64_t)r * a.kw;
-                for (uint32_t s = 0; s < a.kw; ++s) {
-                    const int64_t iw = ow * a.sw + (int64_t)s * a.dw - (int64_t)a.pl;
-                    if (iw < 0 || iw >= (int64_t)a.W) continue;
-                    acc += (uint32_t)((int32_t)__ldg(xr + iw) * (int32_t)__ldg(wr + s));
-                }
+                acc += row_dot(xr, wr, ow * a.sw - (int64_t)a.pl, a);
             }
             for (uint32_t o = G / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
             if (in && g == 0) {

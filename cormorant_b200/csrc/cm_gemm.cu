@@ -1303,19 +1303,21 @@ __global__ void __launch_bounds__(256) matmul_direct_kernel(const int16_t* __res
 
 // The same products for a few rows (n <= NR): a block owns 32 consecutive output columns
 // of one batch step (grid (ceil(m / 32), batch)); lane = column, so each load of a B row
-// reads 32 adjacent words, the block's 8 warps take every 8th k, the A words are
-// broadcast loads, and each lane keeps one int32 wrap sum per row.  The 8 partial sums
-// meet in shared memory (wrap addition: order-free) and warp 0 narrows, adds the
-// epilogue and stores.  Batch steps run in parallel: their output slices do not overlap
+// reads 32 adjacent words, the block's kRowWarps warps take every kRowWarps-th k (32 warps:
+// a batch-1 layer's few blocks finish their k in few memory round trips), the A words are
+// broadcast loads, and each lane keeps one int32 wrap sum per row.  The partial sums meet in
+// shared memory (wrap addition: order-free) and warp 0 narrows, adds the epilogue and stores.  Batch steps run in parallel: their output slices do not overlap
 // (overlapping ones take the in-order loop before the direct path).
+constexpr uint32_t kRowWarps = 32;
+
 template <int NR>
-__global__ void __launch_bounds__(256) matmul_rows_direct_kernel(const int16_t* __restrict__ a,
+__global__ void __launch_bounds__(32 * kRowWarps) matmul_rows_direct_kernel(const int16_t* __restrict__ a,
                                                                  const int16_t* __restrict__ b, int16_t* __restrict__ c,
                                                                  uint32_t n, uint32_t k, uint32_t m, uint64_t a_bs,
                                                                  uint64_t b_bs, uint64_t c_bs, uint32_t epi,
                                                                  const int16_t* __restrict__ bias) {
     griddep_wait();
-    __shared__ uint32_t part[8][NR][32];
+    __shared__ uint32_t part[kRowWarps][NR][32];
     const uint32_t lane = threadIdx.x & 31u, w = threadIdx.x >> 5;
     const uint32_t j = blockIdx.x * 32u + lane;
     const uint64_t z = blockIdx.y;
@@ -1326,7 +1328,7 @@ __global__ void __launch_bounds__(256) matmul_rows_direct_kernel(const int16_t* 
     for (int r = 0; r < NR; ++r) acc[r] = 0;
     if (j < m) {
 #pragma unroll 4
-        for (uint32_t q = w; q < k; q += 8) {
+        for (uint32_t q = w; q < k; q += kRowWarps) {
             const int32_t bv = __ldg(B + (uint64_t)q * m);
 #pragma unroll
             for (int r = 0; r < NR; ++r)
@@ -1342,7 +1344,7 @@ __global__ void __launch_bounds__(256) matmul_rows_direct_kernel(const int16_t* 
             if ((uint32_t)r >= n) break;
             uint32_t s = part[0][r][lane];
 #pragma unroll
-            for (int x = 1; x < 8; ++x) s += part[x][r][lane];
+            for (int x = 1; x < (int)kRowWarps; ++x) s += part[x][r][lane];
             int32_t v = narrow_acc(s);
             if (epi & 2u) v = sat16(v + (int32_t)__ldg(bias + j));
             if (epi & 1u) v = max(v, 0);
@@ -1615,10 +1617,10 @@ void launch_matmul_direct(const Context* cx, const int16_t* a, const int16_t* b,
                           const int16_t* bias, cudaStream_t s) {
     if (n <= 8 && batch <= 65535u) {
         const dim3 grid((m + 31) / 32, batch);
-        if (n == 1) launch_k(matmul_rows_direct_kernel<1>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
-        else if (n == 2) launch_k(matmul_rows_direct_kernel<2>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
-        else if (n <= 4) launch_k(matmul_rows_direct_kernel<4>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
-        else launch_k(matmul_rows_direct_kernel<8>, grid, 256, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        if (n == 1) launch_k(matmul_rows_direct_kernel<1>, grid, 32 * kRowWarps, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else if (n == 2) launch_k(matmul_rows_direct_kernel<2>, grid, 32 * kRowWarps, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else if (n <= 4) launch_k(matmul_rows_direct_kernel<4>, grid, 32 * kRowWarps, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
+        else launch_k(matmul_rows_direct_kernel<8>, grid, 32 * kRowWarps, 0, s, a, b, c, n, k, m, a_bs, b_bs, c_bs, epi, bias);
         return;
     }
     const uint64_t total = (uint64_t)batch * n * m;
