@@ -591,7 +591,9 @@ class NetworkBench:
     def config(self, world):
         calls = ("reference call list, Conv->Relu" + (" and Conv->Add->Relu" if FUSE_RESIDUAL else "")
                  + " and Gemm(MatMul->Add)->Relu chains folded into cm_conv_fused / cm_matmul_fused"
-                 + ("; conv outputs read by convs written as plane images (cm_conv_planes)" if self.planes else "")
+                 + ("; launch-bound Conv->Relu->MaxPool chains as one cm_conv_pool" if not ONE_LAUNCH else "")
+                 + ("; conv outputs read by convs written as plane images (cm_conv_planes), channels-last outputs "
+                    "into the stem's max pool and the final global pool" if self.planes else "")
                  if self.fused else "reference call list, one C-ABI call per node")
         if self.which == "lenet":
             return {"workload": "lenet5 (BASELINE configs[0])", "batch": 1, "input": "1x1x28x28 uniform [0,1)",
