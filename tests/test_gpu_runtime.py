@@ -141,3 +141,31 @@ def test_int8_mma_rate(cm, pairs):
     _lib.check(L.cm_int8_mma_rate(pairs, 16, C.byref(tops), C.byref(ms), None))
     assert L.cm_int8_mma_rate(pairs, 0, C.byref(tops), C.byref(ms), None) == _lib.CM_EINVAL
     assert L.cm_int8_mma_rate(2, 16, C.byref(tops), C.byref(ms), None) == _lib.CM_EINVAL
+
+
+def test_profile_gemm_clock(cm):
+    """While profiling, tensor-core GEMM launches record the SM clock they ran at; without a
+    GEMM since cm_profile_begin the clock reads 0."""
+    import torch
+    from cormorant_b200 import _lib
+    L = _lib.lib()
+    mhz = C.c_double(-1.0)
+    _lib.check(L.cm_profile_begin())
+    _lib.check(L.cm_profile_end())
+    _lib.check(L.cm_profile_gemm_clock(C.byref(mhz)))
+    assert mhz.value == 0.0
+    n = k = m = 1024
+    a = torch.zeros(n * k, dtype=torch.int16, device="cuda")
+    c = torch.empty(n * m, dtype=torch.int16, device="cuda")
+    old = L.cm_set_direct_limit(0)                       # the tensor-core path
+    try:
+        _lib.check(L.cm_profile_begin())
+        for _ in range(3):
+            _lib.check(L.cm_matmul(C.c_void_p(a.data_ptr()), C.c_void_p(a.data_ptr()), C.c_void_p(c.data_ptr()),
+                                   n, k, m, 1, n * k, k * m, n * m))
+        _lib.check(L.cm_profile_end())
+        _lib.check(L.cm_profile_gemm_clock(C.byref(mhz)))
+    finally:
+        L.cm_set_direct_limit(old)
+    assert 300.0 < mhz.value < 2100.0, mhz.value
+    assert L.cm_profile_gemm_clock(None) == _lib.CM_EINVAL
