@@ -1296,30 +1296,32 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
     for (uint32_t item = threadIdx.x; item < rows * g.Ws; item += blockDim.x) {
         const uint32_t i = item / g.Ws, wv = item - i * g.Ws;
         const uint32_t hv = hv0 + i;
-        uint32_t hw[CPC / 4], lw[CPC / 4];
+        // the virtual pixel's words in channel order c2 = (th*S_ + tw)*C_ + c (x = 0 outside
+        // the image and past T_*C2), gathered first, then split four at a time with byte
+        // permutes: hi = the words' high bytes, lo' = their low bytes ^ 0x80
+        uint32_t v[CPC];
 #pragma unroll
-        for (uint32_t q = 0; q < CPC / 4; ++q) { hw[q] = 0; lw[q] = 0x80808080u; }
+        for (uint32_t c2 = T_ * C2; c2 < CPC; ++c2) v[c2] = 0;
 #pragma unroll
         for (uint32_t th = 0; th < (uint32_t)(T_ * S_); ++th) {   // th >= S_: stacked row hv + 1
             const int16_t* lrow = rowbuf + (S_ * i + th) * C_ * W;
-            int32_t sums[S_];
 #pragma unroll
             for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) {
                 const int32_t iw = (int32_t)(S_ * wv + tw) - (int32_t)g.pl;
                 const bool in = iw >= 0 && iw < (int32_t)W;
-                int32_t sum = 0;
 #pragma unroll
-                for (uint32_t c = 0; c < (uint32_t)C_; ++c) {
-                    const uint32_t c2 = (th * S_ + tw) * C_ + c;
-                    const int16_t v = in ? lrow[c * W + (uint32_t)iw] : (int16_t)0;
-                    sum += (int32_t)v - 128;
-                    const uint32_t q = c2 >> 2, sh = 8 * (c2 & 3);
-                    hw[q] |= (uint32_t)(uint8_t)(v >> 8) << sh;
-                    lw[q] = (lw[q] & ~(0xFFu << sh)) | ((((uint32_t)v & 255u) ^ 0x80u) << sh);
-                }
-                sums[tw] = sum;
+                for (uint32_t c = 0; c < (uint32_t)C_; ++c)
+                    v[(th * S_ + tw) * C_ + c] = in ? (uint32_t)(uint16_t)lrow[c * W + (uint32_t)iw] : 0u;
             }
             if (th < (uint32_t)S_ && !fused_rt) {
+                int32_t sums[S_];
+#pragma unroll
+                for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) {
+                    int32_t sum = -128 * C_;
+#pragma unroll
+                    for (uint32_t c = 0; c < (uint32_t)C_; ++c) sum += (int32_t)(int16_t)v[(th * S_ + tw) * C_ + c];
+                    sums[tw] = sum;
+                }
                 int32_t* so = So + ((uint64_t)n * g.Hpo + S_ * hv + th) * g.Wpo + S_ * wv;
                 if constexpr (S_ == 2) {
                     *(int2*)so = make_int2(sums[0], sums[1]);
@@ -1328,6 +1330,13 @@ __global__ void __launch_bounds__(kS2dRowThreads) conv_s2d_rows_kernel(const int
                     for (uint32_t tw = 0; tw < (uint32_t)S_; ++tw) so[tw] = sums[tw];
                 }
             }
+        }
+        uint32_t hw[CPC / 4], lw[CPC / 4];
+#pragma unroll
+        for (uint32_t q = 0; q < CPC / 4; ++q) {
+            const uint32_t p01 = v[4 * q] | (v[4 * q + 1] << 16), p23 = v[4 * q + 2] | (v[4 * q + 3] << 16);
+            hw[q] = __byte_perm(p01, p23, 0x7531);
+            lw[q] = __byte_perm(p01, p23, 0x6420) ^ 0x80808080u;
         }
         int8_t* dst = planes + (((uint64_t)n * g.Hs + hv) * g.Ws + wv) * g.Cp;
 #pragma unroll
