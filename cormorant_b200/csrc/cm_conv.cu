@@ -82,6 +82,19 @@ __global__ void __launch_bounds__(256) conv_epilogue_kernel(int16_t* __restrict_
 // (G a power of two <= 32) taking the kernel rows (c, r) = lane, lane + G, ...;
 // the int32 wrap sums meet by shuffle, bias << 8 is added, one narrowing
 // follows (ConvKernel.cpp:160-230).
+// q = a / b, r = a - q*b, in 32-bit arithmetic when both fit (a 64-bit division is a long
+// instruction sequence on the latency path of these small kernels).
+__device__ __forceinline__ void divmod64(uint64_t a, uint64_t b, uint64_t& q, uint64_t& r) {
+    if (((a | b) >> 32) == 0) {
+        const uint32_t q32 = (uint32_t)a / (uint32_t)b;
+        q = q32;
+        r = (uint32_t)a - q32 * (uint32_t)b;
+    } else {
+        q = a / b;
+        r = a - q * b;
+    }
+}
+
 // One kernel row of a direct conv tap sum: sum over s < kw of x[iw0 + s*dw] * w[s] (taps
 // outside the input row add nothing).  Up to 8 taps issue all their loads before the first
 // multiply, so a row costs one memory round trip instead of one per tap.
@@ -122,10 +135,11 @@ __global__ void __launch_bounds__(256) conv_direct_kernel(const int16_t* __restr
          t0 += stride) {
         const bool live = t0 < total;
         const uint64_t t = live ? t0 : 0;
-        const uint64_t plane = t / ohw;            // n * M + m
-        const uint64_t p = t - plane * ohw;
-        const uint64_t n = plane / a.M, m = plane - n * a.M;
-        const uint32_t oh = (uint32_t)(p / a.out_w), ow = (uint32_t)(p - (uint64_t)oh * a.out_w);
+        uint64_t plane, p, n, m, oh64, ow64;
+        divmod64(t, ohw, plane, p);                // plane = n * M + m
+        divmod64(plane, a.M, n, m);
+        divmod64(p, a.out_w, oh64, ow64);
+        const uint32_t oh = (uint32_t)oh64, ow = (uint32_t)ow64;
         uint32_t acc = 0;
         for (uint32_t kr = g; live && kr < rows; kr += G) {
             const uint32_t c = kr / a.kh, r = kr - c * a.kh;
@@ -169,10 +183,11 @@ __global__ void __launch_bounds__(256) conv_pool_direct_kernel(const int16_t* __
          t0 += stride) {
         const bool live = t0 < total;
         const uint64_t t = live ? t0 : 0;
-        const uint64_t plane = t / qhw;            // n * M + m
-        const uint64_t p = t - plane * qhw;
-        const uint64_t n = plane / a.M, m = plane - n * a.M;
-        const uint32_t qh = (uint32_t)(p / q.out_w), qw = (uint32_t)(p - (uint64_t)qh * q.out_w);
+        uint64_t plane, p, n, m, qh64, qw64;
+        divmod64(t, qhw, plane, p);                // plane = n * M + m
+        divmod64(plane, a.M, n, m);
+        divmod64(p, q.out_w, qh64, qw64);
+        const uint32_t qh = (uint32_t)qh64, qw = (uint32_t)qw64;
         int32_t best = -32768;
         for (uint32_t rd = 0; rd < tap_rounds; ++rd) {
             const uint32_t tap = slot + rd * T;
@@ -661,7 +676,8 @@ __device__ __forceinline__ void sums_reset_image(const SumsReset& z, uint32_t n,
 __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __restrict__ S, uint32_t Hp, uint32_t Wp,
                                                            uint32_t out_h, uint32_t out_w, uint32_t kh, uint32_t kw,
                                                            uint32_t sh, uint32_t sw, uint32_t dh, uint64_t total,
-                                                           int32_t* __restrict__ rowterm, SumsReset z) {
+                                                           int32_t* __restrict__ rowterm, SumsReset z, FastDiv fdP,
+                                                           FastDiv fdW) {
     griddep_wait();
     // blocks past the row-term grid clear the output image's sums, one image at a time
     if (z.S && blockIdx.x >= gridDim.x - z.nimg) {
@@ -670,9 +686,21 @@ __global__ void __launch_bounds__(256) conv_rowterm_kernel(const int32_t* __rest
     }
     const uint64_t nthreads = (uint64_t)(gridDim.x - (z.S ? z.nimg : 0)) * blockDim.x;
     const uint64_t P = (uint64_t)out_h * out_w;
+    const bool small = total < (1ull << 32);
     for (uint64_t t = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += nthreads) {
-        const uint64_t n = t / P, p = t - n * P;
-        const uint32_t oh = (uint32_t)(p / out_w), ow = (uint32_t)(p - (uint64_t)oh * out_w);
+        // multiply-high divisions when the index fits 32 bits (a 64-bit division costs more
+        // than the rest of this thread's work)
+        uint64_t n, p;
+        uint32_t oh, ow;
+        if (small) {
+            const uint32_t n32 = fdP.div((uint32_t)t), p32 = (uint32_t)t - n32 * (uint32_t)P;
+            oh = fdW.div(p32);
+            ow = p32 - oh * out_w;
+            n = n32; p = p32;
+        } else {
+            n = t / P; p = t - n * P;
+            oh = (uint32_t)(p / out_w); ow = (uint32_t)(p - (uint64_t)oh * out_w);
+        }
         const int32_t* b = S + ((uint64_t)n * Hp + (uint64_t)oh * sh) * Wp + (uint64_t)ow * sw;
         uint32_t sum = 0;
         if (kh <= 3 && kw <= 3) {
@@ -738,7 +766,9 @@ void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t W
                     uint32_t kh, uint32_t kw, uint32_t sh, uint32_t sw, uint32_t dh, uint32_t nb, int32_t* rt,
                     cudaStream_t s, SumsReset z = SumsReset{}) {
     const uint64_t need_bytes = ((uint64_t)(out_w - 1) * sw + kw) * 4 * (kRowtermThreads / 32);
-    if (out_w >= 16 && need_bytes <= 48u * 1024u) {
+    // up to 3 x 3 taps the per-output kernel issues all of an output's loads at once; the
+    // separable form pays off for larger windows
+    if (out_w >= 16 && need_bytes <= 48u * 1024u && (kh > 3 || kw > 3)) {
         for (uint32_t b0 = 0; b0 < nb; b0 += 65535u) {
             const uint32_t bz = std::min(65535u, nb - b0);
             SumsReset zb = z;
@@ -751,7 +781,8 @@ void rowterm_launch(const Context* cx, const int32_t* S, uint32_t Hp, uint32_t W
         const uint64_t tot = (uint64_t)nb * out_h * out_w;
         if (z.S) z.nimg = nb;
         launch_k(conv_rowterm_kernel, grid_for(cx, tot, 256, 8) + (z.S ? nb : 0u), 256, 0, s, S, Hp, Wp, out_h, out_w, kh, kw, sh,
-                                                                                        sw, dh, tot, rt, z);
+                                                                                        sw, dh, tot, rt, z,
+                 FastDiv((uint32_t)std::min<uint64_t>((uint64_t)out_h * out_w, 0xFFFFFFFFull)), FastDiv(out_w));
         count_launch();
     }
 }
