@@ -567,7 +567,7 @@ __global__ void __launch_bounds__(256) pool_max_planes_kernel(const int8_t* __re
 // (identity -32768: a window with no tap in the image gives it, as the NCHW pool does),
 // then the hi / lo' split and the group's channel sum, the pixel's sum combined over its
 // groups by shuffles and stored once (no atomics).  Channels past C hold x = 0.
-__global__ void __launch_bounds__(256) pool_max_nhwc_planes_kernel(const int16_t* __restrict__ x,
+__global__ void __launch_bounds__(256, 4) pool_max_nhwc_planes_kernel(const int16_t* __restrict__ x,
                                                                    int8_t* __restrict__ yout, int32_t* __restrict__ yS,
                                                                    PoolPlanesGeo g, uint64_t total, uint32_t g_log,
                                                                    FastDiv fd_ow, FastDiv fd_oh) {

@@ -1168,8 +1168,7 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restri
         if (((uintptr_t)s & 15u) == 0) {
             const uint32_t nv = K / 8;
             const uint4* s4 = (const uint4*)s;
-            for (uint32_t i = lane; i < nv; i += 32) {
-                const uint4 v = __ldcs(s4 + i);
+            auto one = [&](const uint4& v, uint32_t i) {
                 uint2 h, l;
                 h.x = __byte_perm(v.x, v.y, 0x7531);
                 h.y = __byte_perm(v.z, v.w, 0x7531);
@@ -1178,7 +1177,18 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const int16_t* __restri
                 *(uint2*)(dh + 8 * (uint64_t)i) = h;
                 *(uint2*)(dl + 8 * (uint64_t)i) = l;
                 sum += word_sum_minus128(v.x) + word_sum_minus128(v.y) + word_sum_minus128(v.z) + word_sum_minus128(v.w);
+            };
+            // four 16-byte loads in flight per lane before their first use (one memory round
+            // trip per 128 pieces of the row instead of per 32)
+            uint32_t i = lane;
+            for (; i + 96 < nv; i += 128) {
+                uint4 v[4];
+#pragma unroll
+                for (uint32_t u = 0; u < 4; ++u) v[u] = __ldcs(s4 + i + 32 * u);
+#pragma unroll
+                for (uint32_t u = 0; u < 4; ++u) one(v[u], i + 32 * u);
             }
+            for (; i < nv; i += 32) one(__ldcs(s4 + i), i);
             k_done = nv * 8;
         }
         for (uint32_t k = k_done + lane; k < K; k += 32) {
