@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple] = {
     "cm_synchronize": (C.c_int, [_p]),
     "cm_launch_count": (C.c_uint64, []),
     "cm_set_direct_limit": (C.c_uint64, [C.c_uint64]),
+    "cm_set_gemm_split": (C.c_int, [C.c_int]),
     "cm_version": (C.c_char_p, []),
     "cm_selftest_wait_timeout": (C.c_int, [_u]),
     "cm_int8_mma_rate": (C.c_int, [_u, _u, C.POINTER(C.c_double), C.POINTER(C.c_double), C.POINTER(C.c_double)]),

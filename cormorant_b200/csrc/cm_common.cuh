@@ -29,7 +29,15 @@ struct Context {
     // implicit-GEMM convs with packed weights read one input window per K block
     // (CM_CONV_WINDOW=0 at cm_init turns it off)
     int conv_window = 1;
+    // K-split GEMM units for grids of few tiles: -1 = chosen per launch, 0 / 1 = never,
+    // k >= 2 = k units per tile whenever the K blocks allow (CM_GEMM_SPLIT at cm_init,
+    // cm_set_gemm_split)
+    int gemm_split = -1;
+    // per (tile, CTA, epilogue warp) arrival counters of K-split launches: zero between
+    // launches (the last arrival resets its counter; cleared again after a failed launch)
+    uint32_t* split_cnt = nullptr;
 };
+constexpr uint32_t kSplitCounters = 1u << 16;
 
 Context* ctx();                      // nullptr before cm_init
 int set_error(int code, const char* fmt, ...);

@@ -340,6 +340,14 @@ struct GemmArgs {
     uint32_t win, win_stages, win_bytes, win_plane, win_roff, w_bytes, kh;
     // profiling: CTA 0 adds its {SM cycles, ns} from start to exit here (prof_gemm_clock)
     unsigned long long* clk;
+    // K-split (splits > 1; set by launch_persistent, 1 otherwise): work unit u is K blocks
+    // [sp*num_kb/splits, (sp+1)*num_kb/splits) of tile u / splits, sp = u % splits.  Its
+    // raw product sums go to slab (tile, CTA of the pair, sp) of ws, TBN columns of BM
+    // int32 each; cnt counts the slabs landed per (tile, CTA, epilogue warp)
+    uint32_t splits;
+    FastDiv fd_split;
+    int32_t* ws;
+    uint32_t* cnt;
 };
 
 struct Tile {
@@ -386,6 +394,39 @@ __device__ __forceinline__ Tile decode_tile(const GemmArgs& g, uint64_t t, uint3
     return c;
 }
 
+// Work unit u: its tile and its share [kb0, kb1) of the tile's K blocks.
+struct Unit {
+    uint32_t t, sp, kb0, kb1;
+};
+template <bool KS>
+__device__ __forceinline__ Unit decode_unit(const GemmArgs& g, uint64_t u) {
+    if constexpr (!KS) return Unit{(uint32_t)u, 0u, 0u, g.num_kb};
+    Unit r;
+    const uint32_t u32 = (uint32_t)u;               // units < 2^32 (checked at launch)
+    r.t = g.fd_split.div(u32);
+    r.sp = u32 - r.t * g.fd_split.d;
+    r.kb0 = g.fd_split.div(r.sp * g.num_kb);
+    r.kb1 = g.fd_split.div((r.sp + 1u) * g.num_kb);
+    return r;
+}
+
+// Column terms of output columns col0 .. col0+15 (0 past the last column): four 16-byte
+// loads for a full, aligned chunk.
+__device__ __forceinline__ void load_colterms(const int32_t* ct, uint32_t col0, uint32_t cols, uint32_t (&cv)[16]) {
+    if (col0 + 16u <= cols && ((uintptr_t)(ct + col0) & 15u) == 0) {
+        const int4* c4 = (const int4*)(ct + col0);
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+            const int4 x = __ldg(c4 + v);
+            cv[4 * v] = (uint32_t)x.x; cv[4 * v + 1] = (uint32_t)x.y;
+            cv[4 * v + 2] = (uint32_t)x.z; cv[4 * v + 3] = (uint32_t)x.w;
+        }
+    } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) cv[k] = col0 + k < cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
+    }
+}
+
 // Output pixel (n, oh, ow) of tile row i of a conv tile: rows are (image, row, column),
 // or (row, image, column) in the window form.
 __device__ __forceinline__ void conv_pixel(const GemmArgs& g, const Tile& tc, uint32_t i, uint32_t& n, uint32_t& oh,
@@ -418,7 +459,7 @@ __device__ __forceinline__ void conv_pixel(const GemmArgs& g, const Tile& tc, ui
 // single-CTA kernel is bound by.  All TMA completions and epilogue releases go to the
 // even CTA's barriers; its MMA commits arrive on both CTAs' barriers (multicast
 // commit).  No TMA multicast is used.
-template <int TBN, int CG, bool WA = false, bool WIN = false>
+template <int TBN, int CG, bool WA = false, bool WIN = false, bool KS = false>
 __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     gemm_q88_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs g) {
     griddep_wait();
@@ -427,6 +468,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     if (g.clk && blockIdx.x == 0 && threadIdx.x == 0) { clk_c0 = clock64(); clk_t0 = gtimer(); }
     using C = Cfg<TBN, CG, WA>;
     static_assert(!WIN || (TBN == 64 && CG == 1 && !WA), "the window form runs packed 64-column tiles");
+    static_assert(!KS || (!WA && !WIN), "K-split units run the row-major epilogue");
     constexpr int NBUF = C::NBUF;
     constexpr uint32_t HALF = TBN / (C::EPI_WARPS / 4);  // columns per epilogue warp
     constexpr uint32_t CW = 16;                           // columns per TMEM load
@@ -453,7 +495,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
     const uint32_t rank = CG == 2 ? cluster_rank() : 0u;
     const bool leader = rank == 0;
     const uint64_t cid = blockIdx.x / CG, ncl = gridDim.x / CG;
-    const uint64_t total = (uint64_t)g.batch * g.tiles_mc * g.tiles_n;
+    // work units: tiles x K-split units per tile (1 but for K-split launches)
+    const uint64_t total = (uint64_t)g.batch * g.tiles_mc * g.tiles_n * (KS ? g.splits : 1u);
     constexpr uint16_t kPairMask = 0x3;
 
     if (threadIdx.x == 0) {
@@ -521,8 +564,13 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
         if (lane == 0) {
             uint32_t it = 0;
             for (uint64_t t = cid; t < total && !*abort_flag; t += ncl) {
-                const Tile tc = decode_tile<TBN, CG>(g, t, rank);
-                for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
+                uint32_t tt = 0, kb_lo = 0, kb_hi = 0;    // K-split: this unit's tile and K blocks
+                if constexpr (KS) {
+                    const Unit un = decode_unit<true>(g, t);
+                    tt = un.t; kb_lo = un.kb0; kb_hi = un.kb1;
+                }
+                const Tile tc = decode_tile<TBN, CG>(g, KS ? (uint64_t)tt : t, rank);
+                for (uint32_t kb = KS ? kb_lo : 0u; kb < (KS ? kb_hi : g.num_kb); ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(smem_u32(&empty_b[s]), (round & 1u) ^ 1u, wc)) break;
                     uint8_t* st = stg + s * STAGE_B;
@@ -600,7 +648,12 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                 if (!mbar_wait(smem_u32(&acce_b[buf]), (use & 1u) ^ 1u, wc)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + buf * C::ACC_COLS;
-                for (uint32_t kb = 0; kb < g.num_kb; ++kb, ++it) {
+                uint32_t kb_lo = 0, kb_hi = 0;            // K-split: this unit's K blocks
+                if constexpr (KS) {
+                    const Unit un = decode_unit<true>(g, t);
+                    kb_lo = un.kb0; kb_hi = un.kb1;
+                }
+                for (uint32_t kb = KS ? kb_lo : 0u; kb < (KS ? kb_hi : g.num_kb); ++kb, ++it) {
                     const uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(smem_u32(&full_b[s]), round & 1u, wc)) { ok = false; break; }
                     tc_fence_after();
@@ -613,7 +666,7 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                         if (kk >= steps) break;
                         const uint64_t ah = sdesc(a0 + kk * 32), al = sdesc(a0 + PLANE_TILE + kk * 32);
                         const uint64_t bhl = sdesc_n(b0 + kk * 32 * 128);   // 32 K rows x [Bh | Bl]
-                        const uint32_t acc = (kb | kk) != 0u;
+                        const uint32_t acc = KS ? (uint32_t)(((kb - kb_lo) | kk) != 0u) : (uint32_t)((kb | kk) != 0u);
                         if (WA) {
                             // weights (A) x [hi pixels | lo' pixels] (B, 256 K-major rows)
                             umma_i8(d, sdesc(b0 + kk * 32), ah, C::IDESC, acc);
@@ -828,7 +881,8 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             // Everything that does not depend on the accumulator is fetched before the
             // wait, while the tile's MMAs run: the row's output offset, its row term and
             // the epilogue's addends (residual words or the bias row), packed in pairs.
-            const Tile tc = decode_tile<TBN, CG>(g, t, rank);
+            const Unit un = decode_unit<KS>(g, t);
+            const Tile tc = decode_tile<TBN, CG>(g, KS ? (uint64_t)un.t : t, rank);
             bool valid;
             uint64_t rt_idx, o_off;
             if (g.conv) {
@@ -899,38 +953,63 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             // and packed two int16 per word (even column in the low half).
             uint32_t pk[HALF / 2];
             const uint32_t tl = tmem + buf * C::ACC_COLS + ((quarter * 32u) << 16) + cbase;
+            if constexpr (KS) {
+                // the raw product sums 2^16*HH + 2^8*(HL + LH) + LL of this unit's K blocks into
+                // its slab (column-major, so that a warp's stores are 128-byte runs of rows)
+                int32_t* slab = g.ws + (((uint64_t)un.t * CG + rank) * g.splits + un.sp) * (uint64_t)(TBN * BM) + i;
 #pragma unroll
-            for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
-                const uint32_t col0 = tc.n0 + cbase + c0;
-                if (col0 < g.cols) {
-                    uint32_t p[CW], q[CW], cv[CW];
-                    tmem_ld16(tl + c0, p);
-                    tmem_ld16(tl + TBN + c0, q);
-                    // column terms: four 16-byte loads for a full, aligned chunk
-                    if (col0 + CW <= g.cols && ((uintptr_t)(ct + col0) & 15u) == 0) {
-                        const int4* c4 = (const int4*)(ct + col0);
+                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
+                    if (tc.n0 + cbase + c0 < g.cols) {
+                        uint32_t p[CW], q[CW];
+                        tmem_ld16(tl + c0, p);
+                        tmem_ld16(tl + TBN + c0, q);
+                        tmem_ld_wait();
 #pragma unroll
-                        for (int v = 0; v < (int)CW / 4; ++v) {
-                            const int4 x = __ldg(c4 + v);
-                            cv[4 * v] = (uint32_t)x.x; cv[4 * v + 1] = (uint32_t)x.y;
-                            cv[4 * v + 2] = (uint32_t)x.z; cv[4 * v + 3] = (uint32_t)x.w;
-                        }
-                    } else {
+                        for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
+                        tmem_ld16(tl + 2 * TBN + c0, q);
+                        tmem_ld_wait();
 #pragma unroll
-                        for (int k = 0; k < (int)CW; ++k) cv[k] = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
+                        for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] + q[k]) << 8;
+                        tmem_ld16(tl + 3 * TBN + c0, q);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k) __stcg(slab + (uint64_t)(cbase + c0 + k) * BM, (int)(p[k] + q[k]));
                     }
-                    tmem_ld_wait();
+                }
+            } else {
 #pragma unroll
-                    for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
-                    tmem_ld16(tl + 2 * TBN + c0, q);
-                    tmem_ld_wait();
+                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
+                    const uint32_t col0 = tc.n0 + cbase + c0;
+                    if (col0 < g.cols) {
+                        uint32_t p[CW], q[CW], cv[CW];
+                        tmem_ld16(tl + c0, p);
+                        tmem_ld16(tl + TBN + c0, q);
+                        // column terms: four 16-byte loads for a full, aligned chunk
+                        if (col0 + CW <= g.cols && ((uintptr_t)(ct + col0) & 15u) == 0) {
+                            const int4* c4 = (const int4*)(ct + col0);
 #pragma unroll
-                    for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] + q[k]) << 8;
-                    tmem_ld16(tl + 3 * TBN + c0, q);
-                    tmem_ld_wait();
+                            for (int v = 0; v < (int)CW / 4; ++v) {
+                                const int4 x = __ldg(c4 + v);
+                                cv[4 * v] = (uint32_t)x.x; cv[4 * v + 1] = (uint32_t)x.y;
+                                cv[4 * v + 2] = (uint32_t)x.z; cv[4 * v + 3] = (uint32_t)x.w;
+                            }
+                        } else {
 #pragma unroll
-                    for (int k = 0; k < (int)CW; k += 2)
-                        pk[(c0 + k) / 2] = narrow_pack(p[k] + q[k] + rt + cv[k], p[k + 1] + q[k + 1] + rt + cv[k + 1]);
+                            for (int k = 0; k < (int)CW; ++k) cv[k] = col0 + k < g.cols ? (uint32_t)__ldg(ct + col0 + k) : 0u;
+                        }
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] << 8) + q[k];
+                        tmem_ld16(tl + 2 * TBN + c0, q);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k) p[k] = (p[k] + q[k]) << 8;
+                        tmem_ld16(tl + 3 * TBN + c0, q);
+                        tmem_ld_wait();
+#pragma unroll
+                        for (int k = 0; k < (int)CW; k += 2)
+                            pk[(c0 + k) / 2] = narrow_pack(p[k] + q[k] + rt + cv[k], p[k + 1] + q[k + 1] + rt + cv[k + 1]);
+                    }
                 }
             }
             tc_fence_before();
@@ -938,6 +1017,40 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
             if (lane == 0) {                                      // buffer free for the next tile
                 if (CG == 2) mbar_arrive_cluster(map_to_rank(smem_u32(&acce_b[buf]), 0));
                 else mbar_arrive(smem_u32(&acce_b[buf]));
+            }
+            if constexpr (KS) {
+                // The warp whose slab completes the tile's set adds the slabs up (int32 wrap:
+                // exact in any order) and finishes the tile; the others are done with it.
+                // Nothing waits: the slabs are published by a fence before the counter.
+                __threadfence();
+                __syncwarp();
+                uint32_t last = 0;
+                if (lane == 0) {
+                    uint32_t* cnt = g.cnt + ((uint64_t)un.t * CG + rank) * C::EPI_WARPS + (warp - 2);
+                    last = atomicAdd(cnt, 1u) == g.splits - 1u ? 1u : 0u;
+                    if (last) atomicExch(cnt, 0u);                // zero again for the next launch
+                }
+                last = __shfl_sync(0xFFFFFFFFu, last, 0);
+                if (!last) continue;
+                __threadfence();
+#pragma unroll
+                for (uint32_t c0 = 0; c0 < HALF; c0 += CW) {
+                    const uint32_t col0 = tc.n0 + cbase + c0;
+                    if (col0 < g.cols) {
+                        uint32_t a[CW], cv[CW];
+                        load_colterms(ct, col0, g.cols, cv);
+                        const int32_t* sl =
+                            g.ws + ((uint64_t)un.t * CG + rank) * g.splits * (uint64_t)(TBN * BM) + (uint64_t)(cbase + c0) * BM + i;
+#pragma unroll
+                        for (int k = 0; k < (int)CW; ++k) a[k] = rt + cv[k];
+                        for (uint32_t sp = 0; sp < g.splits; ++sp, sl += TBN * BM) {
+#pragma unroll
+                            for (int k = 0; k < (int)CW; ++k) a[k] += (uint32_t)__ldcg(sl + (uint64_t)k * BM);
+                        }
+#pragma unroll
+                        for (int k = 0; k < (int)CW; k += 2) pk[(c0 + k) / 2] = narrow_pack(a[k], a[k + 1]);
+                    }
+                }
             }
             if (!valid) continue;
             // VectorOP ADD (saturating) and RELU on both halfwords of each pair
@@ -1540,20 +1653,41 @@ __global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __res
     }
 }
 
+// K-split units per tile for a launch of `tiles` tiles of num_kb K blocks on `slots`
+// resident CTAs (pairs): as many units as keep the grid to one wave (at most 4, each of at
+// least 4 K blocks), and none if that is fewer than 2.  Measured on ResNet-18's 3x3 convs
+// (plane image in and out, back-to-back launches): 32 images' 7x7x512 conv, 32 pair tiles
+// on 74 pairs, 29.7 -> 25.6 us with 2 units per tile; every split that made a second wave
+// was slower (14x14x256 at 64 images, 98 pair tiles: 33.9 us unsplit, 39.4-62.2 us split 2-4
+// ways) -- a unit's pipeline fill, accumulator drain and slab traffic cost more than the
+// idle slots of a partly filled last wave.
+uint32_t pick_splits(const Context* cx, uint64_t tiles, uint32_t num_kb, uint32_t slots, uint64_t counters_per_tile) {
+    if (cx->gemm_split == 0 || cx->gemm_split == 1 || !cx->split_cnt || slots == 0 || tiles == 0) return 1;
+    if (tiles * counters_per_tile > kSplitCounters) return 1;
+    if (cx->gemm_split > 1) return std::max(1u, std::min<uint32_t>((uint32_t)cx->gemm_split, num_kb / 2));
+    const uint64_t S = std::min<uint64_t>({4u, slots / tiles, num_kb / 4u});
+    return S >= 2 ? (uint32_t)S : 1u;
+}
+
 template <int TBN, int CG, bool WA = false, bool WIN = false>
 int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs& g, cudaStream_t s,
                       size_t win_smem = 0) {
     static int per_sm_clusters = -1;   // co-resident clusters of CG CTAs (one CTA per SM)
     // the window form's shared memory depends on the call (resident weights + windows)
     const size_t smem = WIN ? win_smem : (size_t)Cfg<TBN, CG, WA>::SMEM_LAUNCH;
+    // the K-split variant (row-major epilogue forms only; otherwise the same kernel twice)
+    constexpr bool CAN_KS = !WA && !WIN;
+    const auto kern_one = gemm_q88_kernel<TBN, CG, WA, WIN, false>;
+    const auto kern_ks = gemm_q88_kernel<TBN, CG, WA, WIN, CAN_KS>;
     if (per_sm_clusters < 0) {
-        cudaError_t e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA, WIN>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             WIN ? SMEM_BYTES : Cfg<TBN, CG, WA>::SMEM_LAUNCH);
-        if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+        for (const auto kf : {kern_one, kern_ks}) {
+            cudaError_t e = cudaFuncSetAttribute(kf, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 WIN ? SMEM_BYTES : Cfg<TBN, CG, WA>::SMEM_LAUNCH);
+            if (e != cudaSuccess) return cuda_error(e, "cudaFuncSetAttribute(gemm)");
+            if (CG > 1) cudaFuncSetAttribute(kf, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        }
         int n = cx->sm_count / CG;
         if (CG > 1) {
-            e = cudaFuncSetAttribute(gemm_q88_kernel<TBN, CG, WA, WIN>, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
             cudaLaunchConfig_t q{};
             q.gridDim = dim3(CG * n);
             q.blockDim = dim3(Cfg<TBN, CG, WA>::THREADS);
@@ -1563,7 +1697,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             at.val.clusterDim.x = CG; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
             q.attrs = &at; q.numAttrs = 1;
             int m = 0;
-            if (cudaOccupancyMaxActiveClusters(&m, gemm_q88_kernel<TBN, CG, WA, WIN>, &q) == cudaSuccess && m > 0) n = m;
+            if (cudaOccupancyMaxActiveClusters(&m, kern_one, &q) == cudaSuccess && m > 0) n = m;
             cudaGetLastError();
         }
         per_sm_clusters = n;
@@ -1578,14 +1712,26 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     g.fd_group = FastDiv(GROUP_M * g.tiles_n);
     g.fd_hw = FastDiv(g.conv ? g.tiles_w * g.tiles_h : 1u);
     g.fd_w = FastDiv(g.conv ? g.tiles_w : 1u);
-    const unsigned clusters = (unsigned)std::min<uint64_t>(total, (uint64_t)per_sm_clusters);
+    g.splits = 1; g.fd_split = FastDiv(1u); g.ws = nullptr; g.cnt = nullptr;
+    if (CAN_KS) {
+        const uint32_t S = pick_splits(cx, total, g.num_kb, (uint32_t)per_sm_clusters,
+                                       (uint64_t)CG * Cfg<TBN, CG, WA>::EPI_WARPS);
+        if (S > 1 && total * S < (1ull << 32)) {
+            const int rc = scratch_alloc((void**)&g.ws, (size_t)total * CG * S * TBN * BM * sizeof(int32_t), s);
+            if (rc) return rc;
+            g.splits = S; g.fd_split = FastDiv(S); g.cnt = cx->split_cnt;
+        }
+    }
+    const uint64_t units = total * g.splits;
+    const unsigned clusters = (unsigned)std::min<uint64_t>(units, (uint64_t)per_sm_clusters);
+    const auto kern = g.splits > 1 ? kern_ks : kern_one;
     g.status = cx->status; g.timeout_ns = cx->timeout_ns;
     g.clk = prof_gemm_clock();
     cudaError_t e;
     {
         ProfScope ps_(PK_GEMM, s);
         if (CG == 1) {
-            launch_k(gemm_q88_kernel<TBN, CG, WA, WIN>, clusters, Cfg<TBN, CG, WA>::THREADS, smem, s, ta, tb, g);
+            launch_k(kern, clusters, Cfg<TBN, CG, WA>::THREADS, smem, s, ta, tb, g);
             e = cudaGetLastError();
         } else {
             cudaLaunchConfig_t q{};
@@ -1599,9 +1745,10 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
             at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
             at[1].val.programmaticStreamSerializationAllowed = g_pdl ? 1 : 0;
             q.attrs = at; q.numAttrs = 2;
-            e = cudaLaunchKernelEx(&q, gemm_q88_kernel<TBN, CG, WA, WIN>, ta, tb, g);
+            e = cudaLaunchKernelEx(&q, kern, ta, tb, g);
         }
     }
+    if (g.ws) scratch_free(g.ws, s);
     count_launch();
     return e == cudaSuccess ? CM_OK : cuda_error(e, "gemm launch");
 }

@@ -57,6 +57,8 @@ int finish_sync(cm_stream_t stream) {
     if (st != 0) {
         const int zero = 0;
         cudaMemcpy(g_ctx.status, &zero, sizeof(int), cudaMemcpyHostToDevice);
+        // a K-split GEMM that wound down early leaves some arrival counters raised
+        if (g_ctx.split_cnt) cudaMemset(g_ctx.split_cnt, 0, kSplitCounters * sizeof(uint32_t));
         return set_error(st, "device-side status %d (%s)", st, cm_strerror(st));
     }
     return CM_OK;
@@ -156,6 +158,7 @@ int cm_init(const char* instance) {
     if (g_ready) {
         cudaSetDevice(g_ctx.device);
         cudaFree(g_ctx.status);
+        cudaFree(g_ctx.split_cnt);
         if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
         g_ready = false;
     }
@@ -171,6 +174,12 @@ int cm_init(const char* instance) {
     e = cudaMalloc(&c.status, 256);
     if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(status)");
     cudaMemset(c.status, 0, 256);
+    e = cudaMalloc(&c.split_cnt, kSplitCounters * sizeof(uint32_t));
+    if (e != cudaSuccess) {
+        cudaFree(c.status);
+        return cuda_error(e, "cudaMalloc(split counters)");
+    }
+    cudaMemset(c.split_cnt, 0, kSplitCounters * sizeof(uint32_t));
     // Keep freed scratch cached in the pool instead of returning it to the OS.
     cudaMemPool_t pool;
     if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
@@ -189,11 +198,14 @@ int cm_init(const char* instance) {
     if (mo && *mo) c.matmul_overlap = atoi(mo) != 0;
     const char* cw = getenv("CM_CONV_WINDOW");
     if (cw && *cw) c.conv_window = atoi(cw) != 0;
+    const char* gs = getenv("CM_GEMM_SPLIT");
+    if (gs && *gs) c.gemm_split = atoi(gs);
     const char* pd = getenv("CM_PDL");
     g_pdl = (pd && *pd) ? (atoi(pd) != 0) : 1;
     e = cudaStreamCreateWithFlags(&c.aux_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         cudaFree(c.status);
+        cudaFree(c.split_cnt);
         return cuda_error(e, "cudaStreamCreate(aux)");
     }
     g_ctx = c;
@@ -207,6 +219,7 @@ int cm_release(void) {
     cudaSetDevice(g_ctx.device);
     cudaDeviceSynchronize();
     cudaFree(g_ctx.status);
+    cudaFree(g_ctx.split_cnt);
     if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
     g_ready = false;
     return CM_OK;
@@ -269,6 +282,13 @@ uint64_t cm_set_direct_limit(uint64_t macs) {
     std::lock_guard<std::mutex> lk(g_mu);
     const uint64_t old = g_ctx.direct_max_macs;
     g_ctx.direct_max_macs = macs;
+    return old;
+}
+
+int cm_set_gemm_split(int splits) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    const int old = g_ctx.gemm_split;
+    g_ctx.gemm_split = splits < 0 ? -1 : splits;
     return old;
 }
 

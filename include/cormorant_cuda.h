@@ -84,6 +84,13 @@ uint64_t cm_launch_count(void);               /* kernels launched by this librar
  * the CM_DIRECT_MAX_MACS environment variable at cm_init; 0 = never).  Returns the
  * previous limit.  No reference counterpart; both paths are bit-exact. */
 uint64_t cm_set_direct_limit(uint64_t macs);
+/* K-split tensor-core GEMMs: a launch whose tiles fill at most half the SMs (CTA pairs)
+ * divides each tile's K blocks among 2-4 units that add up exactly (int32 wrap).
+ * splits < 0: chosen per launch (default, or the CM_GEMM_SPLIT environment variable at
+ * cm_init); 0 or 1: never; k >= 2: k units per tile whenever the tile has at least 2k K
+ * blocks.  Returns the previous setting.  No reference counterpart; every setting is
+ * bit-exact. */
+int cm_set_gemm_split(int splits);
 const char* cm_version(void);
 
 /* ---- failure-path self test (no reference counterpart) ------------------------

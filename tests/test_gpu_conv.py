@@ -320,3 +320,47 @@ def test_one_launch_conv_and_pool_match_entries(cm, port, case, epi):
     kernels.RunCalls(arr)
     assert_same(host(y2), host(y1), f"one-launch conv {case} epi {epi}")
     assert_same(host(p2), host(p1), f"one-launch pool after {case}")
+
+
+# K-split tensor-core GEMMs: a tile's K blocks shared among units whose int32 partial sums
+# add up (wrapping) before the one narrowing -- (N, C, H, W, M, kh, kw, sh, sw, dh, dw, pt,
+# pl, pb, pr, bias, depthwise)
+KSPLIT = [
+    (2, 512, 7, 7, 512, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),     # one row tile: single-CTA 128-column tiles
+    (8, 256, 14, 14, 256, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0),   # CTA-pair tiles
+    (4, 64, 28, 28, 48, 3, 3, 2, 2, 1, 1, 1, 1, 1, 1, 1, 0),     # packed 64-column tiles
+    (3, 100, 9, 9, 200, 3, 3, 1, 1, 1, 1, 1, 1, 1, 1, 0, 0),     # partial column tiles, no bias
+]
+
+
+@pytest.mark.parametrize("case", KSPLIT)
+@pytest.mark.parametrize("splits", [0, 2, 3, 4])
+@pytest.mark.parametrize("epi", [0, 3])
+def test_k_split_units(cm, port, case, splits, epi):
+    """Every K-split setting (0 = never; 2-4 units per tile) gives the reference words,
+    with and without the fused residual Add + Relu; full-range words so the int32
+    partial sums wrap."""
+    from cormorant_b200 import _lib, kernels
+    N, C, H, W, M, kh, kw, sh, sw, dh, dw_, pt, pl, pb, pr, hb, dwm = case
+    oh, ow = osz(H, kh, sh, dh, pt, pb), osz(W, kw, sw, dw_, pl, pr)
+    rng = np.random.default_rng(sum(case) + 7 * splits + epi)
+    x = rand16(rng, N * C * H * W)
+    w = rand16(rng, M * C * kh * kw)
+    bias = rand16(rng, M)
+    r = rand16(rng, N * M * oh * ow)
+    size = N * M * oh * ow
+    want = port.conv(x, w, bias if hb else None, N, C, H, W, M, oh, ow, kh, kw, sh, sw, dh, dw_, pt, pl, hb, dwm)[:size]
+    if epi & 2:
+        want = port.vectorop(want, r, size, 0, 1, 0, 0)[:size]
+    if epi & 1:
+        want = port.vectorop(want, None, size, 4, 1, 0, 0)[:size]
+    L = _lib.lib()
+    old = L.cm_set_gemm_split(splits)
+    try:
+        for rep in range(2):                       # the arrival counters are zero again after a launch
+            y = empty(size)
+            kernels.ConvKernelFused(dev(x), dev(w), dev(bias) if hb else None, y, N, C, H, W, M, oh, ow, kh, kw, sh,
+                                    sw, dh, dw_, pt, pl, hb, dwm, epilogue=epi, resid=dev(r) if epi & 2 else None)
+            assert_same(host(y), want, f"K-split {splits} {case} epi {epi} call {rep}")
+    finally:
+        L.cm_set_gemm_split(old)

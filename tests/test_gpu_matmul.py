@@ -253,3 +253,32 @@ def test_chunked_batches(cm, port, n, k, m, batch, bcast, epi):
     assert_same(rows, want, f"chunked {n}x{k}x{m} b{batch} bcast={bcast} epi={epi}")
     gaps = np.concatenate([got[z * c_bs + n * m:(z + 1) * c_bs] for z in range(batch - 1)])
     assert (gaps == -23131).all()                       # the words between slices stay untouched
+
+
+@pytest.mark.parametrize("n,k,m,batch", [(256, 4096, 384, 1), (129, 2048, 131, 2), (300, 1024, 64, 1)])
+@pytest.mark.parametrize("splits", [0, 2, 3, 4])
+def test_k_split_units(cm, port, n, k, m, batch, splits):
+    """K-split MatMul GEMMs (a tile's K blocks over 2-4 units, int32 partial sums added
+    with wrap before the narrowing) give the reference words; with the fused bias + Relu
+    epilogue too.  Full-range words: the partial sums wrap."""
+    from cormorant_b200 import _lib
+    rng = np.random.default_rng(n + k + m + splits)
+    a = rand16(rng, batch * n * k)
+    b = rand16(rng, batch * k * m)
+    bias = rand16(rng, m)
+    want = port.matmul(a, b, n, k, m, batch)[: batch * n * m]
+    L = _lib.lib()
+    old = L.cm_set_gemm_split(splits)
+    try:
+        c = empty(batch * n * m)
+        cm.MatmulKernel(dev(a), dev(b), c, n, k, m, batch)
+        assert_same(host(c), want, f"K-split {splits}: {n}x{k}x{m} b{batch}")
+        c = empty(batch * n * m)
+        cm.kernels.MatmulKernelFused(dev(a), dev(b), c, n, k, m, batch, epilogue=3, bias=dev(bias))
+    finally:
+        L.cm_set_gemm_split(old)
+    for z in range(batch):
+        t = want[z * n * m:(z + 1) * n * m]
+        t = port.vectorop(t, bias, m, 0, n, m, 0, c=t.copy())[: n * m]
+        want[z * n * m:(z + 1) * n * m] = port.vectorop(t, None, n * m, 4, 1, 0, 0)[: n * m]
+    assert_same(host(c), want, f"K-split {splits} fused: {n}x{k}x{m} b{batch}")

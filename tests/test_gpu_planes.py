@@ -165,6 +165,39 @@ def test_residual_from_plane_image(cm, port):
     assert_same(host(got), want, "NCHW residual on the CUDA-core path")
 
 
+@pytest.mark.parametrize("splits", [0, 3])
+def test_k_split_plane_output_and_residual(cm, port, splits):
+    """A residual block of plane images (conv -> planes; conv(planes) + residual planes ->
+    planes + y) on K-split GEMMs: the same words as the unsplit ones and the reference."""
+    from cormorant_b200 import _lib, kernels
+    rng = np.random.default_rng(77 + splits)
+    N, C, H = 4, 256, 14
+    g0 = geo(N, 64, H, H, C, 3, 1, 1)
+    g1 = geo(N, C, H, H, C, 3, 1, 1)
+    g2 = geo(N, C, H, H, 96, 3, 1, 1)
+    x = rand16(rng, N * 64 * H * H)
+    w0, b0 = weights(rng, g0)
+    w1, b1 = weights(rng, g1)
+    w2, b2 = weights(rng, g2)
+    r = oracle(port, x, w0, b0, g0, 1)
+    y1_want = oracle(port, r, w1, b1, g1, 3, r)
+    y2_want = oracle(port, y1_want, w2, b2, g2)
+    L = _lib.lib()
+    old = L.cm_set_gemm_split(splits)
+    try:
+        R = kernels.PlaneImage(N, C, H, H, kernels.conv_plane_frame(*g1))
+        kernels.ConvKernelPlanes(dev(x), None, dev(w0), dev(b0), None, R, *g0, epilogue=1)
+        P = kernels.PlaneImage(N, C, H, H, kernels.conv_plane_frame(*g2))
+        y1 = empty(y1_want.size)
+        kernels.ConvKernelPlanes(None, R, dev(w1), dev(b1), y1, P, *g1, epilogue=3, resid=None, resid_planes=R)
+        y2 = empty(y2_want.size)
+        kernels.ConvKernelPlanes(None, P, dev(w2), dev(b2), y2, None, *g2)
+    finally:
+        L.cm_set_gemm_split(old)
+    assert_same(host(y1), y1_want, f"K-split {splits}: block output")
+    assert_same(host(y2), y2_want, f"K-split {splits}: conv of the block's plane image")
+
+
 @pytest.mark.parametrize("N,C,H,W", [(3, 64, 14, 14), (2, 40, 7, 9), (2, 64, 56, 56)])
 def test_planes_fill_then_conv_and_residual(cm, port, N, C, H, W):
     """cm_planes_fill splits an NCHW tensor no conv produced (a pool output) into a plane
