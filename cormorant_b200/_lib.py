@@ -67,6 +67,10 @@ SIGNATURES: dict[str, tuple] = {
     "cm_conv_writes_nhwc": (C.c_int, [_u] * 17),
     "cm_conv_planes": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p]),
     "cm_conv_planes_async": (C.c_int, [_p] * 6 + [_u] * 18 + [_p, _p, _p]),
+    "cm_matmul_weights_create": (C.c_int, [_p, _u, _u, C.POINTER(_p)]),
+    "cm_matmul_weights_destroy": (None, [_p]),
+    "cm_matmul_prepared": (C.c_int, [_p, _p, _p] + [_u] * 5 + [_p]),
+    "cm_matmul_prepared_async": (C.c_int, [_p, _p, _p] + [_u] * 5 + [_p, _p]),
     "cm_conv_weights_create": (C.c_int, [_p, _p] + [_u] * 17 + [C.POINTER(_p)]),
     "cm_conv_weights_destroy": (None, [_p]),
     "cm_conv_prepared": (C.c_int, [_p] * 5 + [_u, _p, _p]),

@@ -2179,6 +2179,117 @@ int matmul_impl(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsi
 }
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Prepared MatMul B (a network's Gemm weights): planes and column terms built once
+// ---------------------------------------------------------------------------
+struct cm_matmul_weights {
+    const int16_t* b = nullptr;   // the live B, read by the calls that do not use the planes
+    uint32_t k = 0, m = 0;
+    int device = -1;
+    uint32_t packed = 0;
+    int8_t* planes = nullptr;     // null: every call takes cm_matmul's own path
+    int32_t* colterm = nullptr;
+    void* mem = nullptr;
+};
+
+extern "C" int cm_matmul_weights_create(const int16_t* b, unsigned k, unsigned m, cm_matmul_weights_t** out) {
+    if (out) *out = nullptr;                // null on every failure
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!out) return set_error(CM_EINVAL, "cm_matmul_weights_create: null result pointer");
+    if (k > 0 && m > 0 && !b) return set_error(CM_EINVAL, "cm_matmul_weights_create: null B");
+    cm_matmul_weights* w = new (std::nothrow) cm_matmul_weights;
+    if (!w) return set_error(CM_ENOMEM, "cm_matmul_weights_create: out of host memory");
+    w->b = b; w->k = k; w->m = m; w->device = cx->device;
+    if (k == 0 || m == 0 || k > kMaxGemmK) {   // nothing to prepare: calls take cm_matmul's path
+        *out = w;
+        return CM_OK;
+    }
+    w->packed = m <= 64 ? 1u : 0u;
+    const uint64_t b_bytes = ((uint64_t)k * (w->packed ? 128 : 2 * pad_c(m)) + 255) & ~255ull;
+    const uint64_t ct_bytes = ((uint64_t)m * 4 + 255) & ~255ull;
+    cudaError_t e = cudaMalloc(&w->mem, b_bytes + ct_bytes);
+    if (e != cudaSuccess) { delete w; return cuda_error(e, "cm_matmul_weights_create: cudaMalloc"); }
+    w->planes = (int8_t*)w->mem;
+    w->colterm = (int32_t*)((int8_t*)w->mem + b_bytes);
+    cudaStream_t s = nullptr;
+    rc = split_kn(cx, b, 0, m, m, k, 1, w->planes, w->colterm, s, w->packed != 0);
+    if (!rc) {
+        e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) rc = cuda_error(e, "cm_matmul_weights_create");
+    }
+    if (rc) {
+        cudaFree(w->mem);
+        delete w;
+        return rc;
+    }
+    *out = w;
+    return CM_OK;
+}
+
+extern "C" void cm_matmul_weights_destroy(cm_matmul_weights_t* w) {
+    if (!w) return;
+    if (w->mem) {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (w->device >= 0 && cur != w->device) cudaSetDevice(w->device);
+        cudaFree(w->mem);
+        if (cur >= 0 && cur != w->device) cudaSetDevice(cur);
+    }
+    delete w;
+}
+
+extern "C" int cm_matmul_prepared_async(const cm_matmul_weights_t* w, const int16_t* a, int16_t* c, unsigned n,
+                                        unsigned batch, unsigned a_batch_stride, unsigned c_batch_stride,
+                                        unsigned epilogue, const int16_t* bias, cm_stream_t stream) {
+    const Context* cx;
+    int rc = enter(&cx);
+    if (rc) return rc;
+    if (!w) return set_error(CM_EINVAL, "cm_matmul_prepared: null weights");
+    if (w->device != cx->device) return set_error(CM_EINVAL, "cm_matmul_prepared: weights of device %d", w->device);
+    const cudaStream_t s = (cudaStream_t)stream;
+    const unsigned k = w->k, m = w->m;
+    const unsigned __int128 macs = (unsigned __int128)batch * n * m * k;
+    // cm_matmul_fused with B broadcast (b_batch_stride 0) and the prepared planes: the calls
+    // that do not run the one-GEMM form (argument errors, empty and launch-bound sizes,
+    // overlapping output steps, the row-strided form, batch chunks) take that path with the
+    // live B
+    const bool own = w->planes && epilogue <= 3u && !((epilogue & 2u) && !bias) && n > 0 && batch > 0 && a && c &&
+                     macs > cx->direct_max_macs && !(batch > 1 && (uint64_t)c_batch_stride < (uint64_t)n * m) &&
+                     !(n == 1 && batch > 1) &&
+                     !(cx->matmul_overlap && batch >= 2 && std::min<uint64_t>(std::min<uint64_t>(batch, 8), (uint64_t)(macs >> 37)) >= 2);
+    if (!own)
+        return matmul_impl(a, w->b, c, n, k, m, batch, a_batch_stride, 0u, c_batch_stride, epilogue, bias, s);
+    const uint32_t a_batches = a_batch_stride == 0 ? 1u : batch;
+    const uint64_t K_pad = pad_k(k);
+    const uint64_t a_bytes = ((uint64_t)a_batches * 2 * n * K_pad + 255) & ~255ull;
+    const uint64_t rt_bytes = ((uint64_t)a_batches * n * 4 + 255) & ~255ull;
+    void* scratch = nullptr;
+    rc = scratch_alloc(&scratch, a_bytes + rt_bytes, s);
+    if (rc) return rc;
+    int8_t* ap = (int8_t*)scratch;
+    int32_t* rt = (int32_t*)(ap + a_bytes);
+    rc = split_rows(cx, a, a_batch_stride, k, n, k, a_batches, ap, rt, nullptr, s);
+    if (!rc) {
+        GemmPlan p{ap, n, a_batches, w->planes, m, 1, k, (uint32_t)K_pad, pad_c(m), rt, w->colterm, c, m, 1, c_batch_stride, batch};
+        p.b_packed = w->packed;
+        p.epi = (epilogue & 1u) | ((epilogue & 2u) << 1);   // the kernel's bias-row bit is 4
+        p.resid = (epilogue & 2u) ? bias : nullptr;
+        rc = gemm_launch(cx, p, s);
+    }
+    scratch_free(scratch, s);
+    if (rc) return rc;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? CM_OK : cuda_error(e, "cm_matmul_prepared");
+}
+
+extern "C" int cm_matmul_prepared(const cm_matmul_weights_t* w, const int16_t* a, int16_t* c, unsigned n, unsigned batch,
+                                  unsigned a_batch_stride, unsigned c_batch_stride, unsigned epilogue, const int16_t* bias) {
+    int rc = cm_matmul_prepared_async(w, a, c, n, batch, a_batch_stride, c_batch_stride, epilogue, bias, nullptr);
+    return rc ? rc : finish_sync(nullptr);
+}
+
 extern "C" int cm_matmul_async(const int16_t* a, const int16_t* b, int16_t* c, unsigned n, unsigned k, unsigned m,
                                unsigned batch, unsigned a_batch_stride, unsigned b_batch_stride,
                                unsigned c_batch_stride, cm_stream_t stream) {

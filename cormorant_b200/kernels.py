@@ -300,6 +300,45 @@ def ConvKernelPrepared(w, x, xp, y, yp, epilogue=EPI_NONE, resid=None, resid_pla
     check(L.cm_conv_prepared(*args) if stream is None else L.cm_conv_prepared_async(*args, _stream(stream)))
 
 
+class MatmulWeights:
+    """A MatMul B operand (k x m, broadcast over the batch) prepared once
+    (cm_matmul_weights_create): its planes and column terms, so repeated calls with constant
+    weights (a network's Gemm) skip that preparation.  `b` must keep the values it had at
+    creation and stay allocated.  Not a reference object."""
+
+    def __init__(self, b, k, m):
+        import ctypes as C
+        self.k, self.m = int(k), int(m)
+        self._keep = b                          # the buffer the other paths still read
+        out = C.c_void_p()
+        self.ptr = None
+        check(lib().cm_matmul_weights_create(_addr(b), self.k, self.m, C.byref(out)))
+        self.ptr = out.value
+
+    def close(self) -> None:
+        if getattr(self, "ptr", None):
+            lib().cm_matmul_weights_destroy(self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def MatmulKernelPrepared(w, a, c, n, batch=1, a_batch_stride=None, c_batch_stride=None, epilogue=EPI_NONE, bias=None,
+                         stream=None) -> None:
+    """MatmulKernelFused(a, B, c, n, w.k, w.m, batch, a_bs, 0, c_bs, epilogue, bias) with the
+    MatmulWeights `w` of B (cm_matmul_prepared): the same words, without the per-call split
+    of B."""
+    a_bs = n * w.k if a_batch_stride is None else a_batch_stride
+    c_bs = n * w.m if c_batch_stride is None else c_batch_stride
+    L = lib()
+    args = (w.ptr, _addr(a), _addr(c), n, batch, a_bs, c_bs, int(epilogue), _addr(bias))
+    check(L.cm_matmul_prepared(*args) if stream is None else L.cm_matmul_prepared_async(*args, _stream(stream)))
+
+
 def MatmulKernelFused(a, b, c, n, k, m, batch=1, a_batch_stride=None, b_batch_stride=None, c_batch_stride=None,
                       epilogue=EPI_ADD, bias=None, stream=None) -> None:
     """MatmulKernel followed by VectorOP ADD of a bias row broadcast over the n rows

@@ -631,8 +631,17 @@ class GpuBackend:
     def vectorop(self, a, b, c, size, op, outer, a_inc, b_inc):
         self.k.VectorOPKernel(a, b, c, size, op, outer, a_inc, b_inc, stream=self.stream)
 
+    def _prepared_b(self, b, k, m, batch, b_bs):
+        if not self.weights or (batch > 1 and b_bs != 0):
+            return None
+        return self.weights.get(matmul_weights_key(b, k, m))
+
     def matmul(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs):
-        self.k.MatmulKernel(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, stream=self.stream)
+        pw = self._prepared_b(b, k, m, batch, b_bs)
+        if pw is not None:
+            self.k.MatmulKernelPrepared(pw, a, c, n, batch, a_bs, c_bs, stream=self.stream)
+        else:
+            self.k.MatmulKernel(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, stream=self.stream)
 
     def matmul_at(self, a, b, c, a_off, b_off, c_off, n, k, m, batch, a_bs, b_bs, c_bs):
         # run_matmul_at: the element offsets move the three base addresses
@@ -640,8 +649,12 @@ class GpuBackend:
                             a_bs, b_bs, c_bs, stream=self.stream)
 
     def matmul_fused(self, a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epi, bias):
-        self.k.MatmulKernelFused(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi, bias=bias,
-                                 stream=self.stream)
+        pw = self._prepared_b(b, k, m, batch, b_bs)
+        if pw is not None:
+            self.k.MatmulKernelPrepared(pw, a, c, n, batch, a_bs, c_bs, epilogue=epi, bias=bias, stream=self.stream)
+        else:
+            self.k.MatmulKernelFused(a, b, c, n, k, m, batch, a_bs, b_bs, c_bs, epilogue=epi, bias=bias,
+                                     stream=self.stream)
 
     def _prepared(self, w, bias, geo):
         return self.weights.get(weights_key(w, bias, geo)) if self.weights else None
@@ -697,15 +710,30 @@ def weights_key(w, bias, geo) -> tuple:
     return (addr(w), addr(bias), tuple(int(v) for v in geo))
 
 
+def matmul_weights_key(b, k, m) -> tuple:
+    """Lookup key of a MatMul call's prepared B: its buffer and (k, m)."""
+    return ("matmul", b.data_ptr() if hasattr(b, "data_ptr") else int(b), int(k), int(m))
+
+
 def prepare_weights(net: Net, bufs: dict) -> dict:
-    """Prepared weights (kernels.ConvWeights) of every conv in the call list, built once
-    from the device buffers `bufs` (gpu_buffers) holds: pass the result to GpuBackend so
-    that runs skip the per-call weight preparation.  The network's weights are constants;
-    the buffers must keep their values while the result is used."""
+    """Prepared weights of the call list, built once from the device buffers `bufs`
+    (gpu_buffers) holds: kernels.ConvWeights for every conv and kernels.MatmulWeights for
+    every MatMul whose B is a constant shared by its batch steps (a Gemm's weights).  Pass
+    the result to GpuBackend so that runs skip the per-call weight preparation.  The
+    network's weights are constants; the buffers must keep their values while the result
+    is used."""
     from . import kernels
     R = lambda name: None if name is None else bufs[net.resolve(name)]  # noqa: E731
     out = {}
     for node in net.nodes:
+        if node[0] == "matmul":
+            n, k, m, batch, _, b_bs = node[4][:6]
+            if net.resolve(node[2]) in net.consts and (batch == 1 or b_bs == 0):
+                b = R(node[2])
+                key = matmul_weights_key(b, k, m)
+                if key not in out:
+                    out[key] = kernels.MatmulWeights(b, k, m)
+            continue
         if node[0] != "conv":
             continue
         w, b, geo = R(node[2]), R(node[3]), node[5]

@@ -356,6 +356,26 @@ int cm_conv_prepared_async(const cm_conv_weights_t* w, const int16_t* x, const c
                            cm_planes_t* yp, unsigned epilogue, const int16_t* resid,
                            const cm_planes_t* resid_planes, cm_stream_t stream);
 
+/* ---- Prepared MatMul B (no reference counterpart) -------------------------------------
+ * A network's Gemm weights (B, k x m, broadcast over the batch) do not change between runs,
+ * but every MatMul call splits them into the GEMM's planes and column terms again (one
+ * launch; 14 us for ResNet-18's 512 x 1000 classifier).  cm_matmul_weights_create does that
+ * once; cm_matmul_prepared[_async] then returns cm_matmul_fused's words for (a, b, c, n, k,
+ * m, batch, a_batch_stride, 0, c_batch_stride, epilogue, bias) while b keeps the values it
+ * held at creation (the planes are a snapshot; calls that cm_matmul runs on another path --
+ * launch-bound sizes, overlapping output steps, the row-strided form -- read b itself, so b
+ * must stay allocated).  Creation runs on the default stream and waits for it (not inside a
+ * stream capture); *out is null unless it returns CM_OK.  Destroy frees the planes (null is
+ * accepted). */
+typedef struct cm_matmul_weights cm_matmul_weights_t;
+int cm_matmul_weights_create(const int16_t* b, unsigned k, unsigned m, cm_matmul_weights_t** out);
+void cm_matmul_weights_destroy(cm_matmul_weights_t* w);
+int cm_matmul_prepared(const cm_matmul_weights_t* w, const int16_t* a, int16_t* c, unsigned n, unsigned batch,
+                       unsigned a_batch_stride, unsigned c_batch_stride, unsigned epilogue, const int16_t* bias);
+int cm_matmul_prepared_async(const cm_matmul_weights_t* w, const int16_t* a, int16_t* c, unsigned n, unsigned batch,
+                             unsigned a_batch_stride, unsigned c_batch_stride, unsigned epilogue, const int16_t* bias,
+                             cm_stream_t stream);
+
 /* ---- Small call lists in one launch (no reference counterpart) ----------------------
  * A list of small kernel calls -- a batch-1 network, bound by launch latency -- run as ONE
  * CTA that executes them in order, with the results of the entry points named below,

@@ -282,3 +282,54 @@ def test_k_split_units(cm, port, n, k, m, batch, splits):
         t = port.vectorop(t, bias, m, 0, n, m, 0, c=t.copy())[: n * m]
         want[z * n * m:(z + 1) * n * m] = port.vectorop(t, None, n * m, 4, 1, 0, 0)[: n * m]
     assert_same(host(c), want, f"K-split {splits} fused: {n}x{k}x{m} b{batch}")
+
+
+@pytest.mark.parametrize("n,k,m,batch,a_bcast", [(64, 512, 1000, 1, 0), (256, 512, 1000, 1, 0), (300, 261, 64, 3, 0),
+                                                 (129, 130, 131, 2, 1), (7, 13, 5, 1, 0), (1, 400, 120, 5, 0)])
+@pytest.mark.parametrize("epi", [0, 3])
+def test_prepared_b_matches_fused(cm, port, n, k, m, batch, a_bcast, epi):
+    """cm_matmul_prepared with B prepared once equals the reference MatMul (+ bias row Add +
+    Relu) with B broadcast over the batch, word for word, over repeated calls -- on the
+    one-GEMM form and on the paths that read B itself (launch-bound sizes, the row-strided
+    form of n = 1)."""
+    from cormorant_b200 import kernels
+    rng = np.random.default_rng(n * 3 + k + m + batch + epi)
+    a_bs = 0 if a_bcast else n * k
+    a = rand16(rng, (1 if a_bcast else batch) * n * k)
+    b = rand16(rng, k * m)
+    bias = rand16(rng, m)
+    want = port.matmul(a, b, n, k, m, batch, a_bs, 0, n * m)[: batch * n * m]
+    for z in range(batch):
+        t = want[z * n * m:(z + 1) * n * m]
+        if epi & 2:
+            t = port.vectorop(t, bias, m, 0, n, m, 0, c=t.copy())[: n * m]
+        if epi & 1:
+            t = port.vectorop(t, None, n * m, 4, 1, 0, 0)[: n * m]
+        want[z * n * m:(z + 1) * n * m] = t
+    bd = dev(b)
+    w = kernels.MatmulWeights(bd, k, m)
+    try:
+        for rep in range(2):
+            c = empty(batch * n * m)
+            kernels.MatmulKernelPrepared(w, dev(a), c, n, batch, a_bs, n * m, epilogue=epi,
+                                         bias=dev(bias) if epi & 2 else None)
+            assert_same(host(c), want, f"prepared B {n}x{k}x{m} b{batch} epi {epi} call {rep}")
+    finally:
+        w.close()
+
+
+def test_prepared_b_refusals(cm):
+    from cormorant_b200 import CormorantError, _lib, kernels
+    import ctypes as C
+    L = _lib.lib()
+    out = C.c_void_p(1)
+    assert L.cm_matmul_weights_create(None, 16, 16, C.byref(out)) != 0 and not out.value
+    w = kernels.MatmulWeights(dev(np.ones(64 * 32, np.int16)), 64, 32)
+    try:
+        with pytest.raises(CormorantError):          # bias row without a bias
+            kernels.MatmulKernelPrepared(w, dev(np.ones(8 * 64, np.int16)), empty(8 * 32), 8, epilogue=2)
+        with pytest.raises(CormorantError):          # epilogue out of range
+            kernels.MatmulKernelPrepared(w, dev(np.ones(8 * 64, np.int16)), empty(8 * 32), 8, epilogue=4)
+    finally:
+        w.close()
+    assert L.cm_matmul_prepared(None, None, None, 1, 1, 0, 0, 0, None) != 0

@@ -284,8 +284,9 @@ def test_chained_call_list_equals_reference_sequence_on_cpu(port):
 @pytest.mark.parametrize("pool_planes,prepared", [(False, False), (True, False), (False, True)])
 def test_resnet18_chained_batch4_every_output(cm, port, pool_planes, prepared):
     """Plane images on the GPU: every NCHW tensor the chained list still writes, and the
-    logits, equal the oracle's (also with the conv weights prepared once)."""
+    logits, equal the oracle's (also with the conv and Gemm weights prepared once)."""
     import torch
+    from cormorant_b200 import kernels
     net = networks.chain(networks.fuse(networks.resnet18(batch=4)), pool_planes=pool_planes, pool_nhwc=not pool_planes)
     assert net.planes
     assert [n[0] for n in net.nodes[:2]] == ["conv", "poolp" if pool_planes else "poolnp"]
@@ -295,7 +296,9 @@ def test_resnet18_chained_batch4_every_output(cm, port, pool_planes, prepared):
     bufs = networks.gpu_buffers(net, x)
     weights = networks.prepare_weights(net, bufs) if prepared else None
     if prepared:
-        assert len(weights) == sum(1 for n in net.nodes if n[0] == "conv")
+        # every conv's weights and the classifier Gemm's B (a constant)
+        assert len(weights) == sum(1 for n in net.nodes if n[0] == "conv") + 1
+        assert sum(1 for w in weights.values() if isinstance(w, kernels.MatmulWeights)) == 1
     networks.execute(net, networks.GpuBackend(weights=weights), bufs)
     torch.cuda.synchronize()
     for name in net.buffers:
