@@ -163,9 +163,12 @@ static int _load_weight(inference_buf_t *buf, const char *name)
 class _Emitter:
     def __init__(self, net: Net, lib_path: str | None, prepared: bool = False):
         self.net = net
-        # prepared: every conv's weight planes built once by inference_init
-        # (cm_conv_weights_create) and the calls made through cm_conv_prepared_async
+        # prepared: every conv's weight planes and every Gemm's B planes built once by
+        # inference_init (cm_conv_weights_create, cm_matmul_weights_create) and the calls made
+        # through cm_conv_prepared_async / cm_matmul_prepared_async
         self.prepared = prepared
+        self._conv_index: dict = {}
+        self._mm_index: dict = {}
         self.R = net.resolve
         self.layout = plan_layout(net)
         # one init parameter per kernel of the unfused call list, as the reference's
@@ -355,6 +358,14 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             return (f"    /* {i}: VectorOP {_OP_NAMES.get(int(args[1]), args[1])} -> {self.R(c_)} */\n"
                     f"    CHECK(cm_vectorop_async({self._dev(a_)}, {self._dev(b_)}, {self._dev(c_, False)}, "
                     f"{a}, NULL));")
+        if kind == "matmul" and i in self._mm_index:
+            a_, c_, args = node[1], node[3], node[4]
+            epi, bias = (node[5], node[6]) if len(node) > 5 else (0, None)
+            n, _, _, batch, a_bs, _, c_bs = (int(v) for v in args)
+            what = "MatMul" + ("+Add" if epi & 2 else "") + ("+Relu" if epi & 1 else "")
+            return (f"    /* {i}: {what} -> {self.R(c_)} (B prepared by inference_init) */\n"
+                    f"    CHECK(cm_matmul_prepared_async(g_mw[{self._mm_index[i]}], {self._dev(a_)}, {self._dev(c_, False)}, "
+                    f"{n}u, {batch}u, {a_bs}u, {c_bs}u, {int(epi)}u, {self._dev(bias)}, NULL));")
         if kind == "matmul" and len(node) > 5:
             _, a_, b_, c_, args, epi, bias = node
             a = ", ".join(f"{int(v)}u" for v in args)
@@ -408,6 +419,11 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             for _, k, p in self.kernels[1:])
         convs = [i for i, n in enumerate(net.nodes) if n[0] == "conv"] if self.prepared else []
         self._conv_index = {i: j for j, i in enumerate(convs)}
+        # MatMuls whose B is a network constant shared by the batch steps (a Gemm's weights)
+        mms = [i for i, n in enumerate(net.nodes)
+               if self.prepared and n[0] == "matmul" and net.resolve(n[2]) in net.consts
+               and (int(n[4][3]) == 1 or int(n[4][5]) == 0)]
+        self._mm_index = {i: j for j, i in enumerate(mms)}
         calls = "\n".join(self._call(i, n) for i, n in enumerate(net.nodes))
         cwdecl = (f"/* ---- conv weights prepared once (cm_conv_weights_create) ---- */\n"
                   f"static cm_conv_weights_t *g_cw[{len(convs)}];\n") if convs else ""
@@ -418,6 +434,17 @@ int inference_run(inference_buf_t *in_{self.in_c}, inference_buf_t *out_{self.ou
             f"        goto fail;\n    }}"
             for j, i in enumerate(convs))
         cwdestroy = "\n".join(f"    cm_conv_weights_destroy(g_cw[{j}]);\n    g_cw[{j}] = NULL;" for j in range(len(convs)))
+        if mms:
+            cwdecl += (f"/* ---- Gemm B operands prepared once (cm_matmul_weights_create) ---- */\n"
+                       f"static cm_matmul_weights_t *g_mw[{len(mms)}];\n")
+            cwcreate += "\n" + "\n".join(
+                f"    if (cm_matmul_weights_create({self._dev(net.nodes[i][2])}, {int(net.nodes[i][4][1])}u, "
+                f"{int(net.nodes[i][4][2])}u, &g_mw[{j}]) != CM_OK) {{\n"
+                f"        fprintf(stderr, \"inference_init: preparing MatMul {i}: %s\\n\", cm_last_error());\n"
+                f"        goto fail;\n    }}"
+                for j, i in enumerate(mms))
+            cwdestroy += "\n" + "\n".join(f"    cm_matmul_weights_destroy(g_mw[{j}]);\n    g_mw[{j}] = NULL;"
+                                            for j in range(len(mms)))
         pdecl = "\n".join(f"static cm_planes_t *{self._pvar(n)} = NULL;   /* {b}x{c}x{h}x{w}, frame {fr} */"
                           for n, (b, c, h, w, fr) in net.planes.items())
         pcreate = "\n".join(

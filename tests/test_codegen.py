@@ -207,8 +207,9 @@ def test_plane_pool_project_compiles(tmp_path):
 
 
 def test_prepared_project_builds_weights_once(tmp_path):
-    """prepared=True: inference_init creates one cm_conv_weights_t per conv (after the weight
-    pool reaches the device), inference_run calls cm_conv_prepared_async for every conv,
+    """prepared=True: inference_init creates one cm_conv_weights_t per conv and one
+    cm_matmul_weights_t for the classifier Gemm (after the weight pool reaches the device),
+    inference_run calls cm_conv_prepared_async / cm_matmul_prepared_async for them,
     inference_deinit destroys them."""
     net = _net("resnet18_b2", "prepared")
     codegen.emit_project(net, tmp_path, expected=np.zeros(2000, np.int16), prepared=True)
@@ -218,6 +219,11 @@ def test_prepared_project_builds_weights_once(tmp_path):
     assert src.count("cm_conv_weights_destroy(") == nconv
     assert "cm_conv_planes_async(" not in src and "cm_conv_fused_async(" not in src
     assert src.index("cm_buf_sync_to_device(g_wpool)") < src.index("cm_conv_weights_create(")
+    # the classifier Gemm's B: prepared once as well
+    assert src.count("cm_matmul_weights_create(") == 1 == src.count("cm_matmul_prepared_async(")
+    assert src.count("cm_matmul_weights_destroy(") == 1
+    assert "cm_matmul_fused_async(" not in src
+    assert src.index("cm_buf_sync_to_device(g_wpool)") < src.index("cm_matmul_weights_create(")
 
 
 # ---- the reference scheduler's own files (tests/golden/make_calllists.py) ----------
