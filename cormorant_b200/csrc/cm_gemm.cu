@@ -348,6 +348,7 @@ struct GemmArgs {
     FastDiv fd_split;
     int32_t* ws;
     uint32_t* cnt;
+    uint32_t no_split;        // the launch may not allocate: never K-split
 };
 
 struct Tile {
@@ -1713,7 +1714,7 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
     g.fd_hw = FastDiv(g.conv ? g.tiles_w * g.tiles_h : 1u);
     g.fd_w = FastDiv(g.conv ? g.tiles_w : 1u);
     g.splits = 1; g.fd_split = FastDiv(1u); g.ws = nullptr; g.cnt = nullptr;
-    if (CAN_KS) {
+    if (CAN_KS && !g.no_split) {
         const uint32_t S = pick_splits(cx, total, g.num_kb, (uint32_t)per_sm_clusters,
                                        (uint64_t)CG * Cfg<TBN, CG, WA>::EPI_WARPS);
         if (S > 1 && total * S < (1ull << 32)) {
@@ -1809,6 +1810,7 @@ int gemm_launch(const Context* cx, const GemmPlan& p, cudaStream_t s) {
     g.out = p.out; g.ldo = p.ldo; g.ldc = p.ldc ? p.ldc : 1; g.out_bs = p.out_bs;
     g.conv = 0;
     g.rows_per_img = p.rows_per_img;
+    g.no_split = p.no_split;
     g.ksteps = (p.K + 31) / 32;
     g.epi = p.epi; g.resid = p.resid;
     if (p.b_packed) return launch_persistent<64, 1>(cx, ta, tb, g, s);
@@ -2392,6 +2394,7 @@ int noalloc_run(const Context* cx, uint8_t* base, const int16_t* a, const int16_
     if (!rc) rc = split_kn(cx, b, b_bs, m, m, k, b_batches, bp, ct, s);
     if (!rc) {
         GemmPlan p{ap, n, a_batches, bp, m, b_batches, k, (uint32_t)K_pad, pad_c(m), rt, ct, c, m, 1, c_bs, nb};
+        p.no_split = 1;                 // a K-split launch would allocate its slabs
         rc = gemm_launch(cx, p, s);
     }
     return rc;

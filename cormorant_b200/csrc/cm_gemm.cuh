@@ -69,6 +69,9 @@ struct GemmPlan {
     // rows_per_img != 0 (plain mode): row = n*rows_per_img + p is written to
     // out[n*out_bs + p + col*ldc] (conv output pixels of several images, NCHW)
     uint32_t rows_per_img = 0;
+    // 1: never divide the tiles' K blocks among units (a K-split launch allocates its slabs;
+    // the allocation-free entry may not)
+    uint32_t no_split = 0;
     // fused epilogue: bit 1 = add `resid` (same indexing as out, saturating), then
     // bit 0 = ReLU -- VectorOP ADD / RELU applied to the narrowed words
     uint32_t epi = 0;

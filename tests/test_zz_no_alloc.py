@@ -79,3 +79,60 @@ def test_noalloc_rejects_oversized_calls():
     rc = L.cm_matmul_noalloc(_p(a), _p(a), _p(c), n, k, m, 1, n * k, k * m, n * m, None)
     assert rc == CM_EINVAL
     assert b"scratch" in L.cm_last_error()
+
+
+def test_noalloc_allocates_nothing_even_where_the_gemm_would_split(port):
+    """A small grid is where the tensor-core GEMM may divide its tiles' K blocks among units,
+    which needs slab memory from the stream-ordered pool; the allocation-free entry never
+    does that.  With four-way splits forced, the device's default memory pool (the one the
+    library's scratch comes from) must not grow during two cm_matmul_noalloc calls, while
+    the same check around cm_matmul sees its scratch (so the check itself works)."""
+    import torch
+    from cuda.bindings import driver as drv
+
+    import cormorant_b200 as cm
+    from cormorant_b200._lib import lib
+
+    cm.init("0")
+    L = lib()
+    n, k, m = 300, 1024, 200
+    gen = torch.Generator().manual_seed(2718)
+    a16 = torch.randint(-32768, 32768, (n * k,), dtype=torch.int32, generator=gen).to(torch.int16)
+    b16 = torch.randint(-32768, 32768, (k * m,), dtype=torch.int32, generator=gen).to(torch.int16)
+    ad, bd = a16.cuda(), b16.cuda()
+    want = port.matmul(a16.numpy(), b16.numpy(), n, k, m)[: n * m]
+    assert drv.cuInit(0)[0] == drv.CUresult.CUDA_SUCCESS
+    err, dev = drv.cuDeviceGet(torch.cuda.current_device())
+    assert err == drv.CUresult.CUDA_SUCCESS
+    err, pool = drv.cuDeviceGetDefaultMemPool(dev)
+    assert err == drv.CUresult.CUDA_SUCCESS
+    attr_cur = drv.CUmemPool_attribute.CU_MEMPOOL_ATTR_USED_MEM_CURRENT
+    attr_high = drv.CUmemPool_attribute.CU_MEMPOOL_ATTR_USED_MEM_HIGH
+
+    def pool_growth(call):
+        torch.cuda.synchronize()
+        err, cur = drv.cuMemPoolGetAttribute(pool, attr_cur)
+        assert err == drv.CUresult.CUDA_SUCCESS
+        assert drv.cuMemPoolSetAttribute(pool, attr_high, drv.cuuint64_t(0))[0] == drv.CUresult.CUDA_SUCCESS
+        call()
+        torch.cuda.synchronize()
+        err, high = drv.cuMemPoolGetAttribute(pool, attr_high)
+        assert err == drv.CUresult.CUDA_SUCCESS
+        return int(high) - int(cur)
+
+    old = L.cm_set_gemm_split(4)
+    try:
+        c_ref = torch.zeros(n * m, dtype=torch.int16, device="cuda")
+        assert pool_growth(lambda: L.cm_matmul(_p(ad), _p(bd), _p(c_ref), n, k, m, 1, n * k, k * m, n * m)) > 0
+        outs = [torch.full((n * m,), -23131, dtype=torch.int16, device="cuda") for _ in range(2)]
+
+        def two_calls():
+            for c in outs:
+                assert L.cm_matmul_noalloc(_p(ad), _p(bd), _p(c), n, k, m, 1, n * k, k * m, n * m, None) == 0, \
+                    L.cm_last_error()
+        assert pool_growth(two_calls) == 0
+    finally:
+        L.cm_set_gemm_split(old)
+    for c in outs:
+        assert np.array_equal(c.cpu().numpy(), want)
+    assert np.array_equal(c_ref.cpu().numpy(), want)
