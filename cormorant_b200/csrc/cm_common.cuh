@@ -33,10 +33,8 @@ struct Context {
     // k >= 2 = k units per tile whenever the K blocks allow (CM_GEMM_SPLIT at cm_init,
     // cm_set_gemm_split)
     int gemm_split = -1;
-    // per (tile, CTA, epilogue warp) arrival counters of K-split launches: zero between
-    // launches (the last arrival resets its counter; cleared again after a failed launch)
-    uint32_t* split_cnt = nullptr;
 };
+// K-split launches keep at most this many (tile, CTA, epilogue warp) arrival counters
 constexpr uint32_t kSplitCounters = 1u << 16;
 
 Context* ctx();                      // nullptr before cm_init

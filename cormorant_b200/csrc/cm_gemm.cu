@@ -1029,7 +1029,6 @@ __global__ void __launch_bounds__(Cfg<TBN, CG, WA>::THREADS, 1)
                 if (lane == 0) {
                     uint32_t* cnt = g.cnt + ((uint64_t)un.t * CG + rank) * C::EPI_WARPS + (warp - 2);
                     last = atomicAdd(cnt, 1u) == g.splits - 1u ? 1u : 0u;
-                    if (last) atomicExch(cnt, 0u);                // zero again for the next launch
                 }
                 last = __shfl_sync(0xFFFFFFFFu, last, 0);
                 if (!last) continue;
@@ -1654,6 +1653,12 @@ __global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __res
     }
 }
 
+// Zeroes n words (a K-split launch's arrival counters, right before it).
+__global__ void __launch_bounds__(256) clear_words_kernel(uint32_t* __restrict__ p, uint32_t n) {
+    griddep_wait();
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) p[i] = 0u;
+}
+
 // K-split units per tile for a launch of `tiles` tiles of num_kb K blocks on `slots`
 // resident CTAs (pairs): as many units as keep the grid to one wave (at most 4, each of at
 // least 4 K blocks), and none if that is fewer than 2.  Measured on ResNet-18's 3x3 convs
@@ -1663,7 +1668,7 @@ __global__ void __launch_bounds__(256) packed_to_rows_kernel(const int8_t* __res
 // ways) -- a unit's pipeline fill, accumulator drain and slab traffic cost more than the
 // idle slots of a partly filled last wave.
 uint32_t pick_splits(const Context* cx, uint64_t tiles, uint32_t num_kb, uint32_t slots, uint64_t counters_per_tile) {
-    if (cx->gemm_split == 0 || cx->gemm_split == 1 || !cx->split_cnt || slots == 0 || tiles == 0) return 1;
+    if (cx->gemm_split == 0 || cx->gemm_split == 1 || slots == 0 || tiles == 0) return 1;
     if (tiles * counters_per_tile > kSplitCounters) return 1;
     if (cx->gemm_split > 1) return std::max(1u, std::min<uint32_t>((uint32_t)cx->gemm_split, num_kb / 2));
     const uint64_t S = std::min<uint64_t>({4u, slots / tiles, num_kb / 4u});
@@ -1718,9 +1723,17 @@ int launch_persistent(const Context* cx, const CUtensorMap& ta, const CUtensorMa
         const uint32_t S = pick_splits(cx, total, g.num_kb, (uint32_t)per_sm_clusters,
                                        (uint64_t)CG * Cfg<TBN, CG, WA>::EPI_WARPS);
         if (S > 1 && total * S < (1ull << 32)) {
-            const int rc = scratch_alloc((void**)&g.ws, (size_t)total * CG * S * TBN * BM * sizeof(int32_t), s);
+            // the launch's own slabs and arrival counters (stream-ordered scratch, so K-split
+            // launches on different streams never share them); the counters start at zero
+            const size_t slab_bytes = (size_t)total * CG * S * TBN * BM * sizeof(int32_t);
+            const uint32_t ncnt = (uint32_t)(total * CG * Cfg<TBN, CG, WA>::EPI_WARPS);
+            const int rc = scratch_alloc((void**)&g.ws, slab_bytes + (size_t)ncnt * sizeof(uint32_t), s);
             if (rc) return rc;
-            g.splits = S; g.fd_split = FastDiv(S); g.cnt = cx->split_cnt;
+            g.splits = S; g.fd_split = FastDiv(S);
+            g.cnt = (uint32_t*)((uint8_t*)g.ws + slab_bytes);
+            launch_k(clear_words_kernel, std::min<uint32_t>((ncnt + 255) / 256, (uint32_t)cx->sm_count), 256, 0, s, g.cnt,
+                     ncnt);
+            count_launch();
         }
     }
     const uint64_t units = total * g.splits;

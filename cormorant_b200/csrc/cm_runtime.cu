@@ -57,8 +57,6 @@ int finish_sync(cm_stream_t stream) {
     if (st != 0) {
         const int zero = 0;
         cudaMemcpy(g_ctx.status, &zero, sizeof(int), cudaMemcpyHostToDevice);
-        // a K-split GEMM that wound down early leaves some arrival counters raised
-        if (g_ctx.split_cnt) cudaMemset(g_ctx.split_cnt, 0, kSplitCounters * sizeof(uint32_t));
         return set_error(st, "device-side status %d (%s)", st, cm_strerror(st));
     }
     return CM_OK;
@@ -158,7 +156,6 @@ int cm_init(const char* instance) {
     if (g_ready) {
         cudaSetDevice(g_ctx.device);
         cudaFree(g_ctx.status);
-        cudaFree(g_ctx.split_cnt);
         if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
         g_ready = false;
     }
@@ -174,12 +171,6 @@ int cm_init(const char* instance) {
     e = cudaMalloc(&c.status, 256);
     if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(status)");
     cudaMemset(c.status, 0, 256);
-    e = cudaMalloc(&c.split_cnt, kSplitCounters * sizeof(uint32_t));
-    if (e != cudaSuccess) {
-        cudaFree(c.status);
-        return cuda_error(e, "cudaMalloc(split counters)");
-    }
-    cudaMemset(c.split_cnt, 0, kSplitCounters * sizeof(uint32_t));
     // Keep freed scratch cached in the pool instead of returning it to the OS.
     cudaMemPool_t pool;
     if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
@@ -205,7 +196,6 @@ int cm_init(const char* instance) {
     e = cudaStreamCreateWithFlags(&c.aux_stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) {
         cudaFree(c.status);
-        cudaFree(c.split_cnt);
         return cuda_error(e, "cudaStreamCreate(aux)");
     }
     g_ctx = c;
@@ -219,7 +209,6 @@ int cm_release(void) {
     cudaSetDevice(g_ctx.device);
     cudaDeviceSynchronize();
     cudaFree(g_ctx.status);
-    cudaFree(g_ctx.split_cnt);
     if (g_ctx.aux_stream) cudaStreamDestroy(g_ctx.aux_stream);
     g_ready = false;
     return CM_OK;

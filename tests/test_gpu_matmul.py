@@ -333,3 +333,31 @@ def test_prepared_b_refusals(cm):
     finally:
         w.close()
     assert L.cm_matmul_prepared(None, None, None, 1, 1, 0, 0, 0, None) != 0
+
+
+def test_k_split_launches_on_two_streams(cm, port):
+    """K-split GEMMs queued on two unordered streams at once: each launch has its own slabs
+    and arrival counters, so both give the reference words."""
+    import torch
+    from cormorant_b200 import _lib
+    shapes = [(256, 4096, 384), (300, 2048, 200)]
+    rng = np.random.default_rng(99)
+    ops = []
+    for (n, k, m) in shapes:
+        a, b = rand16(rng, n * k), rand16(rng, k * m)
+        ops.append((n, k, m, dev(a), dev(b), port.matmul(a, b, n, k, m)[: n * m]))
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    L = _lib.lib()
+    old = L.cm_set_gemm_split(2)
+    try:
+        outs = [[empty(n * m) for (n, _, m, _, _, _) in ops] for _ in range(4)]
+        torch.cuda.synchronize()                   # inputs and poisoned outputs are in place
+        for rep in range(4):
+            for (n, k, m, ad, bd, _), st, c in zip(ops, streams, outs[rep]):
+                cm.MatmulKernel(ad, bd, c, n, k, m, 1, stream=st)
+        torch.cuda.synchronize()
+    finally:
+        L.cm_set_gemm_split(old)
+    for rep in range(4):
+        for (n, k, m, _, _, want), c in zip(ops, outs[rep]):
+            assert_same(host(c), want, f"two streams, call {rep}: {n}x{k}x{m}")
