@@ -731,8 +731,9 @@ class NetworkBench:
         return [out]
 
     def per_layer(self, stream, passes: int = 3):
-        """Per-call roofline: CUDA events around every call of the
-        call list in eager passes (median over `passes`); conv / MatMul calls against the int8
+        """Per-call roofline of a network's call list: CUDA events around every call of the
+        call list in eager passes (median over `passes`; each call's time includes the host
+        work of issuing it, which dominates launch-bound calls); conv / MatMul calls against the int8
         pipe's ceiling at the timed region's clock (`self.roof_peak`, int8 TOPS), pools and
         VectorOP against the measured HBM copy rate (`self.hbm_gbs`)."""
         import torch
