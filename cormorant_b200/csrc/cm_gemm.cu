@@ -1670,7 +1670,9 @@ __global__ void __launch_bounds__(256) clear_words_kernel(uint32_t* __restrict__
 uint32_t pick_splits(const Context* cx, uint64_t tiles, uint32_t num_kb, uint32_t slots, uint64_t counters_per_tile) {
     if (cx->gemm_split == 0 || cx->gemm_split == 1 || slots == 0 || tiles == 0) return 1;
     if (tiles * counters_per_tile > kSplitCounters) return 1;
-    if (cx->gemm_split > 1) return std::max(1u, std::min<uint32_t>((uint32_t)cx->gemm_split, num_kb / 2));
+    // forced splits: grids of at most four waves (the slabs grow with the grid)
+    if (cx->gemm_split > 1)
+        return tiles <= 4ull * slots ? std::max(1u, std::min<uint32_t>((uint32_t)cx->gemm_split, num_kb / 2)) : 1u;
     const uint64_t S = std::min<uint64_t>({4u, slots / tiles, num_kb / 4u});
     return S >= 2 ? (uint32_t)S : 1u;
 }

@@ -88,8 +88,9 @@ uint64_t cm_set_direct_limit(uint64_t macs);
  * divides each tile's K blocks among 2-4 units that add up exactly (int32 wrap).
  * splits < 0: chosen per launch (default, or the CM_GEMM_SPLIT environment variable at
  * cm_init); 0 or 1: never; k >= 2: k units per tile whenever the tile has at least 2k K
- * blocks.  Returns the previous setting.  No reference counterpart; every setting is
- * bit-exact. */
+ * blocks and the grid is at most four waves (each unit's int32 slab comes from the
+ * stream-ordered scratch pool).  Returns the previous setting.  No reference counterpart;
+ * every setting is bit-exact. */
 int cm_set_gemm_split(int splits);
 const char* cm_version(void);
 
